@@ -1,0 +1,77 @@
+// Host-side declarations shared by the library's translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "common.cuh"
+
+namespace aero {
+
+// ---------------------------------------------------------------- kernels
+// Router projection: logits[t][r] = x_t . W[r] (+ bias[r] for r < n_bias), for
+// rows r in [row_begin, row_end) of the (n_rows, d) f32 matrix W; logits has row
+// stride ld. Chooses a GEMV form for small T and a tiled SIMT GEMM for large T.
+cudaError_t launch_router(const float* x, int T, int d, const float* W, int row_begin, int row_end,
+                          const float* bias, int n_bias, float* logits, int ld, cudaStream_t s);
+
+// Top-k over logits[t][0..E) (row stride ld): idx/w (T, k), sgate[t] =
+// sigmoid(logits[t][E]) when has_shared, xsum16[t][d/16] sums of x (may be null).
+cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int norm, int has_shared,
+                        const float* x, int d, int32_t* idx, float* w, float* sgate, float* xsum16,
+                        cudaStream_t s);
+
+// Dispatch: expert-contiguous permutation of the T*k pairs. Writes offsets[E+1],
+// perm[P] (sorted position -> pair), inv[P] (pair -> sorted position), the active
+// list act_e[n_active] / act_off[n_active+1] (segment starts, in sorted
+// positions) and n_active. `work` is scratch of dispatch_work_bytes(P, E).
+size_t dispatch_work_bytes(int P, int E);
+cudaError_t launch_dispatch(const int32_t* idx, int P, int E, int32_t* offsets, int32_t* perm,
+                            int32_t* inv, int32_t* act_e, int32_t* act_off, int32_t* n_active,
+                            void* work, cudaStream_t s);
+
+struct GemvArgs {
+    QMat gate, up, down;     // routed experts
+    QMat sg, su, sd;         // shared expert (n_expert 1), valid when has_shared
+    const float* x;          // (T, d)
+    const float* xsum16;     // (T, d/16)
+    const int32_t* perm;
+    const int32_t* act_e;
+    const int32_t* act_off;
+    const int32_t* n_active;
+    int T, k, d, F, Fs, has_shared, max_active;
+    int act_ld;              // row stride of act (>= max(F, Fs))
+    float* act;              // (P + T, act_ld)
+    float* asum16;           // (P + T, act_ld/16)
+    float* y;                // (P + T, d)
+};
+cudaError_t launch_gemv_gateup(const GemvArgs& a, cudaStream_t s);
+cudaError_t launch_gemv_down(const GemvArgs& a, cudaStream_t s);
+
+// out[t] = sum_s w[t][s] * y[inv[t*k+s]] (+ sgate[t] * y[P + t]).
+cudaError_t launch_combine(const float* y, const int32_t* inv, const float* w, const float* sgate,
+                           int T, int k, int d, int has_shared, float* out, cudaStream_t s);
+
+// Quant helpers.
+cudaError_t launch_repack(int dtype, const uint8_t* gguf, int64_t n_rows_total, int cols,
+                          int rows_per_expert, int64_t expert0, uint8_t* qs, uint8_t* meta,
+                          int64_t qs_estride, int64_t meta_estride, cudaStream_t s);
+cudaError_t launch_dequant_gguf(int dtype, const uint8_t* gguf, int64_t n_values, float* out,
+                                cudaStream_t s);
+cudaError_t launch_quantize(int dtype, const float* x, int64_t n_values, uint8_t* out,
+                            cudaStream_t s);
+cudaError_t launch_f16_to_f32(const uint16_t* in, int64_t n, float* out, cudaStream_t s);
+
+// ---------------------------------------------------------------- guard
+enum MemClass { kWeightsResident = 0, kWeightsCache, kKVCache, kScratch, kRuntime, kMemClassCount };
+bool guard_try_reserve(size_t bytes, int cls);
+void guard_release(size_t bytes, int cls);
+// cudaMalloc charged to the guard; returns cudaErrorMemoryAllocation when refused.
+cudaError_t guarded_malloc(void** p, size_t bytes, int cls);
+void guarded_free(void* p, size_t bytes, int cls);
+
+std::string fmt_bytes(size_t b);
+
+}  // namespace aero

@@ -1,0 +1,852 @@
+// The C ABI of the library: layer handles, upload, and per-call orchestration.
+//
+// A call runs: router projection -> top-k -> dispatch -> expert products ->
+// combine, all on the handle's stream with no host synchronisation in between
+// (the number of active experts lives on the device; grids are sized for the
+// maximum and surplus CTAs exit). Semantics follow engine/moe.py:117-177 and
+// src/moe.cpp:122-161.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/aero_cuda_moe.h"
+#include "gemm.h"
+#include "gguf_loader.h"
+#include "internal.h"
+
+namespace aero {
+namespace {
+
+thread_local std::string g_free_error;
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+
+bool is_device_ptr(const void* p) {
+    if (!p) return false;
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
+}
+
+struct Alloc {
+    void* p;
+    size_t bytes;
+    int cls;
+};
+
+struct Scratch {
+    int cap_T = 0;
+    void* base = nullptr;
+    size_t bytes = 0;
+    float *x_stage, *out_stage, *lg_stage, *logits, *w, *sgate, *xsum16, *act, *asum16, *y;
+    int32_t *idx, *offsets, *perm, *inv, *act_e, *act_off, *n_active;
+    void* dwork;
+    void* gemm_ws;
+    size_t gemm_ws_bytes = 0;
+};
+
+struct Handle {
+    int device = 0;
+    cudaStream_t stream = nullptr, own_stream = nullptr;
+    std::mutex mu;
+    int d = 0, dp = 0, E = 0, k = 0, F = 0, Fp = 0, Fs = 0, Fsp = 0, norm = 1, has_shared = 0;
+    int e_begin = 0, e_end = 0, has_router = 0, act_ld = 0;
+    int dtype = 0, sh_dtype = 0;
+    QMat gate{}, up{}, down{}, sg{}, su{}, sd{};
+    float* router_ext = nullptr;  // (E + 1, dp): row E = shared gate input (or zeros)
+    float* router_bias = nullptr;
+    std::vector<Alloc> allocs;
+    Scratch sc;
+    std::string err;
+    long calls = 0, tokens = 0;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    float last_ms = 0.f;
+    bool timing = false;
+    // per-stage device time (profiling mode): stages are router, top-k,
+    // dispatch, gate/up, down, combine
+    static constexpr int kStages = 6;
+    bool profiling = false;
+    cudaEvent_t sev[kStages + 1] = {};
+    double stage_ms[kStages] = {};
+    long stage_n[kStages] = {};
+    long launches = 0;        // kernels launched by this handle
+    int last_active = -1;     // active experts of the last profiled call
+
+    ~Handle() {
+        if (device >= 0) cudaSetDevice(device);
+        if (own_stream) cudaStreamSynchronize(own_stream);
+        for (auto& a : allocs) guarded_free(a.p, a.bytes, a.cls);
+        if (sc.base) guarded_free(sc.base, sc.bytes, kScratch);
+        if (ev0) cudaEventDestroy(ev0);
+        if (ev1) cudaEventDestroy(ev1);
+        for (auto& e : sev)
+            if (e) cudaEventDestroy(e);
+        if (own_stream) cudaStreamDestroy(own_stream);
+    }
+    bool fail(const char* fmt, ...) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        std::vsnprintf(buf, sizeof(buf), fmt, ap);
+        va_end(ap);
+        err = buf;
+        return false;
+    }
+    bool cuda_ok(cudaError_t e, const char* what) {
+        if (e == cudaSuccess) return true;
+        cudaGetLastError();
+        return fail("%s: %s", what, cudaGetErrorString(e));
+    }
+    void* dalloc(size_t bytes, int cls, const char* what) {
+        void* p = nullptr;
+        const cudaError_t e = guarded_malloc(&p, bytes, cls);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            fail("device allocation of %s for %s refused: %s", fmt_bytes(bytes).c_str(), what,
+                 e == cudaErrorMemoryAllocation ? "over the memory guard budget or out of device memory"
+                                                : cudaGetErrorString(e));
+            return nullptr;
+        }
+        allocs.push_back({p, bytes, cls});
+        return p;
+    }
+};
+
+int64_t dtype_block_values(int dt) { return dt == AERO_DT_Q8_0 ? 32 : dt == AERO_DT_Q4_K ? 256 : dt == AERO_DT_F32 ? 1 : 0; }
+int64_t dtype_block_bytes(int dt) { return dt == AERO_DT_Q8_0 ? 34 : dt == AERO_DT_Q4_K ? 144 : dt == AERO_DT_F32 ? 4 : 0; }
+int64_t gguf_bytes(int dt, int64_t n) {
+    const int64_t bv = dtype_block_values(dt);
+    return bv ? n / bv * dtype_block_bytes(dt) : -1;
+}
+
+// Upload one expert-tensor family (n_experts x rows x cols, GGUF bytes at src,
+// host or device) into planes. F32 tensors are zero-padded to prow x pcol.
+bool upload_family(Handle& h, const aero_cuda_tensor& t, int total_experts, int e0, int e1, int rows, int cols,
+                   int prow, int pcol, QMat& m, const char* what) {
+    const int dt = t.dtype;
+    if (dt != AERO_DT_Q8_0 && dt != AERO_DT_Q4_K && dt != AERO_DT_F32)
+        return h.fail("%s: unsupported ggml type %d (this library reads F32, Q8_0, Q4_K)", what, dt);
+    const int64_t bv = dtype_block_values(dt);
+    if (cols % bv) return h.fail("%s: row width %d is not a multiple of the %lld-value block", what, cols, (long long)bv);
+    const int64_t per_expert = gguf_bytes(dt, (int64_t)rows * cols);
+    if (!t.data || t.nbytes < per_expert * total_experts)
+        return h.fail("%s: %lld bytes given, %lld needed", what, (long long)t.nbytes, (long long)(per_expert * total_experts));
+    const int ne = e1 - e0;
+    m.dtype = dt;
+    m.rows = dt == AERO_DT_F32 ? prow : rows;
+    m.cols = dt == AERO_DT_F32 ? pcol : cols;
+    m.n_expert = ne;
+    m.qs_estride = align128((int64_t)m.rows * qm_row_qs_bytes(dt, m.cols));
+    m.meta_estride = align128((int64_t)m.rows * qm_row_meta_bytes(dt, m.cols));
+    uint8_t* qs = (uint8_t*)h.dalloc((size_t)(m.qs_estride * ne), kWeightsResident, what);
+    if (!qs) return false;
+    uint8_t* meta = nullptr;
+    if (m.meta_estride > 0) {
+        meta = (uint8_t*)h.dalloc((size_t)(m.meta_estride * ne), kWeightsResident, what);
+        if (!meta) return false;
+    }
+    m.qs = qs;
+    m.meta = meta;
+    const uint8_t* src = static_cast<const uint8_t*>(t.data) + (int64_t)e0 * per_expert;
+    const bool src_dev = is_device_ptr(t.data);
+    if (dt == AERO_DT_F32) {
+        if (!h.cuda_ok(cudaMemsetAsync(qs, 0, (size_t)(m.qs_estride * ne), h.stream), what)) return false;
+        for (int e = 0; e < ne; ++e)
+            if (!h.cuda_ok(cudaMemcpy2DAsync(qs + (int64_t)e * m.qs_estride, (size_t)pcol * 4, src + (int64_t)e * per_expert,
+                                             (size_t)cols * 4, (size_t)cols * 4, (size_t)rows,
+                                             src_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, h.stream),
+                           what))
+                return false;
+        return h.cuda_ok(cudaStreamSynchronize(h.stream), what);
+    }
+    // Quant families: host bytes stream through a bounded staging buffer (at
+    // most 256 MiB of experts at a time), repacked on the device chunk by chunk.
+    // The planes themselves were admitted as one plan at open and are charged
+    // to the guard by their allocations.
+    const int64_t chunk_experts = std::max<int64_t>(1, std::min<int64_t>(ne, (256ll << 20) / std::max<int64_t>(1, per_expert)));
+    const int64_t stage_bytes = chunk_experts * per_expert;
+    uint8_t* stage = nullptr;
+    if (!src_dev) {
+        void* p = nullptr;
+        const cudaError_t e = guarded_malloc(&p, (size_t)stage_bytes, kScratch);
+        if (e != cudaSuccess) {
+            cudaGetLastError();
+            return h.fail("%s: staging buffer of %s refused", what, fmt_bytes((size_t)stage_bytes).c_str());
+        }
+        stage = (uint8_t*)p;
+    }
+    bool ok = true;
+    for (int64_t c0 = 0; c0 < ne && ok; c0 += chunk_experts) {
+        const int64_t cn = std::min<int64_t>(chunk_experts, ne - c0);
+        const uint8_t* s = src + c0 * per_expert;
+        if (!src_dev) {
+            ok = h.cuda_ok(cudaMemcpyAsync(stage, s, (size_t)(cn * per_expert), cudaMemcpyHostToDevice, h.stream), what);
+            s = stage;
+        } else if (dt == AERO_DT_Q4_K && ((uintptr_t)s & 15) != 0) {
+            ok = h.fail("%s: device source is not 16-byte aligned", what);
+        }
+        if (ok)
+            ok = h.cuda_ok(launch_repack(dt, s, cn * rows, cols, rows, c0, qs, meta, m.qs_estride, m.meta_estride, h.stream),
+                           what);
+        if (ok && !src_dev) ok = h.cuda_ok(cudaStreamSynchronize(h.stream), what);  // staging reuse
+    }
+    if (ok) ok = h.cuda_ok(cudaStreamSynchronize(h.stream), what);
+    if (stage) guarded_free(stage, (size_t)stage_bytes, kScratch);
+    return ok;
+}
+
+bool ensure_scratch(Handle& h, int T) {
+    if (T <= h.sc.cap_T && h.sc.base) return true;
+    const int cap = std::max(T, std::max(2 * h.sc.cap_T, 8));
+    const int64_t P = (int64_t)cap * h.k;
+    const int64_t rows = P + cap;
+    size_t off = 0;
+    auto take = [&](size_t b) {
+        const size_t o = off;
+        off += (b + 255) & ~(size_t)255;
+        return o;
+    };
+    const size_t o_x = take((size_t)cap * h.dp * 4), o_out = take((size_t)cap * h.dp * 4);
+    const size_t o_lgs = take((size_t)cap * h.E * 4);
+    const size_t o_lg = take((size_t)cap * (h.E + 1) * 4), o_w = take((size_t)P * 4), o_sg = take((size_t)cap * 4);
+    const size_t o_xs = take((size_t)cap * (h.dp / 16) * 4);
+    const size_t o_act = take((size_t)rows * h.act_ld * 4), o_as = take((size_t)rows * (h.act_ld / 16) * 4);
+    const size_t o_y = take((size_t)rows * h.dp * 4);
+    const size_t o_idx = take((size_t)P * 4), o_off = take((size_t)(h.E + 1) * 4), o_perm = take((size_t)P * 4);
+    const size_t o_inv = take((size_t)P * 4), o_ae = take((size_t)h.E * 4), o_ao = take((size_t)(h.E + 1) * 4);
+    const size_t o_na = take(4), o_dw = take(dispatch_work_bytes((int)P, h.E));
+    const size_t gws = gemm_workspace_bytes(h.dp, h.act_ld, (int)P, cap, h.E + 1);
+    const size_t o_gw = take(gws);
+    void* base = nullptr;
+    const cudaError_t e = guarded_malloc(&base, off, kScratch);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        return h.fail("scratch for %d tokens (%s) refused by the memory guard or the device", cap, fmt_bytes(off).c_str());
+    }
+    if (h.sc.base) {
+        cudaStreamSynchronize(h.stream);
+        guarded_free(h.sc.base, h.sc.bytes, kScratch);
+    }
+    char* b = (char*)base;
+    Scratch& s = h.sc;
+    s.base = base;
+    s.bytes = off;
+    s.cap_T = cap;
+    s.x_stage = (float*)(b + o_x);
+    s.out_stage = (float*)(b + o_out);
+    s.lg_stage = (float*)(b + o_lgs);
+    s.logits = (float*)(b + o_lg);
+    s.w = (float*)(b + o_w);
+    s.sgate = (float*)(b + o_sg);
+    s.xsum16 = (float*)(b + o_xs);
+    s.act = (float*)(b + o_act);
+    s.asum16 = (float*)(b + o_as);
+    s.y = (float*)(b + o_y);
+    s.idx = (int32_t*)(b + o_idx);
+    s.offsets = (int32_t*)(b + o_off);
+    s.perm = (int32_t*)(b + o_perm);
+    s.inv = (int32_t*)(b + o_inv);
+    s.act_e = (int32_t*)(b + o_ae);
+    s.act_off = (int32_t*)(b + o_ao);
+    s.n_active = (int32_t*)(b + o_na);
+    s.dwork = b + o_dw;
+    s.gemm_ws = b + o_gw;
+    s.gemm_ws_bytes = gws;
+    // zero the padded columns of the staging buffers once
+    return h.cuda_ok(cudaMemsetAsync(base, 0, off, h.stream), "scratch clear");
+}
+
+// Core pipeline on device buffers: x (T, dp), out (T, dp). When logits_in is
+// non-null it holds (T, E) caller logits on the device (row stride E).
+bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* out) {
+    Scratch& s = h.sc;
+    cudaStream_t st = h.stream;
+    const int P = T * h.k;
+    const int ld = h.E + 1;
+    auto mark = [&](int i) {
+        if (h.profiling) cudaEventRecord(h.sev[i], st);
+    };
+    mark(0);
+    if (!logits_in) {
+        if (!h.has_router) return h.fail("this layer has no router weights; use the ffn_block form with logits");
+        if (!h.cuda_ok(launch_router(x, T, h.dp, h.router_ext, 0, h.E + h.has_shared, h.router_bias, h.E, s.logits, ld, st),
+                       "router"))
+            return false;
+    } else {
+        if (!h.cuda_ok(cudaMemcpy2DAsync(s.logits, (size_t)ld * 4, logits_in, (size_t)h.E * 4, (size_t)h.E * 4, (size_t)T,
+                                         cudaMemcpyDeviceToDevice, st),
+                       "logits copy"))
+            return false;
+        if (h.has_shared &&
+            !h.cuda_ok(launch_router(x, T, h.dp, h.router_ext, h.E, h.E + 1, nullptr, 0, s.logits, ld, st), "shared gate"))
+            return false;
+    }
+    h.launches += (!logits_in || h.has_shared) ? 1 : 0;
+    mark(1);
+    if (!h.cuda_ok(launch_topk(s.logits, ld, T, h.E, h.k, h.norm, h.has_shared, x, h.dp, s.idx, s.w, s.sgate, s.xsum16, st),
+                   "top-k"))
+        return false;
+    h.launches += 1;
+    mark(2);
+    if (!h.cuda_ok(launch_dispatch(s.idx, P, h.E, s.offsets, s.perm, s.inv, s.act_e, s.act_off, s.n_active, s.dwork, st),
+                   "dispatch"))
+        return false;
+    h.launches += 3;
+    mark(3);
+    GemvArgs a{};
+    a.gate = h.gate;
+    a.up = h.up;
+    a.down = h.down;
+    a.sg = h.sg;
+    a.su = h.su;
+    a.sd = h.sd;
+    a.x = x;
+    a.xsum16 = s.xsum16;
+    a.perm = s.perm;
+    a.act_e = s.act_e;
+    a.act_off = s.act_off;
+    a.n_active = s.n_active;
+    a.T = T;
+    a.k = h.k;
+    a.d = h.dp;
+    a.F = h.Fp;
+    a.Fs = h.Fsp;
+    a.has_shared = h.has_shared;
+    a.max_active = std::min(P, h.E);
+    a.act_ld = h.act_ld;
+    a.act = s.act;
+    a.asum16 = s.asum16;
+    a.y = s.y;
+    if (!h.cuda_ok(launch_gemv_gateup(a, st), "gate/up")) return false;
+    mark(4);
+    if (!h.cuda_ok(launch_gemv_down(a, st), "down")) return false;
+    h.launches += 2 * (1 + h.has_shared);
+    mark(5);
+    if (!h.cuda_ok(launch_combine(s.y, s.inv, s.w, s.sgate, T, h.k, h.dp, h.has_shared, out, st), "combine")) return false;
+    h.launches += 1;
+    mark(6);
+    if (h.profiling) {
+        if (!h.cuda_ok(cudaEventSynchronize(h.sev[6]), "profile")) return false;
+        for (int i = 0; i < Handle::kStages; ++i) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, h.sev[i], h.sev[i + 1]);
+            h.stage_ms[i] += ms;
+            h.stage_n[i] += 1;
+        }
+        cudaMemcpy(&h.last_active, s.n_active, 4, cudaMemcpyDeviceToHost);
+    }
+    return true;
+}
+
+// Host/device wrapper: stages x and out when they are host memory or when the
+// layer is padded internally.
+bool block_entry(Handle& h, const float* x, int T, const float* logits, float* out) {
+    if (T < 0) return h.fail("T=%d", T);
+    if (T == 0) return true;
+    if (cudaSetDevice(h.device) != cudaSuccess) return h.fail("cudaSetDevice(%d) failed", h.device);
+    if (!ensure_scratch(h, T)) return false;
+    Scratch& s = h.sc;
+    cudaStream_t st = h.stream;
+    const bool x_dev = is_device_ptr(x), out_dev = is_device_ptr(out);
+    const bool x_aligned = ((uintptr_t)x & 15) == 0, out_aligned = ((uintptr_t)out & 15) == 0;
+    const bool lg_dev = logits ? is_device_ptr(logits) : false;
+    const float* xin = x;
+    if (!x_dev || h.dp != h.d || !x_aligned) {
+        if (!h.cuda_ok(cudaMemcpy2DAsync(s.x_stage, (size_t)h.dp * 4, x, (size_t)h.d * 4, (size_t)h.d * 4, (size_t)T,
+                                         x_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, st),
+                       "input copy"))
+            return false;
+        xin = s.x_stage;
+    }
+    const float* lg = logits;
+    if (logits && !lg_dev) {
+        if (!h.cuda_ok(cudaMemcpyAsync(s.lg_stage, logits, (size_t)T * h.E * 4, cudaMemcpyHostToDevice, st),
+                       "logits upload"))
+            return false;
+        lg = s.lg_stage;
+    }
+    float* o = (out_dev && h.dp == h.d && out_aligned) ? out : s.out_stage;
+    if (h.timing) cudaEventRecord(h.ev0, st);
+    if (!run_block(h, xin, T, lg, o)) return false;
+    if (h.timing) cudaEventRecord(h.ev1, st);
+    if (o != out) {
+        if (!h.cuda_ok(cudaMemcpy2DAsync(out, (size_t)h.d * 4, o, (size_t)h.dp * 4, (size_t)h.d * 4, (size_t)T,
+                                         out_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st),
+                       "output copy"))
+            return false;
+    }
+    if (!out_dev || !x_dev) {
+        if (!h.cuda_ok(cudaStreamSynchronize(st), "block")) return false;
+        if (h.timing) cudaEventElapsedTime(&h.last_ms, h.ev0, h.ev1);
+    }
+    h.calls++;
+    h.tokens += T;
+    return true;
+}
+
+void copy_err(const std::string& s, char* err, int errlen) {
+    if (err && errlen > 0) std::snprintf(err, (size_t)errlen, "%s", s.c_str());
+}
+
+Handle* open_desc(const aero_cuda_moe_desc* d, std::string* why) {
+    if (!d) {
+        *why = "null descriptor";
+        return nullptr;
+    }
+    auto* h = new Handle();
+    auto bad = [&](const std::string& m) {
+        *why = m.empty() ? h->err : m;
+        delete h;
+        return (Handle*)nullptr;
+    };
+    if (d->n_embd <= 0 || d->n_expert <= 0 || d->ffn_len <= 0) return bad("n_embd, n_expert and ffn_len must be positive");
+    if (d->n_expert_used <= 0 || d->n_expert_used > d->n_expert)
+        return bad("n_expert_used=" + std::to_string(d->n_expert_used) + " out of range for " +
+                   std::to_string(d->n_expert) + " experts");
+    if (d->n_expert_used > 32 || d->n_expert > 1024)
+        return bad("this implementation routes at most 32 of at most 1024 experts");
+    h->device = d->device;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return bad("no CUDA device is available (this library has no CPU path)");
+    }
+    if (h->device < 0 || h->device >= ndev) return bad("device " + std::to_string(h->device) + " does not exist");
+    cudaSetDevice(h->device);
+    if (cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking) != cudaSuccess) return bad("stream creation failed");
+    h->stream = h->own_stream;
+    cudaEventCreate(&h->ev0);
+    cudaEventCreate(&h->ev1);
+    h->d = d->n_embd;
+    h->E = d->n_expert;
+    h->k = d->n_expert_used;
+    h->F = d->ffn_len;
+    h->norm = d->norm_topk_prob ? 1 : 0;
+    h->has_shared = d->has_shared ? 1 : 0;
+    h->Fs = h->has_shared ? (d->ffn_len_shared > 0 ? d->ffn_len_shared : d->ffn_len) : 0;
+    h->e_begin = d->expert_begin;
+    h->e_end = d->expert_end;
+    if (h->e_begin == 0 && h->e_end == 0) h->e_end = h->E;
+    if (h->e_begin < 0 || h->e_end > h->E || h->e_begin >= h->e_end) return bad("bad expert range");
+    h->dtype = d->gate_exps.dtype;
+    if (d->up_exps.dtype != h->dtype || d->down_exps.dtype != h->dtype)
+        return bad("gate/up/down expert tensors must share one ggml type");
+    const bool f32 = h->dtype == AERO_DT_F32;
+    h->dp = f32 ? (int)round_up(h->d, 16) : h->d;
+    h->Fp = f32 ? (int)round_up(h->F, 16) : h->F;
+    if (h->dp % 16 || h->Fp % 16) return bad("n_embd and ffn_len must be multiples of 16");
+    if (h->has_shared) {
+        if (!d->shexp_gate_inp) return bad("has_shared needs shexp_gate_inp");
+        h->sh_dtype = d->shexp_gate.dtype;
+        if (d->shexp_up.dtype != h->sh_dtype || d->shexp_down.dtype != h->sh_dtype)
+            return bad("shared gate/up/down must share one ggml type");
+        if ((h->sh_dtype == AERO_DT_F32) != f32) return bad("shared expert and routed experts must both be F32 or both quantised");
+        h->Fsp = f32 ? (int)round_up(h->Fs, 16) : h->Fs;
+        if (h->Fsp % 16) return bad("ffn_len_shared must be a multiple of 16");
+    }
+    h->act_ld = (int)round_up(std::max(h->Fp, h->Fsp), 16);
+    const int ne = h->e_end - h->e_begin;
+    (void)ne;
+    // router (+ shared gate row) as f32 (E + 1, dp)
+    h->router_ext = (float*)h->dalloc((size_t)(h->E + 1) * h->dp * 4, kWeightsResident, "router");
+    if (!h->router_ext) return bad("");
+    if (!h->cuda_ok(cudaMemsetAsync(h->router_ext, 0, (size_t)(h->E + 1) * h->dp * 4, h->stream), "router")) return bad("");
+    auto put_rows = [&](float* dst, const float* src, int rows) {
+        const bool dev = is_device_ptr(src);
+        return h->cuda_ok(cudaMemcpy2DAsync(dst, (size_t)h->dp * 4, src, (size_t)h->d * 4, (size_t)h->d * 4, (size_t)rows,
+                                            dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, h->stream),
+                          "router upload");
+    };
+    if (d->router) {
+        h->has_router = 1;
+        if (!put_rows(h->router_ext, d->router, h->E)) return bad("");
+    }
+    if (h->has_shared && !put_rows(h->router_ext + (size_t)h->E * h->dp, d->shexp_gate_inp, 1)) return bad("");
+    if (d->router_bias) {
+        h->router_bias = (float*)h->dalloc((size_t)h->E * 4, kWeightsResident, "router bias");
+        if (!h->router_bias) return bad("");
+        if (!h->cuda_ok(cudaMemcpyAsync(h->router_bias, d->router_bias, (size_t)h->E * 4,
+                                        is_device_ptr(d->router_bias) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                                        h->stream),
+                        "router bias"))
+            return bad("");
+    }
+    // plan the whole upload before allocating (admit_plan, src/memory_guard.cpp:192-213)
+    {
+        size_t plan = 0;
+        auto fam = [&](int dt, int rows, int cols, int ne_) {
+            const int pr = dt == AERO_DT_F32 ? (int)round_up(rows, 16) : rows;
+            const int pc = dt == AERO_DT_F32 ? (int)round_up(cols, 16) : cols;
+            return (size_t)ne_ * (size_t)(align128((int64_t)pr * qm_row_qs_bytes(dt, pc)) +
+                                          align128((int64_t)pr * qm_row_meta_bytes(dt, pc)));
+        };
+        plan += 2 * fam(h->dtype, h->F, h->d, h->e_end - h->e_begin) + fam(h->dtype, h->d, h->F, h->e_end - h->e_begin);
+        if (h->has_shared) plan += 2 * fam(h->sh_dtype, h->Fs, h->d, 1) + fam(h->sh_dtype, h->d, h->Fs, 1);
+        char why2[256];
+        if (!aero_cuda_guard_admit_plan(plan, why2, sizeof(why2))) return bad(std::string("load refused: ") + why2);
+    }
+    if (!upload_family(*h, d->gate_exps, h->E, h->e_begin, h->e_end, h->F, h->d, h->Fp, h->dp, h->gate, "ffn_gate_exps"))
+        return bad("");
+    if (!upload_family(*h, d->up_exps, h->E, h->e_begin, h->e_end, h->F, h->d, h->Fp, h->dp, h->up, "ffn_up_exps"))
+        return bad("");
+    if (!upload_family(*h, d->down_exps, h->E, h->e_begin, h->e_end, h->d, h->F, h->dp, h->Fp, h->down, "ffn_down_exps"))
+        return bad("");
+    if (h->has_shared) {
+        if (!upload_family(*h, d->shexp_gate, 1, 0, 1, h->Fs, h->d, h->Fsp, h->dp, h->sg, "ffn_gate_shexp")) return bad("");
+        if (!upload_family(*h, d->shexp_up, 1, 0, 1, h->Fs, h->d, h->Fsp, h->dp, h->su, "ffn_up_shexp")) return bad("");
+        if (!upload_family(*h, d->shexp_down, 1, 0, 1, h->d, h->Fs, h->dp, h->Fsp, h->sd, "ffn_down_shexp")) return bad("");
+    }
+    if (!h->cuda_ok(cudaStreamSynchronize(h->stream), "upload")) return bad("");
+    // expert indices in the planes are local to [e_begin, e_end); the routed
+    // paths below index them by global expert id, so shift the plane bases.
+    auto shift = [&](QMat& m) {
+        m.qs -= (int64_t)h->e_begin * m.qs_estride;
+        if (m.meta) m.meta -= (int64_t)h->e_begin * m.meta_estride;
+    };
+    shift(h->gate);
+    shift(h->up);
+    shift(h->down);
+    return h;
+}
+
+}  // namespace
+}  // namespace aero
+
+using aero::Handle;
+
+extern "C" {
+
+void* aero_cuda_moe_open(const aero_cuda_moe_desc* desc, char* err, int errlen) {
+    std::string why;
+    Handle* h = aero::open_desc(desc, &why);
+    if (!h) aero::copy_err(why, err, errlen);
+    return h;
+}
+
+void aero_cuda_moe_close(void* handle) { delete static_cast<Handle*>(handle); }
+
+int aero_cuda_moe_forward(void* handle, int layer, const float* h_in, int T, int n_embd, float* out) {
+    (void)layer;
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return 0;
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (n_embd != h->d) {
+        h->fail("hidden width %d != n_embd %d", n_embd, h->d);
+        return 0;
+    }
+    if (h->e_begin != 0 || h->e_end != h->E) {
+        h->fail("this handle owns experts [%d, %d) only; use the expert-parallel entry points", h->e_begin, h->e_end);
+        return 0;
+    }
+    return aero::block_entry(*h, h_in, T, nullptr, out) ? 1 : 0;
+}
+
+int aero_cuda_moe_ffn_block(void* handle, const float* h_in, const float* router_logits, int T, float* out) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (!router_logits) {
+        h->fail("router_logits is required");
+        return -1;
+    }
+    if (h->e_begin != 0 || h->e_end != h->E) {
+        h->fail("this handle owns experts [%d, %d) only", h->e_begin, h->e_end);
+        return -1;
+    }
+    return aero::block_entry(*h, h_in, T, router_logits, out) ? 0 : -1;
+}
+
+int aero_cuda_moe_router_logits(void* handle, const float* x, int T, float* logits) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (!h->has_router) {
+        h->fail("this layer has no router weights");
+        return -1;
+    }
+    if (T <= 0) return T == 0 ? 0 : -1;
+    cudaSetDevice(h->device);
+    if (!aero::ensure_scratch(*h, T)) return -1;
+    auto& s = h->sc;
+    const bool xd = aero::is_device_ptr(x), ld = aero::is_device_ptr(logits);
+    if (!h->cuda_ok(cudaMemcpy2DAsync(s.x_stage, (size_t)h->dp * 4, x, (size_t)h->d * 4, (size_t)h->d * 4, (size_t)T,
+                                      xd ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, h->stream),
+                    "input copy"))
+        return -1;
+    if (!h->cuda_ok(aero::launch_router(s.x_stage, T, h->dp, h->router_ext, 0, h->E, h->router_bias, h->E, s.logits, h->E + 1,
+                                        h->stream),
+                    "router"))
+        return -1;
+    if (!h->cuda_ok(cudaMemcpy2DAsync(logits, (size_t)h->E * 4, s.logits, (size_t)(h->E + 1) * 4, (size_t)h->E * 4, (size_t)T,
+                                      ld ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, h->stream),
+                    "logits copy"))
+        return -1;
+    return h->cuda_ok(cudaStreamSynchronize(h->stream), "router") ? 0 : -1;
+}
+
+// Route T rows on a device, staging through guarded scratch.
+static int route_impl(const float* logits, int T, int E, int k, int norm, int64_t* idx, float* w, cudaStream_t st,
+                      std::string* err) {
+    if (k <= 0 || k > E) {
+        *err = "n_expert_used=" + std::to_string(k) + " out of range for " + std::to_string(E) + " experts";
+        return -1;
+    }
+    if (k > 32 || E > 1024) {
+        *err = "this implementation routes at most 32 of at most 1024 experts";
+        return -1;
+    }
+    if (T <= 0) return T == 0 ? 0 : -1;
+    const size_t lg_b = (size_t)T * E * 4, i_b = (size_t)T * k * 4, w_b = (size_t)T * k * 4, o_b = (size_t)T * k * 8;
+    const size_t total = lg_b + i_b + w_b + o_b + 1024;
+    void* base = nullptr;
+    if (aero::guarded_malloc(&base, total, aero::kScratch) != cudaSuccess) {
+        cudaGetLastError();
+        *err = "scratch allocation refused";
+        return -1;
+    }
+    char* b = (char*)base;
+    float* dlg = (float*)b;
+    int32_t* didx = (int32_t*)(b + ((lg_b + 255) & ~(size_t)255));
+    float* dw = (float*)((char*)didx + ((i_b + 255) & ~(size_t)255));
+    bool ok = cudaMemcpyAsync(dlg, logits, lg_b, aero::is_device_ptr(logits) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                              st) == cudaSuccess;
+    ok = ok && aero::launch_topk(dlg, E, T, E, k, norm, 0, nullptr, 0, didx, dw, nullptr, nullptr, st) == cudaSuccess;
+    std::vector<int32_t> hidx((size_t)T * k);
+    ok = ok && cudaMemcpyAsync(hidx.data(), didx, i_b, cudaMemcpyDeviceToHost, st) == cudaSuccess;
+    const bool w_dev = aero::is_device_ptr(w);
+    ok = ok && cudaMemcpyAsync(w, dw, w_b, w_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, st) == cudaSuccess;
+    ok = ok && cudaStreamSynchronize(st) == cudaSuccess;
+    if (ok) {
+        if (aero::is_device_ptr(idx)) {
+            std::vector<int64_t> tmp(hidx.begin(), hidx.end());
+            ok = cudaMemcpy(idx, tmp.data(), o_b, cudaMemcpyHostToDevice) == cudaSuccess;
+        } else {
+            for (size_t i = 0; i < hidx.size(); ++i) idx[i] = hidx[i];
+        }
+    }
+    if (!ok) {
+        *err = std::string("route: ") + cudaGetErrorString(cudaGetLastError());
+    }
+    aero::guarded_free(base, total, aero::kScratch);
+    return ok ? 0 : -1;
+}
+
+int aero_cuda_moe_route(void* handle, const float* logits, int T, int64_t* idx, float* w) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    cudaSetDevice(h->device);
+    return route_impl(logits, T, h->E, h->k, h->norm, idx, w, h->stream, &h->err);
+}
+
+int aero_cuda_route(const float* logits, int T, int n_expert, int k, int norm, int64_t* idx, float* w) {
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        aero::g_free_error = "no CUDA device is available (this library has no CPU path)";
+        return -1;
+    }
+    return route_impl(logits, T, n_expert, k, norm, idx, w, 0, &aero::g_free_error);
+}
+
+int aero_cuda_dispatch(const int64_t* idx, int T, int k, int n_expert, int32_t* offsets, int32_t* perm) {
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        aero::g_free_error = "no CUDA device is available (this library has no CPU path)";
+        return -1;
+    }
+    if (T < 0 || k <= 0 || n_expert <= 0) return -1;
+    const int P = T * k;
+    std::vector<int32_t> h32((size_t)P);
+    const bool dev_in = aero::is_device_ptr(idx);
+    std::vector<int64_t> h64;
+    const int64_t* src = idx;
+    if (dev_in) {
+        h64.resize((size_t)P);
+        if (cudaMemcpy(h64.data(), idx, (size_t)P * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+        src = h64.data();
+    }
+    for (int p = 0; p < P; ++p) {
+        if (src[p] < 0 || src[p] >= n_expert) {
+            aero::g_free_error = "expert index out of range";
+            return -1;
+        }
+        h32[(size_t)p] = (int32_t)src[p];
+    }
+    const size_t work = aero::dispatch_work_bytes(P, n_expert);
+    const size_t total = (size_t)P * 12 + (size_t)(n_expert * 3 + 8) * 4 + work + 2048;
+    void* base = nullptr;
+    if (aero::guarded_malloc(&base, total, aero::kScratch) != cudaSuccess) {
+        cudaGetLastError();
+        aero::g_free_error = "scratch allocation refused";
+        return -1;
+    }
+    char* b = (char*)base;
+    auto al = [](size_t v) { return (v + 255) & ~(size_t)255; };
+    int32_t* didx = (int32_t*)b;
+    int32_t* doff = (int32_t*)(b + al((size_t)P * 4));
+    int32_t* dperm = (int32_t*)((char*)doff + al((size_t)(n_expert + 1) * 4));
+    int32_t* dinv = (int32_t*)((char*)dperm + al((size_t)P * 4));
+    int32_t* dae = (int32_t*)((char*)dinv + al((size_t)P * 4));
+    int32_t* dao = (int32_t*)((char*)dae + al((size_t)n_expert * 4));
+    int32_t* dna = (int32_t*)((char*)dao + al((size_t)(n_expert + 1) * 4));
+    void* dw = (char*)dna + 256;
+    bool ok = cudaMemcpy(didx, h32.data(), (size_t)P * 4, cudaMemcpyHostToDevice) == cudaSuccess;
+    ok = ok && aero::launch_dispatch(didx, P, n_expert, doff, dperm, dinv, dae, dao, dna, dw, 0) == cudaSuccess;
+    ok = ok && cudaMemcpy(offsets, doff, (size_t)(n_expert + 1) * 4, cudaMemcpyDefault) == cudaSuccess;
+    ok = ok && (P == 0 || cudaMemcpy(perm, dperm, (size_t)P * 4, cudaMemcpyDefault) == cudaSuccess);
+    if (!ok) aero::g_free_error = std::string("dispatch: ") + cudaGetErrorString(cudaGetLastError());
+    aero::guarded_free(base, total, aero::kScratch);
+    return ok ? 0 : -1;
+}
+
+int aero_cuda_dequant(int dtype, const uint8_t* raw, int64_t raw_len, float* out, int64_t n) {
+    const int64_t bv = aero::dtype_block_values(dtype);
+    if (bv <= 0 || n < 0 || n % bv) return 0;
+    if (raw_len < aero::gguf_bytes(dtype, n)) return 0;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        aero::g_free_error = "no CUDA device is available (this library has no CPU path)";
+        return 0;
+    }
+    if (n == 0) return 1;
+    const size_t rb = (size_t)aero::gguf_bytes(dtype, n), ob = (size_t)n * 4;
+    void* base = nullptr;
+    const size_t total = ((rb + 255) & ~(size_t)255) + ob;
+    if (aero::guarded_malloc(&base, total, aero::kScratch) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    uint8_t* draw = (uint8_t*)base;
+    float* dout = (float*)((char*)base + ((rb + 255) & ~(size_t)255));
+    bool ok = cudaMemcpy(draw, raw, rb, cudaMemcpyDefault) == cudaSuccess;
+    ok = ok && aero::launch_dequant_gguf(dtype, draw, n, dout, 0) == cudaSuccess;
+    ok = ok && cudaMemcpy(out, dout, ob, cudaMemcpyDefault) == cudaSuccess;
+    if (!ok) cudaGetLastError();
+    aero::guarded_free(base, total, aero::kScratch);
+    return ok ? 1 : 0;
+}
+
+int aero_cuda_quantize(int dtype, const float* x, int64_t n, uint8_t* out, int64_t out_len) {
+    if (dtype != AERO_DT_Q8_0 && dtype != AERO_DT_Q4_K) return 0;
+    const int64_t bv = aero::dtype_block_values(dtype);
+    if (n < 0 || n % bv || out_len < aero::gguf_bytes(dtype, n)) return 0;
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        aero::g_free_error = "no CUDA device is available (this library has no CPU path)";
+        return 0;
+    }
+    if (n == 0) return 1;
+    const bool xd = aero::is_device_ptr(x), od = aero::is_device_ptr(out);
+    const size_t xb = (size_t)n * 4, ob = (size_t)aero::gguf_bytes(dtype, n);
+    void* base = nullptr;
+    size_t total = 0;
+    const float* dx = x;
+    uint8_t* dout = out;
+    if (!xd || !od) {
+        total = (xd ? 0 : ((xb + 255) & ~(size_t)255)) + (od ? 0 : ob);
+        if (aero::guarded_malloc(&base, total, aero::kScratch) != cudaSuccess) {
+            cudaGetLastError();
+            return 0;
+        }
+        char* b = (char*)base;
+        if (!xd) {
+            dx = (const float*)b;
+            b += (xb + 255) & ~(size_t)255;
+        }
+        if (!od) dout = (uint8_t*)b;
+    }
+    bool ok = xd || cudaMemcpy((void*)dx, x, xb, cudaMemcpyHostToDevice) == cudaSuccess;
+    ok = ok && aero::launch_quantize(dtype, dx, n, dout, 0) == cudaSuccess;
+    ok = ok && (od || cudaMemcpy(out, dout, ob, cudaMemcpyDeviceToHost) == cudaSuccess);
+    ok = ok && cudaDeviceSynchronize() == cudaSuccess;
+    if (!ok) cudaGetLastError();
+    if (base) aero::guarded_free(base, total, aero::kScratch);
+    return ok ? 1 : 0;
+}
+
+int aero_cuda_moe_set_stream(void* handle, void* stream) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    h->stream = stream ? (cudaStream_t)stream : h->own_stream;
+    return 0;
+}
+
+int aero_cuda_moe_set_profiling(void* handle, int on) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    cudaSetDevice(h->device);
+    if (on && !h->sev[0])
+        for (auto& e : h->sev)
+            if (cudaEventCreate(&e) != cudaSuccess) return -1;
+    h->profiling = on != 0;
+    for (int i = 0; i < Handle::kStages; ++i) {
+        h->stage_ms[i] = 0.0;
+        h->stage_n[i] = 0;
+    }
+    return 0;
+}
+
+int aero_cuda_moe_stage_times(void* handle, double* ms, int64_t* counts, int n) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    const int m = std::min(n, (int)Handle::kStages);
+    for (int i = 0; i < m; ++i) {
+        if (ms) ms[i] = h->stage_ms[i];
+        if (counts) counts[i] = h->stage_n[i];
+    }
+    return m;
+}
+
+int aero_cuda_moe_info(void* handle, int32_t* out8) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h || !out8) return -1;
+    const int32_t v[8] = {h->d, h->E, h->k, h->F, h->Fs, h->has_shared, h->dtype, h->norm};
+    std::memcpy(out8, v, sizeof(v));
+    return 0;
+}
+
+const char* aero_cuda_moe_last_error(void* handle) {
+    if (!handle) return aero::g_free_error.c_str();
+    return static_cast<Handle*>(handle)->err.c_str();
+}
+
+int aero_cuda_moe_stats(void* handle, char* buf, int len) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    size_t wbytes = 0;
+    for (auto& a : h->allocs) wbytes += a.bytes;
+    const int n = std::snprintf(buf, (size_t)std::max(0, len),
+                                "{\"calls\": %ld, \"tokens\": %ld, \"launches\": %ld, \"weight_bytes\": %zu, "
+                                "\"scratch_bytes\": %zu, \"scratch_tokens\": %d, \"guard_committed\": %zu, "
+                                "\"last_active\": %d, \"last_ms\": %.6f}",
+                                h->calls, h->tokens, h->launches, wbytes, h->sc.bytes, h->sc.cap_T,
+                                aero_cuda_guard_committed(-1), h->last_active, (double)h->last_ms);
+    return n;
+}
+
+int aero_cuda_device_count(void) {
+    int n = 0;
+    if (cudaGetDeviceCount(&n) != cudaSuccess) {
+        cudaGetLastError();
+        return 0;
+    }
+    return n;
+}
+
+}  // extern "C"

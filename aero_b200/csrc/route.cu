@@ -1,0 +1,358 @@
+// Router projection, top-k routing and expert dispatch.
+//
+// Routing follows src/moe.cpp:26-66: experts ranked by descending logit, equal
+// logits ranked by the lower expert index; with norm_topk_prob the k weights are
+// the softmax over the selected logits (max-subtracted, f32 exp), otherwise the
+// full-softmax probability with an f64 denominator over all experts.
+//
+// Dispatch (no reference counterpart — the reference loops token by token):
+// the T*k (token, slot) pairs, pair id p = t*k + s, are counting-sorted by
+// expert; inside an expert they keep pair order, i.e. (token, slot) order.
+#include <algorithm>
+
+#include <cub/block/block_scan.cuh>
+
+#include "internal.h"
+
+namespace aero {
+namespace {
+
+// ----------------------------------------------------------- router, small T
+// One warp per W row; the row is streamed once per group of 8 tokens.
+constexpr int kRouterTG = 8;
+
+__global__ void __launch_bounds__(256) router_gemv_kernel(const float* __restrict__ x, int T, int d,
+                                                          const float* __restrict__ W, int row_begin,
+                                                          int row_end, const float* __restrict__ bias,
+                                                          int n_bias, float* __restrict__ logits, int ld) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = row_begin + blockIdx.x * 8 + warp;
+    if (r >= row_end) return;
+    const float* wr = W + (int64_t)r * d;
+    const int n4 = d >> 2;
+    for (int t0 = 0; t0 < T; t0 += kRouterTG) {
+        float acc[kRouterTG];
+#pragma unroll
+        for (int i = 0; i < kRouterTG; ++i) acc[i] = 0.f;
+        for (int c = lane; c < n4; c += 32) {
+            const float4 wv = ld_f4(wr + 4 * c);
+#pragma unroll
+            for (int i = 0; i < kRouterTG; ++i) {
+                if (t0 + i < T) {
+                    const float4 xv = ld_f4(x + (int64_t)(t0 + i) * d + 4 * c);
+                    acc[i] = fmaf(wv.x, xv.x, acc[i]);
+                    acc[i] = fmaf(wv.y, xv.y, acc[i]);
+                    acc[i] = fmaf(wv.z, xv.z, acc[i]);
+                    acc[i] = fmaf(wv.w, xv.w, acc[i]);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < kRouterTG; ++i) {
+            const float v = warp_sum(acc[i]);
+            if (lane == 0 && t0 + i < T) logits[(int64_t)(t0 + i) * ld + r] = v + (r < n_bias && bias ? bias[r] : 0.f);
+        }
+    }
+}
+
+// ----------------------------------------------------------- router, large T
+// 64x64 output tile per CTA, 256 threads with a 4x4 micro-tile each, K in steps
+// of 16 through shared memory (both operands are K-major in global memory).
+constexpr int kSgBM = 64, kSgBN = 64, kSgBK = 16;
+
+__global__ void __launch_bounds__(256) router_sgemm_kernel(const float* __restrict__ x, int T, int d,
+                                                           const float* __restrict__ W, int row_begin,
+                                                           int row_end, const float* __restrict__ bias,
+                                                           int n_bias, float* __restrict__ logits, int ld) {
+    __shared__ float As[kSgBK][kSgBM + 4];
+    __shared__ float Bs[kSgBK][kSgBN + 4];
+    const int tid = threadIdx.x;
+    const int m0 = blockIdx.y * kSgBM, n0 = row_begin + blockIdx.x * kSgBN;
+    const int tm = (tid / 16) * 4, tn = (tid % 16) * 4;
+    float acc[4][4] = {};
+    // each thread loads one float4 of A and one of B per K step: 64 rows x 4 float4
+    const int lr = tid >> 2, lk = (tid & 3) * 4;
+    for (int k0 = 0; k0 < d; k0 += kSgBK) {
+        {
+            const int gm = m0 + lr;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (gm < T) v = ld_f4(x + (int64_t)gm * d + k0 + lk);
+            As[lk + 0][lr] = v.x;
+            As[lk + 1][lr] = v.y;
+            As[lk + 2][lr] = v.z;
+            As[lk + 3][lr] = v.w;
+            const int gn = n0 + lr;
+            float4 u = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (gn < row_end) u = ld_f4(W + (int64_t)gn * d + k0 + lk);
+            Bs[lk + 0][lr] = u.x;
+            Bs[lk + 1][lr] = u.y;
+            Bs[lk + 2][lr] = u.z;
+            Bs[lk + 3][lr] = u.w;
+        }
+        __syncthreads();
+#pragma unroll
+        for (int kk = 0; kk < kSgBK; ++kk) {
+            float a[4], b[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) a[i] = As[kk][tm + i];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) b[j] = Bs[kk][tn + j];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+#pragma unroll
+                for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const int gm = m0 + tm + i;
+        if (gm >= T) continue;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int gn = n0 + tn + j;
+            if (gn < row_end) logits[(int64_t)gm * ld + gn] = acc[i][j] + (gn < n_bias && bias ? bias[gn] : 0.f);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- top-k
+// One warp per token. Each lane owns experts lane, lane+32, ...; each round the
+// warp elects the best remaining (value desc, index asc) and removes it.
+constexpr int kTopkMaxPerLane = 32;  // E <= 1024
+
+__device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
+    // a ranks before b: larger logit, or equal logit and lower index. A NaN never
+    // ranks before a number (std::partial_sort with NaN is unspecified; this is
+    // one deterministic choice).
+    if (va > vb) return true;
+    if (va == vb) return ia < ib;
+    if (vb != vb && va == va) return true;
+    return false;
+}
+
+__global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int ld, int T, int E,
+                                                   int k, int norm, int has_shared,
+                                                   const float* __restrict__ x, int d, int32_t* __restrict__ idx,
+                                                   float* __restrict__ w, float* __restrict__ sgate,
+                                                   float* __restrict__ xsum16) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int t = blockIdx.x * 8 + warp;
+    if (t >= T) return;
+    const float* lg = logits + (int64_t)t * ld;
+    float v[kTopkMaxPerLane];
+    const int per = (E + 31) >> 5;
+#pragma unroll
+    for (int i = 0; i < kTopkMaxPerLane; ++i) {
+        const int e = lane + 32 * i;
+        v[i] = (i < per && e < E) ? lg[e] : 0.f;
+    }
+    uint32_t taken = 0;  // bit i: slot i of this lane removed (or absent)
+    for (int i = 0; i < kTopkMaxPerLane; ++i)
+        if (!(i < per && lane + 32 * i < E)) taken |= 1u << i;
+
+    float sel_v = 0.f;  // lane j keeps the j-th selected logit (j < k <= 32 handled in rounds)
+    float wsum = 0.f, mx = 0.f;
+    for (int r = 0; r < k; ++r) {
+        float bv = 0.f;
+        int bi = 0x7fffffff;
+#pragma unroll
+        for (int i = 0; i < kTopkMaxPerLane; ++i) {
+            if (taken & (1u << i)) continue;
+            const int e = lane + 32 * i;
+            if (bi == 0x7fffffff || better(v[i], e, bv, bi)) {
+                bv = v[i];
+                bi = e;
+            }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (oi != 0x7fffffff && (bi == 0x7fffffff || better(ov, oi, bv, bi))) {
+                bv = ov;
+                bi = oi;
+            }
+        }
+        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+        if (lane == 0) idx[(int64_t)t * k + r] = bi;
+        if (r == 0) mx = bv;
+        if ((r & 31) == lane) sel_v = bv;  // only valid for k <= 32 (checked by the host)
+    }
+    // weights
+    if (norm) {
+        // softmax over the selected logits; max is the first pick. Sum in
+        // selection order, as src/moe.cpp:47-53.
+        float e_mine = 0.f;
+        if (lane < k) e_mine = expf(sel_v - mx);
+        for (int r = 0; r < k; ++r) wsum += __shfl_sync(0xffffffffu, e_mine, r);
+        if (lane < k) w[(int64_t)t * k + lane] = e_mine / wsum;
+    } else {
+        double den = 0.0;
+#pragma unroll
+        for (int i = 0; i < kTopkMaxPerLane; ++i) {
+            const int e = lane + 32 * i;
+            if (i < per && e < E) den += (double)expf(v[i] - mx);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
+        if (lane < k) w[(int64_t)t * k + lane] = (float)((double)expf(sel_v - mx) / den);
+    }
+    if (has_shared && lane == 0) sgate[t] = sigmoid_f(lg[E]);
+    if (xsum16) {
+        const float* xt = x + (int64_t)t * d;
+        for (int g = lane; g < d / 16; g += 32) {
+            float s = 0.f;
+#pragma unroll
+            for (int i = 0; i < 16; i += 4) {
+                const float4 q = ld_f4(xt + 16 * g + i);
+                s += q.x;
+                s += q.y;
+                s += q.z;
+                s += q.w;
+            }
+            xsum16[(int64_t)t * (d / 16) + g] = s;
+        }
+    }
+}
+
+// ---------------------------------------------------------------- dispatch
+// Chunks of kDispChunk pairs. count: per-chunk per-expert histogram; scan:
+// per-expert running offsets over chunks plus the expert prefix; scatter: each
+// chunk is walked in pair order by one warp, 32 pairs at a time, ranking equal
+// experts with __match_any_sync, so the result is stable.
+constexpr int kDispChunk = 256;
+
+__global__ void dispatch_count_kernel(const int32_t* __restrict__ idx, int P, int E,
+                                      int32_t* __restrict__ counts) {
+    extern __shared__ int32_t hist[];
+    for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
+    __syncthreads();
+    const int p0 = blockIdx.x * kDispChunk;
+    for (int p = p0 + threadIdx.x; p < min(P, p0 + kDispChunk); p += blockDim.x) atomicAdd(&hist[idx[p]], 1);
+    __syncthreads();
+    for (int e = threadIdx.x; e < E; e += blockDim.x) counts[(int64_t)blockIdx.x * E + e] = hist[e];
+}
+
+constexpr int kScanThreads = 1024;
+
+__global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(int32_t* __restrict__ counts, int n_chunks,
+                                                                     int E, int P, int32_t* __restrict__ offsets,
+                                                                     int32_t* __restrict__ act_e,
+                                                                     int32_t* __restrict__ act_off,
+                                                                     int32_t* __restrict__ n_active) {
+    using Scan = cub::BlockScan<int, kScanThreads>;
+    __shared__ typename Scan::TempStorage tmp;
+    __shared__ int carry_tot, carry_act;
+    if (threadIdx.x == 0) {
+        carry_tot = 0;
+        carry_act = 0;
+    }
+    __syncthreads();
+    for (int e0 = 0; e0 < E; e0 += kScanThreads) {
+        const int e = e0 + threadIdx.x;
+        int tot = 0;
+        if (e < E) {
+            // counts[c][e] becomes the within-expert exclusive prefix over chunks
+            for (int c = 0; c < n_chunks; ++c) {
+                const int v = counts[(int64_t)c * E + e];
+                counts[(int64_t)c * E + e] = tot;
+                tot += v;
+            }
+        }
+        int excl, excl_act;
+        Scan(tmp).ExclusiveSum(tot, excl);
+        __syncthreads();
+        Scan(tmp).ExclusiveSum(tot > 0 ? 1 : 0, excl_act);
+        const int base = carry_tot, abase = carry_act;
+        if (e < E) {
+            offsets[e] = base + excl;
+            if (tot > 0) {
+                act_e[abase + excl_act] = e;
+                act_off[abase + excl_act] = base + excl;
+            }
+        }
+        __syncthreads();
+        if (threadIdx.x == kScanThreads - 1) {
+            carry_tot = base + excl + tot;
+            carry_act = abase + excl_act + (tot > 0 ? 1 : 0);
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        offsets[E] = P;
+        act_off[carry_act] = P;
+        *n_active = carry_act;
+    }
+}
+
+__global__ void dispatch_scatter_kernel(const int32_t* __restrict__ idx, int P, int E,
+                                        const int32_t* __restrict__ offsets,
+                                        const int32_t* __restrict__ counts, int32_t* __restrict__ perm,
+                                        int32_t* __restrict__ inv) {
+    extern __shared__ int32_t cursor[];  // per expert, for this chunk
+    const int chunk = blockIdx.x;
+    for (int e = threadIdx.x; e < E; e += blockDim.x) cursor[e] = offsets[e] + counts[(int64_t)chunk * E + e];
+    __syncthreads();
+    if (threadIdx.x >= 32) return;
+    const int lane = threadIdx.x;
+    const int p_end = min(P, (chunk + 1) * kDispChunk);
+    for (int base = chunk * kDispChunk; base < p_end; base += 32) {
+        const int p = base + lane;
+        const bool valid = p < p_end;
+        const int e = valid ? idx[p] : -1 - lane;  // invalid lanes never match a real expert
+        const unsigned peers = __match_any_sync(0xffffffffu, e);
+        const int rank = __popc(peers & ((1u << lane) - 1u));
+        int pos = 0;
+        if (valid) pos = cursor[e] + rank;
+        __syncwarp();
+        if (valid) {
+            perm[pos] = p;
+            inv[p] = pos;
+            // the highest peer advances the cursor past the whole group
+            if ((peers >> lane) == 1u) cursor[e] = pos + 1;
+        }
+        __syncwarp();
+    }
+}
+
+}  // namespace
+
+cudaError_t launch_router(const float* x, int T, int d, const float* W, int row_begin, int row_end,
+                          const float* bias, int n_bias, float* logits, int ld, cudaStream_t s) {
+    const int rows = row_end - row_begin;
+    if (rows <= 0 || T <= 0) return cudaSuccess;
+    if (T <= 32) {
+        router_gemv_kernel<<<(rows + 7) / 8, 256, 0, s>>>(x, T, d, W, row_begin, row_end, bias, n_bias, logits, ld);
+    } else {
+        dim3 grid((rows + kSgBN - 1) / kSgBN, (T + kSgBM - 1) / kSgBM);
+        router_sgemm_kernel<<<grid, 256, 0, s>>>(x, T, d, W, row_begin, row_end, bias, n_bias, logits, ld);
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int norm, int has_shared,
+                        const float* x, int d, int32_t* idx, float* w, float* sgate, float* xsum16,
+                        cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    topk_kernel<<<(T + 7) / 8, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, x, d, idx, w, sgate, xsum16);
+    return cudaGetLastError();
+}
+
+size_t dispatch_work_bytes(int P, int E) {
+    const size_t n_chunks = (size_t)(P + kDispChunk - 1) / kDispChunk;
+    return std::max<size_t>(1, n_chunks) * (size_t)E * sizeof(int32_t);
+}
+
+cudaError_t launch_dispatch(const int32_t* idx, int P, int E, int32_t* offsets, int32_t* perm, int32_t* inv,
+                            int32_t* act_e, int32_t* act_off, int32_t* n_active, void* work, cudaStream_t s) {
+    const int n_chunks = std::max(1, (P + kDispChunk - 1) / kDispChunk);
+    int32_t* counts = static_cast<int32_t*>(work);
+    const size_t hist_smem = (size_t)E * sizeof(int32_t);
+    dispatch_count_kernel<<<n_chunks, 256, hist_smem, s>>>(idx, P, E, counts);
+    dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(counts, n_chunks, E, P, offsets, act_e, act_off, n_active);
+    dispatch_scatter_kernel<<<n_chunks, 128, hist_smem, s>>>(idx, P, E, offsets, counts, perm, inv);
+    return cudaGetLastError();
+}
+
+}  // namespace aero

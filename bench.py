@@ -1,0 +1,339 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 MoE FFN layer (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c5] [--impl ours|reference]
+
+Metric: MoE-layer tokens/s. The default workload is config 5
+(512 experts top-10 + shared expert, Q4_K, 8192-token prefill): the metric is
+quoted at 1/2/4/8 GPUs and config 5 is the configuration defined at those
+counts. A step is one layer call over the workload's tokens (config 1: 64
+one-token calls). Inputs are synthetic (seeded N(0,1) activations, N(0,0.02)
+weights quantised to GGUF blocks); no datasets or checkpoints exist here.
+
+  value        tokens/s over K steps, inputs already in HBM, device time by
+               CUDA events on the layer's stream (max over ranks)
+  e2e          the same through the public API with host buffers: pinned
+               host input -> device, layer, device -> pinned host output
+  roofline     the dominant kernel: algorithmic bytes (GGUF bytes of the
+               experts it streams) / its average duration from per-stage
+               CUDA events, against MEASURED_PEAKS.json
+  cpu_baseline the reference's own MoE block (oracle/_ref, built from its
+               sources) on the host cores, over a bounded token sample
+The working set (weights >= 340 MB) exceeds the 126 MB L2, so no flush runs
+between steps.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+PEAKS_FALLBACK = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "source": "fallback"}
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        d["source"] = "measured"
+        return d
+    return dict(PEAKS_FALLBACK)
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.device = device
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            threading.Thread(target=self._read, daemon=True).start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], 0.0, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 7:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                mx = max(mx, float(parts[1]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[3:7]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return ws, rank, local
+
+
+def layer_bytes(spec):
+    from aero_b200.quant import type_size
+    per_expert = 3 * type_size(spec.dtype, spec.F * spec.d)
+    shared = 3 * type_size(spec.dtype, spec.Fs * spec.d) if spec.Fs else 0
+    return per_expert, shared
+
+
+def cpu_reference(wl, layer, x, logits, budget_s: float, threads: int):
+    """Time the reference's own block (or the C restatement when the reference
+    objects are absent) on a bounded token sample. Returns (tokens/s, kind, sample, threads)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    kind = "reference" if O.ref_available() else "port"
+    fn = O.ref_block if kind == "reference" else O.moe_block
+    if kind == "reference" and layer.shexp and layer.shexp["ffn_len"] != wl.spec.F:
+        kind, fn = "port", O.moe_block
+    n = min(max(threads, 1), x.shape[0])
+    t0 = time.perf_counter()
+    fn(layer, x[:n], logits[:n], nthreads=threads)
+    dt = time.perf_counter() - t0
+    # grow the sample towards the time budget
+    while dt < budget_s / 4 and n < x.shape[0]:
+        n = min(x.shape[0], n * 4)
+        t0 = time.perf_counter()
+        fn(layer, x[:n], logits[:n], nthreads=threads)
+        dt = time.perf_counter() - t0
+    return n / dt, kind, n, dt
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--workload", default="c5")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    ws, rank, local = dist_env()
+    import torch
+    from aero_b200 import synth
+    from aero_b200 import native_cuda as nc
+
+    wl = synth.CONFIGS[args.workload]
+    spec = wl.spec
+    T = wl.T
+    seed = 0
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        x = synth.make_x(T * wl.calls, spec.d, seed, bf16=wl.bf16_x)
+        layer = synth.make_layer(spec, seed, device_gen=torch.cuda.is_available())
+        if wl.zipf_s:
+            synth.attach_zipf(layer, x, wl.zipf_s, seed)
+        lg = x @ layer.router.T + (layer.router_bias if layer.router_bias is not None else 0)
+        threads = os.cpu_count() or 1
+        per_step = max(1.0, 120.0 / (args.steps + args.warmup))
+        times = []
+        for i in range(args.warmup + args.steps):
+            tps, kind, n, dt = cpu_reference(wl, layer, x, lg.astype(np.float32), per_step, threads)
+            if i >= args.warmup:
+                times.append((n, dt))
+        n_tot = sum(n for n, _ in times)
+        t_tot = sum(dt for _, dt in times)
+        v = n_tot / t_tot
+        print(json.dumps({
+            "impl": "reference", "metric": "moe_layer_tokens_per_s", "value": v, "unit": "tokens/s",
+            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000.0 * t_tot / args.steps, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": wl.name, "tokens_per_step": T * wl.calls, "experts": spec.E, "top_k": spec.k,
+                       "d": spec.d, "ffn": spec.F, "shared_ffn": spec.Fs, "quant": "Q8_0" if spec.dtype == 8 else "Q4_K"},
+            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": kind,
+                             "sample": f"{times[-1][0]} tokens of {T * wl.calls} per step"},
+            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
+        return
+
+    nc.lib()
+    nc.require_gpu()
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import datetime
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    dev = local
+
+    x_host = synth.make_x(T * wl.calls, spec.d, seed, bf16=wl.bf16_x)
+    layer = synth.make_layer(spec, seed, device_gen=True)
+    if wl.zipf_s:
+        synth.attach_zipf(layer, x_host, wl.zipf_s, seed)
+    L = synth.open_layer(layer, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+    L.set_stream(stream)
+
+    x_dev = torch.from_numpy(x_host).to(f"cuda:{dev}")
+    out_dev = torch.empty_like(x_dev)
+    lib = nc.lib()
+
+    def step_device():
+        for c in range(wl.calls):
+            xs = x_dev[c * T:(c + 1) * T]
+            os_ = out_dev[c * T:(c + 1) * T]
+            if lib.aero_cuda_moe_forward(L.handle, 0, xs.data_ptr(), T, spec.d, os_.data_ptr()) != 1:
+                raise RuntimeError(nc.last_error(L.handle))
+
+    # ---- value: device-resident inputs
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step_device()
+    stream.synchronize()
+    launches0 = L.stats()["launches"]
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(dev) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step_device()
+        ev1.record(stream)
+        ev1.synchronize()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    launches = L.stats()["launches"] - launches0
+    if ws > 1:
+        t = torch.tensor([ms], device=f"cuda:{dev}")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+        torch.distributed.barrier()
+    tokens_per_step = T * wl.calls * ws
+    value = tokens_per_step * args.steps / (ms / 1000.0)
+
+    # ---- e2e: host buffers through the public API
+    xh = torch.from_numpy(x_host).pin_memory()
+    oh = torch.empty_like(xh).pin_memory()
+
+    def step_host():
+        for c in range(wl.calls):
+            if lib.aero_cuda_moe_forward(L.handle, 0, xh[c * T:(c + 1) * T].data_ptr(), T, spec.d,
+                                         oh[c * T:(c + 1) * T].data_ptr()) != 1:
+                raise RuntimeError(nc.last_error(L.handle))
+
+    for _ in range(args.warmup):
+        step_host()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step_host()
+    e1.record(stream)
+    e1.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    e2e_value = T * wl.calls * ws * args.steps / (e2e_ms / 1000.0)
+
+    # ---- per-stage device times (a separate profiled pass)
+    L.set_profiling(True)
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.steps // 2)):
+            step_device()
+    stream.synchronize()
+    st = L.stage_times()
+    active = L.stats()["last_active"]
+    L.set_profiling(False)
+    stage_avg = {k: (v[0] / v[1] if v[1] else 0.0) for k, v in st.items()}
+    per_expert, shared = layer_bytes(spec)
+    per_mat = per_expert // 3
+    # dominant stage and its algorithmic bytes
+    dom = max(stage_avg, key=stage_avg.get)
+    alg = {
+        "gate_up": active * 2 * per_mat + (2 * shared // 3 if shared else 0),
+        "down": active * per_mat + (shared // 3 if shared else 0),
+        "router": (spec.E + (1 if spec.Fs else 0)) * spec.d * 4 + T * spec.d * 4,
+        "topk": T * (spec.E + 1) * 4,
+        "dispatch": T * spec.k * 16,
+        "combine": (T * spec.k + T) * spec.d * 4 + T * spec.d * 4,
+    }[dom]
+    pk = peaks()
+    achieved = alg / (stage_avg[dom] / 1000.0) / 1e9
+    result = {
+        "metric": "moe_layer_tokens_per_s",
+        "value": value,
+        "unit": "tokens/s",
+        "n_gpus": ws,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms / args.steps,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": wl.name, "tokens_per_step": tokens_per_step, "experts": spec.E, "top_k": spec.k,
+                   "d": spec.d, "ffn": spec.F, "shared_ffn": spec.Fs,
+                   "quant": "Q8_0" if spec.dtype == 8 else "Q4_K", "routing": f"zipf{wl.zipf_s}" if wl.zipf_s else "uniform",
+                   "parallelism": f"ep{ws}" if ws > 1 else "single",
+                   "l2": "no flush: expert weights exceed the 126 MB L2"},
+        "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(x_host.nbytes),
+                "d2h_bytes_per_step": int(x_host.nbytes)},
+        "gpu_launches": int(launches),
+        "clocks": clk.summary(),
+        "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_source": pk["source"],
+                     "algorithmic_bytes": int(alg), "avg_ms": stage_avg[dom], "active_experts": active},
+        "stages_ms": {k: round(v, 5) for k, v in stage_avg.items()},
+    }
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        lg = x_host @ layer.router.T + (layer.router_bias if layer.router_bias is not None else 0)
+        threads = os.cpu_count() or 1
+        tps, kind, n, dt = cpu_reference(wl, layer, x_host, lg.astype(np.float32), args.cpu_seconds, threads)
+        result["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": kind,
+                                  "sample": f"{n} of {T * wl.calls} tokens, {dt:.1f} s"}
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+    L.close()
+    if ws > 1:
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

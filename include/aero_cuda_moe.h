@@ -1,0 +1,181 @@
+/*
+ * aero_cuda_moe — B200 (sm_100a) mixture-of-experts FFN library, plain C ABI.
+ *
+ * Drop-in replacement for the MoE FFN path of the Aero engine. The reference
+ * interfaces each entry point replaces are cited beside it (paths within the
+ * Aero project). Conventions kept from the reference:
+ *   - caller-owned, contiguous, row-major f32 buffers (include/aero/moe.hpp:43-52);
+ *   - aero_moe_* style calls return 0 on success and -1 on refusal
+ *     (include/aero/moe.hpp:17-18); the block hook returns non-zero on success
+ *     (src/model.cpp:169); dequant returns 1 on success (src/kernels.cpp:591);
+ *   - ggml type ids: 0 F32, 1 F16, 8 Q8_0, 12 Q4_K (engine/native.py:23-30).
+ * Pointers to activations may be host or device memory; the library checks with
+ * cudaPointerGetAttributes. With host pointers a call returns when the result is
+ * in the caller's buffer. With device pointers a call is ordered on the handle's
+ * stream and returns once the work is enqueued.
+ * There is no CPU fallback: every compute call runs on the GPU or is refused.
+ */
+#ifndef AERO_CUDA_MOE_H
+#define AERO_CUDA_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define AERO_CUDA_DTYPE_F32 0
+#define AERO_CUDA_DTYPE_F16 1
+#define AERO_CUDA_DTYPE_Q8_0 8
+#define AERO_CUDA_DTYPE_Q4_K 12
+
+/* One tensor given as GGUF bytes (host or device memory). */
+typedef struct aero_cuda_tensor {
+    int32_t dtype;
+    int32_t reserved;
+    const void* data;
+    int64_t nbytes;
+} aero_cuda_tensor;
+
+/* Layer description for aero_cuda_moe_open. Shapes are row-major (out, in):
+ * gate/up (n_expert, ffn_len, n_embd), down (n_expert, n_embd, ffn_len),
+ * router (n_expert, n_embd) f32, shexp gate/up (ffn_len_shared, n_embd),
+ * shexp down (n_embd, ffn_len_shared), shexp_gate_inp (n_embd,) f32.
+ * Mirrors the tensors engine/moe.py:5-12 lists and MoeConfig
+ * (engine/moe.py:46-57). */
+typedef struct aero_cuda_moe_desc {
+    int32_t n_embd, n_expert, n_expert_used, ffn_len;
+    int32_t norm_topk_prob, has_shared, ffn_len_shared, device;
+    /* Expert-parallel ownership: this handle uploads and computes experts
+     * [expert_begin, expert_end); 0,0 means all. Routing is over all experts. */
+    int32_t expert_begin, expert_end;
+    int32_t reserved[6];
+    aero_cuda_tensor gate_exps, up_exps, down_exps;
+    const float* router;         /* may be NULL: then only the *_ffn_block and route calls work */
+    const float* router_bias;    /* (n_expert,) added to the logits, or NULL */
+    const float* shexp_gate_inp; /* required when has_shared */
+    aero_cuda_tensor shexp_gate, shexp_up, shexp_down;
+} aero_cuda_moe_desc;
+
+/* Open a layer: upload the experts once into device-resident, expert-major,
+ * 128-byte-aligned quant-block planes. Every device allocation is charged to
+ * the memory guard below; a refusal returns NULL with the reason in err.
+ * Replaces the per-token fetch path engine/model.py:523-547 + 651-678. */
+void* aero_cuda_moe_open(const aero_cuda_moe_desc* desc, char* err, int errlen);
+
+/* Open layer `layer` straight from a GGUF file (mmap), reading
+ * blk.<layer>.ffn_{gate_inp,gate_exps,up_exps,down_exps}.weight and the
+ * optional shared-expert tensors, expert_count/expert_used_count from the
+ * metadata, norm_topk_prob = 1 (engine/model.py:193-224). Replaces
+ * GgufReader (src/gguf.cpp:150-275) + GGUFReader.tensor_rows
+ * (engine/gguf.py:297-314) on this path. */
+void* aero_cuda_moe_open_gguf(const char* path, int layer, int device, int expert_begin,
+                              int expert_end, char* err, int errlen);
+
+void aero_cuda_moe_close(void* handle);
+
+/* The block hook: exactly the aero_moe_fn signature (include/aero/model.hpp:83-84,
+ * 176-177), so aero_model_set_moe(model, aero_cuda_moe_forward, handle) plugs it
+ * in. Router logits are computed on the device from the layer's router
+ * (engine/model.py:665-666). `layer` is not used to select weights (one handle
+ * per layer). Returns 1 on success, 0 on refusal (src/model.cpp:169). */
+int aero_cuda_moe_forward(void* handle, int layer, const float* h, int T, int n_embd, float* out);
+
+/* The block with caller-supplied router logits (T, n_expert): the contract of
+ * aero_moe_ffn_block (include/aero/moe.hpp:43-52) with the experts already
+ * resident. Returns 0 on success, -1 on refusal. */
+int aero_cuda_moe_ffn_block(void* handle, const float* h, const float* router_logits, int T, float* out);
+
+/* Router logits only, (T, n_expert): exposes the router kernel for the two-level
+ * routing parity check. 0 / -1. */
+int aero_cuda_moe_router_logits(void* handle, const float* h, int T, float* logits);
+
+/* Batched top-k over (T, n_expert) logits with the handle's k and
+ * norm_topk_prob; idx (T, k) int64, w (T, k) f32. aero_moe_route
+ * (include/aero/moe.hpp:17-18) applied to T rows. 0 / -1. */
+int aero_cuda_moe_route(void* handle, const float* logits, int T, int64_t* idx, float* w);
+
+/* Handle-free batched aero_moe_route (src/moe.cpp:26-66): ties go to the lower
+ * index; refuses k outside [1, n_expert], and (a limit of this implementation)
+ * k > 32 or n_expert > 1024. 0 / -1. */
+int aero_cuda_route(const float* logits, int T, int n_expert, int k, int norm_topk_prob,
+                    int64_t* idx, float* w);
+
+/* Dispatch permutation of the T*k (token, slot) pairs of idx (T, k): offsets
+ * (n_expert + 1) is the exclusive prefix sum of per-expert counts and perm (T*k)
+ * lists pair ids t*k+s ordered by (expert, token, slot). No reference
+ * counterpart (the reference routes token by token, src/moe.cpp:136-154).
+ * 0 / -1. */
+int aero_cuda_dispatch(const int64_t* idx, int T, int k, int n_expert, int32_t* offsets,
+                       int32_t* perm);
+
+/* GGUF dequantisation to f32, bit-identical to aero_dequant_ref
+ * (src/kernels.cpp:591-606) for Q8_0, Q4_K and F32. 1 ok / 0 refusal (unknown
+ * type, n not whole blocks, raw_len too short). */
+int aero_cuda_dequant(int dtype, const uint8_t* raw, int64_t raw_len, float* out, int64_t n_values);
+
+/* Block quantiser for Q8_0 / Q4_K (no reference counterpart: the reference only
+ * reads these formats). Bytes equal aero_b200.quant.quantize. 1 ok / 0. */
+int aero_cuda_quantize(int dtype, const float* x, int64_t n_values, uint8_t* out, int64_t out_len);
+
+/* Per-stage device timing with CUDA events on the handle's stream (router,
+ * top-k, dispatch, gate/up, down, combine). While on, each call waits for its
+ * own events. stage_times returns the accumulated milliseconds and call
+ * counts per stage since profiling was switched on. */
+int aero_cuda_moe_set_profiling(void* handle, int on);
+int aero_cuda_moe_stage_times(void* handle, double* ms, int64_t* counts, int n);
+
+/* Run the handle's work on this cudaStream_t (NULL: the handle's own stream). */
+int aero_cuda_moe_set_stream(void* handle, void* stream);
+/* Layer geometry: out[0..7] = n_embd, n_expert, n_expert_used, ffn_len,
+ * ffn_len_shared, has_shared, expert dtype, norm_topk_prob. */
+int aero_cuda_moe_info(void* handle, int32_t* out8);
+/* Last error of a handle, or of the handle-free calls when handle is NULL. */
+const char* aero_cuda_moe_last_error(void* handle);
+/* JSON record: calls, tokens, device bytes by class, last call device time. */
+int aero_cuda_moe_stats(void* handle, char* buf, int len);
+int aero_cuda_device_count(void);
+
+/* ---------------------------------------------------------------- guard
+ * Device memory guard (src/memory_guard.cpp, include/aero/memory_guard.hpp):
+ * classes 0 weights-resident, 1 weights-cache, 2 kv-cache, 3 scratch,
+ * 4 runtime; -1 in aero_cuda_guard_committed means the total. */
+void aero_cuda_guard_set_budget(size_t bytes);
+size_t aero_cuda_guard_budget(void);
+size_t aero_cuda_guard_committed(int cls);
+size_t aero_cuda_guard_headroom(void);
+int aero_cuda_guard_try_reserve(size_t bytes, int cls);
+void aero_cuda_guard_release(size_t bytes, int cls);
+int aero_cuda_guard_admit_plan(size_t planned, char* why, int why_len);
+typedef size_t (*aero_cuda_evict_fn)(void* ctx, size_t need);
+void aero_cuda_guard_set_evictor(aero_cuda_evict_fn fn, void* ctx);
+void aero_cuda_guard_fail_nth_alloc(long n);
+size_t aero_cuda_guard_own_footprint(int device);
+size_t aero_cuda_guard_device_free(int device);
+int aero_cuda_guard_preflight(int device, size_t headroom);
+typedef void (*aero_cuda_breach_fn)(void* ctx, size_t footprint, size_t budget);
+void aero_cuda_guard_set_on_breach(aero_cuda_breach_fn fn, void* ctx);
+int aero_cuda_guard_exceeded(void);
+size_t aero_cuda_guard_peak_footprint(void);
+void aero_cuda_guard_reset_exceeded(void);
+void aero_cuda_guard_start_monitor(int device, unsigned interval_ms);
+void aero_cuda_guard_stop_monitor(void);
+/* LoadGate (src/memory_guard.cpp:314-378). */
+void* aero_cuda_loadgate_open(size_t planned, int device);
+void aero_cuda_loadgate_close(void* gate);
+void aero_cuda_loadgate_set_pause_ms(void* gate, unsigned ms);
+int aero_cuda_loadgate_next_chunk(void* gate, size_t chunk, int cls);
+int aero_cuda_loadgate_pause_and_check(void* gate);
+int aero_cuda_loadgate_ok(void* gate);
+int aero_cuda_loadgate_done(void* gate);
+size_t aero_cuda_loadgate_taken(void* gate);
+size_t aero_cuda_loadgate_reserved(void* gate);
+size_t aero_cuda_loadgate_remaining(void* gate);
+int aero_cuda_loadgate_reason(void* gate, char* buf, int len);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* AERO_CUDA_MOE_H */

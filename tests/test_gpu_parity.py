@@ -1,0 +1,315 @@
+"""GPU parity: the CUDA library through its C ABI against the oracle and the
+reference's golden vectors.
+
+Bars (from the task's north star): routed expert indices and the dispatch
+permutation are bit-exact on identical logits; dequantised values are
+bit-exact; layer outputs are within max-abs-error 2e-3 x RMS(output) for the
+fp32-accumulated decode path and 1e-2 x RMS for the bf16-dequantised prefill
+path.
+"""
+
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from aero_b200 import moe as M
+from aero_b200 import native_cuda as nc
+from aero_b200 import quant as Q
+from aero_b200 import synth
+from golden_blocks import block
+
+pytestmark = pytest.mark.gpu
+
+DECODE_TOL = 2e-3
+PREFILL_TOL = 1e-2
+
+
+def rms(a):
+    return float(np.sqrt(np.mean(np.asarray(a, np.float64) ** 2)))
+
+
+def rel_err(got, want):
+    return float(np.abs(np.asarray(got, np.float64) - want).max()) / max(rms(want), 1e-12)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib(cuda_lib):
+    nc.require_gpu()
+
+
+# ---------------------------------------------------------------- dequant / quant
+def test_dequant_bit_exact_vs_reference(golden):
+    for name in ("q8_random", "q4k_random", "q8_quantised", "q4k_quantised"):
+        raw = golden[f"deq_{name}_raw"].tobytes()
+        want = golden[f"deq_{name}_out"]
+        got = nc.dequant(int(golden[f"deq_{name}_dtype"]), raw, want.size)
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), name
+
+
+def test_dequant_refuses_short_buffer():
+    with pytest.raises(ValueError):
+        nc.dequant(Q.DTYPE_Q4_K, b"\0" * 100, 256)
+
+
+def test_quantize_gpu_equals_host():
+    rng = np.random.default_rng(5)
+    x = (rng.standard_normal(256 * 300) * 0.02).astype(np.float32)
+    x[:256] = 0.0
+    x[256:512] = np.abs(x[256:512])  # a super-block with no negative values
+    x[512:768] *= 50.0
+    for dt in (Q.DTYPE_Q8_0, Q.DTYPE_Q4_K):
+        assert nc.quantize(dt, x) == Q.quantize(x, dt), dt
+
+
+# ---------------------------------------------------------------- routing
+def test_route_matches_reference_cases(golden):
+    for name in golden["route_names"]:
+        lg = golden[f"route_{name}_logits"]
+        k = int(golden[f"route_{name}_k"])
+        for norm in (1, 0):
+            idx, w = nc.route(lg, lg.size, k, bool(norm))
+            assert np.array_equal(idx, golden[f"route_{name}_n{norm}_idx"]), (name, norm)
+            np.testing.assert_allclose(w, golden[f"route_{name}_n{norm}_w"], rtol=2e-6, atol=1e-7)
+
+
+def test_route_batched_bit_exact_with_ties():
+    rng = np.random.default_rng(6)
+    for T, E, k in ((1, 128, 8), (33, 128, 8), (257, 512, 10), (40, 24, 24), (5, 1024, 32)):
+        lg = (np.round(rng.standard_normal((T, E)) * 4) / 4).astype(np.float32)  # heavy ties
+        lg[0, :] = 0.0
+        for norm in (True, False):
+            idx, w = nc.route(lg, E, k, norm)
+            ridx, rw = O.route(lg, k, norm)
+            assert np.array_equal(idx, ridx), (T, E, k, norm)
+            np.testing.assert_allclose(w, rw, rtol=2e-6, atol=1e-7)
+
+
+def test_route_refusals():
+    with pytest.raises(ValueError):
+        nc.route(np.zeros(4, np.float32), 4, 0)
+    with pytest.raises(ValueError):
+        nc.route(np.zeros(4, np.float32), 4, 5)
+    idx, _ = nc.route(np.zeros(4, np.float32), 4, 4)
+    assert list(idx) == [0, 1, 2, 3]
+
+
+def test_dispatch_bit_exact():
+    rng = np.random.default_rng(7)
+    for T, k, E in ((1, 8, 128), (32, 10, 512), (512, 8, 128), (8192, 10, 512), (3, 2, 1000)):
+        idx = rng.integers(0, E, size=(T, k))
+        if T >= 512:  # skewed load, an empty expert and a dominant one
+            idx[: T // 2, 0] = 3
+            idx[idx == 5] = 6
+        off, perm = nc.dispatch(idx, E)
+        roff, rperm = O.dispatch(idx, E)
+        assert np.array_equal(off, roff) and np.array_equal(perm, rperm), (T, k, E)
+
+
+# ---------------------------------------------------------------- blocks
+def test_golden_blocks_ffn_block(golden):
+    """Caller logits (identical to the reference's) -> the reference's outputs."""
+    for name in golden["block_names"]:
+        layer, g = block(golden, name)
+        L = synth.open_layer(layer)
+        try:
+            out = L.ffn_block(g["x"], g["logits"])
+        finally:
+            L.close()
+        assert rel_err(out, g["out"]) <= DECODE_TOL, name
+
+
+def test_golden_blocks_device_router(golden):
+    """Router on the device: idx must equal the reference's on its logits
+    unless a near-tie flips (checked against f64 logits), then outputs match."""
+    for name in golden["block_names"]:
+        layer, g = block(golden, name)
+        L = synth.open_layer(layer)
+        try:
+            lg = L.router_logits(g["x"])
+            np.testing.assert_allclose(lg, g["logits"], rtol=1e-5, atol=1e-5)
+            idx_dev, _ = nc.route(lg, layer.spec.E, layer.spec.k, layer.spec.norm_topk_prob)
+            idx_ref, _ = O.route(g["logits"], layer.spec.k, layer.spec.norm_topk_prob)
+            if np.array_equal(idx_dev, idx_ref):
+                out = L.forward(g["x"])
+                assert rel_err(out, g["out"]) <= DECODE_TOL, name
+        finally:
+            L.close()
+
+
+def test_forward_deterministic_and_device_pointers(golden):
+    torch = pytest.importorskip("torch")
+    layer, g = block(golden, "b_q8")
+    L = synth.open_layer(layer)
+    try:
+        a = L.forward(g["x"])
+        b = L.forward(g["x"])
+        assert np.array_equal(a, b)
+        xt = torch.from_numpy(g["x"]).cuda()
+        c = L.forward(xt)
+        torch.cuda.synchronize()
+        assert np.array_equal(c.cpu().numpy(), a)
+        # an unaligned device view is staged, not read with vector loads
+        big = torch.zeros(g["x"].size + 1, device="cuda")
+        big[1:] = xt.reshape(-1)
+        d = L.forward(big[1:].view(g["x"].shape))
+        torch.cuda.synchronize()
+        assert np.array_equal(d.cpu().numpy(), a)
+    finally:
+        L.close()
+
+
+def _config_check(key, T, seed=0, tol=DECODE_TOL, calls=1):
+    wl = synth.CONFIGS[key]
+    layer = synth.make_layer(wl.spec, seed, device_gen=True)
+    x = synth.make_x(T * calls, wl.spec.d, seed, bf16=wl.bf16_x)
+    if wl.zipf_s:
+        synth.attach_zipf(layer, x, wl.zipf_s, seed)
+    L = synth.open_layer(layer)
+    try:
+        lg = L.router_logits(x)
+        outs = [L.ffn_block(x[i * T:(i + 1) * T], lg[i * T:(i + 1) * T]) for i in range(calls)]
+    finally:
+        L.close()
+    out = np.concatenate(outs)
+    ref = O.moe_block(layer, x, lg, nthreads=os.cpu_count() or 1)
+    err = rel_err(out, ref)
+    assert err <= tol, (key, err)
+    return err
+
+
+def test_config1_decode_q8_0():
+    _config_check("c1", T=1, calls=4)
+
+
+def test_config3_decode_q4_k_shared():
+    _config_check("c3", T=32)
+
+
+def test_config2_prefill_q4_k_zipf_subset():
+    # routing over all 512 tokens of the config, outputs checked on all of them
+    _config_check("c2", T=512, tol=PREFILL_TOL)
+
+
+def test_gguf_open_equals_tensors(tmp_path):
+    spec = synth.LayerSpec(512, 8, 2, 256, 256, Q.DTYPE_Q4_K)
+    layer = synth.make_layer(spec, 21)
+    p = str(tmp_path / "l.gguf")
+    synth.write_gguf(layer, p, layer_index=3)
+    x = synth.make_x(7, 512, 21)
+    A = M.CudaMoeLayer.from_gguf(p, 3)
+    B = synth.open_layer(layer)
+    try:
+        assert A.cfg.n_expert == 8 and A.cfg.n_expert_used == 2 and A.cfg.has_shared
+        assert np.array_equal(A.forward(x), B.forward(x))
+    finally:
+        A.close()
+        B.close()
+
+
+# ---------------------------------------------------------------- drop-in API
+def test_moe_ffn_dropin_matches_loop_reference():
+    """tests/test_arch.py:129-195, run through the GPU path."""
+    rng = np.random.default_rng(9)
+    E, F, NX = 8, 4, 6
+    cfg = M.MoeConfig(n_expert=NX, n_expert_used=2, n_embd=E, ffn_len=F)
+    Gt = rng.standard_normal((NX, F, E)).astype(np.float32) * 0.5
+    Ut = rng.standard_normal((NX, F, E)).astype(np.float32) * 0.5
+    Dt = rng.standard_normal((NX, E, F)).astype(np.float32) * 0.5
+    fetched = []
+
+    def rows(name, expert, block_rows):
+        fetched.append((name, expert))
+        return {"ffn_gate_exps.weight": Gt, "ffn_up_exps.weight": Ut, "ffn_down_exps.weight": Dt}[name][expert]
+
+    Rout = rng.standard_normal((NX, E)).astype(np.float32) * 0.5
+    router_fn = lambda hv: (hv @ Rout.T).reshape(-1)  # noqa: E731
+    h = rng.standard_normal((3, E)).astype(np.float32)
+    out = M.moe_ffn(h, cfg, rows, shexp=None, router_fn=router_fn)
+    with pytest.raises(ValueError):
+        M.moe_ffn(h, cfg, rows, shexp=None)
+    with pytest.raises(ValueError):
+        M.moe_ffn(h, cfg, rows, shexp=None, router_fn=lambda hv: np.zeros(3, dtype=np.float32))
+
+    def ref_one(ht):
+        idx, w = O.route(router_fn(ht), 2)
+        acc = np.zeros(E, dtype=np.float32)
+        for e, wt in zip(idx, w):
+            a = (ht @ Gt[e].T) / (1 + np.exp(-(ht @ Gt[e].T))) * (ht @ Ut[e].T)
+            acc += wt * (a @ Dt[e].T)
+        return acc
+
+    ref = np.stack([ref_one(h[t]) for t in range(3)])
+    assert np.allclose(out, ref, atol=1e-5)
+    assert {e for _, e in fetched} <= set(int(i) for t in range(3) for i in O.route(router_fn(h[t]), 2)[0])
+    sh = {"gate_inp": rng.standard_normal((1, E)).astype(np.float32), "gate": rng.standard_normal((F, E)).astype(np.float32),
+          "up": rng.standard_normal((F, E)).astype(np.float32), "down": rng.standard_normal((E, F)).astype(np.float32)}
+    with_sh = M.moe_ffn(h, cfg, rows, shexp=sh, router_fn=router_fn)
+    assert not np.allclose(out, with_sh)
+    g = 1 / (1 + np.exp(-(h @ sh["gate_inp"].T)))
+    want = ref.copy()
+    for t in range(3):
+        a = (h[t] @ sh["gate"].T) / (1 + np.exp(-(h[t] @ sh["gate"].T))) * (h[t] @ sh["up"].T)
+        want[t] += g[t, 0] * (a @ sh["down"].T)
+    assert np.allclose(with_sh, want, atol=1e-5)
+
+
+def test_fetch_failure_propagates():
+    """tests/test_moe_cpp.cpp:252-268: a failing reader aborts the block."""
+    cfg = M.MoeConfig(n_expert=6, n_expert_used=2, n_embd=16, ffn_len=16, has_shared=False)
+
+    def rows(name, expert, block_rows):
+        if name == "ffn_up_exps.weight":
+            raise KeyError("up missing")
+        return np.zeros((16, 16), np.float32)
+
+    with pytest.raises(KeyError):
+        M.moe_ffn(np.ones((1, 16), np.float32), cfg, rows, router_fn=lambda hv: np.arange(6, dtype=np.float32))
+
+
+def test_device_layer_with_its_router(golden):
+    layer, g = block(golden, "b_q8")
+    L = synth.open_layer(layer)
+    try:
+        cfg = L.cfg
+        a = M.moe_ffn(g["x"], cfg, L, shexp=L.shexp, router_fn=L.router)
+        b = L.forward(g["x"])
+        assert np.array_equal(a, b)
+        c = M.moe_ffn(g["x"], cfg, L, shexp=L.shexp, router_fn=lambda hv: hv @ layer.router.T)
+        assert rel_err(c, g["out"]) <= DECODE_TOL
+    finally:
+        L.close()
+
+
+# ---------------------------------------------------------------- guard on the device
+def test_guard_refuses_oversized_layer():
+    g = nc.MemoryGuard()
+    base = g.committed()
+    spec = synth.LayerSpec(256, 16, 4, 64, 0, Q.DTYPE_Q8_0)
+    layer = synth.make_layer(spec, 3)
+    g.set_budget(base + 4096)
+    try:
+        with pytest.raises(RuntimeError) as e:
+            synth.open_layer(layer)
+        assert "refused" in str(e.value)
+    finally:
+        g.set_budget(0)
+    assert g.committed() == base
+
+
+def test_guard_injected_allocation_failure_leaks_nothing():
+    g = nc.MemoryGuard()
+    base = g.committed()
+    spec = synth.LayerSpec(256, 16, 4, 64, 64, Q.DTYPE_Q8_0)
+    layer = synth.make_layer(spec, 4)
+    for n in (1, 2, 3, 5, 8):
+        g.fail_nth_alloc(n)
+        with pytest.raises(RuntimeError):
+            synth.open_layer(layer)
+        assert g.committed() == base, n
+    g.fail_nth_alloc(0)
+    L = synth.open_layer(layer)
+    assert g.committed() > base
+    L.close()
+    assert g.committed() == base

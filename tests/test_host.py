@@ -1,0 +1,189 @@
+"""Host-side checks that need no GPU: quantisers, GGUF writer, the C-ABI
+library's exports, the memory guard's accounting, and the GGUF parser's
+refusals."""
+
+import os
+import re
+import struct
+
+import numpy as np
+import pytest
+
+import oracle as O
+from aero_b200 import quant as Q
+from aero_b200 import synth
+from aero_b200.gguf import GGUFWriter
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def test_q8_0_matches_gguf_py():
+    gguf = pytest.importorskip("gguf")
+    x = (np.random.default_rng(0).standard_normal((16, 2048)) * 0.02).astype(np.float32)
+    x[0, :32] = 0.0  # an all-zero block (d = 0)
+    want = gguf.quants.quantize(x, gguf.GGMLQuantizationType.Q8_0).tobytes()
+    assert Q.quantize(x, Q.DTYPE_Q8_0) == want
+
+
+def test_q4_k_roundtrip_error():
+    x = (np.random.default_rng(1).standard_normal(256 * 64) * 0.02).astype(np.float32)
+    raw = Q.quantize(x, Q.DTYPE_Q4_K)
+    assert len(raw) == 64 * 144
+    y = O.dequant(Q.DTYPE_Q4_K, raw, x.size)
+    rel = np.sqrt(np.mean((y - x) ** 2)) / np.sqrt(np.mean(x ** 2))
+    assert rel < 0.12
+    # all-zero super-block quantises to d = dmin = 0 and decodes to zeros
+    z = Q.quantize(np.zeros(256, np.float32), Q.DTYPE_Q4_K)
+    assert np.all(O.dequant(Q.DTYPE_Q4_K, z, 256) == 0)
+
+
+def test_type_sizes():
+    assert Q.type_size(Q.DTYPE_Q8_0, 32) == 34
+    assert Q.type_size(Q.DTYPE_Q4_K, 512) == 288
+    with pytest.raises(ValueError):
+        Q.type_size(Q.DTYPE_Q4_K, 100)
+
+
+def test_gguf_writer_layout(tmp_path):
+    w = GGUFWriter("qwen35moe")
+    w.add_u32("qwen35moe.expert_count", 4)
+    w.add_tensor("t0", (3, 32), Q.quantize(np.ones(96, np.float32), Q.DTYPE_Q8_0), Q.DTYPE_Q8_0)
+    w.add_tensor("t1", (2,), np.arange(2, dtype=np.float32).tobytes(), Q.DTYPE_F32)
+    b = w.to_bytes()
+    assert b[:4] == b"GGUF"
+    version, n_t, n_kv = struct.unpack_from("<IQQ", b, 4)
+    assert (version, n_t, n_kv) == (3, 2, 3)
+    assert len(b) % 32 == 0
+
+
+# ---------------------------------------------------------------- the C ABI
+def _header_functions():
+    src = open(os.path.join(ROOT, "include", "aero_cuda_moe.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    names = re.findall(r"\b(aero_cuda_\w+)\s*\(", src)
+    return sorted(set(n for n in names if not n.endswith("_fn")))
+
+
+def test_library_exports_every_header_symbol(cuda_lib):
+    from aero_b200 import native_cuda as nc
+    names = _header_functions()
+    assert len(names) >= 40
+    for n in names:
+        assert hasattr(cuda_lib, n), n
+    declared = {s[0] for s in nc.SYMBOLS}
+    assert set(names) == declared
+
+
+def test_compute_refuses_without_gpu(cuda_lib):
+    """With no visible GPU every compute entry point refuses (no CPU fallback)."""
+    from aero_b200 import native_cuda as nc
+    if nc.gpu_count() > 0:
+        pytest.skip("a GPU is visible")
+    with pytest.raises(nc.CudaMoeUnavailable):
+        nc.route(np.zeros(8, np.float32), 8, 2)
+    lg = np.zeros(8, np.float32)
+    idx = np.zeros(2, np.int64)
+    w = np.zeros(2, np.float32)
+    assert cuda_lib.aero_cuda_route(lg.ctypes.data, 1, 8, 2, 1, idx.ctypes.data, w.ctypes.data) == -1
+    assert "no CUDA device" in nc.last_error()
+
+
+def test_guard_accounting(cuda_lib):
+    from aero_b200 import native_cuda as nc
+    g = nc.MemoryGuard()
+    base = g.committed()
+    g.set_budget(0)
+    assert g.try_reserve(1 << 40, nc.MEM_SCRATCH)  # budget 0 = unbounded
+    g.release(1 << 40, nc.MEM_SCRATCH)
+    g.set_budget(base + 1000)
+    try:
+        assert g.try_reserve(600, nc.MEM_WEIGHTS_RESIDENT)
+        assert not g.try_reserve(600, nc.MEM_SCRATCH)
+        assert g.committed(nc.MEM_WEIGHTS_RESIDENT) >= 600
+        assert g.headroom() == 400
+        ok, why = g.admit_plan(2000)
+        assert not ok and "exceeds" in why
+        ok, why = g.admit_plan(500)
+        assert not ok and "already committed" in why
+        # evictor frees cache bytes on a refusal (src/memory_guard.cpp:172-182)
+        assert g.try_reserve(300, nc.MEM_WEIGHTS_CACHE)
+
+        def evict(need):
+            g.release(300, nc.MEM_WEIGHTS_CACHE)
+            return 300
+
+        g.set_evictor(evict)
+        assert g.try_reserve(250, nc.MEM_SCRATCH)
+        g.set_evictor(None)
+        g.release(250, nc.MEM_SCRATCH)
+        g.release(600, nc.MEM_WEIGHTS_RESIDENT)
+        g.release(10 ** 9, nc.MEM_KV_CACHE)  # never below zero
+        assert g.committed(nc.MEM_KV_CACHE) == 0
+    finally:
+        g.set_budget(0)
+    assert g.committed() == base
+
+
+def test_loadgate_semantics(cuda_lib):
+    from aero_b200 import native_cuda as nc
+    g = nc.MemoryGuard()
+    base = g.committed()
+    g.set_budget(base + 1000)
+    try:
+        gate = nc.LoadGate(700)
+        assert gate.ok()
+        assert gate.next_chunk(300) and gate.next_chunk(300)
+        assert not gate.next_chunk(300)          # 600 + 300 > 700: the plan is complete
+        assert gate.ok() and gate.done()          # completion, not failure
+        assert gate.reserved() == 600
+        g.release(600, nc.MEM_WEIGHTS_CACHE)
+        big = nc.LoadGate(5000)
+        assert not big.ok() and "exceeds" in big.reason()
+        assert g.try_reserve(600, nc.MEM_RUNTIME)
+        stop = nc.LoadGate(300)                  # 600 + 300 <= 1000: admitted
+        assert stop.next_chunk(150)
+        assert g.try_reserve(200, nc.MEM_RUNTIME)  # someone else takes memory mid-load
+        assert not stop.next_chunk(100) and not stop.ok()
+        assert "would exceed" in stop.reason()
+        g.release(150, nc.MEM_WEIGHTS_CACHE)
+        g.release(800, nc.MEM_RUNTIME)
+    finally:
+        g.set_budget(0)
+    assert g.committed() == base
+
+
+def test_gguf_open_refuses_bad_files(cuda_lib, tmp_path):
+    import ctypes
+    bad = tmp_path / "bad.gguf"
+    bad.write_bytes(b"NOPE" + b"\0" * 64)
+    err = ctypes.create_string_buffer(256)
+    assert not cuda_lib.aero_cuda_moe_open_gguf(str(bad).encode(), 0, 0, 0, 0, err, 256)
+    assert b"bad magic" in err.value
+    # a real layer file, truncated in the middle of its data
+    spec = synth.LayerSpec(256, 4, 2, 64, 0, Q.DTYPE_Q8_0)
+    p = tmp_path / "layer.gguf"
+    synth.write_gguf(synth.make_layer(spec, 1), str(p))
+    data = p.read_bytes()
+    t = tmp_path / "trunc.gguf"
+    t.write_bytes(data[: len(data) // 2])
+    assert not cuda_lib.aero_cuda_moe_open_gguf(str(t).encode(), 0, 0, 0, 0, err, 256)
+    assert b"past the end" in err.value or b"truncated" in err.value
+    # wrong layer index: not a MoE layer
+    assert not cuda_lib.aero_cuda_moe_open_gguf(str(p).encode(), 3, 0, 0, 0, err, 256)
+    assert b"missing" in err.value
+
+
+def test_zipf_calibration():
+    spec = synth.LayerSpec(256, 64, 4, 64, 0, Q.DTYPE_Q8_0)
+    layer = synth.make_layer(spec, 2)
+    x = synth.make_x(512, 256, 2)
+    synth.attach_zipf(layer, x, 1.1, 2)
+    lg = x @ layer.router.T + layer.router_bias
+    loads = np.bincount(np.argsort(-lg, axis=1)[:, :4].reshape(-1), minlength=64)
+    assert abs(synth._slope(loads) + 1.1) < 0.05
+    assert loads.max() > 3 * np.median(loads)
+
+
+def test_bf16_inputs_representable():
+    x = synth.make_x(4, 64, 0, bf16=True)
+    assert np.all((x.view(np.uint32) & 0xFFFF) == 0)
