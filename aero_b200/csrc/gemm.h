@@ -1,12 +1,61 @@
 // Prefill grouped GEMM (tcgen05 / TMEM) entry points.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
 
+#include "common.cuh"
+
 namespace aero {
 
-// Device workspace the prefill path needs for P routed pairs and T tokens.
-size_t gemm_workspace_bytes(int dp, int act_ld, int P, int T, int n_groups);
+// One tile of token rows for one expert segment: rows [pos0, pos0 + nvalid) of
+// the permuted activation buffers. expert < 0 marks the shared expert.
+struct GemmTile {
+    int32_t expert, pos0, nvalid, pad;
+};
+
+constexpr int kGemmNT = 256;  // token rows per tile (the MMA N extent, at most 256)
+
+// Upper bound on the number of tiles for P routed pairs and T tokens.
+inline int gemm_max_tiles(int P, int T, int E, int has_shared) {
+    const int act = P < E ? P : E;
+    return act + (P + kGemmNT - 1) / kGemmNT + (has_shared ? (T + kGemmNT - 1) / kGemmNT : 0);
+}
+
+// Device workspace the prefill path needs (tile list + f16 operand buffers).
+size_t gemm_workspace_bytes(int dp, int act_ld, int P, int T, int max_tiles);
+
+struct GemmBuffers {
+    __half* xperm;   // (rows_cap, dp)   token rows sorted by expert, then x for the shared expert
+    __half* act;     // (rows_cap, act_ld)
+    __half* y;       // (rows_cap, dp)
+    GemmTile* tiles;        // (max tiles)
+    int32_t* n_tiles;
+    int32_t* err;           // pipeline timeout code (0 = none)
+    int rows_cap;
+    CUtensorMap tmap_x, tmap_act;
+};
+
+// Carve the workspace and encode the TMA descriptors for it.
+bool gemm_setup(void* ws, size_t ws_bytes, int dp, int act_ld, int P_cap, int T_cap, int max_tiles, GemmBuffers* b,
+                std::string* why);
+
+struct PrefillArgs {
+    QMat gate, up, down, sg, su, sd;
+    const float* x;           // (T, dp) f32
+    const int32_t* perm;      // sorted position -> pair
+    const int32_t* act_e;
+    const int32_t* act_off;
+    const int32_t* n_active;
+    int T, k, dp, F, Fs, has_shared, E;
+    int act_ld;
+};
+
+// gather -> tile list -> gate/up GEMM (+SwiGLU) -> down GEMM. Writes y (f16)
+// for rows [0, P + T); the combine reads it with launch_combine_h.
+cudaError_t launch_prefill(const PrefillArgs& a, GemmBuffers& b, cudaStream_t s, int* launches);
+cudaError_t launch_combine_h(const __half* y, const int32_t* inv, const float* w, const float* sgate,
+                                int T, int k, int d, int has_shared, float* out, cudaStream_t s);
 
 }  // namespace aero

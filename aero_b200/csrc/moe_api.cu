@@ -10,6 +10,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
@@ -52,6 +53,7 @@ struct Scratch {
     void* dwork;
     void* gemm_ws;
     size_t gemm_ws_bytes = 0;
+    int gemv_cap = 0;
 };
 
 struct Handle {
@@ -79,6 +81,11 @@ struct Handle {
     double stage_ms[kStages] = {};
     long stage_n[kStages] = {};
     long launches = 0;        // kernels launched by this handle
+    // prefill (tcgen05 grouped GEMM) path
+    bool gemm_ok = false;     // layer shape/type supports it
+    int gemm_min_tokens = 64; // calls with at least this many tokens use it
+    GemmBuffers gb{};
+    bool gb_ready = false;
     int last_active = -1;     // active experts of the last profiled call
 
     ~Handle() {
@@ -219,12 +226,16 @@ bool ensure_scratch(Handle& h, int T) {
     const size_t o_lgs = take((size_t)cap * h.E * 4);
     const size_t o_lg = take((size_t)cap * (h.E + 1) * 4), o_w = take((size_t)P * 4), o_sg = take((size_t)cap * 4);
     const size_t o_xs = take((size_t)cap * (h.dp / 16) * 4);
-    const size_t o_act = take((size_t)rows * h.act_ld * 4), o_as = take((size_t)rows * (h.act_ld / 16) * 4);
-    const size_t o_y = take((size_t)rows * h.dp * 4);
+    // the f32 GEMV buffers only need to cover calls that take the GEMV path
+    const int64_t gemv_T = h.gemm_ok ? std::min<int64_t>(cap, h.gemm_min_tokens) : cap;
+    const int64_t grows = gemv_T * h.k + gemv_T;
+    const size_t o_act = take((size_t)grows * h.act_ld * 4), o_as = take((size_t)grows * (h.act_ld / 16) * 4);
+    const size_t o_y = take((size_t)grows * h.dp * 4);
     const size_t o_idx = take((size_t)P * 4), o_off = take((size_t)(h.E + 1) * 4), o_perm = take((size_t)P * 4);
     const size_t o_inv = take((size_t)P * 4), o_ae = take((size_t)h.E * 4), o_ao = take((size_t)(h.E + 1) * 4);
     const size_t o_na = take(4), o_dw = take(dispatch_work_bytes((int)P, h.E));
-    const size_t gws = gemm_workspace_bytes(h.dp, h.act_ld, (int)P, cap, h.E + 1);
+    const int max_tiles = gemm_max_tiles((int)P, cap, h.E, h.has_shared);
+    const size_t gws = h.gemm_ok ? gemm_workspace_bytes(h.dp, h.act_ld, (int)P, cap, max_tiles) : 256;
     const size_t o_gw = take(gws);
     void* base = nullptr;
     const cudaError_t e = guarded_malloc(&base, off, kScratch);
@@ -261,6 +272,13 @@ bool ensure_scratch(Handle& h, int T) {
     s.dwork = b + o_dw;
     s.gemm_ws = b + o_gw;
     s.gemm_ws_bytes = gws;
+    s.gemv_cap = (int)gemv_T;
+    h.gb_ready = false;
+    if (h.gemm_ok) {
+        std::string why;
+        if (!gemm_setup(s.gemm_ws, gws, h.dp, h.act_ld, (int)P, cap, max_tiles, &h.gb, &why)) return h.fail("%s", why.c_str());
+        h.gb_ready = true;
+    }
     // zero the padded columns of the staging buffers once
     return h.cuda_ok(cudaMemsetAsync(base, 0, off, h.stream), "scratch clear");
 }
@@ -302,6 +320,37 @@ bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* 
         return false;
     h.launches += 3;
     mark(3);
+    if (h.gemm_ok && h.gb_ready && T >= h.gemm_min_tokens) {
+        PrefillArgs pa{};
+        pa.gate = h.gate;
+        pa.up = h.up;
+        pa.down = h.down;
+        pa.sg = h.sg;
+        pa.su = h.su;
+        pa.sd = h.sd;
+        pa.x = x;
+        pa.perm = s.perm;
+        pa.act_e = s.act_e;
+        pa.act_off = s.act_off;
+        pa.n_active = s.n_active;
+        pa.T = T;
+        pa.k = h.k;
+        pa.dp = h.dp;
+        pa.F = h.Fp;
+        pa.Fs = h.Fsp;
+        pa.has_shared = h.has_shared;
+        pa.E = h.E;
+        pa.act_ld = h.act_ld;
+        int nl = 0;
+        if (!h.cuda_ok(launch_prefill(pa, h.gb, st, &nl), "prefill GEMM")) return false;
+        h.launches += nl;
+        mark(4);
+        mark(5);
+        if (!h.cuda_ok(launch_combine_h(h.gb.y, s.inv, s.w, s.sgate, T, h.k, h.dp, h.has_shared, out, st), "combine"))
+            return false;
+        h.launches += 1;
+    } else {
+    if (T > s.gemv_cap) return h.fail("internal: GEMV scratch covers %d tokens, call has %d", s.gemv_cap, T);
     GemvArgs a{};
     a.gate = h.gate;
     a.up = h.up;
@@ -333,6 +382,7 @@ bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* 
     mark(5);
     if (!h.cuda_ok(launch_combine(s.y, s.inv, s.w, s.sgate, T, h.k, h.dp, h.has_shared, out, st), "combine")) return false;
     h.launches += 1;
+    }
     mark(6);
     if (h.profiling) {
         if (!h.cuda_ok(cudaEventSynchronize(h.sev[6]), "profile")) return false;
@@ -345,6 +395,17 @@ bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* 
         cudaMemcpy(&h.last_active, s.n_active, 4, cudaMemcpyDeviceToHost);
     }
     return true;
+}
+
+// The prefill kernels record a non-zero code when one of their bounded waits
+// expired; report it (and clear it) at the next synchronisation point.
+bool check_pipeline(Handle& h) {
+    if (!h.gb_ready) return true;
+    int32_t code = 0;
+    if (cudaMemcpy(&code, h.gb.err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return h.cuda_ok(cudaGetLastError(), "error flag");
+    if (code == 0) return true;
+    cudaMemset(h.gb.err, 0, 4);
+    return h.fail("prefill GEMM pipeline wait expired (code %d); the call's output is invalid", code);
 }
 
 // Host/device wrapper: stages x and out when they are host memory or when the
@@ -387,6 +448,7 @@ bool block_entry(Handle& h, const float* x, int T, const float* logits, float* o
     if (!out_dev || !x_dev) {
         if (!h.cuda_ok(cudaStreamSynchronize(st), "block")) return false;
         if (h.timing) cudaEventElapsedTime(&h.last_ms, h.ev0, h.ev1);
+        if (!check_pipeline(h)) return false;
     }
     h.calls++;
     h.tokens += T;
@@ -453,7 +515,9 @@ Handle* open_desc(const aero_cuda_moe_desc* d, std::string* why) {
         h->Fsp = f32 ? (int)round_up(h->Fs, 16) : h->Fs;
         if (h->Fsp % 16) return bad("ffn_len_shared must be a multiple of 16");
     }
-    h->act_ld = (int)round_up(std::max(h->Fp, h->Fsp), 16);
+    h->act_ld = (int)round_up(std::max(h->Fp, h->Fsp), 64);
+    h->gemm_ok = !f32 && h->dp % 128 == 0 && h->Fp % 128 == 0 && (!h->has_shared || h->Fsp % 128 == 0);
+    if (const char* v = std::getenv("AERO_GEMM_MIN_TOKENS")) h->gemm_min_tokens = std::max(1, std::atoi(v));
     const int ne = h->e_end - h->e_begin;
     (void)ne;
     // router (+ shared gate row) as f32 (E + 1, dp)
@@ -811,6 +875,20 @@ int aero_cuda_moe_stage_times(void* handle, double* ms, int64_t* counts, int n) 
         if (counts) counts[i] = h->stage_n[i];
     }
     return m;
+}
+
+int aero_cuda_moe_set_option(void* handle, int option, int64_t value) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (option == AERO_CUDA_OPT_GEMM_MIN_TOKENS) {
+        if (value < 1) return -1;
+        h->gemm_min_tokens = (int)std::min<int64_t>(value, 1 << 30);
+        h->sc.cap_T = 0;  // re-plan scratch on the next call
+        return 0;
+    }
+    h->fail("unknown option %d", option);
+    return -1;
 }
 
 int aero_cuda_moe_info(void* handle, int32_t* out8) {

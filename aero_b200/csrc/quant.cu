@@ -108,11 +108,14 @@ __global__ void quantize_q8_0_kernel(const float* __restrict__ x, int64_t nb, ui
     for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(xb[i]));
     const float d = __fdiv_rn(amax, 127.0f);
     const float id = d == 0.f ? 0.f : __fdiv_rn(1.0f, d);
-    uint8_t* o = out + b * 34;
-    const uint16_t dh = __half_as_ushort(__float2half_rn(d));
-    o[0] = (uint8_t)(dh & 0xFF);
-    o[1] = (uint8_t)(dh >> 8);
-    for (int i = 0; i < 32; ++i) o[2 + i] = (uint8_t)(int8_t)(int)rnd_away(__fmul_rn(xb[i], id));
+    // the 34-byte block is 2-byte aligned: write it as 17 little-endian u16 words
+    unsigned short* o = reinterpret_cast<unsigned short*>(out + b * 34);
+    o[0] = __half_as_ushort(__float2half_rn(d));
+    for (int i = 0; i < 32; i += 2) {
+        const uint32_t q0 = (uint32_t)(uint8_t)(int8_t)(int)rnd_away(__fmul_rn(xb[i], id));
+        const uint32_t q1 = (uint32_t)(uint8_t)(int8_t)(int)rnd_away(__fmul_rn(xb[i + 1], id));
+        o[1 + i / 2] = (unsigned short)(q0 | (q1 << 8));
+    }
 }
 
 __global__ void quantize_q4_k_kernel(const float* __restrict__ x, int64_t nb, uint8_t* __restrict__ out) {

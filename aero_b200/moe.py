@@ -218,6 +218,11 @@ class CudaMoeLayer:
             raise ValueError(f"route refused: {nc.last_error(self.handle)}")
         return (idx[0], w[0]) if single else (idx, w)
 
+    def set_gemm_min_tokens(self, n: int) -> None:
+        """Calls with at least n tokens use the tcgen05 grouped-GEMM path."""
+        if self._lib.aero_cuda_moe_set_option(self.handle, nc.OPT_GEMM_MIN_TOKENS, int(n)) != 0:
+            raise ValueError(nc.last_error(self.handle))
+
     def set_stream(self, stream) -> None:
         """Run on a cudaStream_t (int) or a torch.cuda.Stream; None restores the handle's own."""
         s = getattr(stream, "cuda_stream", stream)

@@ -29,6 +29,8 @@ DTYPE_Q4_K = 12
 # memory classes (src/memory_guard.cpp MemClass order)
 MEM_WEIGHTS_RESIDENT, MEM_WEIGHTS_CACHE, MEM_KV_CACHE, MEM_SCRATCH, MEM_RUNTIME = range(5)
 
+OPT_GEMM_MIN_TOKENS = 1
+
 
 class CudaMoeUnavailable(RuntimeError):
     """The CUDA library is not built or no GPU is present. There is no CPU path."""
@@ -71,6 +73,7 @@ SYMBOLS = [
     ("aero_cuda_quantize", c_int, [c_int, _P, c_int64, _P, c_int64]),
     ("aero_cuda_moe_set_profiling", c_int, [_P, c_int]),
     ("aero_cuda_moe_stage_times", c_int, [_P, _P, _P, c_int]),
+    ("aero_cuda_moe_set_option", c_int, [_P, c_int, c_int64]),
     ("aero_cuda_moe_set_stream", c_int, [_P, _P]),
     ("aero_cuda_moe_info", c_int, [_P, POINTER(c_int32)]),
     ("aero_cuda_moe_last_error", c_char_p, [_P]),

@@ -126,6 +126,13 @@ int aero_cuda_quantize(int dtype, const float* x, int64_t n_values, uint8_t* out
 int aero_cuda_moe_set_profiling(void* handle, int on);
 int aero_cuda_moe_stage_times(void* handle, double* ms, int64_t* counts, int n);
 
+/* Options. AERO_CUDA_OPT_GEMM_MIN_TOKENS: calls with at least this many tokens
+ * run the expert products as tcgen05 grouped GEMMs (bf16 operands, fp32
+ * accumulate); smaller calls use the fp32 GEMV path (default 64; also read from
+ * the AERO_GEMM_MIN_TOKENS environment variable at open). 0 / -1. */
+#define AERO_CUDA_OPT_GEMM_MIN_TOKENS 1
+int aero_cuda_moe_set_option(void* handle, int option, int64_t value);
+
 /* Run the handle's work on this cudaStream_t (NULL: the handle's own stream). */
 int aero_cuda_moe_set_stream(void* handle, void* stream);
 /* Layer geometry: out[0..7] = n_embd, n_expert, n_expert_used, ffn_len,

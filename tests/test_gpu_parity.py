@@ -163,6 +163,10 @@ def test_forward_deterministic_and_device_pointers(golden):
 def _config_check(key, T, seed=0, tol=DECODE_TOL, calls=1):
     wl = synth.CONFIGS[key]
     layer = synth.make_layer(wl.spec, seed, device_gen=True)
+    # the device-generated bytes must decode to N(0, 0.02)-like weights
+    w = O.dequant(wl.spec.dtype, layer.gate[: 34 * 64 if wl.spec.dtype == Q.DTYPE_Q8_0 else 144 * 8],
+                  2048)
+    assert 0.015 < float(np.std(w)) < 0.025
     x = synth.make_x(T * calls, wl.spec.d, seed, bf16=wl.bf16_x)
     if wl.zipf_s:
         synth.attach_zipf(layer, x, wl.zipf_s, seed)
@@ -174,6 +178,7 @@ def _config_check(key, T, seed=0, tol=DECODE_TOL, calls=1):
         L.close()
     out = np.concatenate(outs)
     ref = O.moe_block(layer, x, lg, nthreads=os.cpu_count() or 1)
+    assert rms(ref) > 1e-3, "degenerate reference output (weights or routing broken)"
     err = rel_err(out, ref)
     assert err <= tol, (key, err)
     return err
