@@ -74,4 +74,7 @@ void guarded_free(void* p, size_t bytes, int cls);
 
 std::string fmt_bytes(size_t b);
 
+// Sets the message aero_cuda_moe_last_error(NULL) returns on this thread.
+void set_free_error(const std::string& msg);
+
 }  // namespace aero

@@ -583,6 +583,9 @@ Handle* open_desc(const aero_cuda_moe_desc* d, std::string* why) {
 }
 
 }  // namespace
+
+void set_free_error(const std::string& msg) { g_free_error = msg; }
+
 }  // namespace aero
 
 using aero::Handle;

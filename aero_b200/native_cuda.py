@@ -69,6 +69,7 @@ SYMBOLS = [
     ("aero_cuda_moe_route", c_int, [_P, _P, c_int, _P, _P]),
     ("aero_cuda_route", c_int, [_P, c_int, c_int, c_int, c_int, _P, _P]),
     ("aero_cuda_dispatch", c_int, [_P, c_int, c_int, c_int, _P, _P]),
+    ("aero_cuda_dispatch_noalloc", c_int, [_P, c_int, c_int, c_int, _P, _P, _P]),
     ("aero_cuda_dequant", c_int, [c_int, _P, c_int64, _P, c_int64]),
     ("aero_cuda_quantize", c_int, [c_int, _P, c_int64, _P, c_int64]),
     ("aero_cuda_moe_set_profiling", c_int, [_P, c_int]),

@@ -110,6 +110,23 @@ int aero_cuda_route(const float* logits, int T, int n_expert, int k, int norm_to
 int aero_cuda_dispatch(const int64_t* idx, int T, int k, int n_expert, int32_t* offsets,
                        int32_t* perm);
 
+/* aero_cuda_dispatch without any device allocation. No counterpart in the
+ * reference. For callers that must not allocate device memory when they route:
+ * a process whose device budget is fully committed (the memory guard refuses
+ * more), or a pipeline that cannot take cudaMalloc's implicit device-wide
+ * synchronisation. Its scratch is one fixed 2 MiB device array inside this
+ * library, which every GPU that loads the library holds until exit.
+ * Limits: T*k <= 65536 pairs and n_expert <= 1024; larger calls are refused
+ * (use aero_cuda_dispatch). idx (T, k) int64, offsets (n_expert + 1) and perm
+ * (T*k) int32 must be device memory; the work runs on `stream` (NULL: the
+ * default stream) and the call returns when it is done. The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress); make that
+ * first call before any stream capture. All calls share the array: calls whose
+ * work overlaps on the GPU race and corrupt each other's results. 0 / -1; the
+ * reason for -1 is in aero_cuda_moe_last_error(NULL). */
+int aero_cuda_dispatch_noalloc(const int64_t* idx, int T, int k, int n_expert, int32_t* offsets,
+                               int32_t* perm, void* stream);
+
 /* GGUF dequantisation to f32, bit-identical to aero_dequant_ref
  * (src/kernels.cpp:591-606) for Q8_0, Q4_K and F32. 1 ok / 0 refusal (unknown
  * type, n not whole blocks, raw_len too short). */
