@@ -1,27 +1,37 @@
 // Prefill: grouped expert GEMMs on the 5th-generation tensor cores.
 //
 // Per routed expert segment (token rows sorted by expert) and for the shared
-// expert (all tokens), two grouped GEMMs in "weights x tokens" orientation, so
-// the 128-row MMA M extent runs over weight rows and the ragged token count is
-// the N extent (16..256 in steps of 16; nothing is padded to 128 tokens):
-//   gate/up:  D_g = Wg[m0:m0+128, :] . X^T,  D_u = Wu[...] . X^T  (K = d)
+// expert (all tokens), two grouped GEMMs in "weights x tokens" orientation: the
+// 128-row MMA M extent runs over weight rows and the ragged token count is the
+// N extent (16..192 in steps of 16), so nothing is padded to 128 tokens.
+//   gate/up:  D_g = Wg[m0:m0+128, :] . X^T,  D_u = Wu[...] . X^T   (K = d)
 //             epilogue: act = silu(D_g) * D_u  -> f16 act rows
-//   down:     D = Wd[n0:n0+128, :] . act^T (K = F)  -> f16 y rows
+//   down:     D = Wd[n0:n0+128, :] . act^T                        (K = F)
+//             epilogue: f16 y rows
 // Operands are f16 (kind::f16, fp32 accumulate). bf16 operands were measured
 // (and reproduced by a numpy model of the same roundings) at 2.6% of the output
 // RMS in max-abs error on Q4_K layers, above the 1% bar; f16 rounds 8x finer at
-// the same tensor-core rate and measures 0.26%.
-// One CTA computes one (tile, 128-row block). Warp roles, 10 warps:
-//   warp 0     TMA producer of the token operand (cp.async.bulk.tensor, 128B
-//              swizzle, no multicast) and owner of the TMEM allocation
-//   warp 1     one elected thread issues tcgen05.mma (kind::f16, f16 inputs,
-//              fp32 accumulators in TMEM) and tcgen05.commit
-//   warps 2-9  stream the expert's Q4_K / Q8_0 blocks with 16-byte loads,
-//              dequantise in registers (f32 w = s*q - m, then f16) and store
-//              the tile in the canonical K-major SWIZZLE_128B layout; warps 4-7
-//              then run the epilogue from TMEM (tcgen05.ld 32x32b)
-// Stages are double/triple buffered through mbarriers. Every wait is bounded by
-// %globaltimer (2 s); on expiry the CTA records an error code, drains its own
+// the same tensor-core rate.
+//
+// Persistent kernel: one CTA per SM walks work items (tile, 128-row block)
+// blockIdx.x, blockIdx.x + gridDim.x, ... Warp roles (14 warps):
+//   warp 0      TMA producer: the raw quant blocks of the item's 128 weight
+//               rows (2-D tensor map over the expert-major qs plane, 128 values
+//               per stage, a deep ring) and the token operand (f16 rows, 128B
+//               swizzle, K-major; no multicast anywhere)
+//   warp 1      one thread issues tcgen05.mma with the weight operand A in TMEM
+//               and the token operand B in shared memory, fp32 accumulators in
+//               TMEM, tcgen05.commit to the ring barriers
+//   warps 2-9   dequantise from shared memory with packed half2 arithmetic
+//               (Q4_K: s*q - m per 32-value sub-block; Q8_0: d*q) and write A
+//               into TMEM with tcgen05.st (row m of A = TMEM lane m, two f16 per
+//               column); the block headers ride in the same TMA stages
+//   warps 10-13 epilogue: tcgen05.ld of the accumulators, SwiGLU, f16 stores
+// The weight tile never passes through shared memory, which halves the shared
+// memory traffic per K step. The down GEMM double-buffers its accumulators so
+// its epilogue overlaps the next item's main loop.
+// Every wait is bounded by %globaltimer (2 s): on expiry the CTA records an
+// error code (read by the host at its next synchronisation), drains its own
 // copies and MMAs, frees TMEM and exits.
 #include <cudaTypedefs.h>
 
@@ -34,15 +44,20 @@
 namespace aero {
 namespace {
 
-constexpr int kBK = 64;                        // K per stage: 64 f16 = one 128-byte swizzle row
+constexpr int kBK = 64;          // K per MMA stage (A and B)
+constexpr int kRawK = 128;       // K per raw (quant) stage
 constexpr int kTileM = 128;
-constexpr int kThreads = 320;
-constexpr int kDeqThreads = 256;
-constexpr uint32_t kABytes = kTileM * kBK * 2;  // 16 KiB per weight operand per stage
-constexpr uint32_t kBBytes = kGemmNT * kBK * 2; // 32 KiB token operand per stage
+constexpr int kThreads = 448;    // 14 warps
+constexpr int kBStages = 4;
+constexpr uint32_t kBStageBytes = kGemmNT * kBK * 2;  // 24 KiB: up to 192 token rows x 128 B
+constexpr uint32_t kRawRing = 96 * 1024;
 constexpr uint64_t kWaitNs = 2000000000ull;
+// TMEM columns
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kAccStride = kGemmNT;     // 192 columns per accumulator
+constexpr uint32_t kAColBase = 2 * kGemmNT;  // 384: two A stages of 64 columns (gate/up) or 32 (down)
 
-enum : int { kErrFullA = 1, kErrFullB = 2, kErrEmpty = 3, kErrAcc = 4 };
+enum : int { kErrRawFull = 1, kErrBFull = 2, kErrEmpty = 3, kErrAcc = 4, kErrAFull = 5, kErrAEmpty = 6 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -69,7 +84,7 @@ __device__ __forceinline__ uint64_t gtimer() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-// Bounded wait that ignores the abort flag (used to drain this thread's own copies).
+// Bounded wait that ignores the abort flag (used to drain this thread's own work).
 __device__ bool mbar_wait_timed(uint32_t bar, uint32_t parity) {
     const uint64_t t0 = gtimer();
     while (!mbar_try(bar, parity))
@@ -94,15 +109,15 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
-__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
+// D (TMEM) += A (TMEM) * B (shared memory descriptor)
+__device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc, uint32_t acc) {
     asm volatile(
-        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(
             d_tmem),
-        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(acc));
+        "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(acc));
 }
 __device__ __forceinline__ void umma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
@@ -114,27 +129,46 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
           "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
         : "r"(taddr));
 }
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+        "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+        : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
-// K-major operand, SWIZZLE_128B: 8-row groups 1024 bytes apart (SBO), leading
+// K-major B operand, SWIZZLE_128B: 8-row groups 1024 bytes apart (SBO), leading
 // offset unused, descriptor version 1, layout type 2.
 __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
     return (uint64_t)((saddr & 0x3FFFFu) >> 4) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
            ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
-// kind::f16 instruction descriptor: f32 accumulate, f16 A and B (format 0), both
-// K-major.
+// kind::f16 instruction descriptor: f32 accumulate, f16 A and B (format 0), both K-major.
 __device__ __forceinline__ uint32_t idesc_f16(int M, int N) {
     return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-// byte offset of 16-byte chunk c (0..7) of row r inside a SWIZZLE_128B tile
-__device__ __forceinline__ uint32_t sw128_off(int r, int c) {
-    return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((c ^ (r & 7)) << 4));
 }
 
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     __half2 v = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&v);
+}
+__device__ __forceinline__ __half2 u2h(uint32_t v) { return *reinterpret_cast<__half2*>(&v); }
+__device__ __forceinline__ uint32_t h2u(__half2 v) { return *reinterpret_cast<uint32_t*>(&v); }
+
+// Two 4-bit codes (in bits 0-3 and 16-19) -> their exact f16 values: each code
+// lands in the low mantissa bits of 1024.0 (0x6400), then 1024 is subtracted.
+__device__ __forceinline__ __half2 nib2_to_h2(uint32_t spread) {
+    const uint32_t v = (spread & 0x000F000Fu) | 0x64006400u;
+    return __hsub2(u2h(v), u2h(0x64006400u));
+}
+// Two signed 8-bit codes biased by 128 (in bits 0-7 and 16-23) -> exact f16:
+// 1024 + (q + 128), minus 1152.
+__device__ __forceinline__ __half2 byte2_to_h2(uint32_t spread_biased) {
+    const uint32_t v = (spread_biased & 0x00FF00FFu) | 0x64006400u;
+    return __hsub2(u2h(v), u2h(0x64806480u));
 }
 
 struct GemmParams {
@@ -142,120 +176,100 @@ struct GemmParams {
     QMat S0, S1;          // shared expert
     const GemmTile* tiles;
     const int32_t* n_tiles;
-    int K, Ks;            // reduction length for routed / shared tiles
+    int K, Ks;            // reduction length for routed / shared items
     int MT, MTs, MTmax;   // 128-row blocks for routed / shared
+    int e_begin;          // first expert held by the planes (expert parallelism)
     __half* out;
     int out_ld;
     int32_t* err;
 };
 
-// Raw quant data one dequant thread needs for one stage and one matrix.
-struct Raw {
-    uint4 q0, q1;   // Q4_K: q0; Q8_0: q0, q1 (32 int8)
-    uint4 meta;     // Q4_K: 16-byte header; Q8_0: .x = fp16 scale
+struct Item {
+    GemmTile t;
+    int mt, nkb, N;
+    bool shared;
 };
 
-template <int DT>
-__device__ __forceinline__ void raw_load(const QMat& m, int e, int row, int kb, int h, Raw& r) {
-    const uint8_t* qrow = qm_row_qs(m, e, row);
-    const uint8_t* mrow = qm_row_meta(m, e, row);
-    const int k0 = kb * kBK;
-    if (DT == AERO_DT_Q4_K) {
-        const int sb = k0 >> 8, g = (k0 >> 6) & 3;
-        r.q0 = ld_stream16(qrow + sb * 128 + g * 32 + h * 16);
-        r.meta = __ldg(reinterpret_cast<const uint4*>(mrow + sb * 16));
-    } else {
-        const int blk = (k0 >> 5) + h;
-        r.q0 = ld_stream16(qrow + blk * 32);
-        r.q1 = ld_stream16(qrow + blk * 32 + 16);
-        r.meta.x = (uint32_t)__ldg(reinterpret_cast<const unsigned short*>(mrow) + blk);
+// The next work item of this CTA at or after w (skipping blocks a shared tile lacks).
+__device__ __forceinline__ bool item_at(const GemmParams& p, int n_tiles, int& w, Item& it) {
+    const int total = n_tiles * p.MTmax;
+    while (w < total) {
+        const int ti = w / p.MTmax, mt = w % p.MTmax;
+        const GemmTile t = p.tiles[ti];
+        const bool sh = t.expert < 0;
+        if (mt < (sh ? p.MTs : p.MT)) {
+            it.t = t;
+            it.mt = mt;
+            it.shared = sh;
+            it.nkb = (sh ? p.Ks : p.K) / kBK;
+            it.N = (t.nvalid + 15) & ~15;
+            return true;
+        }
+        w += gridDim.x;
     }
+    return false;
 }
 
-// Dequantise and store one thread's share (row r, half h) of a 128 x 64 tile.
-template <int DT>
-__device__ __forceinline__ void raw_store(const Raw& raw, int kb, int r, int h, uint8_t* tile) {
-    if (DT == AERO_DT_Q4_K) {
-        const uint8_t* mb = reinterpret_cast<const uint8_t*>(&raw.meta);
-        const float d = __half2float(__ushort_as_half((unsigned short)(mb[0] | (mb[1] << 8))));
-        const float dmin = __half2float(__ushort_as_half((unsigned short)(mb[2] | (mb[3] << 8))));
-        const int g = (kb & 3);
-        int sc0, m0, sc1, m1;
-        q4k_sc_m(mb + 4, 2 * g, sc0, m0);
-        q4k_sc_m(mb + 4, 2 * g + 1, sc1, m1);
-        const float s0 = d * (float)sc0, n0 = -(dmin * (float)m0);
-        const float s1 = d * (float)sc1, n1 = -(dmin * (float)m1);
-        const uint32_t w[4] = {raw.q0.x, raw.q0.y, raw.q0.z, raw.q0.w};
-        uint32_t lo[8], hi[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const uint32_t l = w[i] & 0x0F0F0F0Fu, u = (w[i] >> 4) & 0x0F0F0F0Fu;
-            lo[2 * i] = pack_h2(fmaf(ubyte_to_f(l, 0), s0, n0), fmaf(ubyte_to_f(l, 1), s0, n0));
-            lo[2 * i + 1] = pack_h2(fmaf(ubyte_to_f(l, 2), s0, n0), fmaf(ubyte_to_f(l, 3), s0, n0));
-            hi[2 * i] = pack_h2(fmaf(ubyte_to_f(u, 0), s1, n1), fmaf(ubyte_to_f(u, 1), s1, n1));
-            hi[2 * i + 1] = pack_h2(fmaf(ubyte_to_f(u, 2), s1, n1), fmaf(ubyte_to_f(u, 3), s1, n1));
-        }
-        // lo values are k = 16h .. 16h+15 (chunks 2h, 2h+1); hi are 32 + 16h .. (chunks 4+2h, 5+2h)
-        *reinterpret_cast<uint4*>(tile + sw128_off(r, 2 * h)) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
-        *reinterpret_cast<uint4*>(tile + sw128_off(r, 2 * h + 1)) = make_uint4(lo[4], lo[5], lo[6], lo[7]);
-        *reinterpret_cast<uint4*>(tile + sw128_off(r, 4 + 2 * h)) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
-        *reinterpret_cast<uint4*>(tile + sw128_off(r, 5 + 2 * h)) = make_uint4(hi[4], hi[5], hi[6], hi[7]);
-    } else {
-        const float d = __half2float(__ushort_as_half((unsigned short)raw.meta.x));
-        const uint32_t w[8] = {raw.q0.x, raw.q0.y, raw.q0.z, raw.q0.w, raw.q1.x, raw.q1.y, raw.q1.z, raw.q1.w};
-        uint32_t o[16];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const uint32_t wb = w[i] ^ 0x80808080u;
-            o[2 * i] = pack_h2(d * sbyte_biased_to_f(wb, 0), d * sbyte_biased_to_f(wb, 1));
-            o[2 * i + 1] = pack_h2(d * sbyte_biased_to_f(wb, 2), d * sbyte_biased_to_f(wb, 3));
-        }
-        // values k = 32h .. 32h+31: chunks 4h .. 4h+3
-#pragma unroll
-        for (int c = 0; c < 4; ++c)
-            *reinterpret_cast<uint4*>(tile + sw128_off(r, 4 * h + c)) =
-                make_uint4(o[4 * c], o[4 * c + 1], o[4 * c + 2], o[4 * c + 3]);
-    }
-}
+// Kernel tensor maps: token operand, then per weight family the qs plane and
+// the header plane, routed (w) and shared (s), matrix 0 and 1.
+struct GemmMaps {
+    CUtensorMap b, w0, w1, s0, s1, mw0, mw1, ms0, ms1;
+};
 
 template <int DT, bool GATEUP>
-__global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_b, GemmParams p) {
-    constexpr int kStages = GATEUP ? 3 : 4;
-    constexpr uint32_t kStage = (GATEUP ? 2 : 1) * kABytes + kBBytes;
-    constexpr uint32_t kTmemCols = GATEUP ? 512 : 256;
+struct Cfg {
+    static constexpr int kRawRowBytes = DT == AERO_DT_Q4_K ? kRawK / 2 : kRawK;  // 64 or 128
+    static constexpr int kMats = GATEUP ? 2 : 1;
+    static constexpr uint32_t kQsBytes = (uint32_t)kMats * kTileM * kRawRowBytes;
+    static constexpr uint32_t kMetaBytes = (uint32_t)kMats * kTileM * 16;  // a 16-byte header slice per row
+    static constexpr uint32_t kRawStageBytes = kQsBytes + kMetaBytes;
+    static constexpr int kRawStages = (int)(kRawRing / kRawStageBytes);
+    static constexpr int kAcc = GATEUP ? 1 : 2;  // accumulator buffers
+    static constexpr size_t kSmem = kRawRing + (size_t)kBStages * kBStageBytes + 1024 + 512;
+};
 
-    const int tile_i = blockIdx.x / p.MTmax, mt = blockIdx.x % p.MTmax;
-    if (tile_i >= *p.n_tiles) return;
-    const GemmTile t = p.tiles[tile_i];
-    const bool shared = t.expert < 0;
-    if (mt >= (shared ? p.MTs : p.MT)) return;
-    const QMat& A0 = shared ? p.S0 : p.A0;
-    const QMat& A1 = shared ? p.S1 : p.A1;
-    const int e = shared ? 0 : t.expert;
-    const int nkb = (shared ? p.Ks : p.K) / kBK;
-    const int N = (t.nvalid + 15) & ~15;
-    const int m0 = mt * kTileM;
+template <int DT, bool GATEUP>
+__global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_constant__ GemmMaps tm, GemmParams p) {
+    using C = Cfg<DT, GATEUP>;
+    constexpr int kRS = C::kRawStages;
+    const int n_tiles = *p.n_tiles;
 
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStage);
-    // full_a[s], full_b[s], empty[s], acc, drain
+    uint8_t* raw_ring = smem;           // kRS x kRawStageBytes
+    uint8_t* b_ring = smem + kRawRing;  // kBStages x kBStageBytes (1024-aligned)
+    uint64_t* bars = reinterpret_cast<uint64_t*>(b_ring + kBStages * kBStageBytes);
     const uint32_t bar0 = smem_u32(bars);
-    auto full_a = [&](int s) { return bar0 + 8u * s; };
-    auto full_b = [&](int s) { return bar0 + 8u * (kStages + s); };
-    auto empty = [&](int s) { return bar0 + 8u * (2 * kStages + s); };
-    const uint32_t acc_bar = bar0 + 8u * (3 * kStages), drain_bar = acc_bar + 8u;
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 3 * kStages + 2);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * kStages + 3);
+    // barrier table: raw_full[kRS], raw_empty[kRS], b_full[4], b_empty[4], a_full[2], a_empty[2],
+    // acc_full[2], acc_empty[2], drain
+    auto raw_full = [&](int s) { return bar0 + 8u * s; };
+    auto raw_empty = [&](int s) { return bar0 + 8u * (kRS + s); };
+    auto b_full = [&](int s) { return bar0 + 8u * (2 * kRS + s); };
+    auto b_empty = [&](int s) { return bar0 + 8u * (2 * kRS + kBStages + s); };
+    auto a_full = [&](int s) { return bar0 + 8u * (2 * kRS + 2 * kBStages + s); };
+    auto a_empty = [&](int s) { return bar0 + 8u * (2 * kRS + 2 * kBStages + 2 + s); };
+    auto acc_full = [&](int s) { return bar0 + 8u * (2 * kRS + 2 * kBStages + 4 + s); };
+    auto acc_empty = [&](int s) { return bar0 + 8u * (2 * kRS + 2 * kBStages + 6 + s); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * kRS + 2 * kBStages + 8);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * kRS + 2 * kBStages + 9);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kRS + 2 * kBStages + 10);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
-        for (int s = 0; s < kStages; ++s) {
-            mbar_init(full_a(s), kDeqThreads);
-            mbar_init(full_b(s), 1);
-            mbar_init(empty(s), 1);
+        for (int s = 0; s < kRS; ++s) {
+            mbar_init(raw_full(s), 1);
+            mbar_init(raw_empty(s), 8);
         }
-        mbar_init(acc_bar, 1);
+        for (int s = 0; s < kBStages; ++s) {
+            mbar_init(b_full(s), 1);
+            mbar_init(b_empty(s), 1);
+        }
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(a_full(s), 8);
+            mbar_init(a_empty(s), 1);
+            mbar_init(acc_full(s), 1);
+            mbar_init(acc_empty(s), 4);
+        }
         mbar_init(drain_bar, 1);
         *abort_flag = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -276,122 +290,264 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
 
     if (warp == 0) {
         if (lane == 0) {
-            // ---- token operand producer
-            int last_kb[kStages];
-            for (int s = 0; s < kStages; ++s) last_kb[s] = -1;
+            // ---------------------------------------------------------- producer
+            int raw_n = 0, b_n = 0;  // running stage counters
             bool ok = true;
-            for (int kb = 0; kb < nkb && ok; ++kb) {
-                const int s = kb % kStages;
-                const uint32_t ph = (kb / kStages) & 1;
-                if (!mbar_wait(empty(s), ph ^ 1, abort_flag)) {
-                    fail(kErrEmpty);
-                    ok = false;
-                    break;
+            Item it;
+            for (int w = blockIdx.x; ok && item_at(p, n_tiles, w, it); w += gridDim.x) {
+                const CUtensorMap* w0 = it.shared ? &tm.s0 : &tm.w0;
+                const CUtensorMap* w1 = it.shared ? &tm.s1 : &tm.w1;
+                const CUtensorMap* m0 = it.shared ? &tm.ms0 : &tm.mw0;
+                const CUtensorMap* m1 = it.shared ? &tm.ms1 : &tm.mw1;
+                const QMat& A = it.shared ? p.S0 : p.A0;
+                const int y0 = (it.shared ? 0 : (it.t.expert - p.e_begin)) * A.rows + it.mt * kTileM;
+                for (int kb = 0; kb < it.nkb && ok; ++kb) {
+                    if ((kb & 1) == 0) {
+                        const int s = raw_n % kRS;
+                        if (!mbar_wait(raw_empty(s), ((raw_n / kRS) & 1) ^ 1, abort_flag)) {
+                            fail(kErrEmpty);
+                            ok = false;
+                            break;
+                        }
+                        const uint32_t dst = smem_u32(raw_ring + s * C::kRawStageBytes);
+                        mbar_expect_tx(raw_full(s), C::kRawStageBytes);
+                        // qs of values [64 kb, 64 kb + 128), and the 16-byte header slice
+                        // covering the 256 values around them
+                        const int x = (kb / 2) * C::kRawRowBytes;
+                        const int xm = (kb / 4) * 16;
+                        tma_load_2d(dst, w0, x, y0, raw_full(s));
+                        tma_load_2d(dst + C::kQsBytes, m0, xm, y0, raw_full(s));
+                        if (GATEUP) {
+                            tma_load_2d(dst + kTileM * C::kRawRowBytes, w1, x, y0, raw_full(s));
+                            tma_load_2d(dst + C::kQsBytes + kTileM * 16, m1, xm, y0, raw_full(s));
+                        }
+                        ++raw_n;
+                    }
+                    const int sb = b_n % kBStages;
+                    if (!mbar_wait(b_empty(sb), ((b_n / kBStages) & 1) ^ 1, abort_flag)) {
+                        fail(kErrEmpty);
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t dst = smem_u32(b_ring + sb * kBStageBytes);
+                    mbar_expect_tx(b_full(sb), (uint32_t)it.N * kBK * 2);
+                    for (int r = 0; r < it.N; r += 16)
+                        tma_load_2d(dst + (uint32_t)r * 128, &tm.b, kb * kBK, it.t.pos0 + r, b_full(sb));
+                    ++b_n;
                 }
-                const uint32_t b_dst = smem_u32(smem + s * kStage + (GATEUP ? 2 : 1) * kABytes);
-                mbar_expect_tx(full_b(s), (uint32_t)N * kBK * 2);
-                for (int r = 0; r < N; r += 16) tma_load_2d(b_dst + (uint32_t)r * 128, &tmap_b, kb * kBK, t.pos0 + r, full_b(s));
-                last_kb[s] = kb;
             }
-            if (!ok || *abort_flag) {
+            if (!ok) {
                 // let every copy this thread issued land before the CTA exits
-                for (int s = 0; s < kStages; ++s)
-                    if (last_kb[s] >= 0) mbar_wait_timed(full_b(s), (last_kb[s] / kStages) & 1);
+                for (int i = 0; i < kRS && i < raw_n; ++i) {
+                    const int n = raw_n - 1 - i;
+                    mbar_wait_timed(raw_full(n % kRS), (n / kRS) & 1);
+                }
+                for (int i = 0; i < kBStages && i < b_n; ++i) {
+                    const int n = b_n - 1 - i;
+                    mbar_wait_timed(b_full(n % kBStages), (n / kBStages) & 1);
+                }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
-            // ---- MMA issuer
-            const uint32_t idesc = idesc_f16(kTileM, N);
-            bool issued = false, ok = true;
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int s = kb % kStages;
-                const uint32_t ph = (kb / kStages) & 1;
-                if (!mbar_wait(full_a(s), ph, abort_flag)) {
-                    fail(kErrFullA);
-                    ok = false;
-                    break;
-                }
-                if (!mbar_wait(full_b(s), ph, abort_flag)) {
-                    fail(kErrFullB);
+            // ---------------------------------------------------------- MMA issuer
+            int a_n = 0, b_n = 0, item_n = 0;
+            bool ok = true, issued = false;
+            Item it;
+            for (int w = blockIdx.x; ok && item_at(p, n_tiles, w, it); w += gridDim.x, ++item_n) {
+                const int ab = item_n % C::kAcc;
+                if (!mbar_wait(acc_empty(ab), ((item_n / C::kAcc) & 1) ^ 1, abort_flag)) {
+                    fail(kErrAcc);
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(smem + s * kStage);
-                const uint32_t b = a0 + (GATEUP ? 2 : 1) * kABytes;
+                const uint32_t idesc = idesc_f16(kTileM, it.N);
+                const uint32_t d0 = tmem + (GATEUP ? 0u : (uint32_t)ab * kAccStride);
+                for (int kb = 0; kb < it.nkb; ++kb) {
+                    const int sa = a_n & 1, sb = b_n % kBStages;
+                    if (!mbar_wait(a_full(sa), (a_n >> 1) & 1, abort_flag)) {
+                        fail(kErrAFull);
+                        ok = false;
+                        break;
+                    }
+                    if (!mbar_wait(b_full(sb), (b_n / kBStages) & 1, abort_flag)) {
+                        fail(kErrBFull);
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t b = smem_u32(b_ring + sb * kBStageBytes);
+                    const uint32_t a0 = tmem + kAColBase + (uint32_t)sa * (GATEUP ? 64u : 32u);
 #pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk) {
-                    const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
-                    umma_f16(tmem, sw128_desc(a0 + kk * 32), sw128_desc(b + kk * 32), idesc, acc);
-                    if (GATEUP) umma_f16(tmem + 256, sw128_desc(a0 + kABytes + kk * 32), sw128_desc(b + kk * 32), idesc, acc);
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
+                        umma_ts(d0, a0 + kk * 8, sw128_desc(b + kk * 32), idesc, acc);
+                        if (GATEUP) umma_ts(d0 + kAccStride, a0 + 32 + kk * 8, sw128_desc(b + kk * 32), idesc, acc);
+                    }
+                    issued = true;
+                    umma_commit(a_empty(sa));
+                    umma_commit(b_empty(sb));
+                    ++a_n;
+                    ++b_n;
                 }
-                issued = true;
-                umma_commit(empty(s));
+                if (ok) umma_commit(acc_full(ab));
             }
-            if (ok) {
-                umma_commit(acc_bar);
-            } else if (issued) {
+            if (!ok && issued) {
                 umma_commit(drain_bar);  // MMAs in flight must finish before TMEM is freed
                 mbar_wait_timed(drain_bar, 0);
             }
         }
-    } else {
-        // ---- dequant producers (warps 2-9), then epilogue (warps 4-7)
-        const int dt = threadIdx.x - 64;
-        const int r = dt >> 1, h = dt & 1;
-        const int row = m0 + r;
-        Raw cur0, cur1, nxt0, nxt1;
-        raw_load<DT>(A0, e, row, 0, h, cur0);
-        if (GATEUP) raw_load<DT>(A1, e, row, 0, h, cur1);
+    } else if (warp < 10) {
+        // -------------------------------------------------------------- dequant
+        const int grp = (warp - 2) >> 2;  // gate/up: the matrix; down: which 32 of the 64 values
+        const int q = warp & 3;           // TMEM lane quarter this warp may access
+        const int r = q * 32 + lane;      // weight row within the 128-row block
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        int raw_n = 0, a_n = 0;
         bool ok = true;
-        for (int kb = 0; kb < nkb; ++kb) {
-            if (kb + 1 < nkb) {
-                raw_load<DT>(A0, e, row, kb + 1, h, nxt0);
-                if (GATEUP) raw_load<DT>(A1, e, row, kb + 1, h, nxt1);
-            }
-            const int s = kb % kStages;
-            const uint32_t ph = (kb / kStages) & 1;
-            if (!mbar_wait(empty(s), ph ^ 1, abort_flag)) {
-                fail(kErrEmpty);
-                ok = false;
-                break;
-            }
-            uint8_t* a0 = smem + s * kStage;
-            raw_store<DT>(cur0, kb, r, h, a0);
-            if (GATEUP) raw_store<DT>(cur1, kb, r, h, a0 + kABytes);
-            fence_proxy_async();
-            mbar_arrive(full_a(s));
-            cur0 = nxt0;
-            if (GATEUP) cur1 = nxt1;
-        }
-        // tcgen05.ld is warp-collective: keep the epilogue decision warp-uniform
-        ok = __all_sync(0xffffffffu, ok);
-        if (ok && warp >= 4 && warp < 8) {
-            const int q = warp & 3;
-            const bool got = __all_sync(0xffffffffu, mbar_wait(acc_bar, 0, abort_flag));
-            if (!got) {
-                fail(kErrAcc);
-            } else {
+        Item it;
+        const int mat = GATEUP ? grp : 0;
+        for (int w = blockIdx.x; ok && item_at(p, n_tiles, w, it); w += gridDim.x) {
+            for (int kb = 0; kb < it.nkb; ++kb) {
+                const int s = raw_n % kRS;
+                if ((kb & 1) == 0) {
+                    const bool got = __all_sync(0xffffffffu, mbar_wait(raw_full(s), (raw_n / kRS) & 1, abort_flag));
+                    if (!got) {
+                        if (lane == 0) fail(kErrRawFull);
+                        ok = false;
+                        break;
+                    }
+                }
+                const int sa = a_n & 1;
+                const bool got = __all_sync(0xffffffffu, mbar_wait(a_empty(sa), ((a_n >> 1) & 1) ^ 1, abort_flag));
+                if (!got) {
+                    if (lane == 0) fail(kErrAEmpty);
+                    ok = false;
+                    break;
+                }
                 tc_fence_after();
-                const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-                const int f = m0 + q * 32 + lane;
-                for (int c0 = 0; c0 < N; c0 += 16) {
-                    uint32_t g[16], u[16];
-                    tmem_ld16(tmem + lane_base + c0, g);
-                    if (GATEUP) tmem_ld16(tmem + lane_base + 256 + c0, u);
-                    tmem_wait_ld();
+                const uint8_t* stage = raw_ring + s * C::kRawStageBytes;
+                // this row's qs for the stage (TMA-swizzled: 64B for Q4_K rows of 64 bytes,
+                // 128B for Q8_0 rows of 128 bytes: logical 16-byte chunk c sits at c ^ f(r))
+                const uint8_t* qrow = stage + mat * kTileM * C::kRawRowBytes + r * C::kRawRowBytes;
+                const int swz = DT == AERO_DT_Q4_K ? ((r >> 1) & 3) : (r & 7);
+                auto qchunk = [&](int c) { return *reinterpret_cast<const uint4*>(qrow + ((c ^ swz) << 4)); };
+                const uint4 meta = *reinterpret_cast<const uint4*>(stage + C::kQsBytes + mat * kTileM * 16 + r * 16);
+                // columns 0-15 and 16-31 of this K-block's 32 TMEM columns (two f16 each);
+                // the down GEMM's warp group `grp` produces only its own half
+                uint32_t c0[16], c1[16];
+                const bool need0 = GATEUP || grp == 0, need1 = GATEUP || grp == 1;
+                if (DT == AERO_DT_Q4_K) {
+                    const uint8_t* mb = reinterpret_cast<const uint8_t*>(&meta);
+                    const float d = __half2float(__ushort_as_half((unsigned short)(mb[0] | (mb[1] << 8))));
+                    const float dmin = __half2float(__ushort_as_half((unsigned short)(mb[2] | (mb[3] << 8))));
+                    const int g = kb & 3;
+                    int sc0, m0, sc1, m1;
+                    q4k_sc_m(mb + 4, 2 * g, sc0, m0);
+                    q4k_sc_m(mb + 4, 2 * g + 1, sc1, m1);
+                    const __half2 s0 = __float2half2_rn(d * (float)sc0), n0 = __float2half2_rn(-(dmin * (float)m0));
+                    const __half2 s1 = __float2half2_rn(d * (float)sc1), n1 = __float2half2_rn(-(dmin * (float)m1));
+                    // 32 bytes of this K-block: chunks 2 (kb & 1) and 2 (kb & 1) + 1 of the 64-byte row
+                    const uint4 v0 = qchunk(2 * (kb & 1)), v1 = qchunk(2 * (kb & 1) + 1);
+                    const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                    // byte pair (2j, 2j+1): low nibbles -> column j, high nibbles -> column 16 + j
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const int col = c0 + j;
-                        if (col < t.nvalid) {
-                            float v = __uint_as_float(g[j]);
-                            if (GATEUP) v = silu_f(v) * __uint_as_float(u[j]);
-                            p.out[(int64_t)(t.pos0 + col) * p.out_ld + f] = __float2half_rn(v);
+                    for (int i = 0; i < 8; ++i) {
+                        const uint32_t a = __byte_perm(wv[i], 0, 0x4140), b = __byte_perm(wv[i], 0, 0x4342);
+                        if (need0) {
+                            c0[2 * i] = h2u(__hfma2(nib2_to_h2(a), s0, n0));
+                            c0[2 * i + 1] = h2u(__hfma2(nib2_to_h2(b), s0, n0));
+                        }
+                        if (need1) {
+                            c1[2 * i] = h2u(__hfma2(nib2_to_h2(a >> 4), s1, n1));
+                            c1[2 * i + 1] = h2u(__hfma2(nib2_to_h2(b >> 4), s1, n1));
+                        }
+                    }
+                } else {
+                    // the 16-byte slice holds 8 fp16 scales for 256 values; this K-block uses two
+                    const uint32_t mw[4] = {meta.x, meta.y, meta.z, meta.w};
+                    const uint32_t sc8 = mw[kb & 3];
+                    const __half2 d0 = __half2half2(__ushort_as_half((unsigned short)(sc8 & 0xFFFFu)));
+                    const __half2 d1 = __half2half2(__ushort_as_half((unsigned short)(sc8 >> 16)));
+                    // 64 bytes of this K-block: chunks 4 (kb & 1) .. 4 (kb & 1) + 3 of the 128-byte row;
+                    // the first 32 values use scale d0, the next 32 d1
+                    if (need0) {
+                        const uint4 v0 = qchunk(4 * (kb & 1)), v1 = qchunk(4 * (kb & 1) + 1);
+                        const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const uint32_t wb = wv[i] ^ 0x80808080u;
+                            c0[2 * i] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4140)), d0));
+                            c0[2 * i + 1] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4342)), d0));
+                        }
+                    }
+                    if (need1) {
+                        const uint4 v0 = qchunk(4 * (kb & 1) + 2), v1 = qchunk(4 * (kb & 1) + 3);
+                        const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const uint32_t wb = wv[i] ^ 0x80808080u;
+                            c1[2 * i] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4140)), d1));
+                            c1[2 * i + 1] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4342)), d1));
                         }
                     }
                 }
+                // gate/up: this warp's matrix, 32 columns; down: this warp group's 16 columns
+                const uint32_t acol = tmem + lane_base + kAColBase + (uint32_t)sa * (GATEUP ? 64u : 32u);
+                if (GATEUP) {
+                    tmem_st16(acol + (uint32_t)grp * 32u, c0);
+                    tmem_st16(acol + (uint32_t)grp * 32u + 16u, c1);
+                } else if (grp == 0) {
+                    tmem_st16(acol, c0);
+                } else {
+                    tmem_st16(acol + 16u, c1);
+                }
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(a_full(sa));
+                ++a_n;
+                if ((kb & 1) || kb + 1 == it.nkb) {
+                    if (lane == 0) mbar_arrive(raw_empty(s));
+                    ++raw_n;
+                }
             }
+        }
+    } else {
+        // -------------------------------------------------------------- epilogue
+        const int q = warp & 3;
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        int item_n = 0;
+        Item it;
+        for (int w = blockIdx.x; item_at(p, n_tiles, w, it); w += gridDim.x, ++item_n) {
+            const int ab = item_n % C::kAcc;
+            const bool got = __all_sync(0xffffffffu, mbar_wait(acc_full(ab), (item_n / C::kAcc) & 1, abort_flag));
+            if (!got) {
+                if (lane == 0) fail(kErrAcc);
+                break;
+            }
+            tc_fence_after();
+            const uint32_t d0 = tmem + lane_base + (GATEUP ? 0u : (uint32_t)ab * kAccStride);
+            const int f = it.mt * kTileM + q * 32 + lane;
+            for (int c0 = 0; c0 < it.N; c0 += 16) {
+                uint32_t g[16], u[16];
+                tmem_ld16(d0 + c0, g);
+                if (GATEUP) tmem_ld16(d0 + kAccStride + c0, u);
+                tmem_wait_ld();
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int col = c0 + j;
+                    if (col < it.t.nvalid) {
+                        float v = __uint_as_float(g[j]);
+                        if (GATEUP) v = silu_f(v) * __uint_as_float(u[j]);
+                        p.out[(int64_t)(it.t.pos0 + col) * p.out_ld + f] = __float2half_rn(v);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(acc_empty(ab));
         }
     }
     tc_fence_before();
@@ -452,8 +608,8 @@ __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t* __rest
 }
 
 __global__ void combine_h_kernel(const __half* __restrict__ y, const int32_t* __restrict__ inv,
-                                    const float* __restrict__ w, const float* __restrict__ sgate, int T, int k, int d,
-                                    int has_shared, float* __restrict__ out) {
+                                 const float* __restrict__ w, const float* __restrict__ sgate, int T, int k, int d,
+                                 int has_shared, float* __restrict__ out) {
     const int d4 = d >> 2;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)T * d4) return;
@@ -462,8 +618,8 @@ __global__ void combine_h_kernel(const __half* __restrict__ y, const int32_t* __
     for (int s = 0; s < k; ++s) {
         const float wt = w[(int64_t)t * k + s];
         const uint2 v = __ldg(reinterpret_cast<const uint2*>(y + (int64_t)inv[(int64_t)t * k + s] * d + c));
-        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
-        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+        const float2 lo = __half22float2(u2h(v.x));
+        const float2 hi = __half22float2(u2h(v.y));
         a0 += wt * lo.x;
         a1 += wt * lo.y;
         a2 += wt * hi.x;
@@ -472,8 +628,8 @@ __global__ void combine_h_kernel(const __half* __restrict__ y, const int32_t* __
     if (has_shared) {
         const float g = sgate[t];
         const uint2 v = __ldg(reinterpret_cast<const uint2*>(y + ((int64_t)T * k + t) * d + c));
-        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
-        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+        const float2 lo = __half22float2(u2h(v.x));
+        const float2 hi = __half22float2(u2h(v.y));
         a0 += g * lo.x;
         a1 += g * lo.y;
         a2 += g * hi.x;
@@ -496,8 +652,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D f16 tensor (rows x cols, row stride ld elements), box 16 rows x 64 cols, 128B swizzle.
-bool make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld) {
+// 2-D f16 activations (rows x cols, row stride ld elements): box 16 rows x 64 cols, 128B swizzle.
+bool make_tmap_act(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {cols, rows};
@@ -509,20 +665,45 @@ bool make_tmap(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, u
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// A weight plane as 2-D bytes [n_expert * rows][row bytes] (experts must be
+// contiguous): box = 128 rows x box_bytes.
+bool make_tmap_plane(CUtensorMap* m, const uint8_t* base, uint64_t row_bytes, int rows, int64_t estride,
+                     int n_local_experts, int box_bytes, CUtensorMapSwizzle swz) {
+    auto fn = encode_fn();
+    if (!fn || !base) return false;
+    if ((uint64_t)estride != row_bytes * (uint64_t)rows || row_bytes % 16) return false;
+    cuuint64_t dims[2] = {row_bytes, (cuuint64_t)rows * (cuuint64_t)n_local_experts};
+    cuuint64_t strides[1] = {row_bytes};
+    cuuint32_t box[2] = {(cuuint32_t)box_bytes, (cuuint32_t)kTileM};
+    cuuint32_t es[2] = {1u, 1u};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, es,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+// qs plane: the raw bytes of 128 values per box row (Q4_K 64 B, 64B swizzle;
+// Q8_0 128 B, 128B swizzle). Header plane: 16-byte slices, no swizzle.
+bool make_tmap_qs(CUtensorMap* m, const QMat& q, int n_local) {
+    const bool q4 = q.dtype == AERO_DT_Q4_K;
+    return make_tmap_plane(m, q.qs, (uint64_t)qm_row_qs_bytes(q.dtype, q.cols), q.rows, q.qs_estride, n_local,
+                           q4 ? kRawK / 2 : kRawK, q4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+}
+bool make_tmap_meta(CUtensorMap* m, const QMat& q, int n_local) {
+    return make_tmap_plane(m, q.meta, (uint64_t)qm_row_meta_bytes(q.dtype, q.cols), q.rows, q.meta_estride, n_local, 16,
+                           CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+
 template <int DT, bool GATEUP>
-cudaError_t launch_gemm(const CUtensorMap& tmap, const GemmParams& p, int max_tiles, cudaStream_t s) {
-    constexpr int kStages = GATEUP ? 3 : 4;
-    constexpr size_t smem = (size_t)kStages * ((GATEUP ? 2 : 1) * kABytes + kBBytes) + 1024 + 256;
+cudaError_t launch_gemm(const GemmMaps& maps, const GemmParams& p, int n_sm, cudaStream_t s) {
+    using C = Cfg<DT, GATEUP>;
+    static_assert(C::kRawStages >= 2, "raw ring too small");
     static bool configured = false;
     if (!configured) {
         cudaError_t e = cudaFuncSetAttribute(grouped_gemm_kernel<DT, GATEUP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)smem);
+                                             (int)C::kSmem);
         if (e != cudaSuccess) return e;
         configured = true;
     }
-    const int grid = max_tiles * p.MTmax;
-    if (grid <= 0) return cudaSuccess;
-    grouped_gemm_kernel<DT, GATEUP><<<grid, kThreads, smem, s>>>(tmap, p);
+    grouped_gemm_kernel<DT, GATEUP><<<n_sm, kThreads, C::kSmem, s>>>(maps, p);
     return cudaGetLastError();
 }
 
@@ -554,18 +735,36 @@ bool gemm_setup(void* ws, size_t ws_bytes, int dp, int act_ld, int P_cap, int T_
     b->n_tiles = reinterpret_cast<int32_t*>(c);
     b->err = b->n_tiles + 1;
     b->rows_cap = (int)rows;
-    if (!make_tmap(&b->tmap_x, b->xperm, rows, (uint64_t)dp, (uint64_t)dp) ||
-        !make_tmap(&b->tmap_act, b->act, rows, (uint64_t)act_ld, (uint64_t)act_ld)) {
-        *why = "cuTensorMapEncodeTiled failed (driver entry point unavailable or bad layout)";
+    if (!make_tmap_act(&b->tmap_x, b->xperm, rows, (uint64_t)dp, (uint64_t)dp) ||
+        !make_tmap_act(&b->tmap_act, b->act, rows, (uint64_t)act_ld, (uint64_t)act_ld)) {
+        *why = "cuTensorMapEncodeTiled failed for the activation buffers";
         return false;
     }
     return true;
 }
 
-cudaError_t launch_prefill(const PrefillArgs& a, GemmBuffers& b, cudaStream_t s, int* launches) {
+bool gemm_weight_maps(const QMat& gate, const QMat& up, const QMat& down, const QMat& sg, const QMat& su, const QMat& sd,
+                      int n_local, int has_shared, GemmWeightMaps* m, std::string* why) {
+    // the planes' base pointers here are the allocations (expert e_begin first)
+    bool ok = make_tmap_qs(&m->q[0], gate, n_local) && make_tmap_qs(&m->q[1], up, n_local) &&
+              make_tmap_qs(&m->q[2], down, n_local) && make_tmap_meta(&m->m[0], gate, n_local) &&
+              make_tmap_meta(&m->m[1], up, n_local) && make_tmap_meta(&m->m[2], down, n_local);
+    if (ok && has_shared)
+        ok = make_tmap_qs(&m->q[3], sg, 1) && make_tmap_qs(&m->q[4], su, 1) && make_tmap_qs(&m->q[5], sd, 1) &&
+             make_tmap_meta(&m->m[3], sg, 1) && make_tmap_meta(&m->m[4], su, 1) && make_tmap_meta(&m->m[5], sd, 1);
+    if (ok && !has_shared)
+        for (int i = 0; i < 3; ++i) {
+            m->q[3 + i] = m->q[i];
+            m->m[3 + i] = m->m[i];
+        }
+    if (!ok) *why = "cuTensorMapEncodeTiled failed for an expert weight plane";
+    return ok;
+}
+
+cudaError_t launch_prefill(const PrefillArgs& a, GemmBuffers& b, const GemmWeightMaps& wm, cudaStream_t s,
+                           int* launches) {
     const int P = a.T * a.k;
     const int rows = P + (a.has_shared ? a.T : 0);
-    const int max_tiles = gemm_max_tiles(P, a.T, a.E, a.has_shared);
     {
         const int64_t n = (int64_t)rows * (a.dp / 8);
         gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(a.x, a.perm, a.k, P, rows, a.dp, b.xperm);
@@ -577,11 +776,12 @@ cudaError_t launch_prefill(const PrefillArgs& a, GemmBuffers& b, cudaStream_t s,
     g.tiles = b.tiles;
     g.n_tiles = b.n_tiles;
     g.err = b.err;
+    g.e_begin = a.e_begin;
     // gate/up
     g.A0 = a.gate;
     g.A1 = a.up;
-    g.S0 = a.sg;
-    g.S1 = a.su;
+    g.S0 = a.has_shared ? a.sg : a.gate;
+    g.S1 = a.has_shared ? a.su : a.up;
     g.K = a.dp;
     g.Ks = a.dp;
     g.MT = a.F / kTileM;
@@ -589,29 +789,44 @@ cudaError_t launch_prefill(const PrefillArgs& a, GemmBuffers& b, cudaStream_t s,
     g.MTmax = g.MT > g.MTs ? g.MT : g.MTs;
     g.out = b.act;
     g.out_ld = a.act_ld;
-    e = a.gate.dtype == AERO_DT_Q4_K ? launch_gemm<AERO_DT_Q4_K, true>(b.tmap_x, g, max_tiles, s)
-                                     : launch_gemm<AERO_DT_Q8_0, true>(b.tmap_x, g, max_tiles, s);
+    GemmMaps maps;
+    maps.b = b.tmap_x;
+    maps.w0 = wm.q[0];
+    maps.w1 = wm.q[1];
+    maps.s0 = wm.q[3];
+    maps.s1 = wm.q[4];
+    maps.mw0 = wm.m[0];
+    maps.mw1 = wm.m[1];
+    maps.ms0 = wm.m[3];
+    maps.ms1 = wm.m[4];
+    e = a.gate.dtype == AERO_DT_Q4_K ? launch_gemm<AERO_DT_Q4_K, true>(maps, g, a.n_sm, s)
+                                     : launch_gemm<AERO_DT_Q8_0, true>(maps, g, a.n_sm, s);
     if (e != cudaSuccess) return e;
     // down
     g.A0 = a.down;
     g.A1 = a.down;
-    g.S0 = a.sd;
-    g.S1 = a.sd;
+    g.S0 = a.has_shared ? a.sd : a.down;
+    g.S1 = g.S0;
     g.K = a.F;
-    g.Ks = a.Fs;
+    g.Ks = a.has_shared ? a.Fs : a.F;
     g.MT = a.dp / kTileM;
     g.MTs = a.has_shared ? a.dp / kTileM : 0;
     g.MTmax = g.MT;
     g.out = b.y;
     g.out_ld = a.dp;
-    e = a.down.dtype == AERO_DT_Q4_K ? launch_gemm<AERO_DT_Q4_K, false>(b.tmap_act, g, max_tiles, s)
-                                     : launch_gemm<AERO_DT_Q8_0, false>(b.tmap_act, g, max_tiles, s);
+    maps.b = b.tmap_act;
+    maps.w0 = maps.w1 = wm.q[2];
+    maps.s0 = maps.s1 = wm.q[5];
+    maps.mw0 = maps.mw1 = wm.m[2];
+    maps.ms0 = maps.ms1 = wm.m[5];
+    e = a.down.dtype == AERO_DT_Q4_K ? launch_gemm<AERO_DT_Q4_K, false>(maps, g, a.n_sm, s)
+                                     : launch_gemm<AERO_DT_Q8_0, false>(maps, g, a.n_sm, s);
     if (launches) *launches += 4;
     return e;
 }
 
-cudaError_t launch_combine_h(const __half* y, const int32_t* inv, const float* w, const float* sgate, int T,
-                                int k, int d, int has_shared, float* out, cudaStream_t s) {
+cudaError_t launch_combine_h(const __half* y, const int32_t* inv, const float* w, const float* sgate, int T, int k,
+                             int d, int has_shared, float* out, cudaStream_t s) {
     const int64_t n = (int64_t)T * (d / 4);
     if (n == 0) return cudaSuccess;
     combine_h_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(y, inv, w, sgate, T, k, d, has_shared, out);

@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <string>
+
 #include "common.cuh"
 
 namespace aero {
@@ -15,7 +17,7 @@ struct GemmTile {
     int32_t expert, pos0, nvalid, pad;
 };
 
-constexpr int kGemmNT = 256;  // token rows per tile (the MMA N extent, at most 256)
+constexpr int kGemmNT = 192;  // token rows per tile (the MMA N extent)
 
 // Upper bound on the number of tiles for P routed pairs and T tokens.
 inline int gemm_max_tiles(int P, int T, int E, int has_shared) {
@@ -41,6 +43,15 @@ struct GemmBuffers {
 bool gemm_setup(void* ws, size_t ws_bytes, int dp, int act_ld, int P_cap, int T_cap, int max_tiles, GemmBuffers* b,
                 std::string* why);
 
+// TMA descriptors of the expert weight planes: q[] the qs planes, m[] the
+// header planes, in the order gate, up, down, shared gate, shared up, shared down.
+struct GemmWeightMaps {
+    CUtensorMap q[6], m[6];
+};
+// Encode them for planes whose qs/meta pointers are the allocation bases.
+bool gemm_weight_maps(const QMat& gate, const QMat& up, const QMat& down, const QMat& sg, const QMat& su, const QMat& sd,
+                      int n_local, int has_shared, GemmWeightMaps* m, std::string* why);
+
 struct PrefillArgs {
     QMat gate, up, down, sg, su, sd;
     const float* x;           // (T, dp) f32
@@ -50,11 +61,14 @@ struct PrefillArgs {
     const int32_t* n_active;
     int T, k, dp, F, Fs, has_shared, E;
     int act_ld;
+    int e_begin;   // first expert held by the planes
+    int n_sm;      // persistent grid size
 };
 
 // gather -> tile list -> gate/up GEMM (+SwiGLU) -> down GEMM. Writes y (f16)
 // for rows [0, P + T); the combine reads it with launch_combine_h.
-cudaError_t launch_prefill(const PrefillArgs& a, GemmBuffers& b, cudaStream_t s, int* launches);
+cudaError_t launch_prefill(const PrefillArgs& a, GemmBuffers& b, const GemmWeightMaps& wm, cudaStream_t s,
+                           int* launches);
 cudaError_t launch_combine_h(const __half* y, const int32_t* inv, const float* w, const float* sgate,
                                 int T, int k, int d, int has_shared, float* out, cudaStream_t s);
 

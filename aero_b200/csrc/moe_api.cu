@@ -86,6 +86,8 @@ struct Handle {
     int gemm_min_tokens = 64; // calls with at least this many tokens use it
     GemmBuffers gb{};
     bool gb_ready = false;
+    GemmWeightMaps wmaps{};
+    int n_sm = 148;
     int last_active = -1;     // active experts of the last profiled call
 
     ~Handle() {
@@ -341,8 +343,10 @@ bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* 
         pa.has_shared = h.has_shared;
         pa.E = h.E;
         pa.act_ld = h.act_ld;
+        pa.e_begin = h.e_begin;
+        pa.n_sm = h.n_sm;
         int nl = 0;
-        if (!h.cuda_ok(launch_prefill(pa, h.gb, st, &nl), "prefill GEMM")) return false;
+        if (!h.cuda_ok(launch_prefill(pa, h.gb, h.wmaps, st, &nl), "prefill GEMM")) return false;
         h.launches += nl;
         mark(4);
         mark(5);
@@ -572,6 +576,14 @@ Handle* open_desc(const aero_cuda_moe_desc* d, std::string* why) {
     if (!h->cuda_ok(cudaStreamSynchronize(h->stream), "upload")) return bad("");
     // expert indices in the planes are local to [e_begin, e_end); the routed
     // paths below index them by global expert id, so shift the plane bases.
+    if (h->gemm_ok) {
+        std::string why;
+        if (!gemm_weight_maps(h->gate, h->up, h->down, h->sg, h->su, h->sd, h->e_end - h->e_begin, h->has_shared,
+                              &h->wmaps, &why))
+            h->gemm_ok = false;  // the layer still runs, on the GEMV path
+        cudaDeviceProp prop;
+        if (cudaGetDeviceProperties(&prop, h->device) == cudaSuccess) h->n_sm = prop.multiProcessorCount;
+    }
     auto shift = [&](QMat& m) {
         m.qs -= (int64_t)h->e_begin * m.qs_estride;
         if (m.meta) m.meta -= (int64_t)h->e_begin * m.meta_estride;
