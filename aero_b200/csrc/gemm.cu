@@ -14,11 +14,13 @@
 // the same tensor-core rate.
 //
 // Persistent kernel: one CTA per SM walks work items (tile, 128-row block)
-// blockIdx.x, blockIdx.x + gridDim.x, ... Warp roles (14 warps):
-//   warp 0      TMA producer: the raw quant blocks of the item's 128 weight
-//               rows (2-D tensor map over the expert-major qs plane, 128 values
-//               per stage, a deep ring) and the token operand (f16 rows, 128B
-//               swizzle, K-major; no multicast anywhere)
+// blockIdx.x, blockIdx.x + gridDim.x, ... Warp roles (15 warps):
+//   warp 0      TMA producer of the raw quant blocks of the item's 128 weight
+//               rows (2-D tensor maps over the expert-major qs and header
+//               planes, 128 values per stage, a deep ring)
+//   warp 14     TMA producer of the token operand (f16 rows, 128B swizzle,
+//               K-major, one box of the tile's height per K step; no multicast
+//               anywhere)
 //   warp 1      one thread issues tcgen05.mma with the weight operand A in TMEM
 //               and the token operand B in shared memory, fp32 accumulators in
 //               TMEM, tcgen05.commit to the ring barriers
@@ -26,7 +28,8 @@
 //               (Q4_K: s*q - m per 32-value sub-block; Q8_0: d*q) and write A
 //               into TMEM with tcgen05.st (row m of A = TMEM lane m, two f16 per
 //               column); the block headers ride in the same TMA stages
-//   warps 10-13 epilogue: tcgen05.ld of the accumulators, SwiGLU, f16 stores
+//   warps 10-13 epilogue: tcgen05.ld of the accumulators 32 columns at a time,
+//               SwiGLU, f16 results staged in shared memory for 16-byte stores
 // The weight tile never passes through shared memory, which halves the shared
 // memory traffic per K step. The down GEMM double-buffers its accumulators so
 // its epilogue overlaps the next item's main loop.
@@ -47,7 +50,8 @@ namespace {
 constexpr int kBK = 64;          // K per MMA stage (A and B)
 constexpr int kRawK = 128;       // K per raw (quant) stage
 constexpr int kTileM = 128;
-constexpr int kThreads = 448;    // 14 warps
+constexpr int kThreads = 480;    // 15 warps
+constexpr int kBMaps = kGemmNT / 16;  // token-operand maps, box heights 16, 32, ..., 192
 constexpr int kBStages = 4;
 constexpr uint32_t kBStageBytes = kGemmNT * kBK * 2;  // 24 KiB: up to 192 token rows x 128 B
 constexpr uint32_t kRawRing = 96 * 1024;
@@ -127,6 +131,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
         "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
           "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%"
+        "20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+          "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+          "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
@@ -210,10 +224,12 @@ __device__ __forceinline__ bool item_at(const GemmParams& p, int n_tiles, int& w
     return false;
 }
 
-// Kernel tensor maps: token operand, then per weight family the qs plane and
-// the header plane, routed (w) and shared (s), matrix 0 and 1.
+// Kernel tensor maps: the token operand with box heights 16, 32, ..., 192 rows
+// (one copy per K step covers a whole tile), then per weight family the qs
+// plane and the header plane, routed (w) and shared (s), matrix 0 and 1.
 struct GemmMaps {
-    CUtensorMap b, w0, w1, s0, s1, mw0, mw1, ms0, ms1;
+    CUtensorMap b[kBMaps];
+    CUtensorMap w0, w1, s0, s1, mw0, mw1, ms0, ms1;
 };
 
 template <int DT, bool GATEUP>
@@ -225,7 +241,7 @@ struct Cfg {
     static constexpr uint32_t kRawStageBytes = kQsBytes + kMetaBytes;
     static constexpr int kRawStages = (int)(kRawRing / kRawStageBytes);
     static constexpr int kAcc = GATEUP ? 1 : 2;  // accumulator buffers
-    static constexpr size_t kSmem = kRawRing + (size_t)kBStages * kBStageBytes + 1024 + 512;
+    static constexpr size_t kSmem = kRawRing + (size_t)kBStages * kBStageBytes + 1024 + 512 + 4 * 2048;
 };
 
 template <int DT, bool GATEUP>
@@ -253,6 +269,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
     const uint32_t drain_bar = bar0 + 8u * (2 * kRS + 2 * kBStages + 8);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * kRS + 2 * kBStages + 9);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kRS + 2 * kBStages + 10);
+    uint8_t* epi_smem = b_ring + kBStages * kBStageBytes + 512;  // 4 warps x 2 KiB output staging
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -301,8 +318,8 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                 const CUtensorMap* m1 = it.shared ? &tm.ms1 : &tm.mw1;
                 const QMat& A = it.shared ? p.S0 : p.A0;
                 const int y0 = (it.shared ? 0 : (it.t.expert - p.e_begin)) * A.rows + it.mt * kTileM;
-                for (int kb = 0; kb < it.nkb && ok; ++kb) {
-                    if ((kb & 1) == 0) {
+                for (int kb = 0; kb < it.nkb && ok; kb += 2) {
+                    {
                         const int s = raw_n % kRS;
                         if (!mbar_wait(raw_empty(s), ((raw_n / kRS) & 1) ^ 1, abort_flag)) {
                             fail(kErrEmpty);
@@ -323,17 +340,6 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                         }
                         ++raw_n;
                     }
-                    const int sb = b_n % kBStages;
-                    if (!mbar_wait(b_empty(sb), ((b_n / kBStages) & 1) ^ 1, abort_flag)) {
-                        fail(kErrEmpty);
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t dst = smem_u32(b_ring + sb * kBStageBytes);
-                    mbar_expect_tx(b_full(sb), (uint32_t)it.N * kBK * 2);
-                    for (int r = 0; r < it.N; r += 16)
-                        tma_load_2d(dst + (uint32_t)r * 128, &tm.b, kb * kBK, it.t.pos0 + r, b_full(sb));
-                    ++b_n;
                 }
             }
             if (!ok) {
@@ -342,6 +348,30 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                     const int n = raw_n - 1 - i;
                     mbar_wait_timed(raw_full(n % kRS), (n / kRS) & 1);
                 }
+            }
+        }
+    } else if (warp == 14) {
+        if (lane == 0) {
+            // ---------------------------------------------------- token producer
+            int b_n = 0;
+            bool ok = true;
+            Item it;
+            for (int w = blockIdx.x; ok && item_at(p, n_tiles, w, it); w += gridDim.x) {
+                const CUtensorMap* bm = &tm.b[it.N / 16 - 1];
+                for (int kb = 0; kb < it.nkb; ++kb) {
+                    const int sb = b_n % kBStages;
+                    if (!mbar_wait(b_empty(sb), ((b_n / kBStages) & 1) ^ 1, abort_flag)) {
+                        fail(kErrEmpty);
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t dst = smem_u32(b_ring + sb * kBStageBytes);
+                    mbar_expect_tx(b_full(sb), (uint32_t)it.N * kBK * 2);
+                    tma_load_2d(dst, bm, kb * kBK, it.t.pos0, b_full(sb));
+                    ++b_n;
+                }
+            }
+            if (!ok) {
                 for (int i = 0; i < kBStages && i < b_n; ++i) {
                     const int n = b_n - 1 - i;
                     mbar_wait_timed(b_full(n % kBStages), (n / kBStages) & 1);
@@ -514,10 +544,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                 }
             }
         }
-    } else {
+    } else if (warp < 14) {
         // -------------------------------------------------------------- epilogue
         const int q = warp & 3;
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        __half* stage = reinterpret_cast<__half*>(epi_smem + (warp - 10) * 2048);
         int item_n = 0;
         Item it;
         for (int w = blockIdx.x; item_at(p, n_tiles, w, it); w += gridDim.x, ++item_n) {
@@ -529,21 +560,35 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
             }
             tc_fence_after();
             const uint32_t d0 = tmem + lane_base + (GATEUP ? 0u : (uint32_t)ab * kAccStride);
-            const int f = it.mt * kTileM + q * 32 + lane;
-            for (int c0 = 0; c0 < it.N; c0 += 16) {
-                uint32_t g[16], u[16];
-                tmem_ld16(d0 + c0, g);
-                if (GATEUP) tmem_ld16(d0 + kAccStride + c0, u);
-                tmem_wait_ld();
+            // 32 columns (tokens) at a time: one TMEM round trip, then the f16 results
+            // go through this warp's 32 x 32 staging tile so each lane stores 16 bytes
+            __half* const out_row0 = p.out + (int64_t)it.t.pos0 * p.out_ld + it.mt * kTileM + q * 32 + (lane & 3) * 8;
+            for (int c0 = 0; c0 < it.N; c0 += 32) {
+                uint32_t g[32];
+                tmem_ld32(d0 + c0, g);
+                if (GATEUP) {
+                    uint32_t u[32];
+                    tmem_ld32(d0 + kAccStride + c0, u);
+                    tmem_wait_ld();
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int col = c0 + j;
-                    if (col < it.t.nvalid) {
-                        float v = __uint_as_float(g[j]);
-                        if (GATEUP) v = silu_f(v) * __uint_as_float(u[j]);
-                        p.out[(int64_t)(it.t.pos0 + col) * p.out_ld + f] = __float2half_rn(v);
+                    for (int j = 0; j < 32; ++j) {
+                        const float v = __uint_as_float(g[j]);
+                        // silu(v) * u; fast exp / divide suffice for an f16 result
+                        stage[j * 32 + lane] = __float2half_rn(__fdividef(v, 1.0f + __expf(-v)) * __uint_as_float(u[j]));
                     }
+                } else {
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) stage[j * 32 + lane] = __float2half_rn(__uint_as_float(g[j]));
                 }
+                __syncwarp();
+#pragma unroll
+                for (int r8 = 0; r8 < 4; ++r8) {
+                    const int j = r8 * 8 + (lane >> 2);
+                    const uint4 v = *reinterpret_cast<const uint4*>(stage + j * 32 + (lane & 3) * 8);
+                    if (c0 + j < it.t.nvalid) *reinterpret_cast<uint4*>(out_row0 + (int64_t)(c0 + j) * p.out_ld) = v;
+                }
+                __syncwarp();
             }
             tc_fence_before();
             __syncwarp();
@@ -652,13 +697,13 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D f16 activations (rows x cols, row stride ld elements): box 16 rows x 64 cols, 128B swizzle.
-bool make_tmap_act(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld) {
+// 2-D f16 activations (rows x cols, row stride ld elements): box box_rows x 64 cols, 128B swizzle.
+bool make_tmap_act(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint64_t ld, uint32_t box_rows) {
     auto fn = encode_fn();
     if (!fn) return false;
     cuuint64_t dims[2] = {cols, rows};
     cuuint64_t strides[1] = {ld * 2};
-    cuuint32_t box[2] = {(cuuint32_t)kBK, 16u};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
     cuuint32_t es[2] = {1u, 1u};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides, box, es,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -735,11 +780,12 @@ bool gemm_setup(void* ws, size_t ws_bytes, int dp, int act_ld, int P_cap, int T_
     b->n_tiles = reinterpret_cast<int32_t*>(c);
     b->err = b->n_tiles + 1;
     b->rows_cap = (int)rows;
-    if (!make_tmap_act(&b->tmap_x, b->xperm, rows, (uint64_t)dp, (uint64_t)dp) ||
-        !make_tmap_act(&b->tmap_act, b->act, rows, (uint64_t)act_ld, (uint64_t)act_ld)) {
-        *why = "cuTensorMapEncodeTiled failed for the activation buffers";
-        return false;
-    }
+    for (int i = 0; i < kBMaps; ++i)
+        if (!make_tmap_act(&b->tmap_x[i], b->xperm, rows, (uint64_t)dp, (uint64_t)dp, 16u * (i + 1)) ||
+            !make_tmap_act(&b->tmap_act[i], b->act, rows, (uint64_t)act_ld, (uint64_t)act_ld, 16u * (i + 1))) {
+            *why = "cuTensorMapEncodeTiled failed for the activation buffers";
+            return false;
+        }
     return true;
 }
 
@@ -790,7 +836,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, GemmBuffers& b, const GemmWeigh
     g.out = b.act;
     g.out_ld = a.act_ld;
     GemmMaps maps;
-    maps.b = b.tmap_x;
+    for (int i = 0; i < kBMaps; ++i) maps.b[i] = b.tmap_x[i];
     maps.w0 = wm.q[0];
     maps.w1 = wm.q[1];
     maps.s0 = wm.q[3];
@@ -814,7 +860,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, GemmBuffers& b, const GemmWeigh
     g.MTmax = g.MT;
     g.out = b.y;
     g.out_ld = a.dp;
-    maps.b = b.tmap_act;
+    for (int i = 0; i < kBMaps; ++i) maps.b[i] = b.tmap_act[i];
     maps.w0 = maps.w1 = wm.q[2];
     maps.s0 = maps.s1 = wm.q[5];
     maps.mw0 = maps.mw1 = wm.m[2];

@@ -36,7 +36,7 @@ struct GemmBuffers {
     int32_t* n_tiles;
     int32_t* err;           // pipeline timeout code (0 = none)
     int rows_cap;
-    CUtensorMap tmap_x, tmap_act;
+    CUtensorMap tmap_x[kGemmNT / 16], tmap_act[kGemmNT / 16];  // box heights 16, 32, ..., kGemmNT
 };
 
 // Carve the workspace and encode the TMA descriptors for it.
