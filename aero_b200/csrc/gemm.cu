@@ -14,21 +14,21 @@
 // the same tensor-core rate.
 //
 // Persistent kernel: one CTA per SM walks work items (tile, 128-row block)
-// blockIdx.x, blockIdx.x + gridDim.x, ... Warp roles (15 warps):
+// blockIdx.x, blockIdx.x + gridDim.x, ... Warp roles (23 warps):
 //   warp 0      TMA producer of the raw quant blocks of the item's 128 weight
 //               rows (2-D tensor maps over the expert-major qs and header
 //               planes, 128 values per stage, a deep ring)
-//   warp 14     TMA producer of the token operand (f16 rows, 128B swizzle,
+//   warp 22     TMA producer of the token operand (f16 rows, 128B swizzle,
 //               K-major, one box of the tile's height per K step; no multicast
 //               anywhere)
 //   warp 1      one thread issues tcgen05.mma with the weight operand A in TMEM
 //               and the token operand B in shared memory, fp32 accumulators in
 //               TMEM, tcgen05.commit to the ring barriers
-//   warps 2-9   dequantise from shared memory with packed half2 arithmetic
+//   warps 2-17  dequantise from shared memory with packed half2 arithmetic
 //               (Q4_K: s*q - m per 32-value sub-block; Q8_0: d*q) and write A
 //               into TMEM with tcgen05.st (row m of A = TMEM lane m, two f16 per
 //               column); the block headers ride in the same TMA stages
-//   warps 10-13 epilogue: tcgen05.ld of the accumulators 32 columns at a time,
+//   warps 18-21 epilogue: tcgen05.ld of the accumulators 16 columns at a time,
 //               SwiGLU, f16 results staged in shared memory for 16-byte stores
 // The weight tile never passes through shared memory, which halves the shared
 // memory traffic per K step. The down GEMM double-buffers its accumulators so
@@ -50,7 +50,10 @@ namespace {
 constexpr int kBK = 64;          // K per MMA stage (A and B)
 constexpr int kRawK = 128;       // K per raw (quant) stage
 constexpr int kTileM = 128;
-constexpr int kThreads = 480;    // 15 warps
+constexpr int kThreads = 736;    // 23 warps
+constexpr int kDeqWarps = 16;
+constexpr int kEpiWarp0 = 2 + kDeqWarps;   // warps 18-21
+constexpr int kTokWarp = kEpiWarp0 + 4;    // warp 22
 constexpr int kBMaps = kGemmNT / 16;  // token-operand maps, box heights 16, 32, ..., 192
 constexpr int kBStages = 4;
 constexpr uint32_t kBStageBytes = kGemmNT * kBK * 2;  // 24 KiB: up to 192 token rows x 128 B
@@ -151,6 +154,11 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* r) {
         "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
         : "memory");
 }
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* r) {
+    asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr), "r"(r[0]), "r"(r[1]),
+                 "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+                 : "memory");
+}
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -241,7 +249,7 @@ struct Cfg {
     static constexpr uint32_t kRawStageBytes = kQsBytes + kMetaBytes;
     static constexpr int kRawStages = (int)(kRawRing / kRawStageBytes);
     static constexpr int kAcc = GATEUP ? 1 : 2;  // accumulator buffers
-    static constexpr size_t kSmem = kRawRing + (size_t)kBStages * kBStageBytes + 1024 + 512 + 4 * 2048;
+    static constexpr size_t kSmem = kRawRing + (size_t)kBStages * kBStageBytes + 1024 + 512 + 4 * 1024;
 };
 
 template <int DT, bool GATEUP>
@@ -269,20 +277,20 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
     const uint32_t drain_bar = bar0 + 8u * (2 * kRS + 2 * kBStages + 8);
     volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * kRS + 2 * kBStages + 9);
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kRS + 2 * kBStages + 10);
-    uint8_t* epi_smem = b_ring + kBStages * kBStageBytes + 512;  // 4 warps x 2 KiB output staging
+    uint8_t* epi_smem = b_ring + kBStages * kBStageBytes + 512;  // 4 warps x 1 KiB output staging
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kRS; ++s) {
             mbar_init(raw_full(s), 1);
-            mbar_init(raw_empty(s), 8);
+            mbar_init(raw_empty(s), kDeqWarps);
         }
         for (int s = 0; s < kBStages; ++s) {
             mbar_init(b_full(s), 1);
             mbar_init(b_empty(s), 1);
         }
         for (int s = 0; s < 2; ++s) {
-            mbar_init(a_full(s), 8);
+            mbar_init(a_full(s), kDeqWarps);
             mbar_init(a_empty(s), 1);
             mbar_init(acc_full(s), 1);
             mbar_init(acc_empty(s), 4);
@@ -350,7 +358,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                 }
             }
         }
-    } else if (warp == 14) {
+    } else if (warp == kTokWarp) {
         if (lane == 0) {
             // ---------------------------------------------------- token producer
             int b_n = 0;
@@ -428,16 +436,21 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                 mbar_wait_timed(drain_bar, 0);
             }
         }
-    } else if (warp < 10) {
+    } else if (warp < kEpiWarp0) {
         // -------------------------------------------------------------- dequant
-        const int grp = (warp - 2) >> 2;  // gate/up: the matrix; down: which 32 of the 64 values
-        const int q = warp & 3;           // TMEM lane quarter this warp may access
-        const int r = q * 32 + lane;      // weight row within the 128-row block
+        // 16 warps: warp (warp & 3) may write TMEM lane quarter q; its combo
+        // c = (warp - 2) / 4 picks its share of each 64-value K-block:
+        //   gate/up: matrix c / 2, values [32 (c % 2), +32)   (16 TMEM columns)
+        //   down:    values [16 c, 16 c + 16)                 (8 TMEM columns)
+        const int cmb = (warp - 2) >> 2;
+        const int q = warp & 3;
+        const int r = q * 32 + lane;  // weight row within the 128-row block
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        const int mat = GATEUP ? (cmb >> 1) : 0;
+        const int half = GATEUP ? (cmb & 1) : 0;
         int raw_n = 0, a_n = 0;
         bool ok = true;
         Item it;
-        const int mat = GATEUP ? grp : 0;
         for (int w = blockIdx.x; ok && item_at(p, n_tiles, w, it); w += gridDim.x) {
             for (int kb = 0; kb < it.nkb; ++kb) {
                 const int s = raw_n % kRS;
@@ -464,74 +477,72 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                 const int swz = DT == AERO_DT_Q4_K ? ((r >> 1) & 3) : (r & 7);
                 auto qchunk = [&](int c) { return *reinterpret_cast<const uint4*>(qrow + ((c ^ swz) << 4)); };
                 const uint4 meta = *reinterpret_cast<const uint4*>(stage + C::kQsBytes + mat * kTileM * 16 + r * 16);
-                // columns 0-15 and 16-31 of this K-block's 32 TMEM columns (two f16 each);
-                // the down GEMM's warp group `grp` produces only its own half
-                uint32_t c0[16], c1[16];
-                const bool need0 = GATEUP || grp == 0, need1 = GATEUP || grp == 1;
+                const uint32_t abase = tmem + lane_base + kAColBase + (uint32_t)sa * (GATEUP ? 64u : 32u);
                 if (DT == AERO_DT_Q4_K) {
+                    // values: low nibbles of the K-block's 32 bytes are values 0-31 (sub-block 2g),
+                    // high nibbles 32-63 (sub-block 2g+1); column j holds values 2j, 2j+1
+                    const bool hi = GATEUP ? half : (cmb >> 1);
                     const uint8_t* mb = reinterpret_cast<const uint8_t*>(&meta);
                     const float d = __half2float(__ushort_as_half((unsigned short)(mb[0] | (mb[1] << 8))));
                     const float dmin = __half2float(__ushort_as_half((unsigned short)(mb[2] | (mb[3] << 8))));
-                    const int g = kb & 3;
-                    int sc0, m0, sc1, m1;
-                    q4k_sc_m(mb + 4, 2 * g, sc0, m0);
-                    q4k_sc_m(mb + 4, 2 * g + 1, sc1, m1);
-                    const __half2 s0 = __float2half2_rn(d * (float)sc0), n0 = __float2half2_rn(-(dmin * (float)m0));
-                    const __half2 s1 = __float2half2_rn(d * (float)sc1), n1 = __float2half2_rn(-(dmin * (float)m1));
-                    // 32 bytes of this K-block: chunks 2 (kb & 1) and 2 (kb & 1) + 1 of the 64-byte row
-                    const uint4 v0 = qchunk(2 * (kb & 1)), v1 = qchunk(2 * (kb & 1) + 1);
-                    const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-                    // byte pair (2j, 2j+1): low nibbles -> column j, high nibbles -> column 16 + j
+                    int sc, mn;
+                    q4k_sc_m(mb + 4, 2 * (kb & 3) + (hi ? 1 : 0), sc, mn);
+                    const __half2 sh = __float2half2_rn(d * (float)sc), nh = __float2half2_rn(-(dmin * (float)mn));
+                    const int shift = hi ? 4 : 0;
+                    if (GATEUP) {
+                        const uint4 v0 = qchunk(2 * (kb & 1)), v1 = qchunk(2 * (kb & 1) + 1);
+                        const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                        uint32_t cols[16];
 #pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const uint32_t a = __byte_perm(wv[i], 0, 0x4140), b = __byte_perm(wv[i], 0, 0x4342);
-                        if (need0) {
-                            c0[2 * i] = h2u(__hfma2(nib2_to_h2(a), s0, n0));
-                            c0[2 * i + 1] = h2u(__hfma2(nib2_to_h2(b), s0, n0));
+                        for (int i = 0; i < 8; ++i) {
+                            const uint32_t a2 = __byte_perm(wv[i], 0, 0x4140) >> shift;
+                            const uint32_t b2 = __byte_perm(wv[i], 0, 0x4342) >> shift;
+                            cols[2 * i] = h2u(__hfma2(nib2_to_h2(a2), sh, nh));
+                            cols[2 * i + 1] = h2u(__hfma2(nib2_to_h2(b2), sh, nh));
                         }
-                        if (need1) {
-                            c1[2 * i] = h2u(__hfma2(nib2_to_h2(a >> 4), s1, n1));
-                            c1[2 * i + 1] = h2u(__hfma2(nib2_to_h2(b >> 4), s1, n1));
+                        tmem_st16(abase + (uint32_t)mat * 32u + (uint32_t)half * 16u, cols);
+                    } else {
+                        // combo c: bytes [16 (c & 1), +16), low (c < 2) or high nibbles -> columns 8c .. 8c+7
+                        const uint4 v = qchunk(2 * (kb & 1) + (cmb & 1));
+                        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+                        uint32_t cols[8];
+#pragma unroll
+                        for (int i = 0; i < 4; ++i) {
+                            cols[2 * i] = h2u(__hfma2(nib2_to_h2(__byte_perm(wv[i], 0, 0x4140) >> shift), sh, nh));
+                            cols[2 * i + 1] = h2u(__hfma2(nib2_to_h2(__byte_perm(wv[i], 0, 0x4342) >> shift), sh, nh));
                         }
+                        tmem_st8(abase + (uint32_t)cmb * 8u, cols);
                     }
                 } else {
                     // the 16-byte slice holds 8 fp16 scales for 256 values; this K-block uses two
+                    // (values 0-31 and 32-63); column j holds values 2j, 2j+1
                     const uint32_t mw[4] = {meta.x, meta.y, meta.z, meta.w};
                     const uint32_t sc8 = mw[kb & 3];
-                    const __half2 d0 = __half2half2(__ushort_as_half((unsigned short)(sc8 & 0xFFFFu)));
-                    const __half2 d1 = __half2half2(__ushort_as_half((unsigned short)(sc8 >> 16)));
-                    // 64 bytes of this K-block: chunks 4 (kb & 1) .. 4 (kb & 1) + 3 of the 128-byte row;
-                    // the first 32 values use scale d0, the next 32 d1
-                    if (need0) {
-                        const uint4 v0 = qchunk(4 * (kb & 1)), v1 = qchunk(4 * (kb & 1) + 1);
+                    const int blk = GATEUP ? half : (cmb >> 1);
+                    const __half2 dd = __half2half2(__ushort_as_half((unsigned short)(blk ? (sc8 >> 16) : (sc8 & 0xFFFFu))));
+                    if (GATEUP) {
+                        const uint4 v0 = qchunk(4 * (kb & 1) + 2 * blk), v1 = qchunk(4 * (kb & 1) + 2 * blk + 1);
                         const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                        uint32_t cols[16];
 #pragma unroll
                         for (int i = 0; i < 8; ++i) {
                             const uint32_t wb = wv[i] ^ 0x80808080u;
-                            c0[2 * i] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4140)), d0));
-                            c0[2 * i + 1] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4342)), d0));
+                            cols[2 * i] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4140)), dd));
+                            cols[2 * i + 1] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4342)), dd));
                         }
-                    }
-                    if (need1) {
-                        const uint4 v0 = qchunk(4 * (kb & 1) + 2), v1 = qchunk(4 * (kb & 1) + 3);
-                        const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                        tmem_st16(abase + (uint32_t)mat * 32u + (uint32_t)half * 16u, cols);
+                    } else {
+                        const uint4 v = qchunk(4 * (kb & 1) + cmb);
+                        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+                        uint32_t cols[8];
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) {
+                        for (int i = 0; i < 4; ++i) {
                             const uint32_t wb = wv[i] ^ 0x80808080u;
-                            c1[2 * i] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4140)), d1));
-                            c1[2 * i + 1] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4342)), d1));
+                            cols[2 * i] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4140)), dd));
+                            cols[2 * i + 1] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4342)), dd));
                         }
+                        tmem_st8(abase + (uint32_t)cmb * 8u, cols);
                     }
-                }
-                // gate/up: this warp's matrix, 32 columns; down: this warp group's 16 columns
-                const uint32_t acol = tmem + lane_base + kAColBase + (uint32_t)sa * (GATEUP ? 64u : 32u);
-                if (GATEUP) {
-                    tmem_st16(acol + (uint32_t)grp * 32u, c0);
-                    tmem_st16(acol + (uint32_t)grp * 32u + 16u, c1);
-                } else if (grp == 0) {
-                    tmem_st16(acol, c0);
-                } else {
-                    tmem_st16(acol + 16u, c1);
                 }
                 tmem_wait_st();
                 tc_fence_before();
@@ -544,11 +555,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                 }
             }
         }
-    } else if (warp < 14) {
+    } else if (warp < kTokWarp) {
         // -------------------------------------------------------------- epilogue
         const int q = warp & 3;
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        __half* stage = reinterpret_cast<__half*>(epi_smem + (warp - 10) * 2048);
+        __half* stage = reinterpret_cast<__half*>(epi_smem + (warp - kEpiWarp0) * 1024);
         int item_n = 0;
         Item it;
         for (int w = blockIdx.x; item_at(p, n_tiles, w, it); w += gridDim.x, ++item_n) {
@@ -560,18 +571,18 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
             }
             tc_fence_after();
             const uint32_t d0 = tmem + lane_base + (GATEUP ? 0u : (uint32_t)ab * kAccStride);
-            // 32 columns (tokens) at a time: one TMEM round trip, then the f16 results
-            // go through this warp's 32 x 32 staging tile so each lane stores 16 bytes
+            // 16 columns (tokens) at a time: one TMEM round trip, then the f16 results
+            // go through this warp's 16 x 32 staging tile so each lane stores 16 bytes
             __half* const out_row0 = p.out + (int64_t)it.t.pos0 * p.out_ld + it.mt * kTileM + q * 32 + (lane & 3) * 8;
-            for (int c0 = 0; c0 < it.N; c0 += 32) {
-                uint32_t g[32];
-                tmem_ld32(d0 + c0, g);
+            for (int c0 = 0; c0 < it.N; c0 += 16) {
+                uint32_t g[16];
+                tmem_ld16(d0 + c0, g);
                 if (GATEUP) {
-                    uint32_t u[32];
-                    tmem_ld32(d0 + kAccStride + c0, u);
+                    uint32_t u[16];
+                    tmem_ld16(d0 + kAccStride + c0, u);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
+                    for (int j = 0; j < 16; ++j) {
                         const float v = __uint_as_float(g[j]);
                         // silu(v) * u; fast exp / divide suffice for an f16 result
                         stage[j * 32 + lane] = __float2half_rn(__fdividef(v, 1.0f + __expf(-v)) * __uint_as_float(u[j]));
@@ -579,11 +590,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                 } else {
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) stage[j * 32 + lane] = __float2half_rn(__uint_as_float(g[j]));
+                    for (int j = 0; j < 16; ++j) stage[j * 32 + lane] = __float2half_rn(__uint_as_float(g[j]));
                 }
                 __syncwarp();
 #pragma unroll
-                for (int r8 = 0; r8 < 4; ++r8) {
+                for (int r8 = 0; r8 < 2; ++r8) {
                     const int j = r8 * 8 + (lane >> 2);
                     const uint4 v = *reinterpret_cast<const uint4*>(stage + j * 32 + (lane & 3) * 8);
                     if (c0 + j < it.t.nvalid) *reinterpret_cast<uint4*>(out_row0 + (int64_t)(c0 + j) * p.out_ld) = v;
