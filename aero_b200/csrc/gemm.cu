@@ -38,6 +38,7 @@
 // copies and MMAs, frees TMEM and exits.
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <cub/block/block_scan.cuh>
 #include <string>
 
@@ -615,22 +616,36 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
 }
 
 // ------------------------------------------------------------------ helpers
-__global__ void gather_kernel(const float* __restrict__ x, const int32_t* __restrict__ perm, int k, int P, int rows,
-                              int dp, __half* __restrict__ xp) {
+// xperm rows: [0, P_real) the routed pairs in sorted order, [P, P + Tsh) the
+// first Tsh input rows for the shared expert. P_real (= offsets[E]) is read on
+// the device: sorted positions [P_real, P) hold skipped slots and are not
+// gathered. Grid-stride over 8-value chunks.
+template <typename XT>
+__global__ void gather_kernel(const XT* __restrict__ x, const int32_t* __restrict__ perm,
+                              const int32_t* __restrict__ p_real, int k, int P, int Tsh, int dp,
+                              __half* __restrict__ xp) {
     const int per_row = dp / 8;
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (int64_t)rows * per_row) return;
-    const int row = (int)(i / per_row), c = (int)(i % per_row) * 8;
-    const int tok = row < P ? perm[row] / k : row - P;
-    const float* src = x + (int64_t)tok * dp + c;
-    const float4 a = ld_f4(src), b = ld_f4(src + 4);
-    *reinterpret_cast<uint4*>(xp + (int64_t)row * dp + c) =
-        make_uint4(pack_h2(a.x, a.y), pack_h2(a.z, a.w), pack_h2(b.x, b.y), pack_h2(b.z, b.w));
+    const int pr = *p_real;
+    const int64_t n = (int64_t)(pr + Tsh) * per_row;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+        const int v = (int)(i / per_row), c = (int)(i % per_row) * 8;
+        const int row = v < pr ? v : P + (v - pr);
+        const int tok = v < pr ? perm[v] / k : v - pr;
+        uint4 o;
+        if constexpr (sizeof(XT) == 2) {
+            o = __ldg(reinterpret_cast<const uint4*>(x + (int64_t)tok * dp + c));
+        } else {
+            const float* src = reinterpret_cast<const float*>(x) + (int64_t)tok * dp + c;
+            const float4 a = ld_f4(src), b = ld_f4(src + 4);
+            o = make_uint4(pack_h2(a.x, a.y), pack_h2(a.z, a.w), pack_h2(b.x, b.y), pack_h2(b.z, b.w));
+        }
+        *reinterpret_cast<uint4*>(xp + (int64_t)row * dp + c) = o;
+    }
 }
 
 __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t* __restrict__ act_e,
                                                            const int32_t* __restrict__ act_off,
-                                                           const int32_t* __restrict__ n_active, int P, int T,
+                                                           const int32_t* __restrict__ n_active, int P, int Tsh,
                                                            int has_shared, GemmTile* __restrict__ tiles,
                                                            int32_t* __restrict__ n_tiles) {
     using Scan = cub::BlockScan<int, 1024>;
@@ -658,13 +673,17 @@ __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t* __rest
     if (threadIdx.x == 0) {
         int c = carry;
         if (has_shared)
-            for (int j = 0; j * kGemmNT < T; ++j) tiles[c++] = GemmTile{-1, P + j * kGemmNT, min(kGemmNT, T - j * kGemmNT), 0};
+            for (int j = 0; j * kGemmNT < Tsh; ++j)
+                tiles[c++] = GemmTile{-1, P + j * kGemmNT, min(kGemmNT, Tsh - j * kGemmNT), 0};
         *n_tiles = c;
     }
 }
 
+// out[t] = sum over slots s of w[t][s] * y[inv[t*k+s]] (+ sgate[t] * y[P + t]
+// for t < Tsh). With idx given, slots whose bucket is >= E_real were skipped.
 __global__ void combine_h_kernel(const __half* __restrict__ y, const int32_t* __restrict__ inv,
-                                 const float* __restrict__ w, const float* __restrict__ sgate, int T, int k, int d,
+                                 const float* __restrict__ w, const float* __restrict__ sgate,
+                                 const int32_t* __restrict__ idx, int E_real, int T, int Tsh, int k, int d,
                                  int has_shared, float* __restrict__ out) {
     const int d4 = d >> 2;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -672,6 +691,7 @@ __global__ void combine_h_kernel(const __half* __restrict__ y, const int32_t* __
     const int t = (int)(i / d4), c = (int)(i % d4) * 4;
     float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
     for (int s = 0; s < k; ++s) {
+        if (idx && idx[(int64_t)t * k + s] >= E_real) continue;
         const float wt = w[(int64_t)t * k + s];
         const uint2 v = __ldg(reinterpret_cast<const uint2*>(y + (int64_t)inv[(int64_t)t * k + s] * d + c));
         const float2 lo = __half22float2(u2h(v.x));
@@ -681,7 +701,7 @@ __global__ void combine_h_kernel(const __half* __restrict__ y, const int32_t* __
         a2 += wt * hi.x;
         a3 += wt * hi.y;
     }
-    if (has_shared) {
+    if (has_shared && t < Tsh) {
         const float g = sgate[t];
         const uint2 v = __ldg(reinterpret_cast<const uint2*>(y + ((int64_t)T * k + t) * d + c));
         const float2 lo = __half22float2(u2h(v.x));
@@ -818,48 +838,55 @@ bool gemm_weight_maps(const QMat& gate, const QMat& up, const QMat& down, const 
     return ok;
 }
 
-cudaError_t launch_prefill(const PrefillArgs& a, GemmBuffers& b, const GemmWeightMaps& wm, cudaStream_t s,
-                           int* launches) {
+cudaError_t launch_prefill_prep(const PrefillArgs& a, GemmBuffers& b, cudaStream_t s) {
     const int P = a.T * a.k;
-    const int rows = P + (a.has_shared ? a.T : 0);
+    const int Tsh = a.has_shared ? a.Tsh : 0;
     {
-        const int64_t n = (int64_t)rows * (a.dp / 8);
-        gather_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(a.x, a.perm, a.k, P, rows, a.dp, b.xperm);
+        const int64_t n = (int64_t)(P + Tsh) * (a.dp / 8);
+        const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)a.n_sm * 16));
+        if (a.x_f16)
+            gather_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(a.x), a.perm, a.p_real, a.k, P, Tsh,
+                                                        a.dp, b.xperm);
+        else
+            gather_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(a.x), a.perm, a.p_real, a.k, P, Tsh,
+                                                       a.dp, b.xperm);
     }
-    build_tiles_kernel<<<1, 1024, 0, s>>>(a.act_e, a.act_off, a.n_active, P, a.T, a.has_shared, b.tiles, b.n_tiles);
-    cudaError_t e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    build_tiles_kernel<<<1, 1024, 0, s>>>(a.act_e, a.act_off, a.n_active, P, Tsh, a.has_shared, b.tiles, b.n_tiles);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_prefill_gemm(const PrefillArgs& a, GemmBuffers& b, const GemmWeightMaps& wm, bool gateup,
+                                cudaStream_t s) {
     GemmParams g{};
     g.tiles = b.tiles;
     g.n_tiles = b.n_tiles;
     g.err = b.err;
     g.e_begin = a.e_begin;
-    // gate/up
-    g.A0 = a.gate;
-    g.A1 = a.up;
-    g.S0 = a.has_shared ? a.sg : a.gate;
-    g.S1 = a.has_shared ? a.su : a.up;
-    g.K = a.dp;
-    g.Ks = a.dp;
-    g.MT = a.F / kTileM;
-    g.MTs = a.has_shared ? a.Fs / kTileM : 0;
-    g.MTmax = g.MT > g.MTs ? g.MT : g.MTs;
-    g.out = b.act;
-    g.out_ld = a.act_ld;
     GemmMaps maps;
-    for (int i = 0; i < kBMaps; ++i) maps.b[i] = b.tmap_x[i];
-    maps.w0 = wm.q[0];
-    maps.w1 = wm.q[1];
-    maps.s0 = wm.q[3];
-    maps.s1 = wm.q[4];
-    maps.mw0 = wm.m[0];
-    maps.mw1 = wm.m[1];
-    maps.ms0 = wm.m[3];
-    maps.ms1 = wm.m[4];
-    e = a.gate.dtype == AERO_DT_Q4_K ? launch_gemm<AERO_DT_Q4_K, true>(maps, g, a.n_sm, s)
-                                     : launch_gemm<AERO_DT_Q8_0, true>(maps, g, a.n_sm, s);
-    if (e != cudaSuccess) return e;
-    // down
+    if (gateup) {
+        g.A0 = a.gate;
+        g.A1 = a.up;
+        g.S0 = a.has_shared ? a.sg : a.gate;
+        g.S1 = a.has_shared ? a.su : a.up;
+        g.K = a.dp;
+        g.Ks = a.dp;
+        g.MT = a.F / kTileM;
+        g.MTs = a.has_shared ? a.Fs / kTileM : 0;
+        g.MTmax = g.MT > g.MTs ? g.MT : g.MTs;
+        g.out = b.act;
+        g.out_ld = a.act_ld;
+        for (int i = 0; i < kBMaps; ++i) maps.b[i] = b.tmap_x[i];
+        maps.w0 = wm.q[0];
+        maps.w1 = wm.q[1];
+        maps.s0 = wm.q[3];
+        maps.s1 = wm.q[4];
+        maps.mw0 = wm.m[0];
+        maps.mw1 = wm.m[1];
+        maps.ms0 = wm.m[3];
+        maps.ms1 = wm.m[4];
+        return a.gate.dtype == AERO_DT_Q4_K ? launch_gemm<AERO_DT_Q4_K, true>(maps, g, a.n_sm, s)
+                                            : launch_gemm<AERO_DT_Q8_0, true>(maps, g, a.n_sm, s);
+    }
     g.A0 = a.down;
     g.A1 = a.down;
     g.S0 = a.has_shared ? a.sd : a.down;
@@ -876,17 +903,17 @@ cudaError_t launch_prefill(const PrefillArgs& a, GemmBuffers& b, const GemmWeigh
     maps.s0 = maps.s1 = wm.q[5];
     maps.mw0 = maps.mw1 = wm.m[2];
     maps.ms0 = maps.ms1 = wm.m[5];
-    e = a.down.dtype == AERO_DT_Q4_K ? launch_gemm<AERO_DT_Q4_K, false>(maps, g, a.n_sm, s)
-                                     : launch_gemm<AERO_DT_Q8_0, false>(maps, g, a.n_sm, s);
-    if (launches) *launches += 4;
-    return e;
+    return a.down.dtype == AERO_DT_Q4_K ? launch_gemm<AERO_DT_Q4_K, false>(maps, g, a.n_sm, s)
+                                        : launch_gemm<AERO_DT_Q8_0, false>(maps, g, a.n_sm, s);
 }
 
-cudaError_t launch_combine_h(const __half* y, const int32_t* inv, const float* w, const float* sgate, int T, int k,
-                             int d, int has_shared, float* out, cudaStream_t s) {
+cudaError_t launch_combine_h(const __half* y, const int32_t* inv, const float* w, const float* sgate,
+                             const int32_t* idx, int E_real, int T, int Tsh, int k, int d, int has_shared, float* out,
+                             cudaStream_t s) {
     const int64_t n = (int64_t)T * (d / 4);
     if (n == 0) return cudaSuccess;
-    combine_h_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(y, inv, w, sgate, T, k, d, has_shared, out);
+    combine_h_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(y, inv, w, sgate, idx, E_real, T, Tsh, k, d,
+                                                                 has_shared, out);
     return cudaGetLastError();
 }
 

@@ -54,7 +54,10 @@ bool gemm_weight_maps(const QMat& gate, const QMat& up, const QMat& down, const 
 
 struct PrefillArgs {
     QMat gate, up, down, sg, su, sd;
-    const float* x;           // (T, dp) f32
+    const void* x;            // (T, dp) f32, or f16 when x_f16
+    int x_f16;
+    int Tsh;                  // the shared expert runs on rows [0, Tsh)
+    const int32_t* p_real;    // device: number of sorted positions that hold real pairs
     const int32_t* perm;      // sorted position -> pair
     const int32_t* act_e;
     const int32_t* act_off;
@@ -65,11 +68,17 @@ struct PrefillArgs {
     int n_sm;      // persistent grid size
 };
 
-// gather -> tile list -> gate/up GEMM (+SwiGLU) -> down GEMM. Writes y (f16)
-// for rows [0, P + T); the combine reads it with launch_combine_h.
-cudaError_t launch_prefill(const PrefillArgs& a, GemmBuffers& b, const GemmWeightMaps& wm, cudaStream_t s,
-                           int* launches);
+// The prefill path: launch_prefill_prep (gather of the f16 operand rows + tile
+// list, 2 kernels), then launch_prefill_gemm with gateup=true (gate/up GEMM +
+// SwiGLU into act) and gateup=false (down GEMM into y, f16, rows [0, P + Tsh));
+// the combine reads y with launch_combine_h.
+cudaError_t launch_prefill_prep(const PrefillArgs& a, GemmBuffers& b, cudaStream_t s);
+cudaError_t launch_prefill_gemm(const PrefillArgs& a, GemmBuffers& b, const GemmWeightMaps& wm, bool gateup,
+                                cudaStream_t s);
+// out[t] = sum_s w[t][s] * y[inv[t*k+s]] (+ sgate[t] * y[P + t] for t < Tsh); with
+// idx non-null, slots whose bucket idx[t*k+s] >= E_real are skipped.
 cudaError_t launch_combine_h(const __half* y, const int32_t* inv, const float* w, const float* sgate,
-                                int T, int k, int d, int has_shared, float* out, cudaStream_t s);
+                             const int32_t* idx, int E_real, int T, int Tsh, int k, int d, int has_shared,
+                             float* out, cudaStream_t s);
 
 }  // namespace aero

@@ -45,7 +45,7 @@ __device__ __forceinline__ bool unit_of(const GemvArgs& a, int b, int groups_rou
         grp = b;
         u.e = 0;
         u.pos0 = P;
-        u.npairs = a.T;
+        u.npairs = a.Tsh;
         u.shared = true;
     }
     return true;
@@ -235,14 +235,16 @@ cudaError_t down_any(int dtype, const GemvArgs& a, bool shared, cudaStream_t s) 
 }
 
 __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __restrict__ inv,
-                               const float* __restrict__ w, const float* __restrict__ sgate, int T, int k,
-                               int d, int has_shared, float* __restrict__ out) {
+                               const float* __restrict__ w, const float* __restrict__ sgate,
+                               const int32_t* __restrict__ idx, int E_real, int T, int Tsh, int k, int d,
+                               int has_shared, float* __restrict__ out) {
     const int d4 = d >> 2;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)T * d4) return;
     const int t = (int)(i / d4), c = (int)(i % d4) * 4;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int s = 0; s < k; ++s) {
+        if (idx && idx[(int64_t)t * k + s] >= E_real) continue;
         const float wt = w[(int64_t)t * k + s];
         const float4 v = ld_f4(y + (int64_t)inv[(int64_t)t * k + s] * d + c);
         acc.x += wt * v.x;
@@ -250,7 +252,7 @@ __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __res
         acc.z += wt * v.z;
         acc.w += wt * v.w;
     }
-    if (has_shared) {
+    if (has_shared && t < Tsh) {
         const float g = sgate[t];
         const float4 v = ld_f4(y + ((int64_t)T * k + t) * d + c);
         acc.x += g * v.x;
@@ -265,21 +267,23 @@ __global__ void combine_kernel(const float* __restrict__ y, const int32_t* __res
 
 cudaError_t launch_gemv_gateup(const GemvArgs& a, cudaStream_t s) {
     cudaError_t e = gateup_any(a.gate.dtype, a, false, s);
-    if (e == cudaSuccess && a.has_shared) e = gateup_any(a.sg.dtype, a, true, s);
+    if (e == cudaSuccess && a.has_shared && a.Tsh > 0) e = gateup_any(a.sg.dtype, a, true, s);
     return e;
 }
 
 cudaError_t launch_gemv_down(const GemvArgs& a, cudaStream_t s) {
     cudaError_t e = down_any(a.down.dtype, a, false, s);
-    if (e == cudaSuccess && a.has_shared) e = down_any(a.sd.dtype, a, true, s);
+    if (e == cudaSuccess && a.has_shared && a.Tsh > 0) e = down_any(a.sd.dtype, a, true, s);
     return e;
 }
 
-cudaError_t launch_combine(const float* y, const int32_t* inv, const float* w, const float* sgate, int T, int k,
-                           int d, int has_shared, float* out, cudaStream_t s) {
+cudaError_t launch_combine(const float* y, const int32_t* inv, const float* w, const float* sgate,
+                           const int32_t* idx, int E_real, int T, int Tsh, int k, int d, int has_shared, float* out,
+                           cudaStream_t s) {
     const int64_t n = (int64_t)T * (d / 4);
     if (n == 0) return cudaSuccess;
-    combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(y, inv, w, sgate, T, k, d, has_shared, out);
+    combine_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(y, inv, w, sgate, idx, E_real, T, Tsh, k, d,
+                                                               has_shared, out);
     return cudaGetLastError();
 }
 

@@ -27,10 +27,12 @@ cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int no
 // perm[P] (sorted position -> pair), inv[P] (pair -> sorted position), the active
 // list act_e[n_active] / act_off[n_active+1] (segment starts, in sorted
 // positions) and n_active. `work` is scratch of dispatch_work_bytes(P, E).
+// Buckets e >= n_real (default: none) are sorted but left out of the active
+// list; act_off[n_active] is then offsets[n_real], the end of the real pairs.
 size_t dispatch_work_bytes(int P, int E);
 cudaError_t launch_dispatch(const int32_t* idx, int P, int E, int32_t* offsets, int32_t* perm,
                             int32_t* inv, int32_t* act_e, int32_t* act_off, int32_t* n_active,
-                            void* work, cudaStream_t s);
+                            void* work, cudaStream_t s, int n_real = -1);
 
 struct GemvArgs {
     QMat gate, up, down;     // routed experts
@@ -42,6 +44,7 @@ struct GemvArgs {
     const int32_t* act_off;
     const int32_t* n_active;
     int T, k, d, F, Fs, has_shared, max_active;
+    int Tsh;                 // the shared expert runs on tokens [0, Tsh)
     int act_ld;              // row stride of act (>= max(F, Fs))
     float* act;              // (P + T, act_ld)
     float* asum16;           // (P + T, act_ld/16)
@@ -50,9 +53,38 @@ struct GemvArgs {
 cudaError_t launch_gemv_gateup(const GemvArgs& a, cudaStream_t s);
 cudaError_t launch_gemv_down(const GemvArgs& a, cudaStream_t s);
 
-// out[t] = sum_s w[t][s] * y[inv[t*k+s]] (+ sgate[t] * y[P + t]).
+// out[t] = sum_s w[t][s] * y[inv[t*k+s]] (+ sgate[t] * y[P + t] for t < Tsh); with
+// idx non-null, slots whose bucket idx[t*k+s] >= E_real are skipped.
 cudaError_t launch_combine(const float* y, const int32_t* inv, const float* w, const float* sgate,
-                           int T, int k, int d, int has_shared, float* out, cudaStream_t s);
+                           const int32_t* idx, int E_real, int T, int Tsh, int k, int d, int has_shared,
+                           float* out, cudaStream_t s);
+
+// Expert-parallel exchange (ep.cu). Rank r owns experts [begin[r], begin[r+1]).
+constexpr int kEpMaxRanks = 64;
+struct EpRankTable {
+    int n;
+    int begin[kEpMaxRanks + 1];
+};
+// Send plan for T local tokens with top-k ids idx (T, k): send_tok/send_rank
+// (S rows, remote ranks in order, tokens in order), counts[n] rows per rank and
+// counts[n] = S, pos (T, n) send row per (token, rank) or -1.
+cudaError_t launch_ep_plan(const int32_t* idx, int T, int k, const EpRankTable& rt, int me, int32_t* send_tok,
+                           int32_t* send_rank, int32_t* counts, int32_t* pos, cudaStream_t s);
+// Writes self rows (T) and send rows (S, read from counts) with their metadata
+// rows of meta_ld int32: k ids (-1 where the destination does not own the
+// slot's expert), k weights, the shared gate (self rows only), zero padding.
+cudaError_t launch_ep_pack(const float* x, int T, int dp, int k, const int32_t* idx, const float* w,
+                           const float* sgate, int has_shared, const EpRankTable& rt, int me,
+                           const int32_t* send_tok, const int32_t* send_rank, const int32_t* counts, int rows_f16,
+                           void* self_rows, int32_t* self_meta, void* send_rows, int32_t* send_meta, int meta_ld,
+                           int max_rows, int n_sm, cudaStream_t s);
+// Receiver side: metadata -> idx (bucket E for slots owned elsewhere), w, sgate.
+cudaError_t launch_ep_prep(const int32_t* meta, int meta_ld, int R, int k, int Tsh, int e_begin, int e_end, int E,
+                           int32_t* idx, float* w, float* sgate, int32_t* bad, cudaStream_t s);
+cudaError_t launch_xsum16(const float* x, int R, int dp, float* xsum16, cudaStream_t s);
+// out[t] = self_out[t] + sum over remote ranks (ascending) of back[pos[t][r]].
+cudaError_t launch_ep_combine(const float* self_out, const float* back, const int32_t* pos, int T, int n, int me,
+                              int dp, float* out, cudaStream_t s);
 
 // Quant helpers.
 cudaError_t launch_repack(int dtype, const uint8_t* gguf, int64_t n_rows_total, int cols,

@@ -49,7 +49,7 @@ struct Scratch {
     void* base = nullptr;
     size_t bytes = 0;
     float *x_stage, *out_stage, *lg_stage, *logits, *w, *sgate, *xsum16, *act, *asum16, *y;
-    int32_t *idx, *offsets, *perm, *inv, *act_e, *act_off, *n_active;
+    int32_t *idx, *offsets, *perm, *inv, *act_e, *act_off, *n_active, *ep_bad;
     void* dwork;
     void* gemm_ws;
     size_t gemm_ws_bytes = 0;
@@ -89,6 +89,9 @@ struct Handle {
     GemmWeightMaps wmaps{};
     int n_sm = 148;
     int last_active = -1;     // active experts of the last profiled call
+    int last_pairs = -1;      // its routed (token, expert) pairs computed here
+    int last_shared_rows = 0; // its rows through the shared expert
+    bool last_gemm = false;   // whether it took the GEMM path
 
     ~Handle() {
         if (device >= 0) cudaSetDevice(device);
@@ -109,6 +112,9 @@ struct Handle {
         va_end(ap);
         err = buf;
         return false;
+    }
+    void mark(int i) {
+        if (profiling) cudaEventRecord(sev[i], stream);
     }
     bool cuda_ok(cudaError_t e, const char* what) {
         if (e == cudaSuccess) return true;
@@ -233,9 +239,10 @@ bool ensure_scratch(Handle& h, int T) {
     const int64_t grows = gemv_T * h.k + gemv_T;
     const size_t o_act = take((size_t)grows * h.act_ld * 4), o_as = take((size_t)grows * (h.act_ld / 16) * 4);
     const size_t o_y = take((size_t)grows * h.dp * 4);
-    const size_t o_idx = take((size_t)P * 4), o_off = take((size_t)(h.E + 1) * 4), o_perm = take((size_t)P * 4);
+    const size_t o_idx = take((size_t)P * 4), o_off = take((size_t)(h.E + 2) * 4), o_perm = take((size_t)P * 4);
     const size_t o_inv = take((size_t)P * 4), o_ae = take((size_t)h.E * 4), o_ao = take((size_t)(h.E + 1) * 4);
-    const size_t o_na = take(4), o_dw = take(dispatch_work_bytes((int)P, h.E));
+    const size_t o_na = take(4), o_dw = take(dispatch_work_bytes((int)P, h.E + 1));
+    const size_t o_bad = take(4);
     const int max_tiles = gemm_max_tiles((int)P, cap, h.E, h.has_shared);
     const size_t gws = h.gemm_ok ? gemm_workspace_bytes(h.dp, h.act_ld, (int)P, cap, max_tiles) : 256;
     const size_t o_gw = take(gws);
@@ -271,6 +278,7 @@ bool ensure_scratch(Handle& h, int T) {
     s.act_e = (int32_t*)(b + o_ae);
     s.act_off = (int32_t*)(b + o_ao);
     s.n_active = (int32_t*)(b + o_na);
+    s.ep_bad = (int32_t*)(b + o_bad);
     s.dwork = b + o_dw;
     s.gemm_ws = b + o_gw;
     s.gemm_ws_bytes = gws;
@@ -285,17 +293,14 @@ bool ensure_scratch(Handle& h, int T) {
     return h.cuda_ok(cudaMemsetAsync(base, 0, off, h.stream), "scratch clear");
 }
 
-// Core pipeline on device buffers: x (T, dp), out (T, dp). When logits_in is
-// non-null it holds (T, E) caller logits on the device (row stride E).
-bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* out) {
+// Router projection + top-k for T tokens of x (T, dp): s.idx, s.w, s.sgate,
+// s.xsum16. When logits_in is non-null it holds (T, E) caller logits on the
+// device (row stride E).
+bool route_stage(Handle& h, const float* x, int T, const float* logits_in) {
     Scratch& s = h.sc;
     cudaStream_t st = h.stream;
-    const int P = T * h.k;
     const int ld = h.E + 1;
-    auto mark = [&](int i) {
-        if (h.profiling) cudaEventRecord(h.sev[i], st);
-    };
-    mark(0);
+    h.mark(0);
     if (!logits_in) {
         if (!h.has_router) return h.fail("this layer has no router weights; use the ffn_block form with logits");
         if (!h.cuda_ok(launch_router(x, T, h.dp, h.router_ext, 0, h.E + h.has_shared, h.router_bias, h.E, s.logits, ld, st),
@@ -311,18 +316,37 @@ bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* 
             return false;
     }
     h.launches += (!logits_in || h.has_shared) ? 1 : 0;
-    mark(1);
+    h.mark(1);
     if (!h.cuda_ok(launch_topk(s.logits, ld, T, h.E, h.k, h.norm, h.has_shared, x, h.dp, s.idx, s.w, s.sgate, s.xsum16, st),
                    "top-k"))
         return false;
     h.launches += 1;
-    mark(2);
-    if (!h.cuda_ok(launch_dispatch(s.idx, P, h.E, s.offsets, s.perm, s.inv, s.act_e, s.act_off, s.n_active, s.dwork, st),
+    h.mark(2);
+    return true;
+}
+
+// Dispatch -> expert products -> combine over T rows of x (f32, or f16 for
+// the GEMM path) whose pairs are in s.idx / s.w. The shared expert runs on rows
+// [0, Tsh). With skip_slots, buckets equal to E mark slots to leave out (their
+// experts live on another rank). The GEMM path runs when x is f16 or T reaches
+// the handle's threshold.
+bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool skip_slots, float* out) {
+    Scratch& s = h.sc;
+    cudaStream_t st = h.stream;
+    const int P = T * h.k;
+    const int n_buckets = skip_slots ? h.E + 1 : h.E;
+    if (!h.cuda_ok(launch_dispatch(s.idx, P, n_buckets, s.offsets, s.perm, s.inv, s.act_e, s.act_off, s.n_active, s.dwork,
+                                   st, h.E),
                    "dispatch"))
         return false;
     h.launches += 3;
-    mark(3);
-    if (h.gemm_ok && h.gb_ready && T >= h.gemm_min_tokens) {
+    h.mark(3);
+    const int32_t* skip_idx = skip_slots ? s.idx : nullptr;
+    const bool use_gemm = h.gemm_ok && h.gb_ready && (x_f16 || T >= h.gemm_min_tokens);
+    if (x_f16 && !use_gemm) return h.fail("f16 rows need the prefill GEMM path, which this layer does not support");
+    h.last_gemm = use_gemm;
+    h.last_shared_rows = h.has_shared ? Tsh : 0;
+    if (use_gemm) {
         PrefillArgs pa{};
         pa.gate = h.gate;
         pa.up = h.up;
@@ -331,6 +355,9 @@ bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* 
         pa.su = h.su;
         pa.sd = h.sd;
         pa.x = x;
+        pa.x_f16 = x_f16 ? 1 : 0;
+        pa.Tsh = Tsh;
+        pa.p_real = s.offsets + h.E;
         pa.perm = s.perm;
         pa.act_e = s.act_e;
         pa.act_off = s.act_off;
@@ -345,60 +372,79 @@ bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* 
         pa.act_ld = h.act_ld;
         pa.e_begin = h.e_begin;
         pa.n_sm = h.n_sm;
-        int nl = 0;
-        if (!h.cuda_ok(launch_prefill(pa, h.gb, h.wmaps, st, &nl), "prefill GEMM")) return false;
-        h.launches += nl;
-        mark(4);
-        mark(5);
-        if (!h.cuda_ok(launch_combine_h(h.gb.y, s.inv, s.w, s.sgate, T, h.k, h.dp, h.has_shared, out, st), "combine"))
+        if (!h.cuda_ok(launch_prefill_prep(pa, h.gb, st), "prefill gather")) return false;
+        h.mark(3);
+        if (!h.cuda_ok(launch_prefill_gemm(pa, h.gb, h.wmaps, true, st), "gate/up GEMM")) return false;
+        h.mark(4);
+        if (!h.cuda_ok(launch_prefill_gemm(pa, h.gb, h.wmaps, false, st), "down GEMM")) return false;
+        h.launches += 4;
+        h.mark(5);
+        if (!h.cuda_ok(launch_combine_h(h.gb.y, s.inv, s.w, s.sgate, skip_idx, h.E, T, Tsh, h.k, h.dp, h.has_shared, out,
+                                        st),
+                       "combine"))
             return false;
         h.launches += 1;
     } else {
-    if (T > s.gemv_cap) return h.fail("internal: GEMV scratch covers %d tokens, call has %d", s.gemv_cap, T);
-    GemvArgs a{};
-    a.gate = h.gate;
-    a.up = h.up;
-    a.down = h.down;
-    a.sg = h.sg;
-    a.su = h.su;
-    a.sd = h.sd;
-    a.x = x;
-    a.xsum16 = s.xsum16;
-    a.perm = s.perm;
-    a.act_e = s.act_e;
-    a.act_off = s.act_off;
-    a.n_active = s.n_active;
-    a.T = T;
-    a.k = h.k;
-    a.d = h.dp;
-    a.F = h.Fp;
-    a.Fs = h.Fsp;
-    a.has_shared = h.has_shared;
-    a.max_active = std::min(P, h.E);
-    a.act_ld = h.act_ld;
-    a.act = s.act;
-    a.asum16 = s.asum16;
-    a.y = s.y;
-    if (!h.cuda_ok(launch_gemv_gateup(a, st), "gate/up")) return false;
-    mark(4);
-    if (!h.cuda_ok(launch_gemv_down(a, st), "down")) return false;
-    h.launches += 2 * (1 + h.has_shared);
-    mark(5);
-    if (!h.cuda_ok(launch_combine(s.y, s.inv, s.w, s.sgate, T, h.k, h.dp, h.has_shared, out, st), "combine")) return false;
-    h.launches += 1;
+        if (T > s.gemv_cap) return h.fail("internal: GEMV scratch covers %d tokens, call has %d", s.gemv_cap, T);
+        GemvArgs a{};
+        a.gate = h.gate;
+        a.up = h.up;
+        a.down = h.down;
+        a.sg = h.sg;
+        a.su = h.su;
+        a.sd = h.sd;
+        a.x = static_cast<const float*>(x);
+        a.xsum16 = s.xsum16;
+        a.perm = s.perm;
+        a.act_e = s.act_e;
+        a.act_off = s.act_off;
+        a.n_active = s.n_active;
+        a.T = T;
+        a.Tsh = Tsh;
+        a.k = h.k;
+        a.d = h.dp;
+        a.F = h.Fp;
+        a.Fs = h.Fsp;
+        a.has_shared = h.has_shared;
+        a.max_active = std::min(P, h.E);
+        a.act_ld = h.act_ld;
+        a.act = s.act;
+        a.asum16 = s.asum16;
+        a.y = s.y;
+        if (!h.cuda_ok(launch_gemv_gateup(a, st), "gate/up")) return false;
+        h.mark(4);
+        if (!h.cuda_ok(launch_gemv_down(a, st), "down")) return false;
+        h.launches += 2 * (1 + (h.has_shared && Tsh > 0));
+        h.mark(5);
+        if (!h.cuda_ok(launch_combine(s.y, s.inv, s.w, s.sgate, skip_idx, h.E, T, Tsh, h.k, h.dp, h.has_shared, out, st),
+                       "combine"))
+            return false;
+        h.launches += 1;
     }
-    mark(6);
-    if (h.profiling) {
-        if (!h.cuda_ok(cudaEventSynchronize(h.sev[6]), "profile")) return false;
-        for (int i = 0; i < Handle::kStages; ++i) {
-            float ms = 0.f;
-            cudaEventElapsedTime(&ms, h.sev[i], h.sev[i + 1]);
-            h.stage_ms[i] += ms;
-            h.stage_n[i] += 1;
-        }
-        cudaMemcpy(&h.last_active, s.n_active, 4, cudaMemcpyDeviceToHost);
-    }
+    h.mark(6);
     return true;
+}
+
+// Accumulates the per-stage event times of a profiled call.
+bool finish_profile(Handle& h) {
+    if (!h.profiling) return true;
+    if (!h.cuda_ok(cudaEventSynchronize(h.sev[6]), "profile")) return false;
+    for (int i = 0; i < Handle::kStages; ++i) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, h.sev[i], h.sev[i + 1]);
+        h.stage_ms[i] += ms;
+        h.stage_n[i] += 1;
+    }
+    cudaMemcpy(&h.last_active, h.sc.n_active, 4, cudaMemcpyDeviceToHost);
+    cudaMemcpy(&h.last_pairs, h.sc.offsets + h.E, 4, cudaMemcpyDeviceToHost);
+    return true;
+}
+
+// Core pipeline on device buffers: x (T, dp), out (T, dp).
+bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* out) {
+    if (!route_stage(h, x, T, logits_in)) return false;
+    if (!expert_stage(h, x, false, T, T, false, out)) return false;
+    return finish_profile(h);
 }
 
 // The prefill kernels record a non-zero code when one of their bounded waits
@@ -914,6 +960,133 @@ int aero_cuda_moe_info(void* handle, int32_t* out8) {
     return 0;
 }
 
+// ------------------------------------------------------------ expert parallel
+// The exchange itself (NCCL all-to-all) belongs to the caller; these three
+// calls are the device work on either side of it. All pointers are device
+// pointers; the work is enqueued on the handle's stream and the calls return
+// without synchronising.
+
+int aero_cuda_ep_meta_ld(void* handle) {
+    auto* h = static_cast<Handle*>(handle);
+    return h ? 2 * h->k + 2 : -1;
+}
+
+static bool ep_rank_table(Handle& h, int n_ranks, int rank, const int32_t* begin, aero::EpRankTable* rt) {
+    if (n_ranks < 1 || n_ranks > aero::kEpMaxRanks) return h.fail("n_ranks=%d outside [1, %d]", n_ranks, aero::kEpMaxRanks);
+    if (rank < 0 || rank >= n_ranks) return h.fail("rank %d outside [0, %d)", rank, n_ranks);
+    if (!begin) return h.fail("rank_expert_begin is required");
+    if (begin[0] != 0 || begin[n_ranks] != h.E) return h.fail("rank_expert_begin must run from 0 to %d", h.E);
+    for (int r = 0; r < n_ranks; ++r)
+        if (begin[r + 1] < begin[r]) return h.fail("rank_expert_begin is not ascending at rank %d", r);
+    if (begin[rank] != h.e_begin || begin[rank + 1] != h.e_end)
+        return h.fail("rank %d owns [%d, %d) in the table but this handle holds [%d, %d)", rank, begin[rank],
+                      begin[rank + 1], h.e_begin, h.e_end);
+    rt->n = n_ranks;
+    for (int r = 0; r <= n_ranks; ++r) rt->begin[r] = begin[r];
+    return true;
+}
+
+int aero_cuda_ep_dispatch(void* handle, const float* x, int T, int n_ranks, int rank, const int32_t* rank_expert_begin,
+                          int row_dtype, void* self_rows, int32_t* self_meta, void* send_rows, int32_t* send_meta,
+                          int send_cap, int32_t* counts, int32_t* pos) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    aero::EpRankTable rt{};
+    if (!ep_rank_table(*h, n_ranks, rank, rank_expert_begin, &rt)) return -1;
+    if (T < 0) return h->fail("T=%d", T), -1;
+    if (row_dtype != AERO_EP_ROWS_F32 && row_dtype != AERO_EP_ROWS_F16) return h->fail("row_dtype %d", row_dtype), -1;
+    if (h->d != h->dp) return h->fail("expert parallel needs n_embd %% 128 == 0 (n_embd=%d)", h->d), -1;
+    const int64_t need = (int64_t)T * std::min(h->k, n_ranks - 1);
+    if (send_cap < need) return h->fail("send_cap %d < T * min(k, n_ranks - 1) = %lld", send_cap, (long long)need), -1;
+    if (!counts || !pos || (T > 0 && (!x || !self_rows || !self_meta)) || (need > 0 && (!send_rows || !send_meta)))
+        return h->fail("null buffer"), -1;
+    for (const void* p : {(const void*)x, (const void*)self_rows, (const void*)send_rows})
+        if (p && (!aero::is_device_ptr(p) || ((uintptr_t)p & 15) != 0))
+            return h->fail("row buffers must be 16-byte aligned device memory"), -1;
+    cudaSetDevice(h->device);
+    if (!aero::ensure_scratch(*h, std::max(T, 1))) return -1;
+    auto& s = h->sc;
+    if (T > 0 && !aero::route_stage(*h, x, T, nullptr)) return -1;
+    // the plan reuses the dispatch buffers: perm holds send_tok, inv send_rank
+    if (!h->cuda_ok(aero::launch_ep_plan(s.idx, T, h->k, rt, rank, s.perm, s.inv, counts, pos, h->stream), "exchange plan"))
+        return -1;
+    if (!h->cuda_ok(aero::launch_ep_pack(x, T, h->dp, h->k, s.idx, s.w, s.sgate, h->has_shared, rt, rank, s.perm, s.inv,
+                                         counts, row_dtype == AERO_EP_ROWS_F16, self_rows, self_meta, send_rows, send_meta,
+                                         2 * h->k + 2, (int)(T + need), h->n_sm, h->stream),
+                    "exchange pack"))
+        return -1;
+    h->launches += 2;
+    return 0;
+}
+
+int aero_cuda_ep_expert_block(void* handle, const void* rows, int row_dtype, const int32_t* meta, int R, int n_shared,
+                              float* out) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (R < 0 || n_shared < 0 || n_shared > R) return h->fail("R=%d n_shared=%d", R, n_shared), -1;
+    if (row_dtype != AERO_EP_ROWS_F32 && row_dtype != AERO_EP_ROWS_F16) return h->fail("row_dtype %d", row_dtype), -1;
+    if (h->d != h->dp) return h->fail("expert parallel needs n_embd %% 128 == 0 (n_embd=%d)", h->d), -1;
+    if (R == 0) return 0;
+    if (!rows || !meta || !out) return h->fail("null buffer"), -1;
+    for (const void* p : {(const void*)rows, (const void*)out})
+        if (!aero::is_device_ptr(p) || ((uintptr_t)p & 15) != 0)
+            return h->fail("rows and out must be 16-byte aligned device memory"), -1;
+    cudaSetDevice(h->device);
+    if (!aero::ensure_scratch(*h, R)) return -1;
+    auto& s = h->sc;
+    const bool f16 = row_dtype == AERO_EP_ROWS_F16;
+    h->mark(0);
+    h->mark(1);
+    if (!h->cuda_ok(aero::launch_ep_prep(meta, 2 * h->k + 2, R, h->k, n_shared, h->e_begin, h->e_end, h->E, s.idx, s.w,
+                                         s.sgate, s.ep_bad, h->stream),
+                    "exchange unpack"))
+        return -1;
+    h->launches += 1;
+    const bool gemv = !f16 && !(h->gemm_ok && h->gb_ready && R >= h->gemm_min_tokens);
+    if (gemv) {
+        if (!h->cuda_ok(aero::launch_xsum16(static_cast<const float*>(rows), R, h->dp, s.xsum16, h->stream), "row sums"))
+            return -1;
+        h->launches += 1;
+    }
+    h->mark(2);
+    if (!aero::expert_stage(*h, rows, f16, R, n_shared, true, out)) return -1;
+    return aero::finish_profile(*h) ? 0 : -1;
+}
+
+int aero_cuda_ep_combine(void* handle, const float* self_out, const float* back, const int32_t* pos, int T, int n_ranks,
+                         int rank, float* out) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (n_ranks < 1 || n_ranks > aero::kEpMaxRanks || rank < 0 || rank >= n_ranks)
+        return h->fail("n_ranks=%d rank=%d", n_ranks, rank), -1;
+    if (T < 0) return h->fail("T=%d", T), -1;
+    if (T == 0) return 0;
+    if (!self_out || !pos || !out || (n_ranks > 1 && !back)) return h->fail("null buffer"), -1;
+    cudaSetDevice(h->device);
+    if (!h->cuda_ok(aero::launch_ep_combine(self_out, back, pos, T, n_ranks, rank, h->dp, out, h->stream), "exchange combine"))
+        return -1;
+    h->launches += 1;
+    return 0;
+}
+
+// Number of metadata ids that named an expert this rank does not own, since
+// the last call (reading it synchronises the handle's stream).
+int aero_cuda_ep_bad_ids(void* handle) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (!h->sc.base) return 0;
+    int32_t v = 0;
+    if (!h->cuda_ok(cudaMemcpyAsync(&v, h->sc.ep_bad, 4, cudaMemcpyDeviceToHost, h->stream), "bad-id count") ||
+        !h->cuda_ok(cudaStreamSynchronize(h->stream), "bad-id count"))
+        return -1;
+    if (v) cudaMemsetAsync(h->sc.ep_bad, 0, 4, h->stream);
+    return v;
+}
+
 const char* aero_cuda_moe_last_error(void* handle) {
     if (!handle) return aero::g_free_error.c_str();
     return static_cast<Handle*>(handle)->err.c_str();
@@ -927,9 +1100,11 @@ int aero_cuda_moe_stats(void* handle, char* buf, int len) {
     const int n = std::snprintf(buf, (size_t)std::max(0, len),
                                 "{\"calls\": %ld, \"tokens\": %ld, \"launches\": %ld, \"weight_bytes\": %zu, "
                                 "\"scratch_bytes\": %zu, \"scratch_tokens\": %d, \"guard_committed\": %zu, "
-                                "\"last_active\": %d, \"last_ms\": %.6f}",
+                                "\"last_active\": %d, \"last_pairs\": %d, \"last_shared_rows\": %d, "
+                                "\"last_gemm\": %d, \"last_ms\": %.6f}",
                                 h->calls, h->tokens, h->launches, wbytes, h->sc.bytes, h->sc.cap_T,
-                                aero_cuda_guard_committed(-1), h->last_active, (double)h->last_ms);
+                                aero_cuda_guard_committed(-1), h->last_active, h->last_pairs, h->last_shared_rows,
+                                h->last_gemm ? 1 : 0, (double)h->last_ms);
     return n;
 }
 

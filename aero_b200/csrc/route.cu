@@ -237,7 +237,8 @@ __global__ void dispatch_count_kernel(const int32_t* __restrict__ idx, int P, in
 constexpr int kScanThreads = 1024;
 
 __global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(int32_t* __restrict__ counts, int n_chunks,
-                                                                     int E, int P, int32_t* __restrict__ offsets,
+                                                                     int E, int n_real, int P,
+                                                                     int32_t* __restrict__ offsets,
                                                                      int32_t* __restrict__ act_e,
                                                                      int32_t* __restrict__ act_off,
                                                                      int32_t* __restrict__ n_active) {
@@ -263,11 +264,12 @@ __global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(int32_t* __
         int excl, excl_act;
         Scan(tmp).ExclusiveSum(tot, excl);
         __syncthreads();
-        Scan(tmp).ExclusiveSum(tot > 0 ? 1 : 0, excl_act);
+        const bool active = tot > 0 && e < n_real;  // buckets >= n_real hold skipped slots
+        Scan(tmp).ExclusiveSum(active ? 1 : 0, excl_act);
         const int base = carry_tot, abase = carry_act;
         if (e < E) {
             offsets[e] = base + excl;
-            if (tot > 0) {
+            if (active) {
                 act_e[abase + excl_act] = e;
                 act_off[abase + excl_act] = base + excl;
             }
@@ -275,13 +277,13 @@ __global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(int32_t* __
         __syncthreads();
         if (threadIdx.x == kScanThreads - 1) {
             carry_tot = base + excl + tot;
-            carry_act = abase + excl_act + (tot > 0 ? 1 : 0);
+            carry_act = abase + excl_act + (active ? 1 : 0);
         }
         __syncthreads();
     }
     if (threadIdx.x == 0) {
         offsets[E] = P;
-        act_off[carry_act] = P;
+        act_off[carry_act] = n_real < E ? offsets[n_real] : P;
         *n_active = carry_act;
     }
 }
@@ -345,12 +347,14 @@ size_t dispatch_work_bytes(int P, int E) {
 }
 
 cudaError_t launch_dispatch(const int32_t* idx, int P, int E, int32_t* offsets, int32_t* perm, int32_t* inv,
-                            int32_t* act_e, int32_t* act_off, int32_t* n_active, void* work, cudaStream_t s) {
+                            int32_t* act_e, int32_t* act_off, int32_t* n_active, void* work, cudaStream_t s,
+                            int n_real) {
+    if (n_real < 0) n_real = E;
     const int n_chunks = std::max(1, (P + kDispChunk - 1) / kDispChunk);
     int32_t* counts = static_cast<int32_t*>(work);
     const size_t hist_smem = (size_t)E * sizeof(int32_t);
     dispatch_count_kernel<<<n_chunks, 256, hist_smem, s>>>(idx, P, E, counts);
-    dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(counts, n_chunks, E, P, offsets, act_e, act_off, n_active);
+    dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(counts, n_chunks, E, n_real, P, offsets, act_e, act_off, n_active);
     dispatch_scatter_kernel<<<n_chunks, 128, hist_smem, s>>>(idx, P, E, offsets, counts, perm, inv);
     return cudaGetLastError();
 }

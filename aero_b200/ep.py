@@ -1,0 +1,203 @@
+"""Expert-parallel MoE layer: one process per GPU, NCCL all-to-all between them.
+
+The reference runs a layer in one process (engine/moe.py:117-177,
+src/moe.cpp:122-161); this is the sharded form of the same computation.
+Rank r holds experts [begin[r], begin[r+1]) of the layer (begin from
+`expert_ranges`), the full router and the shared expert, and owns T_r of the
+step's tokens. A step on each rank:
+
+1. `aero_cuda_ep_dispatch` routes the local tokens over all experts and writes
+   the self rows (every local token, straight into the head of the receive
+   buffer) and one send row per (token, remote rank owning one of its experts),
+   ordered by rank then token, each with a metadata row (expert ids owned by
+   the destination, weights, shared gate);
+2. counts, rows and metadata cross with `all_to_all_single`; received rows land
+   after the self rows;
+3. `aero_cuda_ep_expert_block` runs this rank's experts over all R rows (the
+   self rows also take the shared expert) and writes one f32 row per row;
+4. rows [T_r, R) of that output go back with the reverse `all_to_all_single`,
+   arriving in send-row order;
+5. `aero_cuda_ep_combine` adds, per token, the self part and then the remote
+   parts in rank order.
+
+Every rank takes the same collective steps in the same order, also for T_r = 0.
+The device work runs on the torch current stream, which the NCCL collectives
+order against, so the only host synchronisation is the count exchange.
+"""
+
+from __future__ import annotations
+
+from typing import List
+
+ROWS_F32 = 0
+ROWS_F16 = 1
+
+
+def expert_ranges(n_expert: int, world: int) -> List[int]:
+    """begin[0..world]: rank r holds experts [begin[r], begin[r+1]) (E/world each,
+    the first E % world ranks one more)."""
+    if world < 1 or world > n_expert:
+        raise ValueError(f"world size {world} must be in [1, n_expert={n_expert}]")
+    base, extra = divmod(n_expert, world)
+    begin = [0]
+    for r in range(world):
+        begin.append(begin[-1] + base + (1 if r < extra else 0))
+    return begin
+
+
+def token_shards(T: int, world: int) -> List[int]:
+    """Token offsets[0..world] of a T-token batch split over the ranks."""
+    base, extra = divmod(T, world)
+    off = [0]
+    for r in range(world):
+        off.append(off[-1] + base + (1 if r < extra else 0))
+    return off
+
+
+class CudaEpOps:
+    """The device side of a step, through the library's C ABI (device pointers)."""
+
+    def __init__(self, layer) -> None:
+        from . import native_cuda as nc
+
+        self.nc = nc
+        self.lib = nc.lib()
+        self.layer = layer
+        self.h = layer.handle
+        self.meta_ld = int(self.lib.aero_cuda_ep_meta_ld(self.h))
+
+    def _check(self, rc: int, what: str) -> None:
+        if rc != 0:
+            raise RuntimeError(f"{what}: {self.nc.last_error(self.h)}")
+
+    def set_stream(self, stream) -> None:
+        self.layer.set_stream(stream)
+
+    def dispatch(self, x, T, world, rank, begin, row_dtype, self_rows, self_meta, send_rows, send_meta, counts, pos):
+        tab = (self.nc.c_int32 * len(begin))(*begin)
+        rc = self.lib.aero_cuda_ep_dispatch(self.h, x.data_ptr(), T, world, rank, tab, row_dtype, self_rows.data_ptr(),
+                                            self_meta.data_ptr(), send_rows.data_ptr(), send_meta.data_ptr(),
+                                            send_rows.shape[0], counts.data_ptr(), pos.data_ptr())
+        self._check(rc, "aero_cuda_ep_dispatch")
+
+    def expert_block(self, rows, row_dtype, meta, R, n_shared, out):
+        rc = self.lib.aero_cuda_ep_expert_block(self.h, rows.data_ptr(), row_dtype, meta.data_ptr(), R, n_shared,
+                                                out.data_ptr())
+        self._check(rc, "aero_cuda_ep_expert_block")
+
+    def combine(self, self_out, back, pos, T, world, rank, out):
+        rc = self.lib.aero_cuda_ep_combine(self.h, self_out.data_ptr(), back.data_ptr(), pos.data_ptr(), T, world,
+                                           rank, out.data_ptr())
+        self._check(rc, "aero_cuda_ep_combine")
+
+
+class ExpertParallelMoe:
+    """One rank's share of an expert-parallel MoE layer.
+
+    `ops` does the device work (CudaEpOps for a CudaMoeLayer opened with this
+    rank's expert range); `forward(x)` takes this rank's tokens (T_r, n_embd)
+    f32 on `device` and returns their layer output. `max_tokens` bounds T_r on
+    every rank (it sizes the exchange buffers once). With `row_f16` the rows
+    cross as f16 (the GEMM path's operand type; halves the bytes); otherwise f32.
+    `exchange(out, inp, out_splits, in_splits)` replaces
+    torch.distributed.all_to_all_single over `group` (None splits: equal).
+    """
+
+    def __init__(self, ops, n_embd: int, n_expert: int, k: int, world: int, rank: int, max_tokens: int,
+                 device="cuda", group=None, row_f16: bool = True, guard: bool = True, exchange=None) -> None:
+        import torch
+        import torch.distributed as dist
+
+        self.torch, self.dist = torch, dist
+        self.ops, self.d, self.E, self.k = ops, n_embd, n_expert, k
+        self.world, self.rank, self.group = world, rank, group
+        self.exchange = exchange
+        self.begin = expert_ranges(n_expert, world)
+        self.row_dtype = ROWS_F16 if row_f16 else ROWS_F32
+        self.device = torch.device(device)
+        rdt = torch.float16 if row_f16 else torch.float32
+        ml = ops.meta_ld
+        self.max_tokens = int(max_tokens)
+        send_cap = max(1, self.max_tokens * min(k, world - 1))
+        recv_cap = max(1, self.max_tokens * world)  # self rows + at most every token of every other rank
+        dev = self.device
+        self.send_rows = torch.empty((send_cap, n_embd), dtype=rdt, device=dev)
+        self.send_meta = torch.empty((send_cap, ml), dtype=torch.int32, device=dev)
+        self.recv_rows = torch.empty((recv_cap, n_embd), dtype=rdt, device=dev)
+        self.recv_meta = torch.empty((recv_cap, ml), dtype=torch.int32, device=dev)
+        self.y = torch.empty((recv_cap, n_embd), dtype=torch.float32, device=dev)
+        self.back = torch.empty((send_cap, n_embd), dtype=torch.float32, device=dev)
+        self.counts = torch.zeros(world + 1, dtype=torch.int32, device=dev)
+        self.recv_counts = torch.zeros(world, dtype=torch.int32, device=dev)
+        self.pos = torch.empty((max(1, self.max_tokens), world), dtype=torch.int32, device=dev)
+        self._reserved = 0
+        if self.device.type == "cuda":
+            # one stream for the library's kernels and the collectives' ordering
+            ops.set_stream(torch.cuda.current_stream(self.device))
+        if guard and self.device.type == "cuda":
+            # the exchange buffers are torch allocations; charge them to the
+            # library's memory guard so its accounting covers them
+            from . import native_cuda as nc
+
+            nbytes = sum(t.numel() * t.element_size() for t in (self.send_rows, self.send_meta, self.recv_rows,
+                                                                 self.recv_meta, self.y, self.back, self.pos))
+            g = nc.MemoryGuard()
+            if not g.try_reserve(nbytes, nc.MEM_SCRATCH):
+                raise RuntimeError(f"expert-parallel exchange buffers ({nbytes} bytes) refused by the memory guard")
+            self._guard, self._reserved = g, nbytes
+        self.last_split = None
+
+    def close(self) -> None:
+        if self._reserved:
+            from . import native_cuda as nc
+
+            self._guard.release(self._reserved, nc.MEM_SCRATCH)
+            self._reserved = 0
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _a2a(self, out, inp, out_splits, in_splits) -> None:
+        if self.exchange is not None:
+            self.exchange(out, inp, out_splits, in_splits)
+        else:
+            self.dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def forward(self, x):
+        torch = self.torch
+        T = int(x.shape[0])
+        if x.dim() != 2 or x.shape[1] != self.d:
+            raise ValueError(f"hidden width {tuple(x.shape)} != n_embd {self.d}")
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens on rank {self.rank} > max_tokens {self.max_tokens}")
+        x = x.contiguous().float()
+        n, r = self.world, self.rank
+        self.ops.dispatch(x, T, n, r, self.begin, self.row_dtype, self.recv_rows, self.recv_meta, self.send_rows,
+                          self.send_meta, self.counts, self.pos)
+        self._a2a(self.recv_counts, self.counts[:n], None, None)
+        both = torch.cat([self.counts[:n], self.recv_counts]).cpu().tolist()  # the step's one host sync
+        send, recv = [int(v) for v in both[:n]], [int(v) for v in both[n:]]
+        S, Rr = sum(send), sum(recv)
+        if T + Rr > self.recv_rows.shape[0]:
+            raise RuntimeError(f"rank {r} receives {Rr} rows, more than max_tokens allows")
+        self.last_split = (send, recv)
+        self._a2a(self.recv_rows[T:T + Rr], self.send_rows[:S], recv, send)
+        self._a2a(self.recv_meta[T:T + Rr], self.send_meta[:S], recv, send)
+        self.ops.expert_block(self.recv_rows, self.row_dtype, self.recv_meta, T + Rr, T, self.y)
+        self._a2a(self.back[:S], self.y[T:T + Rr], send, recv)
+        out = torch.empty((T, self.d), dtype=torch.float32, device=self.device)
+        self.ops.combine(self.y, self.back, self.pos, T, n, r, out)
+        return out
+
+    __call__ = forward
+
+
+def open_rank_layer(layer_src, world: int, rank: int, device: int = 0):
+    """Open rank `rank`'s share of a synthetic layer (aero_b200.synth.SynthLayer)."""
+    from . import synth
+
+    begin = expert_ranges(layer_src.spec.E, world)
+    return synth.open_layer(layer_src, device=device, expert_range=(begin[rank], begin[rank + 1]))

@@ -75,6 +75,12 @@ SYMBOLS = [
     ("aero_cuda_moe_set_profiling", c_int, [_P, c_int]),
     ("aero_cuda_moe_stage_times", c_int, [_P, _P, _P, c_int]),
     ("aero_cuda_moe_set_option", c_int, [_P, c_int, c_int64]),
+    ("aero_cuda_ep_meta_ld", c_int, [_P]),
+    ("aero_cuda_ep_dispatch", c_int, [_P, _P, c_int, c_int, c_int, POINTER(c_int32), c_int, _P, _P, _P, _P, c_int,
+                                      _P, _P]),
+    ("aero_cuda_ep_expert_block", c_int, [_P, _P, c_int, _P, c_int, c_int, _P]),
+    ("aero_cuda_ep_combine", c_int, [_P, _P, _P, _P, c_int, c_int, c_int, _P]),
+    ("aero_cuda_ep_bad_ids", c_int, [_P]),
     ("aero_cuda_moe_set_stream", c_int, [_P, _P]),
     ("aero_cuda_moe_info", c_int, [_P, POINTER(c_int32)]),
     ("aero_cuda_moe_last_error", c_char_p, [_P]),

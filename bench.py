@@ -9,14 +9,17 @@ quoted at 1/2/4/8 GPUs and config 5 is the configuration defined at those
 counts. A step is one layer call over the workload's tokens (config 1: 64
 one-token calls). Inputs are synthetic (seeded N(0,1) activations, N(0,0.02)
 weights quantised to GGUF blocks); no datasets or checkpoints exist here.
+With N > 1 (torchrun, one process per GPU) the layer runs expert parallel:
+E/N experts and T/N tokens per rank, rows exchanged by NCCL all-to-all
+(aero_b200.ep); the step's token count stays T (strong scaling).
 
   value        tokens/s over K steps, inputs already in HBM, device time by
                CUDA events on the layer's stream (max over ranks)
+  roofline     prefill: the larger grouped GEMM (tensor-bound: algorithmic
+               FLOPs / its CUDA-event time vs the sustained bf16 peak);
+               decode: the dominant stage (HBM-bound: GGUF bytes streamed)
   e2e          the same through the public API with host buffers: pinned
                host input -> device, layer, device -> pinned host output
-  roofline     the dominant kernel: algorithmic bytes (GGUF bytes of the
-               experts it streams) / its average duration from per-stage
-               CUDA events, against MEASURED_PEAKS.json
   cpu_baseline the reference's own MoE block (oracle/_ref, built from its
                sources) on the host cores, over a bounded token sample
 The working set (weights >= 340 MB) exceeds the 126 MB L2, so no flush runs
@@ -120,6 +123,16 @@ def layer_bytes(spec):
     return per_expert, shared
 
 
+def traffic_record(workload: str, kernel: str):
+    """DRAM bytes per launch of `kernel` on `workload` from the committed ncu
+    summary (profiles/traffic.json), or None when none was captured."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if not os.path.exists(p):
+        return None
+    rec = json.load(open(p)).get(workload, {}).get(kernel)
+    return None if rec is None else rec.get("bytes_per_launch")
+
+
 def cpu_reference(wl, layer, x, logits, budget_s: float, threads: int):
     """Time the reference's own block (or the C restatement when the reference
     objects are absent) on a bounded token sample. Returns (tokens/s, kind, sample, threads)."""
@@ -202,25 +215,54 @@ def main():
         import datetime
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     dev = local
+    cuda = f"cuda:{dev}"
 
     x_host = synth.make_x(T * wl.calls, spec.d, seed, bf16=wl.bf16_x)
     layer = synth.make_layer(spec, seed, device_gen=True)
     if wl.zipf_s:
         synth.attach_zipf(layer, x_host, wl.zipf_s, seed)
-    L = synth.open_layer(layer, device=dev)
     stream = torch.cuda.Stream(device=dev)
-    L.set_stream(stream)
-
-    x_dev = torch.from_numpy(x_host).to(f"cuda:{dev}")
-    out_dev = torch.empty_like(x_dev)
     lib = nc.lib()
+    ep_mode = ws > 1
+    if ep_mode:
+        # expert parallel: experts E/n per rank, tokens T/n per rank, NCCL
+        # all-to-all for the rows (ranks = processes, one GPU each)
+        from aero_b200 import ep
+        if wl.calls != 1:
+            raise SystemExit(f"{wl.name}: expert parallel applies to batched workloads (one call per step)")
+        begin = ep.expert_ranges(spec.E, ws)
+        shards = ep.token_shards(T, ws)
+        L = synth.open_layer(layer, device=dev, expert_range=(begin[rank], begin[rank + 1]))
+        row_f16 = T >= 64  # prefill: rows cross in the GEMM operand type
+        with torch.cuda.stream(stream):
+            moe = ep.ExpertParallelMoe(ep.CudaEpOps(L), spec.d, spec.E, spec.k, ws, rank,
+                                       max_tokens=max(shards[r + 1] - shards[r] for r in range(ws)), device=cuda,
+                                       row_f16=row_f16)
+        x_mine = x_host[shards[rank]:shards[rank + 1]]
+    else:
+        L = synth.open_layer(layer, device=dev)
+        L.set_stream(stream)
+        x_mine = x_host
+    x_dev = torch.from_numpy(x_mine).to(cuda)
+    out_dev = torch.empty_like(x_dev)
+    Tm = x_mine.shape[0] // wl.calls  # tokens per call on this rank
 
     def step_device():
+        if ep_mode:
+            out_dev.copy_(moe.forward(x_dev))
+            return
         for c in range(wl.calls):
-            xs = x_dev[c * T:(c + 1) * T]
-            os_ = out_dev[c * T:(c + 1) * T]
-            if lib.aero_cuda_moe_forward(L.handle, 0, xs.data_ptr(), T, spec.d, os_.data_ptr()) != 1:
+            xs = x_dev[c * Tm:(c + 1) * Tm]
+            os_ = out_dev[c * Tm:(c + 1) * Tm]
+            if lib.aero_cuda_moe_forward(L.handle, 0, xs.data_ptr(), Tm, spec.d, os_.data_ptr()) != 1:
                 raise RuntimeError(nc.last_error(L.handle))
+
+    def max_over_ranks(v):
+        if ws == 1:
+            return v
+        t = torch.tensor([v], device=cuda)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        return float(t.item())
 
     # ---- value: device-resident inputs
     with torch.cuda.stream(stream):
@@ -232,44 +274,49 @@ def main():
         torch.distributed.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(dev) as clk:
+    with Clocks(dev) as clk, torch.cuda.stream(stream):
         ev0.record(stream)
         for _ in range(args.steps):
             step_device()
         ev1.record(stream)
         ev1.synchronize()
     torch.cuda.synchronize()
-    ms = ev0.elapsed_time(ev1)
     launches = L.stats()["launches"] - launches0
+    ms = max_over_ranks(ev0.elapsed_time(ev1))
     if ws > 1:
-        t = torch.tensor([ms], device=f"cuda:{dev}")
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms = float(t.item())
         torch.distributed.barrier()
-    tokens_per_step = T * wl.calls * ws
+    tokens_per_step = T * wl.calls
     value = tokens_per_step * args.steps / (ms / 1000.0)
 
-    # ---- e2e: host buffers through the public API
-    xh = torch.from_numpy(x_host).pin_memory()
+    # ---- e2e: host buffers through the public API every step
+    xh = torch.from_numpy(x_mine).pin_memory()
     oh = torch.empty_like(xh).pin_memory()
 
     def step_host():
+        if ep_mode:
+            xd = xh.to(cuda, non_blocking=True)
+            oh.copy_(moe.forward(xd), non_blocking=True)
+            return
         for c in range(wl.calls):
-            if lib.aero_cuda_moe_forward(L.handle, 0, xh[c * T:(c + 1) * T].data_ptr(), T, spec.d,
-                                         oh[c * T:(c + 1) * T].data_ptr()) != 1:
+            if lib.aero_cuda_moe_forward(L.handle, 0, xh[c * Tm:(c + 1) * Tm].data_ptr(), Tm, spec.d,
+                                         oh[c * Tm:(c + 1) * Tm].data_ptr()) != 1:
                 raise RuntimeError(nc.last_error(L.handle))
 
-    for _ in range(args.warmup):
-        step_host()
-    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step_host()
+    stream.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(args.steps):
-        step_host()
-    e1.record(stream)
-    e1.synchronize()
-    e2e_ms = e0.elapsed_time(e1)
-    e2e_value = T * wl.calls * ws * args.steps / (e2e_ms / 1000.0)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(args.steps):
+            step_host()
+        e1.record(stream)
+        e1.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    e2e_value = tokens_per_step * args.steps / (e2e_ms / 1000.0)
 
     # ---- per-stage device times (a separate profiled pass)
     L.set_profiling(True)
@@ -278,23 +325,45 @@ def main():
             step_device()
     stream.synchronize()
     st = L.stage_times()
-    active = L.stats()["last_active"]
+    stats = L.stats()
     L.set_profiling(False)
     stage_avg = {k: (v[0] / v[1] if v[1] else 0.0) for k, v in st.items()}
+    pk = peaks()
     per_expert, shared = layer_bytes(spec)
     per_mat = per_expert // 3
-    # dominant stage and its algorithmic bytes
-    dom = max(stage_avg, key=stage_avg.get)
-    alg = {
-        "gate_up": active * 2 * per_mat + (2 * shared // 3 if shared else 0),
-        "down": active * per_mat + (shared // 3 if shared else 0),
-        "router": (spec.E + (1 if spec.Fs else 0)) * spec.d * 4 + T * spec.d * 4,
-        "topk": T * (spec.E + 1) * 4,
-        "dispatch": T * spec.k * 16,
-        "combine": (T * spec.k + T) * spec.d * 4 + T * spec.d * 4,
-    }[dom]
-    pk = peaks()
-    achieved = alg / (stage_avg[dom] / 1000.0) / 1e9
+    active = stats["last_active"]
+    if stats.get("last_gemm"):
+        # prefill: the grouped GEMMs are tensor-bound; gate/up is the larger one
+        pairs, srows = stats["last_pairs"], stats["last_shared_rows"]
+        dom = max(("gate_up", "down"), key=lambda k: stage_avg[k])
+        mult = 2 if dom == "gate_up" else 1
+        flops = 2.0 * mult * spec.d * (spec.F * pairs + spec.Fs * srows)
+        achieved = flops / (stage_avg[dom] / 1000.0) / 1e12
+        peak = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+        roof = {"kernel": f"grouped_gemm_{dom}", "bound": "tensor", "achieved": achieved, "peak": peak,
+                "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                "peak_source": f"{pk['source']} bf16 sustained (f16 operands run at the same rate)",
+                "algorithmic_flops": flops, "avg_ms": stage_avg[dom], "pairs": pairs, "shared_rows": srows,
+                "active_experts": active}
+        dtype = "f16"
+    else:
+        dom = max(stage_avg, key=stage_avg.get)
+        alg = {
+            "gate_up": active * 2 * per_mat + (2 * shared // 3 if shared else 0),
+            "down": active * per_mat + (shared // 3 if shared else 0),
+            "router": (spec.E + (1 if spec.Fs else 0)) * spec.d * 4 + Tm * spec.d * 4,
+            "topk": Tm * (spec.E + 1) * 4,
+            "dispatch": Tm * spec.k * 16,
+            "combine": (Tm * spec.k + Tm) * spec.d * 4 + Tm * spec.d * 4,
+        }[dom]
+        achieved = alg / (stage_avg[dom] / 1000.0) / 1e9
+        roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_source": pk["source"],
+                "algorithmic_bytes": int(alg), "avg_ms": stage_avg[dom], "active_experts": active}
+        dtype = "f32"
+    tr = traffic_record(wl.name, roof["kernel"])
+    if tr is not None:
+        roof["traffic"] = tr
     result = {
         "metric": "moe_layer_tokens_per_s",
         "value": value,
@@ -306,7 +375,7 @@ def main():
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
-        "dtype": "f32",
+        "dtype": dtype,
         "data": "synthetic",
         "config": {"workload": wl.name, "tokens_per_step": tokens_per_step, "experts": spec.E, "top_k": spec.k,
                    "d": spec.d, "ffn": spec.F, "shared_ffn": spec.Fs,
@@ -317,11 +386,11 @@ def main():
                 "d2h_bytes_per_step": int(x_host.nbytes)},
         "gpu_launches": int(launches),
         "clocks": clk.summary(),
-        "roofline": {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_source": pk["source"],
-                     "algorithmic_bytes": int(alg), "avg_ms": stage_avg[dom], "active_experts": active},
+        "roofline": roof,
         "stages_ms": {k: round(v, 5) for k, v in stage_avg.items()},
     }
+    if ep_mode:
+        result["exchange_rows"] = {"sent": moe.last_split[0], "received": moe.last_split[1]}
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         lg = x_host @ layer.router.T + (layer.router_bias if layer.router_bias is not None else 0)
         threads = os.cpu_count() or 1
@@ -330,10 +399,12 @@ def main():
                                   "sample": f"{n} of {T * wl.calls} tokens, {dt:.1f} s"}
     if rank == 0:
         print(json.dumps(result), flush=True)
+    if ep_mode:
+        moe.close()
     L.close()
     if ws > 1:
+        torch.distributed.barrier()
         torch.distributed.destroy_process_group()
-
 
 if __name__ == "__main__":
     main()

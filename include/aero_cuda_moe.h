@@ -144,11 +144,59 @@ int aero_cuda_moe_set_profiling(void* handle, int on);
 int aero_cuda_moe_stage_times(void* handle, double* ms, int64_t* counts, int n);
 
 /* Options. AERO_CUDA_OPT_GEMM_MIN_TOKENS: calls with at least this many tokens
- * run the expert products as tcgen05 grouped GEMMs (bf16 operands, fp32
+ * run the expert products as tcgen05 grouped GEMMs (f16 operands, fp32
  * accumulate); smaller calls use the fp32 GEMV path (default 64; also read from
  * the AERO_GEMM_MIN_TOKENS environment variable at open). 0 / -1. */
 #define AERO_CUDA_OPT_GEMM_MIN_TOKENS 1
 int aero_cuda_moe_set_option(void* handle, int option, int64_t value);
+
+/* ------------------------------------------------------- expert parallel
+ * No reference counterpart: the reference runs a layer in one process
+ * (src/moe.cpp:122-161). One process per GPU; rank r opens its layer with
+ * experts [begin[r], begin[r+1]) (aero_cuda_moe_open / _open_gguf expert
+ * range) and a step over its T local tokens is
+ *   1. aero_cuda_ep_dispatch: route the T tokens (router + top-k over all
+ *      experts), write the T self rows and the S send rows (one per token and
+ *      remote rank owning at least one of its experts, remote ranks in order,
+ *      tokens in order) with their metadata, counts[r] send rows per rank;
+ *   2. the caller exchanges counts, rows and metadata (NCCL all-to-all) so
+ *      that the rows from other ranks follow the self rows in one buffer;
+ *   3. aero_cuda_ep_expert_block over the R received rows (self rows first;
+ *      they also take the shared expert): out[r] = sum of w * expert(x) over
+ *      the row's slots this rank owns (+ the shared expert);
+ *   4. the caller sends rows [T, R) of that output back (reverse all-to-all,
+ *      landing in send-row order);
+ *   5. aero_cuda_ep_combine: out[t] = self part + the remote parts in rank
+ *      order.
+ * All buffers are device memory, 16-byte aligned; the work is enqueued on the
+ * handle's stream and the calls do not synchronise. Rows are n_embd wide, f32
+ * or f16 (f16 rows take the tcgen05 GEMM path). A metadata row is
+ * aero_cuda_ep_meta_ld(handle) = 2k + 2 int32: k global expert ids (-1: not
+ * owned by the receiver), k weights (f32 bits), the shared gate (f32 bits),
+ * padding. 0 / -1 with the reason in aero_cuda_moe_last_error(handle). */
+#define AERO_EP_ROWS_F32 0
+#define AERO_EP_ROWS_F16 1
+int aero_cuda_ep_meta_ld(void* handle);
+/* rank_expert_begin: host array of n_ranks + 1 ascending expert ids from 0 to
+ * n_expert; this handle must hold [begin[rank], begin[rank+1]). send_cap (rows
+ * of send_rows / send_meta) must be at least T * min(k, n_ranks - 1). counts:
+ * n_ranks + 1 int32 (counts[n_ranks] = S); pos: (T, n_ranks) int32, the send
+ * row of each (token, remote rank) or -1. */
+int aero_cuda_ep_dispatch(void* handle, const float* x, int T, int n_ranks, int rank,
+                          const int32_t* rank_expert_begin, int row_dtype, void* self_rows,
+                          int32_t* self_meta, void* send_rows, int32_t* send_meta, int send_cap,
+                          int32_t* counts, int32_t* pos);
+/* rows (R, n_embd) with metadata (R, meta_ld); the first n_shared rows take the
+ * shared expert with their metadata's gate. out (R, n_embd) f32. */
+int aero_cuda_ep_expert_block(void* handle, const void* rows, int row_dtype, const int32_t* meta,
+                              int R, int n_shared, float* out);
+/* self_out (T, n_embd): rows [0, T) of the expert block's output; back (S,
+ * n_embd): the returned rows in send-row order; out (T, n_embd) f32. */
+int aero_cuda_ep_combine(void* handle, const float* self_out, const float* back, const int32_t* pos,
+                         int T, int n_ranks, int rank, float* out);
+/* Metadata ids received since the last call that named an expert this handle
+ * does not hold (they were skipped). Synchronises the handle's stream. */
+int aero_cuda_ep_bad_ids(void* handle);
 
 /* Run the handle's work on this cudaStream_t (NULL: the handle's own stream). */
 int aero_cuda_moe_set_stream(void* handle, void* stream);

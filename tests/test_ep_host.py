@@ -1,0 +1,129 @@
+"""Expert-parallel host protocol over gloo on CPU (world sizes 2 and 3).
+
+Each rank runs aero_b200.ep.ExpertParallelMoe with the CPU stand-in ops over
+its token shard; the gathered outputs must equal the oracle's single-process
+block over all tokens. Covers uneven expert ranges (8 experts over 3 ranks),
+uneven and empty token shards, f32 and f16 rows, and the split bookkeeping.
+"""
+
+import os
+import socket
+import sys
+
+import numpy as np
+import pytest
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _layer():
+    from aero_b200 import quant as Q
+    from aero_b200 import synth
+
+    spec = synth.LayerSpec(256, 8, 3, 256, 256, Q.DTYPE_Q4_K)
+    return synth.make_layer(spec, 7)
+
+
+def _worker(rank, world, port, shards, row_f16, q):
+    try:
+        sys.path.insert(0, HERE)
+        sys.path.insert(0, os.path.dirname(HERE))
+        import torch
+        import torch.distributed as dist
+
+        from aero_b200 import ep
+        from aero_b200 import synth
+        from ep_cpu_ops import CpuEpOps
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        layer = _layer()
+        begin = ep.expert_ranges(layer.spec.E, world)
+        ops = CpuEpOps(layer, begin[rank], begin[rank + 1])
+        T_all = shards[-1]
+        x = synth.make_x(T_all, layer.spec.d, 3)
+        mine = torch.from_numpy(x[shards[rank]:shards[rank + 1]].copy())
+        m = ep.ExpertParallelMoe(ops, layer.spec.d, layer.spec.E, layer.spec.k, world, rank,
+                                 max_tokens=max(shards[r + 1] - shards[r] for r in range(world)), device="cpu",
+                                 row_f16=row_f16, guard=False)
+        out = m.forward(mine)
+        send, recv = m.last_split
+        assert send[rank] == 0 and recv[rank] == 0
+        # what each rank sends is what the others receive
+        allsend = [None] * world
+        dist.all_gather_object(allsend, send)
+        for r in range(world):
+            assert allsend[r][rank] == recv[r]
+        outs = [None] * world
+        dist.all_gather_object(outs, out.numpy())
+        if rank == 0:
+            q.put(("ok", np.concatenate(outs, 0)))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent
+        import traceback
+
+        q.put(("err", f"rank {rank}: {e}\n{traceback.format_exc()}"))
+
+
+def _run(world, shards, row_f16):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, shards, row_f16, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    msg = q.get(timeout=240)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert msg[0] == "ok", msg[1]
+    return msg[1]
+
+
+def _reference(shards, row_f16):
+    import oracle as O
+    from aero_b200 import synth
+
+    layer = _layer()
+    x = synth.make_x(shards[-1], layer.spec.d, 3)
+    lg = O.router_logits(x, layer.router, layer.router_bias)
+    # f16 rows: the experts see f16-rounded inputs, the router the f32 ones
+    xe = x.astype(np.float16).astype(np.float32) if row_f16 else x
+    return O.moe_block(layer, xe, lg)
+
+
+@pytest.mark.parametrize("world,shards,row_f16", [
+    (2, [0, 19, 37], False),
+    (2, [0, 0, 12], True),     # rank 0 has no tokens this step
+    (3, [0, 9, 20, 26], False),  # 8 experts over 3 ranks: 3, 3, 2
+])
+def test_ep_protocol_matches_single_process(world, shards, row_f16):
+    got = _run(world, shards, row_f16)
+    want = _reference(shards, row_f16)
+    scale = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
+    assert scale > 1e-4
+    # f16 rows: the reference also computes the shared gate from the rounded
+    # rows, the protocol from the f32 ones (a ~1e-4 relative difference)
+    tol = 1e-3 if row_f16 else 1e-4
+    assert float(np.max(np.abs(got - want))) <= tol * scale
+
+
+def test_expert_ranges_and_shards():
+    from aero_b200 import ep
+
+    assert ep.expert_ranges(512, 8) == [64 * i for i in range(9)]
+    assert ep.expert_ranges(8, 3) == [0, 3, 6, 8]
+    assert ep.token_shards(10, 4) == [0, 3, 6, 8, 10]
+    with pytest.raises(ValueError):
+        ep.expert_ranges(4, 5)

@@ -1,0 +1,266 @@
+"""Expert-parallel layer on the GPU.
+
+One GPU: the ranks are threads, each with its own handle holding its expert
+range and its own stream, exchanging through device copies in place of NCCL
+(the kernels and the host protocol are the same as over NCCL). The sharded
+result must match the single-handle layer over all tokens. With two or more
+GPUs, the same over NCCL with one process per GPU.
+"""
+
+import os
+import socket
+import threading
+
+import numpy as np
+import pytest
+
+import oracle as O
+from aero_b200 import ep
+from aero_b200 import native_cuda as nc
+from aero_b200 import quant as Q
+from aero_b200 import synth
+
+pytestmark = pytest.mark.gpu
+PREFILL_TOL = 1e-2
+
+
+def rms(a):
+    return float(np.sqrt(np.mean(np.asarray(a, np.float64) ** 2)))
+
+
+def rel_err(got, want):
+    return float(np.max(np.abs(np.asarray(got, np.float64) - want))) / max(rms(want), 1e-30)
+
+
+class ThreadExchange:
+    """all_to_all_single between threads of one process (device copies)."""
+
+    def __init__(self, world):
+        self.world = world
+        self.board = [None] * world
+        self.bar = threading.Barrier(world, timeout=120)
+
+    def for_rank(self, rank):
+        import torch
+
+        def a2a(out, inp, out_splits, in_splits):
+            n = self.world
+            out_splits = out_splits or [out.shape[0] // n] * n
+            in_splits = in_splits or [inp.shape[0] // n] * n
+            torch.cuda.current_stream().synchronize()
+            self.board[rank] = (inp, in_splits)
+            self.bar.wait()
+            off = 0
+            for src in range(n):
+                sinp, ss = self.board[src]
+                assert ss[rank] == out_splits[src]
+                so = sum(ss[:rank])
+                c = out_splits[src]
+                if c:
+                    out[off:off + c].copy_(sinp[so:so + c])
+                off += c
+            torch.cuda.current_stream().synchronize()
+            self.bar.wait()
+
+        return a2a
+
+
+def _run_threads(layer, x, world, row_f16, gemm_min=None):
+    import torch
+
+    T = x.shape[0]
+    shards = ep.token_shards(T, world)
+    begin = ep.expert_ranges(layer.spec.E, world)
+    handles = [synth.open_layer(layer, expert_range=(begin[r], begin[r + 1])) for r in range(world)]
+    if gemm_min is not None:
+        for h in handles:
+            h.set_gemm_min_tokens(gemm_min)
+    xg = torch.from_numpy(x).cuda()
+    xch = ThreadExchange(world)
+    outs, errs = [None] * world, []
+
+    def work(r):
+        try:
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                m = ep.ExpertParallelMoe(ep.CudaEpOps(handles[r]), layer.spec.d, layer.spec.E, layer.spec.k, world, r,
+                                         max_tokens=max(shards[i + 1] - shards[i] for i in range(world)),
+                                         row_f16=row_f16, exchange=xch.for_rank(r))
+                mine = xg[shards[r]:shards[r + 1]]
+                o = m.forward(mine)
+                o2 = m.forward(mine)  # a second step reuses the buffers
+                s.synchronize()
+                outs[r] = (o.cpu().numpy(), o2.cpu().numpy())
+                m.close()
+        except Exception as e:  # surfaced below
+            errs.append(f"rank {r}: {e!r}")
+            xch.bar.abort()
+
+    th = [threading.Thread(target=work, args=(r,)) for r in range(world)]
+    for t in th:
+        t.start()
+    for t in th:
+        t.join(timeout=300)
+    try:
+        assert not errs, errs
+        for h in handles:
+            assert ep.CudaEpOps(h).lib.aero_cuda_ep_bad_ids(h.handle) == 0
+    finally:
+        for h in handles:
+            h.close()
+    a = np.concatenate([o[0] for o in outs], 0)
+    b = np.concatenate([o[1] for o in outs], 0)
+    return a, b
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_ep_prefill_matches_single_gpu(world):
+    """c5-shaped layer (512 experts, top-10, shared expert, Q4_K), 2048 tokens, f16 rows."""
+    nc.require_gpu()
+    wl = synth.CONFIGS["c5"]
+    layer = synth.make_layer(wl.spec, 0, device_gen=True)
+    x = synth.make_x(2048, wl.spec.d, 4)
+    L = synth.open_layer(layer)
+    try:
+        L.set_gemm_min_tokens(1)
+        single = L.forward(x)
+        lg = L.router_logits(x)
+    finally:
+        L.close()
+    a, b = _run_threads(layer, x, world, row_f16=True)
+    assert np.array_equal(a, b), "second step differs"
+    # same f16 expert products, partial sums regrouped by rank
+    assert rel_err(a, single) <= 1e-4
+    sel = np.sort(np.random.default_rng(9).choice(x.shape[0], 128, replace=False))
+    ref = O.moe_block(layer, x[sel], lg[sel], nthreads=os.cpu_count() or 1)
+    assert rel_err(a[sel], ref) <= PREFILL_TOL
+
+
+def test_ep_gemv_rows_uneven_experts():
+    """Q8_0 layer, 24 experts over 5 ranks (5,5,5,5,4), f32 rows on the GEMV path."""
+    nc.require_gpu()
+    spec = synth.LayerSpec(1024, 24, 4, 256, 256, Q.DTYPE_Q8_0)
+    layer = synth.make_layer(spec, 33)
+    x = synth.make_x(45, spec.d, 33)
+    L = synth.open_layer(layer)
+    try:
+        L.set_gemm_min_tokens(1 << 20)
+        lg = L.router_logits(x)
+    finally:
+        L.close()
+    a, _ = _run_threads(layer, x, 5, row_f16=False, gemm_min=1 << 20)
+    ref = O.moe_block(layer, x, lg)
+    assert rms(ref) > 1e-3
+    assert rel_err(a, ref) <= 2e-3
+
+
+def test_ep_refusals():
+    nc.require_gpu()
+    import torch
+
+    spec = synth.LayerSpec(1024, 24, 4, 256, 0, Q.DTYPE_Q8_0)
+    layer = synth.make_layer(spec, 34)
+    L = synth.open_layer(layer, expert_range=(0, 12))
+    lib = nc.lib()
+    try:
+        x = torch.zeros((4, 1024), device="cuda")
+        buf = torch.zeros((64, 1024), device="cuda")
+        meta = torch.zeros((64, 10), dtype=torch.int32, device="cuda")
+        cnt = torch.zeros(3, dtype=torch.int32, device="cuda")
+        pos = torch.zeros((4, 2), dtype=torch.int32, device="cuda")
+        tab = (nc.c_int32 * 3)(0, 12, 24)
+
+        def disp(rank, table, cap=64):
+            return lib.aero_cuda_ep_dispatch(L.handle, x.data_ptr(), 4, 2, rank, table, 0, buf.data_ptr(),
+                                             meta.data_ptr(), buf.data_ptr(), meta.data_ptr(), cap, cnt.data_ptr(),
+                                             pos.data_ptr())
+
+        assert disp(0, tab) == 0
+        assert disp(1, tab) == -1 and "this handle holds [0, 12)" in nc.last_error(L.handle)
+        assert disp(0, (nc.c_int32 * 3)(0, 12, 20)) == -1 and "from 0 to 24" in nc.last_error(L.handle)
+        assert disp(0, tab, cap=3) == -1 and "send_cap" in nc.last_error(L.handle)
+        # a forward on a ranged handle is refused: it holds only some experts
+        with pytest.raises(Exception):
+            L.forward(np.zeros((2, 1024), np.float32))
+        # ids this rank does not own are skipped and counted
+        bad = torch.full((2, 10), -1, dtype=torch.int32, device="cuda")
+        bad[0, 0] = 20
+        out = torch.empty((2, 1024), device="cuda")
+        assert lib.aero_cuda_ep_expert_block(L.handle, buf.data_ptr(), 0, bad.data_ptr(), 2, 0, out.data_ptr()) == 0
+        assert lib.aero_cuda_ep_bad_ids(L.handle) == 1
+        assert lib.aero_cuda_ep_bad_ids(L.handle) == 0
+        assert float(out.abs().max()) == 0.0
+    finally:
+        L.close()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _nccl_worker(rank, world, port, q):
+    try:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        wl = synth.CONFIGS["c5"]
+        layer = synth.make_layer(wl.spec, 0)
+        x = synth.make_x(1024, wl.spec.d, 4)
+        shards = ep.token_shards(1024, world)
+        begin = ep.expert_ranges(wl.spec.E, world)
+        h = synth.open_layer(layer, device=rank, expert_range=(begin[rank], begin[rank + 1]))
+        m = ep.ExpertParallelMoe(ep.CudaEpOps(h), wl.spec.d, wl.spec.E, wl.spec.k, world, rank,
+                                 max_tokens=shards[1] - shards[0] + 1, device=f"cuda:{rank}")
+        o = m.forward(torch.from_numpy(x[shards[rank]:shards[rank + 1]]).cuda())
+        outs = [torch.empty((shards[r + 1] - shards[r], wl.spec.d), device=f"cuda:{rank}") for r in range(world)]
+        dist.all_gather(outs, o)
+        if rank == 0:
+            q.put(("ok", torch.cat(outs).cpu().numpy()))
+        dist.barrier()
+        m.close()
+        h.close()
+        dist.destroy_process_group()
+    except Exception as e:
+        import traceback
+
+        q.put(("err", f"rank {rank}: {e}\n{traceback.format_exc()}"))
+
+
+def test_ep_nccl_two_gpus():
+    import torch
+    import torch.multiprocessing as mp
+
+    nc.require_gpu()
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_nccl_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    msg = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    assert msg[0] == "ok", msg[1]
+    wl = synth.CONFIGS["c5"]
+    layer = synth.make_layer(wl.spec, 0)
+    x = synth.make_x(1024, wl.spec.d, 4)
+    L = synth.open_layer(layer)
+    try:
+        L.set_gemm_min_tokens(1)
+        single = L.forward(x)
+    finally:
+        L.close()
+    assert rel_err(msg[1], single) <= 1e-4
