@@ -131,9 +131,13 @@ class ExpertParallelMoe:
         self.recv_counts = torch.zeros(world, dtype=torch.int32, device=dev)
         self.pos = torch.empty((max(1, self.max_tokens), world), dtype=torch.int32, device=dev)
         self._reserved = 0
+        self.stream = None
         if self.device.type == "cuda":
-            # one stream for the library's kernels and the collectives' ordering
-            ops.set_stream(torch.cuda.current_stream(self.device))
+            # the library's kernels and the collectives run on one side stream,
+            # ordered after the caller's stream at entry and before it at exit
+            # (a handle given the legacy default stream would use its own)
+            self.stream = torch.cuda.Stream(device=self.device)
+            ops.set_stream(self.stream)
         if guard and self.device.type == "cuda":
             # the exchange buffers are torch allocations; charge them to the
             # library's memory guard so its accounting covers them
@@ -174,6 +178,22 @@ class ExpertParallelMoe:
         if T > self.max_tokens:
             raise ValueError(f"{T} tokens on rank {self.rank} > max_tokens {self.max_tokens}")
         x = x.contiguous().float()
+        out = torch.empty((T, self.d), dtype=torch.float32, device=self.device)
+        if self.stream is None:
+            self._step(x, out)
+            return out
+        caller = torch.cuda.current_stream(self.device)
+        self.stream.wait_stream(caller)
+        with torch.cuda.stream(self.stream):
+            self._step(x, out)
+        caller.wait_stream(self.stream)
+        x.record_stream(self.stream)
+        out.record_stream(self.stream)
+        return out
+
+    def _step(self, x, out):
+        torch = self.torch
+        T = int(x.shape[0])
         n, r = self.world, self.rank
         self.ops.dispatch(x, T, n, r, self.begin, self.row_dtype, self.recv_rows, self.recv_meta, self.send_rows,
                           self.send_meta, self.counts, self.pos)
@@ -188,9 +208,7 @@ class ExpertParallelMoe:
         self._a2a(self.recv_meta[T:T + Rr], self.send_meta[:S], recv, send)
         self.ops.expert_block(self.recv_rows, self.row_dtype, self.recv_meta, T + Rr, T, self.y)
         self._a2a(self.back[:S], self.y[T:T + Rr], send, recv)
-        out = torch.empty((T, self.d), dtype=torch.float32, device=self.device)
         self.ops.combine(self.y, self.back, self.pos, T, n, r, out)
-        return out
 
     __call__ = forward
 

@@ -212,7 +212,7 @@ def _nccl_worker(rank, world, port, q):
         dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60))
         wl = synth.CONFIGS["c5"]
-        layer = synth.make_layer(wl.spec, 0)
+        layer = synth.make_layer(wl.spec, 0, device_gen=True)
         x = synth.make_x(1024, wl.spec.d, 4)
         shards = ep.token_shards(1024, world)
         begin = ep.expert_ranges(wl.spec.E, world)
@@ -255,7 +255,7 @@ def test_ep_nccl_two_gpus():
             p.kill()
     assert msg[0] == "ok", msg[1]
     wl = synth.CONFIGS["c5"]
-    layer = synth.make_layer(wl.spec, 0)
+    layer = synth.make_layer(wl.spec, 0, device_gen=True)
     x = synth.make_x(1024, wl.spec.d, 4)
     L = synth.open_layer(layer)
     try:
