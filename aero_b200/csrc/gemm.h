@@ -39,6 +39,11 @@ struct GemmBuffers {
     CUtensorMap tmap_x[kGemmNT / 16], tmap_act[kGemmNT / 16];  // box heights 16, 32, ..., kGemmNT
 };
 
+// A 2-D tiled TMA descriptor over a row-major matrix (rows x cols elements of
+// elem_bytes, row stride ld elements): box box_rows x box_cols, no OOB fill.
+bool encode_tmap_2d(CUtensorMap* m, CUtensorMapDataType dt, int elem_bytes, const void* base, uint64_t rows,
+                    uint64_t cols, uint64_t ld, uint32_t box_rows, uint32_t box_cols, CUtensorMapSwizzle swz);
+
 // Carve the workspace and encode the TMA descriptors for it.
 bool gemm_setup(void* ws, size_t ws_bytes, int dp, int act_ld, int P_cap, int T_cap, int max_tiles, GemmBuffers* b,
                 std::string* why);
@@ -80,5 +85,22 @@ cudaError_t launch_prefill_gemm(const PrefillArgs& a, GemmBuffers& b, const Gemm
 cudaError_t launch_combine_h(const __half* y, const int32_t* inv, const float* w, const float* sgate,
                              const int32_t* idx, int E_real, int T, int Tsh, int k, int d, int has_shared,
                              float* out, cudaStream_t s);
+
+// Router projection on the tensor cores (router_tc.cu): f32-accurate logits
+// from three TF32 products of split operands, for prefill batches.
+constexpr int kRtNMax = 128;
+struct RouterTcMaps {
+    CUtensorMap hi, lo;  // W_hi / W_lo tiles of N (<= kRtNMax) rows x 32 values
+    int N, n_rows, dp;
+};
+// Rows per CTA column tile for n_rows router rows; 0 when the shape is not supported.
+int router_tc_tile_rows(int n_rows);
+// Split W (n_rows, dp) f32 into w_hi / w_lo (same shape, device) and encode their maps.
+cudaError_t router_tc_prepare(const float* W, int n_rows, int dp, float* w_hi, float* w_lo, RouterTcMaps* maps,
+                              cudaStream_t s);
+// logits[t][e] = x_t . W[e] (+ bias[e] for e < n_bias) for t < T, e < n_rows;
+// with gate_row, logits[t][n_rows] = x_t . gate_row (f32, K in order). ld % 4 == 0.
+cudaError_t launch_router_tc(const RouterTcMaps& maps, const float* x, int T, const float* bias, int n_bias,
+                             const float* gate_row, float* logits, int ld, int32_t* err, cudaStream_t s);
 
 }  // namespace aero

@@ -49,7 +49,7 @@ struct Scratch {
     void* base = nullptr;
     size_t bytes = 0;
     float *x_stage, *out_stage, *lg_stage, *logits, *w, *sgate, *xsum16, *act, *asum16, *y;
-    int32_t *idx, *offsets, *perm, *inv, *act_e, *act_off, *n_active, *ep_bad;
+    int32_t *idx, *offsets, *perm, *inv, *act_e, *act_off, *n_active, *ep_bad, *tc_err;
     void* dwork;
     void* gemm_ws;
     size_t gemm_ws_bytes = 0;
@@ -66,6 +66,11 @@ struct Handle {
     QMat gate{}, up{}, down{}, sg{}, su{}, sd{};
     float* router_ext = nullptr;  // (E + 1, dp): row E = shared gate input (or zeros)
     float* router_bias = nullptr;
+    // tensor-core router for prefill batches: W split into TF32 hi / lo parts
+    RouterTcMaps rtc{};
+    bool rtc_ok = false;          // the layer's shape allows it
+    bool rtc_enabled = true;      // AERO_CUDA_OPT_ROUTER_TC
+    int lg_ld = 0;                // row stride of the logits scratch: E + 1 rounded up to 4
     std::vector<Alloc> allocs;
     Scratch sc;
     std::string err;
@@ -232,7 +237,7 @@ bool ensure_scratch(Handle& h, int T) {
     };
     const size_t o_x = take((size_t)cap * h.dp * 4), o_out = take((size_t)cap * h.dp * 4);
     const size_t o_lgs = take((size_t)cap * h.E * 4);
-    const size_t o_lg = take((size_t)cap * (h.E + 1) * 4), o_w = take((size_t)P * 4), o_sg = take((size_t)cap * 4);
+    const size_t o_lg = take((size_t)cap * h.lg_ld * 4), o_w = take((size_t)P * 4), o_sg = take((size_t)cap * 4);
     const size_t o_xs = take((size_t)cap * (h.dp / 16) * 4);
     // the f32 GEMV buffers only need to cover calls that take the GEMV path
     const int64_t gemv_T = h.gemm_ok ? std::min<int64_t>(cap, h.gemm_min_tokens) : cap;
@@ -242,7 +247,7 @@ bool ensure_scratch(Handle& h, int T) {
     const size_t o_idx = take((size_t)P * 4), o_off = take((size_t)(h.E + 2) * 4), o_perm = take((size_t)P * 4);
     const size_t o_inv = take((size_t)P * 4), o_ae = take((size_t)h.E * 4), o_ao = take((size_t)(h.E + 1) * 4);
     const size_t o_na = take(4), o_dw = take(dispatch_work_bytes((int)P, h.E + 1));
-    const size_t o_bad = take(4);
+    const size_t o_bad = take(4), o_tce = take(4);
     const int max_tiles = gemm_max_tiles((int)P, cap, h.E, h.has_shared);
     const size_t gws = h.gemm_ok ? gemm_workspace_bytes(h.dp, h.act_ld, (int)P, cap, max_tiles) : 256;
     const size_t o_gw = take(gws);
@@ -279,6 +284,7 @@ bool ensure_scratch(Handle& h, int T) {
     s.act_off = (int32_t*)(b + o_ao);
     s.n_active = (int32_t*)(b + o_na);
     s.ep_bad = (int32_t*)(b + o_bad);
+    s.tc_err = (int32_t*)(b + o_tce);
     s.dwork = b + o_dw;
     s.gemm_ws = b + o_gw;
     s.gemm_ws_bytes = gws;
@@ -293,19 +299,34 @@ bool ensure_scratch(Handle& h, int T) {
     return h.cuda_ok(cudaMemsetAsync(base, 0, off, h.stream), "scratch clear");
 }
 
+// Router logits (+ the shared-gate column E when with_gate and the layer has a
+// shared expert) for T rows of x into s.logits (row stride lg_ld): the tensor
+// cores for batches of at least kRouterTcMinTokens, SIMT kernels below that.
+constexpr int kRouterTcMinTokens = 128;
+bool router_logits_dev(Handle& h, const float* x, int T, bool with_gate) {
+    Scratch& s = h.sc;
+    const bool gate = with_gate && h.has_shared;
+    if (h.rtc_ok && h.rtc_enabled && T >= kRouterTcMinTokens) {
+        return h.cuda_ok(launch_router_tc(h.rtc, x, T, h.router_bias, h.E, gate ? h.router_ext + (size_t)h.E * h.dp : nullptr,
+                                          s.logits, h.lg_ld, s.tc_err, h.stream),
+                         "router (tensor cores)");
+    }
+    return h.cuda_ok(launch_router(x, T, h.dp, h.router_ext, 0, h.E + (gate ? 1 : 0), h.router_bias, h.E, s.logits,
+                                   h.lg_ld, h.stream),
+                     "router");
+}
+
 // Router projection + top-k for T tokens of x (T, dp): s.idx, s.w, s.sgate,
 // s.xsum16. When logits_in is non-null it holds (T, E) caller logits on the
 // device (row stride E).
 bool route_stage(Handle& h, const float* x, int T, const float* logits_in) {
     Scratch& s = h.sc;
     cudaStream_t st = h.stream;
-    const int ld = h.E + 1;
+    const int ld = h.lg_ld;
     h.mark(0);
     if (!logits_in) {
         if (!h.has_router) return h.fail("this layer has no router weights; use the ffn_block form with logits");
-        if (!h.cuda_ok(launch_router(x, T, h.dp, h.router_ext, 0, h.E + h.has_shared, h.router_bias, h.E, s.logits, ld, st),
-                       "router"))
-            return false;
+        if (!router_logits_dev(h, x, T, true)) return false;
     } else {
         if (!h.cuda_ok(cudaMemcpy2DAsync(s.logits, (size_t)ld * 4, logits_in, (size_t)h.E * 4, (size_t)h.E * 4, (size_t)T,
                                          cudaMemcpyDeviceToDevice, st),
@@ -450,6 +471,15 @@ bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* 
 // The prefill kernels record a non-zero code when one of their bounded waits
 // expired; report it (and clear it) at the next synchronisation point.
 bool check_pipeline(Handle& h) {
+    if (h.sc.base && h.rtc_ok) {
+        int32_t code = 0;
+        if (cudaMemcpy(&code, h.sc.tc_err, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+            return h.cuda_ok(cudaGetLastError(), "error flag");
+        if (code != 0) {
+            cudaMemset(h.sc.tc_err, 0, 4);
+            return h.fail("router pipeline wait expired (code %d); the call's output is invalid", code);
+        }
+    }
     if (!h.gb_ready) return true;
     int32_t code = 0;
     if (cudaMemcpy(&code, h.gb.err, 4, cudaMemcpyDeviceToHost) != cudaSuccess) return h.cuda_ok(cudaGetLastError(), "error flag");
@@ -594,9 +624,11 @@ Handle* open_desc(const aero_cuda_moe_desc* d, std::string* why) {
                         "router bias"))
             return bad("");
     }
+    h->lg_ld = (int)round_up(h->E + 1, 4);
+    const bool want_rtc = h->has_router && router_tc_tile_rows(h->E) > 0 && h->dp % 32 == 0;
     // plan the whole upload before allocating (admit_plan, src/memory_guard.cpp:192-213)
     {
-        size_t plan = 0;
+        size_t plan = want_rtc ? 2 * (size_t)h->E * h->dp * 4 : 0;
         auto fam = [&](int dt, int rows, int cols, int ne_) {
             const int pr = dt == AERO_DT_F32 ? (int)round_up(rows, 16) : rows;
             const int pc = dt == AERO_DT_F32 ? (int)round_up(cols, 16) : cols;
@@ -607,6 +639,14 @@ Handle* open_desc(const aero_cuda_moe_desc* d, std::string* why) {
         if (h->has_shared) plan += 2 * fam(h->sh_dtype, h->Fs, h->d, 1) + fam(h->sh_dtype, h->d, h->Fs, 1);
         char why2[256];
         if (!aero_cuda_guard_admit_plan(plan, why2, sizeof(why2))) return bad(std::string("load refused: ") + why2);
+    }
+    if (want_rtc) {
+        float* w_hi = (float*)h->dalloc((size_t)h->E * h->dp * 4, kWeightsResident, "router split (hi)");
+        float* w_lo = w_hi ? (float*)h->dalloc((size_t)h->E * h->dp * 4, kWeightsResident, "router split (lo)") : nullptr;
+        if (!w_lo) return bad("");
+        if (!h->cuda_ok(router_tc_prepare(h->router_ext, h->E, h->dp, w_hi, w_lo, &h->rtc, h->stream), "router split"))
+            return bad("");
+        h->rtc_ok = true;
     }
     if (!upload_family(*h, d->gate_exps, h->E, h->e_begin, h->e_end, h->F, h->d, h->Fp, h->dp, h->gate, "ffn_gate_exps"))
         return bad("");
@@ -707,11 +747,8 @@ int aero_cuda_moe_router_logits(void* handle, const float* x, int T, float* logi
                                       xd ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, h->stream),
                     "input copy"))
         return -1;
-    if (!h->cuda_ok(aero::launch_router(s.x_stage, T, h->dp, h->router_ext, 0, h->E, h->router_bias, h->E, s.logits, h->E + 1,
-                                        h->stream),
-                    "router"))
-        return -1;
-    if (!h->cuda_ok(cudaMemcpy2DAsync(logits, (size_t)h->E * 4, s.logits, (size_t)(h->E + 1) * 4, (size_t)h->E * 4, (size_t)T,
+    if (!aero::router_logits_dev(*h, s.x_stage, T, false)) return -1;
+    if (!h->cuda_ok(cudaMemcpy2DAsync(logits, (size_t)h->E * 4, s.logits, (size_t)h->lg_ld * 4, (size_t)h->E * 4, (size_t)T,
                                       ld ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, h->stream),
                     "logits copy"))
         return -1;
@@ -946,6 +983,11 @@ int aero_cuda_moe_set_option(void* handle, int option, int64_t value) {
         if (value < 1) return -1;
         h->gemm_min_tokens = (int)std::min<int64_t>(value, 1 << 30);
         h->sc.cap_T = 0;  // re-plan scratch on the next call
+        return 0;
+    }
+    if (option == AERO_CUDA_OPT_ROUTER_TC) {
+        if (value != 0 && value != 1) return -1;
+        h->rtc_enabled = value != 0;
         return 0;
     }
     h->fail("unknown option %d", option);

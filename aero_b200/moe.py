@@ -223,6 +223,11 @@ class CudaMoeLayer:
         if self._lib.aero_cuda_moe_set_option(self.handle, nc.OPT_GEMM_MIN_TOKENS, int(n)) != 0:
             raise ValueError(nc.last_error(self.handle))
 
+    def set_router_tc(self, on: bool) -> None:
+        """Project the router of >= 128-token calls on the tensor cores (default) or on the SIMT kernels."""
+        if self._lib.aero_cuda_moe_set_option(self.handle, nc.OPT_ROUTER_TC, 1 if on else 0) != 0:
+            raise ValueError(nc.last_error(self.handle))
+
     def set_stream(self, stream) -> None:
         """Run on a cudaStream_t (int) or a torch.cuda.Stream; None restores the handle's own."""
         s = getattr(stream, "cuda_stream", stream)

@@ -30,6 +30,7 @@ DTYPE_Q4_K = 12
 MEM_WEIGHTS_RESIDENT, MEM_WEIGHTS_CACHE, MEM_KV_CACHE, MEM_SCRATCH, MEM_RUNTIME = range(5)
 
 OPT_GEMM_MIN_TOKENS = 1
+OPT_ROUTER_TC = 2
 
 
 class CudaMoeUnavailable(RuntimeError):

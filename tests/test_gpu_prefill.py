@@ -87,3 +87,34 @@ def test_config5_subset(key):
     assert rel_err(out[sel], ref) <= PREFILL_TOL
     # router on the device gives the same logits, so the same result
     assert np.array_equal(out, out2)
+
+
+@pytest.mark.parametrize("key,T", [("c5", 1000), ("c2", 300)])
+def test_tensor_core_router_f32_accuracy(key, T):
+    """Router logits of >= 128-token calls come from three TF32 products of split
+    operands; they must be as close to the f64 logits as the f32 SIMT kernel's
+    (c2 carries a router bias; 1000 and 300 leave a partial 128-token tile)."""
+    wl = synth.CONFIGS[key]
+    layer = synth.make_layer(wl.spec, 3, device_gen=True)
+    x = synth.make_x(T, wl.spec.d, 3)
+    if wl.zipf_s:
+        synth.attach_zipf(layer, x, wl.zipf_s, 3)
+    L = synth.open_layer(layer)
+    try:
+        tc = L.router_logits(x)
+        L.set_router_tc(False)
+        simt = L.router_logits(x)
+        L.set_router_tc(True)
+        again = L.router_logits(x)
+    finally:
+        L.close()
+    ref64 = O.router_logits(x, layer.router, layer.router_bias, f64=True)
+    e_tc = float(np.max(np.abs(tc.astype(np.float64) - ref64)))
+    e_simt = float(np.max(np.abs(simt.astype(np.float64) - ref64)))
+    assert np.array_equal(tc, again)
+    assert e_simt < 1e-5
+    assert e_tc <= max(4 * e_simt, 1e-6), (e_tc, e_simt)
+    # top-k agrees with the f64 logits' except at near-ties
+    idx_tc, _ = O.route(tc, wl.spec.k)
+    idx_64, _ = O.route(ref64.astype(np.float32), wl.spec.k)
+    assert np.mean(np.all(idx_tc == idx_64, axis=1)) > 0.99
