@@ -98,6 +98,20 @@ __device__ __forceinline__ void q4k_sc_m(const uint8_t* q, int j, int& sc, int& 
     }
 }
 
+// The same, with the 12 packed scale bytes as three little-endian words (bytes
+// 0-3, 4-7, 8-11): register-only, no byte array to index.
+__device__ __forceinline__ void q4k_sc_m_words(uint32_t w0, uint32_t w1, uint32_t w2, int j, int& sc, int& m) {
+    const int sh = 8 * (j & 3);
+    const int b0 = (int)((w0 >> sh) & 0xFFu), b1 = (int)((w1 >> sh) & 0xFFu), b2 = (int)((w2 >> sh) & 0xFFu);
+    if (j < 4) {
+        sc = b0 & 63;  // q[j]
+        m = b1 & 63;   // q[j + 4]
+    } else {
+        sc = (b2 & 15) | ((b0 >> 6) << 4);  // q[j + 4], q[j - 4]
+        m = (b2 >> 4) | ((b1 >> 6) << 4);   // q[j + 4], q[j]
+    }
+}
+
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 

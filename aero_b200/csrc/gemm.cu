@@ -4,8 +4,10 @@
 // expert (all tokens), two grouped GEMMs in "weights x tokens" orientation: the
 // 128-row MMA M extent runs over weight rows and the ragged token count is the
 // N extent (16..192 in steps of 16), so nothing is padded to 128 tokens.
-//   gate/up:  D_g = Wg[m0:m0+128, :] . X^T,  D_u = Wu[...] . X^T   (K = d)
-//             epilogue: act = silu(D_g) * D_u  -> f16 act rows
+//   gate/up:  an item is 64 rows of gate and the same 64 rows of up, interleaved
+//             (M row 2i = gate row i, 2i+1 = up row i): D = [Wg; Wu] . X^T (K = d)
+//             epilogue: act = silu(D_g) * D_u, the partner rows meeting by a lane
+//             shuffle -> f16 act rows
 //   down:     D = Wd[n0:n0+128, :] . act^T                        (K = F)
 //             epilogue: f16 y rows
 // Operands are f16 (kind::f16, fp32 accumulate). bf16 operands were measured
@@ -13,7 +15,7 @@
 // RMS in max-abs error on Q4_K layers, above the 1% bar; f16 rounds 8x finer at
 // the same tensor-core rate.
 //
-// Persistent kernel: one CTA per SM walks work items (tile, 128-row block)
+// Persistent kernel: one CTA per SM walks work items (tile, row block)
 // blockIdx.x, blockIdx.x + gridDim.x, ... Warp roles (23 warps):
 //   warp 0      TMA producer of the raw quant blocks of the item's 128 weight
 //               rows (2-D tensor maps over the expert-major qs and header
@@ -23,16 +25,17 @@
 //               anywhere)
 //   warp 1      one thread issues tcgen05.mma with the weight operand A in TMEM
 //               and the token operand B in shared memory, fp32 accumulators in
-//               TMEM, tcgen05.commit to the ring barriers
+//               TMEM (two, so an item's epilogue overlaps the next main loop),
+//               tcgen05.commit to the ring barriers
 //   warps 2-17  dequantise from shared memory with packed half2 arithmetic
 //               (Q4_K: s*q - m per 32-value sub-block; Q8_0: d*q) and write A
 //               into TMEM with tcgen05.st (row m of A = TMEM lane m, two f16 per
-//               column); the block headers ride in the same TMA stages
+//               column; four A stages of one 64-value K step); the block headers
+//               ride in the same TMA stages
 //   warps 18-21 epilogue: tcgen05.ld of the accumulators 16 columns at a time,
-//               SwiGLU, f16 results staged in shared memory for 16-byte stores
-// The weight tile never passes through shared memory, which halves the shared
-// memory traffic per K step. The down GEMM double-buffers its accumulators so
-// its epilogue overlaps the next item's main loop.
+//               f16 results staged in shared memory for 16-byte stores
+// The weight tile never passes through shared memory as f16, which halves the
+// shared memory traffic per K step.
 // Every wait is bounded by %globaltimer (2 s): on expiry the CTA records an
 // error code (read by the host at its next synchronisation), drains its own
 // copies and MMAs, frees TMEM and exits.
@@ -57,13 +60,16 @@ constexpr int kDeqWarps = 16;
 constexpr int kEpiWarp0 = 2 + kDeqWarps;   // warps 18-21
 constexpr int kTokWarp = kEpiWarp0 + 4;    // warp 22
 constexpr int kBMaps = kGemmNT / 16;  // token-operand maps, box heights 16, 32, ..., 192
-constexpr int kBStages = 4;
+constexpr int kStages = 4;                            // K-step stages (A in TMEM, B in shared memory)
+constexpr int kBStages = kStages;
 constexpr uint32_t kBStageBytes = kGemmNT * kBK * 2;  // 24 KiB: up to 192 token rows x 128 B
 constexpr uint32_t kRawRing = 96 * 1024;
 // TMEM columns
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kAccStride = kGemmNT;     // 192 columns per accumulator
-constexpr uint32_t kAColBase = 2 * kGemmNT;  // 384: two A stages of 64 columns (gate/up) or 32 (down)
+constexpr uint32_t kAccStride = kGemmNT;     // 192 columns per accumulator, two accumulators
+constexpr int kAStages = kStages;            // A stages of one 64-value K step:
+constexpr uint32_t kAStageCols = 32;         //   128 rows x 64 f16 = 32 columns each
+constexpr uint32_t kAColBase = 2 * kGemmNT;  // 384: the A stages fill columns 384-511
 
 enum : int { kErrRawFull = 1, kErrBFull = 2, kErrEmpty = 3, kErrAcc = 4, kErrAFull = 5, kErrAEmpty = 6 };
 
@@ -73,7 +79,7 @@ struct GemmParams {
     const GemmTile* tiles;
     const int32_t* n_tiles;
     int K, Ks;            // reduction length for routed / shared items
-    int MT, MTs, MTmax;   // 128-row blocks for routed / shared
+    int MT, MTs, MTmax;   // row blocks (items) per tile for routed / shared
     int e_begin;          // first expert held by the planes (expert parallelism)
     __half* out;
     int out_ld;
@@ -117,14 +123,23 @@ struct GemmMaps {
 template <int DT, bool GATEUP>
 struct Cfg {
     static constexpr int kRawRowBytes = DT == AERO_DT_Q4_K ? kRawK / 2 : kRawK;  // 64 or 128
-    static constexpr int kMats = GATEUP ? 2 : 1;
-    static constexpr uint32_t kQsBytes = (uint32_t)kMats * kTileM * kRawRowBytes;
-    static constexpr uint32_t kMetaBytes = (uint32_t)kMats * kTileM * 16;  // a 16-byte header slice per row
+    // 128 weight rows per raw stage either way: gate/up items take 64 rows of
+    // each matrix, down items 128 rows
+    static constexpr uint32_t kQsBytes = (uint32_t)kTileM * kRawRowBytes;
+    static constexpr uint32_t kMetaBytes = (uint32_t)kTileM * 16;  // a 16-byte header slice per row
     static constexpr uint32_t kRawStageBytes = kQsBytes + kMetaBytes;
     static constexpr int kRawStages = (int)(kRawRing / kRawStageBytes);
-    static constexpr int kAcc = GATEUP ? 1 : 2;  // accumulator buffers
+    static constexpr int kRowsPerMat = GATEUP ? kTileM / 2 : kTileM;  // weight rows of one matrix per item
     static constexpr size_t kSmem = kRawRing + (size_t)kBStages * kBStageBytes + 1024 + 512 + 4 * 1024;
 };
+
+// Values of a K step are written to TMEM in the order 0, 2, 1, 3, 4, 6, 5, 7,
+// ... (the middle two of every four swapped): a 32-bit word of 4 quant bytes
+// then becomes two f16 pairs (bytes 0, 2) and (bytes 1, 3) with one shift and
+// two masks. The token operand is stored with the same order (gather_kernel,
+// and the gate/up epilogue for the down GEMM's operand), so the products are
+// unchanged.
+__device__ __forceinline__ int kperm(int k) { return (k & ~3) | ((k & 1) << 1) | ((k >> 1) & 1); }
 
 template <int DT, bool GATEUP>
 __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_constant__ GemmMaps tm, GemmParams p) {
@@ -138,19 +153,19 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
     uint8_t* b_ring = smem + kRawRing;  // kBStages x kBStageBytes (1024-aligned)
     uint64_t* bars = reinterpret_cast<uint64_t*>(b_ring + kBStages * kBStageBytes);
     const uint32_t bar0 = smem_u32(bars);
-    // barrier table: raw_full[kRS], raw_empty[kRS], b_full[4], b_empty[4], a_full[2], a_empty[2],
-    // acc_full[2], acc_empty[2], drain
+    // barrier table: raw_full[kRS], raw_empty[kRS], full[kStages], empty[kStages], acc_full[2],
+    // acc_empty[2], drain. A K step's A stage (TMEM) and B stage (shared memory) share one
+    // index and one pair of barriers: full completes when the 16 dequant warps have
+    // arrived and the token copy has landed, empty when the step's MMAs have finished.
     auto raw_full = [&](int s) { return bar0 + 8u * s; };
     auto raw_empty = [&](int s) { return bar0 + 8u * (kRS + s); };
-    auto b_full = [&](int s) { return bar0 + 8u * (2 * kRS + s); };
-    auto b_empty = [&](int s) { return bar0 + 8u * (2 * kRS + kBStages + s); };
-    auto a_full = [&](int s) { return bar0 + 8u * (2 * kRS + 2 * kBStages + s); };
-    auto a_empty = [&](int s) { return bar0 + 8u * (2 * kRS + 2 * kBStages + 2 + s); };
-    auto acc_full = [&](int s) { return bar0 + 8u * (2 * kRS + 2 * kBStages + 4 + s); };
-    auto acc_empty = [&](int s) { return bar0 + 8u * (2 * kRS + 2 * kBStages + 6 + s); };
-    const uint32_t drain_bar = bar0 + 8u * (2 * kRS + 2 * kBStages + 8);
-    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * kRS + 2 * kBStages + 9);
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kRS + 2 * kBStages + 10);
+    auto full = [&](int s) { return bar0 + 8u * (2 * kRS + s); };
+    auto empty = [&](int s) { return bar0 + 8u * (2 * kRS + kStages + s); };
+    auto acc_full = [&](int s) { return bar0 + 8u * (2 * kRS + 2 * kStages + s); };
+    auto acc_empty = [&](int s) { return bar0 + 8u * (2 * kRS + 2 * kStages + 2 + s); };
+    const uint32_t drain_bar = bar0 + 8u * (2 * kRS + 2 * kStages + 4);
+    volatile int* abort_flag = reinterpret_cast<volatile int*>(bars + 2 * kRS + 2 * kStages + 5);
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kRS + 2 * kStages + 6);
     uint8_t* epi_smem = b_ring + kBStages * kBStageBytes + 512;  // 4 warps x 1 KiB output staging
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -159,13 +174,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
             mbar_init(raw_full(s), 1);
             mbar_init(raw_empty(s), kDeqWarps);
         }
-        for (int s = 0; s < kBStages; ++s) {
-            mbar_init(b_full(s), 1);
-            mbar_init(b_empty(s), 1);
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(full(s), kDeqWarps + 1);  // + the token producer's expect_tx arrival
+            mbar_init(empty(s), 1);
         }
         for (int s = 0; s < 2; ++s) {
-            mbar_init(a_full(s), kDeqWarps);
-            mbar_init(a_empty(s), 1);
             mbar_init(acc_full(s), 1);
             mbar_init(acc_empty(s), 4);
         }
@@ -190,7 +203,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
     if (warp == 0) {
         if (lane == 0) {
             // ---------------------------------------------------------- producer
-            int raw_n = 0, b_n = 0;  // running stage counters
+            int raw_n = 0;
             bool ok = true;
             Item it;
             for (int w = blockIdx.x; ok && item_at(p, n_tiles, w, it); w += gridDim.x) {
@@ -199,29 +212,27 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                 const CUtensorMap* m0 = it.shared ? &tm.ms0 : &tm.mw0;
                 const CUtensorMap* m1 = it.shared ? &tm.ms1 : &tm.mw1;
                 const QMat& A = it.shared ? p.S0 : p.A0;
-                const int y0 = (it.shared ? 0 : (it.t.expert - p.e_begin)) * A.rows + it.mt * kTileM;
+                const int y0 = (it.shared ? 0 : (it.t.expert - p.e_begin)) * A.rows + it.mt * C::kRowsPerMat;
                 for (int kb = 0; kb < it.nkb && ok; kb += 2) {
-                    {
-                        const int s = raw_n % kRS;
-                        if (!mbar_wait(raw_empty(s), ((raw_n / kRS) & 1) ^ 1, abort_flag)) {
-                            fail(kErrEmpty);
-                            ok = false;
-                            break;
-                        }
-                        const uint32_t dst = smem_u32(raw_ring + s * C::kRawStageBytes);
-                        mbar_expect_tx(raw_full(s), C::kRawStageBytes);
-                        // qs of values [64 kb, 64 kb + 128), and the 16-byte header slice
-                        // covering the 256 values around them
-                        const int x = (kb / 2) * C::kRawRowBytes;
-                        const int xm = (kb / 4) * 16;
-                        tma_load_2d(dst, w0, x, y0, raw_full(s));
-                        tma_load_2d(dst + C::kQsBytes, m0, xm, y0, raw_full(s));
-                        if (GATEUP) {
-                            tma_load_2d(dst + kTileM * C::kRawRowBytes, w1, x, y0, raw_full(s));
-                            tma_load_2d(dst + C::kQsBytes + kTileM * 16, m1, xm, y0, raw_full(s));
-                        }
-                        ++raw_n;
+                    const int s = raw_n % kRS;
+                    if (!mbar_wait(raw_empty(s), ((raw_n / kRS) & 1) ^ 1, abort_flag)) {
+                        fail(kErrEmpty);
+                        ok = false;
+                        break;
                     }
+                    const uint32_t dst = smem_u32(raw_ring + s * C::kRawStageBytes);
+                    mbar_expect_tx(raw_full(s), C::kRawStageBytes);
+                    // qs of values [64 kb, 64 kb + 128), and the 16-byte header slice
+                    // covering the 256 values around them; gate/up: gate rows then up rows
+                    const int x = (kb / 2) * C::kRawRowBytes;
+                    const int xm = (kb / 4) * 16;
+                    tma_load_2d(dst, w0, x, y0, raw_full(s));
+                    tma_load_2d(dst + C::kQsBytes, m0, xm, y0, raw_full(s));
+                    if (GATEUP) {
+                        tma_load_2d(dst + C::kRowsPerMat * C::kRawRowBytes, w1, x, y0, raw_full(s));
+                        tma_load_2d(dst + C::kQsBytes + C::kRowsPerMat * 16, m1, xm, y0, raw_full(s));
+                    }
+                    ++raw_n;
                 }
             }
             if (!ok) {
@@ -241,67 +252,59 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
             for (int w = blockIdx.x; ok && item_at(p, n_tiles, w, it); w += gridDim.x) {
                 const CUtensorMap* bm = &tm.b[it.N / 16 - 1];
                 for (int kb = 0; kb < it.nkb; ++kb) {
-                    const int sb = b_n % kBStages;
-                    if (!mbar_wait(b_empty(sb), ((b_n / kBStages) & 1) ^ 1, abort_flag)) {
+                    const int sb = b_n % kStages;
+                    if (!mbar_wait(empty(sb), ((b_n / kStages) & 1) ^ 1, abort_flag)) {
                         fail(kErrEmpty);
                         ok = false;
                         break;
                     }
                     const uint32_t dst = smem_u32(b_ring + sb * kBStageBytes);
-                    mbar_expect_tx(b_full(sb), (uint32_t)it.N * kBK * 2);
-                    tma_load_2d(dst, bm, kb * kBK, it.t.pos0, b_full(sb));
+                    mbar_expect_tx(full(sb), (uint32_t)it.N * kBK * 2);
+                    tma_load_2d(dst, bm, kb * kBK, it.t.pos0, full(sb));
                     ++b_n;
                 }
             }
             if (!ok) {
-                for (int i = 0; i < kBStages && i < b_n; ++i) {
+                // the copies in flight land whatever the dequant warps do: wait for
+                // their bytes with a timed wait on the stage's transaction count
+                for (int i = 0; i < kStages && i < b_n; ++i) {
                     const int n = b_n - 1 - i;
-                    mbar_wait_timed(b_full(n % kBStages), (n / kBStages) & 1);
+                    mbar_wait_timed(full(n % kStages), (n / kStages) & 1);
                 }
             }
         }
     } else if (warp == 1) {
         if (lane == 0) {
             // ---------------------------------------------------------- MMA issuer
-            int a_n = 0, b_n = 0, item_n = 0;
+            int a_n = 0, item_n = 0;
             bool ok = true, issued = false;
             Item it;
             for (int w = blockIdx.x; ok && item_at(p, n_tiles, w, it); w += gridDim.x, ++item_n) {
-                const int ab = item_n % C::kAcc;
-                if (!mbar_wait(acc_empty(ab), ((item_n / C::kAcc) & 1) ^ 1, abort_flag)) {
+                const int ab = item_n & 1;
+                if (!mbar_wait(acc_empty(ab), ((item_n >> 1) & 1) ^ 1, abort_flag)) {
                     fail(kErrAcc);
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const uint32_t idesc = idesc_f16(kTileM, it.N);
-                const uint32_t d0 = tmem + (GATEUP ? 0u : (uint32_t)ab * kAccStride);
+                const uint32_t d0 = tmem + (uint32_t)ab * kAccStride;
                 for (int kb = 0; kb < it.nkb; ++kb) {
-                    const int sa = a_n & 1, sb = b_n % kBStages;
-                    if (!mbar_wait(a_full(sa), (a_n >> 1) & 1, abort_flag)) {
+                    const int sa = a_n % kStages;
+                    if (!mbar_wait_backoff(full(sa), (a_n / kStages) & 1, abort_flag)) {
                         fail(kErrAFull);
                         ok = false;
                         break;
                     }
-                    if (!mbar_wait(b_full(sb), (b_n / kBStages) & 1, abort_flag)) {
-                        fail(kErrBFull);
-                        ok = false;
-                        break;
-                    }
                     tc_fence_after();
-                    const uint32_t b = smem_u32(b_ring + sb * kBStageBytes);
-                    const uint32_t a0 = tmem + kAColBase + (uint32_t)sa * (GATEUP ? 64u : 32u);
+                    const uint32_t b = smem_u32(b_ring + sa * kBStageBytes);
+                    const uint32_t a0 = tmem + kAColBase + (uint32_t)sa * kAStageCols;
 #pragma unroll
-                    for (int kk = 0; kk < kBK / 16; ++kk) {
-                        const uint32_t acc = (kb > 0 || kk > 0) ? 1u : 0u;
-                        umma_ts(d0, a0 + kk * 8, sw128_desc(b + kk * 32), idesc, acc);
-                        if (GATEUP) umma_ts(d0 + kAccStride, a0 + 32 + kk * 8, sw128_desc(b + kk * 32), idesc, acc);
-                    }
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        umma_ts(d0, a0 + kk * 8, sw128_desc(b + kk * 32), idesc, (kb > 0 || kk > 0) ? 1u : 0u);
                     issued = true;
-                    umma_commit(a_empty(sa));
-                    umma_commit(b_empty(sb));
+                    umma_commit(empty(sa));
                     ++a_n;
-                    ++b_n;
                 }
                 if (ok) umma_commit(acc_full(ab));
             }
@@ -313,120 +316,106 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
     } else if (warp < kEpiWarp0) {
         // -------------------------------------------------------------- dequant
         // 16 warps: warp (warp & 3) may write TMEM lane quarter q; its combo
-        // c = (warp - 2) / 4 picks its share of each 64-value K-block:
-        //   gate/up: matrix c / 2, values [32 (c % 2), +32)   (16 TMEM columns)
-        //   down:    values [16 c, 16 c + 16)                 (8 TMEM columns)
+        // c = (warp - 2) / 4 takes values [16 c, 16 c + 16) of each 64-value K step
+        // (8 TMEM columns). TMEM lane r is weight row r of the item; gate/up items
+        // interleave the matrices: lane r holds row r / 2 of gate (r even) or up (r odd).
         const int cmb = (warp - 2) >> 2;
         const int q = warp & 3;
-        const int r = q * 32 + lane;  // weight row within the 128-row block
+        const int r = q * 32 + lane;
+        const int srow = GATEUP ? (r & 1) * (kTileM / 2) + (r >> 1) : r;  // row in the raw stage
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-        const int mat = GATEUP ? (cmb >> 1) : 0;
-        const int half = GATEUP ? (cmb & 1) : 0;
+        const int swz = DT == AERO_DT_Q4_K ? ((srow >> 1) & 3) : (srow & 7);
         int raw_n = 0, a_n = 0;
         bool ok = true;
         Item it;
-        for (int w = blockIdx.x; ok && item_at(p, n_tiles, w, it); w += gridDim.x) {
-            for (int kb = 0; kb < it.nkb; ++kb) {
-                const int s = raw_n % kRS;
-                if ((kb & 1) == 0) {
-                    const bool got = __all_sync(0xffffffffu, mbar_wait(raw_full(s), (raw_n / kRS) & 1, abort_flag));
-                    if (!got) {
-                        if (lane == 0) fail(kErrRawFull);
-                        ok = false;
-                        break;
-                    }
+        // this warp's 8 columns of K step kb (from the raw stage's row and header)
+        auto dequant8 = [&](int kb, const uint8_t* qrow, const uint4& meta, uint32_t (&cols)[8]) {
+            if (DT == AERO_DT_Q4_K) {
+                // the K step's 32 bytes: low nibbles are its values 0-31 (sub-block 2g),
+                // high nibbles 32-63 (sub-block 2g+1); this warp's 16 values are one
+                // nibble of 16 bytes
+                const bool hi = cmb >= 2;
+                int sc, mn;
+                q4k_sc_m_words(meta.y, meta.z, meta.w, 2 * (kb & 3) + (hi ? 1 : 0), sc, mn);
+                // (d sc, dmin m) in f16: the 6-bit sc and m are exact as 1024 + v - 1024,
+                // and one rounding of the exact products equals the f32 route's
+                const __half2 k1024 = u2h(0x64006400u);
+                const __half2 scm = __hsub2(u2h((uint32_t)sc | ((uint32_t)mn << 16) | 0x64006400u), k1024);
+                const __half2 prod = __hmul2(u2h(meta.x), scm);  // meta.x = (d, dmin)
+                const __half2 sh = __low2half2(prod), nh = __hneg2(__high2half2(prod));
+                const int c = 2 * (kb & 1) + (cmb & 1);
+                const uint4 v = *reinterpret_cast<const uint4*>(qrow + ((c ^ swz) << 4));
+                const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t w0 = hi ? wv[i] >> 4 : wv[i];
+                    const uint32_t w1 = wv[i] >> (hi ? 12 : 8);
+                    // (bytes 0, 2) and (bytes 1, 3): 1024 + q exactly, then s q - m
+                    const __half2 q02 = __hsub2(u2h((w0 & 0x000F000Fu) | 0x64006400u), k1024);
+                    const __half2 q13 = __hsub2(u2h((w1 & 0x000F000Fu) | 0x64006400u), k1024);
+                    cols[2 * i] = h2u(__hfma2(q02, sh, nh));
+                    cols[2 * i + 1] = h2u(__hfma2(q13, sh, nh));
                 }
-                const int sa = a_n & 1;
-                const bool got = __all_sync(0xffffffffu, mbar_wait(a_empty(sa), ((a_n >> 1) & 1) ^ 1, abort_flag));
-                if (!got) {
-                    if (lane == 0) fail(kErrAEmpty);
+            } else {
+                // the 16-byte slice holds 8 fp16 scales for 256 values; this warp's 16
+                // values lie in block 2 (kb & 3) + cmb / 2
+                const int kq = kb & 3;
+                const uint32_t sc8 = kq == 0 ? meta.x : kq == 1 ? meta.y : kq == 2 ? meta.z : meta.w;
+                const __half2 dd =
+                    __half2half2(__ushort_as_half((unsigned short)((cmb >> 1) ? (sc8 >> 16) : (sc8 & 0xFFFFu))));
+                const int c = 4 * (kb & 1) + cmb;
+                const uint4 v = *reinterpret_cast<const uint4*>(qrow + ((c ^ swz) << 4));
+                const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const uint32_t wb = wv[i] ^ 0x80808080u;
+                    cols[2 * i] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4240)), dd));
+                    cols[2 * i + 1] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4341)), dd));
+                }
+            }
+        };
+        for (int w = blockIdx.x; ok && item_at(p, n_tiles, w, it); w += gridDim.x) {
+            // both K steps of a raw stage per iteration (item K lengths are multiples of
+            // 128): one raw wait, one header load, one tcgen05.wait::st for two stages
+            for (int kb = 0; kb < it.nkb; kb += 2) {
+                const int s = raw_n % kRS;
+                const int sa0 = a_n % kStages, sa1 = (a_n + 1) % kStages;
+                // one lane polls the barriers; __syncwarp orders the rest of the warp
+                // after its acquire
+                bool got = true;
+                if (lane == 0) {
+                    got = mbar_wait(raw_full(s), (raw_n / kRS) & 1, abort_flag) &&
+                          mbar_wait(empty(sa0), ((a_n / kStages) & 1) ^ 1, abort_flag) &&
+                          mbar_wait(empty(sa1), (((a_n + 1) / kStages) & 1) ^ 1, abort_flag);
+                    if (!got) fail(kErrAEmpty);
+                }
+                if (!__shfl_sync(0xffffffffu, got, 0)) {
                     ok = false;
                     break;
                 }
+                __syncwarp();
                 tc_fence_after();
                 const uint8_t* stage = raw_ring + s * C::kRawStageBytes;
-                // this row's qs for the stage (TMA-swizzled: 64B for Q4_K rows of 64 bytes,
-                // 128B for Q8_0 rows of 128 bytes: logical 16-byte chunk c sits at c ^ f(r))
-                const uint8_t* qrow = stage + mat * kTileM * C::kRawRowBytes + r * C::kRawRowBytes;
-                const int swz = DT == AERO_DT_Q4_K ? ((r >> 1) & 3) : (r & 7);
-                auto qchunk = [&](int c) { return *reinterpret_cast<const uint4*>(qrow + ((c ^ swz) << 4)); };
-                const uint4 meta = *reinterpret_cast<const uint4*>(stage + C::kQsBytes + mat * kTileM * 16 + r * 16);
-                const uint32_t abase = tmem + lane_base + kAColBase + (uint32_t)sa * (GATEUP ? 64u : 32u);
-                if (DT == AERO_DT_Q4_K) {
-                    // values: low nibbles of the K-block's 32 bytes are values 0-31 (sub-block 2g),
-                    // high nibbles 32-63 (sub-block 2g+1); column j holds values 2j, 2j+1
-                    const bool hi = GATEUP ? half : (cmb >> 1);
-                    const uint8_t* mb = reinterpret_cast<const uint8_t*>(&meta);
-                    const float d = __half2float(__ushort_as_half((unsigned short)(mb[0] | (mb[1] << 8))));
-                    const float dmin = __half2float(__ushort_as_half((unsigned short)(mb[2] | (mb[3] << 8))));
-                    int sc, mn;
-                    q4k_sc_m(mb + 4, 2 * (kb & 3) + (hi ? 1 : 0), sc, mn);
-                    const __half2 sh = __float2half2_rn(d * (float)sc), nh = __float2half2_rn(-(dmin * (float)mn));
-                    const int shift = hi ? 4 : 0;
-                    if (GATEUP) {
-                        const uint4 v0 = qchunk(2 * (kb & 1)), v1 = qchunk(2 * (kb & 1) + 1);
-                        const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-                        uint32_t cols[16];
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const uint32_t a2 = __byte_perm(wv[i], 0, 0x4140) >> shift;
-                            const uint32_t b2 = __byte_perm(wv[i], 0, 0x4342) >> shift;
-                            cols[2 * i] = h2u(__hfma2(nib2_to_h2(a2), sh, nh));
-                            cols[2 * i + 1] = h2u(__hfma2(nib2_to_h2(b2), sh, nh));
-                        }
-                        tmem_st16(abase + (uint32_t)mat * 32u + (uint32_t)half * 16u, cols);
-                    } else {
-                        // combo c: bytes [16 (c & 1), +16), low (c < 2) or high nibbles -> columns 8c .. 8c+7
-                        const uint4 v = qchunk(2 * (kb & 1) + (cmb & 1));
-                        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-                        uint32_t cols[8];
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            cols[2 * i] = h2u(__hfma2(nib2_to_h2(__byte_perm(wv[i], 0, 0x4140) >> shift), sh, nh));
-                            cols[2 * i + 1] = h2u(__hfma2(nib2_to_h2(__byte_perm(wv[i], 0, 0x4342) >> shift), sh, nh));
-                        }
-                        tmem_st8(abase + (uint32_t)cmb * 8u, cols);
-                    }
-                } else {
-                    // the 16-byte slice holds 8 fp16 scales for 256 values; this K-block uses two
-                    // (values 0-31 and 32-63); column j holds values 2j, 2j+1
-                    const uint32_t mw[4] = {meta.x, meta.y, meta.z, meta.w};
-                    const uint32_t sc8 = mw[kb & 3];
-                    const int blk = GATEUP ? half : (cmb >> 1);
-                    const __half2 dd = __half2half2(__ushort_as_half((unsigned short)(blk ? (sc8 >> 16) : (sc8 & 0xFFFFu))));
-                    if (GATEUP) {
-                        const uint4 v0 = qchunk(4 * (kb & 1) + 2 * blk), v1 = qchunk(4 * (kb & 1) + 2 * blk + 1);
-                        const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-                        uint32_t cols[16];
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const uint32_t wb = wv[i] ^ 0x80808080u;
-                            cols[2 * i] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4140)), dd));
-                            cols[2 * i + 1] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4342)), dd));
-                        }
-                        tmem_st16(abase + (uint32_t)mat * 32u + (uint32_t)half * 16u, cols);
-                    } else {
-                        const uint4 v = qchunk(4 * (kb & 1) + cmb);
-                        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
-                        uint32_t cols[8];
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const uint32_t wb = wv[i] ^ 0x80808080u;
-                            cols[2 * i] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4140)), dd));
-                            cols[2 * i + 1] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4342)), dd));
-                        }
-                        tmem_st8(abase + (uint32_t)cmb * 8u, cols);
-                    }
-                }
+                // this row's qs (TMA-swizzled: 64B for Q4_K rows of 64 bytes, 128B for Q8_0
+                // rows of 128 bytes: logical 16-byte chunk c sits at c ^ f(row))
+                const uint8_t* qrow = stage + srow * C::kRawRowBytes;
+                const uint4 meta = *reinterpret_cast<const uint4*>(stage + C::kQsBytes + srow * 16);
+                const uint32_t acol = tmem + lane_base + kAColBase + (uint32_t)cmb * 8u;
+                uint32_t c0[8], c1[8];
+                dequant8(kb, qrow, meta, c0);
+                dequant8(kb + 1, qrow, meta, c1);
+                tmem_st8(acol + (uint32_t)sa0 * kAStageCols, c0);
+                tmem_st8(acol + (uint32_t)sa1 * kAStageCols, c1);
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(a_full(sa));
-                ++a_n;
-                if ((kb & 1) || kb + 1 == it.nkb) {
-                    if (lane == 0) mbar_arrive(raw_empty(s));
-                    ++raw_n;
+                if (lane == 0) {
+                    mbar_arrive(full(sa0));
+                    mbar_arrive(full(sa1));
+                    mbar_arrive(raw_empty(s));
                 }
+                a_n += 2;
+                ++raw_n;
             }
         }
     } else if (warp < kTokWarp) {
@@ -437,43 +426,64 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
         int item_n = 0;
         Item it;
         for (int w = blockIdx.x; item_at(p, n_tiles, w, it); w += gridDim.x, ++item_n) {
-            const int ab = item_n % C::kAcc;
-            const bool got = __all_sync(0xffffffffu, mbar_wait(acc_full(ab), (item_n / C::kAcc) & 1, abort_flag));
+            const int ab = item_n & 1;
+            const bool got = __shfl_sync(0xffffffffu, lane == 0 ? mbar_wait(acc_full(ab), (item_n >> 1) & 1, abort_flag) : false, 0);
             if (!got) {
                 if (lane == 0) fail(kErrAcc);
                 break;
             }
+            __syncwarp();
             tc_fence_after();
-            const uint32_t d0 = tmem + lane_base + (GATEUP ? 0u : (uint32_t)ab * kAccStride);
-            // 16 columns (tokens) at a time: one TMEM round trip, then the f16 results
-            // go through this warp's 16 x 32 staging tile so each lane stores 16 bytes
-            __half* const out_row0 = p.out + (int64_t)it.t.pos0 * p.out_ld + it.mt * kTileM + q * 32 + (lane & 3) * 8;
-            for (int c0 = 0; c0 < it.N; c0 += 16) {
-                uint32_t g[16];
-                tmem_ld16(d0 + c0, g);
-                if (GATEUP) {
-                    uint32_t u[16];
-                    tmem_ld16(d0 + kAccStride + c0, u);
+            const uint32_t d0 = tmem + lane_base + (uint32_t)ab * kAccStride;
+            if (GATEUP) {
+                // lanes 2i / 2i+1 hold gate / up row 16 q + i of the item's 64 rows.
+                // Per 16 token columns: swap with the partner lane, the even lane forms
+                // act for tokens 0-7, the odd lane for tokens 8-15; stage [16 tok][16 f]
+                // (f in the permuted K order of the down GEMM) and store 32-byte rows.
+                const int fl = lane >> 1, odd = lane & 1;
+                const int fcol = kperm(16 * q + fl) - 16 * q;  // within this warp's 16 f columns
+                __half* const out0 = p.out + (int64_t)it.t.pos0 * p.out_ld + it.mt * (kTileM / 2) + 16 * q;
+                for (int c0 = 0; c0 < it.N; c0 += 16) {
+                    uint32_t v[16];
+                    tmem_ld16(d0 + c0, v);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) {
-                        const float v = __uint_as_float(g[j]);
-                        // silu(v) * u; fast exp / divide suffice for an f16 result
-                        stage[j * 32 + lane] = __float2half_rn(__fdividef(v, 1.0f + __expf(-v)) * __uint_as_float(u[j]));
+                    for (int j = 0; j < 8; ++j) {
+                        // even lane: gate of tokens j (own) with up (partner); odd: tokens 8 + j
+                        const uint32_t send = odd ? v[j] : v[8 + j];
+                        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 1);
+                        const float g = __uint_as_float(odd ? recv : v[j]);
+                        const float u = __uint_as_float(odd ? v[8 + j] : recv);
+                        stage[(8 * odd + j) * 16 + fcol] = __float2half_rn(__fdividef(g, 1.0f + __expf(-g)) * u);
                     }
-                } else {
+                    __syncwarp();
+                    {
+                        const int tok = lane >> 1;
+                        const uint4 o = *reinterpret_cast<const uint4*>(stage + tok * 16 + 8 * odd);
+                        if (c0 + tok < it.t.nvalid)
+                            *reinterpret_cast<uint4*>(out0 + (int64_t)(c0 + tok) * p.out_ld + 8 * odd) = o;
+                    }
+                    __syncwarp();
+                }
+            } else {
+                // 16 columns (tokens) at a time: one TMEM round trip, then the f16 results
+                // go through this warp's 16 x 32 staging tile so each lane stores 16 bytes
+                __half* const out_row0 = p.out + (int64_t)it.t.pos0 * p.out_ld + it.mt * kTileM + q * 32 + (lane & 3) * 8;
+                for (int c0 = 0; c0 < it.N; c0 += 16) {
+                    uint32_t g[16];
+                    tmem_ld16(d0 + c0, g);
                     tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 16; ++j) stage[j * 32 + lane] = __float2half_rn(__uint_as_float(g[j]));
-                }
-                __syncwarp();
+                    __syncwarp();
 #pragma unroll
-                for (int r8 = 0; r8 < 2; ++r8) {
-                    const int j = r8 * 8 + (lane >> 2);
-                    const uint4 v = *reinterpret_cast<const uint4*>(stage + j * 32 + (lane & 3) * 8);
-                    if (c0 + j < it.t.nvalid) *reinterpret_cast<uint4*>(out_row0 + (int64_t)(c0 + j) * p.out_ld) = v;
+                    for (int r8 = 0; r8 < 2; ++r8) {
+                        const int j = r8 * 8 + (lane >> 2);
+                        const uint4 v = *reinterpret_cast<const uint4*>(stage + j * 32 + (lane & 3) * 8);
+                        if (c0 + j < it.t.nvalid) *reinterpret_cast<uint4*>(out_row0 + (int64_t)(c0 + j) * p.out_ld) = v;
+                    }
+                    __syncwarp();
                 }
-                __syncwarp();
             }
             tc_fence_before();
             __syncwarp();
@@ -504,13 +514,16 @@ __global__ void gather_kernel(const XT* __restrict__ x, const int32_t* __restric
         const int v = (int)(i / per_row), c = (int)(i % per_row) * 8;
         const int row = v < pr ? v : P + (v - pr);
         const int tok = v < pr ? perm[v] / k : v - pr;
+        // values in the GEMM's K order: 0, 2, 1, 3 within every four (kperm)
         uint4 o;
         if constexpr (sizeof(XT) == 2) {
-            o = __ldg(reinterpret_cast<const uint4*>(x + (int64_t)tok * dp + c));
+            const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + (int64_t)tok * dp + c));
+            o = make_uint4(__byte_perm(v.x, v.y, 0x5410), __byte_perm(v.x, v.y, 0x7632), __byte_perm(v.z, v.w, 0x5410),
+                           __byte_perm(v.z, v.w, 0x7632));
         } else {
             const float* src = reinterpret_cast<const float*>(x) + (int64_t)tok * dp + c;
             const float4 a = ld_f4(src), b = ld_f4(src + 4);
-            o = make_uint4(pack_h2(a.x, a.y), pack_h2(a.z, a.w), pack_h2(b.x, b.y), pack_h2(b.z, b.w));
+            o = make_uint4(pack_h2(a.x, a.z), pack_h2(a.y, a.w), pack_h2(b.x, b.z), pack_h2(b.y, b.w));
         }
         *reinterpret_cast<uint4*>(xp + (int64_t)row * dp + c) = o;
     }
@@ -554,37 +567,34 @@ __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t* __rest
 
 // out[t] = sum over slots s of w[t][s] * y[inv[t*k+s]] (+ sgate[t] * y[P + t]
 // for t < Tsh). With idx given, slots whose bucket is >= E_real were skipped.
+// Each thread owns 8 columns (one 16-byte load of f16 per row it reads).
 __global__ void combine_h_kernel(const __half* __restrict__ y, const int32_t* __restrict__ inv,
                                  const float* __restrict__ w, const float* __restrict__ sgate,
                                  const int32_t* __restrict__ idx, int E_real, int T, int Tsh, int k, int d,
                                  int has_shared, float* __restrict__ out) {
-    const int d4 = d >> 2;
+    const int d8 = d >> 3;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (int64_t)T * d4) return;
-    const int t = (int)(i / d4), c = (int)(i % d4) * 4;
-    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+    if (i >= (int64_t)T * d8) return;
+    const int t = (int)(i / d8), c = (int)(i % d8) * 8;
+    float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    auto add = [&](float wt, const __half* row) {
+        const uint4 v = __ldg(reinterpret_cast<const uint4*>(row + c));
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float2 f = __half22float2(u2h(u[j]));
+            a[2 * j] += wt * f.x;
+            a[2 * j + 1] += wt * f.y;
+        }
+    };
     for (int s = 0; s < k; ++s) {
         if (idx && idx[(int64_t)t * k + s] >= E_real) continue;
-        const float wt = w[(int64_t)t * k + s];
-        const uint2 v = __ldg(reinterpret_cast<const uint2*>(y + (int64_t)inv[(int64_t)t * k + s] * d + c));
-        const float2 lo = __half22float2(u2h(v.x));
-        const float2 hi = __half22float2(u2h(v.y));
-        a0 += wt * lo.x;
-        a1 += wt * lo.y;
-        a2 += wt * hi.x;
-        a3 += wt * hi.y;
+        add(w[(int64_t)t * k + s], y + (int64_t)inv[(int64_t)t * k + s] * d);
     }
-    if (has_shared && t < Tsh) {
-        const float g = sgate[t];
-        const uint2 v = __ldg(reinterpret_cast<const uint2*>(y + ((int64_t)T * k + t) * d + c));
-        const float2 lo = __half22float2(u2h(v.x));
-        const float2 hi = __half22float2(u2h(v.y));
-        a0 += g * lo.x;
-        a1 += g * lo.y;
-        a2 += g * hi.x;
-        a3 += g * hi.y;
-    }
-    *reinterpret_cast<float4*>(out + (int64_t)t * d + c) = make_float4(a0, a1, a2, a3);
+    if (has_shared && t < Tsh) add(sgate[t], y + ((int64_t)T * k + t) * d);
+    float4* o = reinterpret_cast<float4*>(out + (int64_t)t * d + c);
+    o[0] = make_float4(a[0], a[1], a[2], a[3]);
+    o[1] = make_float4(a[4], a[5], a[6], a[7]);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -633,13 +643,13 @@ bool make_tmap_act(CUtensorMap* m, const void* base, uint64_t rows, uint64_t col
 // A weight plane as 2-D bytes [n_expert * rows][row bytes] (experts must be
 // contiguous): box = 128 rows x box_bytes.
 bool make_tmap_plane(CUtensorMap* m, const uint8_t* base, uint64_t row_bytes, int rows, int64_t estride,
-                     int n_local_experts, int box_bytes, CUtensorMapSwizzle swz) {
+                     int n_local_experts, int box_bytes, CUtensorMapSwizzle swz, int box_rows) {
     auto fn = encode_fn();
     if (!fn || !base) return false;
     if ((uint64_t)estride != row_bytes * (uint64_t)rows || row_bytes % 16) return false;
     cuuint64_t dims[2] = {row_bytes, (cuuint64_t)rows * (cuuint64_t)n_local_experts};
     cuuint64_t strides[1] = {row_bytes};
-    cuuint32_t box[2] = {(cuuint32_t)box_bytes, (cuuint32_t)kTileM};
+    cuuint32_t box[2] = {(cuuint32_t)box_bytes, (cuuint32_t)box_rows};
     cuuint32_t es[2] = {1u, 1u};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t*>(base), dims, strides, box, es,
               CU_TENSOR_MAP_INTERLEAVE_NONE, swz, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -647,14 +657,15 @@ bool make_tmap_plane(CUtensorMap* m, const uint8_t* base, uint64_t row_bytes, in
 }
 // qs plane: the raw bytes of 128 values per box row (Q4_K 64 B, 64B swizzle;
 // Q8_0 128 B, 128B swizzle). Header plane: 16-byte slices, no swizzle.
-bool make_tmap_qs(CUtensorMap* m, const QMat& q, int n_local) {
+// box_rows: 64 for the gate/up families (an item takes 64 rows of each), 128 for down.
+bool make_tmap_qs(CUtensorMap* m, const QMat& q, int n_local, int box_rows) {
     const bool q4 = q.dtype == AERO_DT_Q4_K;
     return make_tmap_plane(m, q.qs, (uint64_t)qm_row_qs_bytes(q.dtype, q.cols), q.rows, q.qs_estride, n_local,
-                           q4 ? kRawK / 2 : kRawK, q4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+                           q4 ? kRawK / 2 : kRawK, q4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B, box_rows);
 }
-bool make_tmap_meta(CUtensorMap* m, const QMat& q, int n_local) {
+bool make_tmap_meta(CUtensorMap* m, const QMat& q, int n_local, int box_rows) {
     return make_tmap_plane(m, q.meta, (uint64_t)qm_row_meta_bytes(q.dtype, q.cols), q.rows, q.meta_estride, n_local, 16,
-                           CU_TENSOR_MAP_SWIZZLE_NONE);
+                           CU_TENSOR_MAP_SWIZZLE_NONE, box_rows);
 }
 
 template <int DT, bool GATEUP>
@@ -712,12 +723,14 @@ bool gemm_setup(void* ws, size_t ws_bytes, int dp, int act_ld, int P_cap, int T_
 bool gemm_weight_maps(const QMat& gate, const QMat& up, const QMat& down, const QMat& sg, const QMat& su, const QMat& sd,
                       int n_local, int has_shared, GemmWeightMaps* m, std::string* why) {
     // the planes' base pointers here are the allocations (expert e_begin first)
-    bool ok = make_tmap_qs(&m->q[0], gate, n_local) && make_tmap_qs(&m->q[1], up, n_local) &&
-              make_tmap_qs(&m->q[2], down, n_local) && make_tmap_meta(&m->m[0], gate, n_local) &&
-              make_tmap_meta(&m->m[1], up, n_local) && make_tmap_meta(&m->m[2], down, n_local);
+    const int h = kTileM / 2;
+    bool ok = make_tmap_qs(&m->q[0], gate, n_local, h) && make_tmap_qs(&m->q[1], up, n_local, h) &&
+              make_tmap_qs(&m->q[2], down, n_local, kTileM) && make_tmap_meta(&m->m[0], gate, n_local, h) &&
+              make_tmap_meta(&m->m[1], up, n_local, h) && make_tmap_meta(&m->m[2], down, n_local, kTileM);
     if (ok && has_shared)
-        ok = make_tmap_qs(&m->q[3], sg, 1) && make_tmap_qs(&m->q[4], su, 1) && make_tmap_qs(&m->q[5], sd, 1) &&
-             make_tmap_meta(&m->m[3], sg, 1) && make_tmap_meta(&m->m[4], su, 1) && make_tmap_meta(&m->m[5], sd, 1);
+        ok = make_tmap_qs(&m->q[3], sg, 1, h) && make_tmap_qs(&m->q[4], su, 1, h) && make_tmap_qs(&m->q[5], sd, 1, kTileM) &&
+             make_tmap_meta(&m->m[3], sg, 1, h) && make_tmap_meta(&m->m[4], su, 1, h) &&
+             make_tmap_meta(&m->m[5], sd, 1, kTileM);
     if (ok && !has_shared)
         for (int i = 0; i < 3; ++i) {
             m->q[3 + i] = m->q[i];
@@ -746,6 +759,8 @@ cudaError_t launch_prefill_prep(const PrefillArgs& a, GemmBuffers& b, cudaStream
 
 cudaError_t launch_prefill_gemm(const PrefillArgs& a, GemmBuffers& b, const GemmWeightMaps& wm, bool gateup,
                                 cudaStream_t s) {
+    // the kernel's stages pair up K steps: every reduction length is a multiple of 128
+    if (a.dp % kRawK || a.F % kRawK || (a.has_shared && a.Fs % kRawK)) return cudaErrorInvalidValue;
     GemmParams g{};
     g.tiles = b.tiles;
     g.n_tiles = b.n_tiles;
@@ -759,8 +774,8 @@ cudaError_t launch_prefill_gemm(const PrefillArgs& a, GemmBuffers& b, const Gemm
         g.S1 = a.has_shared ? a.su : a.up;
         g.K = a.dp;
         g.Ks = a.dp;
-        g.MT = a.F / kTileM;
-        g.MTs = a.has_shared ? a.Fs / kTileM : 0;
+        g.MT = a.F / (kTileM / 2);  // 64 rows of gate and of up per item
+        g.MTs = a.has_shared ? a.Fs / (kTileM / 2) : 0;
         g.MTmax = g.MT > g.MTs ? g.MT : g.MTs;
         g.out = b.act;
         g.out_ld = a.act_ld;
@@ -799,7 +814,7 @@ cudaError_t launch_prefill_gemm(const PrefillArgs& a, GemmBuffers& b, const Gemm
 cudaError_t launch_combine_h(const __half* y, const int32_t* inv, const float* w, const float* sgate,
                              const int32_t* idx, int E_real, int T, int Tsh, int k, int d, int has_shared, float* out,
                              cudaStream_t s) {
-    const int64_t n = (int64_t)T * (d / 4);
+    const int64_t n = (int64_t)T * (d / 8);
     if (n == 0) return cudaSuccess;
     combine_h_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(y, inv, w, sgate, idx, E_real, T, Tsh, k, d,
                                                                  has_shared, out);

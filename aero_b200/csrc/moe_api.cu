@@ -319,7 +319,7 @@ bool router_logits_dev(Handle& h, const float* x, int T, bool with_gate) {
 // Router projection + top-k for T tokens of x (T, dp): s.idx, s.w, s.sgate,
 // s.xsum16. When logits_in is non-null it holds (T, E) caller logits on the
 // device (row stride E).
-bool route_stage(Handle& h, const float* x, int T, const float* logits_in) {
+bool route_stage(Handle& h, const float* x, int T, const float* logits_in, bool need_xsum16) {
     Scratch& s = h.sc;
     cudaStream_t st = h.stream;
     const int ld = h.lg_ld;
@@ -338,7 +338,8 @@ bool route_stage(Handle& h, const float* x, int T, const float* logits_in) {
     }
     h.launches += (!logits_in || h.has_shared) ? 1 : 0;
     h.mark(1);
-    if (!h.cuda_ok(launch_topk(s.logits, ld, T, h.E, h.k, h.norm, h.has_shared, x, h.dp, s.idx, s.w, s.sgate, s.xsum16, st),
+    if (!h.cuda_ok(launch_topk(s.logits, ld, T, h.E, h.k, h.norm, h.has_shared, x, h.dp, s.idx, s.w, s.sgate,
+                               need_xsum16 ? s.xsum16 : nullptr, st),
                    "top-k"))
         return false;
     h.launches += 1;
@@ -463,7 +464,9 @@ bool finish_profile(Handle& h) {
 
 // Core pipeline on device buffers: x (T, dp), out (T, dp).
 bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* out) {
-    if (!route_stage(h, x, T, logits_in)) return false;
+    // the per-16 sums of x only serve the GEMV path
+    const bool gemv = !(h.gemm_ok && h.gb_ready && T >= h.gemm_min_tokens);
+    if (!route_stage(h, x, T, logits_in, gemv)) return false;
     if (!expert_stage(h, x, false, T, T, false, out)) return false;
     return finish_profile(h);
 }
@@ -1049,7 +1052,7 @@ int aero_cuda_ep_dispatch(void* handle, const float* x, int T, int n_ranks, int 
     cudaSetDevice(h->device);
     if (!aero::ensure_scratch(*h, std::max(T, 1))) return -1;
     auto& s = h->sc;
-    if (T > 0 && !aero::route_stage(*h, x, T, nullptr)) return -1;
+    if (T > 0 && !aero::route_stage(*h, x, T, nullptr, false)) return -1;
     // the plan reuses the dispatch buffers: perm holds send_tok, inv send_rank
     if (!h->cuda_ok(aero::launch_ep_plan(s.idx, T, h->k, rt, rank, s.perm, s.inv, counts, pos, h->stream), "exchange plan"))
         return -1;

@@ -221,15 +221,20 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
 // per-expert running offsets over chunks plus the expert prefix; scatter: each
 // chunk is walked in pair order by one warp, 32 pairs at a time, ranking equal
 // experts with __match_any_sync, so the result is stable.
-constexpr int kDispChunk = 256;
+constexpr int kDispChunk = 256;  // minimum chunk; large calls use ~148 chunks (one per SM)
 
-__global__ void dispatch_count_kernel(const int32_t* __restrict__ idx, int P, int E,
+int dispatch_chunk(int P) {
+    const int per = (P + 147) / 148;
+    return std::max(kDispChunk, (per + 31) / 32 * 32);
+}
+
+__global__ void dispatch_count_kernel(const int32_t* __restrict__ idx, int P, int E, int chunk,
                                       int32_t* __restrict__ counts) {
     extern __shared__ int32_t hist[];
     for (int e = threadIdx.x; e < E; e += blockDim.x) hist[e] = 0;
     __syncthreads();
-    const int p0 = blockIdx.x * kDispChunk;
-    for (int p = p0 + threadIdx.x; p < min(P, p0 + kDispChunk); p += blockDim.x) atomicAdd(&hist[idx[p]], 1);
+    const int p0 = blockIdx.x * chunk;
+    for (int p = p0 + threadIdx.x; p < min(P, p0 + chunk); p += blockDim.x) atomicAdd(&hist[idx[p]], 1);
     __syncthreads();
     for (int e = threadIdx.x; e < E; e += blockDim.x) counts[(int64_t)blockIdx.x * E + e] = hist[e];
 }
@@ -288,7 +293,7 @@ __global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(int32_t* __
     }
 }
 
-__global__ void dispatch_scatter_kernel(const int32_t* __restrict__ idx, int P, int E,
+__global__ void dispatch_scatter_kernel(const int32_t* __restrict__ idx, int P, int E, int chunk_len,
                                         const int32_t* __restrict__ offsets,
                                         const int32_t* __restrict__ counts, int32_t* __restrict__ perm,
                                         int32_t* __restrict__ inv) {
@@ -298,8 +303,8 @@ __global__ void dispatch_scatter_kernel(const int32_t* __restrict__ idx, int P, 
     __syncthreads();
     if (threadIdx.x >= 32) return;
     const int lane = threadIdx.x;
-    const int p_end = min(P, (chunk + 1) * kDispChunk);
-    for (int base = chunk * kDispChunk; base < p_end; base += 32) {
+    const int p_end = min(P, (chunk + 1) * chunk_len);
+    for (int base = chunk * chunk_len; base < p_end; base += 32) {
         const int p = base + lane;
         const bool valid = p < p_end;
         const int e = valid ? idx[p] : -1 - lane;  // invalid lanes never match a real expert
@@ -342,7 +347,8 @@ cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int no
 }
 
 size_t dispatch_work_bytes(int P, int E) {
-    const size_t n_chunks = (size_t)(P + kDispChunk - 1) / kDispChunk;
+    const int chunk = dispatch_chunk(P);
+    const size_t n_chunks = (size_t)(P + chunk - 1) / chunk;
     return std::max<size_t>(1, n_chunks) * (size_t)E * sizeof(int32_t);
 }
 
@@ -350,12 +356,13 @@ cudaError_t launch_dispatch(const int32_t* idx, int P, int E, int32_t* offsets, 
                             int32_t* act_e, int32_t* act_off, int32_t* n_active, void* work, cudaStream_t s,
                             int n_real) {
     if (n_real < 0) n_real = E;
-    const int n_chunks = std::max(1, (P + kDispChunk - 1) / kDispChunk);
+    const int chunk = dispatch_chunk(P);
+    const int n_chunks = std::max(1, (P + chunk - 1) / chunk);
     int32_t* counts = static_cast<int32_t*>(work);
     const size_t hist_smem = (size_t)E * sizeof(int32_t);
-    dispatch_count_kernel<<<n_chunks, 256, hist_smem, s>>>(idx, P, E, counts);
+    dispatch_count_kernel<<<n_chunks, 256, hist_smem, s>>>(idx, P, E, chunk, counts);
     dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(counts, n_chunks, E, n_real, P, offsets, act_e, act_off, n_active);
-    dispatch_scatter_kernel<<<n_chunks, 128, hist_smem, s>>>(idx, P, E, offsets, counts, perm, inv);
+    dispatch_scatter_kernel<<<n_chunks, 128, hist_smem, s>>>(idx, P, E, chunk, offsets, counts, perm, inv);
     return cudaGetLastError();
 }
 

@@ -45,12 +45,34 @@ __device__ bool mbar_wait_timed(uint32_t bar, uint32_t parity) {
         if (gtimer() - t0 > kWaitNs) return false;
     return true;
 }
+// try_wait that may suspend the thread until the phase completes or about
+// hint_ns pass, so a waiting warp takes no issue slots from the working ones.
+__device__ __forceinline__ bool mbar_try_suspend(uint32_t bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait for a lone polling thread that shares its SM sub-partition with
+// busy warps: it sleeps between polls so it takes few of their issue slots.
+__device__ bool mbar_wait_backoff(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+    const uint64_t t0 = gtimer();
+    while (true) {
+        if (mbar_try(bar, parity)) return true;
+        if (*abort_flag) return false;
+        if (gtimer() - t0 > kWaitNs) return false;
+        __nanosleep(64);
+    }
+}
 // Bounded wait: false on timeout or when another role of this CTA gave up.
 __device__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
     if (mbar_try(bar, parity)) return true;
     const uint64_t t0 = gtimer();
     while (true) {
-        if (mbar_try(bar, parity)) return true;
+        if (mbar_try_suspend(bar, parity, 20000u)) return true;
         if (*abort_flag) return false;
         if (gtimer() - t0 > kWaitNs) return false;
     }
