@@ -131,6 +131,7 @@ __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
     return false;
 }
 
+template <int PER>  // values per lane: E <= 32 * PER
 __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int ld, int T, int E,
                                                    int k, int norm, int has_shared,
                                                    const float* __restrict__ x, int d, int32_t* __restrict__ idx,
@@ -140,16 +141,16 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
     const int t = blockIdx.x * 8 + warp;
     if (t >= T) return;
     const float* lg = logits + (int64_t)t * ld;
-    float v[kTopkMaxPerLane];
-    const int per = (E + 31) >> 5;
+    float v[PER];
 #pragma unroll
-    for (int i = 0; i < kTopkMaxPerLane; ++i) {
+    for (int i = 0; i < PER; ++i) {
         const int e = lane + 32 * i;
-        v[i] = (i < per && e < E) ? lg[e] : 0.f;
+        v[i] = e < E ? lg[e] : 0.f;
     }
     uint32_t taken = 0;  // bit i: slot i of this lane removed (or absent)
-    for (int i = 0; i < kTopkMaxPerLane; ++i)
-        if (!(i < per && lane + 32 * i < E)) taken |= 1u << i;
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+        if (lane + 32 * i >= E) taken |= 1u << i;
 
     float sel_v = 0.f;  // lane j keeps the j-th selected logit (j < k <= 32 handled in rounds)
     float wsum = 0.f, mx = 0.f;
@@ -157,7 +158,7 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
         float bv = 0.f;
         int bi = 0x7fffffff;
 #pragma unroll
-        for (int i = 0; i < kTopkMaxPerLane; ++i) {
+        for (int i = 0; i < PER; ++i) {
             if (taken & (1u << i)) continue;
             const int e = lane + 32 * i;
             if (bi == 0x7fffffff || better(v[i], e, bv, bi)) {
@@ -190,9 +191,9 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
     } else {
         double den = 0.0;
 #pragma unroll
-        for (int i = 0; i < kTopkMaxPerLane; ++i) {
+        for (int i = 0; i < PER; ++i) {
             const int e = lane + 32 * i;
-            if (i < per && e < E) den += (double)expf(v[i] - mx);
+            if (e < E) den += (double)expf(v[i] - mx);
         }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
@@ -342,7 +343,19 @@ cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int no
                         const float* x, int d, int32_t* idx, float* w, float* sgate, float* xsum16,
                         cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
-    topk_kernel<<<(T + 7) / 8, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, x, d, idx, w, sgate, xsum16);
+    const unsigned grid = (unsigned)((T + 7) / 8);
+    if (E <= 32)
+        topk_kernel<1><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, x, d, idx, w, sgate, xsum16);
+    else if (E <= 64)
+        topk_kernel<2><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, x, d, idx, w, sgate, xsum16);
+    else if (E <= 128)
+        topk_kernel<4><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, x, d, idx, w, sgate, xsum16);
+    else if (E <= 256)
+        topk_kernel<8><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, x, d, idx, w, sgate, xsum16);
+    else if (E <= 512)
+        topk_kernel<16><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, x, d, idx, w, sgate, xsum16);
+    else
+        topk_kernel<32><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, x, d, idx, w, sgate, xsum16);
     return cudaGetLastError();
 }
 
