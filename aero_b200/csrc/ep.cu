@@ -148,26 +148,6 @@ __global__ void ep_prep_kernel(const int32_t* __restrict__ meta, int meta_ld, in
     if (s == 0) sgate[r] = r < Tsh ? __int_as_float(m[2 * k]) : 0.f;
 }
 
-// Per-16-value sums of x rows (the GEMV path's Q4_K min term), one warp per row.
-__global__ void xsum16_kernel(const float* __restrict__ x, int R, int dp, float* __restrict__ xsum16) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int r = blockIdx.x * 8 + warp;
-    if (r >= R) return;
-    const float* xr = x + (int64_t)r * dp;
-    for (int g = lane; g < dp / 16; g += 32) {
-        float s = 0.f;
-#pragma unroll
-        for (int i = 0; i < 16; i += 4) {
-            const float4 q = ld_f4(xr + 16 * g + i);
-            s += q.x;
-            s += q.y;
-            s += q.z;
-            s += q.w;
-        }
-        xsum16[(int64_t)r * (dp / 16) + g] = s;
-    }
-}
-
 // out[t] = self_out[t] + sum over remote ranks r (ascending) of back[pos[t][r]].
 __global__ void ep_combine_kernel(const float* __restrict__ self_out, const float* __restrict__ back,
                                   const int32_t* __restrict__ pos, int T, int n, int me, int dp,
@@ -222,12 +202,6 @@ cudaError_t launch_ep_prep(const int32_t* meta, int meta_ld, int R, int k, int T
     if (n == 0) return cudaSuccess;
     ep_prep_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(meta, meta_ld, R, k, Tsh, e_begin, e_end, E, idx, w,
                                                                sgate, bad);
-    return cudaGetLastError();
-}
-
-cudaError_t launch_xsum16(const float* x, int R, int dp, float* xsum16, cudaStream_t s) {
-    if (R <= 0) return cudaSuccess;
-    xsum16_kernel<<<(R + 7) / 8, 256, 0, s>>>(x, R, dp, xsum16);
     return cudaGetLastError();
 }
 

@@ -1,25 +1,31 @@
 // Decode-path expert products: bandwidth-bound grouped GEMVs on CUDA cores.
 //
-// Only the selected experts' quant blocks are streamed (16-byte non-allocating
-// loads), dequantised in registers and accumulated in fp32; no tensor cores.
-// Each active expert's weights are read once and applied to every token routed
-// to it. Semantics per (token, expert) are those of aero_moe_expert_accum
-// (src/moe.cpp:68-88): act = silu(gate.h) * (up.h), y = down.act, with the
-// routing weight applied later by the combine kernel in slot order.
+// Only the selected experts' quant blocks are streamed, dequantised in
+// registers and accumulated in fp32; no tensor cores. Semantics per (token,
+// expert) are those of aero_moe_expert_accum (src/moe.cpp:68-88): act =
+// silu(gate.h) * (up.h), y = down.act, with the routing weight applied later by
+// the combine kernel in slot order.
 //
-// gate/up: one CTA (4 warps) per (active expert, group of 16 rows); each warp
-//          owns 4 rows and writes act[pos][row] for every routed pair; the CTA
-//          then writes asum16[pos][group] = sum of its 16 act values, which the
-//          Q4_K down product needs for its min term.
-// down:    one CTA per (active expert, group of output rows); lanes split a row
-//          into 16-byte chunks; y[pos][n] per routed pair.
+// A warp computes one row dot at a time: its lanes split the row into 16-byte
+// code chunks (coalesced streaming loads, the next row's chunks prefetched into
+// registers), and each lane keeps the input values matching its chunks in
+// registers for the whole CTA, so the only per-row traffic is the weights. A
+// CTA owns one unit (an active expert, or the shared expert) x 32 rows x one
+// token; tokens of a unit take successive passes (decode units hold 1-2). Per
+// 32-value sub-block the products follow the reference factorisation of the
+// quantised dot (src/kernels.cpp:78-84, 123-156):
+//   Q8_0: d * sum(q x)            Q4_K: d sc * sum(q x) - dmin m * sum(x)
+// Codes become floats by a byte permute into the mantissa of 2^23 and one
+// subtraction (exact).
+#include <algorithm>
+
 #include "internal.h"
 
 namespace aero {
 namespace {
 
-constexpr int kPairGroup = 4;  // tokens accumulated per pass over a row
-constexpr int kMaxSlots = 4;   // 16-byte chunks per lane held in flight per matrix
+constexpr int kWarps = 8;
+constexpr int kMaxChunks = 4;    // code chunks per lane
 
 struct UnitSrc {
     int e;        // expert index within the QMat
@@ -28,21 +34,15 @@ struct UnitSrc {
     bool shared;
 };
 
-__device__ __forceinline__ bool unit_of(const GemvArgs& a, int b, int groups_routed, int groups_shared,
-                                        bool shared_launch, UnitSrc& u, int& grp) {
+__device__ __forceinline__ bool unit_of(const GemvArgs& a, int ui, bool shared_launch, UnitSrc& u) {
     const int P = a.T * a.k;
     if (!shared_launch) {
-        const int n_act = *a.n_active;
-        if (b >= n_act * groups_routed) return false;
-        const int ui = b / groups_routed;
-        grp = b % groups_routed;
+        if (ui >= *a.n_active) return false;
         u.e = a.act_e[ui];
         u.pos0 = a.act_off[ui];
         u.npairs = a.act_off[ui + 1] - u.pos0;
         u.shared = false;
     } else {
-        if (b >= groups_shared) return false;
-        grp = b;
         u.e = 0;
         u.pos0 = P;
         u.npairs = a.Tsh;
@@ -55,166 +55,345 @@ __device__ __forceinline__ int token_of(const GemvArgs& a, const UnitSrc& u, int
     return u.shared ? pos - a.T * a.k : a.perm[pos] / a.k;
 }
 
-template <int DT, bool SHARED>
-__global__ void __launch_bounds__(128) gateup_kernel(GemvArgs a) {
-    const int F = SHARED ? a.Fs : a.F;
-    UnitSrc u;
-    int grp;
-    if (!unit_of(a, blockIdx.x, a.F / 16, a.Fs / 16, SHARED, u, grp)) return;
-    const QMat& G = SHARED ? a.sg : a.gate;
-    const QMat& U = SHARED ? a.su : a.up;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nch = qm_chunks_per_row(DT, a.d);
-    const int xs_ld = a.d / 16;
+// Four codes held one per byte of nb -> floats (byte - bias), exactly.
+__device__ __forceinline__ void bytes4_to_f(uint32_t nb, float bias, float (&f)[4]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k) f[k] = __int_as_float(__byte_perm(nb, 0x4B000000u, 0x7540 + k)) - bias;
+}
 
-    for (int rr = 0; rr < 4; ++rr) {
-        const int j = grp * 16 + warp * 4 + rr;
-        if (j >= F) break;
-        const uint8_t* gq = qm_row_qs(G, u.e, j);
-        const uint8_t* gm = qm_row_meta(G, u.e, j);
-        const uint8_t* uq = qm_row_qs(U, u.e, j);
-        const uint8_t* um = qm_row_meta(U, u.e, j);
-        for (int p0 = 0; p0 < u.npairs; p0 += kPairGroup) {
-            float ga[kPairGroup], ua[kPairGroup];
-            int tok[kPairGroup];
+template <int DT>
+struct Layout;
+// Q8_0 row of K values: K bytes of codes, a f16 scale per 32 values. Chunk c =
+// values [16 c, 16 c + 16).
+template <>
+struct Layout<AERO_DT_Q8_0> {
+    static constexpr int kVals = 16;  // values per chunk
+    static constexpr int kWords = 1;  // 16-byte loads per chunk
+    static __host__ __device__ __forceinline__ int chunks(int K) { return K / 16; }
+};
+// Q4_K row: 256-value super-blocks of 128 code bytes and a 16-byte header.
+// Chunk c = code bytes [16 c, 16 c + 16): super-block c / 8, byte group
+// g = (c % 8) / 2 of 32 bytes, half h = c % 2; its low nibbles are values
+// 64 g + 16 h + [0, 16) (sub-block 2 g) and its high nibbles 64 g + 32 + 16 h +
+// [0, 16) (sub-block 2 g + 1) of the super-block.
+template <>
+struct Layout<AERO_DT_Q4_K> {
+    static constexpr int kVals = 32;
+    static constexpr int kWords = 1;
+    static __host__ __device__ __forceinline__ int chunks(int K) { return K / 32; }
+};
+// F32 (padded to 16) row: chunk c = values [16 c, 16 c + 16), four 16-byte loads.
+template <>
+struct Layout<AERO_DT_F32> {
+    static constexpr int kVals = 16;
+    static constexpr int kWords = 4;
+    static __host__ __device__ __forceinline__ int chunks(int K) { return K / 16; }
+};
+
+// First input index of each run of chunk c (two 16-value runs for Q4_K).
+template <int DT>
+__device__ __forceinline__ int run0(int c) {
+    if (DT == AERO_DT_Q4_K) return (c >> 3) * 256 + ((c & 7) >> 1) * 64 + (c & 1) * 16;
+    return c * Layout<DT>::kVals;
+}
+
+// A lane's share of one row: its chunks' raw bytes and per-chunk scale data.
+template <int DT, int CPL>
+struct RowRaw {
+    uint4 q[CPL][Layout<DT>::kWords];
+    uint4 m[DT == AERO_DT_Q4_K ? CPL : 1];  // Q4_K: header of each chunk's super-block
+    uint32_t sc[DT == AERO_DT_Q8_0 ? CPL : 1];  // Q8_0: f16 scale of each chunk's block
+};
+
+template <int DT, int LPR, int CPL>
+__device__ __forceinline__ void row_load(const QMat& M, int e, int r, int gl, int nch, RowRaw<DT, CPL>& w) {
+    const uint8_t* qs = qm_row_qs(M, e, r);
 #pragma unroll
-            for (int i = 0; i < kPairGroup; ++i) {
-                ga[i] = ua[i] = 0.f;
-                tok[i] = (p0 + i < u.npairs) ? token_of(a, u, u.pos0 + p0 + i) : -1;
-            }
-            for (int cb = 0; cb < nch; cb += 32 * kMaxSlots) {
-                uint4 rg[kMaxSlots], ru[kMaxSlots], mg[kMaxSlots], mu[kMaxSlots];
+    for (int i = 0; i < CPL; ++i) {
+        const int c = gl + LPR * i;
+        if (c < nch) {
 #pragma unroll
-                for (int s = 0; s < kMaxSlots; ++s) {
-                    const int c = cb + s * 32 + lane;
-                    if (c < nch) {
-                        chunk_load<DT>(G, gq, gm, c, rg[s], mg[s]);
-                        chunk_load<DT>(U, uq, um, c, ru[s], mu[s]);
-                    }
-                }
-#pragma unroll
-                for (int s = 0; s < kMaxSlots; ++s) {
-                    const int c = cb + s * 32 + lane;
-                    if (c >= nch) continue;
-                    Chunk kc;
-                    chunk_decode<DT>(c, rg[s], mg[s], kc);
-#pragma unroll
-                    for (int i = 0; i < kPairGroup; ++i)
-                        if (tok[i] >= 0)
-                            ga[i] += chunk_dot<DT>(kc, a.x + (int64_t)tok[i] * a.d, a.xsum16 + (int64_t)tok[i] * xs_ld);
-                    chunk_decode<DT>(c, ru[s], mu[s], kc);
-#pragma unroll
-                    for (int i = 0; i < kPairGroup; ++i)
-                        if (tok[i] >= 0)
-                            ua[i] += chunk_dot<DT>(kc, a.x + (int64_t)tok[i] * a.d, a.xsum16 + (int64_t)tok[i] * xs_ld);
-                }
-            }
-#pragma unroll
-            for (int i = 0; i < kPairGroup; ++i) {
-                const float g = warp_sum(ga[i]);
-                const float uu = warp_sum(ua[i]);
-                if (lane == 0 && tok[i] >= 0) a.act[(int64_t)(u.pos0 + p0 + i) * a.act_ld + j] = silu_f(g) * uu;
+            for (int k = 0; k < Layout<DT>::kWords; ++k) {
+                if (DT == AERO_DT_F32)
+                    w.q[i][k] = __ldg(reinterpret_cast<const uint4*>(qs + (int64_t)c * 64) + k);
+                else
+                    w.q[i][k] = ld_stream16(qs + (int64_t)c * 16);
             }
         }
     }
-    __syncthreads();
-    // 16-row sums of act for this group (fixed summation order)
-    const int as_ld = a.act_ld / 16;
-    for (int p = threadIdx.x; p < u.npairs; p += blockDim.x) {
-        const float* ar = a.act + (int64_t)(u.pos0 + p) * a.act_ld + grp * 16;
-        float s = 0.f;
+    if (DT == AERO_DT_Q4_K) {
+        const uint8_t* mt = qm_row_meta(M, e, r);
 #pragma unroll
-        for (int i = 0; i < 16; ++i) s += (grp * 16 + i < F) ? ar[i] : 0.f;
-        a.asum16[(int64_t)(u.pos0 + p) * as_ld + grp] = s;
+        for (int i = 0; i < CPL; ++i) {
+            const int c = gl + LPR * i;
+            if (c < nch) w.m[i] = __ldg(reinterpret_cast<const uint4*>(mt + (int64_t)(c >> 3) * 16));
+        }
+    } else if (DT == AERO_DT_Q8_0) {
+        const unsigned short* mt = reinterpret_cast<const unsigned short*>(qm_row_meta(M, e, r));
+#pragma unroll
+        for (int i = 0; i < CPL; ++i) {
+            const int c = gl + LPR * i;
+            if (c < nch) w.sc[i] = __ldg(mt + (c >> 1));
+        }
     }
 }
 
-template <int DT, int LPR, bool SHARED>
-__global__ void __launch_bounds__(128) down_kernel(GemvArgs a, int rows_per_cta) {
-    const int Fin = SHARED ? a.Fs : a.F;
-    const int groups = (a.d + rows_per_cta - 1) / rows_per_cta;
-    UnitSrc u;
-    int grp;
-    if (!unit_of(a, blockIdx.x, groups, groups, SHARED, u, grp)) return;
-    const QMat& D = SHARED ? a.sd : a.down;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int sub = lane / LPR, gl = lane % LPR;
-    constexpr int RPW = 32 / LPR;  // rows per warp pass
-    const int nch = qm_chunks_per_row(DT, Fin);
-    const int as_ld = a.act_ld / 16;
+// The lane's input values for its chunks (and, for Q4_K, their run sums).
+template <int DT, int CPL>
+struct LaneInput {
+    float v[CPL][Layout<DT>::kVals];
+    float s[DT == AERO_DT_Q4_K ? CPL : 1][2];
+};
 
-    for (int r0 = grp * rows_per_cta + warp * RPW; r0 < min(a.d, (grp + 1) * rows_per_cta); r0 += 4 * RPW) {
-        const int n = r0 + sub;
-        const bool row_ok = n < a.d && n < (grp + 1) * rows_per_cta;
-        const uint8_t* dq = row_ok ? qm_row_qs(D, u.e, n) : nullptr;
-        const uint8_t* dm = row_ok ? qm_row_meta(D, u.e, n) : nullptr;
-        for (int p0 = 0; p0 < u.npairs; p0 += kPairGroup) {
-            float acc[kPairGroup];
+template <int DT, int LPR, int CPL>
+__device__ __forceinline__ void input_load(const float* x, int gl, int nch, LaneInput<DT, CPL>& in) {
 #pragma unroll
-            for (int i = 0; i < kPairGroup; ++i) acc[i] = 0.f;
-            for (int cb = 0; cb < nch; cb += LPR * kMaxSlots) {
-                uint4 rw[kMaxSlots], mw[kMaxSlots];
+    for (int i = 0; i < CPL; ++i) {
+        const int c = gl + LPR * i;
+        if (c < nch) {
+            if (DT == AERO_DT_Q4_K) {
 #pragma unroll
-                for (int s = 0; s < kMaxSlots; ++s) {
-                    const int c = cb + s * LPR + gl;
-                    if (row_ok && c < nch) chunk_load<DT>(D, dq, dm, c, rw[s], mw[s]);
-                }
+                for (int run = 0; run < 2; ++run) {
+                    const float* p = x + run0<DT>(c) + 32 * run;
+                    float sum = 0.f;
 #pragma unroll
-                for (int s = 0; s < kMaxSlots; ++s) {
-                    const int c = cb + s * LPR + gl;
-                    if (!row_ok || c >= nch) continue;
-                    Chunk kc;
-                    chunk_decode<DT>(c, rw[s], mw[s], kc);
-#pragma unroll
-                    for (int i = 0; i < kPairGroup; ++i) {
-                        if (p0 + i < u.npairs) {
-                            const int64_t pos = u.pos0 + p0 + i;
-                            acc[i] += chunk_dot<DT>(kc, a.act + pos * a.act_ld, a.asum16 + pos * as_ld);
-                        }
+                    for (int j = 0; j < 16; j += 4) {
+                        const float4 f = ld_f4(p + j);
+                        in.v[i][16 * run + j] = f.x;
+                        in.v[i][16 * run + j + 1] = f.y;
+                        in.v[i][16 * run + j + 2] = f.z;
+                        in.v[i][16 * run + j + 3] = f.w;
+                        sum += (f.x + f.y) + (f.z + f.w);
                     }
+                    in.s[i][run] = sum;
                 }
-            }
+            } else {
 #pragma unroll
-            for (int i = 0; i < kPairGroup; ++i) {
-                const float v = group_sum<LPR>(acc[i]);
-                if (gl == 0 && row_ok && p0 + i < u.npairs) a.y[(int64_t)(u.pos0 + p0 + i) * a.d + n] = v;
+                for (int j = 0; j < Layout<DT>::kVals; j += 4) {
+                    const float4 f = ld_f4(x + run0<DT>(c) + j);
+                    in.v[i][j] = f.x;
+                    in.v[i][j + 1] = f.y;
+                    in.v[i][j + 2] = f.z;
+                    in.v[i][j + 3] = f.w;
+                }
             }
         }
     }
+}
+
+// This lane's part of the row dot.
+template <int DT, int LPR, int CPL>
+__device__ __forceinline__ float row_dot(const RowRaw<DT, CPL>& w, const LaneInput<DT, CPL>& in, int gl, int nch) {
+    float acc = 0.f;
+#pragma unroll
+    for (int i = 0; i < CPL; ++i) {
+        const int c = gl + LPR * i;
+        if (c >= nch) continue;
+        const uint32_t raw[4] = {w.q[i][0].x, w.q[i][0].y, w.q[i][0].z, w.q[i][0].w};
+        if (DT == AERO_DT_Q4_K) {
+            const uint4 m = w.m[i];
+            const float d = __half2float(__ushort_as_half((unsigned short)(m.x & 0xFFFFu)));
+            const float dmin = __half2float(__ushort_as_half((unsigned short)(m.x >> 16)));
+            const int g = (c & 7) >> 1;
+#pragma unroll
+            for (int run = 0; run < 2; ++run) {
+                int sc, mn;
+                q4k_sc_m_words(m.y, m.z, m.w, 2 * g + run, sc, mn);
+                float s = 0.f;
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    float f[4];
+                    bytes4_to_f((run ? raw[k] >> 4 : raw[k]) & 0x0F0F0F0Fu, 8388608.0f, f);
+                    s = fmaf(f[0], in.v[i][16 * run + 4 * k], s);
+                    s = fmaf(f[1], in.v[i][16 * run + 4 * k + 1], s);
+                    s = fmaf(f[2], in.v[i][16 * run + 4 * k + 2], s);
+                    s = fmaf(f[3], in.v[i][16 * run + 4 * k + 3], s);
+                }
+                acc += (d * (float)sc) * s - (dmin * (float)mn) * in.s[i][run];
+            }
+        } else if (DT == AERO_DT_Q8_0) {
+            float s = 0.f;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                float f[4];
+                bytes4_to_f(raw[k] ^ 0x80808080u, 8388736.0f, f);  // signed byte q as q + 128
+                s = fmaf(f[0], in.v[i][4 * k], s);
+                s = fmaf(f[1], in.v[i][4 * k + 1], s);
+                s = fmaf(f[2], in.v[i][4 * k + 2], s);
+                s = fmaf(f[3], in.v[i][4 * k + 3], s);
+            }
+            acc = fmaf(__half2float(__ushort_as_half((unsigned short)w.sc[i])), s, acc);
+        } else {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                acc = fmaf(__uint_as_float(w.q[i][k].x), in.v[i][4 * k], acc);
+                acc = fmaf(__uint_as_float(w.q[i][k].y), in.v[i][4 * k + 1], acc);
+                acc = fmaf(__uint_as_float(w.q[i][k].z), in.v[i][4 * k + 2], acc);
+                acc = fmaf(__uint_as_float(w.q[i][k].w), in.v[i][4 * k + 3], acc);
+            }
+        }
+    }
+    return acc;
+}
+
+template <int LPR>
+__device__ __forceinline__ float lanes_sum(float v) {
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// gate/up: CTA = (unit, 32-row block, token of the unit). The warp's row slots
+// (32 / LPR rows at once) walk the block's rows; each slot streams the items
+// gate row j, up row j, gate row j', ... with the next item prefetched.
+template <int DT, int LPR, int CPL, bool SHARED>
+__global__ void __launch_bounds__(kWarps * 32) gateup_kernel(GemvArgs a, int rows_per_cta) {
+    constexpr int kSlots = 32 / LPR;
+    const int F = SHARED ? a.Fs : a.F;
+    const int row_blocks = (F + rows_per_cta - 1) / rows_per_cta;
+    UnitSrc u;
+    const int ui = SHARED ? 0 : (int)blockIdx.x / row_blocks;
+    if (!unit_of(a, ui, SHARED, u)) return;
+    const int rb = (int)blockIdx.x % row_blocks;
+    const QMat& G = SHARED ? a.sg : a.gate;
+    const QMat& U = SHARED ? a.su : a.up;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int slot = lane / LPR, gl = lane % LPR;
+    const int nch = Layout<DT>::chunks(a.d);
+    // tokens of the unit: blockIdx.y, blockIdx.y + gridDim.y, ...
+    for (int t = (int)blockIdx.y; t < u.npairs; t += (int)gridDim.y) {
+    const int64_t pos = u.pos0 + t;
+    LaneInput<DT, CPL> in;
+    input_load<DT, LPR, CPL>(a.x + (int64_t)token_of(a, u, (int)pos) * a.d, gl, nch, in);
+    const int j0 = rb * rows_per_cta + warp * kSlots + slot;
+    const int jstep = kWarps * kSlots;
+    const int jend = min(F, (rb + 1) * rows_per_cta);
+    const int n_items = 2 * ((rb * rows_per_cta + rows_per_cta - j0 + jstep - 1) / jstep);  // same count for every lane
+    auto item_row = [&](int it) { return j0 + (it >> 1) * jstep; };
+    RowRaw<DT, CPL> cur;
+    if (item_row(0) < jend) row_load<DT, LPR, CPL>(G, u.e, item_row(0), gl, nch, cur);
+    float g = 0.f;
+    for (int it = 0; it < n_items; ++it) {
+        const int j = item_row(it);
+        RowRaw<DT, CPL> nxt;
+        if (it + 1 < n_items && item_row(it + 1) < jend)
+            row_load<DT, LPR, CPL>((it + 1) & 1 ? U : G, u.e, item_row(it + 1), gl, nch, nxt);
+        float v = j < jend ? row_dot<DT, LPR, CPL>(cur, in, gl, nch) : 0.f;
+        v = lanes_sum<LPR>(v);
+        if (it & 1) {
+            if (j < jend && gl == 0) a.act[pos * a.act_ld + j] = silu_f(g) * v;
+        } else {
+            g = v;
+        }
+        cur = nxt;
+    }
+    }
+}
+
+// down: CTA = (unit, 32 output rows, token); y[pos][n] = down_n . act[pos].
+template <int DT, int LPR, int CPL, bool SHARED>
+__global__ void __launch_bounds__(kWarps * 32) down_kernel(GemvArgs a, int rows_per_cta) {
+    constexpr int kSlots = 32 / LPR;
+    const int K = SHARED ? a.Fs : a.F;
+    const int row_blocks = (a.d + rows_per_cta - 1) / rows_per_cta;
+    UnitSrc u;
+    const int ui = SHARED ? 0 : (int)blockIdx.x / row_blocks;
+    if (!unit_of(a, ui, SHARED, u)) return;
+    const int rb = (int)blockIdx.x % row_blocks;
+    const QMat& D = SHARED ? a.sd : a.down;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int slot = lane / LPR, gl = lane % LPR;
+    const int nch = Layout<DT>::chunks(K);
+    for (int t = (int)blockIdx.y; t < u.npairs; t += (int)gridDim.y) {
+    const int64_t pos = u.pos0 + t;
+    LaneInput<DT, CPL> in;
+    input_load<DT, LPR, CPL>(a.act + pos * a.act_ld, gl, nch, in);
+    const int n0 = rb * rows_per_cta + warp * kSlots + slot;
+    const int nstep = kWarps * kSlots;
+    const int nend = min(a.d, (rb + 1) * rows_per_cta);
+    RowRaw<DT, CPL> w;
+    if (n0 < nend) row_load<DT, LPR, CPL>(D, u.e, n0, gl, nch, w);
+    for (int n = n0; n < rb * rows_per_cta + rows_per_cta; n += nstep) {
+        const bool ok = n < nend;
+        RowRaw<DT, CPL> nx;
+        if (n + nstep < nend) row_load<DT, LPR, CPL>(D, u.e, n + nstep, gl, nch, nx);
+        float v = ok ? row_dot<DT, LPR, CPL>(w, in, gl, nch) : 0.f;
+        v = lanes_sum<LPR>(v);
+        if (ok && gl == 0) a.y[pos * a.d + n] = v;
+        w = nx;
+    }
+    }
+}
+
+// Lanes per row and chunks per lane for rows of K values: a full warp with up to
+// kMaxChunks chunks per lane, or fewer lanes with one chunk each for short rows.
+template <int DT>
+bool row_split(int K, int* lpr, int* cpl) {
+    const int nch = Layout<DT>::chunks(K);
+    if (nch <= 0) return false;
+    for (int l : {4, 8, 16}) {
+        if (nch <= l) {
+            *lpr = l;
+            *cpl = 1;
+            return true;
+        }
+    }
+    *lpr = 32;
+    *cpl = (nch + 31) / 32;
+    return *cpl <= kMaxChunks;
+}
+
+template <int DT, int LPR, int CPL>
+cudaError_t gemv_launch(const GemvArgs& a, bool shared, bool gateup, cudaStream_t s) {
+    const int rows = gateup ? (shared ? a.Fs : a.F) : a.d;
+    // rows per CTA: about 2048 CTAs over the launch's units (32 rows at least, so
+    // a few decode experts still spread over every SM; 256 at most)
+    const int units = shared ? 1 : std::max(1, a.max_active);
+    int rows_per_cta = 32;
+    while (rows_per_cta < 256 && (int64_t)units * ((rows + rows_per_cta - 1) / rows_per_cta) > 2048) rows_per_cta *= 2;
+    const int row_blocks = (rows + rows_per_cta - 1) / rows_per_cta;
+    // token slots in y: every shared-expert token; up to 4 for a routed expert (decode
+    // experts hold one or two), each CTA looping over the rest
+    const dim3 grid = shared ? dim3(row_blocks, a.Tsh) : dim3(a.max_active * row_blocks, std::min(a.max_pairs, 4));
+    if (grid.x == 0 || grid.y == 0) return cudaSuccess;
+    if (gateup) {
+        if (shared)
+            gateup_kernel<DT, LPR, CPL, true><<<grid, kWarps * 32, 0, s>>>(a, rows_per_cta);
+        else
+            gateup_kernel<DT, LPR, CPL, false><<<grid, kWarps * 32, 0, s>>>(a, rows_per_cta);
+    } else {
+        if (shared)
+            down_kernel<DT, LPR, CPL, true><<<grid, kWarps * 32, 0, s>>>(a, rows_per_cta);
+        else
+            down_kernel<DT, LPR, CPL, false><<<grid, kWarps * 32, 0, s>>>(a, rows_per_cta);
+    }
+    return cudaGetLastError();
+}
+
+template <int DT>
+cudaError_t gemv_dt(const GemvArgs& a, bool shared, bool gateup, cudaStream_t s) {
+    const int K = gateup ? a.d : (shared ? a.Fs : a.F);
+    int lpr = 0, cpl = 0;
+    if (!row_split<DT>(K, &lpr, &cpl)) return cudaErrorInvalidValue;
+    if (lpr == 4) return gemv_launch<DT, 4, 1>(a, shared, gateup, s);
+    if (lpr == 8) return gemv_launch<DT, 8, 1>(a, shared, gateup, s);
+    if (lpr == 16) return gemv_launch<DT, 16, 1>(a, shared, gateup, s);
+    switch (cpl) {
+        case 1: return gemv_launch<DT, 32, 1>(a, shared, gateup, s);
+        case 2: return gemv_launch<DT, 32, 2>(a, shared, gateup, s);
+        case 3: return gemv_launch<DT, 32, 3>(a, shared, gateup, s);
+        case 4: return gemv_launch<DT, 32, 4>(a, shared, gateup, s);
+    }
+    return cudaErrorInvalidValue;
 }
 
 template <int DT>
 cudaError_t gateup_dt(const GemvArgs& a, bool shared, cudaStream_t s) {
-    if (!shared) {
-        const int grid = a.max_active * (a.F / 16);
-        if (grid > 0) gateup_kernel<DT, false><<<grid, 128, 0, s>>>(a);
-    } else {
-        gateup_kernel<DT, true><<<a.Fs / 16, 128, 0, s>>>(a);
-    }
-    return cudaGetLastError();
+    return gemv_dt<DT>(a, shared, true, s);
 }
-
-int pick_lpr(int nch) { return nch >= 64 ? 32 : nch >= 32 ? 16 : 8; }
-
-template <int DT, int LPR>
-cudaError_t down_dt_lpr(const GemvArgs& a, bool shared, cudaStream_t s) {
-    const int rows_per_cta = 4 * (32 / LPR) * 2;
-    const int groups = (a.d + rows_per_cta - 1) / rows_per_cta;
-    if (!shared) {
-        const int grid = a.max_active * groups;
-        if (grid > 0) down_kernel<DT, LPR, false><<<grid, 128, 0, s>>>(a, rows_per_cta);
-    } else {
-        down_kernel<DT, LPR, true><<<groups, 128, 0, s>>>(a, rows_per_cta);
-    }
-    return cudaGetLastError();
-}
-
 template <int DT>
 cudaError_t down_dt(const GemvArgs& a, bool shared, cudaStream_t s) {
-    const int lpr = pick_lpr(qm_chunks_per_row(DT, shared ? a.Fs : a.F));
-    if (lpr == 32) return down_dt_lpr<DT, 32>(a, shared, s);
-    if (lpr == 16) return down_dt_lpr<DT, 16>(a, shared, s);
-    return down_dt_lpr<DT, 8>(a, shared, s);
+    return gemv_dt<DT>(a, shared, false, s);
 }
 
 cudaError_t gateup_any(int dtype, const GemvArgs& a, bool shared, cudaStream_t s) {

@@ -18,10 +18,9 @@ cudaError_t launch_router(const float* x, int T, int d, const float* W, int row_
                           const float* bias, int n_bias, float* logits, int ld, cudaStream_t s);
 
 // Top-k over logits[t][0..E) (row stride ld): idx/w (T, k), sgate[t] =
-// sigmoid(logits[t][E]) when has_shared, xsum16[t][d/16] sums of x (may be null).
-cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int norm, int has_shared,
-                        const float* x, int d, int32_t* idx, float* w, float* sgate, float* xsum16,
-                        cudaStream_t s);
+// sigmoid(logits[t][E]) when has_shared.
+cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int norm, int has_shared, int32_t* idx,
+                        float* w, float* sgate, cudaStream_t s);
 
 // Dispatch: expert-contiguous permutation of the T*k pairs. Writes offsets[E+1],
 // perm[P] (sorted position -> pair), inv[P] (pair -> sorted position), the active
@@ -38,16 +37,15 @@ struct GemvArgs {
     QMat gate, up, down;     // routed experts
     QMat sg, su, sd;         // shared expert (n_expert 1), valid when has_shared
     const float* x;          // (T, d)
-    const float* xsum16;     // (T, d/16)
     const int32_t* perm;
     const int32_t* act_e;
     const int32_t* act_off;
     const int32_t* n_active;
     int T, k, d, F, Fs, has_shared, max_active;
+    int max_pairs;           // upper bound on the pairs of one routed expert (min(T, ...))
     int Tsh;                 // the shared expert runs on tokens [0, Tsh)
     int act_ld;              // row stride of act (>= max(F, Fs))
     float* act;              // (P + T, act_ld)
-    float* asum16;           // (P + T, act_ld/16)
     float* y;                // (P + T, d)
 };
 cudaError_t launch_gemv_gateup(const GemvArgs& a, cudaStream_t s);
@@ -81,7 +79,6 @@ cudaError_t launch_ep_pack(const float* x, int T, int dp, int k, const int32_t* 
 // Receiver side: metadata -> idx (bucket E for slots owned elsewhere), w, sgate.
 cudaError_t launch_ep_prep(const int32_t* meta, int meta_ld, int R, int k, int Tsh, int e_begin, int e_end, int E,
                            int32_t* idx, float* w, float* sgate, int32_t* bad, cudaStream_t s);
-cudaError_t launch_xsum16(const float* x, int R, int dp, float* xsum16, cudaStream_t s);
 // out[t] = self_out[t] + sum over remote ranks (ascending) of back[pos[t][r]].
 cudaError_t launch_ep_combine(const float* self_out, const float* back, const int32_t* pos, int T, int n, int me,
                               int dp, float* out, cudaStream_t s);

@@ -48,7 +48,7 @@ struct Scratch {
     int cap_T = 0;
     void* base = nullptr;
     size_t bytes = 0;
-    float *x_stage, *out_stage, *lg_stage, *logits, *w, *sgate, *xsum16, *act, *asum16, *y;
+    float *x_stage, *out_stage, *lg_stage, *logits, *w, *sgate, *act, *y;
     int32_t *idx, *offsets, *perm, *inv, *act_e, *act_off, *n_active, *ep_bad, *tc_err;
     void* dwork;
     void* gemm_ws;
@@ -238,11 +238,10 @@ bool ensure_scratch(Handle& h, int T) {
     const size_t o_x = take((size_t)cap * h.dp * 4), o_out = take((size_t)cap * h.dp * 4);
     const size_t o_lgs = take((size_t)cap * h.E * 4);
     const size_t o_lg = take((size_t)cap * h.lg_ld * 4), o_w = take((size_t)P * 4), o_sg = take((size_t)cap * 4);
-    const size_t o_xs = take((size_t)cap * (h.dp / 16) * 4);
     // the f32 GEMV buffers only need to cover calls that take the GEMV path
     const int64_t gemv_T = h.gemm_ok ? std::min<int64_t>(cap, h.gemm_min_tokens) : cap;
     const int64_t grows = gemv_T * h.k + gemv_T;
-    const size_t o_act = take((size_t)grows * h.act_ld * 4), o_as = take((size_t)grows * (h.act_ld / 16) * 4);
+    const size_t o_act = take((size_t)grows * h.act_ld * 4);
     const size_t o_y = take((size_t)grows * h.dp * 4);
     const size_t o_idx = take((size_t)P * 4), o_off = take((size_t)(h.E + 2) * 4), o_perm = take((size_t)P * 4);
     const size_t o_inv = take((size_t)P * 4), o_ae = take((size_t)h.E * 4), o_ao = take((size_t)(h.E + 1) * 4);
@@ -272,9 +271,7 @@ bool ensure_scratch(Handle& h, int T) {
     s.logits = (float*)(b + o_lg);
     s.w = (float*)(b + o_w);
     s.sgate = (float*)(b + o_sg);
-    s.xsum16 = (float*)(b + o_xs);
     s.act = (float*)(b + o_act);
-    s.asum16 = (float*)(b + o_as);
     s.y = (float*)(b + o_y);
     s.idx = (int32_t*)(b + o_idx);
     s.offsets = (int32_t*)(b + o_off);
@@ -316,10 +313,10 @@ bool router_logits_dev(Handle& h, const float* x, int T, bool with_gate) {
                      "router");
 }
 
-// Router projection + top-k for T tokens of x (T, dp): s.idx, s.w, s.sgate,
-// s.xsum16. When logits_in is non-null it holds (T, E) caller logits on the
+// Router projection + top-k for T tokens of x (T, dp): s.idx, s.w, s.sgate.
+// When logits_in is non-null it holds (T, E) caller logits on the
 // device (row stride E).
-bool route_stage(Handle& h, const float* x, int T, const float* logits_in, bool need_xsum16) {
+bool route_stage(Handle& h, const float* x, int T, const float* logits_in) {
     Scratch& s = h.sc;
     cudaStream_t st = h.stream;
     const int ld = h.lg_ld;
@@ -338,9 +335,7 @@ bool route_stage(Handle& h, const float* x, int T, const float* logits_in, bool 
     }
     h.launches += (!logits_in || h.has_shared) ? 1 : 0;
     h.mark(1);
-    if (!h.cuda_ok(launch_topk(s.logits, ld, T, h.E, h.k, h.norm, h.has_shared, x, h.dp, s.idx, s.w, s.sgate,
-                               need_xsum16 ? s.xsum16 : nullptr, st),
-                   "top-k"))
+    if (!h.cuda_ok(launch_topk(s.logits, ld, T, h.E, h.k, h.norm, h.has_shared, s.idx, s.w, s.sgate, st), "top-k"))
         return false;
     h.launches += 1;
     h.mark(2);
@@ -416,7 +411,6 @@ bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool ski
         a.su = h.su;
         a.sd = h.sd;
         a.x = static_cast<const float*>(x);
-        a.xsum16 = s.xsum16;
         a.perm = s.perm;
         a.act_e = s.act_e;
         a.act_off = s.act_off;
@@ -429,9 +423,9 @@ bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool ski
         a.Fs = h.Fsp;
         a.has_shared = h.has_shared;
         a.max_active = std::min(P, h.E);
+        a.max_pairs = T;  // a token selects an expert at most once
         a.act_ld = h.act_ld;
         a.act = s.act;
-        a.asum16 = s.asum16;
         a.y = s.y;
         if (!h.cuda_ok(launch_gemv_gateup(a, st), "gate/up")) return false;
         h.mark(4);
@@ -464,9 +458,7 @@ bool finish_profile(Handle& h) {
 
 // Core pipeline on device buffers: x (T, dp), out (T, dp).
 bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* out) {
-    // the per-16 sums of x only serve the GEMV path
-    const bool gemv = !(h.gemm_ok && h.gb_ready && T >= h.gemm_min_tokens);
-    if (!route_stage(h, x, T, logits_in, gemv)) return false;
+    if (!route_stage(h, x, T, logits_in)) return false;
     if (!expert_stage(h, x, false, T, T, false, out)) return false;
     return finish_profile(h);
 }
@@ -784,7 +776,7 @@ static int route_impl(const float* logits, int T, int E, int k, int norm, int64_
     float* dw = (float*)((char*)didx + ((i_b + 255) & ~(size_t)255));
     bool ok = cudaMemcpyAsync(dlg, logits, lg_b, aero::is_device_ptr(logits) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
                               st) == cudaSuccess;
-    ok = ok && aero::launch_topk(dlg, E, T, E, k, norm, 0, nullptr, 0, didx, dw, nullptr, nullptr, st) == cudaSuccess;
+    ok = ok && aero::launch_topk(dlg, E, T, E, k, norm, 0, didx, dw, nullptr, st) == cudaSuccess;
     std::vector<int32_t> hidx((size_t)T * k);
     ok = ok && cudaMemcpyAsync(hidx.data(), didx, i_b, cudaMemcpyDeviceToHost, st) == cudaSuccess;
     const bool w_dev = aero::is_device_ptr(w);
@@ -1052,7 +1044,7 @@ int aero_cuda_ep_dispatch(void* handle, const float* x, int T, int n_ranks, int 
     cudaSetDevice(h->device);
     if (!aero::ensure_scratch(*h, std::max(T, 1))) return -1;
     auto& s = h->sc;
-    if (T > 0 && !aero::route_stage(*h, x, T, nullptr, false)) return -1;
+    if (T > 0 && !aero::route_stage(*h, x, T, nullptr)) return -1;
     // the plan reuses the dispatch buffers: perm holds send_tok, inv send_rank
     if (!h->cuda_ok(aero::launch_ep_plan(s.idx, T, h->k, rt, rank, s.perm, s.inv, counts, pos, h->stream), "exchange plan"))
         return -1;
@@ -1089,12 +1081,6 @@ int aero_cuda_ep_expert_block(void* handle, const void* rows, int row_dtype, con
                     "exchange unpack"))
         return -1;
     h->launches += 1;
-    const bool gemv = !f16 && !(h->gemm_ok && h->gb_ready && R >= h->gemm_min_tokens);
-    if (gemv) {
-        if (!h->cuda_ok(aero::launch_xsum16(static_cast<const float*>(rows), R, h->dp, s.xsum16, h->stream), "row sums"))
-            return -1;
-        h->launches += 1;
-    }
     h->mark(2);
     if (!aero::expert_stage(*h, rows, f16, R, n_shared, true, out)) return -1;
     return aero::finish_profile(*h) ? 0 : -1;

@@ -133,10 +133,8 @@ __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
 
 template <int PER>  // values per lane: E <= 32 * PER
 __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int ld, int T, int E,
-                                                   int k, int norm, int has_shared,
-                                                   const float* __restrict__ x, int d, int32_t* __restrict__ idx,
-                                                   float* __restrict__ w, float* __restrict__ sgate,
-                                                   float* __restrict__ xsum16) {
+                                                   int k, int norm, int has_shared, int32_t* __restrict__ idx,
+                                                   float* __restrict__ w, float* __restrict__ sgate) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * 8 + warp;
     if (t >= T) return;
@@ -200,21 +198,6 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
         if (lane < k) w[(int64_t)t * k + lane] = (float)((double)expf(sel_v - mx) / den);
     }
     if (has_shared && lane == 0) sgate[t] = sigmoid_f(lg[E]);
-    if (xsum16) {
-        const float* xt = x + (int64_t)t * d;
-        for (int g = lane; g < d / 16; g += 32) {
-            float s = 0.f;
-#pragma unroll
-            for (int i = 0; i < 16; i += 4) {
-                const float4 q = ld_f4(xt + 16 * g + i);
-                s += q.x;
-                s += q.y;
-                s += q.z;
-                s += q.w;
-            }
-            xsum16[(int64_t)t * (d / 16) + g] = s;
-        }
-    }
 }
 
 // ---------------------------------------------------------------- dispatch
@@ -339,23 +322,22 @@ cudaError_t launch_router(const float* x, int T, int d, const float* W, int row_
     return cudaGetLastError();
 }
 
-cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int norm, int has_shared,
-                        const float* x, int d, int32_t* idx, float* w, float* sgate, float* xsum16,
-                        cudaStream_t s) {
+cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int norm, int has_shared, int32_t* idx,
+                        float* w, float* sgate, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
     const unsigned grid = (unsigned)((T + 7) / 8);
     if (E <= 32)
-        topk_kernel<1><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, x, d, idx, w, sgate, xsum16);
+        topk_kernel<1><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate);
     else if (E <= 64)
-        topk_kernel<2><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, x, d, idx, w, sgate, xsum16);
+        topk_kernel<2><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate);
     else if (E <= 128)
-        topk_kernel<4><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, x, d, idx, w, sgate, xsum16);
+        topk_kernel<4><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate);
     else if (E <= 256)
-        topk_kernel<8><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, x, d, idx, w, sgate, xsum16);
+        topk_kernel<8><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate);
     else if (E <= 512)
-        topk_kernel<16><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, x, d, idx, w, sgate, xsum16);
+        topk_kernel<16><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate);
     else
-        topk_kernel<32><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, x, d, idx, w, sgate, xsum16);
+        topk_kernel<32><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate);
     return cudaGetLastError();
 }
 
