@@ -112,6 +112,51 @@ __device__ __forceinline__ void q4k_sc_m_words(uint32_t w0, uint32_t w1, uint32_
     }
 }
 
+// One 32-value block of an input row into its integer form (see QInput):
+// writes q1[0..32), q0[0..32), *sx and s16[0..2). Called by one thread.
+__device__ __forceinline__ void qinput_block(const float* x, int8_t* q1, int8_t* q0, float* sx, float* s16) {
+    float v[32];
+    float mx = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+        const float4 f = *reinterpret_cast<const float4*>(x + i);
+        v[i] = f.x;
+        v[i + 1] = f.y;
+        v[i + 2] = f.z;
+        v[i + 3] = f.w;
+    }
+    float a = 0.f, b = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) a += v[i];
+#pragma unroll
+    for (int i = 16; i < 32; ++i) b += v[i];
+    s16[0] = a;
+    s16[1] = b;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) mx = fmaxf(mx, fabsf(v[i]));
+    const float inv = mx > 0.f ? 16383.0f / mx : 0.f;
+    *sx = mx / 16383.0f;
+    uint32_t w1[8], w0[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        uint32_t p1 = 0, p0 = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int q = __float2int_rn(v[4 * i + j] * inv);  // |q| <= 16383
+            p1 |= (uint32_t)(q >> 7 & 0xFF) << (8 * j);
+            p0 |= (uint32_t)(q & 127) << (8 * j);
+        }
+        w1[i] = p1;
+        w0[i] = p0;
+    }
+    uint4* d1 = reinterpret_cast<uint4*>(q1);
+    uint4* d0 = reinterpret_cast<uint4*>(q0);
+    d1[0] = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+    d1[1] = make_uint4(w1[4], w1[5], w1[6], w1[7]);
+    d0[0] = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+    d0[1] = make_uint4(w0[4], w0[5], w0[6], w0[7]);
+}
+
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 

@@ -10,13 +10,17 @@
 // code chunks (coalesced streaming loads, the next row's chunks prefetched into
 // registers), and each lane keeps the input values matching its chunks in
 // registers for the whole CTA, so the only per-row traffic is the weights. A
-// CTA owns one unit (an active expert, or the shared expert) x 32 rows x one
-// token; tokens of a unit take successive passes (decode units hold 1-2). Per
-// 32-value sub-block the products follow the reference factorisation of the
+// CTA owns one unit (an active expert, or the shared expert) x a block of rows
+// x one token; tokens of a unit take successive passes (decode units hold 1-2).
+// Per 32-value sub-block the products follow the reference factorisation of the
 // quantised dot (src/kernels.cpp:78-84, 123-156):
 //   Q8_0: d * sum(q x)            Q4_K: d sc * sum(q x) - dmin m * sum(x)
-// Codes become floats by a byte permute into the mantissa of 2^23 and one
-// subtraction (exact).
+// For the quantised families the input rows come in integer form (QInput: a
+// 15-bit code per value split into two int8 planes, one f32 scale per 32
+// values, exact f32 sums per 16), so sum(q x) is two chains of dp4a over the
+// raw code bytes: no per-value conversion. Its relative error is bounded by
+// 2^-15 of the block's largest input; accumulation is f32. F32 experts take a
+// plain f32 dot.
 #include <algorithm>
 
 #include "internal.h"
@@ -138,47 +142,63 @@ __device__ __forceinline__ void row_load(const QMat& M, int e, int r, int gl, in
     }
 }
 
-// The lane's input values for its chunks (and, for Q4_K, their run sums).
+// The lane's input for its chunks. F32: the values. Q8_0 / Q4_K: per 16-value
+// run the two int8 code planes (4 words each), the block scale and the exact
+// sum of the run.
 template <int DT, int CPL>
 struct LaneInput {
-    float v[CPL][Layout<DT>::kVals];
-    float s[DT == AERO_DT_Q4_K ? CPL : 1][2];
+    static constexpr int kRuns = DT == AERO_DT_Q4_K ? 2 : 1;
+    float v[DT == AERO_DT_F32 ? CPL : 1][DT == AERO_DT_F32 ? 16 : 1];
+    uint32_t hi[DT == AERO_DT_F32 ? 1 : CPL][kRuns][4], lo[DT == AERO_DT_F32 ? 1 : CPL][kRuns][4];
+    float sx[DT == AERO_DT_F32 ? 1 : CPL][kRuns], s16[DT == AERO_DT_F32 ? 1 : CPL][kRuns];
 };
 
 template <int DT, int LPR, int CPL>
-__device__ __forceinline__ void input_load(const float* x, int gl, int nch, LaneInput<DT, CPL>& in) {
+__device__ __forceinline__ void input_load(const float* x, const QInput& q, int64_t row, int gl, int nch,
+                                           LaneInput<DT, CPL>& in) {
 #pragma unroll
     for (int i = 0; i < CPL; ++i) {
         const int c = gl + LPR * i;
-        if (c < nch) {
-            if (DT == AERO_DT_Q4_K) {
+        if (c >= nch) continue;
+        if (DT == AERO_DT_F32) {
 #pragma unroll
-                for (int run = 0; run < 2; ++run) {
-                    const float* p = x + run0<DT>(c) + 32 * run;
-                    float sum = 0.f;
+            for (int j = 0; j < 16; j += 4) {
+                const float4 f = ld_f4(x + row * q.K + run0<DT>(c) + j);
+                in.v[i][j] = f.x;
+                in.v[i][j + 1] = f.y;
+                in.v[i][j + 2] = f.z;
+                in.v[i][j + 3] = f.w;
+            }
+        } else {
 #pragma unroll
-                    for (int j = 0; j < 16; j += 4) {
-                        const float4 f = ld_f4(p + j);
-                        in.v[i][16 * run + j] = f.x;
-                        in.v[i][16 * run + j + 1] = f.y;
-                        in.v[i][16 * run + j + 2] = f.z;
-                        in.v[i][16 * run + j + 3] = f.w;
-                        sum += (f.x + f.y) + (f.z + f.w);
-                    }
-                    in.s[i][run] = sum;
-                }
-            } else {
-#pragma unroll
-                for (int j = 0; j < Layout<DT>::kVals; j += 4) {
-                    const float4 f = ld_f4(x + run0<DT>(c) + j);
-                    in.v[i][j] = f.x;
-                    in.v[i][j + 1] = f.y;
-                    in.v[i][j + 2] = f.z;
-                    in.v[i][j + 3] = f.w;
-                }
+            for (int r = 0; r < LaneInput<DT, CPL>::kRuns; ++r) {
+                const int v0 = run0<DT>(c) + 32 * r;  // first value of the run
+                const uint4 h = __ldg(reinterpret_cast<const uint4*>(q.q1 + row * q.K + v0));
+                const uint4 l = __ldg(reinterpret_cast<const uint4*>(q.q0 + row * q.K + v0));
+                in.hi[i][r][0] = h.x;
+                in.hi[i][r][1] = h.y;
+                in.hi[i][r][2] = h.z;
+                in.hi[i][r][3] = h.w;
+                in.lo[i][r][0] = l.x;
+                in.lo[i][r][1] = l.y;
+                in.lo[i][r][2] = l.z;
+                in.lo[i][r][3] = l.w;
+                in.sx[i][r] = __ldg(q.sx + row * (q.K / 32) + (v0 >> 5));
+                in.s16[i][r] = __ldg(q.s16 + row * (q.K / 16) + (v0 >> 4));
             }
         }
     }
+}
+
+// sum over 16 values of code * input code (128 hi + lo), from 4 words of code bytes.
+__device__ __forceinline__ int dot16(const uint32_t (&w)[4], const uint32_t (&hi)[4], const uint32_t (&lo)[4]) {
+    int a = 0, b = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        a = __dp4a((int)w[k], (int)hi[k], a);
+        b = __dp4a((int)w[k], (int)lo[k], b);
+    }
+    return a * 128 + b;
 }
 
 // This lane's part of the row dot.
@@ -196,33 +216,19 @@ __device__ __forceinline__ float row_dot(const RowRaw<DT, CPL>& w, const LaneInp
             const float dmin = __half2float(__ushort_as_half((unsigned short)(m.x >> 16)));
             const int g = (c & 7) >> 1;
 #pragma unroll
-            for (int run = 0; run < 2; ++run) {
+            for (int r = 0; r < 2; ++r) {
+                // run r: low (r = 0) or high nibbles of the chunk, sub-block 2g + r
                 int sc, mn;
-                q4k_sc_m_words(m.y, m.z, m.w, 2 * g + run, sc, mn);
-                float s = 0.f;
+                q4k_sc_m_words(m.y, m.z, m.w, 2 * g + r, sc, mn);
+                uint32_t nib[4];
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    float f[4];
-                    bytes4_to_f((run ? raw[k] >> 4 : raw[k]) & 0x0F0F0F0Fu, 8388608.0f, f);
-                    s = fmaf(f[0], in.v[i][16 * run + 4 * k], s);
-                    s = fmaf(f[1], in.v[i][16 * run + 4 * k + 1], s);
-                    s = fmaf(f[2], in.v[i][16 * run + 4 * k + 2], s);
-                    s = fmaf(f[3], in.v[i][16 * run + 4 * k + 3], s);
-                }
-                acc += (d * (float)sc) * s - (dmin * (float)mn) * in.s[i][run];
+                for (int k = 0; k < 4; ++k) nib[k] = (r ? raw[k] >> 4 : raw[k]) & 0x0F0F0F0Fu;
+                const int sq = dot16(nib, in.hi[i][r], in.lo[i][r]);
+                acc += (d * (float)sc) * in.sx[i][r] * (float)sq - (dmin * (float)mn) * in.s16[i][r];
             }
         } else if (DT == AERO_DT_Q8_0) {
-            float s = 0.f;
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                float f[4];
-                bytes4_to_f(raw[k] ^ 0x80808080u, 8388736.0f, f);  // signed byte q as q + 128
-                s = fmaf(f[0], in.v[i][4 * k], s);
-                s = fmaf(f[1], in.v[i][4 * k + 1], s);
-                s = fmaf(f[2], in.v[i][4 * k + 2], s);
-                s = fmaf(f[3], in.v[i][4 * k + 3], s);
-            }
-            acc = fmaf(__half2float(__ushort_as_half((unsigned short)w.sc[i])), s, acc);
+            const int sq = dot16(raw, in.hi[i][0], in.lo[i][0]);
+            acc = fmaf(__half2float(__ushort_as_half((unsigned short)w.sc[i])) * in.sx[i][0], (float)sq, acc);
         } else {
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
@@ -247,7 +253,7 @@ __device__ __forceinline__ float lanes_sum(float v) {
 // (32 / LPR rows at once) walk the block's rows; each slot streams the items
 // gate row j, up row j, gate row j', ... with the next item prefetched.
 template <int DT, int LPR, int CPL, bool SHARED>
-__global__ void __launch_bounds__(kWarps * 32) gateup_kernel(GemvArgs a, int rows_per_cta) {
+__global__ void __launch_bounds__(kWarps * 32, 2) gateup_kernel(GemvArgs a, int rows_per_cta) {
     constexpr int kSlots = 32 / LPR;
     const int F = SHARED ? a.Fs : a.F;
     const int row_blocks = (F + rows_per_cta - 1) / rows_per_cta;
@@ -260,11 +266,12 @@ __global__ void __launch_bounds__(kWarps * 32) gateup_kernel(GemvArgs a, int row
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int slot = lane / LPR, gl = lane % LPR;
     const int nch = Layout<DT>::chunks(a.d);
+    __shared__ __align__(16) float act_s[256];  // this block's act values of the current token
     // tokens of the unit: blockIdx.y, blockIdx.y + gridDim.y, ...
     for (int t = (int)blockIdx.y; t < u.npairs; t += (int)gridDim.y) {
     const int64_t pos = u.pos0 + t;
     LaneInput<DT, CPL> in;
-    input_load<DT, LPR, CPL>(a.x + (int64_t)token_of(a, u, (int)pos) * a.d, gl, nch, in);
+    input_load<DT, LPR, CPL>(a.x, a.xq, token_of(a, u, (int)pos), gl, nch, in);
     const int j0 = rb * rows_per_cta + warp * kSlots + slot;
     const int jstep = kWarps * kSlots;
     const int jend = min(F, (rb + 1) * rows_per_cta);
@@ -281,18 +288,33 @@ __global__ void __launch_bounds__(kWarps * 32) gateup_kernel(GemvArgs a, int row
         float v = j < jend ? row_dot<DT, LPR, CPL>(cur, in, gl, nch) : 0.f;
         v = lanes_sum<LPR>(v);
         if (it & 1) {
-            if (j < jend && gl == 0) a.act[pos * a.act_ld + j] = silu_f(g) * v;
+            if (j < jend && gl == 0) {
+                const float h = silu_f(g) * v;
+                a.act[pos * a.act_ld + j] = h;
+                if (DT != AERO_DT_F32) act_s[j - rb * rows_per_cta] = h;
+            }
         } else {
             g = v;
         }
         cur = nxt;
+    }
+    if (DT != AERO_DT_F32) {
+        // the block's act values (whole 32-row blocks: rows_per_cta and F are
+        // multiples of 32) as integer input of the down product
+        __syncthreads();
+        for (int b = threadIdx.x; b * 32 < jend - rb * rows_per_cta; b += blockDim.x) {
+            const int j = rb * rows_per_cta + 32 * b;
+            qinput_block(act_s + 32 * b, a.aq.q1 + pos * a.aq.K + j, a.aq.q0 + pos * a.aq.K + j,
+                         a.aq.sx + pos * (a.aq.K / 32) + (j >> 5), a.aq.s16 + pos * (a.aq.K / 16) + (j >> 4));
+        }
+        __syncthreads();
     }
     }
 }
 
 // down: CTA = (unit, 32 output rows, token); y[pos][n] = down_n . act[pos].
 template <int DT, int LPR, int CPL, bool SHARED>
-__global__ void __launch_bounds__(kWarps * 32) down_kernel(GemvArgs a, int rows_per_cta) {
+__global__ void __launch_bounds__(kWarps * 32, 2) down_kernel(GemvArgs a, int rows_per_cta) {
     constexpr int kSlots = 32 / LPR;
     const int K = SHARED ? a.Fs : a.F;
     const int row_blocks = (a.d + rows_per_cta - 1) / rows_per_cta;
@@ -307,7 +329,7 @@ __global__ void __launch_bounds__(kWarps * 32) down_kernel(GemvArgs a, int rows_
     for (int t = (int)blockIdx.y; t < u.npairs; t += (int)gridDim.y) {
     const int64_t pos = u.pos0 + t;
     LaneInput<DT, CPL> in;
-    input_load<DT, LPR, CPL>(a.act + pos * a.act_ld, gl, nch, in);
+    input_load<DT, LPR, CPL>(a.act, a.aq, pos, gl, nch, in);
     const int n0 = rb * rows_per_cta + warp * kSlots + slot;
     const int nstep = kWarps * kSlots;
     const int nend = min(a.d, (rb + 1) * rows_per_cta);

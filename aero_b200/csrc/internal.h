@@ -17,10 +17,40 @@ namespace aero {
 cudaError_t launch_router(const float* x, int T, int d, const float* W, int row_begin, int row_end,
                           const float* bias, int n_bias, float* logits, int ld, cudaStream_t s);
 
+// Input rows of the decode GEMVs in integer form: per 32-value block b of a row,
+// x ~= sx[b] * (128 * q1 + q0) with q1 in [-128, 127] and q0 in [0, 127] (a
+// 15-bit code split into two int8 planes, so quant codes meet it in dp4a), plus
+// the exact f32 sums of every 16 values (the Q4_K min term). Rows of K values:
+// q1, q0 K bytes each, sx K/32 and s16 K/16 floats.
+struct QInput {
+    int8_t* q1;
+    int8_t* q0;
+    float* sx;
+    float* s16;
+    int K;  // values per row
+};
+inline size_t qinput_bytes(int rows, int K) {
+    return (size_t)rows * ((size_t)2 * K + (size_t)K / 32 * 4 + (size_t)K / 16 * 4);
+}
+// Carves a QInput for `rows` rows of K values out of `base` (qinput_bytes long, 16-byte aligned).
+inline QInput qinput_at(void* base, int rows, int K) {
+    char* b = static_cast<char*>(base);
+    QInput q;
+    q.q1 = reinterpret_cast<int8_t*>(b);
+    q.q0 = reinterpret_cast<int8_t*>(b + (size_t)rows * K);
+    q.sx = reinterpret_cast<float*>(b + (size_t)2 * rows * K);
+    q.s16 = reinterpret_cast<float*>(b + (size_t)2 * rows * K + (size_t)rows * (K / 32) * 4);
+    q.K = K;
+    return q;
+}
+// Quantises R rows of x (row stride ld floats) into q (K = q.K values per row).
+cudaError_t launch_qinput(const float* x, int R, int ld, QInput q, cudaStream_t s);
+
 // Top-k over logits[t][0..E) (row stride ld): idx/w (T, k), sgate[t] =
-// sigmoid(logits[t][E]) when has_shared.
+// sigmoid(logits[t][E]) when has_shared. With xq.q1 non-null, also writes token
+// t's row of x (T, xq.K) as integer input.
 cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int norm, int has_shared, int32_t* idx,
-                        float* w, float* sgate, cudaStream_t s);
+                        float* w, float* sgate, const float* x, QInput xq, cudaStream_t s);
 
 // Dispatch: expert-contiguous permutation of the T*k pairs. Writes offsets[E+1],
 // perm[P] (sorted position -> pair), inv[P] (pair -> sorted position), the active
@@ -37,6 +67,8 @@ struct GemvArgs {
     QMat gate, up, down;     // routed experts
     QMat sg, su, sd;         // shared expert (n_expert 1), valid when has_shared
     const float* x;          // (T, d)
+    QInput xq;               // x rows as integer input (T rows, K = d), for quantised experts
+    QInput aq;               // act rows as integer input (P + T rows, K = act_ld), written by gate/up
     const int32_t* perm;
     const int32_t* act_e;
     const int32_t* act_off;

@@ -51,6 +51,7 @@ struct Scratch {
     float *x_stage, *out_stage, *lg_stage, *logits, *w, *sgate, *act, *y;
     int32_t *idx, *offsets, *perm, *inv, *act_e, *act_off, *n_active, *ep_bad, *tc_err;
     void* dwork;
+    QInput xq{}, aq{};  // GEMV inputs in integer form (null planes for F32 experts)
     void* gemm_ws;
     size_t gemm_ws_bytes = 0;
     int gemv_cap = 0;
@@ -242,6 +243,10 @@ bool ensure_scratch(Handle& h, int T) {
     const int64_t gemv_T = h.gemm_ok ? std::min<int64_t>(cap, h.gemm_min_tokens) : cap;
     const int64_t grows = gemv_T * h.k + gemv_T;
     const size_t o_act = take((size_t)grows * h.act_ld * 4);
+    // integer forms of the GEMV inputs (quantised experts): x rows, act rows
+    const bool qin = h.dtype != AERO_DT_F32;
+    const size_t o_xq = take(qin ? qinput_bytes((int)gemv_T, h.dp) : 0);
+    const size_t o_aq = take(qin ? qinput_bytes((int)grows, h.act_ld) : 0);
     const size_t o_y = take((size_t)grows * h.dp * 4);
     const size_t o_idx = take((size_t)P * 4), o_off = take((size_t)(h.E + 2) * 4), o_perm = take((size_t)P * 4);
     const size_t o_inv = take((size_t)P * 4), o_ae = take((size_t)h.E * 4), o_ao = take((size_t)(h.E + 1) * 4);
@@ -286,6 +291,14 @@ bool ensure_scratch(Handle& h, int T) {
     s.gemm_ws = b + o_gw;
     s.gemm_ws_bytes = gws;
     s.gemv_cap = (int)gemv_T;
+    s.xq = QInput{};
+    s.aq = QInput{};
+    s.xq.K = h.dp;
+    s.aq.K = h.act_ld;
+    if (qin) {
+        s.xq = qinput_at(b + o_xq, (int)gemv_T, h.dp);
+        s.aq = qinput_at(b + o_aq, (int)grows, h.act_ld);
+    }
     h.gb_ready = false;
     if (h.gemm_ok) {
         std::string why;
@@ -316,7 +329,7 @@ bool router_logits_dev(Handle& h, const float* x, int T, bool with_gate) {
 // Router projection + top-k for T tokens of x (T, dp): s.idx, s.w, s.sgate.
 // When logits_in is non-null it holds (T, E) caller logits on the
 // device (row stride E).
-bool route_stage(Handle& h, const float* x, int T, const float* logits_in) {
+bool route_stage(Handle& h, const float* x, int T, const float* logits_in, bool qx) {
     Scratch& s = h.sc;
     cudaStream_t st = h.stream;
     const int ld = h.lg_ld;
@@ -335,7 +348,9 @@ bool route_stage(Handle& h, const float* x, int T, const float* logits_in) {
     }
     h.launches += (!logits_in || h.has_shared) ? 1 : 0;
     h.mark(1);
-    if (!h.cuda_ok(launch_topk(s.logits, ld, T, h.E, h.k, h.norm, h.has_shared, s.idx, s.w, s.sgate, st), "top-k"))
+    // the GEMV path reads x in integer form; top-k writes it in the same pass
+    QInput xq = qx ? s.xq : QInput{};
+    if (!h.cuda_ok(launch_topk(s.logits, ld, T, h.E, h.k, h.norm, h.has_shared, s.idx, s.w, s.sgate, x, xq, st), "top-k"))
         return false;
     h.launches += 1;
     h.mark(2);
@@ -411,6 +426,8 @@ bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool ski
         a.su = h.su;
         a.sd = h.sd;
         a.x = static_cast<const float*>(x);
+        a.xq = s.xq;
+        a.aq = s.aq;
         a.perm = s.perm;
         a.act_e = s.act_e;
         a.act_off = s.act_off;
@@ -458,7 +475,8 @@ bool finish_profile(Handle& h) {
 
 // Core pipeline on device buffers: x (T, dp), out (T, dp).
 bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* out) {
-    if (!route_stage(h, x, T, logits_in)) return false;
+    const bool gemv = !(h.gemm_ok && h.gb_ready && T >= h.gemm_min_tokens);
+    if (!route_stage(h, x, T, logits_in, gemv && h.sc.xq.q1 != nullptr)) return false;
     if (!expert_stage(h, x, false, T, T, false, out)) return false;
     return finish_profile(h);
 }
@@ -776,7 +794,7 @@ static int route_impl(const float* logits, int T, int E, int k, int norm, int64_
     float* dw = (float*)((char*)didx + ((i_b + 255) & ~(size_t)255));
     bool ok = cudaMemcpyAsync(dlg, logits, lg_b, aero::is_device_ptr(logits) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
                               st) == cudaSuccess;
-    ok = ok && aero::launch_topk(dlg, E, T, E, k, norm, 0, didx, dw, nullptr, st) == cudaSuccess;
+    ok = ok && aero::launch_topk(dlg, E, T, E, k, norm, 0, didx, dw, nullptr, nullptr, aero::QInput{}, st) == cudaSuccess;
     std::vector<int32_t> hidx((size_t)T * k);
     ok = ok && cudaMemcpyAsync(hidx.data(), didx, i_b, cudaMemcpyDeviceToHost, st) == cudaSuccess;
     const bool w_dev = aero::is_device_ptr(w);
@@ -1044,7 +1062,7 @@ int aero_cuda_ep_dispatch(void* handle, const float* x, int T, int n_ranks, int 
     cudaSetDevice(h->device);
     if (!aero::ensure_scratch(*h, std::max(T, 1))) return -1;
     auto& s = h->sc;
-    if (T > 0 && !aero::route_stage(*h, x, T, nullptr)) return -1;
+    if (T > 0 && !aero::route_stage(*h, x, T, nullptr, false)) return -1;
     // the plan reuses the dispatch buffers: perm holds send_tok, inv send_rank
     if (!h->cuda_ok(aero::launch_ep_plan(s.idx, T, h->k, rt, rank, s.perm, s.inv, counts, pos, h->stream), "exchange plan"))
         return -1;
@@ -1081,6 +1099,12 @@ int aero_cuda_ep_expert_block(void* handle, const void* rows, int row_dtype, con
                     "exchange unpack"))
         return -1;
     h->launches += 1;
+    const bool gemv = !f16 && !(h->gemm_ok && h->gb_ready && R >= h->gemm_min_tokens);
+    if (gemv && s.xq.q1) {
+        if (!h->cuda_ok(aero::launch_qinput(static_cast<const float*>(rows), R, h->dp, s.xq, h->stream), "row codes"))
+            return -1;
+        h->launches += 1;
+    }
     h->mark(2);
     if (!aero::expert_stage(*h, rows, f16, R, n_shared, true, out)) return -1;
     return aero::finish_profile(*h) ? 0 : -1;

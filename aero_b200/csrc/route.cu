@@ -134,7 +134,8 @@ __device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
 template <int PER>  // values per lane: E <= 32 * PER
 __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int ld, int T, int E,
                                                    int k, int norm, int has_shared, int32_t* __restrict__ idx,
-                                                   float* __restrict__ w, float* __restrict__ sgate) {
+                                                   float* __restrict__ w, float* __restrict__ sgate,
+                                                   const float* __restrict__ x, QInput xq) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * 8 + warp;
     if (t >= T) return;
@@ -198,6 +199,14 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
         if (lane < k) w[(int64_t)t * k + lane] = (float)((double)expf(sel_v - mx) / den);
     }
     if (has_shared && lane == 0) sgate[t] = sigmoid_f(lg[E]);
+    if (xq.q1) {
+        // this token's x row as integer input for the decode GEMVs
+        const int K = xq.K;
+        const float* xr = x + (int64_t)t * K;
+        for (int b = lane; b < K / 32; b += 32)
+            qinput_block(xr + 32 * b, xq.q1 + (int64_t)t * K + 32 * b, xq.q0 + (int64_t)t * K + 32 * b,
+                         xq.sx + (int64_t)t * (K / 32) + b, xq.s16 + (int64_t)t * (K / 16) + 2 * b);
+    }
 }
 
 // ---------------------------------------------------------------- dispatch
@@ -307,7 +316,24 @@ __global__ void dispatch_scatter_kernel(const int32_t* __restrict__ idx, int P, 
     }
 }
 
+// One thread per 32-value block.
+__global__ void qinput_kernel(const float* __restrict__ x, int R, int ld, QInput q) {
+    const int nb = q.K / 32;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)R * nb) return;
+    const int r = (int)(i / nb), b = (int)(i % nb);
+    qinput_block(x + (int64_t)r * ld + 32 * b, q.q1 + (int64_t)r * q.K + 32 * b, q.q0 + (int64_t)r * q.K + 32 * b,
+                 q.sx + (int64_t)r * nb + b, q.s16 + (int64_t)r * (q.K / 16) + 2 * b);
+}
+
 }  // namespace
+
+cudaError_t launch_qinput(const float* x, int R, int ld, QInput q, cudaStream_t s) {
+    const int64_t n = (int64_t)R * (q.K / 32);
+    if (n == 0) return cudaSuccess;
+    qinput_kernel<<<(unsigned)((n + 127) / 128), 128, 0, s>>>(x, R, ld, q);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_router(const float* x, int T, int d, const float* W, int row_begin, int row_end,
                           const float* bias, int n_bias, float* logits, int ld, cudaStream_t s) {
@@ -323,21 +349,21 @@ cudaError_t launch_router(const float* x, int T, int d, const float* W, int row_
 }
 
 cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int norm, int has_shared, int32_t* idx,
-                        float* w, float* sgate, cudaStream_t s) {
+                        float* w, float* sgate, const float* x, QInput xq, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
     const unsigned grid = (unsigned)((T + 7) / 8);
     if (E <= 32)
-        topk_kernel<1><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate);
+        topk_kernel<1><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq);
     else if (E <= 64)
-        topk_kernel<2><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate);
+        topk_kernel<2><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq);
     else if (E <= 128)
-        topk_kernel<4><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate);
+        topk_kernel<4><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq);
     else if (E <= 256)
-        topk_kernel<8><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate);
+        topk_kernel<8><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq);
     else if (E <= 512)
-        topk_kernel<16><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate);
+        topk_kernel<16><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq);
     else
-        topk_kernel<32><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate);
+        topk_kernel<32><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq);
     return cudaGetLastError();
 }
 
