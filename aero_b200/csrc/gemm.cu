@@ -5,7 +5,8 @@
 // 128-row MMA M extent runs over weight rows and the ragged token count is the
 // N extent (16..192 in steps of 16), so nothing is padded to 128 tokens.
 //   gate/up:  an item is 64 rows of gate and the same 64 rows of up, interleaved
-//             (M row 2i = gate row i, 2i+1 = up row i): D = [Wg; Wu] . X^T (K = d)
+//             by half-warps (M rows 32q + i = gate row 16q + i, 32q + 16 + i = up row
+//             16q + i, i < 16): D = [Wg; Wu] . X^T (K = d)
 //             epilogue: act = silu(D_g) * D_u, the partner rows meeting by a lane
 //             shuffle -> f16 act rows
 //   down:     D = Wd[n0:n0+128, :] . act^T                        (K = F)
@@ -318,11 +319,13 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
         // 16 warps: warp (warp & 3) may write TMEM lane quarter q; its combo
         // c = (warp - 2) / 4 takes values [16 c, 16 c + 16) of each 64-value K step
         // (8 TMEM columns). TMEM lane r is weight row r of the item; gate/up items
-        // interleave the matrices: lane r holds row r / 2 of gate (r even) or up (r odd).
+        // interleave the matrices by half-warps: in lane quarter q, lanes 0-15 hold
+        // gate rows 16 q + (0..15) and lanes 16-31 the same rows of up (so the
+        // raw-stage rows an 8-lane phase reads are consecutive: no bank conflicts).
         const int cmb = (warp - 2) >> 2;
         const int q = warp & 3;
         const int r = q * 32 + lane;
-        const int srow = GATEUP ? (r & 1) * (kTileM / 2) + (r >> 1) : r;  // row in the raw stage
+        const int srow = GATEUP ? (lane >> 4) * (kTileM / 2) + q * 16 + (lane & 15) : r;  // row in the raw stage
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
         const int swz = DT == AERO_DT_Q4_K ? ((srow >> 1) & 3) : (srow & 7);
         int raw_n = 0, a_n = 0;
@@ -436,11 +439,11 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
             tc_fence_after();
             const uint32_t d0 = tmem + lane_base + (uint32_t)ab * kAccStride;
             if (GATEUP) {
-                // lanes 2i / 2i+1 hold gate / up row 16 q + i of the item's 64 rows.
-                // Per 16 token columns: swap with the partner lane, the even lane forms
-                // act for tokens 0-7, the odd lane for tokens 8-15; stage [16 tok][16 f]
+                // lanes i / i + 16 hold gate / up row 16 q + i of the item's 64 rows.
+                // Per 16 token columns: swap with the partner lane, the gate lane forms
+                // act for tokens 0-7, the up lane for tokens 8-15; stage [16 tok][16 f]
                 // (f in the permuted K order of the down GEMM) and store 32-byte rows.
-                const int fl = lane >> 1, odd = lane & 1;
+                const int fl = lane & 15, upl = lane >> 4;
                 const int fcol = kperm(16 * q + fl) - 16 * q;  // within this warp's 16 f columns
                 __half* const out0 = p.out + (int64_t)it.t.pos0 * p.out_ld + it.mt * (kTileM / 2) + 16 * q;
                 for (int c0 = 0; c0 < it.N; c0 += 16) {
@@ -449,19 +452,20 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                     tmem_wait_ld();
 #pragma unroll
                     for (int j = 0; j < 8; ++j) {
-                        // even lane: gate of tokens j (own) with up (partner); odd: tokens 8 + j
-                        const uint32_t send = odd ? v[j] : v[8 + j];
-                        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 1);
-                        const float g = __uint_as_float(odd ? recv : v[j]);
-                        const float u = __uint_as_float(odd ? v[8 + j] : recv);
-                        stage[(8 * odd + j) * 16 + fcol] = __float2half_rn(__fdividef(g, 1.0f + __expf(-g)) * u);
+                        // gate lane: tokens j, own gate with the partner's up; up lane: tokens 8 + j
+                        const uint32_t send = upl ? v[j] : v[8 + j];
+                        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, 16);
+                        const float g = __uint_as_float(upl ? recv : v[j]);
+                        const float u = __uint_as_float(upl ? v[8 + j] : recv);
+                        stage[(8 * upl + j) * 16 + fcol] = __float2half_rn(__fdividef(g, 1.0f + __expf(-g)) * u);
                     }
                     __syncwarp();
                     {
-                        const int tok = lane >> 1;
-                        const uint4 o = *reinterpret_cast<const uint4*>(stage + tok * 16 + 8 * odd);
+                        // lane -> (token row, half) of the staged tile: one 16-byte store each
+                        const int tok = lane >> 1, hf = lane & 1;
+                        const uint4 o = *reinterpret_cast<const uint4*>(stage + tok * 16 + 8 * hf);
                         if (c0 + tok < it.t.nvalid)
-                            *reinterpret_cast<uint4*>(out0 + (int64_t)(c0 + tok) * p.out_ld + 8 * odd) = o;
+                            *reinterpret_cast<uint4*>(out0 + (int64_t)(c0 + tok) * p.out_ld + 8 * hf) = o;
                     }
                     __syncwarp();
                 }
