@@ -34,12 +34,13 @@ __device__ __forceinline__ bool slot_in(const int32_t* idx_t, int k, int lo, int
 }
 
 // One CTA. For each remote rank in rank order, the tokens with at least one
-// slot in that rank's range, in token order: send_tok / send_rank for send
-// rows [0, S), counts[r] rows per rank (0 for this rank), counts[n] = S, and
-// pos[t*n + r] = the send row of token t for rank r (-1: not sent; for r = me
+// slot in that rank's range, in token order: send_tok / send_rank for the S
+// sent rows in that compact order, counts[r] rows per rank (0 for this rank),
+// counts[n] = S, and pos[t*n + r] = the row of token t in rank r's slab of the
+// send buffer, r * slab + (its index among r's rows) (-1: not sent; for r = me
 // the token's own row t).
 __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const int32_t* __restrict__ idx, int T, int k,
-                                                               EpRankTable rt, int me,
+                                                               EpRankTable rt, int me, int slab,
                                                                int32_t* __restrict__ send_tok,
                                                                int32_t* __restrict__ send_rank,
                                                                int32_t* __restrict__ counts,
@@ -65,7 +66,7 @@ __global__ void __launch_bounds__(kPlanThreads) ep_plan_kernel(const int32_t* __
                 } else if (hit) {
                     send_tok[base + ex] = t;
                     send_rank[base + ex] = r;
-                    pos[(int64_t)t * n + r] = base + ex;
+                    pos[(int64_t)t * n + r] = r * slab + (base + ex - start);
                 } else {
                     pos[(int64_t)t * n + r] = -1;
                 }
@@ -85,26 +86,43 @@ __device__ __forceinline__ uint32_t pack_h2f(float a, float b) {
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Rows [0, T) are this rank's tokens (self rows), rows [T, T + S) the send rows.
-// Each thread moves 8 values; the thread of a row's first chunk also writes
-// the row's metadata.
+// Rows [0, T) are this rank's tokens (self rows); rows [T, T + n * slab) the send
+// slabs, slab r carrying counts[r] rows for rank r and padding after them whose
+// metadata names no expert. Each thread moves 8 values of a real row; the
+// thread of a row's first chunk also writes the row's metadata.
 template <typename RT>
 __global__ void ep_pack_kernel(const float* __restrict__ x, int T, int dp, int k, const int32_t* __restrict__ idx,
                                const float* __restrict__ w, const float* __restrict__ sgate, int has_shared,
-                               EpRankTable rt, int me, const int32_t* __restrict__ send_tok,
-                               const int32_t* __restrict__ send_rank, const int32_t* __restrict__ counts,
-                               RT* __restrict__ self_rows, int32_t* __restrict__ self_meta, RT* __restrict__ send_rows,
+                               EpRankTable rt, int me, int slab, const int32_t* __restrict__ send_tok,
+                               const int32_t* __restrict__ counts, RT* __restrict__ self_rows,
+                               int32_t* __restrict__ self_meta, RT* __restrict__ send_rows,
                                int32_t* __restrict__ send_meta, int meta_ld) {
     const int per_row = dp / 8;
-    const int S = counts[rt.n];
-    const int64_t total = (int64_t)(T + S) * per_row;
+    const int n = rt.n;
+    const int64_t total = (int64_t)(T + n * slab) * per_row;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int row = (int)(i / per_row), c = (int)(i % per_row) * 8;
         const bool self = row < T;
-        const int t = self ? row : send_tok[row - T];
-        const int dst = self ? me : send_rank[row - T];
-        const int64_t orow = self ? row : row - T;
+        int t = row, dst = me;
+        int64_t orow = row;
+        if (!self) {
+            orow = row - T;
+            dst = (int)(orow / slab);
+            const int kk = (int)(orow % slab);
+            if (kk >= counts[dst]) {
+                // padding: no expert for this row at the receiver
+                if (c == 0) {
+                    int32_t* m = send_meta + orow * meta_ld;
+                    for (int s = 0; s < k; ++s) m[s] = -1;
+                    for (int j = k; j < meta_ld; ++j) m[j] = 0;
+                }
+                continue;
+            }
+            int pre = 0;
+            for (int r = 0; r < dst; ++r) pre += counts[r];
+            t = send_tok[pre + kk];
+        }
         RT* rows = self ? self_rows : send_rows;
         const float* src = x + (int64_t)t * dp + c;
         const float4 a = ld_f4(src), b = ld_f4(src + 4);
@@ -172,26 +190,26 @@ __global__ void ep_combine_kernel(const float* __restrict__ self_out, const floa
 
 }  // namespace
 
-cudaError_t launch_ep_plan(const int32_t* idx, int T, int k, const EpRankTable& rt, int me, int32_t* send_tok,
-                           int32_t* send_rank, int32_t* counts, int32_t* pos, cudaStream_t s) {
-    ep_plan_kernel<<<1, kPlanThreads, 0, s>>>(idx, T, k, rt, me, send_tok, send_rank, counts, pos);
+cudaError_t launch_ep_plan(const int32_t* idx, int T, int k, const EpRankTable& rt, int me, int slab,
+                           int32_t* send_tok, int32_t* send_rank, int32_t* counts, int32_t* pos, cudaStream_t s) {
+    ep_plan_kernel<<<1, kPlanThreads, 0, s>>>(idx, T, k, rt, me, slab, send_tok, send_rank, counts, pos);
     return cudaGetLastError();
 }
 
 cudaError_t launch_ep_pack(const float* x, int T, int dp, int k, const int32_t* idx, const float* w,
-                           const float* sgate, int has_shared, const EpRankTable& rt, int me,
-                           const int32_t* send_tok, const int32_t* send_rank, const int32_t* counts, int rows_f16,
-                           void* self_rows, int32_t* self_meta, void* send_rows, int32_t* send_meta, int meta_ld,
-                           int max_rows, int n_sm, cudaStream_t s) {
-    const int64_t n = (int64_t)max_rows * (dp / 8);
+                           const float* sgate, int has_shared, const EpRankTable& rt, int me, int slab,
+                           const int32_t* send_tok, const int32_t* counts, int rows_f16, void* self_rows,
+                           int32_t* self_meta, void* send_rows, int32_t* send_meta, int meta_ld, int n_sm,
+                           cudaStream_t s) {
+    const int64_t n = (int64_t)(T + rt.n * slab) * (dp / 8);
     const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)n_sm * 16));
     if (rows_f16)
-        ep_pack_kernel<__half><<<grid, 256, 0, s>>>(x, T, dp, k, idx, w, sgate, has_shared, rt, me, send_tok,
-                                                    send_rank, counts, static_cast<__half*>(self_rows), self_meta,
+        ep_pack_kernel<__half><<<grid, 256, 0, s>>>(x, T, dp, k, idx, w, sgate, has_shared, rt, me, slab, send_tok,
+                                                    counts, static_cast<__half*>(self_rows), self_meta,
                                                     static_cast<__half*>(send_rows), send_meta, meta_ld);
     else
-        ep_pack_kernel<float><<<grid, 256, 0, s>>>(x, T, dp, k, idx, w, sgate, has_shared, rt, me, send_tok,
-                                                   send_rank, counts, static_cast<float*>(self_rows), self_meta,
+        ep_pack_kernel<float><<<grid, 256, 0, s>>>(x, T, dp, k, idx, w, sgate, has_shared, rt, me, slab, send_tok,
+                                                   counts, static_cast<float*>(self_rows), self_meta,
                                                    static_cast<float*>(send_rows), send_meta, meta_ld);
     return cudaGetLastError();
 }

@@ -96,18 +96,20 @@ struct EpRankTable {
     int begin[kEpMaxRanks + 1];
 };
 // Send plan for T local tokens with top-k ids idx (T, k): send_tok/send_rank
-// (S rows, remote ranks in order, tokens in order), counts[n] rows per rank and
-// counts[n] = S, pos (T, n) send row per (token, rank) or -1.
-cudaError_t launch_ep_plan(const int32_t* idx, int T, int k, const EpRankTable& rt, int me, int32_t* send_tok,
-                           int32_t* send_rank, int32_t* counts, int32_t* pos, cudaStream_t s);
-// Writes self rows (T) and send rows (S, read from counts) with their metadata
-// rows of meta_ld int32: k ids (-1 where the destination does not own the
-// slot's expert), k weights, the shared gate (self rows only), zero padding.
+// (S rows, remote ranks in order, tokens in order), counts[r] rows per rank and
+// counts[n] = S, pos (T, n): the row of each (token, rank) in the slab layout of
+// the send buffer (rank r's rows at [r * slab, r * slab + counts[r])) or -1.
+cudaError_t launch_ep_plan(const int32_t* idx, int T, int k, const EpRankTable& rt, int me, int slab,
+                           int32_t* send_tok, int32_t* send_rank, int32_t* counts, int32_t* pos, cudaStream_t s);
+// Writes the self rows (T) and the n send slabs of `slab` rows (real rows, then
+// padding whose metadata ids are all -1) with metadata rows of meta_ld int32:
+// k ids (-1 where the destination does not own the slot's expert), k weights,
+// the shared gate (self rows only), zero padding.
 cudaError_t launch_ep_pack(const float* x, int T, int dp, int k, const int32_t* idx, const float* w,
-                           const float* sgate, int has_shared, const EpRankTable& rt, int me,
-                           const int32_t* send_tok, const int32_t* send_rank, const int32_t* counts, int rows_f16,
-                           void* self_rows, int32_t* self_meta, void* send_rows, int32_t* send_meta, int meta_ld,
-                           int max_rows, int n_sm, cudaStream_t s);
+                           const float* sgate, int has_shared, const EpRankTable& rt, int me, int slab,
+                           const int32_t* send_tok, const int32_t* counts, int rows_f16, void* self_rows,
+                           int32_t* self_meta, void* send_rows, int32_t* send_meta, int meta_ld, int n_sm,
+                           cudaStream_t s);
 // Receiver side: metadata -> idx (bucket E for slots owned elsewhere), w, sgate.
 cudaError_t launch_ep_prep(const int32_t* meta, int meta_ld, int R, int k, int Tsh, int e_begin, int e_end, int E,
                            int32_t* idx, float* w, float* sgate, int32_t* bad, cudaStream_t s);

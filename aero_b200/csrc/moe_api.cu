@@ -1043,7 +1043,7 @@ static bool ep_rank_table(Handle& h, int n_ranks, int rank, const int32_t* begin
 
 int aero_cuda_ep_dispatch(void* handle, const float* x, int T, int n_ranks, int rank, const int32_t* rank_expert_begin,
                           int row_dtype, void* self_rows, int32_t* self_meta, void* send_rows, int32_t* send_meta,
-                          int send_cap, int32_t* counts, int32_t* pos) {
+                          int slab_rows, int32_t* counts, int32_t* pos) {
     auto* h = static_cast<Handle*>(handle);
     if (!h) return -1;
     std::lock_guard<std::mutex> lk(h->mu);
@@ -1052,9 +1052,8 @@ int aero_cuda_ep_dispatch(void* handle, const float* x, int T, int n_ranks, int 
     if (T < 0) return h->fail("T=%d", T), -1;
     if (row_dtype != AERO_EP_ROWS_F32 && row_dtype != AERO_EP_ROWS_F16) return h->fail("row_dtype %d", row_dtype), -1;
     if (h->d != h->dp) return h->fail("expert parallel needs n_embd %% 128 == 0 (n_embd=%d)", h->d), -1;
-    const int64_t need = (int64_t)T * std::min(h->k, n_ranks - 1);
-    if (send_cap < need) return h->fail("send_cap %d < T * min(k, n_ranks - 1) = %lld", send_cap, (long long)need), -1;
-    if (!counts || !pos || (T > 0 && (!x || !self_rows || !self_meta)) || (need > 0 && (!send_rows || !send_meta)))
+    if (slab_rows < std::max(T, 1)) return h->fail("slab_rows %d < T = %d", slab_rows, T), -1;
+    if (!counts || !pos || !send_rows || !send_meta || (T > 0 && (!x || !self_rows || !self_meta)))
         return h->fail("null buffer"), -1;
     for (const void* p : {(const void*)x, (const void*)self_rows, (const void*)send_rows})
         if (p && (!aero::is_device_ptr(p) || ((uintptr_t)p & 15) != 0))
@@ -1064,11 +1063,12 @@ int aero_cuda_ep_dispatch(void* handle, const float* x, int T, int n_ranks, int 
     auto& s = h->sc;
     if (T > 0 && !aero::route_stage(*h, x, T, nullptr, false)) return -1;
     // the plan reuses the dispatch buffers: perm holds send_tok, inv send_rank
-    if (!h->cuda_ok(aero::launch_ep_plan(s.idx, T, h->k, rt, rank, s.perm, s.inv, counts, pos, h->stream), "exchange plan"))
+    if (!h->cuda_ok(aero::launch_ep_plan(s.idx, T, h->k, rt, rank, slab_rows, s.perm, s.inv, counts, pos, h->stream),
+                    "exchange plan"))
         return -1;
-    if (!h->cuda_ok(aero::launch_ep_pack(x, T, h->dp, h->k, s.idx, s.w, s.sgate, h->has_shared, rt, rank, s.perm, s.inv,
-                                         counts, row_dtype == AERO_EP_ROWS_F16, self_rows, self_meta, send_rows, send_meta,
-                                         2 * h->k + 2, (int)(T + need), h->n_sm, h->stream),
+    if (!h->cuda_ok(aero::launch_ep_pack(x, T, h->dp, h->k, s.idx, s.w, s.sgate, h->has_shared, rt, rank, slab_rows,
+                                         s.perm, counts, row_dtype == AERO_EP_ROWS_F16, self_rows, self_meta, send_rows,
+                                         send_meta, 2 * h->k + 2, h->n_sm, h->stream),
                     "exchange pack"))
         return -1;
     h->launches += 2;

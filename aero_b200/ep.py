@@ -8,21 +8,23 @@ step's tokens. A step on each rank:
 
 1. `aero_cuda_ep_dispatch` routes the local tokens over all experts and writes
    the self rows (every local token, straight into the head of the receive
-   buffer) and one send row per (token, remote rank owning one of its experts),
-   ordered by rank then token, each with a metadata row (expert ids owned by
-   the destination, weights, shared gate);
-2. counts, rows and metadata cross with `all_to_all_single`; received rows land
-   after the self rows;
+   buffer) and, for every rank, a slab of `max_tokens` send rows: one row per
+   (token, that rank owning one of its experts), tokens in order, each with a
+   metadata row (expert ids owned by the destination, weights, shared gate),
+   then padding rows whose metadata names no expert;
+2. the slabs and their metadata cross with `all_to_all_single` in equal splits,
+   so no host synchronisation is needed; received slabs land after the self
+   rows;
 3. `aero_cuda_ep_expert_block` runs this rank's experts over all R rows (the
    self rows also take the shared expert) and writes one f32 row per row;
 4. rows [T_r, R) of that output go back with the reverse `all_to_all_single`,
-   arriving in send-row order;
+   arriving in the send slabs' layout;
 5. `aero_cuda_ep_combine` adds, per token, the self part and then the remote
    parts in rank order.
 
 Every rank takes the same collective steps in the same order, also for T_r = 0.
-The device work runs on the torch current stream, which the NCCL collectives
-order against, so the only host synchronisation is the count exchange.
+The device work and the collectives are ordered on one stream; the host never
+waits inside a step.
 """
 
 from __future__ import annotations
@@ -77,7 +79,7 @@ class CudaEpOps:
         tab = (self.nc.c_int32 * len(begin))(*begin)
         rc = self.lib.aero_cuda_ep_dispatch(self.h, x.data_ptr(), T, world, rank, tab, row_dtype, self_rows.data_ptr(),
                                             self_meta.data_ptr(), send_rows.data_ptr(), send_meta.data_ptr(),
-                                            send_rows.shape[0], counts.data_ptr(), pos.data_ptr())
+                                            send_rows.shape[0] // world, counts.data_ptr(), pos.data_ptr())
         self._check(rc, "aero_cuda_ep_dispatch")
 
     def expert_block(self, rows, row_dtype, meta, R, n_shared, out):
@@ -118,8 +120,10 @@ class ExpertParallelMoe:
         rdt = torch.float16 if row_f16 else torch.float32
         ml = ops.meta_ld
         self.max_tokens = int(max_tokens)
-        send_cap = max(1, self.max_tokens * min(k, world - 1))
-        recv_cap = max(1, self.max_tokens * world)  # self rows + at most every token of every other rank
+        # one slab of max_tokens rows per rank (a rank sends a token at most once)
+        self.slab = max(1, self.max_tokens)
+        send_cap = world * self.slab
+        recv_cap = self.max_tokens + world * self.slab  # self rows + a slab from every rank
         dev = self.device
         self.send_rows = torch.empty((send_cap, n_embd), dtype=rdt, device=dev)
         self.send_meta = torch.empty((send_cap, ml), dtype=torch.int32, device=dev)
@@ -149,7 +153,23 @@ class ExpertParallelMoe:
             if not g.try_reserve(nbytes, nc.MEM_SCRATCH):
                 raise RuntimeError(f"expert-parallel exchange buffers ({nbytes} bytes) refused by the memory guard")
             self._guard, self._reserved = g, nbytes
-        self.last_split = None
+        # per-phase device times (set_profiling): dispatch, counts (exchange), rows
+        # (row + metadata exchange), experts, back (return exchange), combine
+        self.PHASES = ("dispatch", "counts", "rows", "experts", "back", "combine")
+        self._prof = None
+        self.phase_ms = {k: 0.0 for k in self.PHASES}
+        self.phase_n = 0
+
+    def set_profiling(self, on: bool) -> None:
+        """Time the step's phases with CUDA events on the layer's stream (synchronises each step)."""
+        torch = self.torch
+        self._prof = [torch.cuda.Event(enable_timing=True) for _ in range(len(self.PHASES) + 1)] if on else None
+        self.phase_ms = {k: 0.0 for k in self.PHASES}
+        self.phase_n = 0
+
+    def _mark(self, i: int) -> None:
+        if self._prof is not None:
+            self._prof[i].record(self.stream)
 
     def close(self) -> None:
         if self._reserved:
@@ -191,24 +211,37 @@ class ExpertParallelMoe:
         out.record_stream(self.stream)
         return out
 
+    @property
+    def last_split(self):
+        """(rows sent to each rank, rows received from each rank) in the last step
+        (reads the device counters: synchronises)."""
+        both = self.torch.cat([self.counts[:self.world], self.recv_counts]).cpu().tolist()
+        return [int(v) for v in both[:self.world]], [int(v) for v in both[self.world:]]
+
     def _step(self, x, out):
-        torch = self.torch
         T = int(x.shape[0])
-        n, r = self.world, self.rank
+        n, r, C = self.world, self.rank, self.slab
+        R = T + n * C
+        self._mark(0)
         self.ops.dispatch(x, T, n, r, self.begin, self.row_dtype, self.recv_rows, self.recv_meta, self.send_rows,
                           self.send_meta, self.counts, self.pos)
-        self._a2a(self.recv_counts, self.counts[:n], None, None)
-        both = torch.cat([self.counts[:n], self.recv_counts]).cpu().tolist()  # the step's one host sync
-        send, recv = [int(v) for v in both[:n]], [int(v) for v in both[n:]]
-        S, Rr = sum(send), sum(recv)
-        if T + Rr > self.recv_rows.shape[0]:
-            raise RuntimeError(f"rank {r} receives {Rr} rows, more than max_tokens allows")
-        self.last_split = (send, recv)
-        self._a2a(self.recv_rows[T:T + Rr], self.send_rows[:S], recv, send)
-        self._a2a(self.recv_meta[T:T + Rr], self.send_meta[:S], recv, send)
-        self.ops.expert_block(self.recv_rows, self.row_dtype, self.recv_meta, T + Rr, T, self.y)
-        self._a2a(self.back[:S], self.y[T:T + Rr], send, recv)
+        self._mark(1)
+        self._a2a(self.recv_counts, self.counts[:n], None, None)  # for last_split only; stays on the device
+        self._mark(2)
+        self._a2a(self.recv_rows[T:R], self.send_rows, None, None)
+        self._a2a(self.recv_meta[T:R], self.send_meta, None, None)
+        self._mark(3)
+        self.ops.expert_block(self.recv_rows, self.row_dtype, self.recv_meta, R, T, self.y)
+        self._mark(4)
+        self._a2a(self.back, self.y[T:R], None, None)
+        self._mark(5)
         self.ops.combine(self.y, self.back, self.pos, T, n, r, out)
+        self._mark(6)
+        if self._prof is not None:
+            self._prof[6].synchronize()
+            for i, k in enumerate(self.PHASES):
+                self.phase_ms[k] += self._prof[i].elapsed_time(self._prof[i + 1])
+            self.phase_n += 1
 
     __call__ = forward
 

@@ -391,6 +391,14 @@ def main():
     }
     if ep_mode:
         result["exchange_rows"] = {"sent": moe.last_split[0], "received": moe.last_split[1]}
+        # per-phase device times of rank 0's step (a separate profiled pass)
+        moe.set_profiling(True)
+        with torch.cuda.stream(stream):
+            for _ in range(3):
+                step_device()
+        stream.synchronize()
+        result["ep_phases_ms"] = {k: round(v / max(moe.phase_n, 1), 5) for k, v in moe.phase_ms.items()}
+        moe.set_profiling(False)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         lg = x_host @ layer.router.T + (layer.router_bias if layer.router_bias is not None else 0)
         threads = os.cpu_count() or 1

@@ -160,16 +160,18 @@ int aero_cuda_moe_set_option(void* handle, int option, int64_t value);
  * experts [begin[r], begin[r+1]) (aero_cuda_moe_open / _open_gguf expert
  * range) and a step over its T local tokens is
  *   1. aero_cuda_ep_dispatch: route the T tokens (router + top-k over all
- *      experts), write the T self rows and the S send rows (one per token and
- *      remote rank owning at least one of its experts, remote ranks in order,
- *      tokens in order) with their metadata, counts[r] send rows per rank;
- *   2. the caller exchanges counts, rows and metadata (NCCL all-to-all) so
- *      that the rows from other ranks follow the self rows in one buffer;
- *   3. aero_cuda_ep_expert_block over the R received rows (self rows first;
- *      they also take the shared expert): out[r] = sum of w * expert(x) over
- *      the row's slots this rank owns (+ the shared expert);
+ *      experts), write the T self rows, and the send buffer as n_ranks slabs
+ *      of slab_rows rows: slab r holds one row per token with at least one
+ *      expert on rank r (tokens in order), then padding rows whose metadata
+ *      names no expert; counts[r] real rows per slab;
+ *   2. the caller exchanges the slabs with equal splits (NCCL all-to-all, no
+ *      host synchronisation) so that the slabs from all ranks follow the
+ *      self rows in one buffer;
+ *   3. aero_cuda_ep_expert_block over the R = T + n_ranks * slab_rows rows
+ *      (self rows first; they also take the shared expert): out[r] = sum of
+ *      w * expert(x) over the row's slots this rank owns (+ the shared expert);
  *   4. the caller sends rows [T, R) of that output back (reverse all-to-all,
- *      landing in send-row order);
+ *      landing in the send buffer's slab layout);
  *   5. aero_cuda_ep_combine: out[t] = self part + the remote parts in rank
  *      order.
  * All buffers are device memory, 16-byte aligned; the work is enqueued on the
@@ -182,13 +184,13 @@ int aero_cuda_moe_set_option(void* handle, int option, int64_t value);
 #define AERO_EP_ROWS_F16 1
 int aero_cuda_ep_meta_ld(void* handle);
 /* rank_expert_begin: host array of n_ranks + 1 ascending expert ids from 0 to
- * n_expert; this handle must hold [begin[rank], begin[rank+1]). send_cap (rows
- * of send_rows / send_meta) must be at least T * min(k, n_ranks - 1). counts:
- * n_ranks + 1 int32 (counts[n_ranks] = S); pos: (T, n_ranks) int32, the send
- * row of each (token, remote rank) or -1. */
+ * n_expert; this handle must hold [begin[rank], begin[rank+1]). send_rows /
+ * send_meta hold n_ranks * slab_rows rows; slab_rows >= T. counts: n_ranks + 1
+ * int32 (counts[n_ranks] = total real rows); pos: (T, n_ranks) int32, the send
+ * row of each (token, remote rank) in the slab layout, or -1. */
 int aero_cuda_ep_dispatch(void* handle, const float* x, int T, int n_ranks, int rank,
                           const int32_t* rank_expert_begin, int row_dtype, void* self_rows,
-                          int32_t* self_meta, void* send_rows, int32_t* send_meta, int send_cap,
+                          int32_t* self_meta, void* send_rows, int32_t* send_meta, int slab_rows,
                           int32_t* counts, int32_t* pos);
 /* rows (R, n_embd) with metadata (R, meta_ld); the first n_shared rows take the
  * shared expert with their metadata's gate. out (R, n_embd) f32. */

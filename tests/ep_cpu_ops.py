@@ -67,22 +67,26 @@ class CpuEpOps:
         for t in range(T):
             self_rows[t] = rows_np(t)
             self_meta[t] = meta(t, rank, True)
-        s = 0
+        slab = send_rows.shape[0] // world
         cnt = [0] * world
         pos_np = np.full((max(T, 1), world), -1, np.int32)
+        pad = np.zeros(self.meta_ld, np.int32)
+        pad[:k] = -1
         for r in range(world):
             for t in range(T):
                 if r == rank:
                     pos_np[t, r] = t
                     continue
                 if np.any((idx[t] >= begin[r]) & (idx[t] < begin[r + 1])):
-                    send_rows[s] = rows_np(t)
-                    send_meta[s] = meta(t, r, False)
-                    pos_np[t, r] = s
-                    s += 1
+                    row = r * slab + cnt[r]
+                    send_rows[row] = rows_np(t)
+                    send_meta[row] = meta(t, r, False)
+                    pos_np[t, r] = row
                     cnt[r] += 1
+            for j in range(cnt[r], slab):  # padding rows name no expert
+                send_meta[r * slab + j] = torch.from_numpy(pad)
         counts[:world] = torch.tensor(cnt, dtype=torch.int32)
-        counts[world] = s
+        counts[world] = sum(cnt)
         pos[:max(T, 1)] = torch.from_numpy(pos_np)
 
     def expert_block(self, rows, row_dtype, meta, R, n_shared, out):

@@ -164,21 +164,28 @@ def test_ep_refusals():
     lib = nc.lib()
     try:
         x = torch.zeros((4, 1024), device="cuda")
-        buf = torch.zeros((64, 1024), device="cuda")
-        meta = torch.zeros((64, 10), dtype=torch.int32, device="cuda")
+        slab = 32
+        selfb = torch.zeros((4, 1024), device="cuda")
+        selfm = torch.zeros((4, 10), dtype=torch.int32, device="cuda")
+        buf = torch.zeros((2 * slab, 1024), device="cuda")  # two slabs
+        meta = torch.zeros((2 * slab, 10), dtype=torch.int32, device="cuda")
         cnt = torch.zeros(3, dtype=torch.int32, device="cuda")
         pos = torch.zeros((4, 2), dtype=torch.int32, device="cuda")
         tab = (nc.c_int32 * 3)(0, 12, 24)
 
-        def disp(rank, table, cap=64):
-            return lib.aero_cuda_ep_dispatch(L.handle, x.data_ptr(), 4, 2, rank, table, 0, buf.data_ptr(),
-                                             meta.data_ptr(), buf.data_ptr(), meta.data_ptr(), cap, cnt.data_ptr(),
-                                             pos.data_ptr())
+        def disp(rank, table, slab_rows=slab):
+            return lib.aero_cuda_ep_dispatch(L.handle, x.data_ptr(), 4, 2, rank, table, 0, selfb.data_ptr(),
+                                             selfm.data_ptr(), buf.data_ptr(), meta.data_ptr(), slab_rows,
+                                             cnt.data_ptr(), pos.data_ptr())
 
         assert disp(0, tab) == 0
+        torch.cuda.synchronize()
+        # every row of the other rank's slab past its count names no expert
+        c1 = int(cnt[1])
+        assert bool((meta[slab + c1:, :4] == -1).all())
         assert disp(1, tab) == -1 and "this handle holds [0, 12)" in nc.last_error(L.handle)
         assert disp(0, (nc.c_int32 * 3)(0, 12, 20)) == -1 and "from 0 to 24" in nc.last_error(L.handle)
-        assert disp(0, tab, cap=3) == -1 and "send_cap" in nc.last_error(L.handle)
+        assert disp(0, tab, slab_rows=3) == -1 and "slab_rows" in nc.last_error(L.handle)
         # a forward on a ranged handle is refused: it holds only some experts
         with pytest.raises(Exception):
             L.forward(np.zeros((2, 1024), np.float32))
@@ -186,7 +193,7 @@ def test_ep_refusals():
         bad = torch.full((2, 10), -1, dtype=torch.int32, device="cuda")
         bad[0, 0] = 20
         out = torch.empty((2, 1024), device="cuda")
-        assert lib.aero_cuda_ep_expert_block(L.handle, buf.data_ptr(), 0, bad.data_ptr(), 2, 0, out.data_ptr()) == 0
+        assert lib.aero_cuda_ep_expert_block(L.handle, selfb.data_ptr(), 0, bad.data_ptr(), 2, 0, out.data_ptr()) == 0
         assert lib.aero_cuda_ep_bad_ids(L.handle) == 1
         assert lib.aero_cuda_ep_bad_ids(L.handle) == 0
         assert float(out.abs().max()) == 0.0
