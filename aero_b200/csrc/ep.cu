@@ -166,20 +166,34 @@ __global__ void ep_prep_kernel(const int32_t* __restrict__ meta, int meta_ld, in
     if (s == 0) sgate[r] = r < Tsh ? __int_as_float(m[2 * k]) : 0.f;
 }
 
-// out[t] = self_out[t] + sum over remote ranks r (ascending) of back[pos[t][r]].
-__global__ void ep_combine_kernel(const float* __restrict__ self_out, const float* __restrict__ back,
+// out[t] = self_out[t] + sum over remote ranks r (ascending) of back[pos[t][r]];
+// the partial rows are f32, or f16 (PT = __half).
+template <typename PT>
+__device__ __forceinline__ float4 part4(const PT* p) {
+    if constexpr (sizeof(PT) == 2) {
+        const uint2 v = *reinterpret_cast<const uint2*>(p);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+        return make_float4(a.x, a.y, b.x, b.y);
+    } else {
+        return ld_f4(reinterpret_cast<const float*>(p));
+    }
+}
+
+template <typename PT>
+__global__ void ep_combine_kernel(const PT* __restrict__ self_out, const PT* __restrict__ back,
                                   const int32_t* __restrict__ pos, int T, int n, int me, int dp,
                                   float* __restrict__ out) {
     const int d4 = dp >> 2;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)T * d4) return;
     const int t = (int)(i / d4), c = (int)(i % d4) * 4;
-    float4 acc = ld_f4(self_out + (int64_t)t * dp + c);
+    float4 acc = part4(self_out + (int64_t)t * dp + c);
     for (int r = 0; r < n; ++r) {
         if (r == me) continue;
         const int p = pos[(int64_t)t * n + r];
         if (p < 0) continue;
-        const float4 v = ld_f4(back + (int64_t)p * dp + c);
+        const float4 v = part4(back + (int64_t)p * dp + c);
         acc.x += v.x;
         acc.y += v.y;
         acc.z += v.z;
@@ -223,11 +237,17 @@ cudaError_t launch_ep_prep(const int32_t* meta, int meta_ld, int R, int k, int T
     return cudaGetLastError();
 }
 
-cudaError_t launch_ep_combine(const float* self_out, const float* back, const int32_t* pos, int T, int n, int me,
-                              int dp, float* out, cudaStream_t s) {
+cudaError_t launch_ep_combine(const void* self_out, const void* back, int parts_f16, const int32_t* pos, int T, int n,
+                              int me, int dp, float* out, cudaStream_t s) {
     const int64_t total = (int64_t)T * (dp / 4);
     if (total == 0) return cudaSuccess;
-    ep_combine_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(self_out, back, pos, T, n, me, dp, out);
+    const unsigned grid = (unsigned)((total + 255) / 256);
+    if (parts_f16)
+        ep_combine_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(self_out),
+                                                       static_cast<const __half*>(back), pos, T, n, me, dp, out);
+    else
+        ep_combine_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(self_out),
+                                                      static_cast<const float*>(back), pos, T, n, me, dp, out);
     return cudaGetLastError();
 }
 

@@ -571,11 +571,14 @@ __global__ void __launch_bounds__(1024) build_tiles_kernel(const int32_t* __rest
 
 // out[t] = sum over slots s of w[t][s] * y[inv[t*k+s]] (+ sgate[t] * y[P + t]
 // for t < Tsh). With idx given, slots whose bucket is >= E_real were skipped.
-// Each thread owns 8 columns (one 16-byte load of f16 per row it reads).
+// Each thread owns 8 columns (one 16-byte load of f16 per row it reads). The
+// result rows are f32, or f16 when OUT_F16 (partial rows of an expert-parallel
+// step that cross the network).
+template <bool OUT_F16>
 __global__ void combine_h_kernel(const __half* __restrict__ y, const int32_t* __restrict__ inv,
                                  const float* __restrict__ w, const float* __restrict__ sgate,
                                  const int32_t* __restrict__ idx, int E_real, int T, int Tsh, int k, int d,
-                                 int has_shared, float* __restrict__ out) {
+                                 int has_shared, void* __restrict__ out_v) {
     const int d8 = d >> 3;
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= (int64_t)T * d8) return;
@@ -596,9 +599,14 @@ __global__ void combine_h_kernel(const __half* __restrict__ y, const int32_t* __
         add(w[(int64_t)t * k + s], y + (int64_t)inv[(int64_t)t * k + s] * d);
     }
     if (has_shared && t < Tsh) add(sgate[t], y + ((int64_t)T * k + t) * d);
-    float4* o = reinterpret_cast<float4*>(out + (int64_t)t * d + c);
-    o[0] = make_float4(a[0], a[1], a[2], a[3]);
-    o[1] = make_float4(a[4], a[5], a[6], a[7]);
+    if constexpr (OUT_F16) {
+        *reinterpret_cast<uint4*>(static_cast<__half*>(out_v) + (int64_t)t * d + c) =
+            make_uint4(pack_h2(a[0], a[1]), pack_h2(a[2], a[3]), pack_h2(a[4], a[5]), pack_h2(a[6], a[7]));
+    } else {
+        float4* o = reinterpret_cast<float4*>(static_cast<float*>(out_v) + (int64_t)t * d + c);
+        o[0] = make_float4(a[0], a[1], a[2], a[3]);
+        o[1] = make_float4(a[4], a[5], a[6], a[7]);
+    }
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -816,12 +824,16 @@ cudaError_t launch_prefill_gemm(const PrefillArgs& a, GemmBuffers& b, const Gemm
 }
 
 cudaError_t launch_combine_h(const __half* y, const int32_t* inv, const float* w, const float* sgate,
-                             const int32_t* idx, int E_real, int T, int Tsh, int k, int d, int has_shared, float* out,
-                             cudaStream_t s) {
+                             const int32_t* idx, int E_real, int T, int Tsh, int k, int d, int has_shared, void* out,
+                             int out_f16, cudaStream_t s) {
     const int64_t n = (int64_t)T * (d / 8);
     if (n == 0) return cudaSuccess;
-    combine_h_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(y, inv, w, sgate, idx, E_real, T, Tsh, k, d,
-                                                                 has_shared, out);
+    if (out_f16)
+        combine_h_kernel<true><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(y, inv, w, sgate, idx, E_real, T, Tsh, k, d,
+                                                                           has_shared, out);
+    else
+        combine_h_kernel<false><<<(unsigned)((n + 255) / 256), 256, 0, s>>>(y, inv, w, sgate, idx, E_real, T, Tsh, k,
+                                                                            d, has_shared, out);
     return cudaGetLastError();
 }
 

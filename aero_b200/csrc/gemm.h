@@ -81,10 +81,11 @@ cudaError_t launch_prefill_prep(const PrefillArgs& a, GemmBuffers& b, cudaStream
 cudaError_t launch_prefill_gemm(const PrefillArgs& a, GemmBuffers& b, const GemmWeightMaps& wm, bool gateup,
                                 cudaStream_t s);
 // out[t] = sum_s w[t][s] * y[inv[t*k+s]] (+ sgate[t] * y[P + t] for t < Tsh); with
-// idx non-null, slots whose bucket idx[t*k+s] >= E_real are skipped.
+// idx non-null, slots whose bucket idx[t*k+s] >= E_real are skipped. out rows
+// are f32, or f16 with out_f16.
 cudaError_t launch_combine_h(const __half* y, const int32_t* inv, const float* w, const float* sgate,
                              const int32_t* idx, int E_real, int T, int Tsh, int k, int d, int has_shared,
-                             float* out, cudaStream_t s);
+                             void* out, int out_f16, cudaStream_t s);
 
 // Router projection on the tensor cores (router_tc.cu): f32-accurate logits
 // from three TF32 products of split operands, for prefill batches.

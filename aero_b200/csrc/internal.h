@@ -113,9 +113,10 @@ cudaError_t launch_ep_pack(const float* x, int T, int dp, int k, const int32_t* 
 // Receiver side: metadata -> idx (bucket E for slots owned elsewhere), w, sgate.
 cudaError_t launch_ep_prep(const int32_t* meta, int meta_ld, int R, int k, int Tsh, int e_begin, int e_end, int E,
                            int32_t* idx, float* w, float* sgate, int32_t* bad, cudaStream_t s);
-// out[t] = self_out[t] + sum over remote ranks (ascending) of back[pos[t][r]].
-cudaError_t launch_ep_combine(const float* self_out, const float* back, const int32_t* pos, int T, int n, int me,
-                              int dp, float* out, cudaStream_t s);
+// out[t] = self_out[t] + sum over remote ranks (ascending) of back[pos[t][r]];
+// the partial rows are f32, or f16 with parts_f16.
+cudaError_t launch_ep_combine(const void* self_out, const void* back, int parts_f16, const int32_t* pos, int T, int n,
+                              int me, int dp, float* out, cudaStream_t s);
 
 // Quant helpers.
 cudaError_t launch_repack(int dtype, const uint8_t* gguf, int64_t n_rows_total, int cols,

@@ -362,7 +362,8 @@ bool route_stage(Handle& h, const float* x, int T, const float* logits_in, bool 
 // [0, Tsh). With skip_slots, buckets equal to E mark slots to leave out (their
 // experts live on another rank). The GEMM path runs when x is f16 or T reaches
 // the handle's threshold.
-bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool skip_slots, float* out) {
+bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool skip_slots, void* out,
+                  bool out_f16 = false) {
     Scratch& s = h.sc;
     cudaStream_t st = h.stream;
     const int P = T * h.k;
@@ -375,7 +376,8 @@ bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool ski
     h.mark(3);
     const int32_t* skip_idx = skip_slots ? s.idx : nullptr;
     const bool use_gemm = h.gemm_ok && h.gb_ready && (x_f16 || T >= h.gemm_min_tokens);
-    if (x_f16 && !use_gemm) return h.fail("f16 rows need the prefill GEMM path, which this layer does not support");
+    if ((x_f16 || out_f16) && !use_gemm)
+        return h.fail("f16 rows need the prefill GEMM path, which this layer does not support");
     h.last_gemm = use_gemm;
     h.last_shared_rows = h.has_shared ? Tsh : 0;
     if (use_gemm) {
@@ -412,7 +414,7 @@ bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool ski
         h.launches += 4;
         h.mark(5);
         if (!h.cuda_ok(launch_combine_h(h.gb.y, s.inv, s.w, s.sgate, skip_idx, h.E, T, Tsh, h.k, h.dp, h.has_shared, out,
-                                        st),
+                                        out_f16 ? 1 : 0, st),
                        "combine"))
             return false;
         h.launches += 1;
@@ -449,7 +451,8 @@ bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool ski
         if (!h.cuda_ok(launch_gemv_down(a, st), "down")) return false;
         h.launches += 2 * (1 + (h.has_shared && Tsh > 0));
         h.mark(5);
-        if (!h.cuda_ok(launch_combine(s.y, s.inv, s.w, s.sgate, skip_idx, h.E, T, Tsh, h.k, h.dp, h.has_shared, out, st),
+        if (!h.cuda_ok(launch_combine(s.y, s.inv, s.w, s.sgate, skip_idx, h.E, T, Tsh, h.k, h.dp, h.has_shared,
+                                      static_cast<float*>(out), st),
                        "combine"))
             return false;
         h.launches += 1;
@@ -1076,12 +1079,13 @@ int aero_cuda_ep_dispatch(void* handle, const float* x, int T, int n_ranks, int 
 }
 
 int aero_cuda_ep_expert_block(void* handle, const void* rows, int row_dtype, const int32_t* meta, int R, int n_shared,
-                              float* out) {
+                              void* out, int out_dtype) {
     auto* h = static_cast<Handle*>(handle);
     if (!h) return -1;
     std::lock_guard<std::mutex> lk(h->mu);
     if (R < 0 || n_shared < 0 || n_shared > R) return h->fail("R=%d n_shared=%d", R, n_shared), -1;
     if (row_dtype != AERO_EP_ROWS_F32 && row_dtype != AERO_EP_ROWS_F16) return h->fail("row_dtype %d", row_dtype), -1;
+    if (out_dtype != AERO_EP_ROWS_F32 && out_dtype != AERO_EP_ROWS_F16) return h->fail("out_dtype %d", out_dtype), -1;
     if (h->d != h->dp) return h->fail("expert parallel needs n_embd %% 128 == 0 (n_embd=%d)", h->d), -1;
     if (R == 0) return 0;
     if (!rows || !meta || !out) return h->fail("null buffer"), -1;
@@ -1106,22 +1110,26 @@ int aero_cuda_ep_expert_block(void* handle, const void* rows, int row_dtype, con
         h->launches += 1;
     }
     h->mark(2);
-    if (!aero::expert_stage(*h, rows, f16, R, n_shared, true, out)) return -1;
+    if (!aero::expert_stage(*h, rows, f16, R, n_shared, true, out, out_dtype == AERO_EP_ROWS_F16)) return -1;
     return aero::finish_profile(*h) ? 0 : -1;
 }
 
-int aero_cuda_ep_combine(void* handle, const float* self_out, const float* back, const int32_t* pos, int T, int n_ranks,
-                         int rank, float* out) {
+int aero_cuda_ep_combine(void* handle, const void* self_out, const void* back, int parts_dtype, const int32_t* pos, int T,
+                         int n_ranks, int rank, float* out) {
     auto* h = static_cast<Handle*>(handle);
     if (!h) return -1;
     std::lock_guard<std::mutex> lk(h->mu);
     if (n_ranks < 1 || n_ranks > aero::kEpMaxRanks || rank < 0 || rank >= n_ranks)
         return h->fail("n_ranks=%d rank=%d", n_ranks, rank), -1;
     if (T < 0) return h->fail("T=%d", T), -1;
+    if (parts_dtype != AERO_EP_ROWS_F32 && parts_dtype != AERO_EP_ROWS_F16)
+        return h->fail("parts_dtype %d", parts_dtype), -1;
     if (T == 0) return 0;
     if (!self_out || !pos || !out || (n_ranks > 1 && !back)) return h->fail("null buffer"), -1;
     cudaSetDevice(h->device);
-    if (!h->cuda_ok(aero::launch_ep_combine(self_out, back, pos, T, n_ranks, rank, h->dp, out, h->stream), "exchange combine"))
+    if (!h->cuda_ok(aero::launch_ep_combine(self_out, back, parts_dtype == AERO_EP_ROWS_F16, pos, T, n_ranks, rank, h->dp,
+                                            out, h->stream),
+                    "exchange combine"))
         return -1;
     h->launches += 1;
     return 0;

@@ -83,13 +83,15 @@ class CudaEpOps:
         self._check(rc, "aero_cuda_ep_dispatch")
 
     def expert_block(self, rows, row_dtype, meta, R, n_shared, out):
+        out_dtype = ROWS_F16 if out.element_size() == 2 else ROWS_F32
         rc = self.lib.aero_cuda_ep_expert_block(self.h, rows.data_ptr(), row_dtype, meta.data_ptr(), R, n_shared,
-                                                out.data_ptr())
+                                                out.data_ptr(), out_dtype)
         self._check(rc, "aero_cuda_ep_expert_block")
 
     def combine(self, self_out, back, pos, T, world, rank, out):
-        rc = self.lib.aero_cuda_ep_combine(self.h, self_out.data_ptr(), back.data_ptr(), pos.data_ptr(), T, world,
-                                           rank, out.data_ptr())
+        parts = ROWS_F16 if back.element_size() == 2 else ROWS_F32
+        rc = self.lib.aero_cuda_ep_combine(self.h, self_out.data_ptr(), back.data_ptr(), parts, pos.data_ptr(), T,
+                                           world, rank, out.data_ptr())
         self._check(rc, "aero_cuda_ep_combine")
 
 
@@ -100,7 +102,8 @@ class ExpertParallelMoe:
     rank's expert range); `forward(x)` takes this rank's tokens (T_r, n_embd)
     f32 on `device` and returns their layer output. `max_tokens` bounds T_r on
     every rank (it sizes the exchange buffers once). With `row_f16` the rows
-    cross as f16 (the GEMM path's operand type; halves the bytes); otherwise f32.
+    cross as f16 (the GEMM path's operand type; halves the bytes), and so do the
+    partial outputs coming back; otherwise both are f32.
     `exchange(out, inp, out_splits, in_splits)` replaces
     torch.distributed.all_to_all_single over `group` (None splits: equal).
     """
@@ -129,8 +132,10 @@ class ExpertParallelMoe:
         self.send_meta = torch.empty((send_cap, ml), dtype=torch.int32, device=dev)
         self.recv_rows = torch.empty((recv_cap, n_embd), dtype=rdt, device=dev)
         self.recv_meta = torch.empty((recv_cap, ml), dtype=torch.int32, device=dev)
-        self.y = torch.empty((recv_cap, n_embd), dtype=torch.float32, device=dev)
-        self.back = torch.empty((send_cap, n_embd), dtype=torch.float32, device=dev)
+        # partial outputs cross back in the rows' type (f16 for prefill: the GEMM's
+        # per-expert results are f16 already)
+        self.y = torch.empty((recv_cap, n_embd), dtype=rdt, device=dev)
+        self.back = torch.empty((send_cap, n_embd), dtype=rdt, device=dev)
         self.counts = torch.zeros(world + 1, dtype=torch.int32, device=dev)
         self.recv_counts = torch.zeros(world, dtype=torch.int32, device=dev)
         self.pos = torch.empty((max(1, self.max_tokens), world), dtype=torch.int32, device=dev)

@@ -79,8 +79,8 @@ SYMBOLS = [
     ("aero_cuda_ep_meta_ld", c_int, [_P]),
     ("aero_cuda_ep_dispatch", c_int, [_P, _P, c_int, c_int, c_int, POINTER(c_int32), c_int, _P, _P, _P, _P, c_int,
                                       _P, _P]),
-    ("aero_cuda_ep_expert_block", c_int, [_P, _P, c_int, _P, c_int, c_int, _P]),
-    ("aero_cuda_ep_combine", c_int, [_P, _P, _P, _P, c_int, c_int, c_int, _P]),
+    ("aero_cuda_ep_expert_block", c_int, [_P, _P, c_int, _P, c_int, c_int, _P, c_int]),
+    ("aero_cuda_ep_combine", c_int, [_P, _P, _P, c_int, _P, c_int, c_int, c_int, _P]),
     ("aero_cuda_ep_bad_ids", c_int, [_P]),
     ("aero_cuda_moe_set_stream", c_int, [_P, _P]),
     ("aero_cuda_moe_info", c_int, [_P, POINTER(c_int32)]),

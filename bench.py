@@ -308,6 +308,7 @@ def main():
     stream.synchronize()
     if ws > 1:
         torch.distributed.barrier()
+    torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with torch.cuda.stream(stream):
         e0.record(stream)

@@ -169,7 +169,8 @@ int aero_cuda_moe_set_option(void* handle, int option, int64_t value);
  *      self rows in one buffer;
  *   3. aero_cuda_ep_expert_block over the R = T + n_ranks * slab_rows rows
  *      (self rows first; they also take the shared expert): out[r] = sum of
- *      w * expert(x) over the row's slots this rank owns (+ the shared expert);
+ *      w * expert(x) over the row's slots this rank owns (+ the shared expert),
+ *      as f32 or f16 partial rows;
  *   4. the caller sends rows [T, R) of that output back (reverse all-to-all,
  *      landing in the send buffer's slab layout);
  *   5. aero_cuda_ep_combine: out[t] = self part + the remote parts in rank
@@ -193,13 +194,15 @@ int aero_cuda_ep_dispatch(void* handle, const float* x, int T, int n_ranks, int 
                           int32_t* self_meta, void* send_rows, int32_t* send_meta, int slab_rows,
                           int32_t* counts, int32_t* pos);
 /* rows (R, n_embd) with metadata (R, meta_ld); the first n_shared rows take the
- * shared expert with their metadata's gate. out (R, n_embd) f32. */
+ * shared expert with their metadata's gate. out (R, n_embd) in out_dtype: f32,
+ * or f16 (halves the return exchange; needs the GEMM path, i.e. f16 rows). */
 int aero_cuda_ep_expert_block(void* handle, const void* rows, int row_dtype, const int32_t* meta,
-                              int R, int n_shared, float* out);
-/* self_out (T, n_embd): rows [0, T) of the expert block's output; back (S,
- * n_embd): the returned rows in send-row order; out (T, n_embd) f32. */
-int aero_cuda_ep_combine(void* handle, const float* self_out, const float* back, const int32_t* pos,
-                         int T, int n_ranks, int rank, float* out);
+                              int R, int n_shared, void* out, int out_dtype);
+/* self_out (T, n_embd): rows [0, T) of the expert block's output; back
+ * (n_ranks * slab_rows, n_embd): the returned rows in the send slabs' layout;
+ * both in parts_dtype (AERO_EP_ROWS_*). out (T, n_embd) f32. */
+int aero_cuda_ep_combine(void* handle, const void* self_out, const void* back, int parts_dtype,
+                         const int32_t* pos, int T, int n_ranks, int rank, float* out);
 /* Metadata ids received since the last call that named an expert this handle
  * does not hold (they were skipped). Synchronises the handle's stream. */
 int aero_cuda_ep_bad_ids(void* handle);

@@ -113,9 +113,9 @@ def test_ep_protocol_matches_single_process(world, shards, row_f16):
     want = _reference(shards, row_f16)
     scale = float(np.sqrt(np.mean(want.astype(np.float64) ** 2)))
     assert scale > 1e-4
-    # f16 rows: the reference also computes the shared gate from the rounded
-    # rows, the protocol from the f32 ones (a ~1e-4 relative difference)
-    tol = 1e-3 if row_f16 else 1e-4
+    # f16 rows: the partial outputs also cross back as f16 (one more rounding of
+    # ~5e-4 relative per element), so the prefill bar applies
+    tol = 1e-2 if row_f16 else 1e-4
     assert float(np.max(np.abs(got - want))) <= tol * scale
 
 

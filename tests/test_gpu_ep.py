@@ -129,8 +129,9 @@ def test_ep_prefill_matches_single_gpu(world):
         L.close()
     a, b = _run_threads(layer, x, world, row_f16=True)
     assert np.array_equal(a, b), "second step differs"
-    # same f16 expert products, partial sums regrouped by rank
-    assert rel_err(a, single) <= 1e-4
+    # same f16 expert products; the per-rank partial sums are rounded to f16 once
+    # for the return exchange
+    assert rel_err(a, single) <= 5e-3
     sel = np.sort(np.random.default_rng(9).choice(x.shape[0], 128, replace=False))
     ref = O.moe_block(layer, x[sel], lg[sel], nthreads=os.cpu_count() or 1)
     assert rel_err(a[sel], ref) <= PREFILL_TOL
@@ -193,7 +194,7 @@ def test_ep_refusals():
         bad = torch.full((2, 10), -1, dtype=torch.int32, device="cuda")
         bad[0, 0] = 20
         out = torch.empty((2, 1024), device="cuda")
-        assert lib.aero_cuda_ep_expert_block(L.handle, selfb.data_ptr(), 0, bad.data_ptr(), 2, 0, out.data_ptr()) == 0
+        assert lib.aero_cuda_ep_expert_block(L.handle, selfb.data_ptr(), 0, bad.data_ptr(), 2, 0, out.data_ptr(), 0) == 0
         assert lib.aero_cuda_ep_bad_ids(L.handle) == 1
         assert lib.aero_cuda_ep_bad_ids(L.handle) == 0
         assert float(out.abs().max()) == 0.0
@@ -270,4 +271,4 @@ def test_ep_nccl_two_gpus():
         single = L.forward(x)
     finally:
         L.close()
-    assert rel_err(msg[1], single) <= 1e-4
+    assert rel_err(msg[1], single) <= 5e-3  # f16 partial rows cross the network
