@@ -1,0 +1,391 @@
+// Expert-parallel exchange over peer memory: one process per GPU, each rank's
+// exchange window mapped into every other rank's address space (CUDA IPC over
+// NVLink / NVSwitch), so the rows and the partial outputs cross as plain stores
+// from the kernels that produce them, with no collective library in the step.
+//
+// Window of rank q (same layout on every rank; slab s holds the rows of rank
+// (q + s) mod n, so slab 0 is q's own tokens):
+//   rows [n][slab][dp]      token rows (f16 or f32) written by their owner
+//   meta [n][slab][meta_ld] metadata rows (k ids owned by q or -1, k weights,
+//                           shared gate, padding)
+//   back [n][slab][dp]      partial outputs of q's rows computed by rank
+//                           (q + s) mod n, in q's row order for that rank
+//   cnt  [n]                rows in each slab this step
+//   flag_rows [n], flag_back [n]   step number of the last completed write
+//   done_pack, done_ret     CTA counters of the two writing kernels
+//   err                     first wait that gave up (0: none)
+// A step (epoch e):
+//   plan    per destination rank, its tokens in order (send_tok, pos)
+//   pack    rows + metadata into the destination windows; the last CTA then
+//           writes cnt and flag_rows = e into every peer's window
+//   prep    waits for flag_rows = e from every peer, then metadata -> buckets
+//   (this rank's experts over its window rows, into a local y)
+//   return  y rows of slabs 1..n-1 into the owners' back slabs; the last CTA
+//           sets flag_back = e in every peer's window
+//   combine waits for flag_back = e, then self part + remote parts in rank
+//           order (the same sum, in the same order, as the all-to-all path)
+// One buffer per direction suffices: a rank writes step e+1 rows into a peer
+// only after its own step-e combine, which waited for that peer's step-e
+// returns, which the peer sent after it had finished reading its step-e rows;
+// and a peer returns step e+1 partials only after reading step e+1 rows, which
+// this rank writes after its step-e combine has read the step-e partials.
+// Every wait is bounded (kPeerWaitNs of %globaltimer): on expiry the CTA records
+// an error code in the window, later waits of the rank return at once, and the
+// host reads the code (aero_cuda_ep_peer_status).
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cub/block/block_scan.cuh>
+
+#include "internal.h"
+
+namespace aero {
+namespace {
+
+constexpr int kPlanThreads = 1024;
+constexpr uint64_t kPeerWaitNs = 5ull * 1000 * 1000 * 1000;
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint64_t gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+template <typename T>
+__device__ __forceinline__ T* wptr(const EpPeerTable& p, int rank, int64_t off) {
+    return reinterpret_cast<T*>(p.base[rank] + off);
+}
+
+// Thread 0 waits until flags[1..n-1] of this rank's window reach `epoch`; the
+// CTA gets the result. A wait that runs out records `code` in the window.
+__device__ bool peer_wait(const EpPeerTable& p, int64_t flag_off, uint32_t epoch, int code) {
+    __shared__ int ok_s;
+    if (threadIdx.x == 0) {
+        volatile int32_t* err = wptr<int32_t>(p, p.me, p.off_err);
+        const uint32_t* flags = wptr<const uint32_t>(p, p.me, flag_off);
+        int ok = *err == 0;
+        const uint64_t t0 = gtimer();
+        for (int s = 1; s < p.n && ok; ++s) {
+            while ((int32_t)(ld_acquire_sys(flags + s) - epoch) < 0) {
+                if (*err != 0) {
+                    ok = 0;
+                    break;
+                }
+                if (gtimer() - t0 > kPeerWaitNs) {
+                    atomicCAS(const_cast<int32_t*>(err), 0, code);
+                    ok = 0;
+                    break;
+                }
+                __nanosleep(128);
+            }
+        }
+        __threadfence();
+        ok_s = ok;
+    }
+    __syncthreads();
+    return ok_s != 0;
+}
+
+// Called by every thread of every CTA after its stores: the last CTA to get
+// here runs `last(tid)` for tid in [0, blockDim) after all CTAs' stores are
+// visible system-wide.
+template <typename F>
+__device__ __forceinline__ void after_all_ctas(uint32_t* done, F last) {
+    __shared__ int is_last;
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        is_last = atomicAdd(done, 1u) == gridDim.x - 1;
+        if (is_last) {
+            *done = 0;  // ready for the next launch
+            __threadfence_system();
+        }
+    }
+    __syncthreads();
+    if (is_last) last((int)threadIdx.x);
+}
+
+// One CTA per destination rank r: its tokens in order. send_tok[r*slab + j] is
+// the j-th token with at least one expert on r; pos[t*n + r] is where that
+// token's partial for r comes back in this rank's window ((r - me) mod n)*slab
+// + j (r = me: t, the self slab), or -1; counts[r] rows (counts[me] = T).
+__global__ void __launch_bounds__(kPlanThreads) ep_peer_plan_kernel(const int32_t* __restrict__ idx, int T, int k,
+                                                                    EpRankTable rt, int me, int slab,
+                                                                    int32_t* __restrict__ send_tok,
+                                                                    int32_t* __restrict__ counts,
+                                                                    int32_t* __restrict__ pos) {
+    using Scan = cub::BlockScan<int, kPlanThreads>;
+    __shared__ typename Scan::TempStorage tmp;
+    const int n = rt.n, r = blockIdx.x;
+    if (r == me) {
+        for (int t = threadIdx.x; t < T; t += kPlanThreads) pos[(int64_t)t * n + r] = t;
+        if (threadIdx.x == 0) counts[r] = T;
+        return;
+    }
+    const int lo = rt.begin[r], hi = rt.begin[r + 1];
+    const int base_slab = ((r - me + n) % n) * slab;
+    int carry = 0;
+    for (int t0 = 0; t0 < T; t0 += kPlanThreads) {
+        const int t = t0 + threadIdx.x;
+        bool hit = false;
+        if (t < T)
+            for (int s = 0; s < k; ++s) {
+                const int e = idx[(int64_t)t * k + s];
+                hit |= e >= lo && e < hi;
+            }
+        int ex, tot;
+        Scan(tmp).ExclusiveSum(hit ? 1 : 0, ex, tot);
+        if (t < T) {
+            if (hit) {
+                send_tok[(int64_t)r * slab + carry + ex] = t;
+                pos[(int64_t)t * n + r] = base_slab + carry + ex;
+            } else {
+                pos[(int64_t)t * n + r] = -1;
+            }
+        }
+        carry += tot;
+        __syncthreads();  // tmp reuse
+    }
+    if (threadIdx.x == 0) counts[r] = carry;
+}
+
+__device__ __forceinline__ uint32_t pack_h2f(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+// Rows and metadata of this rank's tokens into every destination window (slab
+// s = 0: own window; s > 0: rank (me + s) mod n, whose slab for this rank is
+// (n - s) mod n). One warp per row: 16-byte stores of 8 values per lane, the
+// metadata row by the first lanes.
+template <typename RT>
+__global__ void ep_peer_pack_kernel(EpPeerTable p, const float* __restrict__ x, int T,
+                                    const int32_t* __restrict__ idx, const float* __restrict__ w,
+                                    const float* __restrict__ sgate, int has_shared, EpRankTable rt,
+                                    const int32_t* __restrict__ send_tok, const int32_t* __restrict__ counts,
+                                    uint32_t epoch) {
+    const int n = p.n, me = p.me, slab = p.slab, dp = p.dp, k = p.k;
+    const int lane = threadIdx.x & 31;
+    const int R = n * slab;
+    const int nw = (int)((gridDim.x * blockDim.x) >> 5);
+    for (int row = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); row < R; row += nw) {
+        const int s = row / slab, j = row - s * slab;
+        const int r = (me + s) % n;
+        if (j >= (s == 0 ? T : counts[r])) continue;  // whole warp
+        const int t = s == 0 ? j : send_tok[(int64_t)r * slab + j];
+        const int64_t drow = (int64_t)((n - s) % n) * slab + j;  // row in r's window
+        const float* src = x + (int64_t)t * dp;
+        RT* dst = wptr<RT>(p, r, p.off_rows) + drow * dp;
+#pragma unroll 4
+        for (int c = lane * 8; c < dp; c += 256) {
+            const float4 a = ld_f4(src + c), b = ld_f4(src + c + 4);
+            if constexpr (sizeof(RT) == 2) {
+                *reinterpret_cast<uint4*>(dst + c) =
+                    make_uint4(pack_h2f(a.x, a.y), pack_h2f(a.z, a.w), pack_h2f(b.x, b.y), pack_h2f(b.z, b.w));
+            } else {
+                float* o = reinterpret_cast<float*>(dst) + c;
+                *reinterpret_cast<float4*>(o) = a;
+                *reinterpret_cast<float4*>(o + 4) = b;
+            }
+        }
+        int32_t* m = wptr<int32_t>(p, r, p.off_meta) + drow * p.meta_ld;
+        if (lane < k) {
+            const int lo = rt.begin[r], hi = rt.begin[r + 1];
+            const int e = idx[(int64_t)t * k + lane];
+            m[lane] = (e >= lo && e < hi) ? e : -1;
+            m[k + lane] = __float_as_int(w[(int64_t)t * k + lane]);
+        }
+        if (lane < p.meta_ld - 2 * k)
+            m[2 * k + lane] = lane == 0 ? __float_as_int(s == 0 && has_shared ? sgate[t] : 0.f) : 0;
+    }
+    after_all_ctas(wptr<uint32_t>(p, me, p.off_done_pack), [&](int tid) {
+        if (tid == 0) wptr<int32_t>(p, me, p.off_cnt)[0] = T;
+        if (tid >= 1 && tid < n) {
+            const int r = (me + tid) % n, slot = n - tid;
+            wptr<int32_t>(p, r, p.off_cnt)[slot] = counts[r];
+            st_release_sys(wptr<uint32_t>(p, r, p.off_flag_rows) + slot, epoch);
+        }
+    });
+}
+
+// Waits for every peer's rows, then metadata rows of the window -> buckets
+// (E for slots owned elsewhere and for unused slab rows), weights, shared gates
+// (slab 0 rows only). Ids that are neither -1 nor owned here count in *bad.
+__global__ void ep_peer_prep_kernel(EpPeerTable p, int T, int e_begin, int e_end, int E, uint32_t epoch,
+                                    int32_t* __restrict__ idx, float* __restrict__ w, float* __restrict__ sgate,
+                                    int32_t* __restrict__ bad) {
+    peer_wait(p, p.off_flag_rows, epoch, kEpErrRowsWait);
+    const int k = p.k, R = p.n * p.slab;
+    const volatile int32_t* cnt = wptr<int32_t>(p, p.me, p.off_cnt);
+    const int32_t* meta = wptr<const int32_t>(p, p.me, p.off_meta);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)R * k;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int r = (int)(i / k), q = (int)(i % k);
+        const int s = r / p.slab, j = r % p.slab;
+        const bool valid = j < (s == 0 ? T : cnt[s]);
+        const int32_t* m = meta + (int64_t)r * p.meta_ld;
+        const int e = valid ? m[q] : -1;
+        const bool own = e >= e_begin && e < e_end;
+        if (!own && e != -1) atomicAdd(bad, 1);
+        idx[i] = own ? e : E;
+        w[i] = valid ? __int_as_float(m[k + q]) : 0.f;
+        if (q == 0) sgate[r] = r < T ? __int_as_float(m[2 * k]) : 0.f;
+    }
+}
+
+// y rows of slabs 1..n-1 into the owners' back slabs (one warp per row,
+// 16-byte units), then the last CTA raises flag_back in every peer's window.
+template <typename PT>
+__global__ void ep_peer_return_kernel(EpPeerTable p, const PT* __restrict__ y, uint32_t epoch) {
+    const int n = p.n, me = p.me, slab = p.slab;
+    const int lane = threadIdx.x & 31;
+    const int units = p.dp * (int)sizeof(PT) / 16;
+    const int rows = (n - 1) * slab;
+    const volatile int32_t* cnt = wptr<int32_t>(p, me, p.off_cnt);
+    const int nw = (int)((gridDim.x * blockDim.x) >> 5);
+    for (int row = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); row < rows; row += nw) {
+        const int s = 1 + row / slab, j = row - (s - 1) * slab;
+        if (j >= cnt[s]) continue;  // whole warp
+        const int owner = (me + s) % n;
+        const uint4* src = reinterpret_cast<const uint4*>(y + ((int64_t)s * slab + j) * p.dp);
+        uint4* dst = reinterpret_cast<uint4*>(wptr<PT>(p, owner, p.off_back) + ((int64_t)(n - s) * slab + j) * p.dp);
+#pragma unroll 4
+        for (int u = lane; u < units; u += 32) dst[u] = src[u];
+    }
+    after_all_ctas(wptr<uint32_t>(p, me, p.off_done_ret), [&](int tid) {
+        if (tid >= 1 && tid < n) {
+            const int owner = (me + tid) % n;
+            st_release_sys(wptr<uint32_t>(p, owner, p.off_flag_back) + (n - tid), epoch);
+        }
+    });
+}
+
+template <typename PT>
+__device__ __forceinline__ float4 part4(const PT* q) {
+    if constexpr (sizeof(PT) == 2) {
+        const uint2 v = *reinterpret_cast<const uint2*>(q);
+        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+        return make_float4(a.x, a.y, b.x, b.y);
+    } else {
+        return *reinterpret_cast<const float4*>(q);
+    }
+}
+
+// Waits for every peer's returns, then out[t] = y[t] + the remote parts in
+// ascending rank order.
+template <typename PT>
+__global__ void ep_peer_combine_kernel(EpPeerTable p, const PT* __restrict__ y, const int32_t* __restrict__ pos, int T,
+                                       uint32_t epoch, float* __restrict__ out) {
+    peer_wait(p, p.off_flag_back, epoch, kEpErrBackWait);
+    const int n = p.n, dp = p.dp, d4 = dp >> 2;
+    const PT* back = wptr<const PT>(p, p.me, p.off_back);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)T * d4;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int t = (int)(i / d4), c = (int)(i % d4) * 4;
+        float4 acc = part4(y + (int64_t)t * dp + c);
+        for (int r = 0; r < n; ++r) {
+            if (r == p.me) continue;
+            const int q = pos[(int64_t)t * n + r];
+            if (q < 0) continue;
+            const float4 v = part4(back + (int64_t)q * dp + c);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        *reinterpret_cast<float4*>(out + (int64_t)t * dp + c) = acc;
+    }
+}
+
+unsigned grid_for(int64_t items, int n_sm, int per_sm) {
+    return (unsigned)std::max<int64_t>(1, std::min<int64_t>((items + 255) / 256, (int64_t)n_sm * per_sm));
+}
+
+}  // namespace
+
+EpPeerTable ep_peer_layout(int n, int me, int slab, int dp, int k, int rows_f16, size_t* bytes) {
+    EpPeerTable p{};
+    p.n = n;
+    p.me = me;
+    p.slab = slab;
+    p.dp = dp;
+    p.k = k;
+    p.meta_ld = 2 * k + 2;
+    p.rows_f16 = rows_f16;
+    const int64_t R = (int64_t)n * slab;
+    const int64_t esz = rows_f16 ? 2 : 4;
+    int64_t off = 0;
+    auto take = [&](int64_t b) {
+        const int64_t o = off;
+        off += (b + 255) & ~(int64_t)255;
+        return o;
+    };
+    p.off_rows = take(R * dp * esz);
+    p.off_meta = take(R * p.meta_ld * 4);
+    p.off_back = take(R * dp * esz);
+    p.off_cnt = take((int64_t)n * 4);
+    p.off_flag_rows = take((int64_t)n * 4);
+    p.off_flag_back = take((int64_t)n * 4);
+    p.off_done_pack = take(4);
+    p.off_done_ret = take(4);
+    p.off_err = take(4);
+    *bytes = (size_t)off;
+    return p;
+}
+
+cudaError_t launch_ep_peer_plan(const int32_t* idx, int T, int k, const EpRankTable& rt, int me, int slab,
+                                int32_t* send_tok, int32_t* counts, int32_t* pos, cudaStream_t s) {
+    ep_peer_plan_kernel<<<rt.n, kPlanThreads, 0, s>>>(idx, T, k, rt, me, slab, send_tok, counts, pos);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_peer_pack(const EpPeerTable& p, const float* x, int T, const int32_t* idx, const float* w,
+                                const float* sgate, int has_shared, const EpRankTable& rt, const int32_t* send_tok,
+                                const int32_t* counts, uint32_t epoch, int n_sm, cudaStream_t s) {
+    const unsigned grid = grid_for((int64_t)p.n * p.slab * 32, n_sm, 8);  // a warp per row
+    if (p.rows_f16)
+        ep_peer_pack_kernel<__half><<<grid, 256, 0, s>>>(p, x, T, idx, w, sgate, has_shared, rt, send_tok, counts, epoch);
+    else
+        ep_peer_pack_kernel<float><<<grid, 256, 0, s>>>(p, x, T, idx, w, sgate, has_shared, rt, send_tok, counts, epoch);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_peer_prep(const EpPeerTable& p, int T, int e_begin, int e_end, int E, uint32_t epoch,
+                                int32_t* idx, float* w, float* sgate, int32_t* bad, int n_sm, cudaStream_t s) {
+    const unsigned grid = grid_for((int64_t)p.n * p.slab * p.k, n_sm, 4);
+    ep_peer_prep_kernel<<<grid, 256, 0, s>>>(p, T, e_begin, e_end, E, epoch, idx, w, sgate, bad);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_peer_return(const EpPeerTable& p, const void* y, uint32_t epoch, int n_sm, cudaStream_t s) {
+    const unsigned grid = grid_for((int64_t)(p.n - 1) * p.slab * 32, n_sm, 8);  // a warp per row
+    if (p.rows_f16)
+        ep_peer_return_kernel<__half><<<grid, 256, 0, s>>>(p, static_cast<const __half*>(y), epoch);
+    else
+        ep_peer_return_kernel<float><<<grid, 256, 0, s>>>(p, static_cast<const float*>(y), epoch);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_peer_combine(const EpPeerTable& p, const void* y, const int32_t* pos, int T, uint32_t epoch,
+                                   float* out, int n_sm, cudaStream_t s) {
+    const unsigned grid = grid_for((int64_t)T * (p.dp / 4), n_sm, 8);
+    if (p.rows_f16)
+        ep_peer_combine_kernel<__half><<<grid, 256, 0, s>>>(p, static_cast<const __half*>(y), pos, T, epoch, out);
+    else
+        ep_peer_combine_kernel<float><<<grid, 256, 0, s>>>(p, static_cast<const float*>(y), pos, T, epoch, out);
+    return cudaGetLastError();
+}
+
+}  // namespace aero

@@ -101,7 +101,10 @@ cudaError_t router_tc_prepare(const float* W, int n_rows, int dp, float* w_hi, f
                               cudaStream_t s);
 // logits[t][e] = x_t . W[e] (+ bias[e] for e < n_bias) for t < T, e < n_rows;
 // with gate_row, logits[t][n_rows] = x_t . gate_row (f32, K in order). ld % 4 == 0.
+// partial (partial_rows x ld floats, may be null) lets small batches split K
+// over more CTAs; the splits are summed in a fixed order.
 cudaError_t launch_router_tc(const RouterTcMaps& maps, const float* x, int T, const float* bias, int n_bias,
-                             const float* gate_row, float* logits, int ld, int32_t* err, cudaStream_t s);
+                             const float* gate_row, float* logits, int ld, int32_t* err, float* partial,
+                             int partial_rows, int n_sm, cudaStream_t s);
 
 }  // namespace aero

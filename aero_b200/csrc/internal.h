@@ -118,6 +118,35 @@ cudaError_t launch_ep_prep(const int32_t* meta, int meta_ld, int R, int k, int T
 cudaError_t launch_ep_combine(const void* self_out, const void* back, int parts_f16, const int32_t* pos, int T, int n,
                               int me, int dp, float* out, cudaStream_t s);
 
+// Expert-parallel exchange over peer memory (ep_peer.cu): every rank's window,
+// mapped into this process, and the byte offsets of its regions (the same on
+// every rank).
+struct EpPeerTable {
+    int n, me, slab, dp, k, meta_ld, rows_f16;
+    int64_t off_rows, off_meta, off_back, off_cnt, off_flag_rows, off_flag_back, off_done_pack, off_done_ret, off_err;
+    char* base[kEpMaxRanks];
+};
+enum : int { kEpErrRowsWait = 21, kEpErrBackWait = 22 };
+// Region offsets for n ranks, slabs of `slab` rows of dp values (f16 or f32);
+// *bytes = window size.
+EpPeerTable ep_peer_layout(int n, int me, int slab, int dp, int k, int rows_f16, size_t* bytes);
+// Per destination rank: send_tok[r*slab + j] = its j-th token, counts[r] (counts[me] = T),
+// pos (T, n): the row in this rank's window where the partial for (t, r) returns, or -1.
+cudaError_t launch_ep_peer_plan(const int32_t* idx, int T, int k, const EpRankTable& rt, int me, int slab,
+                                int32_t* send_tok, int32_t* counts, int32_t* pos, cudaStream_t s);
+// Rows and metadata into the destination windows, then cnt and flag_rows = epoch in every peer.
+cudaError_t launch_ep_peer_pack(const EpPeerTable& p, const float* x, int T, const int32_t* idx, const float* w,
+                                const float* sgate, int has_shared, const EpRankTable& rt, const int32_t* send_tok,
+                                const int32_t* counts, uint32_t epoch, int n_sm, cudaStream_t s);
+// Waits for every peer's rows of this epoch, then window metadata -> idx / w / sgate (R = n * slab rows).
+cudaError_t launch_ep_peer_prep(const EpPeerTable& p, int T, int e_begin, int e_end, int E, uint32_t epoch,
+                                int32_t* idx, float* w, float* sgate, int32_t* bad, int n_sm, cudaStream_t s);
+// y rows of the peers' slabs back into their windows, then flag_back = epoch in every peer.
+cudaError_t launch_ep_peer_return(const EpPeerTable& p, const void* y, uint32_t epoch, int n_sm, cudaStream_t s);
+// Waits for every peer's returns, then out[t] = y[t] + remote parts in rank order.
+cudaError_t launch_ep_peer_combine(const EpPeerTable& p, const void* y, const int32_t* pos, int T, uint32_t epoch,
+                                   float* out, int n_sm, cudaStream_t s);
+
 // Quant helpers.
 cudaError_t launch_repack(int dtype, const uint8_t* gguf, int64_t n_rows_total, int cols,
                           int rows_per_expert, int64_t expert0, uint8_t* qs, uint8_t* meta,

@@ -44,17 +44,44 @@ struct Alloc {
     int cls;
 };
 
+// rows of split-K partial logits kept for the tensor-core router (splits x tokens)
+constexpr int kRouterPartRows = 8192;
+
 struct Scratch {
     int cap_T = 0;
     void* base = nullptr;
     size_t bytes = 0;
     float *x_stage, *out_stage, *lg_stage, *logits, *w, *sgate, *act, *y;
+    float* lg_part = nullptr;  // router split-K partials (lg_part_rows x lg_ld)
+    int lg_part_rows = 0;
     int32_t *idx, *offsets, *perm, *inv, *act_e, *act_off, *n_active, *ep_bad, *tc_err;
     void* dwork;
     QInput xq{}, aq{};  // GEMV inputs in integer form (null planes for F32 experts)
     void* gemm_ws;
     size_t gemm_ws_bytes = 0;
     int gemv_cap = 0;
+};
+
+// Expert-parallel exchange over peer memory: this rank's window (IPC-exported),
+// the peers' windows mapped here, and the step's local buffers.
+struct PeerCtx {
+    bool open = false, connected = false;
+    EpPeerTable tab{};
+    EpRankTable rt{};
+    char* window = nullptr;
+    size_t window_bytes = 0;
+    void* y = nullptr;  // expert-block output for the window's rows (row type)
+    size_t y_bytes = 0;
+    int32_t* aux = nullptr;  // send_tok (n * slab), counts (n + 1), pos (slab * n)
+    size_t aux_bytes = 0;
+    std::vector<char*> mapped;  // peers' windows opened here
+    uint32_t epoch = 0;
+    // phase timing (profiling): route, pack, rows wait + unpack, experts, return, combine
+    static constexpr int kPhases = 6;
+    bool prof = false;
+    cudaEvent_t ev[kPhases + 1] = {};
+    double ms[kPhases] = {};
+    long n_prof = 0;
 };
 
 struct Handle {
@@ -98,10 +125,27 @@ struct Handle {
     int last_pairs = -1;      // its routed (token, expert) pairs computed here
     int last_shared_rows = 0; // its rows through the shared expert
     bool last_gemm = false;   // whether it took the GEMM path
+    PeerCtx peer;
+
+    void peer_release() {
+        for (char* m : peer.mapped)
+            if (m) cudaIpcCloseMemHandle(m);
+        peer.mapped.clear();
+        if (peer.window) guarded_free(peer.window, peer.window_bytes, kScratch);
+        if (peer.y) guarded_free(peer.y, peer.y_bytes, kScratch);
+        if (peer.aux) guarded_free(peer.aux, peer.aux_bytes, kScratch);
+        for (auto& e : peer.ev)
+            if (e) cudaEventDestroy(e);
+        peer = PeerCtx{};
+    }
 
     ~Handle() {
         if (device >= 0) cudaSetDevice(device);
         if (own_stream) cudaStreamSynchronize(own_stream);
+        if (peer.open) {
+            cudaStreamSynchronize(stream);
+            peer_release();
+        }
         for (auto& a : allocs) guarded_free(a.p, a.bytes, a.cls);
         if (sc.base) guarded_free(sc.base, sc.bytes, kScratch);
         if (ev0) cudaEventDestroy(ev0);
@@ -252,6 +296,9 @@ bool ensure_scratch(Handle& h, int T) {
     const size_t o_inv = take((size_t)P * 4), o_ae = take((size_t)h.E * 4), o_ao = take((size_t)(h.E + 1) * 4);
     const size_t o_na = take(4), o_dw = take(dispatch_work_bytes((int)P, h.E + 1));
     const size_t o_bad = take(4), o_tce = take(4);
+    // split-K partial logits of the tensor-core router (small batches)
+    const int part_rows = h.rtc_ok ? (int)std::min<int64_t>(kRouterPartRows, (int64_t)8 * cap) : 0;
+    const size_t o_lgp = take((size_t)part_rows * h.lg_ld * 4);
     const int max_tiles = gemm_max_tiles((int)P, cap, h.E, h.has_shared);
     const size_t gws = h.gemm_ok ? gemm_workspace_bytes(h.dp, h.act_ld, (int)P, cap, max_tiles) : 256;
     const size_t o_gw = take(gws);
@@ -287,6 +334,8 @@ bool ensure_scratch(Handle& h, int T) {
     s.n_active = (int32_t*)(b + o_na);
     s.ep_bad = (int32_t*)(b + o_bad);
     s.tc_err = (int32_t*)(b + o_tce);
+    s.lg_part = part_rows ? (float*)(b + o_lgp) : nullptr;
+    s.lg_part_rows = part_rows;
     s.dwork = b + o_dw;
     s.gemm_ws = b + o_gw;
     s.gemm_ws_bytes = gws;
@@ -318,7 +367,7 @@ bool router_logits_dev(Handle& h, const float* x, int T, bool with_gate) {
     const bool gate = with_gate && h.has_shared;
     if (h.rtc_ok && h.rtc_enabled && T >= kRouterTcMinTokens) {
         return h.cuda_ok(launch_router_tc(h.rtc, x, T, h.router_bias, h.E, gate ? h.router_ext + (size_t)h.E * h.dp : nullptr,
-                                          s.logits, h.lg_ld, s.tc_err, h.stream),
+                                          s.logits, h.lg_ld, s.tc_err, s.lg_part, s.lg_part_rows, h.n_sm, h.stream),
                          "router (tensor cores)");
     }
     return h.cuda_ok(launch_router(x, T, h.dp, h.router_ext, 0, h.E + (gate ? 1 : 0), h.router_bias, h.E, s.logits,
@@ -372,7 +421,7 @@ bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool ski
                                    st, h.E),
                    "dispatch"))
         return false;
-    h.launches += 3;
+    h.launches += 4;
     h.mark(3);
     const int32_t* skip_idx = skip_slots ? s.idx : nullptr;
     const bool use_gemm = h.gemm_ok && h.gb_ready && (x_f16 || T >= h.gemm_min_tokens);
@@ -1148,6 +1197,255 @@ int aero_cuda_ep_bad_ids(void* handle) {
         return -1;
     if (v) cudaMemsetAsync(h->sc.ep_bad, 0, 4, h->stream);
     return v;
+}
+
+// ------------------------------------------------ expert parallel, peer memory
+
+int aero_cuda_ep_peer_open(void* handle, int n_ranks, int rank, const int32_t* rank_expert_begin, int slab_rows,
+                           int row_dtype, void* ipc_out) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    auto& pc = h->peer;
+    if (pc.open) return h->fail("the peer exchange is already open on this handle"), -1;
+    aero::EpRankTable rt{};
+    if (!ep_rank_table(*h, n_ranks, rank, rank_expert_begin, &rt)) return -1;
+    if (n_ranks < 2) return h->fail("the peer exchange needs at least 2 ranks"), -1;
+    if (row_dtype != AERO_EP_ROWS_F32 && row_dtype != AERO_EP_ROWS_F16) return h->fail("row_dtype %d", row_dtype), -1;
+    if (h->d != h->dp) return h->fail("expert parallel needs n_embd %% 128 == 0 (n_embd=%d)", h->d), -1;
+    if (slab_rows < 1) return h->fail("slab_rows %d", slab_rows), -1;
+    if ((int64_t)n_ranks * slab_rows > (1 << 24)) return h->fail("n_ranks * slab_rows too large"), -1;
+    if (!ipc_out) return h->fail("null ipc_out"), -1;
+    cudaSetDevice(h->device);
+    const int R = n_ranks * slab_rows;
+    if (!aero::ensure_scratch(*h, R)) return -1;
+    if (row_dtype == AERO_EP_ROWS_F16 && !(h->gemm_ok && h->gb_ready))
+        return h->fail("f16 rows need the prefill GEMM path, which this layer does not support"), -1;
+    size_t wbytes = 0;
+    aero::EpPeerTable tab = aero::ep_peer_layout(n_ranks, rank, slab_rows, h->dp, h->k,
+                                                 row_dtype == AERO_EP_ROWS_F16, &wbytes);
+    const size_t esz = row_dtype == AERO_EP_ROWS_F16 ? 2 : 4;
+    const size_t ybytes = (size_t)R * h->dp * esz;
+    const size_t abytes = ((size_t)R + n_ranks + 1 + (size_t)slab_rows * n_ranks) * 4;
+    void *w = nullptr, *y = nullptr, *a = nullptr;
+    cudaError_t e = aero::guarded_malloc(&w, wbytes, aero::kScratch);
+    if (e == cudaSuccess) e = aero::guarded_malloc(&y, ybytes, aero::kScratch);
+    if (e == cudaSuccess) e = aero::guarded_malloc(&a, abytes, aero::kScratch);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        if (w) aero::guarded_free(w, wbytes, aero::kScratch);
+        if (y) aero::guarded_free(y, ybytes, aero::kScratch);
+        return h->fail("peer exchange buffers (%s) refused by the memory guard or the device",
+                       aero::fmt_bytes(wbytes + ybytes + abytes).c_str()),
+               -1;
+    }
+    pc.window = static_cast<char*>(w);
+    pc.window_bytes = wbytes;
+    pc.y = y;
+    pc.y_bytes = ybytes;
+    pc.aux = static_cast<int32_t*>(a);
+    pc.aux_bytes = abytes;
+    pc.open = true;
+    pc.rt = rt;
+    tab.base[rank] = pc.window;
+    pc.tab = tab;
+    cudaIpcMemHandle_t ih;
+    if (!h->cuda_ok(cudaMemsetAsync(pc.window, 0, wbytes, h->stream), "window clear") ||
+        !h->cuda_ok(cudaStreamSynchronize(h->stream), "window clear") ||
+        !h->cuda_ok(cudaIpcGetMemHandle(&ih, pc.window), "IPC handle of the window")) {
+        h->peer_release();
+        return -1;
+    }
+    // the blob: the window's IPC handle, then this GPU's UUID (ranks on one
+    // GPU are refused at connect)
+    static_assert(sizeof(cudaIpcMemHandle_t) + sizeof(cudaUUID_t) <= AERO_EP_IPC_BYTES, "IPC blob size");
+    cudaDeviceProp prop{};
+    if (!h->cuda_ok(cudaGetDeviceProperties(&prop, h->device), "device properties")) {
+        h->peer_release();
+        return -1;
+    }
+    std::memset(ipc_out, 0, AERO_EP_IPC_BYTES);
+    std::memcpy(ipc_out, &ih, sizeof ih);
+    std::memcpy(static_cast<char*>(ipc_out) + sizeof ih, &prop.uuid, sizeof prop.uuid);
+    return 0;
+}
+
+int aero_cuda_ep_peer_connect(void* handle, const void* ipc_all) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    auto& pc = h->peer;
+    if (!pc.open) return h->fail("aero_cuda_ep_peer_open first"), -1;
+    if (pc.connected) return h->fail("the peer exchange is already connected"), -1;
+    if (!ipc_all) return h->fail("null ipc_all"), -1;
+    cudaSetDevice(h->device);
+    const int n = pc.tab.n;
+    const char* blobs = static_cast<const char*>(ipc_all);
+    // ranks on one GPU would run kernels that wait on each other side by side
+    const char* my_uuid = blobs + (size_t)pc.tab.me * AERO_EP_IPC_BYTES + sizeof(cudaIpcMemHandle_t);
+    for (int r = 0; r < n; ++r)
+        if (r != pc.tab.me &&
+            std::memcmp(blobs + (size_t)r * AERO_EP_IPC_BYTES + sizeof(cudaIpcMemHandle_t), my_uuid,
+                        sizeof(cudaUUID_t)) == 0)
+            return h->fail("rank %d runs on this rank's GPU %d: the peer exchange needs one GPU per rank", r, h->device),
+                   -1;
+    pc.mapped.assign(n, nullptr);
+    for (int r = 0; r < n; ++r) {
+        if (r == pc.tab.me) continue;
+        cudaIpcMemHandle_t ih;
+        std::memcpy(&ih, blobs + (size_t)r * AERO_EP_IPC_BYTES, sizeof ih);
+        void* p = nullptr;
+        if (!h->cuda_ok(cudaIpcOpenMemHandle(&p, ih, cudaIpcMemLazyEnablePeerAccess), "opening a peer's window"))
+            return h->fail("rank %d's window: %s", r, h->err.c_str()), -1;
+        pc.mapped[r] = static_cast<char*>(p);
+        pc.tab.base[r] = static_cast<char*>(p);
+    }
+    pc.connected = true;
+    return 0;
+}
+
+int aero_cuda_ep_peer_step(void* handle, const float* x, int T, float* out) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    auto& pc = h->peer;
+    if (!pc.connected) return h->fail("the peer exchange is not connected"), -1;
+    const auto& tab = pc.tab;
+    if (T < 0 || T > tab.slab) return h->fail("T=%d outside [0, slab_rows=%d]", T, tab.slab), -1;
+    if (T > 0) {
+        if (!x || !out) return h->fail("null buffer"), -1;
+        for (const void* p : {(const void*)x, (const void*)out})
+            if (!aero::is_device_ptr(p) || ((uintptr_t)p & 15) != 0)
+                return h->fail("x and out must be 16-byte aligned device memory"), -1;
+    }
+    cudaSetDevice(h->device);
+    auto& s = h->sc;
+    const int n = tab.n, me = tab.me, R = n * tab.slab;
+    const bool f16 = tab.rows_f16 != 0;
+    int32_t* send_tok = pc.aux;
+    int32_t* counts = pc.aux + R;
+    int32_t* pos = counts + n + 1;
+    const uint32_t epoch = ++pc.epoch;
+    cudaStream_t st = h->stream;
+    auto mark = [&](int i) {
+        if (pc.prof) cudaEventRecord(pc.ev[i], st);
+    };
+    bool ok = true;
+    mark(0);
+    if (T > 0) {
+        ok = aero::route_stage(*h, x, T, nullptr, false);
+    } else {
+        for (int i = 0; i < 3; ++i) h->mark(i);
+    }
+    mark(1);
+    ok = ok && h->cuda_ok(aero::launch_ep_peer_plan(s.idx, T, h->k, pc.rt, me, tab.slab, send_tok, counts, pos, st),
+                          "exchange plan");
+    ok = ok && h->cuda_ok(aero::launch_ep_peer_pack(tab, x, T, s.idx, s.w, s.sgate, h->has_shared, pc.rt, send_tok,
+                                                    counts, epoch, h->n_sm, st),
+                          "exchange pack");
+    mark(2);
+    ok = ok && h->cuda_ok(aero::launch_ep_peer_prep(tab, T, h->e_begin, h->e_end, h->E, epoch, s.idx, s.w, s.sgate,
+                                                    s.ep_bad, h->n_sm, st),
+                          "exchange unpack");
+    const void* rows = tab.base[me] + tab.off_rows;
+    const bool gemv = !f16 && !(h->gemm_ok && h->gb_ready && R >= h->gemm_min_tokens);
+    if (ok && gemv && s.xq.q1)
+        ok = h->cuda_ok(aero::launch_qinput(static_cast<const float*>(rows), R, h->dp, s.xq, st), "row codes");
+    mark(3);
+    ok = ok && aero::expert_stage(*h, rows, f16, R, T, true, pc.y, f16);
+    mark(4);
+    ok = ok && h->cuda_ok(aero::launch_ep_peer_return(tab, pc.y, epoch, h->n_sm, st), "exchange return");
+    mark(5);
+    ok = ok && h->cuda_ok(aero::launch_ep_peer_combine(tab, pc.y, pos, T, epoch, out, h->n_sm, st), "exchange combine");
+    mark(6);
+    h->launches += 5 + (gemv ? 1 : 0);
+    if (!ok) return -1;
+    if (h->profiling && !aero::finish_profile(*h)) return -1;
+    if (pc.prof) {
+        if (!h->cuda_ok(cudaEventSynchronize(pc.ev[6]), "profile")) return -1;
+        for (int i = 0; i < aero::PeerCtx::kPhases; ++i) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, pc.ev[i], pc.ev[i + 1]);
+            pc.ms[i] += ms;
+        }
+        pc.n_prof += 1;
+    }
+    h->calls += 1;
+    h->tokens += T;
+    return 0;
+}
+
+// 0: every wait of the steps so far completed; otherwise the code of the first
+// that gave up (21: rows, 22: returns). Synchronises the handle's stream.
+int aero_cuda_ep_peer_status(void* handle) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    auto& pc = h->peer;
+    if (!pc.open) return h->fail("the peer exchange is not open"), -1;
+    cudaSetDevice(h->device);
+    int32_t v = 0;
+    if (!h->cuda_ok(cudaMemcpyAsync(&v, pc.window + pc.tab.off_err, 4, cudaMemcpyDeviceToHost, h->stream), "status") ||
+        !h->cuda_ok(cudaStreamSynchronize(h->stream), "status"))
+        return -1;
+    return v;
+}
+
+int aero_cuda_ep_peer_counts(void* handle, int32_t* sent, int32_t* received) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    auto& pc = h->peer;
+    if (!pc.connected) return h->fail("the peer exchange is not connected"), -1;
+    cudaSetDevice(h->device);
+    const int n = pc.tab.n, me = pc.tab.me, R = n * pc.tab.slab;
+    std::vector<int32_t> c(n + 1), w(n);
+    if (!h->cuda_ok(cudaMemcpyAsync(c.data(), pc.aux + R, (size_t)n * 4, cudaMemcpyDeviceToHost, h->stream), "counts") ||
+        !h->cuda_ok(cudaMemcpyAsync(w.data(), pc.window + pc.tab.off_cnt, (size_t)n * 4, cudaMemcpyDeviceToHost,
+                                    h->stream),
+                    "counts") ||
+        !h->cuda_ok(cudaStreamSynchronize(h->stream), "counts"))
+        return -1;
+    for (int r = 0; r < n; ++r) {
+        if (sent) sent[r] = r == me ? 0 : c[r];
+        if (received) received[r] = r == me ? 0 : w[(r - me + n) % n];
+    }
+    return 0;
+}
+
+// on != 0: time the phases of every step (synchronises each step); ms (6
+// doubles, may be null) receives the mean per phase since the last read:
+// route, pack, rows wait + unpack, experts, return, combine. Returns the
+// number of steps averaged.
+int aero_cuda_ep_peer_profile(void* handle, int on, double* ms) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    auto& pc = h->peer;
+    if (!pc.open) return h->fail("the peer exchange is not open"), -1;
+    cudaSetDevice(h->device);
+    const long n = pc.n_prof;
+    for (int i = 0; i < aero::PeerCtx::kPhases; ++i) {
+        if (ms) ms[i] = n ? pc.ms[i] / n : 0.0;
+        pc.ms[i] = 0.0;
+    }
+    pc.n_prof = 0;
+    if (on && !pc.ev[0])
+        for (auto& e : pc.ev)
+            if (!h->cuda_ok(cudaEventCreate(&e), "profile events")) return -1;
+    pc.prof = on != 0;
+    return (int)n;
+}
+
+int aero_cuda_ep_peer_close(void* handle) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (!h->peer.open) return 0;
+    cudaSetDevice(h->device);
+    cudaStreamSynchronize(h->stream);
+    h->peer_release();
+    return 0;
 }
 
 const char* aero_cuda_moe_last_error(void* handle) {

@@ -48,7 +48,7 @@ constexpr size_t kOffActOff = kOffActE + al256((size_t)kNoAllocMaxExperts * 4); 
 constexpr size_t kOffNAct = kOffActOff + al256((size_t)(kNoAllocMaxExperts + 1) * 4);
 constexpr size_t kOffFlag = kOffNAct + 256;                                     // int32 error flag
 constexpr size_t kOffWork = kOffFlag + 256;                                     // per-chunk histograms
-static_assert(kOffWork + (size_t)((kNoAllocMaxPairs + 255) / 256) * kNoAllocMaxExperts * 4 <= kNoAllocScratchBytes,
+static_assert(kOffWork + (size_t)((kNoAllocMaxPairs + 255) / 256 + 1) * kNoAllocMaxExperts * 4 <= kNoAllocScratchBytes,
               "no-alloc scratch layout does not fit");
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];

@@ -234,8 +234,38 @@ __global__ void dispatch_count_kernel(const int32_t* __restrict__ idx, int P, in
 
 constexpr int kScanThreads = 1024;
 
-__global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(int32_t* __restrict__ counts, int n_chunks,
-                                                                     int E, int n_real, int P,
+// Per expert (a lane of each warp), the chunk histogram becomes the
+// within-expert exclusive prefix over chunks: warp w of the CTA sums a
+// contiguous run of chunks, the runs are prefixed across warps, and each run
+// is rewritten from its prefix. totals[e] = the expert's pair count.
+__global__ void __launch_bounds__(kScanThreads) dispatch_colscan_kernel(int32_t* __restrict__ counts, int n_chunks,
+                                                                        int E, int32_t* __restrict__ totals) {
+    __shared__ int part[32][33];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int e = blockIdx.x * 32 + lane;
+    const int per = (n_chunks + 31) / 32;
+    const int c0 = warp * per, c1 = min(n_chunks, c0 + per);
+    int sum = 0;
+    if (e < E)
+        for (int c = c0; c < c1; ++c) sum += counts[(int64_t)c * E + e];
+    part[warp][lane] = sum;
+    __syncthreads();
+    int run = 0;
+    for (int w = 0; w < warp; ++w) run += part[w][lane];
+    if (e < E) {
+        for (int c = c0; c < c1; ++c) {
+            const int v = counts[(int64_t)c * E + e];
+            counts[(int64_t)c * E + e] = run;
+            run += v;
+        }
+        if (warp == 31) totals[e] = run;
+    }
+}
+
+// Expert offsets (exclusive prefix of totals), offsets[E] = P, and the active
+// experts below n_real in order with their offsets.
+__global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(const int32_t* __restrict__ totals, int E,
+                                                                     int n_real, int P,
                                                                      int32_t* __restrict__ offsets,
                                                                      int32_t* __restrict__ act_e,
                                                                      int32_t* __restrict__ act_off,
@@ -250,15 +280,7 @@ __global__ void __launch_bounds__(kScanThreads) dispatch_scan_kernel(int32_t* __
     __syncthreads();
     for (int e0 = 0; e0 < E; e0 += kScanThreads) {
         const int e = e0 + threadIdx.x;
-        int tot = 0;
-        if (e < E) {
-            // counts[c][e] becomes the within-expert exclusive prefix over chunks
-            for (int c = 0; c < n_chunks; ++c) {
-                const int v = counts[(int64_t)c * E + e];
-                counts[(int64_t)c * E + e] = tot;
-                tot += v;
-            }
-        }
+        const int tot = e < E ? totals[e] : 0;
         int excl, excl_act;
         Scan(tmp).ExclusiveSum(tot, excl);
         __syncthreads();
@@ -370,7 +392,7 @@ cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int no
 size_t dispatch_work_bytes(int P, int E) {
     const int chunk = dispatch_chunk(P);
     const size_t n_chunks = (size_t)(P + chunk - 1) / chunk;
-    return std::max<size_t>(1, n_chunks) * (size_t)E * sizeof(int32_t);
+    return (std::max<size_t>(1, n_chunks) + 1) * (size_t)E * sizeof(int32_t);  // histograms, then totals
 }
 
 cudaError_t launch_dispatch(const int32_t* idx, int P, int E, int32_t* offsets, int32_t* perm, int32_t* inv,
@@ -380,9 +402,11 @@ cudaError_t launch_dispatch(const int32_t* idx, int P, int E, int32_t* offsets, 
     const int chunk = dispatch_chunk(P);
     const int n_chunks = std::max(1, (P + chunk - 1) / chunk);
     int32_t* counts = static_cast<int32_t*>(work);
+    int32_t* totals = counts + (size_t)n_chunks * E;
     const size_t hist_smem = (size_t)E * sizeof(int32_t);
     dispatch_count_kernel<<<n_chunks, 256, hist_smem, s>>>(idx, P, E, chunk, counts);
-    dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(counts, n_chunks, E, n_real, P, offsets, act_e, act_off, n_active);
+    dispatch_colscan_kernel<<<(E + 31) / 32, kScanThreads, 0, s>>>(counts, n_chunks, E, totals);
+    dispatch_scan_kernel<<<1, kScanThreads, 0, s>>>(totals, E, n_real, P, offsets, act_e, act_off, n_active);
     dispatch_scatter_kernel<<<n_chunks, 128, hist_smem, s>>>(idx, P, E, chunk, offsets, counts, perm, inv);
     return cudaGetLastError();
 }

@@ -24,6 +24,9 @@
 //               the epilogue: TMEM -> registers (+ bias) -> logits rows
 // The CTAs of the first column tile also compute the shared-expert gate column
 // (x . g over K in stage order) on the split warps, which touch every x value.
+// Batches too small to cover the SMs split K over up to 8 CTA layers (grid z);
+// each layer writes its partial logits and router_reduce_kernel adds the
+// layers in order, then the bias (deterministic for a given batch size).
 // Every mbarrier wait is bounded; a CTA that gives up records an error code and
 // drains its issued MMAs before freeing TMEM.
 #include <cuda.h>
@@ -49,7 +52,7 @@ constexpr size_t kRtSmem = (size_t)kRtStages * kRtStageBytes + 1024 + 256;
 enum : int { kRtErrFull = 11, kRtErrSplit = 12, kRtErrEmpty = 13, kRtErrAcc = 14 };
 
 struct RouterTcParams {
-    int T, K;          // tokens, reduction length (dp)
+    int T, K;          // tokens, reduction length of one K split (dp / splits)
     int n_rows, N;     // router rows on the tensor cores; rows per CTA tile
     const float* bias;
     int n_bias;
@@ -57,6 +60,7 @@ struct RouterTcParams {
     float* logits;
     int ld;
     int32_t* err;
+    float* partial;    // split K: per-split logits [split][T][ld] (no bias), summed by router_reduce_kernel
 };
 
 __device__ __forceinline__ float tf32_hi(float v) {
@@ -85,6 +89,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int m0 = blockIdx.x * kRtM, n0 = blockIdx.y * p.N;
     const int nk = p.K / kRtK;
+    const int kbase = (int)blockIdx.z * p.K;  // this CTA's K split
     const uint32_t tmem_cols = kRtTmemCols;
     auto fail = [&](int code) {
         *abort_flag = 1;
@@ -122,9 +127,9 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
                     break;
                 }
                 mbar_expect_tx(full(s), bytes);
-                tma_load_2d(smem_u32(xh(s)), &tx, kb * kRtK, m0, full(s));
-                tma_load_2d(smem_u32(wh(s)), &twh, kb * kRtK, n0, full(s));
-                tma_load_2d(smem_u32(wl(s)), &twl, kb * kRtK, n0, full(s));
+                tma_load_2d(smem_u32(xh(s)), &tx, kbase + kb * kRtK, m0, full(s));
+                tma_load_2d(smem_u32(wh(s)), &twh, kbase + kb * kRtK, n0, full(s));
+                tma_load_2d(smem_u32(wl(s)), &twl, kbase + kb * kRtK, n0, full(s));
             }
         }
     } else if (warp == 1) {
@@ -177,7 +182,7 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
             }
             uint8_t* hrow = xh(s) + r * 128;
             uint8_t* lrow = xl(s) + r * 128;
-            const float* g = do_gate ? p.gate_row + kb * kRtK : nullptr;
+            const float* g = do_gate ? p.gate_row + kbase + kb * kRtK : nullptr;
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 const int off = (c ^ (r & 7)) << 4;  // 128B swizzle: logical chunk c of row r
@@ -205,7 +210,11 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
             } else {
                 tc_fence_after();
                 const uint32_t lane_base = (uint32_t)(q * 32) << 16;
-                float* out = p.logits + (int64_t)row * p.ld + n0;
+                // split K: this split's partial sums, reduced (with the bias) by a second kernel
+                const bool part = p.partial != nullptr;
+                float* dst = part ? p.partial + (size_t)blockIdx.z * p.T * p.ld : p.logits;
+                const float* bias = part ? nullptr : p.bias;
+                float* out = dst + (int64_t)row * p.ld + n0;
                 for (int c0 = 0; c0 < p.N; c0 += 16) {
                     uint32_t v0[16], v1[16], vc[16];
                     tmem_ld16(tmem + lane_base + (uint32_t)c0, v0);
@@ -221,17 +230,17 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
                         for (int j = 0; j < 16; j += 4) {
                             const int e = n0 + c0 + j;
                             float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-                            if (p.bias) {
-                                if (e < p.n_bias) o.x += p.bias[e];
-                                if (e + 1 < p.n_bias) o.y += p.bias[e + 1];
-                                if (e + 2 < p.n_bias) o.z += p.bias[e + 2];
-                                if (e + 3 < p.n_bias) o.w += p.bias[e + 3];
+                            if (bias) {
+                                if (e < p.n_bias) o.x += bias[e];
+                                if (e + 1 < p.n_bias) o.y += bias[e + 1];
+                                if (e + 2 < p.n_bias) o.z += bias[e + 2];
+                                if (e + 3 < p.n_bias) o.w += bias[e + 3];
                             }
                             *reinterpret_cast<float4*>(out + c0 + j) = o;
                         }
                     }
                 }
-                if (do_gate && row < p.T) p.logits[(int64_t)row * p.ld + p.n_rows] = g_acc;
+                if (do_gate && row < p.T) dst[(int64_t)row * p.ld + p.n_rows] = g_acc;
             }
         }
     }
@@ -241,6 +250,19 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
         tc_fence_after();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(tmem_cols));
     }
+}
+
+// logits[t][c] = sum over splits (in order) of partial[s][t][c] (+ bias[c] for c < n_bias),
+// for c < cols (the router rows and, when present, the shared-gate column).
+__global__ void router_reduce_kernel(const float* __restrict__ partial, int splits, int T, int ld, int cols,
+                                     const float* __restrict__ bias, int n_bias, float* __restrict__ logits) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)T * cols) return;
+    const int t = (int)(i / cols), c = (int)(i % cols);
+    float v = 0.f;
+    for (int sp = 0; sp < splits; ++sp) v += partial[((size_t)sp * T + t) * ld + c];
+    if (bias && c < n_bias) v += bias[c];
+    logits[(int64_t)t * ld + c] = v;
 }
 
 __global__ void split_tf32_kernel(const float* __restrict__ in, int64_t n, float* __restrict__ hi,
@@ -282,7 +304,8 @@ cudaError_t router_tc_prepare(const float* W, int n_rows, int dp, float* w_hi, f
 }
 
 cudaError_t launch_router_tc(const RouterTcMaps& maps, const float* x, int T, const float* bias, int n_bias,
-                             const float* gate_row, float* logits, int ld, int32_t* err, cudaStream_t s) {
+                             const float* gate_row, float* logits, int ld, int32_t* err, float* partial,
+                             int partial_rows, int n_sm, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
     if ((ld & 3) || ((uintptr_t)logits & 15)) return cudaErrorInvalidValue;
     CUtensorMap tx;
@@ -296,9 +319,21 @@ cudaError_t launch_router_tc(const RouterTcMaps& maps, const float* x, int T, co
         if (e != cudaSuccess) return e;
         configured = true;
     }
+    // small batches: split K over up to 8 CTA layers (one CTA per SM), taking
+    // the split count with the fewest K blocks per SM, fewer splits on ties
+    // (each split writes partial logits; a second kernel adds them in order)
+    const int tiles = ((T + kRtM - 1) / kRtM) * (maps.n_rows / maps.N);
+    int splits = 1;
+    auto work = [&](int sp) { return (int64_t)((tiles * sp + n_sm - 1) / n_sm) * (maps.dp / sp); };
+    // (a split keeps at least two K blocks: the two main accumulators alternate per block)
+    for (int sp = 2; partial && sp <= 8; sp *= 2)
+        if (maps.dp % (sp * kRtK) == 0 && maps.dp / sp >= 2 * kRtK && (int64_t)sp * T <= partial_rows &&
+            work(sp) < work(splits))
+            splits = sp;
     RouterTcParams p{};
     p.T = T;
-    p.K = maps.dp;
+    p.K = maps.dp / splits;
+    p.partial = splits > 1 ? partial : nullptr;
     p.n_rows = maps.n_rows;
     p.N = maps.N;
     p.bias = bias;
@@ -307,8 +342,14 @@ cudaError_t launch_router_tc(const RouterTcMaps& maps, const float* x, int T, co
     p.logits = logits;
     p.ld = ld;
     p.err = err;
-    dim3 grid((T + kRtM - 1) / kRtM, maps.n_rows / maps.N);
+    dim3 grid((T + kRtM - 1) / kRtM, maps.n_rows / maps.N, splits);
     router_tc_kernel<<<grid, kRtThreads, kRtSmem, s>>>(tx, maps.hi, maps.lo, p);
+    if (splits > 1) {
+        const int cols = maps.n_rows + (gate_row ? 1 : 0);
+        const int64_t n = (int64_t)T * cols;
+        router_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(partial, splits, T, ld, cols, bias, n_bias,
+                                                                         logits);
+    }
     return cudaGetLastError();
 }
 

@@ -29,10 +29,12 @@ waits inside a step.
 
 from __future__ import annotations
 
+import ctypes
 from typing import List
 
 ROWS_F32 = 0
 ROWS_F16 = 1
+IPC_BYTES = 128  # AERO_EP_IPC_BYTES
 
 
 def expert_ranges(n_expert: int, world: int) -> List[int]:
@@ -249,6 +251,138 @@ class ExpertParallelMoe:
             self.phase_n += 1
 
     __call__ = forward
+
+
+class PeerExpertParallelMoe:
+    """One rank's share of an expert-parallel MoE layer, exchanging over peer memory.
+
+    Same step as ExpertParallelMoe (same partial sums, added in the same rank
+    order), with no collective library inside it: every rank's exchange window
+    is mapped into the other ranks' processes (CUDA IPC), the dispatch kernel
+    stores the rows straight into their owners' windows, the owners' return
+    kernel stores the partial outputs straight back, and the kernels wait for
+    the peers' step flags (aero_cuda_ep_peer_* in the C ABI). One GPU per rank.
+    Construction and `close` are collective over `group` (all-gather of the
+    window handles, barriers); every rank must run the same number of steps.
+    `gather(bytes) -> list of bytes in rank order` replaces the all-gather.
+    """
+
+    PHASES = ("route", "pack", "rows_wait", "experts", "return", "combine")
+
+    def __init__(self, layer, n_embd: int, n_expert: int, k: int, world: int, rank: int, max_tokens: int,
+                 device="cuda", group=None, row_f16: bool = True, gather=None) -> None:
+        import torch
+        import torch.distributed as dist
+
+        from . import native_cuda as nc
+
+        self.torch, self.dist, self.nc = torch, dist, nc
+        self.lib = nc.lib()
+        self.layer, self.h = layer, layer.handle
+        self.d, self.E, self.k = n_embd, n_expert, k
+        self.world, self.rank, self.group = world, rank, group
+        self.begin = expert_ranges(n_expert, world)
+        self.row_dtype = ROWS_F16 if row_f16 else ROWS_F32
+        self.device = torch.device(device)
+        self.max_tokens = max(1, int(max_tokens))
+        self.stream = torch.cuda.Stream(device=self.device)
+        layer.set_stream(self.stream)
+        tab = (nc.c_int32 * len(self.begin))(*self.begin)
+        ipc = (ctypes.c_char * IPC_BYTES)()
+        rc = self.lib.aero_cuda_ep_peer_open(self.h, world, rank, tab, self.max_tokens, self.row_dtype, ipc)
+        self.opened = rc == 0
+        err = "" if self.opened else nc.last_error(self.h)
+        blobs = (gather or self._gather)(bytes(ipc) if self.opened else b"")
+        if not all(len(b) == IPC_BYTES for b in blobs):
+            self.close(barrier=False)
+            raise RuntimeError(f"peer exchange unavailable: rank {rank}: {err or 'another rank failed to open'}")
+        allh = b"".join(blobs)
+        rc = self.lib.aero_cuda_ep_peer_connect(self.h, allh)
+        ok = self._all_ok(rc == 0)
+        if not ok:
+            why = nc.last_error(self.h) if rc != 0 else "another rank failed to connect"
+            self.close(barrier=False)
+            raise RuntimeError(f"peer exchange unavailable: rank {rank}: {why}")
+        torch.cuda.synchronize(self.device)
+        if dist.is_initialized():
+            dist.barrier(group=group)
+        self.phase_ms = {k: 0.0 for k in self.PHASES}
+        self.phase_n = 0
+
+    def _gather(self, blob: bytes):
+        dist, torch = self.dist, self.torch
+        if self.world == 1:
+            return [blob]
+        t = torch.zeros(IPC_BYTES + 1, dtype=torch.uint8, device=self.device)
+        if blob:
+            t[:IPC_BYTES] = torch.frombuffer(bytearray(blob), dtype=torch.uint8)
+            t[IPC_BYTES] = 1
+        out = torch.empty(self.world * (IPC_BYTES + 1), dtype=torch.uint8, device=self.device)
+        dist.all_gather_into_tensor(out, t, group=self.group)
+        rows = out.view(self.world, IPC_BYTES + 1).cpu()
+        return [bytes(r[:IPC_BYTES].numpy().tobytes()) if int(r[IPC_BYTES]) else b"" for r in rows]
+
+    def _all_ok(self, ok: bool) -> bool:
+        dist, torch = self.dist, self.torch
+        if not dist.is_initialized() or self.world == 1:
+            return ok
+        f = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.device)
+        dist.all_reduce(f, op=dist.ReduceOp.MIN, group=self.group)
+        return bool(int(f.item()))
+
+    def forward(self, x):
+        torch = self.torch
+        T = int(x.shape[0])
+        if x.dim() != 2 or x.shape[1] != self.d:
+            raise ValueError(f"hidden width {tuple(x.shape)} != n_embd {self.d}")
+        if T > self.max_tokens:
+            raise ValueError(f"{T} tokens on rank {self.rank} > max_tokens {self.max_tokens}")
+        x = x.contiguous().float()
+        out = torch.empty((T, self.d), dtype=torch.float32, device=self.device)
+        caller = torch.cuda.current_stream(self.device)
+        self.stream.wait_stream(caller)
+        rc = self.lib.aero_cuda_ep_peer_step(self.h, x.data_ptr() if T else None, T, out.data_ptr() if T else None)
+        if rc != 0:
+            raise RuntimeError(f"aero_cuda_ep_peer_step: {self.nc.last_error(self.h)}")
+        caller.wait_stream(self.stream)
+        x.record_stream(self.stream)
+        out.record_stream(self.stream)
+        return out
+
+    __call__ = forward
+
+    def status(self) -> int:
+        """0, or the code of the first wait that gave up (synchronises)."""
+        return int(self.lib.aero_cuda_ep_peer_status(self.h))
+
+    @property
+    def last_split(self):
+        """(rows sent to each rank, rows received from each rank) in the last step (synchronises)."""
+        sent = (self.nc.c_int32 * self.world)()
+        recv = (self.nc.c_int32 * self.world)()
+        if self.lib.aero_cuda_ep_peer_counts(self.h, sent, recv) != 0:
+            raise RuntimeError(self.nc.last_error(self.h))
+        return list(sent), list(recv)
+
+    def set_profiling(self, on: bool) -> None:
+        """Time the step's phases (synchronises each step); read them with `read_phases`."""
+        self.lib.aero_cuda_ep_peer_profile(self.h, 1 if on else 0, None)
+
+    def read_phases(self):
+        """Mean device ms per phase since the last read."""
+        ms = (ctypes.c_double * len(self.PHASES))()
+        n = self.lib.aero_cuda_ep_peer_profile(self.h, 1, ms)
+        return {k: float(v) for k, v in zip(self.PHASES, ms)}, int(n)
+
+    def close(self, barrier: bool = True) -> None:
+        """Collective: waits for this rank's work, then for every rank, then frees the window."""
+        if self.h is None:
+            return
+        self.torch.cuda.synchronize(self.device)
+        if barrier and self.dist.is_initialized() and self.world > 1:
+            self.dist.barrier(group=self.group)
+        self.lib.aero_cuda_ep_peer_close(self.h)
+        self.h = None
 
 
 def open_rank_layer(layer_src, world: int, rank: int, device: int = 0):

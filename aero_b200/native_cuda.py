@@ -13,7 +13,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import (CFUNCTYPE, POINTER, Structure, c_char_p, c_float, c_int, c_int32, c_int64,
+from ctypes import (CFUNCTYPE, POINTER, Structure, c_char_p, c_double, c_float, c_int, c_int32, c_int64,
                     c_long, c_size_t, c_uint, c_uint8, c_void_p)
 
 import numpy as np
@@ -82,6 +82,13 @@ SYMBOLS = [
     ("aero_cuda_ep_expert_block", c_int, [_P, _P, c_int, _P, c_int, c_int, _P, c_int]),
     ("aero_cuda_ep_combine", c_int, [_P, _P, _P, c_int, _P, c_int, c_int, c_int, _P]),
     ("aero_cuda_ep_bad_ids", c_int, [_P]),
+    ("aero_cuda_ep_peer_open", c_int, [_P, c_int, c_int, POINTER(c_int32), c_int, c_int, _P]),
+    ("aero_cuda_ep_peer_connect", c_int, [_P, _P]),
+    ("aero_cuda_ep_peer_step", c_int, [_P, _P, c_int, _P]),
+    ("aero_cuda_ep_peer_status", c_int, [_P]),
+    ("aero_cuda_ep_peer_counts", c_int, [_P, POINTER(c_int32), POINTER(c_int32)]),
+    ("aero_cuda_ep_peer_profile", c_int, [_P, c_int, POINTER(c_double)]),
+    ("aero_cuda_ep_peer_close", c_int, [_P]),
     ("aero_cuda_moe_set_stream", c_int, [_P, _P]),
     ("aero_cuda_moe_info", c_int, [_P, POINTER(c_int32)]),
     ("aero_cuda_moe_last_error", c_char_p, [_P]),

@@ -10,8 +10,10 @@ counts. A step is one layer call over the workload's tokens (config 1: 64
 one-token calls). Inputs are synthetic (seeded N(0,1) activations, N(0,0.02)
 weights quantised to GGUF blocks); no datasets or checkpoints exist here.
 With N > 1 (torchrun, one process per GPU) the layer runs expert parallel:
-E/N experts and T/N tokens per rank, rows exchanged by NCCL all-to-all
-(aero_b200.ep); the step's token count stays T (strong scaling).
+E/N experts and T/N tokens per rank; the rows and partial outputs cross by
+stores into the peers' exchange windows (CUDA IPC over NVLink, no collective
+library in the step; --exchange nccl uses NCCL all-to-all instead,
+aero_b200.ep); the step's token count stays T (strong scaling).
 
   value        tokens/s over K steps, inputs already in HBM, device time by
                CUDA events on the layer's stream (max over ranks)
@@ -164,6 +166,8 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="expert parallel (N > 1): rows cross by peer-memory stores (default) or NCCL all-to-all")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -234,10 +238,21 @@ def main():
         shards = ep.token_shards(T, ws)
         L = synth.open_layer(layer, device=dev, expert_range=(begin[rank], begin[rank + 1]))
         row_f16 = T >= 64  # prefill: rows cross in the GEMM operand type
-        with torch.cuda.stream(stream):
-            moe = ep.ExpertParallelMoe(ep.CudaEpOps(L), spec.d, spec.E, spec.k, ws, rank,
-                                       max_tokens=max(shards[r + 1] - shards[r] for r in range(ws)), device=cuda,
-                                       row_f16=row_f16)
+        max_tok = max(shards[r + 1] - shards[r] for r in range(ws))
+        moe = None
+        exchange = args.exchange
+        if exchange == "peer":
+            try:
+                moe = ep.PeerExpertParallelMoe(L, spec.d, spec.E, spec.k, ws, rank, max_tokens=max_tok, device=cuda,
+                                               row_f16=row_f16)
+            except RuntimeError as e:  # collective: every rank falls back together
+                if rank == 0:
+                    print(f"# {e}; using the NCCL all-to-all exchange", file=sys.stderr, flush=True)
+                exchange = "nccl"
+        if moe is None:
+            with torch.cuda.stream(stream):
+                moe = ep.ExpertParallelMoe(ep.CudaEpOps(L), spec.d, spec.E, spec.k, ws, rank, max_tokens=max_tok,
+                                           device=cuda, row_f16=row_f16)
         x_mine = x_host[shards[rank]:shards[rank + 1]]
     else:
         L = synth.open_layer(layer, device=dev)
@@ -275,6 +290,10 @@ def main():
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(dev) as clk, torch.cuda.stream(stream):
+        # the sampler's start-up differs per rank: line the ranks up after it
+        if ws > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
         ev0.record(stream)
         for _ in range(args.steps):
             step_device()
@@ -391,6 +410,8 @@ def main():
         "stages_ms": {k: round(v, 5) for k, v in stage_avg.items()},
     }
     if ep_mode:
+        result["config"]["exchange"] = "peer memory (CUDA IPC, NVLink stores)" if exchange == "peer" else \
+            "NCCL all-to-all"
         result["exchange_rows"] = {"sent": moe.last_split[0], "received": moe.last_split[1]}
         # per-phase device times of rank 0's step (a separate profiled pass)
         moe.set_profiling(True)
@@ -398,7 +419,12 @@ def main():
             for _ in range(3):
                 step_device()
         stream.synchronize()
-        result["ep_phases_ms"] = {k: round(v / max(moe.phase_n, 1), 5) for k, v in moe.phase_ms.items()}
+        if exchange == "peer":
+            ph, _ = moe.read_phases()
+            result["ep_phases_ms"] = {k: round(v, 5) for k, v in ph.items()}
+            result["exchange_status"] = moe.status()
+        else:
+            result["ep_phases_ms"] = {k: round(v / max(moe.phase_n, 1), 5) for k, v in moe.phase_ms.items()}
         moe.set_profiling(False)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         lg = x_host @ layer.router.T + (layer.router_bias if layer.router_bias is not None else 0)

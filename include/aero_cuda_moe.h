@@ -207,6 +207,41 @@ int aero_cuda_ep_combine(void* handle, const void* self_out, const void* back, i
  * does not hold (they were skipped). Synchronises the handle's stream. */
 int aero_cuda_ep_bad_ids(void* handle);
 
+/* Expert parallel over peer memory: the same step without a collective
+ * library. Each rank allocates an exchange window (rows, metadata and returned
+ * partials for n_ranks slabs of slab_rows rows, plus step flags) that the other
+ * ranks map through CUDA IPC; the dispatch kernel stores the rows straight into
+ * the owners' windows over NVLink, the owners' return kernel stores the partial
+ * outputs straight back, and kernels wait for the peers' step flags (bounded
+ * waits; a wait that gives up is reported by aero_cuda_ep_peer_status). Needs
+ * one GPU per rank with peer access between them. Protocol:
+ *   aero_cuda_ep_peer_open on every rank -> all-gather the AERO_EP_IPC_BYTES
+ *   handles (rank order) -> aero_cuda_ep_peer_connect -> a host barrier ->
+ *   steps (aero_cuda_ep_peer_step, every rank the same number of times, T = 0
+ *   allowed) -> synchronise, host barrier -> aero_cuda_ep_peer_close. */
+#define AERO_EP_IPC_BYTES 128
+int aero_cuda_ep_peer_open(void* handle, int n_ranks, int rank, const int32_t* rank_expert_begin,
+                           int slab_rows, int row_dtype, void* ipc_out);
+/* ipc_all: n_ranks blobs of AERO_EP_IPC_BYTES bytes (as written by
+ * aero_cuda_ep_peer_open), in rank order. Refused when two ranks share a GPU. */
+int aero_cuda_ep_peer_connect(void* handle, const void* ipc_all);
+/* x (T, n_embd) f32 device, T <= slab_rows -> out (T, n_embd) f32 device;
+ * enqueued on the handle's stream. */
+int aero_cuda_ep_peer_step(void* handle, const float* x, int T, float* out);
+/* 0, or the code of the first wait that gave up (21 rows, 22 returns);
+ * synchronises the handle's stream. */
+int aero_cuda_ep_peer_status(void* handle);
+/* Rows sent to / received from each rank in the last step (host arrays of
+ * n_ranks; synchronises). */
+int aero_cuda_ep_peer_counts(void* handle, int32_t* sent, int32_t* received);
+/* Phase timing (on != 0; synchronises each step); ms (6 doubles or NULL): mean
+ * device time per phase since the last read (route, pack, rows wait + unpack,
+ * experts, return, combine). Returns the number of steps averaged. */
+int aero_cuda_ep_peer_profile(void* handle, int on, double* ms);
+/* Unmaps the peers' windows and frees this rank's (call after a host barrier
+ * that follows every rank's last step). */
+int aero_cuda_ep_peer_close(void* handle);
+
 /* Run the handle's work on this cudaStream_t (NULL: the handle's own stream). */
 int aero_cuda_moe_set_stream(void* handle, void* stream);
 /* Layer geometry: out[0..7] = n_embd, n_expert, n_expert_used, ffn_len,

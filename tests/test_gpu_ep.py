@@ -272,3 +272,98 @@ def test_ep_nccl_two_gpus():
     finally:
         L.close()
     assert rel_err(msg[1], single) <= 5e-3  # f16 partial rows cross the network
+
+
+def _peer_worker(rank, world, port, q):
+    try:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        wl = synth.CONFIGS["c5"]
+        layer = synth.make_layer(wl.spec, 0, device_gen=True)
+        T = 1024
+        x = synth.make_x(T, wl.spec.d, 4)
+        shards = ep.token_shards(T, world)
+        begin = ep.expert_ranges(wl.spec.E, world)
+        dev = f"cuda:{rank}"
+        h = synth.open_layer(layer, device=rank, expert_range=(begin[rank], begin[rank + 1]))
+        mine = torch.from_numpy(x[shards[rank]:shards[rank + 1]]).to(dev)
+
+        def gather(o):
+            outs = [torch.empty((shards[r + 1] - shards[r], wl.spec.d), device=dev) for r in range(world)]
+            dist.all_gather(outs, o.contiguous())
+            return torch.cat(outs).cpu().numpy()
+
+        # the all-to-all path first, as the reference for the peer path
+        m = ep.ExpertParallelMoe(ep.CudaEpOps(h), wl.spec.d, wl.spec.E, wl.spec.k, world, rank, max_tokens=T,
+                                 device=dev)
+        ref = gather(m.forward(mine))
+        torch.cuda.synchronize()
+        m.close()
+        p = ep.PeerExpertParallelMoe(h, wl.spec.d, wl.spec.E, wl.spec.k, world, rank, max_tokens=T, device=dev)
+        o1 = gather(p.forward(mine))
+        o2 = gather(p.forward(mine))  # second step: flags of the next epoch, buffers reused
+        sent, recv = p.last_split
+        # third step: every token on rank 0, none on the others
+        x0 = torch.from_numpy(x).to(dev) if rank == 0 else torch.empty((0, wl.spec.d), device=dev)
+        o3 = p.forward(x0)
+        torch.cuda.synchronize()
+        o3 = o3.cpu().numpy() if rank == 0 else None
+        st = p.status()
+        p.close()
+        if rank == 0:
+            q.put(("ok", (ref, o1, o2, o3, st, sent, recv)))
+        dist.barrier()
+        h.close()
+        dist.destroy_process_group()
+    except Exception as e:
+        import traceback
+
+        q.put(("err", f"rank {rank}: {e}\n{traceback.format_exc()}"))
+
+
+def test_ep_peer_two_gpus():
+    """Rows and partial outputs cross by peer stores; the result matches the all-to-all path's."""
+    import torch
+    import torch.multiprocessing as mp
+
+    nc.require_gpu()
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    msg = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    assert msg[0] == "ok", msg[1]
+    ref, o1, o2, o3, st, sent, recv = msg[1]
+    assert st == 0
+    # same partial rows added in the same order as the all-to-all path; the
+    # expert products see the rows at other positions of their tiles
+    assert rel_err(o1, ref) <= 1e-3
+    assert np.array_equal(o1, o2)
+    assert sent[0] == 0 and recv[0] == 0 and 0 < sent[1] <= 512 and 0 < recv[1] <= 512
+    wl = synth.CONFIGS["c5"]
+    layer = synth.make_layer(wl.spec, 0, device_gen=True)
+    x = synth.make_x(1024, wl.spec.d, 4)
+    L = synth.open_layer(layer)
+    try:
+        L.set_gemm_min_tokens(1)
+        single = L.forward(x)
+    finally:
+        L.close()
+    assert rel_err(o1, single) <= 5e-3
+    assert rel_err(o3, single) <= 5e-3
