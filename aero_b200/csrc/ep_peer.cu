@@ -99,13 +99,14 @@ __device__ bool peer_wait(const EpPeerTable& p, int64_t flag_off, uint32_t epoch
 
 // Called by every thread of every CTA after its stores: the last CTA to get
 // here runs `last(tid)` for tid in [0, blockDim) after all CTAs' stores are
-// visible system-wide.
+// visible system-wide. (The barrier orders the CTA's stores before thread 0's
+// system-scope fence, which is cumulative over them.)
 template <typename F>
 __device__ __forceinline__ void after_all_ctas(uint32_t* done, F last) {
     __shared__ int is_last;
-    __threadfence_system();
     __syncthreads();
     if (threadIdx.x == 0) {
+        __threadfence_system();
         is_last = atomicAdd(done, 1u) == gridDim.x - 1;
         if (is_last) {
             *done = 0;  // ready for the next launch
@@ -247,7 +248,8 @@ __global__ void ep_peer_prep_kernel(EpPeerTable p, int T, int e_begin, int e_end
 // y rows of slabs 1..n-1 into the owners' back slabs (one warp per row,
 // 16-byte units), then the last CTA raises flag_back in every peer's window.
 template <typename PT>
-__global__ void ep_peer_return_kernel(EpPeerTable p, const PT* __restrict__ y, uint32_t epoch) {
+__global__ void ep_peer_return_kernel(EpPeerTable p, const PT* __restrict__ y, uint32_t epoch,
+                                      int32_t* __restrict__ recv_out) {
     const int n = p.n, me = p.me, slab = p.slab;
     const int lane = threadIdx.x & 31;
     const int units = p.dp * (int)sizeof(PT) / 16;
@@ -264,6 +266,78 @@ __global__ void ep_peer_return_kernel(EpPeerTable p, const PT* __restrict__ y, u
         for (int u = lane; u < units; u += 32) dst[u] = src[u];
     }
     after_all_ctas(wptr<uint32_t>(p, me, p.off_done_ret), [&](int tid) {
+        // this step's received counts, kept before the peers may write the next step's
+        if (tid < n) recv_out[tid] = cnt[tid];
+        if (tid >= 1 && tid < n) {
+            const int owner = (me + tid) % n;
+            st_release_sys(wptr<uint32_t>(p, owner, p.off_flag_back) + (n - tid), epoch);
+        }
+    });
+}
+
+// The expert block's last step fused with the return: window row r gets
+// sum over its slots of w * ye[inv] (+ sgate * ye[R*k + r] for the self rows)
+// from the f16 per-expert GEMM outputs ye, written as PT straight to its
+// destination: this rank's y for slab 0, the owner's back slab otherwise
+// (padding rows are skipped). One warp per row, 8 values per lane per chunk.
+// Then the last CTA raises flag_back in every peer's window.
+template <typename PT>
+__global__ void ep_peer_combine_return_kernel(EpPeerTable p, const __half* __restrict__ ye,
+                                              const int32_t* __restrict__ inv, const float* __restrict__ w,
+                                              const float* __restrict__ sgate, const int32_t* __restrict__ idx,
+                                              int E_real, int T, int has_shared, PT* __restrict__ yself,
+                                              uint32_t epoch, int32_t* __restrict__ recv_out) {
+    const int n = p.n, me = p.me, slab = p.slab, dp = p.dp, k = p.k;
+    const int lane = threadIdx.x & 31;
+    const int R = n * slab;
+    const volatile int32_t* cnt = wptr<int32_t>(p, me, p.off_cnt);
+    const int nw = (int)((gridDim.x * blockDim.x) >> 5);
+    for (int r = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); r < R; r += nw) {
+        const int s = r / slab, j = r - s * slab;
+        if (j >= (s == 0 ? T : cnt[s])) continue;  // whole warp
+        PT* dst = s == 0 ? yself + (int64_t)j * dp
+                         : wptr<PT>(p, (me + s) % n, p.off_back) + ((int64_t)(n - s) * slab + j) * dp;
+        // this row's slots, lane q holding slot q (k <= 32)
+        int my_row = -1;
+        float my_w = 0.f;
+        if (lane < k && idx[(int64_t)r * k + lane] < E_real) {
+            my_row = inv[(int64_t)r * k + lane];
+            my_w = w[(int64_t)r * k + lane];
+        }
+        const bool sh = has_shared && s == 0;
+        const float sw = sh ? sgate[j] : 0.f;
+        for (int c = lane * 8; c < dp; c += 256) {
+            float a[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            auto add = [&](float wt, const __half* row) {
+                const uint4 v = *reinterpret_cast<const uint4*>(row + c);
+                const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const __half2 h2 = *reinterpret_cast<const __half2*>(&u[q]);
+                    const float2 f = __half22float2(h2);
+                    a[2 * q] += wt * f.x;
+                    a[2 * q + 1] += wt * f.y;
+                }
+            };
+            for (int q = 0; q < k; ++q) {
+                const int row = __shfl_sync(0xffffffffu, my_row, q);
+                const float wt = __shfl_sync(0xffffffffu, my_w, q);
+                if (row >= 0) add(wt, ye + (int64_t)row * dp);
+            }
+            if (sh) add(sw, ye + ((int64_t)R * k + j) * dp);
+            if constexpr (sizeof(PT) == 2) {
+                *reinterpret_cast<uint4*>(dst + c) =
+                    make_uint4(pack_h2f(a[0], a[1]), pack_h2f(a[2], a[3]), pack_h2f(a[4], a[5]), pack_h2f(a[6], a[7]));
+            } else {
+                float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(dst) + c);
+                o[0] = make_float4(a[0], a[1], a[2], a[3]);
+                o[1] = make_float4(a[4], a[5], a[6], a[7]);
+            }
+        }
+    }
+    after_all_ctas(wptr<uint32_t>(p, me, p.off_done_ret), [&](int tid) {
+        // this step's received counts, kept before the peers may write the next step's
+        if (tid < n) recv_out[tid] = cnt[tid];
         if (tid >= 1 && tid < n) {
             const int owner = (me + tid) % n;
             st_release_sys(wptr<uint32_t>(p, owner, p.off_flag_back) + (n - tid), epoch);
@@ -369,12 +443,27 @@ cudaError_t launch_ep_peer_prep(const EpPeerTable& p, int T, int e_begin, int e_
     return cudaGetLastError();
 }
 
-cudaError_t launch_ep_peer_return(const EpPeerTable& p, const void* y, uint32_t epoch, int n_sm, cudaStream_t s) {
+cudaError_t launch_ep_peer_return(const EpPeerTable& p, const void* y, uint32_t epoch, int32_t* recv_out, int n_sm,
+                                  cudaStream_t s) {
     const unsigned grid = grid_for((int64_t)(p.n - 1) * p.slab * 32, n_sm, 8);  // a warp per row
     if (p.rows_f16)
-        ep_peer_return_kernel<__half><<<grid, 256, 0, s>>>(p, static_cast<const __half*>(y), epoch);
+        ep_peer_return_kernel<__half><<<grid, 256, 0, s>>>(p, static_cast<const __half*>(y), epoch, recv_out);
     else
-        ep_peer_return_kernel<float><<<grid, 256, 0, s>>>(p, static_cast<const float*>(y), epoch);
+        ep_peer_return_kernel<float><<<grid, 256, 0, s>>>(p, static_cast<const float*>(y), epoch, recv_out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_peer_combine_return(const EpPeerTable& p, const __half* ye, const int32_t* inv, const float* w,
+                                          const float* sgate, const int32_t* idx, int E_real, int T, int has_shared,
+                                          void* yself, uint32_t epoch, int32_t* recv_out, int n_sm,
+                                          cudaStream_t s) {
+    const unsigned grid = grid_for((int64_t)p.n * p.slab * 32, n_sm, 8);  // a warp per row
+    if (p.rows_f16)
+        ep_peer_combine_return_kernel<__half><<<grid, 256, 0, s>>>(p, ye, inv, w, sgate, idx, E_real, T, has_shared,
+                                                                   static_cast<__half*>(yself), epoch, recv_out);
+    else
+        ep_peer_combine_return_kernel<float><<<grid, 256, 0, s>>>(p, ye, inv, w, sgate, idx, E_real, T, has_shared,
+                                                                  static_cast<float*>(yself), epoch, recv_out);
     return cudaGetLastError();
 }
 

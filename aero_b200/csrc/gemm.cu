@@ -317,8 +317,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
     } else if (warp < kEpiWarp0) {
         // -------------------------------------------------------------- dequant
         // 16 warps: warp (warp & 3) may write TMEM lane quarter q; its combo
-        // c = (warp - 2) / 4 takes values [16 c, 16 c + 16) of each 64-value K step
-        // (8 TMEM columns). TMEM lane r is weight row r of the item; gate/up items
+        // c = (warp - 2) / 4 takes one 32-value quant sub-block (Q4_K) or block
+        // (Q8_0) per raw stage of two 64-value K steps: K step kb + c / 2, values
+        // [32 (c & 1), 32 (c & 1) + 32) (16 TMEM columns), so each thread decodes
+        // one scale per stage. TMEM lane r is weight row r of the item; gate/up items
         // interleave the matrices by half-warps: in lane quarter q, lanes 0-15 hold
         // gate rows 16 q + (0..15) and lanes 16-31 the same rows of up (so the
         // raw-stage rows an 8-lane phase reads are consecutive: no bank conflicts).
@@ -328,31 +330,37 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
         const int srow = GATEUP ? (lane >> 4) * (kTileM / 2) + q * 16 + (lane & 15) : r;  // row in the raw stage
         const uint32_t lane_base = (uint32_t)(q * 32) << 16;
         const int swz = DT == AERO_DT_Q4_K ? ((srow >> 1) & 3) : (srow & 7);
-        int raw_n = 0, a_n = 0;
-        bool ok = true;
-        Item it;
-        // this warp's 8 columns of K step kb (from the raw stage's row and header)
-        auto dequant8 = [&](int kb, const uint8_t* qrow, const uint4& meta, uint32_t (&cols)[8]) {
+        const int step = cmb >> 1, half = cmb & 1;
+        // this thread's 32 values of K step ks: the 32 raw bytes (two 16-byte chunks
+        // of its stage row, TMA-swizzled: 64B for Q4_K rows of 64 bytes, 128B for Q8_0
+        // rows of 128 bytes, logical chunk c at c ^ f(row)) and the row's header slice
+        uint4 meta, v0, v1;
+        auto load = [&](int rn, int ks) {
+            const uint8_t* stage = raw_ring + (rn % kRS) * C::kRawStageBytes;
+            const uint8_t* qrow = stage + srow * C::kRawRowBytes;
+            meta = *reinterpret_cast<const uint4*>(stage + C::kQsBytes + srow * 16);
+            const int c = DT == AERO_DT_Q4_K ? 2 * (ks & 1) : 4 * (ks & 1) + 2 * half;
+            v0 = *reinterpret_cast<const uint4*>(qrow + ((c ^ swz) << 4));
+            v1 = *reinterpret_cast<const uint4*>(qrow + (((c + 1) ^ swz) << 4));
+        };
+        // -> 16 TMEM columns (f16 pairs in the kperm order)
+        auto convert = [&](int ks, uint32_t (&cols)[16]) {
+            const uint32_t wv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
             if (DT == AERO_DT_Q4_K) {
                 // the K step's 32 bytes: low nibbles are its values 0-31 (sub-block 2g),
-                // high nibbles 32-63 (sub-block 2g+1); this warp's 16 values are one
-                // nibble of 16 bytes
-                const bool hi = cmb >= 2;
+                // high nibbles 32-63 (sub-block 2g+1)
                 int sc, mn;
-                q4k_sc_m_words(meta.y, meta.z, meta.w, 2 * (kb & 3) + (hi ? 1 : 0), sc, mn);
+                q4k_sc_m_words(meta.y, meta.z, meta.w, 2 * (ks & 3) + half, sc, mn);
                 // (d sc, dmin m) in f16: the 6-bit sc and m are exact as 1024 + v - 1024,
                 // and one rounding of the exact products equals the f32 route's
                 const __half2 k1024 = u2h(0x64006400u);
                 const __half2 scm = __hsub2(u2h((uint32_t)sc | ((uint32_t)mn << 16) | 0x64006400u), k1024);
                 const __half2 prod = __hmul2(u2h(meta.x), scm);  // meta.x = (d, dmin)
                 const __half2 sh = __low2half2(prod), nh = __hneg2(__high2half2(prod));
-                const int c = 2 * (kb & 1) + (cmb & 1);
-                const uint4 v = *reinterpret_cast<const uint4*>(qrow + ((c ^ swz) << 4));
-                const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    const uint32_t w0 = hi ? wv[i] >> 4 : wv[i];
-                    const uint32_t w1 = wv[i] >> (hi ? 12 : 8);
+                for (int i = 0; i < 8; ++i) {
+                    const uint32_t w0 = half ? wv[i] >> 4 : wv[i];
+                    const uint32_t w1 = wv[i] >> (half ? 12 : 8);
                     // (bytes 0, 2) and (bytes 1, 3): 1024 + q exactly, then s q - m
                     const __half2 q02 = __hsub2(u2h((w0 & 0x000F000Fu) | 0x64006400u), k1024);
                     const __half2 q13 = __hsub2(u2h((w1 & 0x000F000Fu) | 0x64006400u), k1024);
@@ -360,26 +368,27 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                     cols[2 * i + 1] = h2u(__hfma2(q13, sh, nh));
                 }
             } else {
-                // the 16-byte slice holds 8 fp16 scales for 256 values; this warp's 16
-                // values lie in block 2 (kb & 3) + cmb / 2
-                const int kq = kb & 3;
+                // the 16-byte slice holds 8 fp16 scales for 256 values; this thread's
+                // 32 values are block 2 (ks & 3) + half
+                const int kq = ks & 3;
                 const uint32_t sc8 = kq == 0 ? meta.x : kq == 1 ? meta.y : kq == 2 ? meta.z : meta.w;
-                const __half2 dd =
-                    __half2half2(__ushort_as_half((unsigned short)((cmb >> 1) ? (sc8 >> 16) : (sc8 & 0xFFFFu))));
-                const int c = 4 * (kb & 1) + cmb;
-                const uint4 v = *reinterpret_cast<const uint4*>(qrow + ((c ^ swz) << 4));
-                const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+                const __half2 dd = __half2half2(__ushort_as_half((unsigned short)(half ? (sc8 >> 16) : (sc8 & 0xFFFFu))));
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
+                for (int i = 0; i < 8; ++i) {
                     const uint32_t wb = wv[i] ^ 0x80808080u;
                     cols[2 * i] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4240)), dd));
                     cols[2 * i + 1] = h2u(__hmul2(byte2_to_h2(__byte_perm(wb, 0, 0x4341)), dd));
                 }
             }
         };
+        // Passes over the CTA's items, both K steps of a raw stage per pass (item K
+        // lengths are multiples of 128): one raw wait, one header load, one
+        // tcgen05.wait::st for two stages. (Issuing the next pass's raw wait and
+        // loads before this pass's arrivals measured slower.)
+        int raw_n = 0, a_n = 0;
+        bool ok = true;
+        Item it;
         for (int w = blockIdx.x; ok && item_at(p, n_tiles, w, it); w += gridDim.x) {
-            // both K steps of a raw stage per iteration (item K lengths are multiples of
-            // 128): one raw wait, one header load, one tcgen05.wait::st for two stages
             for (int kb = 0; kb < it.nkb; kb += 2) {
                 const int s = raw_n % kRS;
                 const int sa0 = a_n % kStages, sa1 = (a_n + 1) % kStages;
@@ -398,21 +407,17 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                 }
                 __syncwarp();
                 tc_fence_after();
-                const uint8_t* stage = raw_ring + s * C::kRawStageBytes;
-                // this row's qs (TMA-swizzled: 64B for Q4_K rows of 64 bytes, 128B for Q8_0
-                // rows of 128 bytes: logical 16-byte chunk c sits at c ^ f(row))
-                const uint8_t* qrow = stage + srow * C::kRawRowBytes;
-                const uint4 meta = *reinterpret_cast<const uint4*>(stage + C::kQsBytes + srow * 16);
-                const uint32_t acol = tmem + lane_base + kAColBase + (uint32_t)cmb * 8u;
-                uint32_t c0[8], c1[8];
-                dequant8(kb, qrow, meta, c0);
-                dequant8(kb + 1, qrow, meta, c1);
-                tmem_st8(acol + (uint32_t)sa0 * kAStageCols, c0);
-                tmem_st8(acol + (uint32_t)sa1 * kAStageCols, c1);
+                load(raw_n, kb + step);
+                uint32_t cc[16];
+                convert(kb + step, cc);
+                tmem_st16(tmem + lane_base + kAColBase + (uint32_t)(step ? sa1 : sa0) * kAStageCols +
+                              (uint32_t)half * 16u,
+                          cc);
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) {
+                    // every dequant warp arrives on both stages of the pass
                     mbar_arrive(full(sa0));
                     mbar_arrive(full(sa1));
                     mbar_arrive(raw_empty(s));
@@ -506,30 +511,34 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
 // xperm rows: [0, P_real) the routed pairs in sorted order, [P, P + Tsh) the
 // first Tsh input rows for the shared expert. P_real (= offsets[E]) is read on
 // the device: sorted positions [P_real, P) hold skipped slots and are not
-// gathered. Grid-stride over 8-value chunks.
+// gathered. One warp per row, 8 values (one 16-byte store) per lane per chunk.
 template <typename XT>
 __global__ void gather_kernel(const XT* __restrict__ x, const int32_t* __restrict__ perm,
                               const int32_t* __restrict__ p_real, int k, int P, int Tsh, int dp,
                               __half* __restrict__ xp) {
-    const int per_row = dp / 8;
     const int pr = *p_real;
-    const int64_t n = (int64_t)(pr + Tsh) * per_row;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
-        const int v = (int)(i / per_row), c = (int)(i % per_row) * 8;
+    const int rows = pr + Tsh;
+    const int lane = threadIdx.x & 31;
+    const int nw = (int)((gridDim.x * blockDim.x) >> 5);
+    for (int v = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); v < rows; v += nw) {
         const int row = v < pr ? v : P + (v - pr);
         const int tok = v < pr ? perm[v] / k : v - pr;
-        // values in the GEMM's K order: 0, 2, 1, 3 within every four (kperm)
-        uint4 o;
-        if constexpr (sizeof(XT) == 2) {
-            const uint4 v = __ldg(reinterpret_cast<const uint4*>(x + (int64_t)tok * dp + c));
-            o = make_uint4(__byte_perm(v.x, v.y, 0x5410), __byte_perm(v.x, v.y, 0x7632), __byte_perm(v.z, v.w, 0x5410),
-                           __byte_perm(v.z, v.w, 0x7632));
-        } else {
-            const float* src = reinterpret_cast<const float*>(x) + (int64_t)tok * dp + c;
-            const float4 a = ld_f4(src), b = ld_f4(src + 4);
-            o = make_uint4(pack_h2(a.x, a.z), pack_h2(a.y, a.w), pack_h2(b.x, b.z), pack_h2(b.y, b.w));
+        __half* dst = xp + (int64_t)row * dp;
+#pragma unroll 4
+        for (int c = lane * 8; c < dp; c += 256) {
+            // values in the GEMM's K order: 0, 2, 1, 3 within every four (kperm)
+            uint4 o;
+            if constexpr (sizeof(XT) == 2) {
+                const uint4 u = __ldg(reinterpret_cast<const uint4*>(x + (int64_t)tok * dp + c));
+                o = make_uint4(__byte_perm(u.x, u.y, 0x5410), __byte_perm(u.x, u.y, 0x7632),
+                               __byte_perm(u.z, u.w, 0x5410), __byte_perm(u.z, u.w, 0x7632));
+            } else {
+                const float* src = reinterpret_cast<const float*>(x) + (int64_t)tok * dp + c;
+                const float4 a = ld_f4(src), b = ld_f4(src + 4);
+                o = make_uint4(pack_h2(a.x, a.z), pack_h2(a.y, a.w), pack_h2(b.x, b.z), pack_h2(b.y, b.w));
+            }
+            *reinterpret_cast<uint4*>(dst + c) = o;
         }
-        *reinterpret_cast<uint4*>(xp + (int64_t)row * dp + c) = o;
     }
 }
 
@@ -756,8 +765,8 @@ cudaError_t launch_prefill_prep(const PrefillArgs& a, GemmBuffers& b, cudaStream
     const int P = a.T * a.k;
     const int Tsh = a.has_shared ? a.Tsh : 0;
     {
-        const int64_t n = (int64_t)(P + Tsh) * (a.dp / 8);
-        const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, (int64_t)a.n_sm * 16));
+        const int64_t warps = (int64_t)(P + Tsh);  // a warp per row
+        const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((warps + 7) / 8, (int64_t)a.n_sm * 16));
         if (a.x_f16)
             gather_kernel<__half><<<grid, 256, 0, s>>>(static_cast<const __half*>(a.x), a.perm, a.p_real, a.k, P, Tsh,
                                                         a.dp, b.xperm);

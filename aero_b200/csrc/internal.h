@@ -142,7 +142,16 @@ cudaError_t launch_ep_peer_pack(const EpPeerTable& p, const float* x, int T, con
 cudaError_t launch_ep_peer_prep(const EpPeerTable& p, int T, int e_begin, int e_end, int E, uint32_t epoch,
                                 int32_t* idx, float* w, float* sgate, int32_t* bad, int n_sm, cudaStream_t s);
 // y rows of the peers' slabs back into their windows, then flag_back = epoch in every peer.
-cudaError_t launch_ep_peer_return(const EpPeerTable& p, const void* y, uint32_t epoch, int n_sm, cudaStream_t s);
+// (both return launches copy the window's received counts to recv_out (n) first)
+cudaError_t launch_ep_peer_return(const EpPeerTable& p, const void* y, uint32_t epoch, int32_t* recv_out, int n_sm,
+                                  cudaStream_t s);
+// GEMM path: the expert block's combine over the window rows (f16 per-expert
+// outputs ye, slots from inv / w / idx, shared rows at ye[R*k + t]) written
+// straight to y (slab 0) and the owners' back slabs, then flag_back = epoch.
+cudaError_t launch_ep_peer_combine_return(const EpPeerTable& p, const __half* ye, const int32_t* inv, const float* w,
+                                          const float* sgate, const int32_t* idx, int E_real, int T, int has_shared,
+                                          void* yself, uint32_t epoch, int32_t* recv_out, int n_sm,
+                                          cudaStream_t s);
 // Waits for every peer's returns, then out[t] = y[t] + remote parts in rank order.
 cudaError_t launch_ep_peer_combine(const EpPeerTable& p, const void* y, const int32_t* pos, int T, uint32_t epoch,
                                    float* out, int n_sm, cudaStream_t s);

@@ -72,7 +72,7 @@ struct PeerCtx {
     size_t window_bytes = 0;
     void* y = nullptr;  // expert-block output for the window's rows (row type)
     size_t y_bytes = 0;
-    int32_t* aux = nullptr;  // send_tok (n * slab), counts (n + 1), pos (slab * n)
+    int32_t* aux = nullptr;  // send_tok (n * slab), counts (n + 1), pos (slab * n), received (n)
     size_t aux_bytes = 0;
     std::vector<char*> mapped;  // peers' windows opened here
     uint32_t epoch = 0;
@@ -361,7 +361,7 @@ bool ensure_scratch(Handle& h, int T) {
 // Router logits (+ the shared-gate column E when with_gate and the layer has a
 // shared expert) for T rows of x into s.logits (row stride lg_ld): the tensor
 // cores for batches of at least kRouterTcMinTokens, SIMT kernels below that.
-constexpr int kRouterTcMinTokens = 128;
+constexpr int kRouterTcMinTokens = 16;
 bool router_logits_dev(Handle& h, const float* x, int T, bool with_gate) {
     Scratch& s = h.sc;
     const bool gate = with_gate && h.has_shared;
@@ -412,7 +412,7 @@ bool route_stage(Handle& h, const float* x, int T, const float* logits_in, bool 
 // experts live on another rank). The GEMM path runs when x is f16 or T reaches
 // the handle's threshold.
 bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool skip_slots, void* out,
-                  bool out_f16 = false) {
+                  bool out_f16 = false, bool gemm_skip_combine = false) {
     Scratch& s = h.sc;
     cudaStream_t st = h.stream;
     const int P = T * h.k;
@@ -462,11 +462,14 @@ bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool ski
         if (!h.cuda_ok(launch_prefill_gemm(pa, h.gb, h.wmaps, false, st), "down GEMM")) return false;
         h.launches += 4;
         h.mark(5);
-        if (!h.cuda_ok(launch_combine_h(h.gb.y, s.inv, s.w, s.sgate, skip_idx, h.E, T, Tsh, h.k, h.dp, h.has_shared, out,
-                                        out_f16 ? 1 : 0, st),
-                       "combine"))
-            return false;
-        h.launches += 1;
+        // (the caller may fuse the combine into its own kernel: expert parallel over peer memory)
+        if (!gemm_skip_combine) {
+            if (!h.cuda_ok(launch_combine_h(h.gb.y, s.inv, s.w, s.sgate, skip_idx, h.E, T, Tsh, h.k, h.dp, h.has_shared,
+                                            out, out_f16 ? 1 : 0, st),
+                           "combine"))
+                return false;
+            h.launches += 1;
+        }
     } else {
         if (T > s.gemv_cap) return h.fail("internal: GEMV scratch covers %d tokens, call has %d", s.gemv_cap, T);
         GemvArgs a{};
@@ -1226,7 +1229,7 @@ int aero_cuda_ep_peer_open(void* handle, int n_ranks, int rank, const int32_t* r
                                                  row_dtype == AERO_EP_ROWS_F16, &wbytes);
     const size_t esz = row_dtype == AERO_EP_ROWS_F16 ? 2 : 4;
     const size_t ybytes = (size_t)R * h->dp * esz;
-    const size_t abytes = ((size_t)R + n_ranks + 1 + (size_t)slab_rows * n_ranks) * 4;
+    const size_t abytes = ((size_t)R + n_ranks + 1 + (size_t)slab_rows * n_ranks + n_ranks) * 4;
     void *w = nullptr, *y = nullptr, *a = nullptr;
     cudaError_t e = aero::guarded_malloc(&w, wbytes, aero::kScratch);
     if (e == cudaSuccess) e = aero::guarded_malloc(&y, ybytes, aero::kScratch);
@@ -1325,6 +1328,7 @@ int aero_cuda_ep_peer_step(void* handle, const float* x, int T, float* out) {
     int32_t* send_tok = pc.aux;
     int32_t* counts = pc.aux + R;
     int32_t* pos = counts + n + 1;
+    int32_t* received = pos + (size_t)tab.slab * n;
     const uint32_t epoch = ++pc.epoch;
     cudaStream_t st = h->stream;
     auto mark = [&](int i) {
@@ -1352,9 +1356,16 @@ int aero_cuda_ep_peer_step(void* handle, const float* x, int T, float* out) {
     if (ok && gemv && s.xq.q1)
         ok = h->cuda_ok(aero::launch_qinput(static_cast<const float*>(rows), R, h->dp, s.xq, st), "row codes");
     mark(3);
-    ok = ok && aero::expert_stage(*h, rows, f16, R, T, true, pc.y, f16);
+    // GEMM path: its combine is fused with the return (rows written straight to their owners)
+    const bool fused = h->gemm_ok && h->gb_ready && (f16 || R >= h->gemm_min_tokens);
+    ok = ok && aero::expert_stage(*h, rows, f16, R, T, true, pc.y, f16, fused);
     mark(4);
-    ok = ok && h->cuda_ok(aero::launch_ep_peer_return(tab, pc.y, epoch, h->n_sm, st), "exchange return");
+    if (fused)
+        ok = ok && h->cuda_ok(aero::launch_ep_peer_combine_return(tab, h->gb.y, s.inv, s.w, s.sgate, s.idx, h->E, T,
+                                                                  h->has_shared, pc.y, epoch, received, h->n_sm, st),
+                              "exchange combine + return");
+    else
+        ok = ok && h->cuda_ok(aero::launch_ep_peer_return(tab, pc.y, epoch, received, h->n_sm, st), "exchange return");
     mark(5);
     ok = ok && h->cuda_ok(aero::launch_ep_peer_combine(tab, pc.y, pos, T, epoch, out, h->n_sm, st), "exchange combine");
     mark(6);
@@ -1400,10 +1411,10 @@ int aero_cuda_ep_peer_counts(void* handle, int32_t* sent, int32_t* received) {
     cudaSetDevice(h->device);
     const int n = pc.tab.n, me = pc.tab.me, R = n * pc.tab.slab;
     std::vector<int32_t> c(n + 1), w(n);
+    // (the window's own counts may already hold a peer's next step: read the step's copy)
+    const int32_t* step_recv = pc.aux + R + n + 1 + (size_t)pc.tab.slab * n;
     if (!h->cuda_ok(cudaMemcpyAsync(c.data(), pc.aux + R, (size_t)n * 4, cudaMemcpyDeviceToHost, h->stream), "counts") ||
-        !h->cuda_ok(cudaMemcpyAsync(w.data(), pc.window + pc.tab.off_cnt, (size_t)n * 4, cudaMemcpyDeviceToHost,
-                                    h->stream),
-                    "counts") ||
+        !h->cuda_ok(cudaMemcpyAsync(w.data(), step_recv, (size_t)n * 4, cudaMemcpyDeviceToHost, h->stream), "counts") ||
         !h->cuda_ok(cudaStreamSynchronize(h->stream), "counts"))
         return -1;
     for (int r = 0; r < n; ++r) {

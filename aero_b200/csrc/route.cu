@@ -121,15 +121,21 @@ __global__ void __launch_bounds__(256) router_sgemm_kernel(const float* __restri
 // warp elects the best remaining (value desc, index asc) and removes it.
 constexpr int kTopkMaxPerLane = 32;  // E <= 1024
 
-__device__ __forceinline__ bool better(float va, int ia, float vb, int ib) {
-    // a ranks before b: larger logit, or equal logit and lower index. A NaN never
-    // ranks before a number (std::partial_sort with NaN is unspecified; this is
-    // one deterministic choice).
-    if (va > vb) return true;
-    if (va == vb) return ia < ib;
-    if (vb != vb && va == va) return true;
-    return false;
+// Order-preserving unsigned image of a logit: larger value -> larger key, -0
+// as +0, NaN below every number (key 0; std::partial_sort in the reference
+// leaves NaN order unspecified, this is one deterministic choice). key_value
+// inverts it (NaN for 0).
+__device__ __forceinline__ uint32_t order_key(float v) {
+    if (v != v) return 0u;
+    uint32_t u = __float_as_uint(v);
+    if (u == 0x80000000u) u = 0u;
+    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
+__device__ __forceinline__ float key_value(uint32_t k) {
+    if (k == 0u) return __uint_as_float(0x7FC00000u);
+    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
 
 template <int PER>  // values per lane: E <= 32 * PER
 __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int ld, int T, int E,
@@ -146,35 +152,41 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
         const int e = lane + 32 * i;
         v[i] = e < E ? lg[e] : 0.f;
     }
-    uint32_t taken = 0;  // bit i: slot i of this lane removed (or absent)
+    // Selection on 64-bit keys: the order-preserving bits of the logit above the
+    // complemented index, so the largest key is the larger logit and, on equal
+    // logits, the lower index (the order of `better`; NaNs rank below every
+    // number, lower index first among them). Each lane keeps its best remaining
+    // key; a round is one warp max, and only the winning lane rescans its slots.
+    uint64_t key[PER];
 #pragma unroll
-    for (int i = 0; i < PER; ++i)
-        if (lane + 32 * i >= E) taken |= 1u << i;
+    for (int i = 0; i < PER; ++i) {
+        const int e = lane + 32 * i;
+        key[i] = e < E ? ((uint64_t)order_key(v[i]) << 32) | (0xFFFFFFFFu - (uint32_t)e) : 0ull;
+    }
+    uint64_t lb = 0;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) lb = key[i] > lb ? key[i] : lb;
 
     float sel_v = 0.f;  // lane j keeps the j-th selected logit (j < k <= 32 handled in rounds)
     float wsum = 0.f, mx = 0.f;
     for (int r = 0; r < k; ++r) {
-        float bv = 0.f;
-        int bi = 0x7fffffff;
-#pragma unroll
-        for (int i = 0; i < PER; ++i) {
-            if (taken & (1u << i)) continue;
-            const int e = lane + 32 * i;
-            if (bi == 0x7fffffff || better(v[i], e, bv, bi)) {
-                bv = v[i];
-                bi = e;
-            }
-        }
+        uint64_t best = lb;
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
-            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-            if (oi != 0x7fffffff && (bi == 0x7fffffff || better(ov, oi, bv, bi))) {
-                bv = ov;
-                bi = oi;
+            const uint64_t ot = __shfl_xor_sync(0xffffffffu, best, o);
+            best = ot > best ? ot : best;
+        }
+        const int bi = (int)(0xFFFFFFFFu - (uint32_t)best);
+        const float bv = key_value((uint32_t)(best >> 32));
+        if ((bi & 31) == lane) {
+            const int slot = bi >> 5;
+            lb = 0;
+#pragma unroll
+            for (int i = 0; i < PER; ++i) {
+                if (i == slot) key[i] = 0ull;
+                lb = key[i] > lb ? key[i] : lb;
             }
         }
-        if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
         if (lane == 0) idx[(int64_t)t * k + r] = bi;
         if (r == 0) mx = bv;
         if ((r & 31) == lane) sel_v = bv;  // only valid for k <= 32 (checked by the host)

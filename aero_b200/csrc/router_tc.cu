@@ -256,9 +256,8 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
 // for c < cols (the router rows and, when present, the shared-gate column).
 __global__ void router_reduce_kernel(const float* __restrict__ partial, int splits, int T, int ld, int cols,
                                      const float* __restrict__ bias, int n_bias, float* __restrict__ logits) {
-    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i >= (int64_t)T * cols) return;
-    const int t = (int)(i / cols), c = (int)(i % cols);
+    const int c = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y;
+    if (c >= cols) return;
     float v = 0.f;
     for (int sp = 0; sp < splits; ++sp) v += partial[((size_t)sp * T + t) * ld + c];
     if (bias && c < n_bias) v += bias[c];
@@ -346,8 +345,7 @@ cudaError_t launch_router_tc(const RouterTcMaps& maps, const float* x, int T, co
     router_tc_kernel<<<grid, kRtThreads, kRtSmem, s>>>(tx, maps.hi, maps.lo, p);
     if (splits > 1) {
         const int cols = maps.n_rows + (gate_row ? 1 : 0);
-        const int64_t n = (int64_t)T * cols;
-        router_reduce_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(partial, splits, T, ld, cols, bias, n_bias,
+        router_reduce_kernel<<<dim3((cols + 127) / 128, T), 128, 0, s>>>(partial, splits, T, ld, cols, bias, n_bias,
                                                                          logits);
     }
     return cudaGetLastError();

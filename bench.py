@@ -413,7 +413,9 @@ def main():
         result["config"]["exchange"] = "peer memory (CUDA IPC, NVLink stores)" if exchange == "peer" else \
             "NCCL all-to-all"
         result["exchange_rows"] = {"sent": moe.last_split[0], "received": moe.last_split[1]}
-        # per-phase device times of rank 0's step (a separate profiled pass)
+        # per-phase device times of rank 0's step (a separate profiled pass, the
+        # ranks lined up first: a phase that waits for peers also times their lag)
+        torch.distributed.barrier()
         moe.set_profiling(True)
         with torch.cuda.stream(stream):
             for _ in range(3):

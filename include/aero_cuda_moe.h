@@ -149,7 +149,7 @@ int aero_cuda_moe_stage_times(void* handle, double* ms, int64_t* counts, int n);
  * the AERO_GEMM_MIN_TOKENS environment variable at open). 0 / -1. */
 #define AERO_CUDA_OPT_GEMM_MIN_TOKENS 1
 /* AERO_CUDA_OPT_ROUTER_TC: 1 (default) projects the router of calls with at
- * least 128 tokens on the tensor cores (three TF32 products of split f32
+ * least 16 tokens on the tensor cores (three TF32 products of split f32
  * operands, f32 accumulate: f32-level accuracy); 0 keeps the f32 SIMT kernels. */
 #define AERO_CUDA_OPT_ROUTER_TC 2
 int aero_cuda_moe_set_option(void* handle, int option, int64_t value);

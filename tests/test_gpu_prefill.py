@@ -89,11 +89,12 @@ def test_config5_subset(key):
     assert np.array_equal(out, out2)
 
 
-@pytest.mark.parametrize("key,T", [("c5", 1000), ("c2", 300)])
+@pytest.mark.parametrize("key,T", [("c5", 1000), ("c2", 300), ("c3", 32), ("c5", 2048)])
 def test_tensor_core_router_f32_accuracy(key, T):
-    """Router logits of >= 128-token calls come from three TF32 products of split
+    """Router logits of >= 16-token calls come from three TF32 products of split
     operands; they must be as close to the f64 logits as the f32 SIMT kernel's
-    (c2 carries a router bias; 1000 and 300 leave a partial 128-token tile)."""
+    (c2 carries a router bias; 1000, 300 and 32 leave a partial 128-token tile;
+    small batches split K over several CTAs and add the parts in order)."""
     wl = synth.CONFIGS[key]
     layer = synth.make_layer(wl.spec, 3, device_gen=True)
     x = synth.make_x(T, wl.spec.d, 3)
@@ -117,4 +118,4 @@ def test_tensor_core_router_f32_accuracy(key, T):
     # top-k agrees with the f64 logits' except at near-ties
     idx_tc, _ = O.route(tc, wl.spec.k)
     idx_64, _ = O.route(ref64.astype(np.float32), wl.spec.k)
-    assert np.mean(np.all(idx_tc == idx_64, axis=1)) > 0.99
+    assert np.sum(~np.all(idx_tc == idx_64, axis=1)) <= max(1, T // 100)
