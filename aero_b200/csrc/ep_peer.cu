@@ -15,9 +15,9 @@
 //   done_pack, done_ret     CTA counters of the two writing kernels
 //   err                     first wait that gave up (0: none)
 // A step (epoch e):
-//   plan    per destination rank, its tokens in order (send_tok, pos)
-//   pack    rows + metadata into the destination windows; the last CTA then
-//           writes cnt and flag_rows = e into every peer's window
+//   pack    one warp per token: rows + metadata into the destination windows
+//           (rows in arrival order within a slab); the last CTA then writes
+//           cnt and flag_rows = e into every peer's window
 //   prep    waits for flag_rows = e from every peer, then metadata -> buckets
 //   (this rank's experts over its window rows, into a local y)
 //   return  y rows of slabs 1..n-1 into the owners' back slabs; the last CTA
@@ -43,7 +43,6 @@
 namespace aero {
 namespace {
 
-constexpr int kPlanThreads = 1024;
 constexpr uint64_t kPeerWaitNs = 5ull * 1000 * 1000 * 1000;
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
@@ -117,104 +116,106 @@ __device__ __forceinline__ void after_all_ctas(uint32_t* done, F last) {
     if (is_last) last((int)threadIdx.x);
 }
 
-// One CTA per destination rank r: its tokens in order. send_tok[r*slab + j] is
-// the j-th token with at least one expert on r; pos[t*n + r] is where that
-// token's partial for r comes back in this rank's window ((r - me) mod n)*slab
-// + j (r = me: t, the self slab), or -1; counts[r] rows (counts[me] = T).
-__global__ void __launch_bounds__(kPlanThreads) ep_peer_plan_kernel(const int32_t* __restrict__ idx, int T, int k,
-                                                                    EpRankTable rt, int me, int slab,
-                                                                    int32_t* __restrict__ send_tok,
-                                                                    int32_t* __restrict__ counts,
-                                                                    int32_t* __restrict__ pos) {
-    using Scan = cub::BlockScan<int, kPlanThreads>;
-    __shared__ typename Scan::TempStorage tmp;
-    const int n = rt.n, r = blockIdx.x;
-    if (r == me) {
-        for (int t = threadIdx.x; t < T; t += kPlanThreads) pos[(int64_t)t * n + r] = t;
-        if (threadIdx.x == 0) counts[r] = T;
-        return;
-    }
-    const int lo = rt.begin[r], hi = rt.begin[r + 1];
-    const int base_slab = ((r - me + n) % n) * slab;
-    int carry = 0;
-    for (int t0 = 0; t0 < T; t0 += kPlanThreads) {
-        const int t = t0 + threadIdx.x;
-        bool hit = false;
-        if (t < T)
-            for (int s = 0; s < k; ++s) {
-                const int e = idx[(int64_t)t * k + s];
-                hit |= e >= lo && e < hi;
-            }
-        int ex, tot;
-        Scan(tmp).ExclusiveSum(hit ? 1 : 0, ex, tot);
-        if (t < T) {
-            if (hit) {
-                send_tok[(int64_t)r * slab + carry + ex] = t;
-                pos[(int64_t)t * n + r] = base_slab + carry + ex;
-            } else {
-                pos[(int64_t)t * n + r] = -1;
-            }
-        }
-        carry += tot;
-        __syncthreads();  // tmp reuse
-    }
-    if (threadIdx.x == 0) counts[r] = carry;
-}
-
 __device__ __forceinline__ uint32_t pack_h2f(float a, float b) {
     const __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<const uint32_t*>(&h);
 }
 
-// Rows and metadata of this rank's tokens into every destination window (slab
-// s = 0: own window; s > 0: rank (me + s) mod n, whose slab for this rank is
-// (n - s) mod n). One warp per row: 16-byte stores of 8 values per lane, the
-// metadata row by the first lanes.
+// Rows and metadata of this rank's tokens into every destination window, one
+// warp per token: the token's k experts name its destination ranks; its row
+// is read and converted once, then stored to each destination (slab 0 of this
+// rank's own window at row t; for rank r != me, slab (me - r) mod n of r's
+// window at the next free row j, taken from slot_ctr[r]). pos[t*n + r] is where
+// the token's partial for r comes back in this rank's window
+// (((r - me) mod n) * slab + j, or t for r = me, -1 where r holds none of its
+// experts). Rows sit in arrival order within a slab: a row's result does not
+// depend on its position. The last CTA publishes the counts and raises
+// flag_rows in every peer's window, then clears slot_ctr for the next step.
 template <typename RT>
 __global__ void ep_peer_pack_kernel(EpPeerTable p, const float* __restrict__ x, int T,
                                     const int32_t* __restrict__ idx, const float* __restrict__ w,
                                     const float* __restrict__ sgate, int has_shared, EpRankTable rt,
-                                    const int32_t* __restrict__ send_tok, const int32_t* __restrict__ counts,
-                                    uint32_t epoch) {
+                                    int32_t* __restrict__ slot_ctr, int32_t* __restrict__ counts,
+                                    int32_t* __restrict__ pos, uint32_t epoch) {
+    constexpr int kMaxChunks = 8;  // dp <= 2048: 8 chunks of 8 values per lane
     const int n = p.n, me = p.me, slab = p.slab, dp = p.dp, k = p.k;
     const int lane = threadIdx.x & 31;
-    const int R = n * slab;
     const int nw = (int)((gridDim.x * blockDim.x) >> 5);
-    for (int row = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); row < R; row += nw) {
-        const int s = row / slab, j = row - s * slab;
-        const int r = (me + s) % n;
-        if (j >= (s == 0 ? T : counts[r])) continue;  // whole warp
-        const int t = s == 0 ? j : send_tok[(int64_t)r * slab + j];
-        const int64_t drow = (int64_t)((n - s) % n) * slab + j;  // row in r's window
+    const int nch = dp / 256;
+    for (int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); t < T; t += nw) {
+        // destination ranks of this token's slots
+        int e = -1, owner = -1;
+        if (lane < k) {
+            e = idx[(int64_t)t * k + lane];
+            owner = 0;
+            while (owner + 1 < n && e >= rt.begin[owner + 1]) ++owner;
+        }
+        uint32_t lo_bits = owner >= 0 && owner < 32 ? 1u << owner : 0u;
+        uint32_t hi_bits = owner >= 32 ? 1u << (owner - 32) : 0u;
+        lo_bits = __reduce_or_sync(0xffffffffu, lo_bits);
+        hi_bits = __reduce_or_sync(0xffffffffu, hi_bits);
+        const uint64_t dests = ((uint64_t)hi_bits << 32 | lo_bits) | (1ull << me);
+        const float wt = lane < k ? w[(int64_t)t * k + lane] : 0.f;
+        const float sg = has_shared ? sgate[t] : 0.f;
+        // the row, converted once
+        uint4 hv[kMaxChunks];
+        float4 fa[kMaxChunks], fb[kMaxChunks];
         const float* src = x + (int64_t)t * dp;
-        RT* dst = wptr<RT>(p, r, p.off_rows) + drow * dp;
-#pragma unroll 4
-        for (int c = lane * 8; c < dp; c += 256) {
-            const float4 a = ld_f4(src + c), b = ld_f4(src + c + 4);
-            if constexpr (sizeof(RT) == 2) {
-                *reinterpret_cast<uint4*>(dst + c) =
-                    make_uint4(pack_h2f(a.x, a.y), pack_h2f(a.z, a.w), pack_h2f(b.x, b.y), pack_h2f(b.z, b.w));
-            } else {
-                float* o = reinterpret_cast<float*>(dst) + c;
-                *reinterpret_cast<float4*>(o) = a;
-                *reinterpret_cast<float4*>(o + 4) = b;
+#pragma unroll
+        for (int i = 0; i < kMaxChunks; ++i) {
+            if (i < nch) {
+                const float4 a = ld_f4(src + i * 256 + lane * 8), b = ld_f4(src + i * 256 + lane * 8 + 4);
+                if constexpr (sizeof(RT) == 2) {
+                    hv[i] = make_uint4(pack_h2f(a.x, a.y), pack_h2f(a.z, a.w), pack_h2f(b.x, b.y), pack_h2f(b.z, b.w));
+                } else {
+                    fa[i] = a;
+                    fb[i] = b;
+                }
             }
         }
-        int32_t* m = wptr<int32_t>(p, r, p.off_meta) + drow * p.meta_ld;
-        if (lane < k) {
-            const int lo = rt.begin[r], hi = rt.begin[r + 1];
-            const int e = idx[(int64_t)t * k + lane];
-            m[lane] = (e >= lo && e < hi) ? e : -1;
-            m[k + lane] = __float_as_int(w[(int64_t)t * k + lane]);
+        int my_pos = -1;  // lane r < n: pos[t*n + r]
+        for (uint64_t rest = dests; rest; rest &= rest - 1) {
+            const int r = __ffsll((long long)rest) - 1;
+            int j = t;
+            if (r != me) {
+                if (lane == 0) j = atomicAdd(slot_ctr + r, 1);
+                j = __shfl_sync(0xffffffffu, j, 0);
+            }
+            const int s = (r - me + n) % n;                          // r's slab in this rank's window
+            const int64_t drow = (int64_t)((n - s) % n) * slab + j;  // the row in r's window
+            if (lane == r) my_pos = s * slab + j;
+            RT* dst = wptr<RT>(p, r, p.off_rows) + drow * dp;
+#pragma unroll
+            for (int i = 0; i < kMaxChunks; ++i) {
+                if (i < nch) {
+                    if constexpr (sizeof(RT) == 2) {
+                        *reinterpret_cast<uint4*>(dst + i * 256 + lane * 8) = hv[i];
+                    } else {
+                        float* o = reinterpret_cast<float*>(dst) + i * 256 + lane * 8;
+                        *reinterpret_cast<float4*>(o) = fa[i];
+                        *reinterpret_cast<float4*>(o + 4) = fb[i];
+                    }
+                }
+            }
+            int32_t* m = wptr<int32_t>(p, r, p.off_meta) + drow * p.meta_ld;
+            if (lane < k) {
+                m[lane] = owner == r ? e : -1;
+                m[k + lane] = __float_as_int(wt);
+            }
+            if (lane < p.meta_ld - 2 * k) m[2 * k + lane] = lane == 0 ? __float_as_int(r == me ? sg : 0.f) : 0;
         }
-        if (lane < p.meta_ld - 2 * k)
-            m[2 * k + lane] = lane == 0 ? __float_as_int(s == 0 && has_shared ? sgate[t] : 0.f) : 0;
+        if (lane < n) pos[(int64_t)t * n + lane] = my_pos;
     }
     after_all_ctas(wptr<uint32_t>(p, me, p.off_done_pack), [&](int tid) {
-        if (tid == 0) wptr<int32_t>(p, me, p.off_cnt)[0] = T;
-        if (tid >= 1 && tid < n) {
-            const int r = (me + tid) % n, slot = n - tid;
-            wptr<int32_t>(p, r, p.off_cnt)[slot] = counts[r];
+        if (tid == me) {
+            counts[me] = T;
+            wptr<int32_t>(p, me, p.off_cnt)[0] = T;
+        } else if (tid < n) {
+            const int r = tid, slot = (me - r + n) % n;
+            const int c = slot_ctr[r];
+            counts[r] = c;
+            slot_ctr[r] = 0;  // for the next step
+            wptr<int32_t>(p, r, p.off_cnt)[slot] = c;
             st_release_sys(wptr<uint32_t>(p, r, p.off_flag_rows) + slot, epoch);
         }
     });
@@ -345,41 +346,49 @@ __global__ void ep_peer_combine_return_kernel(EpPeerTable p, const __half* __res
     });
 }
 
+// 8 values of a partial row (f16 or f32) added to acc.
 template <typename PT>
-__device__ __forceinline__ float4 part4(const PT* q) {
+__device__ __forceinline__ void add8(const PT* q, float (&acc)[8]) {
     if constexpr (sizeof(PT) == 2) {
-        const uint2 v = *reinterpret_cast<const uint2*>(q);
-        const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
-        const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
-        return make_float4(a.x, a.y, b.x, b.y);
+        const uint4 v = *reinterpret_cast<const uint4*>(q);
+        const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&u[i]));
+            acc[2 * i] += f.x;
+            acc[2 * i + 1] += f.y;
+        }
     } else {
-        return *reinterpret_cast<const float4*>(q);
+        const float4 a = *reinterpret_cast<const float4*>(q), b = *reinterpret_cast<const float4*>(q + 4);
+        acc[0] += a.x, acc[1] += a.y, acc[2] += a.z, acc[3] += a.w;
+        acc[4] += b.x, acc[5] += b.y, acc[6] += b.z, acc[7] += b.w;
     }
 }
 
 // Waits for every peer's returns, then out[t] = y[t] + the remote parts in
-// ascending rank order.
+// ascending rank order. One warp per token (lane r holds pos[t][r]), 8 values
+// per lane per chunk.
 template <typename PT>
 __global__ void ep_peer_combine_kernel(EpPeerTable p, const PT* __restrict__ y, const int32_t* __restrict__ pos, int T,
                                        uint32_t epoch, float* __restrict__ out) {
     peer_wait(p, p.off_flag_back, epoch, kEpErrBackWait);
-    const int n = p.n, dp = p.dp, d4 = dp >> 2;
+    const int n = p.n, dp = p.dp;
+    const int lane = threadIdx.x & 31;
     const PT* back = wptr<const PT>(p, p.me, p.off_back);
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < (int64_t)T * d4;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int t = (int)(i / d4), c = (int)(i % d4) * 4;
-        float4 acc = part4(y + (int64_t)t * dp + c);
-        for (int r = 0; r < n; ++r) {
-            if (r == p.me) continue;
-            const int q = pos[(int64_t)t * n + r];
-            if (q < 0) continue;
-            const float4 v = part4(back + (int64_t)q * dp + c);
-            acc.x += v.x;
-            acc.y += v.y;
-            acc.z += v.z;
-            acc.w += v.w;
+    const int nw = (int)((gridDim.x * blockDim.x) >> 5);
+    for (int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); t < T; t += nw) {
+        const int my_pos = lane < n && lane != p.me ? pos[(int64_t)t * n + lane] : -1;
+        for (int c = lane * 8; c < dp; c += 256) {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            add8(y + (int64_t)t * dp + c, acc);
+            for (int r = 0; r < n; ++r) {
+                const int q = __shfl_sync(0xffffffffu, my_pos, r);
+                if (q >= 0) add8(back + (int64_t)q * dp + c, acc);
+            }
+            float4* o = reinterpret_cast<float4*>(out + (int64_t)t * dp + c);
+            o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+            o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
         }
-        *reinterpret_cast<float4*>(out + (int64_t)t * dp + c) = acc;
     }
 }
 
@@ -419,20 +428,17 @@ EpPeerTable ep_peer_layout(int n, int me, int slab, int dp, int k, int rows_f16,
     return p;
 }
 
-cudaError_t launch_ep_peer_plan(const int32_t* idx, int T, int k, const EpRankTable& rt, int me, int slab,
-                                int32_t* send_tok, int32_t* counts, int32_t* pos, cudaStream_t s) {
-    ep_peer_plan_kernel<<<rt.n, kPlanThreads, 0, s>>>(idx, T, k, rt, me, slab, send_tok, counts, pos);
-    return cudaGetLastError();
-}
-
 cudaError_t launch_ep_peer_pack(const EpPeerTable& p, const float* x, int T, const int32_t* idx, const float* w,
-                                const float* sgate, int has_shared, const EpRankTable& rt, const int32_t* send_tok,
-                                const int32_t* counts, uint32_t epoch, int n_sm, cudaStream_t s) {
-    const unsigned grid = grid_for((int64_t)p.n * p.slab * 32, n_sm, 8);  // a warp per row
+                                const float* sgate, int has_shared, const EpRankTable& rt, int32_t* slot_ctr,
+                                int32_t* counts, int32_t* pos, uint32_t epoch, int n_sm, cudaStream_t s) {
+    if (p.dp % 256 || p.dp > 2048 || p.k > 32 || p.n > 32) return cudaErrorInvalidValue;
+    const unsigned grid = grid_for((int64_t)std::max(T, 1) * 32, n_sm, 8);  // a warp per token
     if (p.rows_f16)
-        ep_peer_pack_kernel<__half><<<grid, 256, 0, s>>>(p, x, T, idx, w, sgate, has_shared, rt, send_tok, counts, epoch);
+        ep_peer_pack_kernel<__half><<<grid, 256, 0, s>>>(p, x, T, idx, w, sgate, has_shared, rt, slot_ctr, counts, pos,
+                                                         epoch);
     else
-        ep_peer_pack_kernel<float><<<grid, 256, 0, s>>>(p, x, T, idx, w, sgate, has_shared, rt, send_tok, counts, epoch);
+        ep_peer_pack_kernel<float><<<grid, 256, 0, s>>>(p, x, T, idx, w, sgate, has_shared, rt, slot_ctr, counts, pos,
+                                                        epoch);
     return cudaGetLastError();
 }
 
@@ -469,7 +475,8 @@ cudaError_t launch_ep_peer_combine_return(const EpPeerTable& p, const __half* ye
 
 cudaError_t launch_ep_peer_combine(const EpPeerTable& p, const void* y, const int32_t* pos, int T, uint32_t epoch,
                                    float* out, int n_sm, cudaStream_t s) {
-    const unsigned grid = grid_for((int64_t)T * (p.dp / 4), n_sm, 8);
+    const unsigned grid = grid_for((int64_t)std::max(T, 1) * 32, n_sm, 8);  // a warp per token
+    if (p.dp % 256) return cudaErrorInvalidValue;
     if (p.rows_f16)
         ep_peer_combine_kernel<__half><<<grid, 256, 0, s>>>(p, static_cast<const __half*>(y), pos, T, epoch, out);
     else

@@ -130,14 +130,14 @@ enum : int { kEpErrRowsWait = 21, kEpErrBackWait = 22 };
 // Region offsets for n ranks, slabs of `slab` rows of dp values (f16 or f32);
 // *bytes = window size.
 EpPeerTable ep_peer_layout(int n, int me, int slab, int dp, int k, int rows_f16, size_t* bytes);
-// Per destination rank: send_tok[r*slab + j] = its j-th token, counts[r] (counts[me] = T),
-// pos (T, n): the row in this rank's window where the partial for (t, r) returns, or -1.
-cudaError_t launch_ep_peer_plan(const int32_t* idx, int T, int k, const EpRankTable& rt, int me, int slab,
-                                int32_t* send_tok, int32_t* counts, int32_t* pos, cudaStream_t s);
-// Rows and metadata into the destination windows, then cnt and flag_rows = epoch in every peer.
+// Rows and metadata of the T local tokens into the destination windows (one warp
+// per token; row slots taken from slot_ctr, zero between steps), pos (T, n): the
+// row in this rank's window where the partial for (t, r) returns, or -1;
+// counts[r] rows sent to r (counts[me] = T); then cnt and flag_rows = epoch in
+// every peer. dp a multiple of 256 up to 2048.
 cudaError_t launch_ep_peer_pack(const EpPeerTable& p, const float* x, int T, const int32_t* idx, const float* w,
-                                const float* sgate, int has_shared, const EpRankTable& rt, const int32_t* send_tok,
-                                const int32_t* counts, uint32_t epoch, int n_sm, cudaStream_t s);
+                                const float* sgate, int has_shared, const EpRankTable& rt, int32_t* slot_ctr,
+                                int32_t* counts, int32_t* pos, uint32_t epoch, int n_sm, cudaStream_t s);
 // Waits for every peer's rows of this epoch, then window metadata -> idx / w / sgate (R = n * slab rows).
 cudaError_t launch_ep_peer_prep(const EpPeerTable& p, int T, int e_begin, int e_end, int E, uint32_t epoch,
                                 int32_t* idx, float* w, float* sgate, int32_t* bad, int n_sm, cudaStream_t s);

@@ -72,12 +72,12 @@ struct PeerCtx {
     size_t window_bytes = 0;
     void* y = nullptr;  // expert-block output for the window's rows (row type)
     size_t y_bytes = 0;
-    int32_t* aux = nullptr;  // send_tok (n * slab), counts (n + 1), pos (slab * n), received (n)
+    int32_t* aux = nullptr;  // slot counters (n), counts (n + 1), pos (slab * n), received (n)
     size_t aux_bytes = 0;
     std::vector<char*> mapped;  // peers' windows opened here
     uint32_t epoch = 0;
-    // phase timing (profiling): route, pack, rows wait + unpack, experts, return, combine
-    static constexpr int kPhases = 6;
+    // phase timing (profiling): route, plan, pack, rows wait + unpack, experts, return, combine
+    static constexpr int kPhases = 7;
     bool prof = false;
     cudaEvent_t ev[kPhases + 1] = {};
     double ms[kPhases] = {};
@@ -1213,10 +1213,12 @@ int aero_cuda_ep_peer_open(void* handle, int n_ranks, int rank, const int32_t* r
     if (pc.open) return h->fail("the peer exchange is already open on this handle"), -1;
     aero::EpRankTable rt{};
     if (!ep_rank_table(*h, n_ranks, rank, rank_expert_begin, &rt)) return -1;
-    if (n_ranks < 2) return h->fail("the peer exchange needs at least 2 ranks"), -1;
+    if (n_ranks < 2 || n_ranks > 32) return h->fail("the peer exchange runs on 2 to 32 ranks (%d)", n_ranks), -1;
     if (row_dtype != AERO_EP_ROWS_F32 && row_dtype != AERO_EP_ROWS_F16) return h->fail("row_dtype %d", row_dtype), -1;
     if (h->d != h->dp) return h->fail("expert parallel needs n_embd %% 128 == 0 (n_embd=%d)", h->d), -1;
     if (slab_rows < 1) return h->fail("slab_rows %d", slab_rows), -1;
+    if (h->dp % 256 || h->dp > 2048)
+        return h->fail("the peer exchange moves rows of up to 2048 values in 256-value chunks (n_embd=%d)", h->d), -1;
     if ((int64_t)n_ranks * slab_rows > (1 << 24)) return h->fail("n_ranks * slab_rows too large"), -1;
     if (!ipc_out) return h->fail("null ipc_out"), -1;
     cudaSetDevice(h->device);
@@ -1229,7 +1231,7 @@ int aero_cuda_ep_peer_open(void* handle, int n_ranks, int rank, const int32_t* r
                                                  row_dtype == AERO_EP_ROWS_F16, &wbytes);
     const size_t esz = row_dtype == AERO_EP_ROWS_F16 ? 2 : 4;
     const size_t ybytes = (size_t)R * h->dp * esz;
-    const size_t abytes = ((size_t)R + n_ranks + 1 + (size_t)slab_rows * n_ranks + n_ranks) * 4;
+    const size_t abytes = ((size_t)n_ranks + n_ranks + 1 + (size_t)slab_rows * n_ranks + n_ranks) * 4;
     void *w = nullptr, *y = nullptr, *a = nullptr;
     cudaError_t e = aero::guarded_malloc(&w, wbytes, aero::kScratch);
     if (e == cudaSuccess) e = aero::guarded_malloc(&y, ybytes, aero::kScratch);
@@ -1254,6 +1256,7 @@ int aero_cuda_ep_peer_open(void* handle, int n_ranks, int rank, const int32_t* r
     pc.tab = tab;
     cudaIpcMemHandle_t ih;
     if (!h->cuda_ok(cudaMemsetAsync(pc.window, 0, wbytes, h->stream), "window clear") ||
+        !h->cuda_ok(cudaMemsetAsync(pc.aux, 0, abytes, h->stream), "window clear") ||
         !h->cuda_ok(cudaStreamSynchronize(h->stream), "window clear") ||
         !h->cuda_ok(cudaIpcGetMemHandle(&ih, pc.window), "IPC handle of the window")) {
         h->peer_release();
@@ -1325,8 +1328,8 @@ int aero_cuda_ep_peer_step(void* handle, const float* x, int T, float* out) {
     auto& s = h->sc;
     const int n = tab.n, me = tab.me, R = n * tab.slab;
     const bool f16 = tab.rows_f16 != 0;
-    int32_t* send_tok = pc.aux;
-    int32_t* counts = pc.aux + R;
+    int32_t* slot_ctr = pc.aux;
+    int32_t* counts = pc.aux + n;
     int32_t* pos = counts + n + 1;
     int32_t* received = pos + (size_t)tab.slab * n;
     const uint32_t epoch = ++pc.epoch;
@@ -1342,12 +1345,11 @@ int aero_cuda_ep_peer_step(void* handle, const float* x, int T, float* out) {
         for (int i = 0; i < 3; ++i) h->mark(i);
     }
     mark(1);
-    ok = ok && h->cuda_ok(aero::launch_ep_peer_plan(s.idx, T, h->k, pc.rt, me, tab.slab, send_tok, counts, pos, st),
-                          "exchange plan");
-    ok = ok && h->cuda_ok(aero::launch_ep_peer_pack(tab, x, T, s.idx, s.w, s.sgate, h->has_shared, pc.rt, send_tok,
-                                                    counts, epoch, h->n_sm, st),
+    mark(2);  // (the plan is part of the pack: one phase is empty)
+    ok = ok && h->cuda_ok(aero::launch_ep_peer_pack(tab, x, T, s.idx, s.w, s.sgate, h->has_shared, pc.rt, slot_ctr,
+                                                    counts, pos, epoch, h->n_sm, st),
                           "exchange pack");
-    mark(2);
+    mark(3);
     ok = ok && h->cuda_ok(aero::launch_ep_peer_prep(tab, T, h->e_begin, h->e_end, h->E, epoch, s.idx, s.w, s.sgate,
                                                     s.ep_bad, h->n_sm, st),
                           "exchange unpack");
@@ -1355,25 +1357,25 @@ int aero_cuda_ep_peer_step(void* handle, const float* x, int T, float* out) {
     const bool gemv = !f16 && !(h->gemm_ok && h->gb_ready && R >= h->gemm_min_tokens);
     if (ok && gemv && s.xq.q1)
         ok = h->cuda_ok(aero::launch_qinput(static_cast<const float*>(rows), R, h->dp, s.xq, st), "row codes");
-    mark(3);
+    mark(4);
     // GEMM path: its combine is fused with the return (rows written straight to their owners)
     const bool fused = h->gemm_ok && h->gb_ready && (f16 || R >= h->gemm_min_tokens);
     ok = ok && aero::expert_stage(*h, rows, f16, R, T, true, pc.y, f16, fused);
-    mark(4);
+    mark(5);
     if (fused)
         ok = ok && h->cuda_ok(aero::launch_ep_peer_combine_return(tab, h->gb.y, s.inv, s.w, s.sgate, s.idx, h->E, T,
                                                                   h->has_shared, pc.y, epoch, received, h->n_sm, st),
                               "exchange combine + return");
     else
         ok = ok && h->cuda_ok(aero::launch_ep_peer_return(tab, pc.y, epoch, received, h->n_sm, st), "exchange return");
-    mark(5);
-    ok = ok && h->cuda_ok(aero::launch_ep_peer_combine(tab, pc.y, pos, T, epoch, out, h->n_sm, st), "exchange combine");
     mark(6);
+    ok = ok && h->cuda_ok(aero::launch_ep_peer_combine(tab, pc.y, pos, T, epoch, out, h->n_sm, st), "exchange combine");
+    mark(7);
     h->launches += 5 + (gemv ? 1 : 0);
     if (!ok) return -1;
     if (h->profiling && !aero::finish_profile(*h)) return -1;
     if (pc.prof) {
-        if (!h->cuda_ok(cudaEventSynchronize(pc.ev[6]), "profile")) return -1;
+        if (!h->cuda_ok(cudaEventSynchronize(pc.ev[aero::PeerCtx::kPhases]), "profile")) return -1;
         for (int i = 0; i < aero::PeerCtx::kPhases; ++i) {
             float ms = 0.f;
             cudaEventElapsedTime(&ms, pc.ev[i], pc.ev[i + 1]);
@@ -1409,11 +1411,11 @@ int aero_cuda_ep_peer_counts(void* handle, int32_t* sent, int32_t* received) {
     auto& pc = h->peer;
     if (!pc.connected) return h->fail("the peer exchange is not connected"), -1;
     cudaSetDevice(h->device);
-    const int n = pc.tab.n, me = pc.tab.me, R = n * pc.tab.slab;
+    const int n = pc.tab.n, me = pc.tab.me;
     std::vector<int32_t> c(n + 1), w(n);
     // (the window's own counts may already hold a peer's next step: read the step's copy)
-    const int32_t* step_recv = pc.aux + R + n + 1 + (size_t)pc.tab.slab * n;
-    if (!h->cuda_ok(cudaMemcpyAsync(c.data(), pc.aux + R, (size_t)n * 4, cudaMemcpyDeviceToHost, h->stream), "counts") ||
+    const int32_t* step_recv = pc.aux + n + n + 1 + (size_t)pc.tab.slab * n;
+    if (!h->cuda_ok(cudaMemcpyAsync(c.data(), pc.aux + n, (size_t)n * 4, cudaMemcpyDeviceToHost, h->stream), "counts") ||
         !h->cuda_ok(cudaMemcpyAsync(w.data(), step_recv, (size_t)n * 4, cudaMemcpyDeviceToHost, h->stream), "counts") ||
         !h->cuda_ok(cudaStreamSynchronize(h->stream), "counts"))
         return -1;
@@ -1424,9 +1426,9 @@ int aero_cuda_ep_peer_counts(void* handle, int32_t* sent, int32_t* received) {
     return 0;
 }
 
-// on != 0: time the phases of every step (synchronises each step); ms (6
+// on != 0: time the phases of every step (synchronises each step); ms (7
 // doubles, may be null) receives the mean per phase since the last read:
-// route, pack, rows wait + unpack, experts, return, combine. Returns the
+// route, plan, pack, rows wait + unpack, experts, return, combine. Returns the
 // number of steps averaged.
 int aero_cuda_ep_peer_profile(void* handle, int on, double* ms) {
     auto* h = static_cast<Handle*>(handle);

@@ -267,7 +267,7 @@ class PeerExpertParallelMoe:
     `gather(bytes) -> list of bytes in rank order` replaces the all-gather.
     """
 
-    PHASES = ("route", "pack", "rows_wait", "experts", "return", "combine")
+    PHASES = ("route", "plan", "pack", "rows_wait", "experts", "return", "combine")
 
     def __init__(self, layer, n_embd: int, n_expert: int, k: int, world: int, rank: int, max_tokens: int,
                  device="cuda", group=None, row_f16: bool = True, gather=None) -> None:

@@ -56,7 +56,9 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi sampling during the timed region."""
+    """nvidia-smi sampling (every 200 ms), started once before any timed work so
+    that the sampler's start-up never lands in a timed region; summary(t0, t1)
+    reads the samples of a window around one."""
 
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
@@ -65,9 +67,9 @@ class Clocks:
     def __init__(self, device: int):
         self.device = device
         self.proc = None
-        self.lines = []
+        self.lines = []  # (host time, csv line)
 
-    def __enter__(self):
+    def start(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -75,26 +77,31 @@ class Clocks:
             threading.Thread(target=self._read, daemon=True).start()
         except (OSError, FileNotFoundError):
             self.proc = None
-        time.sleep(0.3)
         return self
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
 
-    def __exit__(self, *a):
+    def stop(self):
         if self.proc:
-            time.sleep(0.25)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            self.proc = None
 
-    def summary(self):
+    def summary(self, t0: float, t1: float, pad: float = 0.3):
+        """Samples from pad seconds before t0 to pad seconds after t1 (regions
+        shorter than the sampling period get the samples that bracket them)."""
+        if self.proc:
+            time.sleep(max(0.0, t1 + pad - time.time()))
         sm, mx, reasons = [], 0.0, set()
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
-        for ln in self.lines:
+        for ts, ln in list(self.lines):
+            if ts < t0 - pad or ts > t1 + pad:
+                continue
             parts = [p.strip() for p in ln.split(",")]
             if len(parts) < 7:
                 continue
@@ -220,6 +227,17 @@ def main():
         torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
     dev = local
     cuda = f"cuda:{dev}"
+    clk = Clocks(dev).start()  # runs until the end, so its start-up is outside every timed region
+    try:
+        run_ours(args, ws, rank, dev, cuda, wl, spec, T, seed, clk)
+    finally:
+        clk.stop()
+
+
+def run_ours(args, ws, rank, dev, cuda, wl, spec, T, seed, clk):
+    import torch
+    from aero_b200 import synth
+    from aero_b200 import native_cuda as nc
 
     x_host = synth.make_x(T * wl.calls, spec.d, seed, bf16=wl.bf16_x)
     layer = synth.make_layer(spec, seed, device_gen=True)
@@ -289,17 +307,16 @@ def main():
         torch.distributed.barrier()
     torch.cuda.synchronize()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with Clocks(dev) as clk, torch.cuda.stream(stream):
-        # the sampler's start-up differs per rank: line the ranks up after it
-        if ws > 1:
-            torch.distributed.barrier()
-        torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
         ev0.record(stream)
+        t_start = time.time()
         for _ in range(args.steps):
             step_device()
         ev1.record(stream)
         ev1.synchronize()
+        t_end = time.time()
     torch.cuda.synchronize()
+    clocks = clk.summary(t_start, t_end)
     launches = L.stats()["launches"] - launches0
     ms = max_over_ranks(ev0.elapsed_time(ev1))
     if ws > 1:
@@ -405,7 +422,7 @@ def main():
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(x_host.nbytes),
                 "d2h_bytes_per_step": int(x_host.nbytes)},
         "gpu_launches": int(launches),
-        "clocks": clk.summary(),
+        "clocks": clocks,
         "roofline": roof,
         "stages_ms": {k: round(v, 5) for k, v in stage_avg.items()},
     }
@@ -442,6 +459,7 @@ def main():
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
 
 if __name__ == "__main__":
     main()

@@ -234,9 +234,9 @@ int aero_cuda_ep_peer_status(void* handle);
 /* Rows sent to / received from each rank in the last step (host arrays of
  * n_ranks; synchronises). */
 int aero_cuda_ep_peer_counts(void* handle, int32_t* sent, int32_t* received);
-/* Phase timing (on != 0; synchronises each step); ms (6 doubles or NULL): mean
- * device time per phase since the last read (route, pack, rows wait + unpack,
- * experts, return, combine). Returns the number of steps averaged. */
+/* Phase timing (on != 0; synchronises each step); ms (7 doubles or NULL): mean
+ * device time per phase since the last read (route, plan, pack, rows wait +
+ * unpack, experts, return, combine). Returns the number of steps averaged. */
 int aero_cuda_ep_peer_profile(void* handle, int on, double* ms);
 /* Unmaps the peers' windows and frees this rank's (call after a host barrier
  * that follows every rank's last step). */
