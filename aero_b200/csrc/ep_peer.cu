@@ -61,6 +61,28 @@ __device__ __forceinline__ uint64_t gtimer() {
     return t;
 }
 
+// Row stores through the bulk-copy engine: a warp stages a row in shared
+// memory and one lane copies it to the (local or peer) destination with
+// cp.async.bulk (plain bulk copies shared -> global, no multicast); 16-byte
+// aligned addresses and sizes.
+__device__ __forceinline__ uint32_t sh_u32(const void* q) { return (uint32_t)__cvta_generic_to_shared(q); }
+__device__ __forceinline__ void bulk_store(void* gdst, uint32_t ssrc, uint32_t bytes) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(gdst), "r"(ssrc), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// the staged rows may be overwritten
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// the copies are complete, ordered before this thread's later generic stores
+__device__ __forceinline__ void bulk_wait_all() {
+    asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// this thread's shared-memory writes, visible to the bulk-copy engine
+__device__ __forceinline__ void fence_to_async_shared() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+constexpr int kRowWarps = 8;  // warps (staging rows) per CTA of the row-moving kernels
+
 template <typename T>
 __device__ __forceinline__ T* wptr(const EpPeerTable& p, int rank, int64_t off) {
     return reinterpret_cast<T*>(p.base[rank] + off);
@@ -142,6 +164,9 @@ __global__ void ep_peer_pack_kernel(EpPeerTable p, const float* __restrict__ x, 
     const int lane = threadIdx.x & 31;
     const int nw = (int)((gridDim.x * blockDim.x) >> 5);
     const int nch = dp / 256;
+    extern __shared__ __align__(16) uint8_t row_stage[];
+    RT* srow = reinterpret_cast<RT*>(row_stage + (size_t)(threadIdx.x >> 5) * dp * sizeof(RT));
+    const uint32_t row_bytes = (uint32_t)(dp * sizeof(RT));
     for (int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); t < T; t += nw) {
         // destination ranks of this token's slots
         int e = -1, owner = -1;
@@ -157,22 +182,33 @@ __global__ void ep_peer_pack_kernel(EpPeerTable p, const float* __restrict__ x, 
         const uint64_t dests = ((uint64_t)hi_bits << 32 | lo_bits) | (1ull << me);
         const float wt = lane < k ? w[(int64_t)t * k + lane] : 0.f;
         const float sg = has_shared ? sgate[t] : 0.f;
-        // the row, converted once
-        uint4 hv[kMaxChunks];
+        // the row, converted once into this warp's staging row (after the bulk
+        // copies of the previous token have read it)
         float4 fa[kMaxChunks], fb[kMaxChunks];
         const float* src = x + (int64_t)t * dp;
 #pragma unroll
-        for (int i = 0; i < kMaxChunks; ++i) {
+        for (int i = 0; i < kMaxChunks; ++i)
             if (i < nch) {
-                const float4 a = ld_f4(src + i * 256 + lane * 8), b = ld_f4(src + i * 256 + lane * 8 + 4);
+                fa[i] = ld_f4(src + i * 256 + lane * 8);
+                fb[i] = ld_f4(src + i * 256 + lane * 8 + 4);
+            }
+        if (lane == 0) bulk_wait_read();
+        __syncwarp();
+#pragma unroll
+        for (int i = 0; i < kMaxChunks; ++i)
+            if (i < nch) {
+                const float4 a = fa[i], b = fb[i];
                 if constexpr (sizeof(RT) == 2) {
-                    hv[i] = make_uint4(pack_h2f(a.x, a.y), pack_h2f(a.z, a.w), pack_h2f(b.x, b.y), pack_h2f(b.z, b.w));
+                    *reinterpret_cast<uint4*>(srow + i * 256 + lane * 8) =
+                        make_uint4(pack_h2f(a.x, a.y), pack_h2f(a.z, a.w), pack_h2f(b.x, b.y), pack_h2f(b.z, b.w));
                 } else {
-                    fa[i] = a;
-                    fb[i] = b;
+                    float* o = reinterpret_cast<float*>(srow) + i * 256 + lane * 8;
+                    *reinterpret_cast<float4*>(o) = a;
+                    *reinterpret_cast<float4*>(o + 4) = b;
                 }
             }
-        }
+        fence_to_async_shared();
+        __syncwarp();
         int my_pos = -1;  // lane r < n: pos[t*n + r]
         for (uint64_t rest = dests; rest; rest &= rest - 1) {
             const int r = __ffsll((long long)rest) - 1;
@@ -184,19 +220,7 @@ __global__ void ep_peer_pack_kernel(EpPeerTable p, const float* __restrict__ x, 
             const int s = (r - me + n) % n;                          // r's slab in this rank's window
             const int64_t drow = (int64_t)((n - s) % n) * slab + j;  // the row in r's window
             if (lane == r) my_pos = s * slab + j;
-            RT* dst = wptr<RT>(p, r, p.off_rows) + drow * dp;
-#pragma unroll
-            for (int i = 0; i < kMaxChunks; ++i) {
-                if (i < nch) {
-                    if constexpr (sizeof(RT) == 2) {
-                        *reinterpret_cast<uint4*>(dst + i * 256 + lane * 8) = hv[i];
-                    } else {
-                        float* o = reinterpret_cast<float*>(dst) + i * 256 + lane * 8;
-                        *reinterpret_cast<float4*>(o) = fa[i];
-                        *reinterpret_cast<float4*>(o + 4) = fb[i];
-                    }
-                }
-            }
+            if (lane == 0) bulk_store(wptr<RT>(p, r, p.off_rows) + drow * dp, sh_u32(srow), row_bytes);
             int32_t* m = wptr<int32_t>(p, r, p.off_meta) + drow * p.meta_ld;
             if (lane < k) {
                 m[lane] = owner == r ? e : -1;
@@ -205,7 +229,9 @@ __global__ void ep_peer_pack_kernel(EpPeerTable p, const float* __restrict__ x, 
             if (lane < p.meta_ld - 2 * k) m[2 * k + lane] = lane == 0 ? __float_as_int(r == me ? sg : 0.f) : 0;
         }
         if (lane < n) pos[(int64_t)t * n + lane] = my_pos;
+        if (lane == 0) bulk_commit();
     }
+    if (lane == 0) bulk_wait_all();
     after_all_ctas(wptr<uint32_t>(p, me, p.off_done_pack), [&](int tid) {
         if (tid == me) {
             counts[me] = T;
@@ -293,9 +319,13 @@ __global__ void ep_peer_combine_return_kernel(EpPeerTable p, const __half* __res
     const int R = n * slab;
     const volatile int32_t* cnt = wptr<int32_t>(p, me, p.off_cnt);
     const int nw = (int)((gridDim.x * blockDim.x) >> 5);
+    extern __shared__ __align__(16) uint8_t row_stage[];
+    PT* srow = reinterpret_cast<PT*>(row_stage + (size_t)(threadIdx.x >> 5) * dp * sizeof(PT));
     for (int r = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); r < R; r += nw) {
         const int s = r / slab, j = r - s * slab;
         if (j >= (s == 0 ? T : cnt[s])) continue;  // whole warp
+        if (lane == 0) bulk_wait_read();  // the previous row's copy has read the staging row
+        __syncwarp();
         PT* dst = s == 0 ? yself + (int64_t)j * dp
                          : wptr<PT>(p, (me + s) % n, p.off_back) + ((int64_t)(n - s) * slab + j) * dp;
         // this row's slots, lane q holding slot q (k <= 32)
@@ -327,15 +357,22 @@ __global__ void ep_peer_combine_return_kernel(EpPeerTable p, const __half* __res
             }
             if (sh) add(sw, ye + ((int64_t)R * k + j) * dp);
             if constexpr (sizeof(PT) == 2) {
-                *reinterpret_cast<uint4*>(dst + c) =
+                *reinterpret_cast<uint4*>(srow + c) =
                     make_uint4(pack_h2f(a[0], a[1]), pack_h2f(a[2], a[3]), pack_h2f(a[4], a[5]), pack_h2f(a[6], a[7]));
             } else {
-                float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(dst) + c);
+                float4* o = reinterpret_cast<float4*>(reinterpret_cast<float*>(srow) + c);
                 o[0] = make_float4(a[0], a[1], a[2], a[3]);
                 o[1] = make_float4(a[4], a[5], a[6], a[7]);
             }
         }
+        fence_to_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+            bulk_store(dst, sh_u32(srow), (uint32_t)(dp * sizeof(PT)));
+            bulk_commit();
+        }
     }
+    if (lane == 0) bulk_wait_all();
     after_all_ctas(wptr<uint32_t>(p, me, p.off_done_ret), [&](int tid) {
         // this step's received counts, kept before the peers may write the next step's
         if (tid < n) recv_out[tid] = cnt[tid];
@@ -366,29 +403,28 @@ __device__ __forceinline__ void add8(const PT* q, float (&acc)[8]) {
 }
 
 // Waits for every peer's returns, then out[t] = y[t] + the remote parts in
-// ascending rank order. One warp per token (lane r holds pos[t][r]), 8 values
-// per lane per chunk.
+// ascending rank order. One warp per (token, 256-value chunk): lane r holds
+// pos[t][r], each lane adds 8 values of every part.
 template <typename PT>
 __global__ void ep_peer_combine_kernel(EpPeerTable p, const PT* __restrict__ y, const int32_t* __restrict__ pos, int T,
                                        uint32_t epoch, float* __restrict__ out) {
     peer_wait(p, p.off_flag_back, epoch, kEpErrBackWait);
-    const int n = p.n, dp = p.dp;
+    const int n = p.n, dp = p.dp, nch = dp / 256;
     const int lane = threadIdx.x & 31;
     const PT* back = wptr<const PT>(p, p.me, p.off_back);
     const int nw = (int)((gridDim.x * blockDim.x) >> 5);
-    for (int t = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); t < T; t += nw) {
+    for (int u = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); u < T * nch; u += nw) {
+        const int t = u / nch, c = (u - t * nch) * 256 + lane * 8;
         const int my_pos = lane < n && lane != p.me ? pos[(int64_t)t * n + lane] : -1;
-        for (int c = lane * 8; c < dp; c += 256) {
-            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-            add8(y + (int64_t)t * dp + c, acc);
-            for (int r = 0; r < n; ++r) {
-                const int q = __shfl_sync(0xffffffffu, my_pos, r);
-                if (q >= 0) add8(back + (int64_t)q * dp + c, acc);
-            }
-            float4* o = reinterpret_cast<float4*>(out + (int64_t)t * dp + c);
-            o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
-            o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        add8(y + (int64_t)t * dp + c, acc);
+        for (int r = 0; r < n; ++r) {
+            const int q = __shfl_sync(0xffffffffu, my_pos, r);
+            if (q >= 0) add8(back + (int64_t)q * dp + c, acc);
         }
+        float4* o = reinterpret_cast<float4*>(out + (int64_t)t * dp + c);
+        o[0] = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        o[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
 }
 
@@ -432,13 +468,20 @@ cudaError_t launch_ep_peer_pack(const EpPeerTable& p, const float* x, int T, con
                                 const float* sgate, int has_shared, const EpRankTable& rt, int32_t* slot_ctr,
                                 int32_t* counts, int32_t* pos, uint32_t epoch, int n_sm, cudaStream_t s) {
     if (p.dp % 256 || p.dp > 2048 || p.k > 32 || p.n > 32) return cudaErrorInvalidValue;
-    const unsigned grid = grid_for((int64_t)std::max(T, 1) * 32, n_sm, 8);  // a warp per token
-    if (p.rows_f16)
-        ep_peer_pack_kernel<__half><<<grid, 256, 0, s>>>(p, x, T, idx, w, sgate, has_shared, rt, slot_ctr, counts, pos,
-                                                         epoch);
-    else
-        ep_peer_pack_kernel<float><<<grid, 256, 0, s>>>(p, x, T, idx, w, sgate, has_shared, rt, slot_ctr, counts, pos,
-                                                        epoch);
+    const size_t smem = (size_t)kRowWarps * p.dp * (p.rows_f16 ? 2 : 4);
+    const unsigned grid = grid_for((int64_t)std::max(T, 1) * 32, n_sm, 4);  // a warp per token
+    cudaError_t e;
+    if (p.rows_f16) {
+        e = cudaFuncSetAttribute(ep_peer_pack_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        ep_peer_pack_kernel<__half><<<grid, kRowWarps * 32, smem, s>>>(p, x, T, idx, w, sgate, has_shared, rt, slot_ctr,
+                                                                      counts, pos, epoch);
+    } else {
+        e = cudaFuncSetAttribute(ep_peer_pack_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        ep_peer_pack_kernel<float><<<grid, kRowWarps * 32, smem, s>>>(p, x, T, idx, w, sgate, has_shared, rt, slot_ctr,
+                                                                     counts, pos, epoch);
+    }
     return cudaGetLastError();
 }
 
@@ -463,20 +506,30 @@ cudaError_t launch_ep_peer_combine_return(const EpPeerTable& p, const __half* ye
                                           const float* sgate, const int32_t* idx, int E_real, int T, int has_shared,
                                           void* yself, uint32_t epoch, int32_t* recv_out, int n_sm,
                                           cudaStream_t s) {
-    const unsigned grid = grid_for((int64_t)p.n * p.slab * 32, n_sm, 8);  // a warp per row
-    if (p.rows_f16)
-        ep_peer_combine_return_kernel<__half><<<grid, 256, 0, s>>>(p, ye, inv, w, sgate, idx, E_real, T, has_shared,
-                                                                   static_cast<__half*>(yself), epoch, recv_out);
-    else
-        ep_peer_combine_return_kernel<float><<<grid, 256, 0, s>>>(p, ye, inv, w, sgate, idx, E_real, T, has_shared,
-                                                                  static_cast<float*>(yself), epoch, recv_out);
+    if (p.dp % 256) return cudaErrorInvalidValue;
+    const size_t smem = (size_t)kRowWarps * p.dp * (p.rows_f16 ? 2 : 4);
+    const unsigned grid = grid_for((int64_t)p.n * p.slab * 32, n_sm, 4);  // a warp per row
+    cudaError_t e;
+    if (p.rows_f16) {
+        e = cudaFuncSetAttribute(ep_peer_combine_return_kernel<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem);
+        if (e != cudaSuccess) return e;
+        ep_peer_combine_return_kernel<__half><<<grid, kRowWarps * 32, smem, s>>>(
+            p, ye, inv, w, sgate, idx, E_real, T, has_shared, static_cast<__half*>(yself), epoch, recv_out);
+    } else {
+        e = cudaFuncSetAttribute(ep_peer_combine_return_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem);
+        if (e != cudaSuccess) return e;
+        ep_peer_combine_return_kernel<float><<<grid, kRowWarps * 32, smem, s>>>(
+            p, ye, inv, w, sgate, idx, E_real, T, has_shared, static_cast<float*>(yself), epoch, recv_out);
+    }
     return cudaGetLastError();
 }
 
 cudaError_t launch_ep_peer_combine(const EpPeerTable& p, const void* y, const int32_t* pos, int T, uint32_t epoch,
                                    float* out, int n_sm, cudaStream_t s) {
-    const unsigned grid = grid_for((int64_t)std::max(T, 1) * 32, n_sm, 8);  // a warp per token
     if (p.dp % 256) return cudaErrorInvalidValue;
+    const unsigned grid = grid_for((int64_t)std::max(T, 1) * (p.dp / 256) * 32, n_sm, 8);  // a warp per chunk
     if (p.rows_f16)
         ep_peer_combine_kernel<__half><<<grid, 256, 0, s>>>(p, static_cast<const __half*>(y), pos, T, epoch, out);
     else
