@@ -264,20 +264,25 @@ class PeerExpertParallelMoe:
     the peers' step flags (aero_cuda_ep_peer_* in the C ABI). One GPU per rank.
     Construction and `close` are collective over `group` (all-gather of the
     window handles, barriers); every rank must run the same number of steps.
-    `gather(bytes) -> list of bytes in rank order` replaces the all-gather.
+    When any rank cannot open or map the windows, every rank raises
+    RuntimeError("peer exchange unavailable: ...") (callers fall back together).
+    `gather(bytes) -> list of bytes in rank order` replaces the all-gather;
+    `lib` replaces the library (an object with the aero_cuda_ep_peer_* calls and
+    last_error(handle)).
     """
 
     PHASES = ("route", "plan", "pack", "rows_wait", "experts", "return", "combine")
 
     def __init__(self, layer, n_embd: int, n_expert: int, k: int, world: int, rank: int, max_tokens: int,
-                 device="cuda", group=None, row_f16: bool = True, gather=None) -> None:
+                 device="cuda", group=None, row_f16: bool = True, gather=None, lib=None) -> None:
         import torch
         import torch.distributed as dist
 
         from . import native_cuda as nc
 
         self.torch, self.dist, self.nc = torch, dist, nc
-        self.lib = nc.lib()
+        self.lib = lib if lib is not None else nc.lib()
+        self._last_error = (lambda: lib.last_error(self.h)) if lib is not None else (lambda: nc.last_error(self.h))
         self.layer, self.h = layer, layer.handle
         self.d, self.E, self.k = n_embd, n_expert, k
         self.world, self.rank, self.group = world, rank, group
@@ -285,13 +290,15 @@ class PeerExpertParallelMoe:
         self.row_dtype = ROWS_F16 if row_f16 else ROWS_F32
         self.device = torch.device(device)
         self.max_tokens = max(1, int(max_tokens))
-        self.stream = torch.cuda.Stream(device=self.device)
-        layer.set_stream(self.stream)
+        self.cuda = self.device.type == "cuda"
+        self.stream = torch.cuda.Stream(device=self.device) if self.cuda else None
+        if self.cuda:
+            layer.set_stream(self.stream)
         tab = (nc.c_int32 * len(self.begin))(*self.begin)
         ipc = (ctypes.c_char * IPC_BYTES)()
         rc = self.lib.aero_cuda_ep_peer_open(self.h, world, rank, tab, self.max_tokens, self.row_dtype, ipc)
         self.opened = rc == 0
-        err = "" if self.opened else nc.last_error(self.h)
+        err = "" if self.opened else self._last_error()
         blobs = (gather or self._gather)(bytes(ipc) if self.opened else b"")
         if not all(len(b) == IPC_BYTES for b in blobs):
             self.close(barrier=False)
@@ -300,10 +307,11 @@ class PeerExpertParallelMoe:
         rc = self.lib.aero_cuda_ep_peer_connect(self.h, allh)
         ok = self._all_ok(rc == 0)
         if not ok:
-            why = nc.last_error(self.h) if rc != 0 else "another rank failed to connect"
+            why = self._last_error() if rc != 0 else "another rank failed to connect"
             self.close(barrier=False)
             raise RuntimeError(f"peer exchange unavailable: rank {rank}: {why}")
-        torch.cuda.synchronize(self.device)
+        if self.cuda:
+            torch.cuda.synchronize(self.device)
         if dist.is_initialized():
             dist.barrier(group=group)
         self.phase_ms = {k: 0.0 for k in self.PHASES}
@@ -378,7 +386,8 @@ class PeerExpertParallelMoe:
         """Collective: waits for this rank's work, then for every rank, then frees the window."""
         if self.h is None:
             return
-        self.torch.cuda.synchronize(self.device)
+        if self.cuda:
+            self.torch.cuda.synchronize(self.device)
         if barrier and self.dist.is_initialized() and self.world > 1:
             self.dist.barrier(group=self.group)
         self.lib.aero_cuda_ep_peer_close(self.h)

@@ -127,3 +127,102 @@ def test_expert_ranges_and_shards():
     assert ep.token_shards(10, 4) == [0, 3, 6, 8, 10]
     with pytest.raises(ValueError):
         ep.expert_ranges(4, 5)
+
+
+class _FakePeerLib:
+    """The aero_cuda_ep_peer_* calls of the C ABI, failing where told (host logic only)."""
+
+    def __init__(self, rank, fail_open=(), fail_connect=()):
+        self.rank, self.fail_open, self.fail_connect = rank, fail_open, fail_connect
+        self.calls = []
+
+    def aero_cuda_ep_peer_open(self, h, world, rank, tab, slab, row_dtype, ipc):
+        self.calls.append("open")
+        if rank in self.fail_open:
+            return -1
+        ipc[:8] = bytes([rank + 1] * 8)
+        return 0
+
+    def aero_cuda_ep_peer_connect(self, h, blobs):
+        self.calls.append("connect")
+        self.blobs = blobs
+        return -1 if self.rank in self.fail_connect else 0
+
+    def aero_cuda_ep_peer_close(self, h):
+        self.calls.append("close")
+        return 0
+
+    def last_error(self, h):
+        return "refused by the fake"
+
+
+def _peer_setup_worker(rank, world, port, case, q):
+    try:
+        sys.path.insert(0, os.path.dirname(HERE))
+        import torch.distributed as dist
+
+        from aero_b200 import ep
+
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+
+        class Layer:
+            handle = 1
+
+            def set_stream(self, s):
+                raise AssertionError("no stream on the CPU")
+
+        lib = _FakePeerLib(rank, fail_open=case.get("fail_open", ()), fail_connect=case.get("fail_connect", ()))
+        try:
+            m = ep.PeerExpertParallelMoe(Layer(), 256, 8, 2, world, rank, max_tokens=16, device="cpu", lib=lib)
+        except RuntimeError as e:
+            res = ("raised", str(e), lib.calls)
+        else:
+            ipc = ep.IPC_BYTES
+            got = [lib.blobs[r * ipc] for r in range(world)]
+            m.close()
+            res = ("ok", got, lib.calls)
+        outs = [None] * world
+        dist.all_gather_object(outs, res)
+        if rank == 0:
+            q.put(("ok", outs))
+        dist.destroy_process_group()
+    except Exception as e:  # reported to the parent
+        import traceback
+
+        q.put(("err", f"rank {rank}: {e}\n{traceback.format_exc()}"))
+
+
+@pytest.mark.parametrize("case", [{}, {"fail_open": (1,)}, {"fail_connect": (0,)}])
+def test_peer_exchange_setup_is_collective(case):
+    """Every rank gets every rank's window blob in rank order; when one rank
+    cannot open or map, all ranks raise together (and release what they opened)."""
+    import torch.multiprocessing as mp
+
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_setup_worker, args=(r, world, port, case, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    msg = q.get(timeout=180)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert msg[0] == "ok", msg[1]
+    outs = msg[1]
+    if not case:
+        for kind, got, calls in outs:
+            assert kind == "ok"
+            assert got == [r + 1 for r in range(world)]
+            assert calls == ["open", "connect", "close"]
+    else:
+        for r, (kind, why, calls) in enumerate(outs):
+            assert kind == "raised" and "peer exchange unavailable" in why
+            assert calls[-1] == "close"
+        if "fail_open" in case:
+            assert all("connect" not in c for _, _, c in outs)
+            assert "refused by the fake" in outs[1][1]
