@@ -46,11 +46,22 @@ inline QInput qinput_at(void* base, int rows, int K) {
 // Quantises R rows of x (row stride ld floats) into q (K = q.K values per row).
 cudaError_t launch_qinput(const float* x, int R, int ld, QInput q, cudaStream_t s);
 
+// The dispatch of a single-token call, written by the top-k pass: its k pairs
+// are k distinct experts, each pair its own segment in slot order (perm, inv
+// identity; act_e = the selected experts, act_off[i] = i, n_active = k,
+// *p_real = k). Pairs computed independently and combined in slot order give
+// the same result as the expert-sorted dispatch.
+struct SingleDispatch {
+    int32_t *perm = nullptr, *inv = nullptr, *act_e = nullptr, *act_off = nullptr, *n_active = nullptr,
+            *p_real = nullptr;
+};
 // Top-k over logits[t][0..E) (row stride ld): idx/w (T, k), sgate[t] =
 // sigmoid(logits[t][E]) when has_shared. With xq.q1 non-null, also writes token
-// t's row of x (T, xq.K) as integer input.
+// t's row of x (T, xq.K) as integer input. With T == 1 and one.perm non-null,
+// also writes that call's dispatch (SingleDispatch).
 cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int norm, int has_shared, int32_t* idx,
-                        float* w, float* sgate, const float* x, QInput xq, cudaStream_t s);
+                        float* w, float* sgate, const float* x, QInput xq, cudaStream_t s,
+                        SingleDispatch one = SingleDispatch{});
 
 // Dispatch: expert-contiguous permutation of the T*k pairs. Writes offsets[E+1],
 // perm[P] (sorted position -> pair), inv[P] (pair -> sorted position), the active

@@ -399,7 +399,18 @@ bool route_stage(Handle& h, const float* x, int T, const float* logits_in, bool 
     h.mark(1);
     // the GEMV path reads x in integer form; top-k writes it in the same pass
     QInput xq = qx ? s.xq : QInput{};
-    if (!h.cuda_ok(launch_topk(s.logits, ld, T, h.E, h.k, h.norm, h.has_shared, s.idx, s.w, s.sgate, x, xq, st), "top-k"))
+    // a single token's dispatch comes from the top-k pass (expert_stage skips the sort)
+    SingleDispatch one{};
+    if (T == 1) {
+        one.perm = s.perm;
+        one.inv = s.inv;
+        one.act_e = s.act_e;
+        one.act_off = s.act_off;
+        one.n_active = s.n_active;
+        one.p_real = s.offsets + h.E;
+    }
+    if (!h.cuda_ok(launch_topk(s.logits, ld, T, h.E, h.k, h.norm, h.has_shared, s.idx, s.w, s.sgate, x, xq, st, one),
+                   "top-k"))
         return false;
     h.launches += 1;
     h.mark(2);
@@ -417,11 +428,14 @@ bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool ski
     cudaStream_t st = h.stream;
     const int P = T * h.k;
     const int n_buckets = skip_slots ? h.E + 1 : h.E;
-    if (!h.cuda_ok(launch_dispatch(s.idx, P, n_buckets, s.offsets, s.perm, s.inv, s.act_e, s.act_off, s.n_active, s.dwork,
-                                   st, h.E),
-                   "dispatch"))
-        return false;
-    h.launches += 4;
+    // (a single token's pairs were laid out by route_stage's top-k pass)
+    if (T != 1 || skip_slots) {
+        if (!h.cuda_ok(launch_dispatch(s.idx, P, n_buckets, s.offsets, s.perm, s.inv, s.act_e, s.act_off, s.n_active,
+                                       s.dwork, st, h.E),
+                       "dispatch"))
+            return false;
+        h.launches += 4;
+    }
     h.mark(3);
     const int32_t* skip_idx = skip_slots ? s.idx : nullptr;
     const bool use_gemm = h.gemm_ok && h.gb_ready && (x_f16 || T >= h.gemm_min_tokens);

@@ -55,6 +55,46 @@ __global__ void __launch_bounds__(256) router_gemv_kernel(const float* __restric
     }
 }
 
+// ----------------------------------------------------------- router, T <= 4
+// One CTA per W row: its 256 threads split the row (one float4 of W per step,
+// all of the row's loads in flight at once) and a block reduction adds them.
+constexpr int kRouterTinyT = 4;
+
+__global__ void __launch_bounds__(256) router_tiny_kernel(const float* __restrict__ x, int T, int d,
+                                                          const float* __restrict__ W, int row_begin,
+                                                          const float* __restrict__ bias, int n_bias,
+                                                          float* __restrict__ logits, int ld) {
+    __shared__ float part[kRouterTinyT][8];
+    const int r = row_begin + blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const float* wr = W + (int64_t)r * d;
+    float acc[kRouterTinyT] = {0.f, 0.f, 0.f, 0.f};
+    for (int c = threadIdx.x * 4; c < d; c += 256 * 4) {
+        const float4 wv = ld_f4(wr + c);
+#pragma unroll
+        for (int i = 0; i < kRouterTinyT; ++i)
+            if (i < T) {
+                const float4 xv = ld_f4(x + (int64_t)i * d + c);
+                acc[i] = fmaf(wv.x, xv.x, acc[i]);
+                acc[i] = fmaf(wv.y, xv.y, acc[i]);
+                acc[i] = fmaf(wv.z, xv.z, acc[i]);
+                acc[i] = fmaf(wv.w, xv.w, acc[i]);
+            }
+    }
+#pragma unroll
+    for (int i = 0; i < kRouterTinyT; ++i) {
+        const float v = warp_sum(acc[i]);
+        if (lane == 0) part[i][warp] = v;
+    }
+    __syncthreads();
+    if (threadIdx.x < T) {
+        float v = 0.f;
+#pragma unroll
+        for (int w8 = 0; w8 < 8; ++w8) v += part[threadIdx.x][w8];
+        logits[(int64_t)threadIdx.x * ld + r] = v + (r < n_bias && bias ? bias[r] : 0.f);
+    }
+}
+
 // ----------------------------------------------------------- router, large T
 // 64x64 output tile per CTA, 256 threads with a 4x4 micro-tile each, K in steps
 // of 16 through shared memory (both operands are K-major in global memory).
@@ -141,7 +181,7 @@ template <int PER>  // values per lane: E <= 32 * PER
 __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int ld, int T, int E,
                                                    int k, int norm, int has_shared, int32_t* __restrict__ idx,
                                                    float* __restrict__ w, float* __restrict__ sgate,
-                                                   const float* __restrict__ x, QInput xq) {
+                                                   const float* __restrict__ x, QInput xq, SingleDispatch one) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.x * 8 + warp;
     if (t >= T) return;
@@ -168,6 +208,7 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
     for (int i = 0; i < PER; ++i) lb = key[i] > lb ? key[i] : lb;
 
     float sel_v = 0.f;  // lane j keeps the j-th selected logit (j < k <= 32 handled in rounds)
+    int sel_i = 0;      // and its expert
     float wsum = 0.f, mx = 0.f;
     for (int r = 0; r < k; ++r) {
         uint64_t best = lb;
@@ -189,7 +230,23 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
         }
         if (lane == 0) idx[(int64_t)t * k + r] = bi;
         if (r == 0) mx = bv;
-        if ((r & 31) == lane) sel_v = bv;  // only valid for k <= 32 (checked by the host)
+        if ((r & 31) == lane) {  // only valid for k <= 32 (checked by the host)
+            sel_v = bv;
+            sel_i = bi;
+        }
+    }
+    if (one.perm && T == 1) {
+        if (lane < k) {
+            one.perm[lane] = lane;
+            one.inv[lane] = lane;
+            one.act_e[lane] = sel_i;
+            one.act_off[lane] = lane;
+        }
+        if (lane == 0) {
+            one.act_off[k] = k;
+            *one.n_active = k;
+            *one.p_real = k;
+        }
     }
     // weights
     if (norm) {
@@ -373,7 +430,9 @@ cudaError_t launch_router(const float* x, int T, int d, const float* W, int row_
                           const float* bias, int n_bias, float* logits, int ld, cudaStream_t s) {
     const int rows = row_end - row_begin;
     if (rows <= 0 || T <= 0) return cudaSuccess;
-    if (T <= 32) {
+    if (T <= kRouterTinyT && d % 4 == 0) {
+        router_tiny_kernel<<<rows, 256, 0, s>>>(x, T, d, W, row_begin, bias, n_bias, logits, ld);
+    } else if (T <= 32) {
         router_gemv_kernel<<<(rows + 7) / 8, 256, 0, s>>>(x, T, d, W, row_begin, row_end, bias, n_bias, logits, ld);
     } else {
         dim3 grid((rows + kSgBN - 1) / kSgBN, (T + kSgBM - 1) / kSgBM);
@@ -383,21 +442,21 @@ cudaError_t launch_router(const float* x, int T, int d, const float* W, int row_
 }
 
 cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int norm, int has_shared, int32_t* idx,
-                        float* w, float* sgate, const float* x, QInput xq, cudaStream_t s) {
+                        float* w, float* sgate, const float* x, QInput xq, cudaStream_t s, SingleDispatch one) {
     if (T <= 0) return cudaSuccess;
     const unsigned grid = (unsigned)((T + 7) / 8);
     if (E <= 32)
-        topk_kernel<1><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq);
+        topk_kernel<1><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq, one);
     else if (E <= 64)
-        topk_kernel<2><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq);
+        topk_kernel<2><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq, one);
     else if (E <= 128)
-        topk_kernel<4><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq);
+        topk_kernel<4><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq, one);
     else if (E <= 256)
-        topk_kernel<8><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq);
+        topk_kernel<8><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq, one);
     else if (E <= 512)
-        topk_kernel<16><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq);
+        topk_kernel<16><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq, one);
     else
-        topk_kernel<32><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq);
+        topk_kernel<32><<<grid, 256, 0, s>>>(logits, ld, T, E, k, norm, has_shared, idx, w, sgate, x, xq, one);
     return cudaGetLastError();
 }
 
