@@ -328,6 +328,82 @@ def _peer_worker(rank, world, port, q):
         q.put(("err", f"rank {rank}: {e}\n{traceback.format_exc()}"))
 
 
+def _peer_f32_worker(rank, world, port, q):
+    """Decode-sized steps with f32 rows over peer memory: the GEMV path (16 tokens)
+    and the GEMM path with f32 rows and f32 partials (128 tokens)."""
+    try:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        wl = synth.CONFIGS["c3"]
+        layer = synth.make_layer(wl.spec, 1, device_gen=True)
+        begin = ep.expert_ranges(wl.spec.E, world)
+        dev = f"cuda:{rank}"
+        h = synth.open_layer(layer, device=rank, expert_range=(begin[rank], begin[rank + 1]))
+        # the SIMT router computes each token's logits the same way at any batch size, so
+        # the sharded and the single-handle runs route identically
+        h.set_router_tc(False)
+        res = {}
+        for T in (16, 128):
+            x = synth.make_x(T, wl.spec.d, 6)
+            shards = ep.token_shards(T, world)
+            p = ep.PeerExpertParallelMoe(h, wl.spec.d, wl.spec.E, wl.spec.k, world, rank,
+                                         max_tokens=shards[1] - shards[0], device=dev, row_f16=False)
+            o = p.forward(torch.from_numpy(x[shards[rank]:shards[rank + 1]]).to(dev))
+            outs = [torch.empty((shards[r + 1] - shards[r], wl.spec.d), device=dev) for r in range(world)]
+            dist.all_gather(outs, o)
+            res[T] = (torch.cat(outs).cpu().numpy(), p.status())
+            p.close()
+        if rank == 0:
+            q.put(("ok", res))
+        dist.barrier()
+        h.close()
+        dist.destroy_process_group()
+    except Exception as e:
+        import traceback
+
+        q.put(("err", f"rank {rank}: {e}\n{traceback.format_exc()}"))
+
+
+def test_ep_peer_two_gpus_f32_rows():
+    import torch
+    import torch.multiprocessing as mp
+
+    nc.require_gpu()
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_f32_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    msg = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    assert msg[0] == "ok", msg[1]
+    wl = synth.CONFIGS["c3"]
+    layer = synth.make_layer(wl.spec, 1, device_gen=True)
+    L = synth.open_layer(layer)
+    try:
+        L.set_router_tc(False)
+        for T, (got, st) in msg[1].items():
+            assert st == 0
+            single = L.forward(synth.make_x(T, wl.spec.d, 6))
+            assert rel_err(got, single) <= 1e-4, T  # f32 rows and partials
+    finally:
+        L.close()
+
+
 def test_ep_peer_two_gpus():
     """Rows and partial outputs cross by peer stores; the result matches the all-to-all path's."""
     import torch
