@@ -1,7 +1,8 @@
 // Expert-parallel exchange over peer memory: one process per GPU, each rank's
 // exchange window mapped into every other rank's address space (CUDA IPC over
-// NVLink / NVSwitch), so the rows and the partial outputs cross as plain stores
-// from the kernels that produce them, with no collective library in the step.
+// NVLink / NVSwitch), so the rows and the partial outputs cross as stores from
+// the kernels that produce them (rows staged in shared memory and sent with
+// bulk copies), with no collective library in the step.
 //
 // Window of rank q (same layout on every rank; slab s holds the rows of rank
 // (q + s) mod n, so slab 0 is q's own tokens):
@@ -19,9 +20,11 @@
 //           (rows in arrival order within a slab); the last CTA then writes
 //           cnt and flag_rows = e into every peer's window
 //   prep    waits for flag_rows = e from every peer, then metadata -> buckets
-//   (this rank's experts over its window rows, into a local y)
-//   return  y rows of slabs 1..n-1 into the owners' back slabs; the last CTA
-//           sets flag_back = e in every peer's window
+//   (this rank's experts over its window rows)
+//   return  each row's partial output into its owner's back slab (slab 0:
+//           this rank's y); on the GEMM path this is the expert block's
+//           combine itself. The last CTA sets flag_back = e in every peer's
+//           window
 //   combine waits for flag_back = e, then self part + remote parts in rank
 //           order (the same sum, in the same order, as the all-to-all path)
 // One buffer per direction suffices: a rank writes step e+1 rows into a peer
@@ -36,7 +39,6 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
-#include <cub/block/block_scan.cuh>
 
 #include "internal.h"
 
