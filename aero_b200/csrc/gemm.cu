@@ -68,8 +68,8 @@ constexpr uint32_t kRawRing = 96 * 1024;
 // TMEM columns
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccStride = kGemmNT;     // 192 columns per accumulator, two accumulators
-constexpr int kAStages = kStages;            // A stages of one 64-value K step:
-constexpr uint32_t kAStageCols = 32;         //   128 rows x 64 f16 = 32 columns each
+// A stages (kStages, one 64-value K step each): 128 rows x 64 f16 = 32 columns each
+constexpr uint32_t kAStageCols = 32;
 constexpr uint32_t kAColBase = 2 * kGemmNT;  // 384: the A stages fill columns 384-511
 
 enum : int { kErrRawFull = 1, kErrBFull = 2, kErrEmpty = 3, kErrAcc = 4, kErrAFull = 5, kErrAEmpty = 6 };

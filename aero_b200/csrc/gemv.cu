@@ -59,12 +59,6 @@ __device__ __forceinline__ int token_of(const GemvArgs& a, const UnitSrc& u, int
     return u.shared ? pos - a.T * a.k : a.perm[pos] / a.k;
 }
 
-// Four codes held one per byte of nb -> floats (byte - bias), exactly.
-__device__ __forceinline__ void bytes4_to_f(uint32_t nb, float bias, float (&f)[4]) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k) f[k] = __int_as_float(__byte_perm(nb, 0x4B000000u, 0x7540 + k)) - bias;
-}
-
 template <int DT>
 struct Layout;
 // Q8_0 row of K values: K bytes of codes, a f16 scale per 32 values. Chunk c =
