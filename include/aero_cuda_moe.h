@@ -226,7 +226,9 @@ int aero_cuda_ep_peer_open(void* handle, int n_ranks, int rank, const int32_t* r
  * aero_cuda_ep_peer_open), in rank order. Refused when two ranks share a GPU. */
 int aero_cuda_ep_peer_connect(void* handle, const void* ipc_all);
 /* x (T, n_embd) f32 device, T <= slab_rows -> out (T, n_embd) f32 device;
- * enqueued on the handle's stream. */
+ * enqueued on the handle's stream. A step refused on one rank (or a rank that
+ * stops stepping) leaves the other ranks' waits to give up after 5 s; their
+ * aero_cuda_ep_peer_status then reports it and their outputs are not valid. */
 int aero_cuda_ep_peer_step(void* handle, const float* x, int T, float* out);
 /* 0, or the code of the first wait that gave up (21 rows, 22 returns);
  * synchronises the handle's stream. */
