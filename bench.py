@@ -449,8 +449,11 @@ def run_ours(args, ws, rank, dev, cuda, wl, spec, T, seed, clk):
         lg = x_host @ layer.router.T + (layer.router_bias if layer.router_bias is not None else 0)
         threads = os.cpu_count() or 1
         tps, kind, n, dt = cpu_reference(wl, layer, x_host, lg.astype(np.float32), args.cpu_seconds, threads)
+        # the reference block itself is single-threaded (tokens shard over processes / threads)
+        tps1, _, n1, dt1 = cpu_reference(wl, layer, x_host, lg.astype(np.float32), args.cpu_seconds / 5, 1)
         result["cpu_baseline"] = {"value": tps, "unit": "tokens/s", "cores": threads, "kind": kind,
-                                  "sample": f"{n} of {T * wl.calls} tokens, {dt:.1f} s"}
+                                  "sample": f"{n} of {T * wl.calls} tokens, {dt:.1f} s",
+                                  "single_thread": {"value": tps1, "sample": f"{n1} tokens, {dt1:.1f} s"}}
     if rank == 0:
         print(json.dumps(result), flush=True)
     if ep_mode:
