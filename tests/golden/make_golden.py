@@ -1,11 +1,11 @@
 #!/usr/bin/env python3
 """Generate tests/golden/golden.npz from the REFERENCE ITSELF.
 
-Run in a container that has the reference checkout (default /root/reference)
-after `make -C oracle all` built oracle/_ref/libaero_ssm.so from the
-reference's own src/ssm.cpp, src/moe.cpp, src/kernels.cpp:
+Run where the reference checkout exists (its root given by --ref), after
+`make -C oracle all` built oracle/_ref/libaero_ssm.so from the reference's own
+src/ssm.cpp, src/moe.cpp, src/kernels.cpp:
 
-    python tests/golden/make_golden.py [--ref /root/reference]
+    python tests/golden/make_golden.py [--ref REFERENCE_ROOT]
 
 What it records, each produced by the reference's code:
   * dequant vectors: engine/quant.py dequantize AND the C++ aero_dequant_ref on
