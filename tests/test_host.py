@@ -187,3 +187,24 @@ def test_zipf_calibration():
 def test_bf16_inputs_representable():
     x = synth.make_x(4, 64, 0, bf16=True)
     assert np.all((x.view(np.uint32) & 0xFFFF) == 0)
+
+
+def test_bench_gemm_roofline_bound():
+    """bench.py's prefill roofline takes the larger of the tensor and HBM times as the bound:
+    config 5's gate/up GEMM is tensor-bound, config 2's (512 tokens, 128 experts) HBM-bound."""
+    import bench
+    from aero_b200 import synth
+
+    pk = {"bf16_tflops": 1641.0, "bf16_tflops_sustained": 1392.6, "hbm_gbs": 6545.0, "source": "measured"}
+    for key, stats, st, bound, frac in (
+            ("c5", {"last_pairs": 81920, "last_shared_rows": 8192, "last_active": 512},
+             {"gate_up": 0.559, "down": 0.315}, "tensor", 0.4855),
+            ("c2", {"last_pairs": 4096, "last_shared_rows": 0, "last_active": 126},
+             {"gate_up": 0.193, "down": 0.1065}, "hbm", 0.1765)):
+        spec = synth.CONFIGS[key].spec
+        per_expert, shared = bench.layer_bytes(spec)
+        r = bench.gemm_roofline(spec, stats, st, pk, per_expert // 3, shared)
+        assert r["kernel"] == "grouped_gemm_gate_up"
+        assert r["bound"] == bound and r["other_bound"]["bound"] != bound
+        assert abs(r["frac"] - frac) < 2e-3, (key, r["frac"])
+        assert abs(r["frac"] - r["achieved"] / r["peak"]) < 1e-12
