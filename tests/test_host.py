@@ -208,3 +208,18 @@ def test_bench_gemm_roofline_bound():
         assert r["bound"] == bound and r["other_bound"]["bound"] != bound
         assert abs(r["frac"] - frac) < 2e-3, (key, r["frac"])
         assert abs(r["frac"] - r["achieved"] / r["peak"]) < 1e-12
+
+
+def test_bench_clock_window():
+    """The clock sampler keeps running; a timed region reads the samples around it only, and
+    flags hardware slowdowns seen there."""
+    import bench
+
+    c = bench.Clocks(0)
+    line = lambda mhz, slow: f"{mhz}, 1965, 700.0, {slow}, Not Active, Not Active, Not Active"  # noqa: E731
+    c.lines = [(9.0, line(1200, "Not Active")), (10.1, line(1965, "Not Active")), (10.3, line(1950, "Active")),
+               (11.5, line(1000, "Not Active"))]
+    r = c.summary(10.2, 10.25, pad=0.3)
+    assert r["samples"] == 2 and r["sm_mhz"] == 1957.5 and r["sm_max_mhz"] == 1965.0
+    assert r["reasons"] == ["hw_slowdown"]
+    assert c.summary(20.0, 20.1)["reasons"] == ["unsampled"]
