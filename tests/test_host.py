@@ -223,3 +223,21 @@ def test_bench_clock_window():
     assert r["samples"] == 2 and r["sm_mhz"] == 1957.5 and r["sm_max_mhz"] == 1965.0
     assert r["reasons"] == ["hw_slowdown"]
     assert c.summary(20.0, 20.1)["reasons"] == ["unsampled"]
+
+
+def test_ctypes_signatures_match_header():
+    """Every ctypes declaration has as many arguments as the header's prototype."""
+    from aero_b200 import native_cuda as nc
+
+    src = open(os.path.join(ROOT, "include", "aero_cuda_moe.h")).read()
+    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    protos = {}
+    for m in re.finditer(r"\b(aero_cuda_\w+)\s*\(([^;{]*?)\)\s*;", src, flags=re.S):
+        name, params = m.group(1), " ".join(m.group(2).split())
+        if name.endswith("_fn"):
+            continue
+        protos[name] = 0 if params in ("", "void") else params.count(",") + 1
+    assert len(protos) >= 40
+    for name, _restype, argtypes in nc.SYMBOLS:
+        assert name in protos, name
+        assert len(argtypes) == protos[name], (name, len(argtypes), protos[name])
