@@ -32,9 +32,10 @@
 // returns, which the peer sent after it had finished reading its step-e rows;
 // and a peer returns step e+1 partials only after reading step e+1 rows, which
 // this rank writes after its step-e combine has read the step-e partials.
-// Every wait is bounded (kPeerWaitNs of %globaltimer): on expiry the CTA records
-// an error code in the window, later waits of the rank return at once, and the
-// host reads the code (aero_cuda_ep_peer_status).
+// Every wait is bounded (wait_ns of %globaltimer, a handle option, 5 s by
+// default): on expiry the CTA records an error code in the window (and in the
+// handle's host-mapped error word), later waits of the rank return at once, and
+// the host reads the code (aero_cuda_ep_peer_status, or the next call).
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -44,8 +45,6 @@
 
 namespace aero {
 namespace {
-
-constexpr uint64_t kPeerWaitNs = 5ull * 1000 * 1000 * 1000;
 
 __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
     uint32_t v;
@@ -105,8 +104,11 @@ __device__ bool peer_wait(const EpPeerTable& p, int64_t flag_off, uint32_t epoch
                     ok = 0;
                     break;
                 }
-                if (gtimer() - t0 > kPeerWaitNs) {
-                    atomicCAS(const_cast<int32_t*>(err), 0, code);
+                if (gtimer() - t0 > p.wait_ns) {
+                    if (atomicCAS(const_cast<int32_t*>(err), 0, code) == 0 && p.err_host) {
+                        *reinterpret_cast<volatile int32_t*>(p.err_host) = code;
+                        __threadfence_system();
+                    }
                     ok = 0;
                     break;
                 }

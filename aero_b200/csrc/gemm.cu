@@ -85,6 +85,7 @@ struct GemmParams {
     __half* out;
     int out_ld;
     int32_t* err;
+    int32_t* err_host;    // host-mapped copy of the first code, or null
 };
 
 struct Item {
@@ -198,7 +199,10 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
 
     auto fail = [&](int code) {
         *abort_flag = 1;
-        atomicCAS(p.err, 0, code);
+        if (atomicCAS(p.err, 0, code) == 0 && p.err_host) {
+            *reinterpret_cast<volatile int32_t*>(p.err_host) = code;
+            __threadfence_system();
+        }
     };
 
     if (warp == 0) {
@@ -786,6 +790,7 @@ cudaError_t launch_prefill_gemm(const PrefillArgs& a, GemmBuffers& b, const Gemm
     g.tiles = b.tiles;
     g.n_tiles = b.n_tiles;
     g.err = b.err;
+    g.err_host = b.err_host;
     g.e_begin = a.e_begin;
     GemmMaps maps;
     if (gateup) {

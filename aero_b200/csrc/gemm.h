@@ -35,6 +35,7 @@ struct GemmBuffers {
     GemmTile* tiles;        // (max tiles)
     int32_t* n_tiles;
     int32_t* err;           // pipeline timeout code (0 = none)
+    int32_t* err_host = nullptr;  // host-mapped copy of the first code, or null
     int rows_cap;
     CUtensorMap tmap_x[kGemmNT / 16], tmap_act[kGemmNT / 16];  // box heights 16, 32, ..., kGemmNT
 };
@@ -104,7 +105,7 @@ cudaError_t router_tc_prepare(const float* W, int n_rows, int dp, float* w_hi, f
 // partial (partial_rows x ld floats, may be null) lets small batches split K
 // over more CTAs; the splits are summed in a fixed order.
 cudaError_t launch_router_tc(const RouterTcMaps& maps, const float* x, int T, const float* bias, int n_bias,
-                             const float* gate_row, float* logits, int ld, int32_t* err, float* partial,
-                             int partial_rows, int n_sm, cudaStream_t s);
+                             const float* gate_row, float* logits, int ld, int32_t* err, int32_t* err_host,
+                             float* partial, int partial_rows, int n_sm, cudaStream_t s);
 
 }  // namespace aero

@@ -134,6 +134,8 @@ cudaError_t launch_ep_combine(const void* self_out, const void* back, int parts_
 // every rank).
 struct EpPeerTable {
     int n, me, slab, dp, k, meta_ld, rows_f16;
+    uint64_t wait_ns;    // limit of every flag wait
+    int32_t* err_host;   // host-mapped copy of the first expired wait's code, or null
     int64_t off_rows, off_meta, off_back, off_cnt, off_flag_rows, off_flag_back, off_done_pack, off_done_ret, off_err;
     char* base[kEpMaxRanks];
 };

@@ -114,6 +114,10 @@ struct Handle {
     double stage_ms[kStages] = {};
     long stage_n[kStages] = {};
     long launches = 0;        // kernels launched by this handle
+    // host-mapped word where the kernels copy the first code of a bounded wait
+    // that gave up: the host reads it at the next call without synchronising
+    int32_t* err_host = nullptr;
+    uint64_t peer_wait_ns = 5000000000ull;  // AERO_CUDA_OPT_PEER_WAIT_MS
     // prefill (tcgen05 grouped GEMM) path
     bool gemm_ok = false;     // layer shape/type supports it
     int gemm_min_tokens = 64; // calls with at least this many tokens use it
@@ -153,6 +157,7 @@ struct Handle {
         for (auto& e : sev)
             if (e) cudaEventDestroy(e);
         if (own_stream) cudaStreamDestroy(own_stream);
+        if (err_host) cudaFreeHost(err_host);
     }
     bool fail(const char* fmt, ...) {
         char buf[512];
@@ -352,6 +357,7 @@ bool ensure_scratch(Handle& h, int T) {
     if (h.gemm_ok) {
         std::string why;
         if (!gemm_setup(s.gemm_ws, gws, h.dp, h.act_ld, (int)P, cap, max_tiles, &h.gb, &why)) return h.fail("%s", why.c_str());
+        h.gb.err_host = h.err_host;
         h.gb_ready = true;
     }
     // zero the padded columns of the staging buffers once
@@ -367,7 +373,8 @@ bool router_logits_dev(Handle& h, const float* x, int T, bool with_gate) {
     const bool gate = with_gate && h.has_shared;
     if (h.rtc_ok && h.rtc_enabled && T >= kRouterTcMinTokens) {
         return h.cuda_ok(launch_router_tc(h.rtc, x, T, h.router_bias, h.E, gate ? h.router_ext + (size_t)h.E * h.dp : nullptr,
-                                          s.logits, h.lg_ld, s.tc_err, s.lg_part, s.lg_part_rows, h.n_sm, h.stream),
+                                          s.logits, h.lg_ld, s.tc_err, h.err_host, s.lg_part, s.lg_part_rows, h.n_sm,
+                                          h.stream),
                          "router (tensor cores)");
     }
     return h.cuda_ok(launch_router(x, T, h.dp, h.router_ext, 0, h.E + (gate ? 1 : 0), h.router_bias, h.E, s.logits,
@@ -553,6 +560,7 @@ bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* 
 // The prefill kernels record a non-zero code when one of their bounded waits
 // expired; report it (and clear it) at the next synchronisation point.
 bool check_pipeline(Handle& h) {
+    if (h.err_host) *reinterpret_cast<volatile int32_t*>(h.err_host) = 0;  // read below from the device flags
     if (h.sc.base && h.rtc_ok) {
         int32_t code = 0;
         if (cudaMemcpy(&code, h.sc.tc_err, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
@@ -570,10 +578,26 @@ bool check_pipeline(Handle& h) {
     return h.fail("prefill GEMM pipeline wait expired (code %d); the call's output is invalid", code);
 }
 
+// An earlier call's kernel gave up a bounded wait after that call returned (a
+// device-pointer call does not synchronise): report it now, once, and refuse
+// this call. The code is the kernel's (router, prefill GEMM or peer exchange).
+bool take_async_error(Handle& h) {
+    if (!h.err_host) return true;
+    const int32_t code = *reinterpret_cast<volatile int32_t*>(h.err_host);
+    if (code == 0) return true;
+    *reinterpret_cast<volatile int32_t*>(h.err_host) = 0;
+    if (h.sc.base) cudaMemsetAsync(h.sc.tc_err, 0, 4, h.stream);
+    if (h.gb_ready) cudaMemsetAsync(h.gb.err, 0, 4, h.stream);
+    return h.fail("a bounded device wait of an earlier call on this handle gave up (code %d): that call's output is "
+                  "invalid; this call was not run",
+                  code);
+}
+
 // Host/device wrapper: stages x and out when they are host memory or when the
 // layer is padded internally.
 bool block_entry(Handle& h, const float* x, int T, const float* logits, float* out) {
     if (T < 0) return h.fail("T=%d", T);
+    if (!take_async_error(h)) return false;
     if (T == 0) return true;
     if (cudaSetDevice(h.device) != cudaSuccess) return h.fail("cudaSetDevice(%d) failed", h.device);
     if (!ensure_scratch(h, T)) return false;
@@ -648,6 +672,13 @@ Handle* open_desc(const aero_cuda_moe_desc* d, std::string* why) {
     cudaSetDevice(h->device);
     if (cudaStreamCreateWithFlags(&h->own_stream, cudaStreamNonBlocking) != cudaSuccess) return bad("stream creation failed");
     h->stream = h->own_stream;
+    if (cudaHostAlloc(reinterpret_cast<void**>(&h->err_host), 4, cudaHostAllocMapped | cudaHostAllocPortable) !=
+        cudaSuccess) {
+        cudaGetLastError();
+        h->err_host = nullptr;
+        return bad("host-mapped error word allocation failed");
+    }
+    *reinterpret_cast<volatile int32_t*>(h->err_host) = 0;
     cudaEventCreate(&h->ev0);
     cudaEventCreate(&h->ev1);
     h->d = d->n_embd;
@@ -1072,8 +1103,35 @@ int aero_cuda_moe_set_option(void* handle, int option, int64_t value) {
         h->rtc_enabled = value != 0;
         return 0;
     }
+    if (option == AERO_CUDA_OPT_PEER_WAIT_MS) {
+        if (value < 1 || value > 600000) return h->fail("peer wait limit %lld ms outside [1, 600000]", (long long)value), -1;
+        h->peer_wait_ns = (uint64_t)value * 1000000ull;
+        h->peer.tab.wait_ns = h->peer_wait_ns;  // applies to the next step of an open exchange
+        return 0;
+    }
     h->fail("unknown option %d", option);
     return -1;
+}
+
+int aero_cuda_moe_status(void* handle) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    cudaSetDevice(h->device);
+    if (!h->cuda_ok(cudaStreamSynchronize(h->stream), "status")) return -1;
+    int32_t code = h->err_host ? *reinterpret_cast<volatile int32_t*>(h->err_host) : 0;
+    int32_t dev[3] = {0, 0, 0};
+    if (h->sc.base && h->rtc_ok) cudaMemcpy(&dev[0], h->sc.tc_err, 4, cudaMemcpyDeviceToHost);
+    if (h->gb_ready) cudaMemcpy(&dev[1], h->gb.err, 4, cudaMemcpyDeviceToHost);
+    if (h->peer.open) cudaMemcpy(&dev[2], h->peer.window + h->peer.tab.off_err, 4, cudaMemcpyDeviceToHost);
+    for (int32_t v : dev)
+        if (code == 0) code = v;
+    // the pipeline codes are cleared; a peer exchange's code stays (its waits return at once from then on)
+    if (h->err_host) *reinterpret_cast<volatile int32_t*>(h->err_host) = 0;
+    if (h->sc.base && h->rtc_ok) cudaMemset(h->sc.tc_err, 0, 4);
+    if (h->gb_ready) cudaMemset(h->gb.err, 0, 4);
+    if (!h->cuda_ok(cudaGetLastError(), "status")) return -1;
+    return code;
 }
 
 int aero_cuda_moe_info(void* handle, int32_t* out8) {
@@ -1218,6 +1276,54 @@ int aero_cuda_ep_bad_ids(void* handle) {
 
 // ------------------------------------------------ expert parallel, peer memory
 
+// The window layout a rank opened, carried in its IPC blob after the handle and
+// the GPU UUID; connect compares every rank's with its own.
+struct PeerLayout {
+    uint32_t magic, n_ranks, slab_rows, row_dtype, dp, k, n_expert, reserved;
+    uint64_t window_bytes, table_hash;
+};
+constexpr size_t kBlobLayoutOff = sizeof(cudaIpcMemHandle_t) + sizeof(cudaUUID_t);
+constexpr uint32_t kPeerLayoutMagic = 0x41455031u;  // "AEP1"
+
+static PeerLayout peer_layout_of(int n, int slab, int row_dtype, int dp, int k, int E, size_t wbytes,
+                                 const aero::EpRankTable& rt) {
+    PeerLayout l{};
+    l.magic = kPeerLayoutMagic;
+    l.n_ranks = (uint32_t)n;
+    l.slab_rows = (uint32_t)slab;
+    l.row_dtype = (uint32_t)row_dtype;
+    l.dp = (uint32_t)dp;
+    l.k = (uint32_t)k;
+    l.n_expert = (uint32_t)E;
+    l.window_bytes = wbytes;
+    uint64_t hsh = 1469598103934665603ull;  // FNV-1a over the expert table
+    for (int r = 0; r <= rt.n; ++r) {
+        hsh ^= (uint64_t)(uint32_t)rt.begin[r];
+        hsh *= 1099511628211ull;
+    }
+    l.table_hash = hsh;
+    return l;
+}
+
+static bool peer_layout_equal(const PeerLayout& a, const PeerLayout& b, std::string* why) {
+    char buf[160];
+    auto diff = [&](const char* what, unsigned long long x, unsigned long long y) {
+        std::snprintf(buf, sizeof buf, "%s %llu here, %llu there", what, x, y);
+        *why = buf;
+        return false;
+    };
+    if (b.magic != kPeerLayoutMagic) return diff("layout tag", a.magic, b.magic);
+    if (a.n_ranks != b.n_ranks) return diff("n_ranks", a.n_ranks, b.n_ranks);
+    if (a.slab_rows != b.slab_rows) return diff("slab_rows", a.slab_rows, b.slab_rows);
+    if (a.row_dtype != b.row_dtype) return diff("row type", a.row_dtype, b.row_dtype);
+    if (a.dp != b.dp) return diff("row width", a.dp, b.dp);
+    if (a.k != b.k) return diff("k", a.k, b.k);
+    if (a.n_expert != b.n_expert) return diff("n_expert", a.n_expert, b.n_expert);
+    if (a.window_bytes != b.window_bytes) return diff("window bytes", a.window_bytes, b.window_bytes);
+    if (a.table_hash != b.table_hash) return diff("expert table hash", a.table_hash, b.table_hash);
+    return true;
+}
+
 int aero_cuda_ep_peer_open(void* handle, int n_ranks, int rank, const int32_t* rank_expert_begin, int slab_rows,
                            int row_dtype, void* ipc_out) {
     auto* h = static_cast<Handle*>(handle);
@@ -1267,6 +1373,8 @@ int aero_cuda_ep_peer_open(void* handle, int n_ranks, int rank, const int32_t* r
     pc.open = true;
     pc.rt = rt;
     tab.base[rank] = pc.window;
+    tab.wait_ns = h->peer_wait_ns;
+    tab.err_host = h->err_host;
     pc.tab = tab;
     cudaIpcMemHandle_t ih;
     if (!h->cuda_ok(cudaMemsetAsync(pc.window, 0, wbytes, h->stream), "window clear") ||
@@ -1276,17 +1384,19 @@ int aero_cuda_ep_peer_open(void* handle, int n_ranks, int rank, const int32_t* r
         h->peer_release();
         return -1;
     }
-    // the blob: the window's IPC handle, then this GPU's UUID (ranks on one
-    // GPU are refused at connect)
-    static_assert(sizeof(cudaIpcMemHandle_t) + sizeof(cudaUUID_t) <= AERO_EP_IPC_BYTES, "IPC blob size");
+    // the blob: the window's IPC handle, this GPU's UUID (ranks on one GPU are
+    // refused at connect), then the window layout every rank must share
+    static_assert(kBlobLayoutOff + sizeof(PeerLayout) <= AERO_EP_IPC_BYTES, "IPC blob size");
     cudaDeviceProp prop{};
     if (!h->cuda_ok(cudaGetDeviceProperties(&prop, h->device), "device properties")) {
         h->peer_release();
         return -1;
     }
+    const PeerLayout lay = peer_layout_of(n_ranks, slab_rows, row_dtype, h->dp, h->k, h->E, wbytes, rt);
     std::memset(ipc_out, 0, AERO_EP_IPC_BYTES);
     std::memcpy(ipc_out, &ih, sizeof ih);
     std::memcpy(static_cast<char*>(ipc_out) + sizeof ih, &prop.uuid, sizeof prop.uuid);
+    std::memcpy(static_cast<char*>(ipc_out) + kBlobLayoutOff, &lay, sizeof lay);
     return 0;
 }
 
@@ -1301,6 +1411,20 @@ int aero_cuda_ep_peer_connect(void* handle, const void* ipc_all) {
     cudaSetDevice(h->device);
     const int n = pc.tab.n;
     const char* blobs = static_cast<const char*>(ipc_all);
+    // every rank must have opened the same window layout: a rank whose slabs or
+    // rows were larger would store past the end of its peers' windows
+    PeerLayout mine;
+    std::memcpy(&mine, blobs + (size_t)pc.tab.me * AERO_EP_IPC_BYTES + kBlobLayoutOff, sizeof mine);
+    for (int r = 0; r < n; ++r) {
+        PeerLayout o;
+        std::memcpy(&o, blobs + (size_t)r * AERO_EP_IPC_BYTES + kBlobLayoutOff, sizeof o);
+        std::string why;
+        if (!peer_layout_equal(mine, o, &why))
+            return h->fail("rank %d opened a different exchange window layout (%s); every rank must pass the same "
+                           "n_ranks, slab_rows (max_tokens), row type, expert table and layer shape",
+                           r, why.c_str()),
+                   -1;
+    }
     // ranks on one GPU would run kernels that wait on each other side by side
     const char* my_uuid = blobs + (size_t)pc.tab.me * AERO_EP_IPC_BYTES + sizeof(cudaIpcMemHandle_t);
     for (int r = 0; r < n; ++r)
@@ -1332,6 +1456,7 @@ int aero_cuda_ep_peer_step(void* handle, const float* x, int T, float* out) {
     if (!pc.connected) return h->fail("the peer exchange is not connected"), -1;
     const auto& tab = pc.tab;
     if (T < 0 || T > tab.slab) return h->fail("T=%d outside [0, slab_rows=%d]", T, tab.slab), -1;
+    if (!aero::take_async_error(*h)) return -1;
     if (T > 0) {
         if (!x || !out) return h->fail("null buffer"), -1;
         for (const void* p : {(const void*)x, (const void*)out})

@@ -60,6 +60,7 @@ struct RouterTcParams {
     float* logits;
     int ld;
     int32_t* err;
+    int32_t* err_host; // host-mapped copy of the first code (read by the host without synchronising), or null
     float* partial;    // split K: per-split logits [split][T][ld] (no bias), summed by router_reduce_kernel
 };
 
@@ -93,7 +94,10 @@ __global__ void __launch_bounds__(kRtThreads, 1) router_tc_kernel(const __grid_c
     const uint32_t tmem_cols = kRtTmemCols;
     auto fail = [&](int code) {
         *abort_flag = 1;
-        atomicCAS(p.err, 0, code);
+        if (atomicCAS(p.err, 0, code) == 0 && p.err_host) {
+            *reinterpret_cast<volatile int32_t*>(p.err_host) = code;
+            __threadfence_system();
+        }
     };
     if (threadIdx.x == 0) {
         for (int s = 0; s < kRtStages; ++s) {
@@ -303,8 +307,8 @@ cudaError_t router_tc_prepare(const float* W, int n_rows, int dp, float* w_hi, f
 }
 
 cudaError_t launch_router_tc(const RouterTcMaps& maps, const float* x, int T, const float* bias, int n_bias,
-                             const float* gate_row, float* logits, int ld, int32_t* err, float* partial,
-                             int partial_rows, int n_sm, cudaStream_t s) {
+                             const float* gate_row, float* logits, int ld, int32_t* err, int32_t* err_host,
+                             float* partial, int partial_rows, int n_sm, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
     if ((ld & 3) || ((uintptr_t)logits & 15)) return cudaErrorInvalidValue;
     CUtensorMap tx;
@@ -341,6 +345,7 @@ cudaError_t launch_router_tc(const RouterTcMaps& maps, const float* x, int T, co
     p.logits = logits;
     p.ld = ld;
     p.err = err;
+    p.err_host = err_host;
     dim3 grid((T + kRtM - 1) / kRtM, maps.n_rows / maps.N, splits);
     router_tc_kernel<<<grid, kRtThreads, kRtSmem, s>>>(tx, maps.hi, maps.lo, p);
     if (splits > 1) {

@@ -228,6 +228,19 @@ class CudaMoeLayer:
         if self._lib.aero_cuda_moe_set_option(self.handle, nc.OPT_ROUTER_TC, 1 if on else 0) != 0:
             raise ValueError(nc.last_error(self.handle))
 
+    def set_peer_wait_ms(self, ms: int) -> None:
+        """How long a peer-exchange kernel waits for a peer before giving up (code 21 / 22)."""
+        if self._lib.aero_cuda_moe_set_option(self.handle, nc.OPT_PEER_WAIT_MS, int(ms)) != 0:
+            raise ValueError(nc.last_error(self.handle))
+
+    def status(self) -> int:
+        """0, or the code of the first bounded device wait of this layer's kernels that gave up
+        since the last read (synchronises)."""
+        rc = self._lib.aero_cuda_moe_status(self.handle)
+        if rc < 0:
+            raise RuntimeError(nc.last_error(self.handle))
+        return int(rc)
+
     def set_stream(self, stream) -> None:
         """Run on a cudaStream_t (int) or a torch.cuda.Stream; None restores the handle's own."""
         s = getattr(stream, "cuda_stream", stream)

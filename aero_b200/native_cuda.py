@@ -31,6 +31,7 @@ MEM_WEIGHTS_RESIDENT, MEM_WEIGHTS_CACHE, MEM_KV_CACHE, MEM_SCRATCH, MEM_RUNTIME 
 
 OPT_GEMM_MIN_TOKENS = 1
 OPT_ROUTER_TC = 2
+OPT_PEER_WAIT_MS = 3
 
 
 class CudaMoeUnavailable(RuntimeError):
@@ -76,6 +77,7 @@ SYMBOLS = [
     ("aero_cuda_moe_set_profiling", c_int, [_P, c_int]),
     ("aero_cuda_moe_stage_times", c_int, [_P, _P, _P, c_int]),
     ("aero_cuda_moe_set_option", c_int, [_P, c_int, c_int64]),
+    ("aero_cuda_moe_status", c_int, [_P]),
     ("aero_cuda_ep_meta_ld", c_int, [_P]),
     ("aero_cuda_ep_dispatch", c_int, [_P, _P, c_int, c_int, c_int, POINTER(c_int32), c_int, _P, _P, _P, _P, c_int,
                                       _P, _P]),

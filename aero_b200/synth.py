@@ -9,11 +9,14 @@ regenerated alone:
     3 down (E, d, F)         4 shexp gate_inp (d,) 5 shexp gate (Fs, d)
     6 shexp up (Fs, d)       7 shexp down (d, Fs)
 
-Two generators produce the weights: numpy (default_rng(seed * 1000 + i)) for
-the small layers the tests use, and the GPU (torch.randn with a seeded CUDA
-generator, quantised by aero_cuda_quantize) for benchmark-size layers, where
-host generation would take minutes. The router, bias and inputs always come
-from numpy, so the routing of a configuration does not depend on the device.
+Three generators produce the weights: numpy (default_rng(seed * 1000 + i)) for
+the small layers the tests use; the GPU (torch.randn with a seeded CUDA
+generator, quantised by aero_cuda_quantize) for benchmark-size layers; and, for
+benchmark-size layers that must not touch the GPU (the CPU reference arm of
+bench.py), numpy over blocks of experts in worker processes, block b of tensor
+i drawn from PCG64(seed * 1000 + i) jumped b times. The router, bias and inputs
+always come from numpy, so the routing of a configuration does not depend on
+the generator.
 
 Zipf-skewed routing (configs 2 and 5): a per-expert logit bias
 b_e = tau * log p_rank(e), p_r proportional to r^-s over a seeded random
@@ -63,6 +66,10 @@ CONFIGS = {
                    bf16_x=True, note="Q4_K prefill, 512 tokens, Zipf(1.1) expert load"),
     "c3": Workload("c3_decode_q4_k_shared", LayerSpec(2048, 512, 10, 512, 512, DTYPE_Q4_K), T=32,
                    note="512 experts top-10 + sigmoid-gated shared expert, 32-token decode batch"),
+    "c4b1": Workload("c4_moe_decode_b1_q4_k", LayerSpec(2048, 128, 8, 768, 0, DTYPE_Q4_K), T=1, calls=64,
+                     note="config-4 decoder's MoE layer (Q4_K, 128 experts top-8, F=768), batch 1, 64 calls"),
+    "c4b16": Workload("c4_moe_decode_b16_q4_k", LayerSpec(2048, 128, 8, 768, 0, DTYPE_Q4_K), T=16, calls=4,
+                      note="config-4 decoder's MoE layer, batch 16, 4 calls"),
     "c5": Workload("c5_prefill_q4_k_shared", LayerSpec(2048, 512, 10, 512, 512, DTYPE_Q4_K), T=8192,
                    note="512 experts top-10 + shared expert, 8192-token prefill, uniform routing"),
     "c5z": Workload("c5_prefill_q4_k_shared_zipf1.2", LayerSpec(2048, 512, 10, 512, 512, DTYPE_Q4_K), T=8192,
@@ -111,8 +118,36 @@ def _quant_gpu(seed, i, n, dtype):
     return np.frombuffer(b, dtype=np.uint8)
 
 
-def make_layer(spec: LayerSpec, seed: int = 0, device_gen: bool = False) -> SynthLayer:
-    gen = _quant_gpu if device_gen else _quant_np
+def _host_block(args):
+    seed, i, b, n, dtype = args
+    g = np.random.Generator(np.random.PCG64(seed * 1000 + i).jumped(b))
+    w = (g.standard_normal(n, dtype=np.float32) * np.float32(0.02)).astype(np.float32)
+    return w if dtype == DTYPE_F32 else np.frombuffer(quantize(w, dtype), dtype=np.uint8)
+
+
+_HOST_POOL = None
+
+
+def _quant_host_parallel(seed, i, n, dtype, block=1 << 24):
+    """N(0, 0.02) values in blocks of `block` values (a multiple of 256), each
+    block from its own jumped PCG64 stream, quantised in a spawn process pool."""
+    global _HOST_POOL
+    import multiprocessing as mp
+    import os
+    nb = (n + block - 1) // block
+    jobs = [(seed, i, b, min(block, n - b * block), dtype) for b in range(nb)]
+    if nb == 1:
+        return _host_block(jobs[0])
+    if _HOST_POOL is None:
+        _HOST_POOL = mp.get_context("spawn").Pool(min(16, os.cpu_count() or 1))
+    return np.concatenate(_HOST_POOL.map(_host_block, jobs))
+
+
+def make_layer(spec: LayerSpec, seed: int = 0, device_gen: bool = False, host_parallel: bool = False) -> SynthLayer:
+    """device_gen: weights from the GPU generator; host_parallel: from the
+    block-parallel numpy generator (no GPU); neither: the single-stream numpy
+    generator."""
+    gen = _quant_gpu if device_gen else (_quant_host_parallel if host_parallel else _quant_np)
     d, E, F, Fs = spec.d, spec.E, spec.F, spec.Fs
     router = _normal_np(seed, 0, E * d, 0.02).reshape(E, d)
     gate = gen(seed, 1, E * F * d, spec.dtype)
@@ -128,7 +163,8 @@ def make_layer(spec: LayerSpec, seed: int = 0, device_gen: bool = False) -> Synt
             "dtype": spec.dtype,
             "ffn_len": Fs,
         }
-    return SynthLayer(spec, router, gate, up, down, None, shexp, {"seed": seed, "device_gen": device_gen})
+    return SynthLayer(spec, router, gate, up, down, None, shexp,
+                      {"seed": seed, "device_gen": device_gen, "host_parallel": host_parallel})
 
 
 def make_x(T: int, d: int, seed: int = 0, bf16: bool = False) -> np.ndarray:

@@ -2,6 +2,7 @@
 """Benchmark of the B200 MoE FFN layer (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--workload c5] [--impl ours|reference]
+    python bench.py --profile --workload c5 [--tokens T] [--calls C] [--gemm-min N]
 
 Metric: MoE-layer tokens/s. The default workload is config 5
 (512 experts top-10 + shared expert, Q4_K, 8192-token prefill): the metric is
@@ -18,14 +19,25 @@ aero_b200.ep); the step's token count stays T (strong scaling).
   value        tokens/s over K steps, inputs already in HBM, device time by
                CUDA events on the layer's stream (max over ranks)
   roofline     prefill: the larger grouped GEMM (tensor-bound: algorithmic
-               FLOPs / its CUDA-event time vs the sustained bf16 peak);
-               decode: the dominant stage (HBM-bound: GGUF bytes streamed)
+               FLOPs / its CUDA-event time vs the measured burst bf16 peak,
+               the step being ~1 ms); decode: the whole layer call (HBM-bound:
+               GGUF bytes of the experts it streams + router + activations)
+  traffic      ncu DRAM read + write bytes per launch of that kernel (TRAFFIC
+               below, from the capture its comment names)
   e2e          the same through the public API with host buffers: pinned
                host input -> device, layer, device -> pinned host output
+  decode       at N = 1, the decode configurations (c1, c4 batch 1 and 16,
+               c3) timed the same way, with their HBM bytes and fraction
   cpu_baseline the reference's own MoE block (oracle/_ref, built from its
                sources) on the host cores, over a bounded token sample
 The working set (weights >= 340 MB) exceeds the 126 MB L2, so no flush runs
 between steps.
+
+--impl reference times the reference's own CPU block (oracle/_ref) on rank 0
+with all host threads, on the same workload and config, with weights from the
+host generator (no GPU and none of this package's native code on that arm).
+--profile runs a few layer calls with device-resident inputs and prints the
+per-stage device times: the command the profile summaries are captured from.
 """
 
 from __future__ import annotations
@@ -132,14 +144,43 @@ def layer_bytes(spec):
     return per_expert, shared
 
 
+# DRAM read + write bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)
+# of the dominant kernel of a workload, keyed (workload, kernel). Each entry
+# names the capture it comes from; a kernel changed since its capture has no
+# entry (traffic: null) until it is captured again.
+TRAFFIC = {
+}
+
+
 def traffic_record(workload: str, kernel: str):
-    """DRAM bytes per launch of `kernel` on `workload` from the committed ncu
-    summary (profiles/traffic.json), or None when none was captured."""
-    p = os.path.join(ROOT, "profiles", "traffic.json")
-    if not os.path.exists(p):
-        return None
-    rec = json.load(open(p)).get(workload, {}).get(kernel)
-    return None if rec is None else rec.get("bytes_per_launch")
+    rec = TRAFFIC.get((workload, kernel))
+    return None if rec is None else rec[0]
+
+
+def config_dict(wl, ws: int) -> dict:
+    """The workload's config record, identical on both arms."""
+    spec = wl.spec
+    return {"workload": wl.name, "tokens_per_step": wl.T * wl.calls, "tokens_per_call": wl.T, "experts": spec.E,
+            "top_k": spec.k, "d": spec.d, "ffn": spec.F, "shared_ffn": spec.Fs,
+            "quant": "Q8_0" if spec.dtype == 8 else "Q4_K",
+            "routing": f"zipf{wl.zipf_s}" if wl.zipf_s else "uniform",
+            "parallelism": f"ep{ws}" if ws > 1 else "single",
+            "l2": "no flush: expert weights exceed the 126 MB L2"}
+
+
+def decode_bytes(spec, x, router, bias, T: int, calls: int) -> int:
+    """Algorithmic HBM bytes of `calls` layer calls of T tokens: GGUF bytes of the
+    distinct experts each call selects (top-k of x @ router^T + bias, computed
+    here on the host), the shared expert, the f32 router (+ shared gate row)
+    and the activations in and out."""
+    per_expert, shared = layer_bytes(spec)
+    lg = x @ router.T + (bias if bias is not None else 0)
+    total = 0
+    for c in range(calls):
+        sel = np.argpartition(-lg[c * T:(c + 1) * T], spec.k - 1, axis=1)[:, :spec.k]
+        total += len(np.unique(sel)) * per_expert + shared
+        total += (spec.E + (1 if spec.Fs else 0)) * spec.d * 4 + 2 * T * spec.d * 4
+    return int(total)
 
 
 def cpu_reference(wl, layer, x, logits, budget_s: float, threads: int):
@@ -166,9 +207,10 @@ def cpu_reference(wl, layer, x, logits, budget_s: float, threads: int):
 
 def gemm_roofline(spec, stats, stage_avg, pk, per_mat, shared):
     """Roofline of the larger grouped GEMM of a prefill call (gate/up or down). Its bound is the
-    larger of the tensor time (algorithmic FLOPs, 2 * rows * n per weight row, at the sustained
-    bf16 peak: f16 operands run at the same rate) and the HBM time (GGUF bytes of the expert
-    matrices it streams, at the measured copy bandwidth); the other is reported beside it."""
+    larger of the tensor time (algorithmic FLOPs, 2 * rows * n per weight row, at the measured
+    burst bf16 peak: the GEMM runs inside a ~1 ms step, and f16 operands run at the bf16 rate)
+    and the HBM time (GGUF bytes of the expert matrices it streams, at the measured copy
+    bandwidth); the other is reported beside it."""
     pairs, srows = stats["last_pairs"], stats["last_shared_rows"]
     active = stats["last_active"]
     dom = max(("gate_up", "down"), key=lambda k: stage_avg[k])
@@ -176,9 +218,11 @@ def gemm_roofline(spec, stats, stage_avg, pk, per_mat, shared):
     flops = 2.0 * mult * spec.d * (spec.F * pairs + spec.Fs * srows)
     nbytes = active * mult * per_mat + (mult * shared // 3 if shared else 0)
     t_s = stage_avg[dom] / 1000.0
-    peak_tc = pk.get("bf16_tflops_sustained", pk["bf16_tflops"])
+    peak_tc = pk["bf16_tflops"]
     tc = {"bound": "tensor", "achieved": flops / t_s / 1e12, "peak": peak_tc, "unit": "TFLOP/s",
-          "peak_source": f"{pk['source']} bf16 sustained (f16 operands run at the same rate)"}
+          "peak_source": f"{pk['source']} bf16 burst (f16 operands run at the same rate)"}
+    if "bf16_tflops_sustained" in pk:
+        tc["frac_of_sustained"] = tc["achieved"] / pk["bf16_tflops_sustained"]
     hbm = {"bound": "hbm", "achieved": nbytes / t_s / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
            "peak_source": f"{pk['source']} HBM copy"}
     for r in (tc, hbm):
@@ -200,51 +244,31 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-record")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="expert parallel (N > 1): rows cross by peer-memory stores (default) or NCCL all-to-all")
+    ap.add_argument("--profile", action="store_true",
+                    help="run --calls layer calls of --tokens tokens and print the per-stage device times")
+    ap.add_argument("--tokens", type=int, default=0, help="--profile: tokens per call (default: the workload's)")
+    ap.add_argument("--calls", type=int, default=3, help="--profile: layer calls")
+    ap.add_argument("--gemm-min", type=int, default=0, help="--profile: GEMM path threshold (0: library default)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     ws, rank, local = dist_env()
-    import torch
     from aero_b200 import synth
-    from aero_b200 import native_cuda as nc
 
     wl = synth.CONFIGS[args.workload]
-    spec = wl.spec
-    T = wl.T
-    seed = 0
-
     if args.impl == "reference":
-        if rank != 0:
-            return
-        x = synth.make_x(T * wl.calls, spec.d, seed, bf16=wl.bf16_x)
-        layer = synth.make_layer(spec, seed, device_gen=torch.cuda.is_available())
-        if wl.zipf_s:
-            synth.attach_zipf(layer, x, wl.zipf_s, seed)
-        lg = x @ layer.router.T + (layer.router_bias if layer.router_bias is not None else 0)
-        threads = os.cpu_count() or 1
-        per_step = max(1.0, 120.0 / (args.steps + args.warmup))
-        times = []
-        for i in range(args.warmup + args.steps):
-            tps, kind, n, dt = cpu_reference(wl, layer, x, lg.astype(np.float32), per_step, threads)
-            if i >= args.warmup:
-                times.append((n, dt))
-        n_tot = sum(n for n, _ in times)
-        t_tot = sum(dt for _, dt in times)
-        v = n_tot / t_tot
-        print(json.dumps({
-            "impl": "reference", "metric": "moe_layer_tokens_per_s", "value": v, "unit": "tokens/s",
-            "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": 1000.0 * t_tot / args.steps, "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": wl.name, "tokens_per_step": T * wl.calls, "experts": spec.E, "top_k": spec.k,
-                       "d": spec.d, "ffn": spec.F, "shared_ffn": spec.Fs, "quant": "Q8_0" if spec.dtype == 8 else "Q4_K"},
-            "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": kind,
-                             "sample": f"{times[-1][0]} tokens of {T * wl.calls} per step"},
-            "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-        }), flush=True)
+        if rank == 0:
+            run_reference(args, ws, wl)
         return
+    if args.profile:
+        run_profile(args, wl)
+        return
+
+    import torch
+    from aero_b200 import native_cuda as nc
 
     nc.lib()
     nc.require_gpu()
@@ -256,9 +280,78 @@ def main():
     cuda = f"cuda:{dev}"
     clk = Clocks(dev).start()  # runs until the end, so its start-up is outside every timed region
     try:
-        run_ours(args, ws, rank, dev, cuda, wl, spec, T, seed, clk)
+        run_ours(args, ws, rank, dev, cuda, wl, wl.spec, wl.T, 0, clk)
     finally:
         clk.stop()
+
+
+def run_reference(args, ws, wl):
+    """The reference's own CPU block (oracle/_ref) on this host's cores, on the
+    workload's config, each step a bounded token sample; weights come from the
+    host generator, so nothing on this arm uses the GPU or this package's
+    native library."""
+    from aero_b200 import synth
+    spec, T = wl.spec, wl.T
+    x = synth.make_x(T * wl.calls, spec.d, 0, bf16=wl.bf16_x)
+    layer = synth.make_layer(spec, 0, host_parallel=True)
+    if wl.zipf_s:
+        synth.attach_zipf(layer, x, wl.zipf_s, 0)
+    lg = (x @ layer.router.T + (layer.router_bias if layer.router_bias is not None else 0)).astype(np.float32)
+    threads = os.cpu_count() or 1
+    per_step = max(1.0, 120.0 / (args.steps + args.warmup))
+    times = []
+    kind = "reference"
+    for i in range(args.warmup + args.steps):
+        _, kind, n, dt = cpu_reference(wl, layer, x, lg, per_step, threads)
+        if i >= args.warmup:
+            times.append((n, dt))
+    n_tot = sum(n for n, _ in times)
+    t_tot = sum(dt for _, dt in times)
+    v = n_tot / t_tot
+    tokens_per_step = T * wl.calls
+    print(json.dumps({
+        "impl": "reference", "metric": "moe_layer_tokens_per_s", "value": v, "unit": "tokens/s",
+        "n_gpus": ws, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1000.0 * tokens_per_step / v,
+        "ms_per_step_note": f"a full {tokens_per_step}-token step at the measured rate; each timed step ran a "
+                            f"{times[-1][0]}-token sample",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(wl, ws),
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": threads, "kind": kind,
+                         "sample": f"{times[-1][0]} tokens of {tokens_per_step} per step"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_profile(args, wl):
+    """A few layer calls with device-resident inputs; prints the per-stage
+    device times of the last one (the command profile captures run)."""
+    import torch
+    from aero_b200 import native_cuda as nc
+    from aero_b200 import synth
+
+    nc.require_gpu()
+    T = args.tokens or wl.T
+    layer = synth.make_layer(wl.spec, 0, device_gen=True)
+    x_host = synth.make_x(T, wl.spec.d, 0, bf16=wl.bf16_x)
+    if wl.zipf_s:
+        synth.attach_zipf(layer, x_host, wl.zipf_s, 0)
+    L = synth.open_layer(layer)
+    if args.gemm_min:
+        L.set_gemm_min_tokens(args.gemm_min)
+    x = torch.from_numpy(x_host).cuda()
+    out = torch.empty_like(x)
+    lib = nc.lib()
+    for i in range(args.calls):
+        if i == args.calls - 1:
+            L.set_profiling(True)
+        if lib.aero_cuda_moe_forward(L.handle, 0, x.data_ptr(), T, wl.spec.d, out.data_ptr()) != 1:
+            raise RuntimeError(nc.last_error(L.handle))
+    torch.cuda.synchronize()
+    st = L.stage_times()
+    L.close()
+    print(json.dumps({"workload": wl.name, "tokens": T, "stages_ms": {k: v[0] / max(v[1], 1) for k, v in st.items()},
+                      "checksum": float(np.abs(out.cpu().numpy()).sum())}))
 
 
 def run_ours(args, ws, rank, dev, cuda, wl, spec, T, seed, clk):
@@ -400,19 +493,12 @@ def run_ours(args, ws, rank, dev, cuda, wl, spec, T, seed, clk):
         roof = gemm_roofline(spec, stats, stage_avg, pk, per_mat, shared)
         dtype = "f16"
     else:
-        dom = max(stage_avg, key=stage_avg.get)
-        alg = {
-            "gate_up": active * 2 * per_mat + (2 * shared // 3 if shared else 0),
-            "down": active * per_mat + (shared // 3 if shared else 0),
-            "router": (spec.E + (1 if spec.Fs else 0)) * spec.d * 4 + Tm * spec.d * 4,
-            "topk": Tm * (spec.E + 1) * 4,
-            "dispatch": Tm * spec.k * 16,
-            "combine": (Tm * spec.k + Tm) * spec.d * 4 + Tm * spec.d * 4,
-        }[dom]
-        achieved = alg / (stage_avg[dom] / 1000.0) / 1e9
-        roof = {"kernel": dom, "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
-                "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_source": pk["source"],
-                "algorithmic_bytes": int(alg), "avg_ms": stage_avg[dom], "active_experts": active}
+        # decode: the whole layer call streams the selected experts' blocks once
+        alg = decode_bytes(spec, x_mine, layer.router, layer.router_bias, Tm, wl.calls)
+        achieved = alg / (ms / args.steps / 1000.0) / 1e9
+        roof = {"kernel": "decode_layer", "bound": "hbm", "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": achieved / pk["hbm_gbs"], "traffic": None, "peak_source": f"{pk['source']} HBM copy",
+                "algorithmic_bytes": alg, "avg_ms": ms / args.steps}
         dtype = "f32"
     tr = traffic_record(wl.name, roof["kernel"])
     if tr is not None:
@@ -430,11 +516,7 @@ def run_ours(args, ws, rank, dev, cuda, wl, spec, T, seed, clk):
         "vs_baseline": None,
         "dtype": dtype,
         "data": "synthetic",
-        "config": {"workload": wl.name, "tokens_per_step": tokens_per_step, "experts": spec.E, "top_k": spec.k,
-                   "d": spec.d, "ffn": spec.F, "shared_ffn": spec.Fs,
-                   "quant": "Q8_0" if spec.dtype == 8 else "Q4_K", "routing": f"zipf{wl.zipf_s}" if wl.zipf_s else "uniform",
-                   "parallelism": f"ep{ws}" if ws > 1 else "single",
-                   "l2": "no flush: expert weights exceed the 126 MB L2"},
+        "config": config_dict(wl, ws),
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": int(x_host.nbytes),
                 "d2h_bytes_per_step": int(x_host.nbytes)},
         "gpu_launches": int(launches),
@@ -443,8 +525,7 @@ def run_ours(args, ws, rank, dev, cuda, wl, spec, T, seed, clk):
         "stages_ms": {k: round(v, 5) for k, v in stage_avg.items()},
     }
     if ep_mode:
-        result["config"]["exchange"] = "peer memory (CUDA IPC, NVLink stores)" if exchange == "peer" else \
-            "NCCL all-to-all"
+        result["exchange"] = "peer memory (CUDA IPC, NVLink stores)" if exchange == "peer" else "NCCL all-to-all"
         result["exchange_rows"] = {"sent": moe.last_split[0], "received": moe.last_split[1]}
         # per-phase device times of rank 0's step (a separate profiled pass, the
         # ranks lined up first: a phase that waits for peers also times their lag)
@@ -461,6 +542,8 @@ def run_ours(args, ws, rank, dev, cuda, wl, spec, T, seed, clk):
         else:
             result["ep_phases_ms"] = {k: round(v / max(moe.phase_n, 1), 5) for k, v in moe.phase_ms.items()}
         moe.set_profiling(False)
+    if ws == 1 and not args.no_decode and not wl.name.startswith(("c1", "c3", "c4")):
+        result["decode"] = decode_records(args, dev, stream, pk)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         lg = x_host @ layer.router.T + (layer.router_bias if layer.router_bias is not None else 0)
         threads = os.cpu_count() or 1
@@ -478,6 +561,51 @@ def run_ours(args, ws, rank, dev, cuda, wl, spec, T, seed, clk):
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
+
+def decode_records(args, dev, stream, pk) -> dict:
+    """The decode configurations at N = 1: one step = the workload's calls with
+    device-resident inputs, timed by CUDA events over `args.steps` steps; HBM
+    bytes as in decode_bytes, fraction of the measured copy bandwidth."""
+    import torch
+    from aero_b200 import native_cuda as nc
+    from aero_b200 import synth
+
+    lib = nc.lib()
+    out = {}
+    for key in ("c1", "c4b1", "c4b16", "c3"):
+        wl = synth.CONFIGS[key]
+        spec, T = wl.spec, wl.T
+        x_host = synth.make_x(T * wl.calls, spec.d, 0, bf16=wl.bf16_x)
+        layer = synth.make_layer(spec, 0, device_gen=True)
+        L = synth.open_layer(layer, device=dev)
+        L.set_stream(stream)
+        x = torch.from_numpy(x_host).to(f"cuda:{dev}")
+        o = torch.empty_like(x)
+
+        def step():
+            for c in range(wl.calls):
+                if lib.aero_cuda_moe_forward(L.handle, 0, x[c * T:].data_ptr(), T, spec.d, o[c * T:].data_ptr()) != 1:
+                    raise RuntimeError(nc.last_error(L.handle))
+
+        with torch.cuda.stream(stream):
+            for _ in range(args.warmup):
+                step()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(args.steps):
+                step()
+            e1.record(stream)
+        e1.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        nbytes = decode_bytes(spec, x_host, layer.router, layer.router_bias, T, wl.calls)
+        gbs = nbytes / (ms / 1000.0) / 1e9
+        out[key] = {"workload": wl.name, "tokens_per_call": T, "calls_per_step": wl.calls, "ms_per_step": ms,
+                    "us_per_call": 1000.0 * ms / wl.calls, "tokens_per_s": T * wl.calls / (ms / 1000.0),
+                    "hbm_bytes_per_step": nbytes, "achieved_gbs": gbs, "frac_of_hbm": gbs / pk["hbm_gbs"]}
+        L.close()
+        del x, o
+    return out
 
 
 if __name__ == "__main__":

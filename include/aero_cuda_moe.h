@@ -119,7 +119,8 @@ int aero_cuda_dispatch(const int64_t* idx, int T, int k, int n_expert, int32_t* 
  * Limits: T*k <= 65536 pairs and n_expert <= 1024; larger calls are refused
  * (use aero_cuda_dispatch). idx (T, k) int64, offsets (n_expert + 1) and perm
  * (T*k) int32 must be device memory; the work runs on `stream` (NULL: the
- * default stream) and the call returns when it is done. The first call on a
+ * default stream) and every call waits for that work to finish before it
+ * returns (it reads the kernels' error flag back to the host). The first call on a
  * device looks up the array's device address (cudaGetSymbolAddress); make that
  * first call before any stream capture. All calls share the array: calls whose
  * work overlaps on the GPU race and corrupt each other's results. 0 / -1; the
@@ -152,7 +153,20 @@ int aero_cuda_moe_stage_times(void* handle, double* ms, int64_t* counts, int n);
  * least 16 tokens on the tensor cores (three TF32 products of split f32
  * operands, f32 accumulate: f32-level accuracy); 0 keeps the f32 SIMT kernels. */
 #define AERO_CUDA_OPT_ROUTER_TC 2
+/* AERO_CUDA_OPT_PEER_WAIT_MS: how long a peer-exchange kernel waits for a
+ * peer's step flag before it gives up and records code 21 / 22 (default 5000;
+ * 1 to 600000). Applies from the next step. */
+#define AERO_CUDA_OPT_PEER_WAIT_MS 3
 int aero_cuda_moe_set_option(void* handle, int option, int64_t value);
+
+/* 0, or the code of the first bounded device wait of this handle's kernels that
+ * gave up since the last status read (router pipeline, prefill GEMM pipeline,
+ * peer exchange: 21 rows, 22 returns), after synchronising the handle's stream.
+ * A wait that gives up during a call with device pointers (which returns
+ * without synchronising) is also reported by the handle's next call, which is
+ * then refused. No reference counterpart (the reference has no device waits).
+ * The pipeline codes are cleared by the read; a peer-exchange code stays. */
+int aero_cuda_moe_status(void* handle);
 
 /* ------------------------------------------------------- expert parallel
  * No reference counterpart: the reference runs a layer in one process
@@ -223,12 +237,18 @@ int aero_cuda_ep_bad_ids(void* handle);
 int aero_cuda_ep_peer_open(void* handle, int n_ranks, int rank, const int32_t* rank_expert_begin,
                            int slab_rows, int row_dtype, void* ipc_out);
 /* ipc_all: n_ranks blobs of AERO_EP_IPC_BYTES bytes (as written by
- * aero_cuda_ep_peer_open), in rank order. Refused when two ranks share a GPU. */
+ * aero_cuda_ep_peer_open), in rank order. Each blob carries its rank's window
+ * layout (n_ranks, slab_rows, row type, row width, k, n_expert, window size and
+ * a hash of the expert table); connect is refused, before any peer window is
+ * mapped, when any rank's layout differs from this rank's, and when two ranks
+ * share a GPU. */
 int aero_cuda_ep_peer_connect(void* handle, const void* ipc_all);
 /* x (T, n_embd) f32 device, T <= slab_rows -> out (T, n_embd) f32 device;
  * enqueued on the handle's stream. A step refused on one rank (or a rank that
- * stops stepping) leaves the other ranks' waits to give up after 5 s; their
- * aero_cuda_ep_peer_status then reports it and their outputs are not valid. */
+ * stops stepping) leaves the other ranks' waits to give up after the handle's
+ * peer wait limit (AERO_CUDA_OPT_PEER_WAIT_MS, 5 s by default); their
+ * aero_cuda_ep_peer_status then reports it, their outputs are not valid, and
+ * their next step is refused once with the code in the error message. */
 int aero_cuda_ep_peer_step(void* handle, const float* x, int T, float* out);
 /* 0, or the code of the first wait that gave up (21 rows, 22 returns);
  * synchronises the handle's stream. */

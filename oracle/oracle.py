@@ -31,9 +31,14 @@ _orc = None
 _ref = None
 
 
-def build(ref_root: str = "/root/reference") -> None:
-    """make the oracle (and the reference objects when ref_root exists)."""
-    args = ["make", "-s", "-C", HERE, "all", f"REF={ref_root}"]
+def reference_root() -> str:
+    """The reference checkout: $AERO_REF, else a "reference" directory beside this repository."""
+    return os.environ.get("AERO_REF") or os.path.abspath(os.path.join(HERE, "..", "..", "reference"))
+
+
+def build(ref_root: str = "") -> None:
+    """make the oracle (and the reference objects when the reference tree exists)."""
+    args = ["make", "-s", "-C", HERE, "all", f"REF={ref_root or reference_root()}"]
     subprocess.run(args, check=True, capture_output=True)
 
 

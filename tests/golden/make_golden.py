@@ -203,7 +203,9 @@ def block_case(M, Q, spec, T, seed, zipf_s=0.0):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", default=os.environ.get("AERO_REF") or os.path.abspath(
+        os.path.join(os.path.dirname(__file__), "..", "..", "..", "reference")),
+        help="the reference checkout (default: $AERO_REF, else a 'reference' directory beside this repository)")
     args = ap.parse_args()
     M, NS, Q, lib = load_reference(args.ref)
     out = {}

@@ -130,22 +130,31 @@ def test_expert_ranges_and_shards():
 
 
 class _FakePeerLib:
-    """The aero_cuda_ep_peer_* calls of the C ABI, failing where told (host logic only)."""
+    """The aero_cuda_ep_peer_* calls of the C ABI, failing where told (host logic only).
+    Like the library, each blob carries the window layout (here the slab rows) and
+    connect refuses a blob set whose layouts differ."""
 
     def __init__(self, rank, fail_open=(), fail_connect=()):
         self.rank, self.fail_open, self.fail_connect = rank, fail_open, fail_connect
         self.calls = []
+        self.why = "refused by the fake"
 
     def aero_cuda_ep_peer_open(self, h, world, rank, tab, slab, row_dtype, ipc):
         self.calls.append("open")
         if rank in self.fail_open:
             return -1
         ipc[:8] = bytes([rank + 1] * 8)
+        ipc[8:12] = int(slab).to_bytes(4, "little")
         return 0
 
     def aero_cuda_ep_peer_connect(self, h, blobs):
         self.calls.append("connect")
         self.blobs = blobs
+        ipc = len(blobs) // self.world if hasattr(self, "world") else 128
+        slabs = {bytes(blobs[r * ipc + 8:r * ipc + 12]) for r in range(len(blobs) // ipc)}
+        if len(slabs) > 1:
+            self.why = "a different exchange window layout"
+            return -1
         return -1 if self.rank in self.fail_connect else 0
 
     def aero_cuda_ep_peer_close(self, h):
@@ -153,7 +162,7 @@ class _FakePeerLib:
         return 0
 
     def last_error(self, h):
-        return "refused by the fake"
+        return self.why
 
 
 def _peer_setup_worker(rank, world, port, case, q):
@@ -174,8 +183,10 @@ def _peer_setup_worker(rank, world, port, case, q):
                 raise AssertionError("no stream on the CPU")
 
         lib = _FakePeerLib(rank, fail_open=case.get("fail_open", ()), fail_connect=case.get("fail_connect", ()))
+        lib.world = world
+        max_tokens = case.get("max_tokens", {}).get(rank, 16)
         try:
-            m = ep.PeerExpertParallelMoe(Layer(), 256, 8, 2, world, rank, max_tokens=16, device="cpu", lib=lib)
+            m = ep.PeerExpertParallelMoe(Layer(), 256, 8, 2, world, rank, max_tokens=max_tokens, device="cpu", lib=lib)
         except RuntimeError as e:
             res = ("raised", str(e), lib.calls)
         else:
@@ -194,7 +205,7 @@ def _peer_setup_worker(rank, world, port, case, q):
         q.put(("err", f"rank {rank}: {e}\n{traceback.format_exc()}"))
 
 
-@pytest.mark.parametrize("case", [{}, {"fail_open": (1,)}, {"fail_connect": (0,)}])
+@pytest.mark.parametrize("case", [{}, {"fail_open": (1,)}, {"fail_connect": (0,)}, {"max_tokens": {2: 32}}])
 def test_peer_exchange_setup_is_collective(case):
     """Every rank gets every rank's window blob in rank order; when one rank
     cannot open or map, all ranks raise together (and release what they opened)."""
@@ -226,3 +237,5 @@ def test_peer_exchange_setup_is_collective(case):
         if "fail_open" in case:
             assert all("connect" not in c for _, _, c in outs)
             assert "refused by the fake" in outs[1][1]
+        if "max_tokens" in case:  # every rank sees the mismatch and raises with the reason
+            assert all("different exchange window layout" in why for _, why, _ in outs)

@@ -443,3 +443,119 @@ def test_ep_peer_two_gpus():
         L.close()
     assert rel_err(o1, single) <= 5e-3
     assert rel_err(o3, single) <= 5e-3
+
+
+def test_peer_connect_refuses_a_different_window_layout():
+    """Two ranks' windows opened on one GPU (no kernel runs): connect compares the
+    layouts in the blobs before it maps anything, so a rank that opened larger slabs
+    is refused on both sides; with equal layouts the shared GPU is refused."""
+    import ctypes
+
+    nc.require_gpu()
+    spec = synth.LayerSpec(512, 16, 4, 256, 256, Q.DTYPE_Q4_K)
+    layer = synth.make_layer(spec, 41)
+    begin = ep.expert_ranges(spec.E, 2)
+    lib = nc.lib()
+    hs = [synth.open_layer(layer, expert_range=(begin[r], begin[r + 1])) for r in range(2)]
+    tab = (nc.c_int32 * 3)(*begin)
+    try:
+        for slabs, want in (((16, 32), "different exchange window layout"), ((16, 16), "one GPU per rank")):
+            blobs = []
+            for r in range(2):
+                ipc = (ctypes.c_char * ep.IPC_BYTES)()
+                assert lib.aero_cuda_ep_peer_open(hs[r].handle, 2, r, tab, slabs[r], ep.ROWS_F32, ipc) == 0, \
+                    nc.last_error(hs[r].handle)
+                blobs.append(bytes(ipc))
+            allb = b"".join(blobs)
+            for r in range(2):
+                assert lib.aero_cuda_ep_peer_connect(hs[r].handle, allb) == -1
+                assert want in nc.last_error(hs[r].handle), (slabs, nc.last_error(hs[r].handle))
+                assert lib.aero_cuda_ep_peer_close(hs[r].handle) == 0
+    finally:
+        for h in hs:
+            h.close()
+
+
+def _peer_skip_worker(rank, world, port, q):
+    """Rank 1 leaves one step out (between steps, nothing of its own in flight): rank 0's
+    wait for its rows gives up after the handle's 50 ms limit with code 21, its later
+    waits of that step return at once, its next call is refused with the code, and both
+    ranks still close their windows."""
+    try:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60))
+        spec = synth.LayerSpec(512, 16, 4, 256, 256, Q.DTYPE_Q4_K)
+        layer = synth.make_layer(spec, 42)
+        begin = ep.expert_ranges(spec.E, world)
+        dev = f"cuda:{rank}"
+        h = synth.open_layer(layer, device=rank, expert_range=(begin[rank], begin[rank + 1]))
+        h.set_peer_wait_ms(50)
+        p = ep.PeerExpertParallelMoe(h, spec.d, spec.E, spec.k, world, rank, max_tokens=8, device=dev, row_f16=False)
+        x = torch.from_numpy(synth.make_x(8, spec.d, 42 + rank)).to(dev)
+        p.forward(x)
+        torch.cuda.synchronize()
+        st1 = p.status()
+        dist.barrier()
+        refused = None
+        if rank == 0:
+            import time
+            t0 = time.time()
+            p.forward(x)  # rank 1 does not step: this rank's waits give up
+            torch.cuda.synchronize()
+            waited = time.time() - t0
+            st2 = p.status()
+            st_layer = h.status()
+            try:
+                p.forward(x)
+            except RuntimeError as e:
+                refused = str(e)
+        else:
+            waited, st2, st_layer = 0.0, p.status(), h.status()
+        dist.barrier()
+        p.close()
+        res = (st1, st2, st_layer, refused, waited)
+        outs = [None] * world
+        dist.all_gather_object(outs, res)
+        if rank == 0:
+            q.put(("ok", outs))
+        h.close()
+        dist.destroy_process_group()
+    except Exception as e:
+        import traceback
+
+        q.put(("err", f"rank {rank}: {e}\n{traceback.format_exc()}"))
+
+
+def test_ep_peer_wait_gives_up_when_a_rank_skips_a_step():
+    import torch
+    import torch.multiprocessing as mp
+
+    nc.require_gpu()
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_peer_skip_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    msg = q.get(timeout=300)
+    for p in procs:
+        p.join(timeout=120)
+        if p.is_alive():
+            p.kill()
+    assert msg[0] == "ok", msg[1]
+    (a1, a2, a_layer, a_refused, a_wait), (b1, b2, b_layer, _, _) = msg[1]
+    assert a1 == 0 and b1 == 0
+    assert a2 == 21 and a_layer == 21  # rows wait (kEpErrRowsWait)
+    assert a_refused is not None and "code 21" in a_refused
+    assert a_wait < 5.0  # the 50 ms limit, not the 5 s default
+    assert b2 == 0 and b_layer == 0

@@ -185,7 +185,18 @@ def _config_check(key, T, seed=0, tol=DECODE_TOL, calls=1):
 
 
 def test_config1_decode_q8_0():
-    _config_check("c1", T=1, calls=4)
+    """All 64 tokens of config 1, one call each."""
+    _config_check("c1", T=1, calls=64)
+
+
+def test_config4_moe_layer_batch1():
+    """Config 4's MoE layer (Q4_K, 128 experts top-8, F=768) at decode batch 1: 64 calls."""
+    _config_check("c4b1", T=1, calls=64)
+
+
+def test_config4_moe_layer_batch16():
+    """Config 4's MoE layer at decode batch 16: 4 calls of 16 tokens."""
+    _config_check("c4b16", T=16, calls=4)
 
 
 def test_config3_decode_q4_k_shared():

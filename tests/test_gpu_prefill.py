@@ -87,6 +87,61 @@ def test_config5_subset(key):
     assert rel_err(out[sel], ref) <= PREFILL_TOL
     # router on the device gives the same logits, so the same result
     assert np.array_equal(out, out2)
+    assert L_status_ok(wl, layer)
+
+
+def L_status_ok(wl, layer) -> bool:
+    """A fresh handle reports no expired device wait after a full call."""
+    L = synth.open_layer(layer)
+    try:
+        L.forward(synth.make_x(256, wl.spec.d, 9))
+        return L.status() == 0
+    finally:
+        L.close()
+
+
+def routing_flips(idx_dev, lg_dev, lg_ref, k):
+    """Tokens whose device top-k (indices in order) differs from the reference's top-k on
+    its own logits, each with its smallest adjacent gap among the reference's k + 1
+    largest logits, its k-th / (k+1)-th gap, and the row's largest |device - reference|
+    logit difference."""
+    idx_ref, _ = O.route(lg_ref, k)
+    flips = []
+    for t in np.nonzero(~np.all(idx_dev == idx_ref, axis=1))[0]:
+        top = np.sort(lg_ref[t].astype(np.float64))[::-1][:k + 1]
+        flips.append({"token": int(t), "min_gap": float(np.min(top[:-1] - top[1:])),
+                      "kth_gap": float(top[k - 1] - top[k]),
+                      "delta": float(np.max(np.abs(lg_dev[t].astype(np.float64) - lg_ref[t])))})
+    return flips
+
+
+@pytest.mark.parametrize("key", ["c5", "c5z"])
+def test_routing_l2_config5(key):
+    """Routing level 2 at config 5 (8192 tokens, 512 experts top-10): the device router and
+    top-k against the reference's routing of its own f32 logits, h @ W_r^T (+ bias) in numpy
+    (engine/model.py:665-666). A token may differ only at a near-tie: two logits among the
+    k + 1 largest whose gap is within twice the row's largest device-reference logit
+    difference. The count and gaps are printed (pytest -s)."""
+    wl = synth.CONFIGS[key]
+    layer = synth.make_layer(wl.spec, 0, device_gen=True)
+    x = synth.make_x(wl.T, wl.spec.d, 0)
+    if wl.zipf_s:
+        synth.attach_zipf(layer, x, wl.zipf_s, 0)
+    L = synth.open_layer(layer)
+    try:
+        lg_dev = L.router_logits(x)
+    finally:
+        L.close()
+    idx_dev, _ = nc.route(lg_dev, wl.spec.E, wl.spec.k)
+    lg_ref = (x @ layer.router.T + (layer.router_bias if layer.router_bias is not None else 0)).astype(np.float32)
+    flips = routing_flips(idx_dev, lg_dev, lg_ref, wl.spec.k)
+    print(f"\nrouting L2 {key}: {len(flips)} of {wl.T} tokens differ; max logit difference "
+          f"{float(np.max(np.abs(lg_dev.astype(np.float64) - lg_ref))):.3g}; " +
+          "; ".join(f"t{f['token']} min gap {f['min_gap']:.3g} k/k+1 gap {f['kth_gap']:.3g} delta {f['delta']:.3g}"
+                    for f in flips))
+    for f in flips:
+        assert f["min_gap"] <= 2 * f["delta"], f
+    assert len(flips) <= 64  # a near-tie at that bound is rare: about one token in a thousand at most
 
 
 @pytest.mark.parametrize("key,T", [("c5", 1000), ("c2", 300), ("c3", 32), ("c5", 2048)])
@@ -115,7 +170,7 @@ def test_tensor_core_router_f32_accuracy(key, T):
     assert np.array_equal(tc, again)
     assert e_simt < 1e-5
     assert e_tc <= max(4 * e_simt, 1e-6), (e_tc, e_simt)
-    # top-k agrees with the f64 logits' except at near-ties
+    # top-k agrees with the f64 logits' except at near-ties within the logits' difference
     idx_tc, _ = O.route(tc, wl.spec.k)
-    idx_64, _ = O.route(ref64.astype(np.float32), wl.spec.k)
-    assert np.sum(~np.all(idx_tc == idx_64, axis=1)) <= max(1, T // 100)
+    for f in routing_flips(idx_tc, tc, ref64.astype(np.float32), wl.spec.k):
+        assert f["min_gap"] <= 2 * f["delta"] + 1e-7, f

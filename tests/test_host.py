@@ -191,14 +191,15 @@ def test_bf16_inputs_representable():
 
 def test_bench_gemm_roofline_bound():
     """bench.py's prefill roofline takes the larger of the tensor and HBM times as the bound:
-    config 5's gate/up GEMM is tensor-bound, config 2's (512 tokens, 128 experts) HBM-bound."""
+    config 5's gate/up GEMM is tensor-bound, config 2's (512 tokens, 128 experts) HBM-bound.
+    The tensor fraction is against the burst peak (the GEMM runs inside a ~1 ms step)."""
     import bench
     from aero_b200 import synth
 
     pk = {"bf16_tflops": 1641.0, "bf16_tflops_sustained": 1392.6, "hbm_gbs": 6545.0, "source": "measured"}
     for key, stats, st, bound, frac in (
             ("c5", {"last_pairs": 81920, "last_shared_rows": 8192, "last_active": 512},
-             {"gate_up": 0.559, "down": 0.315}, "tensor", 0.4855),
+             {"gate_up": 0.559, "down": 0.315}, "tensor", 0.4120),
             ("c2", {"last_pairs": 4096, "last_shared_rows": 0, "last_active": 126},
              {"gate_up": 0.193, "down": 0.1065}, "hbm", 0.1765)):
         spec = synth.CONFIGS[key].spec
@@ -208,6 +209,33 @@ def test_bench_gemm_roofline_bound():
         assert r["bound"] == bound and r["other_bound"]["bound"] != bound
         assert abs(r["frac"] - frac) < 2e-3, (key, r["frac"])
         assert abs(r["frac"] - r["achieved"] / r["peak"]) < 1e-12
+        tc = r if r["bound"] == "tensor" else r["other_bound"]
+        assert tc["peak"] == pk["bf16_tflops"]
+        assert abs(tc["frac_of_sustained"] - tc["achieved"] / pk["bf16_tflops_sustained"]) < 1e-12
+
+
+def test_bench_decode_bytes_and_config():
+    """Decode HBM bytes count each call's distinct experts once, plus router, shared expert and
+    activations; both bench arms print the same config record."""
+    import bench
+    from aero_b200 import synth
+
+    spec = synth.LayerSpec(64, 8, 2, 32, 32, synth.DTYPE_Q4_K)
+    router = np.eye(8, 64, dtype=np.float32)
+    x = np.zeros((4, 64), np.float32)
+    x[0, 0] = x[1, 0] = 5.0  # calls of 2 tokens: both tokens pick expert 0 (+ a tie-broken partner)
+    x[2, 3], x[3, 4] = 5.0, 5.0
+    per_expert, shared = bench.layer_bytes(spec)
+    got = bench.decode_bytes(spec, x, router, None, 2, 2)
+    lg = x @ router.T
+    want = 0
+    for c in range(2):
+        sel = np.argpartition(-lg[2 * c:2 * c + 2], 1, axis=1)[:, :2]
+        want += len(np.unique(sel)) * per_expert + shared + 9 * 64 * 4 + 2 * 2 * 64 * 4
+    assert got == want
+    wl = synth.CONFIGS["c5"]
+    assert bench.config_dict(wl, 1) == bench.config_dict(wl, 1) and bench.config_dict(wl, 8)["parallelism"] == "ep8"
+    assert bench.config_dict(wl, 1)["tokens_per_step"] == 8192
 
 
 def test_bench_clock_window():
