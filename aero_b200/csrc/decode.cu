@@ -1,0 +1,652 @@
+// Decode (calls of up to 32 tokens): the whole MoE layer in one cooperative
+// launch, four phases separated by two grid barriers.
+//
+//   A  router logits (f32, x . W_r + bias, plus the shared-gate column) and the
+//      call's x rows coded as integer input                       | barrier 1
+//   B  in every CTA, from the logits: top-k per token (src/moe.cpp:26-66, the
+//      same selection as the top-k kernel) and the dispatch of the T*k pairs
+//      into expert segments (counting sort, stable in (token, slot) order),
+//      kept in shared memory
+//   C  gate/up GEMVs over the active experts (and the shared expert): act =
+//      silu(gate . x) * (up . x), coded as integer input for the down product
+//                                                                   | barrier 2
+//   D  down GEMVs, each CTA owning a block of output rows for every active
+//      expert, then the combine of those rows: out[t] = sum over slots in order
+//      of w * y + sgate * y_shared (src/moe.cpp:68-120)
+//
+// GEMV lanes. A lane owns 64 consecutive values of a row: for Q4_K the 32 code
+// bytes of sub-blocks 2g and 2g+1 of one super-block plus that super-block's
+// 16-byte header (one header load and one scale decode per row and lane);
+// for Q8_0 two whole 32-value blocks and their two fp16 scales. Rows of K
+// values take K/64 lanes (groups of 1 to 32 lanes; a warp computes 32/group
+// rows at a time). Only the selected experts' blocks are read, each once per
+// call; accumulation is f32.
+//
+// Integer input (x and act rows), per 16 values: a 15-bit code split into two
+// int8 planes (v ~= sx * (128 q1 + q0), |128 q1 + q0| <= 16383) and the exact f32
+// sum of the 16 values (the Q4_K min term). A lane's 64 values are then four
+// blocks: sum(q x) is two chains of dp4a over the raw code bytes per block, and
+// the per-sub-block factorisation of the quantised dot (src/kernels.cpp:78-84,
+// 123-156) applies the scales once per block:
+//   Q8_0: d * sum(q x)          Q4_K: d sc * sum(q x) - dmin m * sum(x)
+// The input coding error is at most 2^-15 of each 16-value block's largest |v|.
+//
+// Every grid-barrier wait is bounded (%globaltimer): a CTA that gives up
+// records an error code (device word and the handle's host-mapped word) and
+// returns; the host reports it at its next synchronisation or call.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cub/block/block_scan.cuh>
+
+#include "internal.h"
+#include "topk.cuh"
+
+namespace aero {
+namespace {
+
+constexpr int kDecThreads = 384;
+constexpr int kDecWarps = kDecThreads / 32;
+constexpr int kScanItems = (1024 + kDecThreads) / kDecThreads;  // items per thread: E + 1 <= 1025 values
+constexpr int kRouterTokGroup = 4;  // tokens per router warp task
+constexpr int kJBlock = 16;         // act rows per gate/up warp task (one coding block)
+constexpr int kErrBarrier = 31;
+
+__device__ __forceinline__ uint64_t dec_gtimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid barrier b of this launch: every CTA adds one to the counter, which only
+// grows (launch seq's barrier b completes at (seq * 2 + b + 1) * gridDim.x,
+// modulo 2^32). False when the wait ran out (the error is recorded).
+__device__ bool grid_barrier(const DecodeArgs& a, int b, volatile int* abort_s) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t target = (a.seq * 2u + (uint32_t)b + 1u) * gridDim.x;
+        __threadfence();
+        atomicAdd(a.bar, 1u);
+        const uint64_t t0 = dec_gtimer();
+        while ((int32_t)(ld_acquire_gpu(a.bar) - target) < 0) {
+            if (dec_gtimer() - t0 > a.wait_ns) {
+                if (atomicCAS(a.err, 0, kErrBarrier) == 0 && a.err_host) {
+                    *reinterpret_cast<volatile int32_t*>(a.err_host) = kErrBarrier;
+                    __threadfence_system();
+                }
+                *abort_s = 1;
+                break;
+            }
+            __nanosleep(32);
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    return *abort_s == 0;
+}
+
+// ------------------------------------------------------------ integer input
+// Row of K values: q1 [K] int8, q0 [K] int8, then (sx, s16) per 16 values.
+__host__ __device__ inline int64_t qx_row_bytes(int K) { return (int64_t)K * 2 + (int64_t)K / 2; }
+
+// Codes the 16 values v[0..16) into the row at column c (a multiple of 16).
+__device__ __forceinline__ void qx_code16(const float* v, uint8_t* row, int K, int c) {
+    float mx = 0.f, s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        mx = fmaxf(mx, fabsf(v[i]));
+        s += v[i];
+    }
+    const float inv = mx > 0.f ? 16383.0f / mx : 0.f;
+    uint32_t w1[4], w0[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        uint32_t p1 = 0, p0 = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int q = __float2int_rn(v[4 * i + j] * inv);  // |q| <= 16383
+            p1 |= (uint32_t)(q >> 7 & 0xFF) << (8 * j);
+            p0 |= (uint32_t)(q & 127) << (8 * j);
+        }
+        w1[i] = p1;
+        w0[i] = p0;
+    }
+    *reinterpret_cast<uint4*>(row + c) = make_uint4(w1[0], w1[1], w1[2], w1[3]);
+    *reinterpret_cast<uint4*>(row + K + c) = make_uint4(w0[0], w0[1], w0[2], w0[3]);
+    *reinterpret_cast<float2*>(row + 2 * K + (c / 16) * 8) = make_float2(mx / 16383.0f, s);
+}
+
+// A lane's 64 values of one input row: both code planes and the four blocks' (sx, s16).
+struct XSlice {
+    uint32_t h[16], l[16];
+    float sx[4], s16[4];
+};
+
+__device__ __forceinline__ void xs_load(const uint8_t* row, int K, int gl, XSlice& s) {
+    const uint4* ph = reinterpret_cast<const uint4*>(row + 64 * gl);
+    const uint4* pl = reinterpret_cast<const uint4*>(row + K + 64 * gl);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        const uint4 a = ph[i], b = pl[i];
+        s.h[4 * i] = a.x, s.h[4 * i + 1] = a.y, s.h[4 * i + 2] = a.z, s.h[4 * i + 3] = a.w;
+        s.l[4 * i] = b.x, s.l[4 * i + 1] = b.y, s.l[4 * i + 2] = b.z, s.l[4 * i + 3] = b.w;
+    }
+    const float4* ps = reinterpret_cast<const float4*>(row + 2 * K + 32 * gl);
+    const float4 s0 = ps[0], s1 = ps[1];
+    s.sx[0] = s0.x, s.s16[0] = s0.y, s.sx[1] = s0.z, s.s16[1] = s0.w;
+    s.sx[2] = s1.x, s.s16[2] = s1.y, s.sx[3] = s1.z, s.s16[3] = s1.w;
+}
+
+// ------------------------------------------------------------ weight slices
+template <int DT>
+struct WSlice;
+template <>
+struct WSlice<AERO_DT_Q4_K> {
+    uint4 a, b, hdr;  // 32 code bytes, the super-block header
+};
+template <>
+struct WSlice<AERO_DT_Q8_0> {
+    uint4 q[4];
+    uint32_t sc;  // the two blocks' fp16 scales
+};
+
+__device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+
+template <int DT>
+__device__ __forceinline__ void ws_load(const QMat& M, int e, int r, int gl, WSlice<DT>& w) {
+    const uint8_t* qs = qm_row_qs(M, e, r);
+    const uint8_t* mt = qm_row_meta(M, e, r);
+    if constexpr (DT == AERO_DT_Q4_K) {
+        w.a = ldg16(qs + 32 * gl);
+        w.b = ldg16(qs + 32 * gl + 16);
+        w.hdr = ldg16(mt + 16 * (gl >> 2));
+    } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w.q[i] = ldg16(qs + 64 * gl + 16 * i);
+        w.sc = __ldg(reinterpret_cast<const uint32_t*>(mt + 4 * gl));
+    }
+}
+
+// sum over 16 values (4 words of codes) of code * (128 q1 + q0)
+__device__ __forceinline__ int dot16(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, const uint32_t* h,
+                                     const uint32_t* l) {
+    int a = __dp4a((int)w0, (int)h[0], 0), b = __dp4a((int)w0, (int)l[0], 0);
+    a = __dp4a((int)w1, (int)h[1], a), b = __dp4a((int)w1, (int)l[1], b);
+    a = __dp4a((int)w2, (int)h[2], a), b = __dp4a((int)w2, (int)l[2], b);
+    a = __dp4a((int)w3, (int)h[3], a), b = __dp4a((int)w3, (int)l[3], b);
+    return a * 128 + b;
+}
+
+// acc[t] += this lane's part of row . input t, for t < nt.
+template <int DT, int NTP>
+__device__ __forceinline__ void ws_dot(const WSlice<DT>& w, int gl, const XSlice (&xs)[NTP], int nt,
+                                       float (&acc)[NTP]) {
+    if constexpr (DT == AERO_DT_Q4_K) {
+        const uint32_t q[8] = {w.a.x, w.a.y, w.a.z, w.a.w, w.b.x, w.b.y, w.b.z, w.b.w};
+        uint32_t lo[8], hi[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            lo[i] = q[i] & 0x0F0F0F0Fu;
+            hi[i] = (q[i] >> 4) & 0x0F0F0F0Fu;
+        }
+        const float d = __half2float(__ushort_as_half((unsigned short)(w.hdr.x & 0xFFFFu)));
+        const float dmin = __half2float(__ushort_as_half((unsigned short)(w.hdr.x >> 16)));
+        const int g = gl & 3;
+        int sc0, m0, sc1, m1;
+        q4k_sc_m_words(w.hdr.y, w.hdr.z, w.hdr.w, 2 * g, sc0, m0);
+        q4k_sc_m_words(w.hdr.y, w.hdr.z, w.hdr.w, 2 * g + 1, sc1, m1);
+        const float a0 = d * (float)sc0, b0 = dmin * (float)m0, a1 = d * (float)sc1, b1 = dmin * (float)m1;
+#pragma unroll
+        for (int t = 0; t < NTP; ++t) {
+            if (t < nt) {
+                const XSlice& x = xs[t];
+                // low nibbles: sub-block 2g (values 0-31 = blocks 0, 1); high: 2g+1 (blocks 2, 3)
+                const int s0 = dot16(lo[0], lo[1], lo[2], lo[3], x.h, x.l);
+                const int s1 = dot16(lo[4], lo[5], lo[6], lo[7], x.h + 4, x.l + 4);
+                const int s2 = dot16(hi[0], hi[1], hi[2], hi[3], x.h + 8, x.l + 8);
+                const int s3 = dot16(hi[4], hi[5], hi[6], hi[7], x.h + 12, x.l + 12);
+                const float p0 = fmaf(x.sx[0], (float)s0, x.sx[1] * (float)s1);
+                const float p1 = fmaf(x.sx[2], (float)s2, x.sx[3] * (float)s3);
+                acc[t] += (a0 * p0 - b0 * (x.s16[0] + x.s16[1])) + (a1 * p1 - b1 * (x.s16[2] + x.s16[3]));
+            }
+        }
+    } else {
+        const float d0 = __half2float(__ushort_as_half((unsigned short)(w.sc & 0xFFFFu)));
+        const float d1 = __half2float(__ushort_as_half((unsigned short)(w.sc >> 16)));
+#pragma unroll
+        for (int t = 0; t < NTP; ++t) {
+            if (t < nt) {
+                const XSlice& x = xs[t];
+                const int s0 = dot16(w.q[0].x, w.q[0].y, w.q[0].z, w.q[0].w, x.h, x.l);
+                const int s1 = dot16(w.q[1].x, w.q[1].y, w.q[1].z, w.q[1].w, x.h + 4, x.l + 4);
+                const int s2 = dot16(w.q[2].x, w.q[2].y, w.q[2].z, w.q[2].w, x.h + 8, x.l + 8);
+                const int s3 = dot16(w.q[3].x, w.q[3].y, w.q[3].z, w.q[3].w, x.h + 12, x.l + 12);
+                acc[t] += d0 * fmaf(x.sx[0], (float)s0, x.sx[1] * (float)s1) +
+                          d1 * fmaf(x.sx[2], (float)s2, x.sx[3] * (float)s3);
+            }
+        }
+    }
+}
+
+template <int NTP>
+__device__ __forceinline__ void group_reduce(float (&acc)[NTP], int group) {
+#pragma unroll
+    for (int t = 0; t < NTP; ++t)
+        for (int o = group >> 1; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+}
+
+__host__ __device__ inline int pow2_at_least(int v) {
+    int p = 1;
+    while (p < v) p <<= 1;
+    return p;
+}
+
+// ------------------------------------------------------------ shared state
+// Per-CTA tables of the call's routing (phase B), then the down phase's rows.
+struct DecShared {
+    int32_t* cnt;     // [E] pairs per expert, then the scatter's cursor
+    int32_t* off;     // [E + 1] expert offsets
+    int32_t* idx;     // [P] selected expert of pair p = t * k + s
+    float* w;         // [P]
+    int32_t* perm;    // [P] sorted position -> pair
+    int32_t* inv;     // [P] pair -> sorted position
+    float* sgate;     // [T]
+    int32_t* u_e;     // [U] unit expert (-1: the shared expert)
+    int32_t* u_pos;   // [U] first sorted position (shared: P)
+    int32_t* u_n;     // [U] pairs (shared: T)
+    int32_t* gu_pre;  // [U + 1] gate/up task prefix
+    int32_t* dn_pre;  // [U + 1] down task prefix (this CTA)
+    float* act;       // [warps][kJBlock][NTP] gate/up act staging
+    float* y;         // [(P + T) * rows_per_cta] down outputs of this CTA's rows
+};
+
+// Exclusive scan of v[0..n) in place (n <= kScanItems * blockDim.x); returns the total.
+template <typename Scan>
+__device__ int block_excl_scan(int32_t* v, int n, typename Scan::TempStorage& tmp) {
+    int in[kScanItems], out[kScanItems], tot;
+#pragma unroll
+    for (int j = 0; j < kScanItems; ++j) {
+        const int i = kScanItems * threadIdx.x + j;
+        in[j] = i < n ? v[i] : 0;
+    }
+    Scan(tmp).ExclusiveSum(in, out, tot);
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < kScanItems; ++j) {
+        const int i = kScanItems * threadIdx.x + j;
+        if (i < n) v[i] = out[j];
+    }
+    __syncthreads();
+    return tot;
+}
+
+template <int DT, int NTP, int PER>
+__global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(DecodeArgs a) {
+    extern __shared__ __align__(16) uint8_t dsm[];
+    using Scan = cub::BlockScan<int, kDecThreads>;
+    __shared__ typename Scan::TempStorage scan_tmp;
+    __shared__ int abort_s, n_units_s;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int T = a.T, E = a.E, k = a.k, P = T * k;
+    const int Tsh = a.has_shared ? T : 0;
+    if (threadIdx.x == 0) abort_s = 0;
+
+    // ---------------------------------------------------------------- phase A
+    {
+        const int n_rows = a.logits_in ? (a.has_shared ? 1 : 0) : E + (a.has_shared ? 1 : 0);
+        const int row0 = a.logits_in ? E : 0;
+        const int n_tg = (T + kRouterTokGroup - 1) / kRouterTokGroup;
+        const int n_tasks = n_rows * n_tg;
+        const int n_warps = gridDim.x * kDecWarps;
+        const int nf4 = a.dp / 128;  // float4 per lane (dp <= 2048: at most 16)
+        for (int task = blockIdx.x * kDecWarps + warp; task < n_tasks; task += n_warps) {
+            const int tg = task / n_rows, r = row0 + task % n_rows;
+            const float* wr = a.router + (int64_t)r * a.dp;
+            float4 wv[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+                if (i < nf4) wv[i] = __ldg(reinterpret_cast<const float4*>(wr) + lane + 32 * i);
+            for (int t = tg * kRouterTokGroup; t < min(T, (tg + 1) * kRouterTokGroup); ++t) {
+                const float4* xr = reinterpret_cast<const float4*>(a.x + (int64_t)t * a.dp);
+                float acc = 0.f;
+#pragma unroll
+                for (int i = 0; i < 16; ++i)
+                    if (i < nf4) {
+                        const float4 xv = __ldg(xr + lane + 32 * i);
+                        acc = fmaf(wv[i].x, xv.x, acc);
+                        acc = fmaf(wv[i].y, xv.y, acc);
+                        acc = fmaf(wv[i].z, xv.z, acc);
+                        acc = fmaf(wv[i].w, xv.w, acc);
+                    }
+                acc = warp_sum(acc);
+                if (lane == 0) a.logits[(int64_t)t * a.lg_ld + r] = acc + (r < E && a.bias ? a.bias[r] : 0.f);
+            }
+        }
+        // the call's x rows as integer input (one thread per 16 values)
+        const int nb = a.dp / 16;
+        for (int i = blockIdx.x * kDecThreads + threadIdx.x; i < T * nb; i += gridDim.x * kDecThreads) {
+            const int t = i / nb, c = (i % nb) * 16;
+            float v[16];
+            const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)t * a.dp + c);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float4 f = __ldg(src + j);
+                v[4 * j] = f.x, v[4 * j + 1] = f.y, v[4 * j + 2] = f.z, v[4 * j + 3] = f.w;
+            }
+            qx_code16(v, a.xq + (int64_t)t * qx_row_bytes(a.dp), a.dp, c);
+        }
+    }
+    if (!grid_barrier(a, 0, &abort_s)) return;
+
+    // ---------------------------------------------------------------- phase B
+    DecShared S;
+    {
+        uint8_t* p = dsm;
+        auto take = [&](size_t bytes) {
+            uint8_t* q = p;
+            p += (bytes + 15) & ~(size_t)15;
+            return q;
+        };
+        const int Umax = min(P, E) + 1;
+        S.cnt = (int32_t*)take((size_t)E * 4);
+        S.off = (int32_t*)take((size_t)(E + 1) * 4);
+        S.idx = (int32_t*)take((size_t)P * 4);
+        S.w = (float*)take((size_t)P * 4);
+        S.perm = (int32_t*)take((size_t)P * 4);
+        S.inv = (int32_t*)take((size_t)P * 4);
+        S.sgate = (float*)take((size_t)T * 4);
+        S.u_e = (int32_t*)take((size_t)Umax * 4);
+        S.u_pos = (int32_t*)take((size_t)Umax * 4);
+        S.u_n = (int32_t*)take((size_t)Umax * 4);
+        S.gu_pre = (int32_t*)take((size_t)(Umax + 1) * 4);
+        S.dn_pre = (int32_t*)take((size_t)(Umax + 1) * 4);
+        S.act = (float*)take((size_t)kDecWarps * kJBlock * NTP * 4);
+        S.y = (float*)take((size_t)(P + Tsh) * a.rows_per_cta * 4);
+    }
+    const float* lg_base = a.logits_in ? a.logits_in : a.logits;
+    const int lg_ld = a.logits_in ? a.ld_in : a.lg_ld;
+    for (int t = warp; t < T; t += kDecWarps) {
+        int sel_i = 0;
+        topk_warp<PER>(lg_base + (int64_t)t * lg_ld, E, k, a.norm, S.idx + t * k, S.w + t * k, &sel_i);
+        if (lane == 0 && a.has_shared) S.sgate[t] = sigmoid_f(a.logits[(int64_t)t * a.lg_ld + E]);
+    }
+    for (int e = threadIdx.x; e < E; e += kDecThreads) S.cnt[e] = 0;
+    __syncthreads();
+    for (int p = threadIdx.x; p < P; p += kDecThreads) atomicAdd(&S.cnt[S.idx[p]], 1);
+    __syncthreads();
+    // expert offsets (exclusive prefix of the counts)
+    for (int e = threadIdx.x; e < E; e += kDecThreads) S.off[e] = S.cnt[e];
+    __syncthreads();
+    block_excl_scan<Scan>(S.off, E, scan_tmp);
+    if (threadIdx.x == 0) S.off[E] = P;
+    // the active units: experts in ascending order, then the shared expert
+    {
+        int in[kScanItems], out[kScanItems], tot;
+#pragma unroll
+        for (int j = 0; j < kScanItems; ++j) {
+            const int e = kScanItems * threadIdx.x + j;
+            in[j] = e < E && S.cnt[e] > 0 ? 1 : 0;
+        }
+        Scan(scan_tmp).ExclusiveSum(in, out, tot);
+#pragma unroll
+        for (int j = 0; j < kScanItems; ++j) {
+            const int e = kScanItems * threadIdx.x + j;
+            if (in[j]) {
+                S.u_e[out[j]] = e;
+                S.u_pos[out[j]] = S.off[e];
+                S.u_n[out[j]] = S.cnt[e];
+            }
+        }
+        if (threadIdx.x == 0) {
+            int U = tot;
+            if (a.has_shared) {
+                S.u_e[U] = -1;
+                S.u_pos[U] = P;
+                S.u_n[U] = T;
+                ++U;
+            }
+            n_units_s = U;
+        }
+    }
+    __syncthreads();
+    // stable scatter (warp 0): pairs in order, equal experts ranked by __match_any_sync
+    for (int e = threadIdx.x; e < E; e += kDecThreads) S.cnt[e] = S.off[e];  // cursor
+    __syncthreads();
+    if (warp == 0) {
+        for (int base = 0; base < P; base += 32) {
+            const int p = base + lane;
+            const bool valid = p < P;
+            const int e = valid ? S.idx[p] : -1 - lane;
+            const unsigned peers = __match_any_sync(0xffffffffu, e);
+            const int rank = __popc(peers & ((1u << lane) - 1u));
+            const int pos = valid ? S.cnt[e] + rank : 0;
+            __syncwarp();
+            if (valid) {
+                S.perm[pos] = p;
+                S.inv[p] = pos;
+                if ((peers >> lane) == 1u) S.cnt[e] = pos + 1;
+            }
+            __syncwarp();
+        }
+    }
+    __syncthreads();
+    const int U = n_units_s;
+    // task counts per unit: gate/up (unit, 16-row block, token group) and this CTA's
+    // down tasks (unit, token group: a task streams the CTA's rows)
+    const int rows_lo = blockIdx.x * a.rows_per_cta, rows_hi = min(a.dp, rows_lo + a.rows_per_cta);
+    const int n_rows_d = max(0, rows_hi - rows_lo);
+    for (int u = threadIdx.x; u < U; u += kDecThreads) {
+        const bool sh = S.u_e[u] < 0;
+        const int F = sh ? a.Fs : a.F;
+        const int ng = (S.u_n[u] + NTP - 1) / NTP;
+        S.gu_pre[u] = (F / kJBlock) * ng;
+        S.dn_pre[u] = n_rows_d > 0 ? ng : 0;
+    }
+    __syncthreads();
+    const int n_gu = block_excl_scan<Scan>(S.gu_pre, U, scan_tmp);
+    const int n_dn = block_excl_scan<Scan>(S.dn_pre, U, scan_tmp);
+    if (threadIdx.x == 0) {
+        S.gu_pre[U] = n_gu;
+        S.dn_pre[U] = n_dn;
+    }
+    if (blockIdx.x == 0) {
+        // the call's routing for the host (stats, profiling)
+        for (int p = threadIdx.x; p < P; p += kDecThreads) {
+            a.idx_out[p] = S.idx[p];
+            a.w_out[p] = S.w[p];
+        }
+        if (threadIdx.x == 0) {
+            *a.n_active_out = U - (a.has_shared ? 1 : 0);
+            *a.p_real_out = P;
+        }
+    }
+    __syncthreads();
+
+    auto find_unit = [&](const int32_t* pre, int task) {
+        int lo = 0, hi = U - 1;  // the last u with pre[u] <= task
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (pre[mid] <= task)
+                lo = mid;
+            else
+                hi = mid - 1;
+        }
+        return lo;
+    };
+
+    // ---------------------------------------------------------------- phase C
+    {
+        const int K = a.dp;
+        const int group = pow2_at_least(K / 64);
+        const int rpw = 32 / group;
+        const int gl = lane & (group - 1), sub = lane / group;
+        const bool lane_on = gl < K / 64;
+        float* act_w = S.act + warp * kJBlock * NTP;
+        const int n_warps = gridDim.x * kDecWarps;
+        for (int task = warp * gridDim.x + blockIdx.x; task < n_gu; task += n_warps) {
+            const int u = find_unit(S.gu_pre, task);
+            const int rel = task - S.gu_pre[u];
+            const bool sh = S.u_e[u] < 0;
+            const int F = sh ? a.Fs : a.F;
+            const int nblk = F / kJBlock;
+            const int tg = rel / nblk, jb = rel % nblk;
+            const int nt = min(NTP, S.u_n[u] - tg * NTP);
+            const QMat& G = sh ? a.sg : a.gate;
+            const QMat& Up = sh ? a.su : a.up;
+            const int e = sh ? 0 : S.u_e[u];
+            XSlice xs[NTP];
+            int arow[NTP];
+#pragma unroll
+            for (int i = 0; i < NTP; ++i) {
+                const int j = tg * NTP + min(i, nt - 1);
+                const int tok = sh ? j : S.perm[S.u_pos[u] + j] / k;
+                arow[i] = S.u_pos[u] + j;  // sorted position (shared: P + token)
+                if (lane_on) xs_load(a.xq + (int64_t)tok * qx_row_bytes(K), K, gl, xs[i]);
+            }
+            // row passes: rows jb * 16 + p * rpw + sub, gate then up, the next item's weights in flight
+            const int n_pass = (kJBlock + rpw - 1) / rpw;
+            const int n_items = 2 * n_pass;
+            auto item_row = [&](int it) { return jb * kJBlock + (it >> 1) * rpw + sub; };
+            auto item_ok = [&](int it) { return lane_on && (it >> 1) * rpw + sub < kJBlock; };
+            WSlice<DT> cur, nxt;
+            if (item_ok(0)) ws_load<DT>(G, e, item_row(0), gl, cur);
+            float g[NTP];
+            for (int it = 0; it < n_items; ++it) {
+                if (it + 1 < n_items && item_ok(it + 1)) ws_load<DT>((it + 1) & 1 ? Up : G, e, item_row(it + 1), gl, nxt);
+                float acc[NTP];
+#pragma unroll
+                for (int i = 0; i < NTP; ++i) acc[i] = 0.f;
+                if (item_ok(it)) ws_dot<DT, NTP>(cur, gl, xs, nt, acc);
+                group_reduce<NTP>(acc, group);
+                if (it & 1) {
+                    const int jj = (it >> 1) * rpw + sub;
+                    if (gl == 0 && jj < kJBlock) {
+#pragma unroll
+                        for (int i = 0; i < NTP; ++i) act_w[jj * NTP + i] = silu_f(g[i]) * acc[i];
+                    }
+                } else {
+#pragma unroll
+                    for (int i = 0; i < NTP; ++i) g[i] = acc[i];
+                }
+                cur = nxt;
+            }
+            __syncwarp();
+            if (lane < nt) {
+                float v[kJBlock];
+#pragma unroll
+                for (int jj = 0; jj < kJBlock; ++jj) v[jj] = act_w[jj * NTP + lane];
+                qx_code16(v, a.aq + (int64_t)arow[lane] * qx_row_bytes(a.act_ld), a.act_ld, jb * kJBlock);
+            }
+            __syncwarp();
+        }
+    }
+    if (!grid_barrier(a, 1, &abort_s)) return;
+
+    // ---------------------------------------------------------------- phase D
+    for (int task = warp; task < n_dn; task += kDecWarps) {
+        const int u = find_unit(S.dn_pre, task);
+        const int tg = task - S.dn_pre[u];
+        const bool sh = S.u_e[u] < 0;
+        const int K = sh ? a.Fs : a.F;
+        const int group = pow2_at_least(K / 64);
+        const int rpw = 32 / group;
+        const int gl = lane & (group - 1), sub = lane / group;
+        const bool lane_on = gl < K / 64;
+        const int nrg = (n_rows_d + rpw - 1) / rpw;
+        const int nt = min(NTP, S.u_n[u] - tg * NTP);
+        const QMat& D = sh ? a.sd : a.down;
+        const int e = sh ? 0 : S.u_e[u];
+        XSlice xs[NTP];
+        int arow[NTP];
+#pragma unroll
+        for (int i = 0; i < NTP; ++i) {
+            arow[i] = S.u_pos[u] + tg * NTP + min(i, nt - 1);
+            if (lane_on) xs_load(a.aq + (int64_t)arow[i] * qx_row_bytes(a.act_ld), a.act_ld, gl, xs[i]);
+        }
+        // the CTA's rows, rpw at a time, the next rows' weights in flight
+        auto row_ok = [&](int rg) { return lane_on && rows_lo + rg * rpw + sub < rows_hi; };
+        WSlice<DT> cur, nxt;
+        if (row_ok(0)) ws_load<DT>(D, e, rows_lo + sub, gl, cur);
+        for (int rg = 0; rg < nrg; ++rg) {
+            if (rg + 1 < nrg && row_ok(rg + 1)) ws_load<DT>(D, e, rows_lo + (rg + 1) * rpw + sub, gl, nxt);
+            float acc[NTP];
+#pragma unroll
+            for (int i = 0; i < NTP; ++i) acc[i] = 0.f;
+            if (row_ok(rg)) ws_dot<DT, NTP>(cur, gl, xs, nt, acc);
+            group_reduce<NTP>(acc, group);
+            const int nn = rg * rpw + sub;
+            if (row_ok(rg) && gl == 0) {
+#pragma unroll
+                for (int i = 0; i < NTP; ++i)
+                    if (i < nt) S.y[(int64_t)arow[i] * a.rows_per_cta + nn] = acc[i];
+            }
+            cur = nxt;
+        }
+    }
+    __syncthreads();
+    // combine: out[t][n] = sum_s w[t][s] * y[(t, s)][n] (slot order) + sgate[t] * y_shared[t][n]
+    for (int i = threadIdx.x; i < T * n_rows_d; i += kDecThreads) {
+        const int t = i / n_rows_d, nn = i % n_rows_d;
+        float o = 0.f;
+        for (int s = 0; s < k; ++s) o += S.w[t * k + s] * S.y[(int64_t)S.inv[t * k + s] * a.rows_per_cta + nn];
+        if (a.has_shared) o += S.sgate[t] * S.y[(int64_t)(P + t) * a.rows_per_cta + nn];
+        a.out[(int64_t)t * a.dp + rows_lo + nn] = o;
+    }
+}
+
+template <int DT, int NTP>
+const void* decode_kernel_for(int E) {
+    if (E <= 128) return (const void*)decode_kernel<DT, NTP, 4>;
+    if (E <= 256) return (const void*)decode_kernel<DT, NTP, 8>;
+    if (E <= 512) return (const void*)decode_kernel<DT, NTP, 16>;
+    return (const void*)decode_kernel<DT, NTP, 32>;
+}
+
+size_t decode_smem_bytes(int T, int E, int k, int has_shared, int rows_per_cta, int ntp) {
+    const int P = T * k, Umax = std::min(P, E) + 1;
+    auto al = [](size_t b) { return (b + 15) & ~(size_t)15; };
+    return al((size_t)E * 4) + al((size_t)(E + 1) * 4) + 4 * al((size_t)P * 4) + al((size_t)T * 4) +
+           3 * al((size_t)Umax * 4) + 2 * al((size_t)(Umax + 1) * 4) + al((size_t)kDecWarps * kJBlock * ntp * 4) +
+           al((size_t)(P + (has_shared ? T : 0)) * rows_per_cta * 4);
+}
+
+}  // namespace
+
+int64_t decode_qx_row_bytes(int K) { return qx_row_bytes(K); }
+
+bool decode_supported(int dtype, int T, int E, int k, int dp, int F, int Fs, int has_shared) {
+    if (dtype != AERO_DT_Q4_K && dtype != AERO_DT_Q8_0) return false;
+    if (T < 1 || T > kDecodeMaxTokens || k < 1 || k > 32 || E < k || E > 1024) return false;
+    if (std::min(T * k, E) + (has_shared ? 1 : 0) > kScanItems * kDecThreads) return false;
+    if (dp % 128 || dp > 2048 || F % 64 || F > 2048 || F < 64) return false;
+    if (has_shared && (Fs % 64 || Fs > 2048 || Fs < 64)) return false;
+    return true;
+}
+
+cudaError_t launch_decode(const DecodeArgs& args, int n_sm, cudaStream_t s) {
+    DecodeArgs a = args;
+    const int ntp = a.T == 1 ? 1 : 2;
+    const void* fn = nullptr;
+    if (a.gate.dtype == AERO_DT_Q4_K)
+        fn = ntp == 1 ? decode_kernel_for<AERO_DT_Q4_K, 1>(a.E) : decode_kernel_for<AERO_DT_Q4_K, 2>(a.E);
+    else
+        fn = ntp == 1 ? decode_kernel_for<AERO_DT_Q8_0, 1>(a.E) : decode_kernel_for<AERO_DT_Q8_0, 2>(a.E);
+    const int grid = n_sm;  // one CTA per SM (checked below against the occupancy)
+    a.rows_per_cta = (a.dp + grid - 1) / grid;
+    const size_t smem = decode_smem_bytes(a.T, a.E, a.k, a.has_shared, a.rows_per_cta, ntp);
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    int per_sm = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kDecThreads, smem);
+    if (e != cudaSuccess) return e;
+    if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+    void* params[] = {&a};
+    return cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kDecThreads), params, smem, s);
+}
+
+}  // namespace aero

@@ -100,6 +100,39 @@ cudaError_t launch_combine(const float* y, const int32_t* inv, const float* w, c
                            const int32_t* idx, int E_real, int T, int Tsh, int k, int d, int has_shared,
                            float* out, cudaStream_t s);
 
+// Decode (decode.cu): the whole layer of a call of up to kDecodeMaxTokens tokens
+// in one cooperative launch (router, top-k, dispatch, gate/up, down, combine),
+// for Q8_0 / Q4_K experts.
+constexpr int kDecodeMaxTokens = 32;
+struct DecodeArgs {
+    const float* x;           // (T, dp) f32
+    const float* logits_in;   // caller logits (T, ld_in), or null: the router runs
+    int ld_in;
+    const float* router;      // (E + 1, dp) f32, row E = the shared-gate input
+    const float* bias;        // (E) or null
+    QMat gate, up, down, sg, su, sd;
+    int T, E, k, norm, has_shared, dp, F, Fs;
+    int act_ld;               // row length of the coded act rows (>= max(F, Fs), multiple of 64)
+    float* logits;            // (T, lg_ld) scratch (column E: the shared-gate logit)
+    int lg_ld;
+    uint8_t* xq;              // T coded x rows (decode_qx_row_bytes(dp) each)
+    uint8_t* aq;              // T * k + T coded act rows (decode_qx_row_bytes(act_ld) each)
+    int32_t* idx_out;         // (T * k) selected experts, written for the host
+    float* w_out;             // (T * k)
+    int32_t* n_active_out;    // active experts of the call
+    int32_t* p_real_out;      // T * k
+    float* out;               // (T, dp) f32
+    uint32_t* bar;            // grid-barrier counter (only grows; zero when the handle's scratch is made)
+    uint32_t seq;             // launches made on this counter before this one
+    int32_t* err;
+    int32_t* err_host;
+    uint64_t wait_ns;
+    int rows_per_cta;         // set by launch_decode
+};
+bool decode_supported(int dtype, int T, int E, int k, int dp, int F, int Fs, int has_shared);
+int64_t decode_qx_row_bytes(int K);
+cudaError_t launch_decode(const DecodeArgs& a, int n_sm, cudaStream_t s);
+
 // Expert-parallel exchange (ep.cu). Rank r owns experts [begin[r], begin[r+1]).
 constexpr int kEpMaxRanks = 64;
 struct EpRankTable {

@@ -60,6 +60,10 @@ struct Scratch {
     void* gemm_ws;
     size_t gemm_ws_bytes = 0;
     int gemv_cap = 0;
+    // fused decode path: coded x and act rows, grid-barrier counter and error word
+    uint8_t *dxq = nullptr, *daq = nullptr;
+    uint32_t* dbar = nullptr;
+    int32_t* derr = nullptr;
 };
 
 // Expert-parallel exchange over peer memory: this rank's window (IPC-exported),
@@ -118,6 +122,8 @@ struct Handle {
     // that gave up: the host reads it at the next call without synchronising
     int32_t* err_host = nullptr;
     uint64_t peer_wait_ns = 5000000000ull;  // AERO_CUDA_OPT_PEER_WAIT_MS
+    bool decode_enabled = true;             // AERO_CUDA_OPT_DECODE_FUSED
+    uint32_t dec_seq = 0;                   // fused decode launches on the current barrier counter
     // prefill (tcgen05 grouped GEMM) path
     bool gemm_ok = false;     // layer shape/type supports it
     int gemm_min_tokens = 64; // calls with at least this many tokens use it
@@ -301,6 +307,11 @@ bool ensure_scratch(Handle& h, int T) {
     const size_t o_inv = take((size_t)P * 4), o_ae = take((size_t)h.E * 4), o_ao = take((size_t)(h.E + 1) * 4);
     const size_t o_na = take(4), o_dw = take(dispatch_work_bytes((int)P, h.E + 1));
     const size_t o_bad = take(4), o_tce = take(4);
+    const int dT = std::min(cap, kDecodeMaxTokens);
+    const bool dec = h.dtype != AERO_DT_F32;
+    const size_t o_dxq = take(dec ? (size_t)dT * decode_qx_row_bytes(h.dp) : 0);
+    const size_t o_daq = take(dec ? (size_t)(dT * h.k + dT) * decode_qx_row_bytes(h.act_ld) : 0);
+    const size_t o_dbar = take(8);
     // split-K partial logits of the tensor-core router (small batches)
     const int part_rows = h.rtc_ok ? (int)std::min<int64_t>(kRouterPartRows, (int64_t)8 * cap) : 0;
     const size_t o_lgp = take((size_t)part_rows * h.lg_ld * 4);
@@ -339,6 +350,11 @@ bool ensure_scratch(Handle& h, int T) {
     s.n_active = (int32_t*)(b + o_na);
     s.ep_bad = (int32_t*)(b + o_bad);
     s.tc_err = (int32_t*)(b + o_tce);
+    s.dxq = dec ? (uint8_t*)(b + o_dxq) : nullptr;
+    s.daq = dec ? (uint8_t*)(b + o_daq) : nullptr;
+    s.dbar = (uint32_t*)(b + o_dbar);
+    s.derr = (int32_t*)(b + o_dbar + 4);
+    h.dec_seq = 0;  // the new scratch is cleared below: the barrier counter starts at zero
     s.lg_part = part_rows ? (float*)(b + o_lgp) : nullptr;
     s.lg_part_rows = part_rows;
     s.dwork = b + o_dw;
@@ -549,8 +565,66 @@ bool finish_profile(Handle& h) {
     return true;
 }
 
+// The fused decode kernel over the call (calls of up to kDecodeMaxTokens tokens).
+bool decode_call(Handle& h, const float* x, int T, const float* logits_in, float* out) {
+    Scratch& s = h.sc;
+    DecodeArgs a{};
+    a.x = x;
+    a.logits_in = logits_in;
+    a.ld_in = h.E;
+    a.router = h.router_ext;
+    a.bias = h.router_bias;
+    a.gate = h.gate;
+    a.up = h.up;
+    a.down = h.down;
+    a.sg = h.sg;
+    a.su = h.su;
+    a.sd = h.sd;
+    a.T = T;
+    a.E = h.E;
+    a.k = h.k;
+    a.norm = h.norm;
+    a.has_shared = h.has_shared;
+    a.dp = h.dp;
+    a.F = h.Fp;
+    a.Fs = h.Fsp;
+    a.act_ld = h.act_ld;
+    a.logits = s.logits;
+    a.lg_ld = h.lg_ld;
+    a.xq = s.dxq;
+    a.aq = s.daq;
+    a.idx_out = s.idx;
+    a.w_out = s.w;
+    a.n_active_out = s.n_active;
+    a.p_real_out = s.offsets + h.E;
+    a.out = out;
+    a.bar = s.dbar;
+    a.seq = h.dec_seq;
+    a.err = s.derr;
+    a.err_host = h.err_host;
+    a.wait_ns = 1000000000ull;  // a grid barrier normally completes in microseconds
+    for (int i = 0; i < 4; ++i) h.mark(i);  // one kernel: its time is reported as the gate/up stage
+    if (!h.cuda_ok(launch_decode(a, h.n_sm, h.stream), "decode layer")) return false;
+    h.dec_seq += 1;
+    h.launches += 1;
+    h.last_gemm = false;
+    h.last_shared_rows = h.has_shared ? T : 0;
+    for (int i = 4; i < 7; ++i) h.mark(i);
+    return true;
+}
+
+bool decode_eligible(const Handle& h, int T, const float* logits_in) {
+    return h.decode_enabled && h.sc.dxq && (logits_in || h.has_router) &&
+           (!h.has_shared || h.sh_dtype == h.dtype) && h.e_begin == 0 && h.e_end == h.E &&
+           decode_supported(h.dtype, T, h.E, h.k, h.dp, h.Fp, h.Fsp, h.has_shared);
+}
+
 // Core pipeline on device buffers: x (T, dp), out (T, dp).
 bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* out) {
+    if (decode_eligible(h, T, logits_in)) {
+        if (!decode_call(h, x, T, logits_in, out)) return false;
+        return finish_profile(h);
+    }
     const bool gemv = !(h.gemm_ok && h.gb_ready && T >= h.gemm_min_tokens);
     if (!route_stage(h, x, T, logits_in, gemv && h.sc.xq.q1 != nullptr)) return false;
     if (!expert_stage(h, x, false, T, T, false, out)) return false;
@@ -561,6 +635,16 @@ bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* 
 // expired; report it (and clear it) at the next synchronisation point.
 bool check_pipeline(Handle& h) {
     if (h.err_host) *reinterpret_cast<volatile int32_t*>(h.err_host) = 0;  // read below from the device flags
+    if (h.sc.base) {
+        int32_t code = 0;
+        if (cudaMemcpy(&code, h.sc.derr, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+            return h.cuda_ok(cudaGetLastError(), "error flag");
+        if (code != 0) {
+            cudaMemset(h.sc.dbar, 0, 8);
+            h.dec_seq = 0;
+            return h.fail("decode grid barrier wait expired (code %d); the call's output is invalid", code);
+        }
+    }
     if (h.sc.base && h.rtc_ok) {
         int32_t code = 0;
         if (cudaMemcpy(&code, h.sc.tc_err, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
@@ -586,7 +670,11 @@ bool take_async_error(Handle& h) {
     const int32_t code = *reinterpret_cast<volatile int32_t*>(h.err_host);
     if (code == 0) return true;
     *reinterpret_cast<volatile int32_t*>(h.err_host) = 0;
-    if (h.sc.base) cudaMemsetAsync(h.sc.tc_err, 0, 4, h.stream);
+    if (h.sc.base) {
+        cudaMemsetAsync(h.sc.tc_err, 0, 4, h.stream);
+        cudaMemsetAsync(h.sc.dbar, 0, 8, h.stream);  // barrier counter and decode error word
+        h.dec_seq = 0;
+    }
     if (h.gb_ready) cudaMemsetAsync(h.gb.err, 0, 4, h.stream);
     return h.fail("a bounded device wait of an earlier call on this handle gave up (code %d): that call's output is "
                   "invalid; this call was not run",
@@ -780,6 +868,8 @@ Handle* open_desc(const aero_cuda_moe_desc* d, std::string* why) {
         if (!gemm_weight_maps(h->gate, h->up, h->down, h->sg, h->su, h->sd, h->e_end - h->e_begin, h->has_shared,
                               &h->wmaps, &why))
             h->gemm_ok = false;  // the layer still runs, on the GEMV path
+    }
+    {
         cudaDeviceProp prop;
         if (cudaGetDeviceProperties(&prop, h->device) == cudaSuccess) h->n_sm = prop.multiProcessorCount;
     }
@@ -1103,6 +1193,11 @@ int aero_cuda_moe_set_option(void* handle, int option, int64_t value) {
         h->rtc_enabled = value != 0;
         return 0;
     }
+    if (option == AERO_CUDA_OPT_DECODE_FUSED) {
+        if (value != 0 && value != 1) return -1;
+        h->decode_enabled = value != 0;
+        return 0;
+    }
     if (option == AERO_CUDA_OPT_PEER_WAIT_MS) {
         if (value < 1 || value > 600000) return h->fail("peer wait limit %lld ms outside [1, 600000]", (long long)value), -1;
         h->peer_wait_ns = (uint64_t)value * 1000000ull;
@@ -1120,7 +1215,8 @@ int aero_cuda_moe_status(void* handle) {
     cudaSetDevice(h->device);
     if (!h->cuda_ok(cudaStreamSynchronize(h->stream), "status")) return -1;
     int32_t code = h->err_host ? *reinterpret_cast<volatile int32_t*>(h->err_host) : 0;
-    int32_t dev[3] = {0, 0, 0};
+    int32_t dev[4] = {0, 0, 0, 0};
+    if (h->sc.base) cudaMemcpy(&dev[3], h->sc.derr, 4, cudaMemcpyDeviceToHost);
     if (h->sc.base && h->rtc_ok) cudaMemcpy(&dev[0], h->sc.tc_err, 4, cudaMemcpyDeviceToHost);
     if (h->gb_ready) cudaMemcpy(&dev[1], h->gb.err, 4, cudaMemcpyDeviceToHost);
     if (h->peer.open) cudaMemcpy(&dev[2], h->peer.window + h->peer.tab.off_err, 4, cudaMemcpyDeviceToHost);
@@ -1130,6 +1226,10 @@ int aero_cuda_moe_status(void* handle) {
     if (h->err_host) *reinterpret_cast<volatile int32_t*>(h->err_host) = 0;
     if (h->sc.base && h->rtc_ok) cudaMemset(h->sc.tc_err, 0, 4);
     if (h->gb_ready) cudaMemset(h->gb.err, 0, 4);
+    if (dev[3] != 0) {
+        cudaMemset(h->sc.dbar, 0, 8);
+        h->dec_seq = 0;
+    }
     if (!h->cuda_ok(cudaGetLastError(), "status")) return -1;
     return code;
 }

@@ -13,6 +13,7 @@
 #include <cub/block/block_scan.cuh>
 
 #include "internal.h"
+#include "topk.cuh"
 
 namespace aero {
 namespace {
@@ -157,25 +158,8 @@ __global__ void __launch_bounds__(256) router_sgemm_kernel(const float* __restri
 }
 
 // ---------------------------------------------------------------- top-k
-// One warp per token. Each lane owns experts lane, lane+32, ...; each round the
-// warp elects the best remaining (value desc, index asc) and removes it.
+// One warp per token (topk_warp in topk.cuh).
 constexpr int kTopkMaxPerLane = 32;  // E <= 1024
-
-// Order-preserving unsigned image of a logit: larger value -> larger key, -0
-// as +0, NaN below every number (key 0; std::partial_sort in the reference
-// leaves NaN order unspecified, this is one deterministic choice). key_value
-// inverts it (NaN for 0).
-__device__ __forceinline__ uint32_t order_key(float v) {
-    if (v != v) return 0u;
-    uint32_t u = __float_as_uint(v);
-    if (u == 0x80000000u) u = 0u;
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
-}
-__device__ __forceinline__ float key_value(uint32_t k) {
-    if (k == 0u) return __uint_as_float(0x7FC00000u);
-    return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
-}
-
 
 template <int PER>  // values per lane: E <= 32 * PER
 __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ logits, int ld, int T, int E,
@@ -186,55 +170,8 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
     const int t = blockIdx.x * 8 + warp;
     if (t >= T) return;
     const float* lg = logits + (int64_t)t * ld;
-    float v[PER];
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-        const int e = lane + 32 * i;
-        v[i] = e < E ? lg[e] : 0.f;
-    }
-    // Selection on 64-bit keys: the order-preserving bits of the logit above the
-    // complemented index, so the largest key is the larger logit and, on equal
-    // logits, the lower index (the order of `better`; NaNs rank below every
-    // number, lower index first among them). Each lane keeps its best remaining
-    // key; a round is one warp max, and only the winning lane rescans its slots.
-    uint64_t key[PER];
-#pragma unroll
-    for (int i = 0; i < PER; ++i) {
-        const int e = lane + 32 * i;
-        key[i] = e < E ? ((uint64_t)order_key(v[i]) << 32) | (0xFFFFFFFFu - (uint32_t)e) : 0ull;
-    }
-    uint64_t lb = 0;
-#pragma unroll
-    for (int i = 0; i < PER; ++i) lb = key[i] > lb ? key[i] : lb;
-
-    float sel_v = 0.f;  // lane j keeps the j-th selected logit (j < k <= 32 handled in rounds)
-    int sel_i = 0;      // and its expert
-    float wsum = 0.f, mx = 0.f;
-    for (int r = 0; r < k; ++r) {
-        uint64_t best = lb;
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) {
-            const uint64_t ot = __shfl_xor_sync(0xffffffffu, best, o);
-            best = ot > best ? ot : best;
-        }
-        const int bi = (int)(0xFFFFFFFFu - (uint32_t)best);
-        const float bv = key_value((uint32_t)(best >> 32));
-        if ((bi & 31) == lane) {
-            const int slot = bi >> 5;
-            lb = 0;
-#pragma unroll
-            for (int i = 0; i < PER; ++i) {
-                if (i == slot) key[i] = 0ull;
-                lb = key[i] > lb ? key[i] : lb;
-            }
-        }
-        if (lane == 0) idx[(int64_t)t * k + r] = bi;
-        if (r == 0) mx = bv;
-        if ((r & 31) == lane) {  // only valid for k <= 32 (checked by the host)
-            sel_v = bv;
-            sel_i = bi;
-        }
-    }
+    int sel_i = 0;
+    topk_warp<PER>(lg, E, k, norm, idx + (int64_t)t * k, w + (int64_t)t * k, &sel_i);
     if (one.perm && T == 1) {
         if (lane < k) {
             one.perm[lane] = lane;
@@ -247,25 +184,6 @@ __global__ void __launch_bounds__(256) topk_kernel(const float* __restrict__ log
             *one.n_active = k;
             *one.p_real = k;
         }
-    }
-    // weights
-    if (norm) {
-        // softmax over the selected logits; max is the first pick. Sum in
-        // selection order, as src/moe.cpp:47-53.
-        float e_mine = 0.f;
-        if (lane < k) e_mine = expf(sel_v - mx);
-        for (int r = 0; r < k; ++r) wsum += __shfl_sync(0xffffffffu, e_mine, r);
-        if (lane < k) w[(int64_t)t * k + lane] = e_mine / wsum;
-    } else {
-        double den = 0.0;
-#pragma unroll
-        for (int i = 0; i < PER; ++i) {
-            const int e = lane + 32 * i;
-            if (e < E) den += (double)expf(v[i] - mx);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) den += __shfl_xor_sync(0xffffffffu, den, o);
-        if (lane < k) w[(int64_t)t * k + lane] = (float)((double)expf(sel_v - mx) / den);
     }
     if (has_shared && lane == 0) sgate[t] = sigmoid_f(lg[E]);
     if (xq.q1) {

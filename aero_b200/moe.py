@@ -228,6 +228,11 @@ class CudaMoeLayer:
         if self._lib.aero_cuda_moe_set_option(self.handle, nc.OPT_ROUTER_TC, 1 if on else 0) != 0:
             raise ValueError(nc.last_error(self.handle))
 
+    def set_decode_fused(self, on: bool) -> None:
+        """Calls of up to 32 tokens as one fused kernel (default) or as separate kernels."""
+        if self._lib.aero_cuda_moe_set_option(self.handle, nc.OPT_DECODE_FUSED, 1 if on else 0) != 0:
+            raise ValueError(nc.last_error(self.handle))
+
     def set_peer_wait_ms(self, ms: int) -> None:
         """How long a peer-exchange kernel waits for a peer before giving up (code 21 / 22)."""
         if self._lib.aero_cuda_moe_set_option(self.handle, nc.OPT_PEER_WAIT_MS, int(ms)) != 0:

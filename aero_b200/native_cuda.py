@@ -32,6 +32,7 @@ MEM_WEIGHTS_RESIDENT, MEM_WEIGHTS_CACHE, MEM_KV_CACHE, MEM_SCRATCH, MEM_RUNTIME 
 OPT_GEMM_MIN_TOKENS = 1
 OPT_ROUTER_TC = 2
 OPT_PEER_WAIT_MS = 3
+OPT_DECODE_FUSED = 4
 
 
 class CudaMoeUnavailable(RuntimeError):

@@ -157,6 +157,11 @@ int aero_cuda_moe_stage_times(void* handle, double* ms, int64_t* counts, int n);
  * peer's step flag before it gives up and records code 21 / 22 (default 5000;
  * 1 to 600000). Applies from the next step. */
 #define AERO_CUDA_OPT_PEER_WAIT_MS 3
+/* AERO_CUDA_OPT_DECODE_FUSED: 1 (default) runs calls of up to 32 tokens on Q8_0 /
+ * Q4_K layers as one cooperative kernel (router, top-k, dispatch, gate/up,
+ * down, combine); 0 runs them as the separate router / top-k / dispatch / GEMV /
+ * combine kernels. */
+#define AERO_CUDA_OPT_DECODE_FUSED 4
 int aero_cuda_moe_set_option(void* handle, int option, int64_t value);
 
 /* 0, or the code of the first bounded device wait of this handle's kernels that
