@@ -639,12 +639,28 @@ cudaError_t launch_decode(const DecodeArgs& args, int n_sm, cudaStream_t s) {
     const int grid = n_sm;  // one CTA per SM (checked below against the occupancy)
     a.rows_per_cta = (a.dp + grid - 1) / grid;
     const size_t smem = decode_smem_bytes(a.T, a.E, a.k, a.has_shared, a.rows_per_cta, ntp);
-    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    int per_sm = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kDecThreads, smem);
-    if (e != cudaSuccess) return e;
-    if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+    // the dynamic shared memory each instantiation has been allowed so far (the
+    // attribute call and the occupancy check run when it has to grow, not per call)
+    struct Allowed {
+        const void* fn;
+        size_t smem;
+    };
+    static thread_local Allowed allowed[32] = {};
+    Allowed* slot = nullptr;
+    for (auto& x : allowed)
+        if (x.fn == fn || x.fn == nullptr) {
+            slot = &x;
+            break;
+        }
+    if (!slot || slot->fn != fn || slot->smem < smem) {
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        int per_sm = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kDecThreads, smem);
+        if (e != cudaSuccess) return e;
+        if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+        if (slot) *slot = Allowed{fn, smem};
+    }
     void* params[] = {&a};
     return cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kDecThreads), params, smem, s);
 }

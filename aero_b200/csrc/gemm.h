@@ -29,15 +29,16 @@ inline int gemm_max_tiles(int P, int T, int E, int has_shared) {
 size_t gemm_workspace_bytes(int dp, int act_ld, int P, int T, int max_tiles);
 
 struct GemmBuffers {
-    __half* xperm;   // (rows_cap, dp)   token rows sorted by expert, then x for the shared expert
-    __half* act;     // (rows_cap, act_ld)
+    __half* x16;     // (T_cap, dp)       the call's input rows as f16, in the GEMM's K order
+    __half* act;     // (rows_cap, act_ld) act rows by sorted position (shared expert: P + token)
     __half* y;       // (rows_cap, dp)
     GemmTile* tiles;        // (max tiles)
     int32_t* n_tiles;
     int32_t* err;           // pipeline timeout code (0 = none)
     int32_t* err_host = nullptr;  // host-mapped copy of the first code, or null
     int rows_cap;
-    CUtensorMap tmap_x[kGemmNT / 16], tmap_act[kGemmNT / 16];  // box heights 16, 32, ..., kGemmNT
+    CUtensorMap tmap_x16;                   // x16 rows for tile::gather4 loads (box: 64 values x 1 row)
+    CUtensorMap tmap_act[kGemmNT / 16];     // act tiles, box heights 16, 32, ..., kGemmNT
 };
 
 // A 2-D tiled TMA descriptor over a row-major matrix (rows x cols elements of
@@ -74,10 +75,11 @@ struct PrefillArgs {
     int n_sm;      // persistent grid size
 };
 
-// The prefill path: launch_prefill_prep (gather of the f16 operand rows + tile
+// The prefill path: launch_prefill_prep (the f16 copy of the input rows + tile
 // list, 2 kernels), then launch_prefill_gemm with gateup=true (gate/up GEMM +
-// SwiGLU into act) and gateup=false (down GEMM into y, f16, rows [0, P + Tsh));
-// the combine reads y with launch_combine_h.
+// SwiGLU into act; the token operand gathered from x16 by token id) and
+// gateup=false (down GEMM into y, f16, rows [0, P + Tsh)); the combine reads y
+// with launch_combine_h.
 cudaError_t launch_prefill_prep(const PrefillArgs& a, GemmBuffers& b, cudaStream_t s);
 cudaError_t launch_prefill_gemm(const PrefillArgs& a, GemmBuffers& b, const GemmWeightMaps& wm, bool gateup,
                                 cudaStream_t s);
