@@ -1,32 +1,37 @@
 // Decode (calls of up to 32 tokens): the whole MoE layer in one cooperative
-// launch, four phases separated by two grid barriers.
+// launch, five phases separated by three grid barriers.
 //
 //   A  router logits (f32, x . W_r + bias, plus the shared-gate column) and the
-//      call's x rows coded as integer input                       | barrier 1
+//      call's x rows coded as integer input                         | barrier 1
 //   B  in every CTA, from the logits: top-k per token (src/moe.cpp:26-66, the
 //      same selection as the top-k kernel) and the dispatch of the T*k pairs
 //      into expert segments (counting sort, stable in (token, slot) order),
 //      kept in shared memory
-//   C  gate/up GEMVs over the active experts (and the shared expert): act =
-//      silu(gate . x) * (up . x), coded as integer input for the down product
-//                                                                   | barrier 2
-//   D  down GEMVs, each CTA owning a block of output rows for every active
-//      expert, then the combine of those rows: out[t] = sum over slots in order
-//      of w * y + sgate * y_shared (src/moe.cpp:68-120)
+//   C  gate/up GEMVs over the active experts and the shared expert: act =
+//      silu(gate . x) * (up . x) per (pair, 16-row block), coded as integer
+//      input for the down product                                    | barrier 2
+//   D  down GEMVs per (pair, 32-row batch): y[pair] in f32            | barrier 3
+//   E  combine: out[t] = sum over slots in order of w * y + sgate * y_shared
+//      (src/moe.cpp:68-120)
 //
 // GEMV lanes. A lane owns 64 consecutive values of a row: for Q4_K the 32 code
 // bytes of sub-blocks 2g and 2g+1 of one super-block plus that super-block's
 // 16-byte header (one header load and one scale decode per row and lane);
-// for Q8_0 two whole 32-value blocks and their two fp16 scales. Rows of K
-// values take K/64 lanes (groups of 1 to 32 lanes; a warp computes 32/group
-// rows at a time). Only the selected experts' blocks are read, each once per
-// call; accumulation is f32.
+// for Q8_0 two whole 32-value blocks and their two fp16 scales. Rows of K values
+// take a group of G = pow2(K/64) lanes; a warp covers 32/G rows per pass. A warp
+// task takes G passes (one row per lane group per pass) with the next passes'
+// weights in flight (a ring of kRing loads), accumulating one partial per pass
+// in each lane; a reduce-scatter across the group then leaves every lane with
+// the full sum of one pass (G - 1 shuffles per lane for G rows, instead of
+// log2 G per row). Only the selected experts' blocks are read from HBM, once
+// per pair (a pair's token re-reads its expert's rows from L2 when the expert
+// has several tokens); accumulation is f32.
 //
 // Integer input (x and act rows), per 16 values: a 15-bit code split into two
 // int8 planes (v ~= sx * (128 q1 + q0), |128 q1 + q0| <= 16383) and the exact f32
-// sum of the 16 values (the Q4_K min term). A lane's 64 values are then four
-// blocks: sum(q x) is two chains of dp4a over the raw code bytes per block, and
-// the per-sub-block factorisation of the quantised dot (src/kernels.cpp:78-84,
+// sum of the 16 values (the Q4_K min term). A lane's 64 values are four blocks:
+// sum(q x) is two chains of dp4a over the raw code bytes per block, and the
+// per-sub-block factorisation of the quantised dot (src/kernels.cpp:78-84,
 // 123-156) applies the scales once per block:
 //   Q8_0: d * sum(q x)          Q4_K: d sc * sum(q x) - dmin m * sum(x)
 // The input coding error is at most 2^-15 of each 16-value block's largest |v|.
@@ -45,11 +50,13 @@
 namespace aero {
 namespace {
 
-constexpr int kDecThreads = 384;
+constexpr int kDecThreads = 256;
 constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kScanItems = (1024 + kDecThreads) / kDecThreads;  // items per thread: E + 1 <= 1025 values
 constexpr int kRouterTokGroup = 4;  // tokens per router warp task
-constexpr int kJBlock = 16;         // act rows per gate/up warp task (one coding block)
+constexpr int kJBlock = 16;         // act rows per gate/up task (one coding block)
+constexpr int kRing = 4;            // weight rows in flight per lane
+constexpr int kBarriers = 3;
 constexpr int kErrBarrier = 31;
 
 __device__ __forceinline__ uint64_t dec_gtimer() {
@@ -64,12 +71,12 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
 }
 
 // Grid barrier b of this launch: every CTA adds one to the counter, which only
-// grows (launch seq's barrier b completes at (seq * 2 + b + 1) * gridDim.x,
-// modulo 2^32). False when the wait ran out (the error is recorded).
+// grows (launch seq's barrier b completes at (seq * kBarriers + b + 1) *
+// gridDim.x, modulo 2^32). False when the wait ran out (the error is recorded).
 __device__ bool grid_barrier(const DecodeArgs& a, int b, volatile int* abort_s) {
     __syncthreads();
     if (threadIdx.x == 0) {
-        const uint32_t target = (a.seq * 2u + (uint32_t)b + 1u) * gridDim.x;
+        const uint32_t target = (a.seq * (uint32_t)kBarriers + (uint32_t)b + 1u) * gridDim.x;
         __threadfence();
         atomicAdd(a.bar, 1u);
         const uint64_t t0 = dec_gtimer();
@@ -82,7 +89,7 @@ __device__ bool grid_barrier(const DecodeArgs& a, int b, volatile int* abort_s) 
                 *abort_s = 1;
                 break;
             }
-            __nanosleep(32);
+            __nanosleep(64);
         }
         __threadfence();
     }
@@ -157,10 +164,12 @@ struct WSlice<AERO_DT_Q8_0> {
 
 __device__ __forceinline__ uint4 ldg16(const void* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
 
+// Row r of one expert's matrix, from the expert's plane bases (qs, meta).
 template <int DT>
-__device__ __forceinline__ void ws_load(const QMat& M, int e, int r, int gl, WSlice<DT>& w) {
-    const uint8_t* qs = qm_row_qs(M, e, r);
-    const uint8_t* mt = qm_row_meta(M, e, r);
+__device__ __forceinline__ void ws_load(const uint8_t* qs, const uint8_t* mt, int64_t qs_row, int64_t mt_row, int r,
+                                        int gl, WSlice<DT>& w) {
+    qs += (int64_t)r * qs_row;
+    mt += (int64_t)r * mt_row;
     if constexpr (DT == AERO_DT_Q4_K) {
         w.a = ldg16(qs + 32 * gl);
         w.b = ldg16(qs + 32 * gl + 16);
@@ -182,10 +191,21 @@ __device__ __forceinline__ int dot16(uint32_t w0, uint32_t w1, uint32_t w2, uint
     return a * 128 + b;
 }
 
-// acc[t] += this lane's part of row . input t, for t < nt.
-template <int DT, int NTP>
-__device__ __forceinline__ void ws_dot(const WSlice<DT>& w, int gl, const XSlice (&xs)[NTP], int nt,
-                                       float (&acc)[NTP]) {
+// The 6-bit scale and min of sub-block j (src/kernels.cpp:65-73) from the three
+// words of packed scale bytes, without a branch on j < 4 (lanes of one warp hold
+// different j): for j < 4 sc = q[j] & 63, m = q[j + 4] & 63; otherwise
+// sc = (q[j + 4] & 15) | ((q[j - 4] >> 6) << 4), m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4).
+__device__ __forceinline__ void q4k_sc_m_nb(uint32_t w0, uint32_t w1, uint32_t w2, int j, int& sc, int& m) {
+    const int sh = 8 * (j & 3);
+    const int b0 = (int)((w0 >> sh) & 0xFFu), b1 = (int)((w1 >> sh) & 0xFFu), b2 = (int)((w2 >> sh) & 0xFFu);
+    const bool lo = j < 4;
+    sc = lo ? (b0 & 63) : ((b2 & 15) | ((b0 >> 6) << 4));
+    m = lo ? (b1 & 63) : ((b2 >> 4) | ((b1 >> 6) << 4));
+}
+
+// This lane's part of (row . input).
+template <int DT>
+__device__ __forceinline__ float ws_dot(const WSlice<DT>& w, int gl, const XSlice& x) {
     if constexpr (DT == AERO_DT_Q4_K) {
         const uint32_t q[8] = {w.a.x, w.a.y, w.a.z, w.a.w, w.b.x, w.b.y, w.b.z, w.b.w};
         uint32_t lo[8], hi[8];
@@ -198,46 +218,77 @@ __device__ __forceinline__ void ws_dot(const WSlice<DT>& w, int gl, const XSlice
         const float dmin = __half2float(__ushort_as_half((unsigned short)(w.hdr.x >> 16)));
         const int g = gl & 3;
         int sc0, m0, sc1, m1;
-        q4k_sc_m_words(w.hdr.y, w.hdr.z, w.hdr.w, 2 * g, sc0, m0);
-        q4k_sc_m_words(w.hdr.y, w.hdr.z, w.hdr.w, 2 * g + 1, sc1, m1);
-        const float a0 = d * (float)sc0, b0 = dmin * (float)m0, a1 = d * (float)sc1, b1 = dmin * (float)m1;
-#pragma unroll
-        for (int t = 0; t < NTP; ++t) {
-            if (t < nt) {
-                const XSlice& x = xs[t];
-                // low nibbles: sub-block 2g (values 0-31 = blocks 0, 1); high: 2g+1 (blocks 2, 3)
-                const int s0 = dot16(lo[0], lo[1], lo[2], lo[3], x.h, x.l);
-                const int s1 = dot16(lo[4], lo[5], lo[6], lo[7], x.h + 4, x.l + 4);
-                const int s2 = dot16(hi[0], hi[1], hi[2], hi[3], x.h + 8, x.l + 8);
-                const int s3 = dot16(hi[4], hi[5], hi[6], hi[7], x.h + 12, x.l + 12);
-                const float p0 = fmaf(x.sx[0], (float)s0, x.sx[1] * (float)s1);
-                const float p1 = fmaf(x.sx[2], (float)s2, x.sx[3] * (float)s3);
-                acc[t] += (a0 * p0 - b0 * (x.s16[0] + x.s16[1])) + (a1 * p1 - b1 * (x.s16[2] + x.s16[3]));
-            }
-        }
+        q4k_sc_m_nb(w.hdr.y, w.hdr.z, w.hdr.w, 2 * g, sc0, m0);
+        q4k_sc_m_nb(w.hdr.y, w.hdr.z, w.hdr.w, 2 * g + 1, sc1, m1);
+        // low nibbles: sub-block 2g (values 0-31 = blocks 0, 1); high: 2g+1 (blocks 2, 3)
+        const int s0 = dot16(lo[0], lo[1], lo[2], lo[3], x.h, x.l);
+        const int s1 = dot16(lo[4], lo[5], lo[6], lo[7], x.h + 4, x.l + 4);
+        const int s2 = dot16(hi[0], hi[1], hi[2], hi[3], x.h + 8, x.l + 8);
+        const int s3 = dot16(hi[4], hi[5], hi[6], hi[7], x.h + 12, x.l + 12);
+        const float p0 = fmaf(x.sx[0], (float)s0, x.sx[1] * (float)s1);
+        const float p1 = fmaf(x.sx[2], (float)s2, x.sx[3] * (float)s3);
+        return (d * (float)sc0 * p0 - dmin * (float)m0 * (x.s16[0] + x.s16[1])) +
+               (d * (float)sc1 * p1 - dmin * (float)m1 * (x.s16[2] + x.s16[3]));
     } else {
         const float d0 = __half2float(__ushort_as_half((unsigned short)(w.sc & 0xFFFFu)));
         const float d1 = __half2float(__ushort_as_half((unsigned short)(w.sc >> 16)));
-#pragma unroll
-        for (int t = 0; t < NTP; ++t) {
-            if (t < nt) {
-                const XSlice& x = xs[t];
-                const int s0 = dot16(w.q[0].x, w.q[0].y, w.q[0].z, w.q[0].w, x.h, x.l);
-                const int s1 = dot16(w.q[1].x, w.q[1].y, w.q[1].z, w.q[1].w, x.h + 4, x.l + 4);
-                const int s2 = dot16(w.q[2].x, w.q[2].y, w.q[2].z, w.q[2].w, x.h + 8, x.l + 8);
-                const int s3 = dot16(w.q[3].x, w.q[3].y, w.q[3].z, w.q[3].w, x.h + 12, x.l + 12);
-                acc[t] += d0 * fmaf(x.sx[0], (float)s0, x.sx[1] * (float)s1) +
-                          d1 * fmaf(x.sx[2], (float)s2, x.sx[3] * (float)s3);
-            }
-        }
+        const int s0 = dot16(w.q[0].x, w.q[0].y, w.q[0].z, w.q[0].w, x.h, x.l);
+        const int s1 = dot16(w.q[1].x, w.q[1].y, w.q[1].z, w.q[1].w, x.h + 4, x.l + 4);
+        const int s2 = dot16(w.q[2].x, w.q[2].y, w.q[2].z, w.q[2].w, x.h + 8, x.l + 8);
+        const int s3 = dot16(w.q[3].x, w.q[3].y, w.q[3].z, w.q[3].w, x.h + 12, x.l + 12);
+        return d0 * fmaf(x.sx[0], (float)s0, x.sx[1] * (float)s1) + d1 * fmaf(x.sx[2], (float)s2, x.sx[3] * (float)s3);
     }
 }
 
-template <int NTP>
-__device__ __forceinline__ void group_reduce(float (&acc)[NTP], int group) {
+constexpr int kChunk = 4;  // row dots reduced together (and rows in flight per lane)
+
+// v[i] (i < 4) holds this lane's partial of chunk item i, for lane groups of
+// G >= 4 lanes (runtime). Two halving steps over the top two bits of the
+// group's lane index, then sums over the remaining bits: v[0] ends with the
+// group's full sum of item (lane % G) / (G / 4).
+__device__ __forceinline__ void chunk_reduce(float (&v)[kChunk], int G, int lane) {
+    {
+        const int o = G >> 1;
+        const bool up = (lane & o) != 0;
 #pragma unroll
-    for (int t = 0; t < NTP; ++t)
-        for (int o = group >> 1; o > 0; o >>= 1) acc[t] += __shfl_xor_sync(0xffffffffu, acc[t], o);
+        for (int i = 0; i < 2; ++i) {
+            const float send = up ? v[i] : v[i + 2];
+            const float keep = up ? v[i + 2] : v[i];
+            v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+    }
+    {
+        const int o = G >> 2;
+        const bool up = (lane & o) != 0;
+        const float send = up ? v[0] : v[1];
+        const float keep = up ? v[1] : v[0];
+        v[0] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+    for (int o = G >> 3; o >= 1; o >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+}
+
+// n_items row dots (a multiple of 4) of this lane group, 4 rows in flight:
+// load(p, w) fetches item p's weights; after each chunk, emit(q, v) is called
+// by every lane with v the full dot of item q = chunk start + (lane % G) / (G / 4).
+template <int DT, typename Load, typename Emit>
+__device__ __forceinline__ void gemv_items(int n_items, int G, Load load, Emit emit, bool on, int gl,
+                                           const XSlice& x, int lane) {
+    WSlice<DT> ring[kChunk];
+#pragma unroll
+    for (int s = 0; s < kChunk; ++s)
+        if (on && s < n_items) load(s, ring[s]);
+    const int spread = G / kChunk;
+#pragma unroll 1
+    for (int c0 = 0; c0 < n_items; c0 += kChunk) {
+        float acc[kChunk];
+#pragma unroll
+        for (int s = 0; s < kChunk; ++s) {
+            acc[s] = on ? ws_dot<DT>(ring[s], gl, x) : 0.f;
+            if (on && c0 + s + kChunk < n_items) load(c0 + s + kChunk, ring[s]);
+        }
+        chunk_reduce(acc, G, lane);
+        emit(c0 + gl / spread, acc[0]);
+    }
 }
 
 __host__ __device__ inline int pow2_at_least(int v) {
@@ -246,8 +297,63 @@ __host__ __device__ inline int pow2_at_least(int v) {
     return p;
 }
 
+// One gate/up task: rows jb * 16 .. + 16 of gate and up of expert e for one
+// input row (x_row, K values, lane groups of G = pow2(K / 64) >= 4). Item q =
+// 2 * pass + matrix (0 gate, 1 up), pass p covering rows p * (32 / G) + sub of
+// the block; the block's act lands in act_w[16].
+template <int DT>
+__device__ __forceinline__ void gateup_task(const QMat& Gm, const QMat& Um, int e, int jb, int K, int G,
+                                            const uint8_t* x_row, int lane, float* act_w) {
+    const int rpw = 32 / G;
+    const int gl = lane % G, sub = lane / G;
+    const bool on = gl < K / 64;
+    XSlice x;
+    if (on) xs_load(x_row, K, gl, x);
+    const int64_t qs_row = qm_row_qs_bytes(Gm.dtype, Gm.cols), mt_row = qm_row_meta_bytes(Gm.dtype, Gm.cols);
+    const int r0 = jb * kJBlock + sub;
+    const uint8_t* q0 = Gm.qs + (int64_t)e * Gm.qs_estride + (int64_t)r0 * qs_row;
+    const uint8_t* m0 = Gm.meta + (int64_t)e * Gm.meta_estride + (int64_t)r0 * mt_row;
+    const uint8_t* q1 = Um.qs + (int64_t)e * Um.qs_estride + (int64_t)r0 * qs_row;
+    const uint8_t* m1 = Um.meta + (int64_t)e * Um.meta_estride + (int64_t)r0 * mt_row;
+    auto load = [&](int q, WSlice<DT>& w) {
+        const int r = (q >> 1) * rpw;
+        if (q & 1)
+            ws_load<DT>(q1, m1, qs_row, mt_row, r, gl, w);
+        else
+            ws_load<DT>(q0, m0, qs_row, mt_row, r, gl, w);
+    };
+    const int spread = G / kChunk;
+    auto emit = [&](int q, float v) {
+        const float partner = __shfl_xor_sync(0xffffffffu, v, spread);  // the other matrix of the row
+        if ((q & 1) == 0 && gl % spread == 0) act_w[(q >> 1) * rpw + sub] = silu_f(v) * partner;
+    };
+    gemv_items<DT>(2 * (kJBlock / rpw), G, load, emit, on, gl, x, lane);
+}
+
+// One down task: rows b * 32 .. + 32 of expert e's down matrix (K values each,
+// groups of G = pow2(K / 64) >= 4 lanes) for one act row (row length ld); y_row
+// receives them. Pass p covers rows p * (32 / G) + sub.
+template <int DT>
+__device__ __forceinline__ void down_task(const QMat& D, int e, int b, int K, int G, const uint8_t* x_row, int ld,
+                                          int lane, float* y_row) {
+    const int rpw = 32 / G;
+    const int gl = lane % G, sub = lane / G;
+    const bool on = gl < K / 64;
+    XSlice x;
+    if (on) xs_load(x_row, ld, gl, x);
+    const int64_t qs_row = qm_row_qs_bytes(D.dtype, D.cols), mt_row = qm_row_meta_bytes(D.dtype, D.cols);
+    const uint8_t* q0 = D.qs + (int64_t)e * D.qs_estride + (int64_t)(b * 32 + sub) * qs_row;
+    const uint8_t* m0 = D.meta + (int64_t)e * D.meta_estride + (int64_t)(b * 32 + sub) * mt_row;
+    auto load = [&](int p, WSlice<DT>& w) { ws_load<DT>(q0, m0, qs_row, mt_row, p * rpw, gl, w); };
+    const int spread = G / kChunk;
+    auto emit = [&](int p, float v) {
+        if (gl % spread == 0) y_row[b * 32 + p * rpw + sub] = v;
+    };
+    gemv_items<DT>(G, G, load, emit, on, gl, x, lane);
+}
+
 // ------------------------------------------------------------ shared state
-// Per-CTA tables of the call's routing (phase B), then the down phase's rows.
+// Per-CTA tables of the call's routing (phase B).
 struct DecShared {
     int32_t* cnt;     // [E] pairs per expert, then the scatter's cursor
     int32_t* off;     // [E + 1] expert offsets
@@ -260,9 +366,8 @@ struct DecShared {
     int32_t* u_pos;   // [U] first sorted position (shared: P)
     int32_t* u_n;     // [U] pairs (shared: T)
     int32_t* gu_pre;  // [U + 1] gate/up task prefix
-    int32_t* dn_pre;  // [U + 1] down task prefix (this CTA)
-    float* act;       // [warps][kJBlock][NTP] gate/up act staging
-    float* y;         // [(P + T) * rows_per_cta] down outputs of this CTA's rows
+    int32_t* dn_pre;  // [U + 1] down task prefix
+    float* act;       // [warps][kJBlock] gate/up act staging
 };
 
 // Exclusive scan of v[0..n) in place (n <= kScanItems * blockDim.x); returns the total.
@@ -285,7 +390,20 @@ __device__ int block_excl_scan(int32_t* v, int n, typename Scan::TempStorage& tm
     return tot;
 }
 
-template <int DT, int NTP, int PER>
+// The last u with pre[u] <= task (pre[0] = 0, U >= 1).
+__device__ __forceinline__ int find_unit(const int32_t* pre, int U, int task) {
+    int lo = 0, hi = U - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (pre[mid] <= task)
+            lo = mid;
+        else
+            hi = mid - 1;
+    }
+    return lo;
+}
+
+template <int DT, int PER>
 __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(DecodeArgs a) {
     extern __shared__ __align__(16) uint8_t dsm[];
     using Scan = cub::BlockScan<int, kDecThreads>;
@@ -293,7 +411,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(DecodeArgs a) {
     __shared__ int abort_s, n_units_s;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int T = a.T, E = a.E, k = a.k, P = T * k;
-    const int Tsh = a.has_shared ? T : 0;
+    const int n_warps = gridDim.x * kDecWarps;
+    const int gwarp = blockIdx.x * kDecWarps + warp;
     if (threadIdx.x == 0) abort_s = 0;
 
     // ---------------------------------------------------------------- phase A
@@ -302,9 +421,8 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(DecodeArgs a) {
         const int row0 = a.logits_in ? E : 0;
         const int n_tg = (T + kRouterTokGroup - 1) / kRouterTokGroup;
         const int n_tasks = n_rows * n_tg;
-        const int n_warps = gridDim.x * kDecWarps;
         const int nf4 = a.dp / 128;  // float4 per lane (dp <= 2048: at most 16)
-        for (int task = blockIdx.x * kDecWarps + warp; task < n_tasks; task += n_warps) {
+        for (int task = gwarp; task < n_tasks; task += n_warps) {
             const int tg = task / n_rows, r = row0 + task % n_rows;
             const float* wr = a.router + (int64_t)r * a.dp;
             float4 wv[16];
@@ -365,8 +483,7 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(DecodeArgs a) {
         S.u_n = (int32_t*)take((size_t)Umax * 4);
         S.gu_pre = (int32_t*)take((size_t)(Umax + 1) * 4);
         S.dn_pre = (int32_t*)take((size_t)(Umax + 1) * 4);
-        S.act = (float*)take((size_t)kDecWarps * kJBlock * NTP * 4);
-        S.y = (float*)take((size_t)(P + Tsh) * a.rows_per_cta * 4);
+        S.act = (float*)take((size_t)kDecWarps * kJBlock * 4);
     }
     const float* lg_base = a.logits_in ? a.logits_in : a.logits;
     const int lg_ld = a.logits_in ? a.ld_in : a.lg_ld;
@@ -436,24 +553,17 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(DecodeArgs a) {
     }
     __syncthreads();
     const int U = n_units_s;
-    // task counts per unit: gate/up (unit, 16-row block, token group) and this CTA's
-    // down tasks (unit, token group: a task streams the CTA's rows)
-    const int rows_lo = blockIdx.x * a.rows_per_cta, rows_hi = min(a.dp, rows_lo + a.rows_per_cta);
-    const int n_rows_d = max(0, rows_hi - rows_lo);
+    // tasks per unit: gate/up (input row, 16-row block), down (input row, 32-row batch);
+    // a unit's tasks are consecutive, the blocks of one input row innermost
+    const int n_batch = a.dp / 32;
     for (int u = threadIdx.x; u < U; u += kDecThreads) {
-        const bool sh = S.u_e[u] < 0;
-        const int F = sh ? a.Fs : a.F;
-        const int ng = (S.u_n[u] + NTP - 1) / NTP;
-        S.gu_pre[u] = (F / kJBlock) * ng;
-        S.dn_pre[u] = n_rows_d > 0 ? ng : 0;
+        const int F = S.u_e[u] < 0 ? a.Fs : a.F;
+        S.gu_pre[u] = S.u_n[u] * (F / kJBlock);
+        S.dn_pre[u] = S.u_n[u] * n_batch;
     }
     __syncthreads();
     const int n_gu = block_excl_scan<Scan>(S.gu_pre, U, scan_tmp);
     const int n_dn = block_excl_scan<Scan>(S.dn_pre, U, scan_tmp);
-    if (threadIdx.x == 0) {
-        S.gu_pre[U] = n_gu;
-        S.dn_pre[U] = n_dn;
-    }
     if (blockIdx.x == 0) {
         // the call's routing for the host (stats, profiling)
         for (int p = threadIdx.x; p < P; p += kDecThreads) {
@@ -467,80 +577,34 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(DecodeArgs a) {
     }
     __syncthreads();
 
-    auto find_unit = [&](const int32_t* pre, int task) {
-        int lo = 0, hi = U - 1;  // the last u with pre[u] <= task
-        while (lo < hi) {
-            const int mid = (lo + hi + 1) >> 1;
-            if (pre[mid] <= task)
-                lo = mid;
-            else
-                hi = mid - 1;
-        }
-        return lo;
-    };
-
     // ---------------------------------------------------------------- phase C
+    // tasks in contiguous ranges per warp, so a warp's consecutive tasks mostly
+    // share their input row (loaded once)
     {
         const int K = a.dp;
-        const int group = pow2_at_least(K / 64);
-        const int rpw = 32 / group;
-        const int gl = lane & (group - 1), sub = lane / group;
-        const bool lane_on = gl < K / 64;
-        float* act_w = S.act + warp * kJBlock * NTP;
-        const int n_warps = gridDim.x * kDecWarps;
-        for (int task = warp * gridDim.x + blockIdx.x; task < n_gu; task += n_warps) {
-            const int u = find_unit(S.gu_pre, task);
+        const int G = pow2_at_least(K / 64);
+        float* act_w = S.act + warp * kJBlock;
+        const int per = (n_gu + n_warps - 1) / n_warps;
+        const int t_lo = gwarp * per, t_hi = min(n_gu, t_lo + per);
+        for (int task = t_lo; task < t_hi; ++task) {
+            const int u = find_unit(S.gu_pre, U, task);
             const int rel = task - S.gu_pre[u];
             const bool sh = S.u_e[u] < 0;
-            const int F = sh ? a.Fs : a.F;
-            const int nblk = F / kJBlock;
-            const int tg = rel / nblk, jb = rel % nblk;
-            const int nt = min(NTP, S.u_n[u] - tg * NTP);
-            const QMat& G = sh ? a.sg : a.gate;
-            const QMat& Up = sh ? a.su : a.up;
+            const int nblk = (sh ? a.Fs : a.F) / kJBlock;
+            const int i = rel / nblk, jb = rel % nblk;
+            const int tok = sh ? i : S.perm[S.u_pos[u] + i] / k;
+            const uint8_t* x_row = a.xq + (int64_t)tok * qx_row_bytes(K);
+            const QMat& Gm = sh ? a.sg : a.gate;
+            const QMat& Um = sh ? a.su : a.up;
             const int e = sh ? 0 : S.u_e[u];
-            XSlice xs[NTP];
-            int arow[NTP];
-#pragma unroll
-            for (int i = 0; i < NTP; ++i) {
-                const int j = tg * NTP + min(i, nt - 1);
-                const int tok = sh ? j : S.perm[S.u_pos[u] + j] / k;
-                arow[i] = S.u_pos[u] + j;  // sorted position (shared: P + token)
-                if (lane_on) xs_load(a.xq + (int64_t)tok * qx_row_bytes(K), K, gl, xs[i]);
-            }
-            // row passes: rows jb * 16 + p * rpw + sub, gate then up, the next item's weights in flight
-            const int n_pass = (kJBlock + rpw - 1) / rpw;
-            const int n_items = 2 * n_pass;
-            auto item_row = [&](int it) { return jb * kJBlock + (it >> 1) * rpw + sub; };
-            auto item_ok = [&](int it) { return lane_on && (it >> 1) * rpw + sub < kJBlock; };
-            WSlice<DT> cur, nxt;
-            if (item_ok(0)) ws_load<DT>(G, e, item_row(0), gl, cur);
-            float g[NTP];
-            for (int it = 0; it < n_items; ++it) {
-                if (it + 1 < n_items && item_ok(it + 1)) ws_load<DT>((it + 1) & 1 ? Up : G, e, item_row(it + 1), gl, nxt);
-                float acc[NTP];
-#pragma unroll
-                for (int i = 0; i < NTP; ++i) acc[i] = 0.f;
-                if (item_ok(it)) ws_dot<DT, NTP>(cur, gl, xs, nt, acc);
-                group_reduce<NTP>(acc, group);
-                if (it & 1) {
-                    const int jj = (it >> 1) * rpw + sub;
-                    if (gl == 0 && jj < kJBlock) {
-#pragma unroll
-                        for (int i = 0; i < NTP; ++i) act_w[jj * NTP + i] = silu_f(g[i]) * acc[i];
-                    }
-                } else {
-#pragma unroll
-                    for (int i = 0; i < NTP; ++i) g[i] = acc[i];
-                }
-                cur = nxt;
-            }
+            gateup_task<DT>(Gm, Um, e, jb, K, G, x_row, lane, act_w);
             __syncwarp();
-            if (lane < nt) {
+            if (lane == 0) {
                 float v[kJBlock];
 #pragma unroll
-                for (int jj = 0; jj < kJBlock; ++jj) v[jj] = act_w[jj * NTP + lane];
-                qx_code16(v, a.aq + (int64_t)arow[lane] * qx_row_bytes(a.act_ld), a.act_ld, jb * kJBlock);
+                for (int jj = 0; jj < kJBlock; ++jj) v[jj] = act_w[jj];
+                const int arow = S.u_pos[u] + i;  // sorted position (shared: P + token)
+                qx_code16(v, a.aq + (int64_t)arow * qx_row_bytes(a.act_ld), a.act_ld, jb * kJBlock);
             }
             __syncwarp();
         }
@@ -548,71 +612,61 @@ __global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(DecodeArgs a) {
     if (!grid_barrier(a, 1, &abort_s)) return;
 
     // ---------------------------------------------------------------- phase D
-    for (int task = warp; task < n_dn; task += kDecWarps) {
-        const int u = find_unit(S.dn_pre, task);
-        const int tg = task - S.dn_pre[u];
-        const bool sh = S.u_e[u] < 0;
-        const int K = sh ? a.Fs : a.F;
-        const int group = pow2_at_least(K / 64);
-        const int rpw = 32 / group;
-        const int gl = lane & (group - 1), sub = lane / group;
-        const bool lane_on = gl < K / 64;
-        const int nrg = (n_rows_d + rpw - 1) / rpw;
-        const int nt = min(NTP, S.u_n[u] - tg * NTP);
-        const QMat& D = sh ? a.sd : a.down;
-        const int e = sh ? 0 : S.u_e[u];
-        XSlice xs[NTP];
-        int arow[NTP];
-#pragma unroll
-        for (int i = 0; i < NTP; ++i) {
-            arow[i] = S.u_pos[u] + tg * NTP + min(i, nt - 1);
-            if (lane_on) xs_load(a.aq + (int64_t)arow[i] * qx_row_bytes(a.act_ld), a.act_ld, gl, xs[i]);
+    {
+        const int per = (n_dn + n_warps - 1) / n_warps;
+        const int t_lo = gwarp * per, t_hi = min(n_dn, t_lo + per);
+        for (int task = t_lo; task < t_hi; ++task) {
+            const int u = find_unit(S.dn_pre, U, task);
+            const int rel = task - S.dn_pre[u];
+            const bool sh = S.u_e[u] < 0;
+            const int K = sh ? a.Fs : a.F;
+            const int G = pow2_at_least(K / 64);
+            const int i = rel / n_batch, b = rel % n_batch;
+            const int arow = S.u_pos[u] + i;
+            const uint8_t* x_row = a.aq + (int64_t)arow * qx_row_bytes(a.act_ld);
+            const QMat& D = sh ? a.sd : a.down;
+            const int e = sh ? 0 : S.u_e[u];
+            float* y_row = a.y + (int64_t)arow * a.dp;
+            down_task<DT>(D, e, b, K, G, x_row, a.act_ld, lane, y_row);
         }
-        // the CTA's rows, rpw at a time, the next rows' weights in flight
-        auto row_ok = [&](int rg) { return lane_on && rows_lo + rg * rpw + sub < rows_hi; };
-        WSlice<DT> cur, nxt;
-        if (row_ok(0)) ws_load<DT>(D, e, rows_lo + sub, gl, cur);
-        for (int rg = 0; rg < nrg; ++rg) {
-            if (rg + 1 < nrg && row_ok(rg + 1)) ws_load<DT>(D, e, rows_lo + (rg + 1) * rpw + sub, gl, nxt);
-            float acc[NTP];
-#pragma unroll
-            for (int i = 0; i < NTP; ++i) acc[i] = 0.f;
-            if (row_ok(rg)) ws_dot<DT, NTP>(cur, gl, xs, nt, acc);
-            group_reduce<NTP>(acc, group);
-            const int nn = rg * rpw + sub;
-            if (row_ok(rg) && gl == 0) {
-#pragma unroll
-                for (int i = 0; i < NTP; ++i)
-                    if (i < nt) S.y[(int64_t)arow[i] * a.rows_per_cta + nn] = acc[i];
+    }
+    if (!grid_barrier(a, 2, &abort_s)) return;
+
+    // ---------------------------------------------------------------- phase E
+    // out[t][n] = sum_s w[t][s] * y[inv(t, s)][n] (slot order) + sgate[t] * y[P + t][n]
+    {
+        const int d4 = a.dp / 4;
+        for (int i = blockIdx.x * kDecThreads + threadIdx.x; i < T * d4; i += gridDim.x * kDecThreads) {
+            const int t = i / d4, c = (i % d4) * 4;
+            float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int s = 0; s < k; ++s) {
+                const float ws = S.w[t * k + s];
+                const float4 v = *reinterpret_cast<const float4*>(a.y + (int64_t)S.inv[t * k + s] * a.dp + c);
+                o.x += ws * v.x, o.y += ws * v.y, o.z += ws * v.z, o.w += ws * v.w;
             }
-            cur = nxt;
+            if (a.has_shared) {
+                const float g = S.sgate[t];
+                const float4 v = *reinterpret_cast<const float4*>(a.y + (int64_t)(P + t) * a.dp + c);
+                o.x += g * v.x, o.y += g * v.y, o.z += g * v.z, o.w += g * v.w;
+            }
+            *reinterpret_cast<float4*>(a.out + (int64_t)t * a.dp + c) = o;
         }
     }
-    __syncthreads();
-    // combine: out[t][n] = sum_s w[t][s] * y[(t, s)][n] (slot order) + sgate[t] * y_shared[t][n]
-    for (int i = threadIdx.x; i < T * n_rows_d; i += kDecThreads) {
-        const int t = i / n_rows_d, nn = i % n_rows_d;
-        float o = 0.f;
-        for (int s = 0; s < k; ++s) o += S.w[t * k + s] * S.y[(int64_t)S.inv[t * k + s] * a.rows_per_cta + nn];
-        if (a.has_shared) o += S.sgate[t] * S.y[(int64_t)(P + t) * a.rows_per_cta + nn];
-        a.out[(int64_t)t * a.dp + rows_lo + nn] = o;
-    }
 }
 
-template <int DT, int NTP>
+template <int DT>
 const void* decode_kernel_for(int E) {
-    if (E <= 128) return (const void*)decode_kernel<DT, NTP, 4>;
-    if (E <= 256) return (const void*)decode_kernel<DT, NTP, 8>;
-    if (E <= 512) return (const void*)decode_kernel<DT, NTP, 16>;
-    return (const void*)decode_kernel<DT, NTP, 32>;
+    if (E <= 128) return (const void*)decode_kernel<DT, 4>;
+    if (E <= 256) return (const void*)decode_kernel<DT, 8>;
+    if (E <= 512) return (const void*)decode_kernel<DT, 16>;
+    return (const void*)decode_kernel<DT, 32>;
 }
 
-size_t decode_smem_bytes(int T, int E, int k, int has_shared, int rows_per_cta, int ntp) {
+size_t decode_smem_bytes(int T, int E, int k) {
     const int P = T * k, Umax = std::min(P, E) + 1;
     auto al = [](size_t b) { return (b + 15) & ~(size_t)15; };
     return al((size_t)E * 4) + al((size_t)(E + 1) * 4) + 4 * al((size_t)P * 4) + al((size_t)T * 4) +
-           3 * al((size_t)Umax * 4) + 2 * al((size_t)(Umax + 1) * 4) + al((size_t)kDecWarps * kJBlock * ntp * 4) +
-           al((size_t)(P + (has_shared ? T : 0)) * rows_per_cta * 4);
+           3 * al((size_t)Umax * 4) + 2 * al((size_t)(Umax + 1) * 4) + al((size_t)kDecWarps * kJBlock * 4);
 }
 
 }  // namespace
@@ -623,22 +677,18 @@ bool decode_supported(int dtype, int T, int E, int k, int dp, int F, int Fs, int
     if (dtype != AERO_DT_Q4_K && dtype != AERO_DT_Q8_0) return false;
     if (T < 1 || T > kDecodeMaxTokens || k < 1 || k > 32 || E < k || E > 1024) return false;
     if (std::min(T * k, E) + (has_shared ? 1 : 0) > kScanItems * kDecThreads) return false;
-    if (dp % 128 || dp > 2048 || F % 64 || F > 2048 || F < 64) return false;
-    if (has_shared && (Fs % 64 || Fs > 2048 || Fs < 64)) return false;
+    // lane groups of at least 4 lanes: rows of at least 192 values (4 groups of 64 lanes' values)
+    if (dp % 128 || dp > 2048 || dp < 256 || F % 64 || F > 2048 || F < 192) return false;
+    if (has_shared && (Fs % 64 || Fs > 2048 || Fs < 192)) return false;
     return true;
 }
 
 cudaError_t launch_decode(const DecodeArgs& args, int n_sm, cudaStream_t s) {
     DecodeArgs a = args;
-    const int ntp = a.T == 1 ? 1 : 2;
-    const void* fn = nullptr;
-    if (a.gate.dtype == AERO_DT_Q4_K)
-        fn = ntp == 1 ? decode_kernel_for<AERO_DT_Q4_K, 1>(a.E) : decode_kernel_for<AERO_DT_Q4_K, 2>(a.E);
-    else
-        fn = ntp == 1 ? decode_kernel_for<AERO_DT_Q8_0, 1>(a.E) : decode_kernel_for<AERO_DT_Q8_0, 2>(a.E);
+    const void* fn = a.gate.dtype == AERO_DT_Q4_K ? decode_kernel_for<AERO_DT_Q4_K>(a.E)
+                                                  : decode_kernel_for<AERO_DT_Q8_0>(a.E);
     const int grid = n_sm;  // one CTA per SM (checked below against the occupancy)
-    a.rows_per_cta = (a.dp + grid - 1) / grid;
-    const size_t smem = decode_smem_bytes(a.T, a.E, a.k, a.has_shared, a.rows_per_cta, ntp);
+    const size_t smem = decode_smem_bytes(a.T, a.E, a.k);
     // the dynamic shared memory each instantiation has been allowed so far (the
     // attribute call and the occupancy check run when it has to grow, not per call)
     struct Allowed {

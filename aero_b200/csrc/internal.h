@@ -121,13 +121,13 @@ struct DecodeArgs {
     float* w_out;             // (T * k)
     int32_t* n_active_out;    // active experts of the call
     int32_t* p_real_out;      // T * k
+    float* y;                 // (T * k + T, dp) f32: each pair's expert output (shared expert: rows T * k + t)
     float* out;               // (T, dp) f32
     uint32_t* bar;            // grid-barrier counter (only grows; zero when the handle's scratch is made)
     uint32_t seq;             // launches made on this counter before this one
     int32_t* err;
     int32_t* err_host;
     uint64_t wait_ns;
-    int rows_per_cta;         // set by launch_decode
 };
 bool decode_supported(int dtype, int T, int E, int k, int dp, int F, int Fs, int has_shared);
 int64_t decode_qx_row_bytes(int K);

@@ -62,6 +62,7 @@ struct Scratch {
     int gemv_cap = 0;
     // fused decode path: coded x and act rows, grid-barrier counter and error word
     uint8_t *dxq = nullptr, *daq = nullptr;
+    float* dy = nullptr;
     uint32_t* dbar = nullptr;
     int32_t* derr = nullptr;
 };
@@ -311,6 +312,7 @@ bool ensure_scratch(Handle& h, int T) {
     const bool dec = h.dtype != AERO_DT_F32;
     const size_t o_dxq = take(dec ? (size_t)dT * decode_qx_row_bytes(h.dp) : 0);
     const size_t o_daq = take(dec ? (size_t)(dT * h.k + dT) * decode_qx_row_bytes(h.act_ld) : 0);
+    const size_t o_dy = take(dec ? (size_t)(dT * h.k + dT) * h.dp * 4 : 0);
     const size_t o_dbar = take(8);
     // split-K partial logits of the tensor-core router (small batches)
     const int part_rows = h.rtc_ok ? (int)std::min<int64_t>(kRouterPartRows, (int64_t)8 * cap) : 0;
@@ -352,6 +354,7 @@ bool ensure_scratch(Handle& h, int T) {
     s.tc_err = (int32_t*)(b + o_tce);
     s.dxq = dec ? (uint8_t*)(b + o_dxq) : nullptr;
     s.daq = dec ? (uint8_t*)(b + o_daq) : nullptr;
+    s.dy = dec ? (float*)(b + o_dy) : nullptr;
     s.dbar = (uint32_t*)(b + o_dbar);
     s.derr = (int32_t*)(b + o_dbar + 4);
     h.dec_seq = 0;  // the new scratch is cleared below: the barrier counter starts at zero
@@ -597,6 +600,7 @@ bool decode_call(Handle& h, const float* x, int T, const float* logits_in, float
     a.w_out = s.w;
     a.n_active_out = s.n_active;
     a.p_real_out = s.offsets + h.E;
+    a.y = s.dy;
     a.out = out;
     a.bar = s.dbar;
     a.seq = h.dec_seq;

@@ -66,15 +66,16 @@ def test_fused_decode_matches_oracle_and_separate_kernels(dt, T):
 def test_fused_decode_shapes(case):
     """No shared expert with norm_topk_prob = 0 (full-softmax weights); a 2048-wide layer
     with F = 768 (16-lane row groups with idle lanes in the down product); k = 32 of 1024
-    experts at 32 tokens (the dispatch tables at their limit)."""
+    experts at 32 tokens with F = 192 (the dispatch tables at their limit, 3 of 4 lanes
+    active per down row)."""
     if case == "no_shared_norm0":
-        spec = synth.LayerSpec(256, 40, 6, 128, 0, Q.DTYPE_Q8_0, norm_topk_prob=False)
+        spec = synth.LayerSpec(256, 40, 6, 256, 0, Q.DTYPE_Q8_0, norm_topk_prob=False)
         T = 9
     elif case == "wide":
         spec = synth.LayerSpec(2048, 16, 4, 768, 768, Q.DTYPE_Q4_K)
         T = 5
     else:
-        spec = synth.LayerSpec(256, 1024, 32, 64, 64, Q.DTYPE_Q8_0)
+        spec = synth.LayerSpec(256, 1024, 32, 192, 192, Q.DTYPE_Q8_0)
         T = 32
     layer = synth.make_layer(spec, 52)
     x = synth.make_x(T, spec.d, 52)
