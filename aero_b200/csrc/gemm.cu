@@ -22,10 +22,8 @@
 //               rows (2-D tensor maps over the expert-major qs and header
 //               planes, 128 values per stage, a deep ring)
 //   warp 22     TMA producer of the token operand (f16 rows, 128B swizzle,
-//               K-major; no multicast anywhere): gate/up gathers the tile's
-//               token rows from the f16 copy of x by token id (tile::gather4,
-//               four rows per copy, the warp's lanes issuing them), down loads
-//               one box of the tile's height of the act rows per K step
+//               K-major, one box of the tile's height per K step; no multicast
+//               anywhere)
 //   warp 1      one thread issues tcgen05.mma with the weight operand A in TMEM
 //               and the token operand B in shared memory, fp32 accumulators in
 //               TMEM (two, so an item's epilogue overlaps the next main loop),
@@ -77,8 +75,6 @@ constexpr uint32_t kAColBase = 2 * kGemmNT;  // 384: the A stages fill columns 3
 enum : int { kErrRawFull = 1, kErrBFull = 2, kErrEmpty = 3, kErrAcc = 4, kErrAFull = 5, kErrAEmpty = 6 };
 
 struct GemmParams {
-    const int32_t* perm;  // gate/up: sorted position -> pair (token = pair / k); shared tiles start at P
-    int k, P;
     QMat A0, A1;          // routed: gate, up (gate/up GEMM) or down
     QMat S0, S1;          // shared expert
     const GemmTile* tiles;
@@ -122,8 +118,7 @@ __device__ __forceinline__ bool item_at(const GemmParams& p, int n_tiles, int& w
 // (one copy per K step covers a whole tile), then per weight family the qs
 // plane and the header plane, routed (w) and shared (s), matrix 0 and 1.
 struct GemmMaps {
-    CUtensorMap b[kBMaps];  // down: act tiles
-    CUtensorMap g;          // gate/up: the x16 rows (gather4)
+    CUtensorMap b[kBMaps];  // token operand tiles: xperm (gate/up) or act (down) rows
     CUtensorMap w0, w1, s0, s1, mw0, mw1, ms0, ms1;
 };
 
@@ -254,58 +249,33 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
             }
         }
     } else if (warp == kTokWarp) {
-        // -------------------------------------------------------- token producer
-        int b_n = 0;
-        bool ok = true;
-        Item it;
-        for (int w = blockIdx.x; ok && item_at(p, n_tiles, w, it); w += gridDim.x) {
-            // gate/up: the token of each of the tile's rows (rows past nvalid repeat the
-            // last valid one; their outputs are never stored); lane l holds the gather
-            // groups l and l + 32, four rows each
-            int tok[2][4];
-            if (GATEUP) {
-#pragma unroll
-                for (int gi = 0; gi < 2; ++gi)
-#pragma unroll
-                    for (int r = 0; r < 4; ++r) {
-                        const int pos = it.t.pos0 + min(4 * (lane + 32 * gi) + r, it.t.nvalid - 1);
-                        tok[gi][r] = pos >= p.P ? pos - p.P : __ldg(p.perm + pos) / p.k;
-                    }
-            }
-            for (int kb = 0; kb < it.nkb; ++kb) {
-                const int sb = b_n % kStages;
-                bool got = true;
-                if (lane == 0) {
-                    got = mbar_wait(empty(sb), ((b_n / kStages) & 1) ^ 1, abort_flag);
-                    if (got)
-                        mbar_expect_tx(full(sb), (uint32_t)it.N * kBK * 2);
-                    else
+        if (lane == 0) {
+            // ---------------------------------------------------- token producer
+            int b_n = 0;
+            bool ok = true;
+            Item it;
+            for (int w = blockIdx.x; ok && item_at(p, n_tiles, w, it); w += gridDim.x) {
+                const CUtensorMap* bm = &tm.b[it.N / 16 - 1];
+                for (int kb = 0; kb < it.nkb; ++kb) {
+                    const int sb = b_n % kStages;
+                    if (!mbar_wait(empty(sb), ((b_n / kStages) & 1) ^ 1, abort_flag)) {
                         fail(kErrEmpty);
-                }
-                if (!__shfl_sync(0xffffffffu, got, 0)) {
-                    ok = false;
-                    break;
-                }
-                __syncwarp();
-                const uint32_t dst = smem_u32(b_ring + sb * kBStageBytes);
-                if (GATEUP) {
-#pragma unroll
-                    for (int gi = 0; gi < 2; ++gi) {
-                        const int g = lane + 32 * gi;
-                        if (4 * g < it.N) tma_gather4(dst + (uint32_t)g * 512u, &tm.g, kb * kBK, tok[gi], full(sb));
+                        ok = false;
+                        break;
                     }
-                } else if (lane == 0) {
-                    tma_load_2d(dst, &tm.b[it.N / 16 - 1], kb * kBK, it.t.pos0, full(sb));
+                    const uint32_t dst = smem_u32(b_ring + sb * kBStageBytes);
+                    mbar_expect_tx(full(sb), (uint32_t)it.N * kBK * 2);
+                    tma_load_2d(dst, bm, kb * kBK, it.t.pos0, full(sb));
+                    ++b_n;
                 }
-                ++b_n;
             }
-        }
-        if (!ok && lane == 0) {
-            // the copies in flight land whatever the dequant warps do: wait for
-            // their bytes with a timed wait on the stage's transaction count
-            for (int i = 0; i < kStages && i < b_n; ++i) {
-                const int n = b_n - 1 - i;
-                mbar_wait_timed(full(n % kStages), (n / kStages) & 1);
+            if (!ok) {
+                // the copies in flight land whatever the dequant warps do: wait for
+                // their bytes with a timed wait on the stage's transaction count
+                for (int i = 0; i < kStages && i < b_n; ++i) {
+                    const int n = b_n - 1 - i;
+                    mbar_wait_timed(full(n % kStages), (n / kStages) & 1);
+                }
             }
         }
     } else if (warp == 1) {
@@ -543,8 +513,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
 
 // ------------------------------------------------------------------ helpers
 // x16 row r = input row r as f16 with its values in the GEMM's K order (0, 2,
-// 1, 3 within every four: kperm); the gate/up token producer gathers the rows
-// of each tile from here by token id. One warp per row, 8 values (one 16-byte
+// 1, 3 within every four: kperm). One warp per row, 8 values (one 16-byte
 // store) per lane per chunk.
 template <typename XT>
 __global__ void x16_kernel(const XT* __restrict__ x, int rows, int dp, __half* __restrict__ x16) {
@@ -566,6 +535,28 @@ __global__ void x16_kernel(const XT* __restrict__ x, int rows, int dp, __half* _
             }
             *reinterpret_cast<uint4*>(dst + c) = o;
         }
+    }
+}
+
+// xperm rows: [0, P_real) the routed pairs in sorted order, [P, P + Tsh) the
+// first Tsh input rows for the shared expert, copied from x16 (which the 34 MB
+// of a config-5 call keep in L2). P_real (= offsets[E]) is read on the device:
+// sorted positions [P_real, P) hold skipped slots and are not gathered. One
+// warp per row, 16-byte copies.
+__global__ void gather_kernel(const __half* __restrict__ x16, const int32_t* __restrict__ perm,
+                              const int32_t* __restrict__ p_real, int k, int P, int Tsh, int dp,
+                              __half* __restrict__ xp) {
+    const int pr = *p_real;
+    const int rows = pr + Tsh;
+    const int lane = threadIdx.x & 31;
+    const int nw = (int)((gridDim.x * blockDim.x) >> 5);
+    for (int v = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5); v < rows; v += nw) {
+        const int row = v < pr ? v : P + (v - pr);
+        const int tok = v < pr ? perm[v] / k : v - pr;
+        const uint4* src = reinterpret_cast<const uint4*>(x16 + (int64_t)tok * dp);
+        uint4* dst = reinterpret_cast<uint4*>(xp + (int64_t)row * dp);
+#pragma unroll 4
+        for (int c = lane; c < dp / 8; c += 32) dst[c] = __ldg(src + c);
     }
 }
 
@@ -736,8 +727,8 @@ cudaError_t launch_gemm(const GemmMaps& maps, const GemmParams& p, int n_sm, cud
 size_t gemm_workspace_bytes(int dp, int act_ld, int P, int T, int max_tiles) {
     auto al = [](size_t v) { return (v + 1023) & ~(size_t)1023; };
     const size_t rows = (size_t)P + T;
-    return al((size_t)T * dp * 2) + al(rows * act_ld * 2) + al(rows * dp * 2) + al((size_t)max_tiles * sizeof(GemmTile)) +
-           1024;
+    return al((size_t)T * dp * 2) + al(rows * dp * 2) + al(rows * act_ld * 2) + al(rows * dp * 2) +
+           al((size_t)max_tiles * sizeof(GemmTile)) + 1024;
 }
 
 bool gemm_setup(void* ws, size_t ws_bytes, int dp, int act_ld, int P_cap, int T_cap, int max_tiles, GemmBuffers* b,
@@ -751,6 +742,8 @@ bool gemm_setup(void* ws, size_t ws_bytes, int dp, int act_ld, int P_cap, int T_
     char* c = static_cast<char*>(ws);
     b->x16 = reinterpret_cast<__half*>(c);
     c += al((size_t)T_cap * dp * 2);
+    b->xperm = reinterpret_cast<__half*>(c);
+    c += al(rows * dp * 2);
     b->act = reinterpret_cast<__half*>(c);
     c += al(rows * act_ld * 2);
     b->y = reinterpret_cast<__half*>(c);
@@ -760,12 +753,9 @@ bool gemm_setup(void* ws, size_t ws_bytes, int dp, int act_ld, int P_cap, int T_
     b->n_tiles = reinterpret_cast<int32_t*>(c);
     b->err = b->n_tiles + 1;
     b->rows_cap = (int)rows;
-    if (!make_tmap_act(&b->tmap_x16, b->x16, (uint64_t)T_cap, (uint64_t)dp, (uint64_t)dp, 1u)) {
-        *why = "cuTensorMapEncodeTiled failed for the input rows";
-        return false;
-    }
     for (int i = 0; i < kBMaps; ++i)
-        if (!make_tmap_act(&b->tmap_act[i], b->act, rows, (uint64_t)act_ld, (uint64_t)act_ld, 16u * (i + 1))) {
+        if (!make_tmap_act(&b->tmap_x[i], b->xperm, rows, (uint64_t)dp, (uint64_t)dp, 16u * (i + 1)) ||
+            !make_tmap_act(&b->tmap_act[i], b->act, rows, (uint64_t)act_ld, (uint64_t)act_ld, 16u * (i + 1))) {
             *why = "cuTensorMapEncodeTiled failed for the activation buffers";
             return false;
         }
@@ -803,6 +793,11 @@ cudaError_t launch_prefill_prep(const PrefillArgs& a, GemmBuffers& b, cudaStream
         else
             x16_kernel<float><<<grid, 256, 0, s>>>(static_cast<const float*>(a.x), a.T, a.dp, b.x16);
     }
+    {
+        const int64_t warps = (int64_t)(P + Tsh);  // a warp per row
+        const unsigned grid = (unsigned)std::max<int64_t>(1, std::min<int64_t>((warps + 7) / 8, (int64_t)a.n_sm * 16));
+        gather_kernel<<<grid, 256, 0, s>>>(b.x16, a.perm, a.p_real, a.k, P, Tsh, a.dp, b.xperm);
+    }
     build_tiles_kernel<<<1, 1024, 0, s>>>(a.act_e, a.act_off, a.n_active, P, Tsh, a.has_shared, b.tiles, b.n_tiles);
     return cudaGetLastError();
 }
@@ -817,9 +812,6 @@ cudaError_t launch_prefill_gemm(const PrefillArgs& a, GemmBuffers& b, const Gemm
     g.err = b.err;
     g.err_host = b.err_host;
     g.e_begin = a.e_begin;
-    g.perm = a.perm;
-    g.k = a.k;
-    g.P = a.T * a.k;
     GemmMaps maps{};
     if (gateup) {
         g.A0 = a.gate;
@@ -833,7 +825,7 @@ cudaError_t launch_prefill_gemm(const PrefillArgs& a, GemmBuffers& b, const Gemm
         g.MTmax = g.MT > g.MTs ? g.MT : g.MTs;
         g.out = b.act;
         g.out_ld = a.act_ld;
-        maps.g = b.tmap_x16;
+        for (int i = 0; i < kBMaps; ++i) maps.b[i] = b.tmap_x[i];
         maps.w0 = wm.q[0];
         maps.w1 = wm.q[1];
         maps.s0 = wm.q[3];

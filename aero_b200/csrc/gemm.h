@@ -30,6 +30,7 @@ size_t gemm_workspace_bytes(int dp, int act_ld, int P, int T, int max_tiles);
 
 struct GemmBuffers {
     __half* x16;     // (T_cap, dp)       the call's input rows as f16, in the GEMM's K order
+    __half* xperm;   // (rows_cap, dp)    x16 rows by sorted position (shared expert: P + token)
     __half* act;     // (rows_cap, act_ld) act rows by sorted position (shared expert: P + token)
     __half* y;       // (rows_cap, dp)
     GemmTile* tiles;        // (max tiles)
@@ -37,8 +38,7 @@ struct GemmBuffers {
     int32_t* err;           // pipeline timeout code (0 = none)
     int32_t* err_host = nullptr;  // host-mapped copy of the first code, or null
     int rows_cap;
-    CUtensorMap tmap_x16;                   // x16 rows for tile::gather4 loads (box: 64 values x 1 row)
-    CUtensorMap tmap_act[kGemmNT / 16];     // act tiles, box heights 16, 32, ..., kGemmNT
+    CUtensorMap tmap_x[kGemmNT / 16], tmap_act[kGemmNT / 16];  // box heights 16, 32, ..., kGemmNT
 };
 
 // A 2-D tiled TMA descriptor over a row-major matrix (rows x cols elements of
@@ -75,9 +75,9 @@ struct PrefillArgs {
     int n_sm;      // persistent grid size
 };
 
-// The prefill path: launch_prefill_prep (the f16 copy of the input rows + tile
-// list, 2 kernels), then launch_prefill_gemm with gateup=true (gate/up GEMM +
-// SwiGLU into act; the token operand gathered from x16 by token id) and
+// The prefill path: launch_prefill_prep (the f16 copy of the input rows, its
+// rows gathered into sorted-pair order, the tile list: 3 kernels), then
+// launch_prefill_gemm with gateup=true (gate/up GEMM + SwiGLU into act) and
 // gateup=false (down GEMM into y, f16, rows [0, P + Tsh)); the combine reads y
 // with launch_combine_h.
 cudaError_t launch_prefill_prep(const PrefillArgs& a, GemmBuffers& b, cudaStream_t s);

@@ -500,7 +500,7 @@ bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool ski
         if (!h.cuda_ok(launch_prefill_gemm(pa, h.gb, h.wmaps, true, st), "gate/up GEMM")) return false;
         h.mark(4);
         if (!h.cuda_ok(launch_prefill_gemm(pa, h.gb, h.wmaps, false, st), "down GEMM")) return false;
-        h.launches += 4;
+        h.launches += 5;  // x16, gather, tile list, two GEMMs
         h.mark(5);
         // (the caller may fuse the combine into its own kernel: expert parallel over peer memory)
         if (!gemm_skip_combine) {

@@ -85,17 +85,6 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
-// Four rows (rows[0..3]) of a 2-D tensor map whose box is one row high, columns
-// [x, x + box width), landing as consecutive rows at dst (no multicast).
-__device__ __forceinline__ void tma_gather4(uint32_t dst, const CUtensorMap* map, int x, const int (&rows)[4],
-                                            uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
-        "%4, %5, %6}], [%7];" ::"r"(dst),
-        "l"((uint64_t)map), "r"(x), "r"(rows[0]), "r"(rows[1]), "r"(rows[2]), "r"(rows[3]), "r"(bar)
-        : "memory");
-}
-
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 
