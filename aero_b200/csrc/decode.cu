@@ -55,7 +55,7 @@ constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kScanItems = (1024 + kDecThreads) / kDecThreads;  // items per thread: E + 1 <= 1025 values
 constexpr int kRouterTokGroup = 4;  // tokens per router warp task
 constexpr int kJBlock = 16;         // act rows per gate/up task (one coding block)
-constexpr int kRing = 4;            // weight rows in flight per lane
+constexpr int kRing = 2;            // weight rows in flight per lane (two CTAs per SM)
 constexpr int kBarriers = 3;
 constexpr int kErrBarrier = 31;
 
@@ -181,6 +181,21 @@ __device__ __forceinline__ void ws_load(const uint8_t* qs, const uint8_t* mt, in
     }
 }
 
+// dp4a with unsigned bytes in a and signed bytes in b
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+// sum over 16 values (4 words of unsigned codes) of code * (128 q1 + q0)
+__device__ __forceinline__ int dot16u(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, const uint32_t* h,
+                                      const uint32_t* l) {
+    int a = dp4a_us(w0, h[0], 0), b = dp4a_us(w0, l[0], 0);
+    a = dp4a_us(w1, h[1], a), b = dp4a_us(w1, l[1], b);
+    a = dp4a_us(w2, h[2], a), b = dp4a_us(w2, l[2], b);
+    a = dp4a_us(w3, h[3], a), b = dp4a_us(w3, l[3], b);
+    return a * 128 + b;
+}
 // sum over 16 values (4 words of codes) of code * (128 q1 + q0)
 __device__ __forceinline__ int dot16(uint32_t w0, uint32_t w1, uint32_t w2, uint32_t w3, const uint32_t* h,
                                      const uint32_t* l) {
@@ -191,16 +206,22 @@ __device__ __forceinline__ int dot16(uint32_t w0, uint32_t w1, uint32_t w2, uint
     return a * 128 + b;
 }
 
-// The 6-bit scale and min of sub-block j (src/kernels.cpp:65-73) from the three
-// words of packed scale bytes, without a branch on j < 4 (lanes of one warp hold
+// The 6-bit scales and mins of sub-blocks j and j + 1 (j = 2g even) from the
+// three words of packed scale bytes q[0..12) (src/kernels.cpp:65-73), two
+// 16-bit lanes at a time and without a branch on j < 4 (lanes of one warp hold
 // different j): for j < 4 sc = q[j] & 63, m = q[j + 4] & 63; otherwise
 // sc = (q[j + 4] & 15) | ((q[j - 4] >> 6) << 4), m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4).
-__device__ __forceinline__ void q4k_sc_m_nb(uint32_t w0, uint32_t w1, uint32_t w2, int j, int& sc, int& m) {
+// sc2 / m2 hold sub-block j in bits 0-7 and j + 1 in bits 16-23.
+__device__ __forceinline__ void q4k_sc_m_pair(uint32_t w0, uint32_t w1, uint32_t w2, int j, uint32_t& sc2,
+                                              uint32_t& m2) {
     const int sh = 8 * (j & 3);
-    const int b0 = (int)((w0 >> sh) & 0xFFu), b1 = (int)((w1 >> sh) & 0xFFu), b2 = (int)((w2 >> sh) & 0xFFu);
+    // bytes j, j + 1 (mod 4) of each word, spread to bits 0-7 and 16-23
+    const uint32_t y = __byte_perm(w0 >> sh, 0, 0x5140), z = __byte_perm(w1 >> sh, 0, 0x5140),
+                   w = __byte_perm(w2 >> sh, 0, 0x5140);
+    const uint32_t hy = (y & 0x00C000C0u) >> 2, hz = (z & 0x00C000C0u) >> 2;
     const bool lo = j < 4;
-    sc = lo ? (b0 & 63) : ((b2 & 15) | ((b0 >> 6) << 4));
-    m = lo ? (b1 & 63) : ((b2 >> 4) | ((b1 >> 6) << 4));
+    sc2 = lo ? (y & 0x003F003Fu) : ((w & 0x000F000Fu) | hy);
+    m2 = lo ? (z & 0x003F003Fu) : (((w >> 4) & 0x000F000Fu) | hz);
 }
 
 // This lane's part of (row . input).
@@ -208,27 +229,29 @@ template <int DT>
 __device__ __forceinline__ float ws_dot(const WSlice<DT>& w, int gl, const XSlice& x) {
     if constexpr (DT == AERO_DT_Q4_K) {
         const uint32_t q[8] = {w.a.x, w.a.y, w.a.z, w.a.w, w.b.x, w.b.y, w.b.z, w.b.w};
+        // low nibbles as bytes; high nibbles kept in place (16 x the code, an
+        // unsigned byte), the factor 16 folded into the scale below
         uint32_t lo[8], hi[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             lo[i] = q[i] & 0x0F0F0F0Fu;
-            hi[i] = (q[i] >> 4) & 0x0F0F0F0Fu;
+            hi[i] = q[i] & 0xF0F0F0F0u;
         }
         const float d = __half2float(__ushort_as_half((unsigned short)(w.hdr.x & 0xFFFFu)));
         const float dmin = __half2float(__ushort_as_half((unsigned short)(w.hdr.x >> 16)));
-        const int g = gl & 3;
-        int sc0, m0, sc1, m1;
-        q4k_sc_m_nb(w.hdr.y, w.hdr.z, w.hdr.w, 2 * g, sc0, m0);
-        q4k_sc_m_nb(w.hdr.y, w.hdr.z, w.hdr.w, 2 * g + 1, sc1, m1);
+        uint32_t sc2, m2;
+        q4k_sc_m_pair(w.hdr.y, w.hdr.z, w.hdr.w, 2 * (gl & 3), sc2, m2);
         // low nibbles: sub-block 2g (values 0-31 = blocks 0, 1); high: 2g+1 (blocks 2, 3)
-        const int s0 = dot16(lo[0], lo[1], lo[2], lo[3], x.h, x.l);
-        const int s1 = dot16(lo[4], lo[5], lo[6], lo[7], x.h + 4, x.l + 4);
-        const int s2 = dot16(hi[0], hi[1], hi[2], hi[3], x.h + 8, x.l + 8);
-        const int s3 = dot16(hi[4], hi[5], hi[6], hi[7], x.h + 12, x.l + 12);
+        const int s0 = dot16u(lo[0], lo[1], lo[2], lo[3], x.h, x.l);
+        const int s1 = dot16u(lo[4], lo[5], lo[6], lo[7], x.h + 4, x.l + 4);
+        const int s2 = dot16u(hi[0], hi[1], hi[2], hi[3], x.h + 8, x.l + 8);
+        const int s3 = dot16u(hi[4], hi[5], hi[6], hi[7], x.h + 12, x.l + 12);
         const float p0 = fmaf(x.sx[0], (float)s0, x.sx[1] * (float)s1);
         const float p1 = fmaf(x.sx[2], (float)s2, x.sx[3] * (float)s3);
-        return (d * (float)sc0 * p0 - dmin * (float)m0 * (x.s16[0] + x.s16[1])) +
-               (d * (float)sc1 * p1 - dmin * (float)m1 * (x.s16[2] + x.s16[3]));
+        const float sc0 = (float)(sc2 & 0xFFu), sc1 = (float)(sc2 >> 16);
+        const float m0 = (float)(m2 & 0xFFu), m1 = (float)(m2 >> 16);
+        return (d * sc0 * p0 - dmin * m0 * (x.s16[0] + x.s16[1])) +
+               (d * sc1 * 0.0625f * p1 - dmin * m1 * (x.s16[2] + x.s16[3]));
     } else {
         const float d0 = __half2float(__ushort_as_half((unsigned short)(w.sc & 0xFFFFu)));
         const float d1 = __half2float(__ushort_as_half((unsigned short)(w.sc >> 16)));
@@ -240,7 +263,7 @@ __device__ __forceinline__ float ws_dot(const WSlice<DT>& w, int gl, const XSlic
     }
 }
 
-constexpr int kChunk = 4;  // row dots reduced together (and rows in flight per lane)
+constexpr int kChunk = 4;  // row dots reduced together
 
 // v[i] (i < 4) holds this lane's partial of chunk item i, for lane groups of
 // G >= 4 lanes (runtime). Two halving steps over the top two bits of the
@@ -267,15 +290,15 @@ __device__ __forceinline__ void chunk_reduce(float (&v)[kChunk], int G, int lane
     for (int o = G >> 3; o >= 1; o >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
 }
 
-// n_items row dots (a multiple of 4) of this lane group, 4 rows in flight:
+// n_items row dots (a multiple of 4) of this lane group, kRing rows in flight:
 // load(p, w) fetches item p's weights; after each chunk, emit(q, v) is called
 // by every lane with v the full dot of item q = chunk start + (lane % G) / (G / 4).
 template <int DT, typename Load, typename Emit>
 __device__ __forceinline__ void gemv_items(int n_items, int G, Load load, Emit emit, bool on, int gl,
                                            const XSlice& x, int lane) {
-    WSlice<DT> ring[kChunk];
+    WSlice<DT> ring[kRing];
 #pragma unroll
-    for (int s = 0; s < kChunk; ++s)
+    for (int s = 0; s < kRing; ++s)
         if (on && s < n_items) load(s, ring[s]);
     const int spread = G / kChunk;
 #pragma unroll 1
@@ -283,8 +306,8 @@ __device__ __forceinline__ void gemv_items(int n_items, int G, Load load, Emit e
         float acc[kChunk];
 #pragma unroll
         for (int s = 0; s < kChunk; ++s) {
-            acc[s] = on ? ws_dot<DT>(ring[s], gl, x) : 0.f;
-            if (on && c0 + s + kChunk < n_items) load(c0 + s + kChunk, ring[s]);
+            acc[s] = on ? ws_dot<DT>(ring[s % kRing], gl, x) : 0.f;
+            if (on && c0 + s + kRing < n_items) load(c0 + s + kRing, ring[s % kRing]);
         }
         chunk_reduce(acc, G, lane);
         emit(c0 + gl / spread, acc[0]);
@@ -404,7 +427,7 @@ __device__ __forceinline__ int find_unit(const int32_t* pre, int U, int task) {
 }
 
 template <int DT, int PER>
-__global__ void __launch_bounds__(kDecThreads, 1) decode_kernel(DecodeArgs a) {
+__global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
     extern __shared__ __align__(16) uint8_t dsm[];
     using Scan = cub::BlockScan<int, kDecThreads>;
     __shared__ typename Scan::TempStorage scan_tmp;
@@ -687,7 +710,7 @@ cudaError_t launch_decode(const DecodeArgs& args, int n_sm, cudaStream_t s) {
     DecodeArgs a = args;
     const void* fn = a.gate.dtype == AERO_DT_Q4_K ? decode_kernel_for<AERO_DT_Q4_K>(a.E)
                                                   : decode_kernel_for<AERO_DT_Q8_0>(a.E);
-    const int grid = n_sm;  // one CTA per SM (checked below against the occupancy)
+    const int grid = 2 * n_sm;  // two CTAs per SM (checked below against the occupancy)
     const size_t smem = decode_smem_bytes(a.T, a.E, a.k);
     // the dynamic shared memory each instantiation has been allowed so far (the
     // attribute call and the occupancy check run when it has to grow, not per call)
@@ -708,7 +731,7 @@ cudaError_t launch_decode(const DecodeArgs& args, int n_sm, cudaStream_t s) {
         int per_sm = 0;
         e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kDecThreads, smem);
         if (e != cudaSuccess) return e;
-        if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+        if (per_sm < 2) return cudaErrorCooperativeLaunchTooLarge;
         if (slot) *slot = Allowed{fn, smem};
     }
     void* params[] = {&a};
