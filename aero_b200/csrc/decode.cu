@@ -437,6 +437,10 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
     const int n_warps = gridDim.x * kDecWarps;
     const int gwarp = blockIdx.x * kDecWarps + warp;
     if (threadIdx.x == 0) abort_s = 0;
+    auto stamp = [&](int i) {
+        if (a.stamps && blockIdx.x == 0 && threadIdx.x == 0) a.stamps[i] = dec_gtimer();
+    };
+    stamp(0);
 
     // ---------------------------------------------------------------- phase A
     {
@@ -483,6 +487,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
         }
     }
     if (!grid_barrier(a, 0, &abort_s)) return;
+    stamp(1);
 
     // ---------------------------------------------------------------- phase B
     DecShared S;
@@ -600,6 +605,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
     }
     __syncthreads();
 
+    stamp(2);
     // ---------------------------------------------------------------- phase C
     // tasks in contiguous ranges per warp, so a warp's consecutive tasks mostly
     // share their input row (loaded once)
@@ -633,6 +639,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
         }
     }
     if (!grid_barrier(a, 1, &abort_s)) return;
+    stamp(3);
 
     // ---------------------------------------------------------------- phase D
     {
@@ -654,6 +661,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
         }
     }
     if (!grid_barrier(a, 2, &abort_s)) return;
+    stamp(4);
 
     // ---------------------------------------------------------------- phase E
     // out[t][n] = sum_s w[t][s] * y[inv(t, s)][n] (slot order) + sgate[t] * y[P + t][n]
@@ -675,6 +683,8 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
             *reinterpret_cast<float4*>(a.out + (int64_t)t * a.dp + c) = o;
         }
     }
+    __syncthreads();
+    stamp(5);
 }
 
 template <int DT>

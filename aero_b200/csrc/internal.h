@@ -128,6 +128,7 @@ struct DecodeArgs {
     int32_t* err;
     int32_t* err_host;
     uint64_t wait_ns;
+    uint64_t* stamps;         // null, or 6 %globaltimer stamps of CTA 0: start, ends of phases A..E (profiling)
 };
 bool decode_supported(int dtype, int T, int E, int k, int dp, int F, int Fs, int has_shared);
 int64_t decode_qx_row_bytes(int K);

@@ -65,6 +65,7 @@ struct Scratch {
     float* dy = nullptr;
     uint32_t* dbar = nullptr;
     int32_t* derr = nullptr;
+    uint64_t* dstamps = nullptr;  // phase stamps of the fused decode kernel (profiling)
 };
 
 // Expert-parallel exchange over peer memory: this rank's window (IPC-exported),
@@ -136,6 +137,7 @@ struct Handle {
     int last_pairs = -1;      // its routed (token, expert) pairs computed here
     int last_shared_rows = 0; // its rows through the shared expert
     bool last_gemm = false;   // whether it took the GEMM path
+    bool last_decode = false; // whether it took the fused decode kernel
     PeerCtx peer;
 
     void peer_release() {
@@ -314,6 +316,7 @@ bool ensure_scratch(Handle& h, int T) {
     const size_t o_daq = take(dec ? (size_t)(dT * h.k + dT) * decode_qx_row_bytes(h.act_ld) : 0);
     const size_t o_dy = take(dec ? (size_t)(dT * h.k + dT) * h.dp * 4 : 0);
     const size_t o_dbar = take(8);
+    const size_t o_dst = take(6 * 8);
     // split-K partial logits of the tensor-core router (small batches)
     const int part_rows = h.rtc_ok ? (int)std::min<int64_t>(kRouterPartRows, (int64_t)8 * cap) : 0;
     const size_t o_lgp = take((size_t)part_rows * h.lg_ld * 4);
@@ -357,6 +360,7 @@ bool ensure_scratch(Handle& h, int T) {
     s.dy = dec ? (float*)(b + o_dy) : nullptr;
     s.dbar = (uint32_t*)(b + o_dbar);
     s.derr = (int32_t*)(b + o_dbar + 4);
+    s.dstamps = (uint64_t*)(b + o_dst);
     h.dec_seq = 0;  // the new scratch is cleared below: the barrier counter starts at zero
     s.lg_part = part_rows ? (float*)(b + o_lgp) : nullptr;
     s.lg_part_rows = part_rows;
@@ -557,11 +561,25 @@ bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool ski
 bool finish_profile(Handle& h) {
     if (!h.profiling) return true;
     if (!h.cuda_ok(cudaEventSynchronize(h.sev[6]), "profile")) return false;
-    for (int i = 0; i < Handle::kStages; ++i) {
-        float ms = 0.f;
-        cudaEventElapsedTime(&ms, h.sev[i], h.sev[i + 1]);
-        h.stage_ms[i] += ms;
-        h.stage_n[i] += 1;
+    if (h.last_decode) {
+        // one kernel: its phases by the stamps of its first CTA (router = A, top-k and
+        // dispatch = B, gate/up = C, down = D, combine = E)
+        uint64_t t[6];
+        if (!h.cuda_ok(cudaMemcpy(t, h.sc.dstamps, sizeof t, cudaMemcpyDeviceToHost), "profile")) return false;
+        const double ph[Handle::kStages] = {(t[1] - t[0]) * 1e-6, (t[2] - t[1]) * 1e-6, 0.0,
+                                            (t[3] - t[2]) * 1e-6, (t[4] - t[3]) * 1e-6, (t[5] - t[4]) * 1e-6};
+        for (int i = 0; i < Handle::kStages; ++i) {
+            h.stage_ms[i] += ph[i];
+            h.stage_n[i] += 1;
+        }
+        h.last_decode = false;
+    } else {
+        for (int i = 0; i < Handle::kStages; ++i) {
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, h.sev[i], h.sev[i + 1]);
+            h.stage_ms[i] += ms;
+            h.stage_n[i] += 1;
+        }
     }
     cudaMemcpy(&h.last_active, h.sc.n_active, 4, cudaMemcpyDeviceToHost);
     cudaMemcpy(&h.last_pairs, h.sc.offsets + h.E, 4, cudaMemcpyDeviceToHost);
@@ -607,8 +625,10 @@ bool decode_call(Handle& h, const float* x, int T, const float* logits_in, float
     a.err = s.derr;
     a.err_host = h.err_host;
     a.wait_ns = 1000000000ull;  // a grid barrier normally completes in microseconds
-    for (int i = 0; i < 4; ++i) h.mark(i);  // one kernel: its time is reported as the gate/up stage
+    a.stamps = h.profiling ? s.dstamps : nullptr;
+    for (int i = 0; i < 4; ++i) h.mark(i);
     if (!h.cuda_ok(launch_decode(a, h.n_sm, h.stream), "decode layer")) return false;
+    h.last_decode = true;
     h.dec_seq += 1;
     h.launches += 1;
     h.last_gemm = false;
@@ -625,6 +645,7 @@ bool decode_eligible(const Handle& h, int T, const float* logits_in) {
 
 // Core pipeline on device buffers: x (T, dp), out (T, dp).
 bool run_block(Handle& h, const float* x, int T, const float* logits_in, float* out) {
+    h.last_decode = false;
     if (decode_eligible(h, T, logits_in)) {
         if (!decode_call(h, x, T, logits_in, out)) return false;
         return finish_profile(h);
