@@ -54,9 +54,8 @@ constexpr int kDecThreads = 256;
 constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kScanItems = (1024 + kDecThreads) / kDecThreads;  // items per thread: E + 1 <= 1025 values
 constexpr int kRouterTokGroup = 4;  // tokens per router warp task
-constexpr int kJBlock = 16;         // act rows per gate/up task (one coding block)
+constexpr int kJBlock = 16;         // rows of gate and of up per block of the gate/up stream
 constexpr int kRing = 2;            // weight rows in flight per lane (two CTAs per SM)
-constexpr int kBarriers = 3;
 constexpr int kErrBarrier = 31;
 
 __device__ __forceinline__ uint64_t dec_gtimer() {
@@ -71,12 +70,13 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
 }
 
 // Grid barrier b of this launch: every CTA adds one to the counter, which only
-// grows (launch seq's barrier b completes at (seq * kBarriers + b + 1) *
-// gridDim.x, modulo 2^32). False when the wait ran out (the error is recorded).
+// grows (barrier b completes when it reaches bar_base + (b + 1) * gridDim.x,
+// modulo 2^32; bar_base counts the arrivals of the earlier launches). False when
+// the wait ran out (the error is recorded).
 __device__ bool grid_barrier(const DecodeArgs& a, int b, volatile int* abort_s) {
     __syncthreads();
     if (threadIdx.x == 0) {
-        const uint32_t target = (a.seq * (uint32_t)kBarriers + (uint32_t)b + 1u) * gridDim.x;
+        const uint32_t target = a.bar_base + ((uint32_t)b + 1u) * gridDim.x;
         __threadfence();
         atomicAdd(a.bar, 1u);
         const uint64_t t0 = dec_gtimer();
@@ -290,90 +290,61 @@ __device__ __forceinline__ void chunk_reduce(float (&v)[kChunk], int G, int lane
     for (int o = G >> 3; o >= 1; o >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
 }
 
-// n_items row dots (a multiple of 4) of this lane group, kRing rows in flight:
-// load(p, w) fetches item p's weights; after each chunk, emit(q, v) is called
-// by every lane with v the full dot of item q = chunk start + (lane % G) / (G / 4).
-template <int DT, typename Load, typename Emit>
-__device__ __forceinline__ void gemv_items(int n_items, int G, Load load, Emit emit, bool on, int gl,
-                                           const XSlice& x, int lane) {
-    WSlice<DT> ring[kRing];
-#pragma unroll
-    for (int s = 0; s < kRing; ++s)
-        if (on && s < n_items) load(s, ring[s]);
-    const int spread = G / kChunk;
-#pragma unroll 1
-    for (int c0 = 0; c0 < n_items; c0 += kChunk) {
-        float acc[kChunk];
-#pragma unroll
-        for (int s = 0; s < kChunk; ++s) {
-            acc[s] = on ? ws_dot<DT>(ring[s % kRing], gl, x) : 0.f;
-            if (on && c0 + s + kRing < n_items) load(c0 + s + kRing, ring[s % kRing]);
-        }
-        chunk_reduce(acc, G, lane);
-        emit(c0 + gl / spread, acc[0]);
-    }
-}
-
 __host__ __device__ inline int pow2_at_least(int v) {
     int p = 1;
     while (p < v) p <<= 1;
     return p;
 }
 
-// One gate/up task: rows jb * 16 .. + 16 of gate and up of expert e for one
-// input row (x_row, K values, lane groups of G = pow2(K / 64) >= 4). Item q =
-// 2 * pass + matrix (0 gate, 1 up), pass p covering rows p * (32 / G) + sub of
-// the block; the block's act lands in act_w[16].
-template <int DT>
-__device__ __forceinline__ void gateup_task(const QMat& Gm, const QMat& Um, int e, int jb, int K, int G,
-                                            const uint8_t* x_row, int lane, float* act_w) {
-    const int rpw = 32 / G;
-    const int gl = lane % G, sub = lane / G;
-    const bool on = gl < K / 64;
-    XSlice x;
-    if (on) xs_load(x_row, K, gl, x);
-    const int64_t qs_row = qm_row_qs_bytes(Gm.dtype, Gm.cols), mt_row = qm_row_meta_bytes(Gm.dtype, Gm.cols);
-    const int r0 = jb * kJBlock + sub;
-    const uint8_t* q0 = Gm.qs + (int64_t)e * Gm.qs_estride + (int64_t)r0 * qs_row;
-    const uint8_t* m0 = Gm.meta + (int64_t)e * Gm.meta_estride + (int64_t)r0 * mt_row;
-    const uint8_t* q1 = Um.qs + (int64_t)e * Um.qs_estride + (int64_t)r0 * qs_row;
-    const uint8_t* m1 = Um.meta + (int64_t)e * Um.meta_estride + (int64_t)r0 * mt_row;
-    auto load = [&](int q, WSlice<DT>& w) {
-        const int r = (q >> 1) * rpw;
-        if (q & 1)
-            ws_load<DT>(q1, m1, qs_row, mt_row, r, gl, w);
-        else
-            ws_load<DT>(q0, m0, qs_row, mt_row, r, gl, w);
-    };
-    const int spread = G / kChunk;
-    auto emit = [&](int q, float v) {
-        const float partner = __shfl_xor_sync(0xffffffffu, v, spread);  // the other matrix of the row
-        if ((q & 1) == 0 && gl % spread == 0) act_w[(q >> 1) * rpw + sub] = silu_f(v) * partner;
-    };
-    gemv_items<DT>(2 * (kJBlock / rpw), G, load, emit, on, gl, x, lane);
+// The lane's 64 values [64 gl, 64 gl + 64) of an f32 row, coded in registers
+// (the same 16-value blocks as qx_code16).
+__device__ __forceinline__ void xs_code_f32(const float* row, int gl, XSlice& x) {
+    const float4* src = reinterpret_cast<const float4*>(row + 64 * gl);
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+        float v[16];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const float4 f = src[4 * b + j];
+            v[4 * j] = f.x, v[4 * j + 1] = f.y, v[4 * j + 2] = f.z, v[4 * j + 3] = f.w;
+        }
+        float mx = 0.f, s = 0.f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            mx = fmaxf(mx, fabsf(v[i]));
+            s += v[i];
+        }
+        const float inv = mx > 0.f ? 16383.0f / mx : 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            uint32_t p1 = 0, p0 = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int q = __float2int_rn(v[4 * i + j] * inv);
+                p1 |= (uint32_t)(q >> 7 & 0xFF) << (8 * j);
+                p0 |= (uint32_t)(q & 127) << (8 * j);
+            }
+            x.h[4 * b + i] = p1;
+            x.l[4 * b + i] = p0;
+        }
+        x.sx[b] = mx / 16383.0f;
+        x.s16[b] = s;
+    }
 }
 
-// One down task: rows b * 32 .. + 32 of expert e's down matrix (K values each,
-// groups of G = pow2(K / 64) >= 4 lanes) for one act row (row length ld); y_row
-// receives them. Pass p covers rows p * (32 / G) + sub.
-template <int DT>
-__device__ __forceinline__ void down_task(const QMat& D, int e, int b, int K, int G, const uint8_t* x_row, int ld,
-                                          int lane, float* y_row) {
-    const int rpw = 32 / G;
-    const int gl = lane % G, sub = lane / G;
-    const bool on = gl < K / 64;
-    XSlice x;
-    if (on) xs_load(x_row, ld, gl, x);
-    const int64_t qs_row = qm_row_qs_bytes(D.dtype, D.cols), mt_row = qm_row_meta_bytes(D.dtype, D.cols);
-    const uint8_t* q0 = D.qs + (int64_t)e * D.qs_estride + (int64_t)(b * 32 + sub) * qs_row;
-    const uint8_t* m0 = D.meta + (int64_t)e * D.meta_estride + (int64_t)(b * 32 + sub) * mt_row;
-    auto load = [&](int p, WSlice<DT>& w) { ws_load<DT>(q0, m0, qs_row, mt_row, p * rpw, gl, w); };
-    const int spread = G / kChunk;
-    auto emit = [&](int p, float v) {
-        if (gl % spread == 0) y_row[b * 32 + p * rpw + sub] = v;
-    };
-    gemv_items<DT>(G, G, load, emit, on, gl, x, lane);
-}
+// A warp's position in a stream of GEMV chunks (4 row dots each). The stream
+// runs over units (experts, then the shared expert), the unit's input rows,
+// blocks of rows, and the chunks of a block; `pre` holds each unit's first
+// chunk. Gate/up: blocks of 16 rows of gate and up, chunk c = items 4c..4c+3,
+// item q = 2 * pass + matrix (0 gate, 1 up), pass p covering rows p * (32 / G)
+// + sub of the block. Down: blocks of 32 rows, item q = pass q.
+struct Cursor {
+    int u, i, blk, c;   // unit, its input row, block, chunk of the block
+    int n_i, n_blk, n_c;
+    int G;              // lane group (K of the unit's matrices)
+    int K;
+    bool sh;
+};
 
 // ------------------------------------------------------------ shared state
 // Per-CTA tables of the call's routing (phase B).
@@ -388,9 +359,8 @@ struct DecShared {
     int32_t* u_e;     // [U] unit expert (-1: the shared expert)
     int32_t* u_pos;   // [U] first sorted position (shared: P)
     int32_t* u_n;     // [U] pairs (shared: T)
-    int32_t* gu_pre;  // [U + 1] gate/up task prefix
-    int32_t* dn_pre;  // [U + 1] down task prefix
-    float* act;       // [warps][kJBlock] gate/up act staging
+    int32_t* gu_pre;  // [U + 1] first gate/up chunk of each unit
+    int32_t* dn_pre;  // [U + 1] first down chunk of each unit
 };
 
 // Exclusive scan of v[0..n) in place (n <= kScanItems * blockDim.x); returns the total.
@@ -426,6 +396,115 @@ __device__ __forceinline__ int find_unit(const int32_t* pre, int U, int task) {
     return lo;
 }
 
+// Unit parameters of a cursor (gateup: the gate/up stream, else the down stream).
+__device__ __forceinline__ void cursor_unit(Cursor& c, const DecShared& S, const DecodeArgs& a, bool gateup) {
+    c.sh = S.u_e[c.u] < 0;
+    c.n_i = S.u_n[c.u];
+    if (gateup) {
+        c.K = a.dp;
+        c.n_blk = (c.sh ? a.Fs : a.F) / kJBlock;
+    } else {
+        c.K = c.sh ? a.Fs : a.F;
+        c.n_blk = a.dp / 32;
+    }
+    c.G = pow2_at_least(c.K / 64);
+    c.n_c = c.G / kChunk;
+}
+
+__device__ __forceinline__ void cursor_at(Cursor& c, int chunk, const int32_t* pre, int U, const DecShared& S,
+                                          const DecodeArgs& a, bool gateup) {
+    c.u = find_unit(pre, U, chunk);
+    cursor_unit(c, S, a, gateup);
+    int rel = chunk - pre[c.u];
+    c.c = rel % c.n_c;
+    rel /= c.n_c;
+    c.blk = rel % c.n_blk;
+    c.i = rel / c.n_blk;
+}
+
+__device__ __forceinline__ void cursor_next(Cursor& c, const DecShared& S, const DecodeArgs& a, bool gateup, int U) {
+    if (++c.c < c.n_c) return;
+    c.c = 0;
+    if (++c.blk < c.n_blk) return;
+    c.blk = 0;
+    if (++c.i < c.n_i) return;
+    c.i = 0;
+    if (++c.u < U) cursor_unit(c, S, a, gateup);
+}
+
+// Weights of item s of the cursor's chunk for this lane.
+template <int DT>
+__device__ __forceinline__ void cursor_load(const Cursor& c, int s, const DecShared& S, const DecodeArgs& a,
+                                            bool gateup, int lane, WSlice<DT>& w) {
+    const int gl = lane % c.G, sub = lane / c.G, rpw = 32 / c.G;
+    if (gl >= c.K / 64) return;
+    const int e = c.sh ? 0 : S.u_e[c.u];
+    const QMat* M;
+    int row;
+    if (gateup) {
+        const int q = kChunk * c.c + s;
+        M = (q & 1) ? (c.sh ? &a.su : &a.up) : (c.sh ? &a.sg : &a.gate);
+        row = c.blk * kJBlock + (q >> 1) * rpw + sub;
+    } else {
+        M = c.sh ? &a.sd : &a.down;
+        row = c.blk * 32 + (kChunk * c.c + s) * rpw + sub;
+    }
+    const int64_t qs_row = qm_row_qs_bytes(M->dtype, M->cols), mt_row = qm_row_meta_bytes(M->dtype, M->cols);
+    ws_load<DT>(M->qs + (int64_t)e * M->qs_estride, M->meta + (int64_t)e * M->meta_estride, qs_row, mt_row, row, gl, w);
+}
+
+// A warp's contiguous range [lo, hi) of a chunk stream: 4 row dots per chunk,
+// kRing rows in flight across chunk boundaries; the input slice is (re)made when
+// the unit or its input row changes; emit(cursor, v) gets each chunk's result
+// (v = the full dot of item (lane % G) / (G / 4) of the chunk, in every lane).
+template <int DT, typename MakeX, typename Emit>
+__device__ __forceinline__ void gemv_stream(int lo, int hi, const int32_t* pre, int U, const DecShared& S,
+                                            const DecodeArgs& a, bool gateup, int lane, MakeX make_x, Emit emit) {
+    if (lo >= hi) return;
+    Cursor cc, lc;
+    cursor_at(cc, lo, pre, U, S, a, gateup);
+    lc = cc;
+    int ls = 0;                      // loader: item of its chunk
+    int left = (hi - lo) * kChunk;   // items still to load
+    WSlice<DT> ring[kRing];
+    auto advance_load = [&]() {
+        --left;
+        if (++ls == kChunk) {
+            ls = 0;
+            if (left > 0) cursor_next(lc, S, a, gateup, U);
+        }
+    };
+#pragma unroll
+    for (int r = 0; r < kRing; ++r)
+        if (left > 0) {
+            cursor_load<DT>(lc, ls, S, a, gateup, lane, ring[r]);
+            advance_load();
+        }
+    XSlice x;
+    int xu = -1, xi = -1;
+    for (int chunk = lo; chunk < hi; ++chunk) {
+        const int gl = lane % cc.G;
+        const bool on = gl < cc.K / 64;
+        if (cc.u != xu || cc.i != xi) {
+            if (on) make_x(cc, gl, x);
+            xu = cc.u;
+            xi = cc.i;
+        }
+        float acc[kChunk];
+#pragma unroll
+        for (int s = 0; s < kChunk; ++s) {
+            acc[s] = on ? ws_dot<DT>(ring[s % kRing], gl, x) : 0.f;
+            if (left > 0) {
+                cursor_load<DT>(lc, ls, S, a, gateup, lane, ring[s % kRing]);
+                advance_load();
+            }
+        }
+        chunk_reduce(acc, cc.G, lane);
+        emit(cc, acc[0]);
+        if (chunk + 1 < hi) cursor_next(cc, S, a, gateup, U);
+    }
+}
+
 template <int DT, int PER>
 __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
     extern __shared__ __align__(16) uint8_t dsm[];
@@ -436,10 +515,13 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
     const int T = a.T, E = a.E, k = a.k, P = T * k;
     const int n_warps = gridDim.x * kDecWarps;
     const int gwarp = blockIdx.x * kDecWarps + warp;
+    const bool topk_spread = T > kDecWarps;  // top-k by one warp per token over the grid
+    int nb = 0;                              // grid barriers passed
     if (threadIdx.x == 0) abort_s = 0;
     auto stamp = [&](int i) {
         if (a.stamps && blockIdx.x == 0 && threadIdx.x == 0) a.stamps[i] = dec_gtimer();
     };
+    auto barrier = [&]() { return grid_barrier(a, nb++, &abort_s); };
     stamp(0);
 
     // ---------------------------------------------------------------- phase A
@@ -473,9 +555,9 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
             }
         }
         // the call's x rows as integer input (one thread per 16 values)
-        const int nb = a.dp / 16;
-        for (int i = blockIdx.x * kDecThreads + threadIdx.x; i < T * nb; i += gridDim.x * kDecThreads) {
-            const int t = i / nb, c = (i % nb) * 16;
+        const int nb16 = a.dp / 16;
+        for (int i = blockIdx.x * kDecThreads + threadIdx.x; i < T * nb16; i += gridDim.x * kDecThreads) {
+            const int t = i / nb16, c = (i % nb16) * 16;
             float v[16];
             const float4* src = reinterpret_cast<const float4*>(a.x + (int64_t)t * a.dp + c);
 #pragma unroll
@@ -486,7 +568,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
             qx_code16(v, a.xq + (int64_t)t * qx_row_bytes(a.dp), a.dp, c);
         }
     }
-    if (!grid_barrier(a, 0, &abort_s)) return;
+    if (!barrier()) return;
     stamp(1);
 
     // ---------------------------------------------------------------- phase B
@@ -511,14 +593,28 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
         S.u_n = (int32_t*)take((size_t)Umax * 4);
         S.gu_pre = (int32_t*)take((size_t)(Umax + 1) * 4);
         S.dn_pre = (int32_t*)take((size_t)(Umax + 1) * 4);
-        S.act = (float*)take((size_t)kDecWarps * kJBlock * 4);
     }
     const float* lg_base = a.logits_in ? a.logits_in : a.logits;
     const int lg_ld = a.logits_in ? a.ld_in : a.lg_ld;
-    for (int t = warp; t < T; t += kDecWarps) {
-        int sel_i = 0;
-        topk_warp<PER>(lg_base + (int64_t)t * lg_ld, E, k, a.norm, S.idx + t * k, S.w + t * k, &sel_i);
-        if (lane == 0 && a.has_shared) S.sgate[t] = sigmoid_f(a.logits[(int64_t)t * a.lg_ld + E]);
+    if (topk_spread) {
+        // one warp per token over the grid, then every CTA reads the T * k choices
+        for (int t = gwarp; t < T; t += n_warps) {
+            int sel_i = 0;
+            topk_warp<PER>(lg_base + (int64_t)t * lg_ld, E, k, a.norm, a.idx_out + t * k, a.w_out + t * k, &sel_i);
+            if (lane == 0) a.sgate_out[t] = a.has_shared ? sigmoid_f(a.logits[(int64_t)t * a.lg_ld + E]) : 0.f;
+        }
+        if (!barrier()) return;
+        for (int p = threadIdx.x; p < P; p += kDecThreads) {
+            S.idx[p] = __ldcg(a.idx_out + p);
+            S.w[p] = __ldcg(a.w_out + p);
+        }
+        for (int t = threadIdx.x; t < T; t += kDecThreads) S.sgate[t] = __ldcg(a.sgate_out + t);
+    } else {
+        for (int t = warp; t < T; t += kDecWarps) {
+            int sel_i = 0;
+            topk_warp<PER>(lg_base + (int64_t)t * lg_ld, E, k, a.norm, S.idx + t * k, S.w + t * k, &sel_i);
+            if (lane == 0 && a.has_shared) S.sgate[t] = sigmoid_f(a.logits[(int64_t)t * a.lg_ld + E]);
+        }
     }
     for (int e = threadIdx.x; e < E; e += kDecThreads) S.cnt[e] = 0;
     __syncthreads();
@@ -581,86 +677,73 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
     }
     __syncthreads();
     const int U = n_units_s;
-    // tasks per unit: gate/up (input row, 16-row block), down (input row, 32-row batch);
-    // a unit's tasks are consecutive, the blocks of one input row innermost
-    const int n_batch = a.dp / 32;
+    // chunks per unit: input rows x blocks x (G / 4)
     for (int u = threadIdx.x; u < U; u += kDecThreads) {
-        const int F = S.u_e[u] < 0 ? a.Fs : a.F;
-        S.gu_pre[u] = S.u_n[u] * (F / kJBlock);
-        S.dn_pre[u] = S.u_n[u] * n_batch;
+        const bool sh = S.u_e[u] < 0;
+        const int Fu = sh ? a.Fs : a.F;
+        S.gu_pre[u] = S.u_n[u] * (Fu / kJBlock) * (pow2_at_least(a.dp / 64) / kChunk);
+        S.dn_pre[u] = S.u_n[u] * (a.dp / 32) * (pow2_at_least(Fu / 64) / kChunk);
     }
     __syncthreads();
     const int n_gu = block_excl_scan<Scan>(S.gu_pre, U, scan_tmp);
     const int n_dn = block_excl_scan<Scan>(S.dn_pre, U, scan_tmp);
     if (blockIdx.x == 0) {
         // the call's routing for the host (stats, profiling)
-        for (int p = threadIdx.x; p < P; p += kDecThreads) {
-            a.idx_out[p] = S.idx[p];
-            a.w_out[p] = S.w[p];
-        }
+        if (!topk_spread)
+            for (int p = threadIdx.x; p < P; p += kDecThreads) {
+                a.idx_out[p] = S.idx[p];
+                a.w_out[p] = S.w[p];
+            }
         if (threadIdx.x == 0) {
             *a.n_active_out = U - (a.has_shared ? 1 : 0);
             *a.p_real_out = P;
         }
     }
     __syncthreads();
-
     stamp(2);
+
     // ---------------------------------------------------------------- phase C
-    // tasks in contiguous ranges per warp, so a warp's consecutive tasks mostly
-    // share their input row (loaded once)
+    // act[pair][row] = silu(gate . x) * (up . x) in f32; a warp streams its
+    // contiguous range of chunks (2 rows of gate and up each)
     {
-        const int K = a.dp;
-        const int G = pow2_at_least(K / 64);
-        float* act_w = S.act + warp * kJBlock;
         const int per = (n_gu + n_warps - 1) / n_warps;
-        const int t_lo = gwarp * per, t_hi = min(n_gu, t_lo + per);
-        for (int task = t_lo; task < t_hi; ++task) {
-            const int u = find_unit(S.gu_pre, U, task);
-            const int rel = task - S.gu_pre[u];
-            const bool sh = S.u_e[u] < 0;
-            const int nblk = (sh ? a.Fs : a.F) / kJBlock;
-            const int i = rel / nblk, jb = rel % nblk;
-            const int tok = sh ? i : S.perm[S.u_pos[u] + i] / k;
-            const uint8_t* x_row = a.xq + (int64_t)tok * qx_row_bytes(K);
-            const QMat& Gm = sh ? a.sg : a.gate;
-            const QMat& Um = sh ? a.su : a.up;
-            const int e = sh ? 0 : S.u_e[u];
-            gateup_task<DT>(Gm, Um, e, jb, K, G, x_row, lane, act_w);
-            __syncwarp();
-            if (lane == 0) {
-                float v[kJBlock];
-#pragma unroll
-                for (int jj = 0; jj < kJBlock; ++jj) v[jj] = act_w[jj];
-                const int arow = S.u_pos[u] + i;  // sorted position (shared: P + token)
-                qx_code16(v, a.aq + (int64_t)arow * qx_row_bytes(a.act_ld), a.act_ld, jb * kJBlock);
+        const int lo = gwarp * per, hi = min(n_gu, lo + per);
+        auto make_x = [&](const Cursor& c, int gl, XSlice& x) {
+            const int tok = c.sh ? c.i : S.perm[S.u_pos[c.u] + c.i] / k;
+            xs_load(a.xq + (int64_t)tok * qx_row_bytes(a.dp), a.dp, gl, x);
+        };
+        auto emit = [&](const Cursor& c, float v) {
+            const int gl = lane % c.G, spread = c.G / kChunk;
+            const int q = kChunk * c.c + gl / spread;  // this lane's item of the chunk
+            const float partner = __shfl_xor_sync(0xffffffffu, v, spread);  // the other matrix of the row
+            if ((q & 1) == 0 && gl % spread == 0) {
+                const int row = c.blk * kJBlock + (q >> 1) * (32 / c.G) + lane / c.G;
+                a.act[(int64_t)(S.u_pos[c.u] + c.i) * a.act_ld + row] = silu_f(v) * partner;
             }
-            __syncwarp();
-        }
+        };
+        gemv_stream<DT>(lo, hi, S.gu_pre, U, S, a, true, lane, make_x, emit);
     }
-    if (!grid_barrier(a, 1, &abort_s)) return;
+    if (!barrier()) return;
     stamp(3);
 
     // ---------------------------------------------------------------- phase D
+    // y[pair][row] = down row . act[pair] (act coded per lane as it is first used)
     {
         const int per = (n_dn + n_warps - 1) / n_warps;
-        const int t_lo = gwarp * per, t_hi = min(n_dn, t_lo + per);
-        for (int task = t_lo; task < t_hi; ++task) {
-            const int u = find_unit(S.dn_pre, U, task);
-            const int rel = task - S.dn_pre[u];
-            const bool sh = S.u_e[u] < 0;
-            const int K = sh ? a.Fs : a.F;
-            const int G = pow2_at_least(K / 64);
-            const int i = rel / n_batch, b = rel % n_batch;
-            const int arow = S.u_pos[u] + i;
-            const uint8_t* x_row = a.aq + (int64_t)arow * qx_row_bytes(a.act_ld);
-            const QMat& D = sh ? a.sd : a.down;
-            const int e = sh ? 0 : S.u_e[u];
-            float* y_row = a.y + (int64_t)arow * a.dp;
-            down_task<DT>(D, e, b, K, G, x_row, a.act_ld, lane, y_row);
-        }
+        const int lo = gwarp * per, hi = min(n_dn, lo + per);
+        auto make_x = [&](const Cursor& c, int gl, XSlice& x) {
+            xs_code_f32(a.act + (int64_t)(S.u_pos[c.u] + c.i) * a.act_ld, gl, x);
+        };
+        auto emit = [&](const Cursor& c, float v) {
+            const int gl = lane % c.G, spread = c.G / kChunk;
+            if (gl % spread == 0) {
+                const int row = c.blk * 32 + (kChunk * c.c + gl / spread) * (32 / c.G) + lane / c.G;
+                a.y[(int64_t)(S.u_pos[c.u] + c.i) * a.dp + row] = v;
+            }
+        };
+        gemv_stream<DT>(lo, hi, S.dn_pre, U, S, a, false, lane, make_x, emit);
     }
-    if (!grid_barrier(a, 2, &abort_s)) return;
+    if (!barrier()) return;
     stamp(4);
 
     // ---------------------------------------------------------------- phase E
@@ -672,12 +755,12 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
             float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
             for (int s = 0; s < k; ++s) {
                 const float ws = S.w[t * k + s];
-                const float4 v = *reinterpret_cast<const float4*>(a.y + (int64_t)S.inv[t * k + s] * a.dp + c);
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(a.y + (int64_t)S.inv[t * k + s] * a.dp + c));
                 o.x += ws * v.x, o.y += ws * v.y, o.z += ws * v.z, o.w += ws * v.w;
             }
             if (a.has_shared) {
                 const float g = S.sgate[t];
-                const float4 v = *reinterpret_cast<const float4*>(a.y + (int64_t)(P + t) * a.dp + c);
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(a.y + (int64_t)(P + t) * a.dp + c));
                 o.x += g * v.x, o.y += g * v.y, o.z += g * v.z, o.w += g * v.w;
             }
             *reinterpret_cast<float4*>(a.out + (int64_t)t * a.dp + c) = o;
@@ -699,7 +782,7 @@ size_t decode_smem_bytes(int T, int E, int k) {
     const int P = T * k, Umax = std::min(P, E) + 1;
     auto al = [](size_t b) { return (b + 15) & ~(size_t)15; };
     return al((size_t)E * 4) + al((size_t)(E + 1) * 4) + 4 * al((size_t)P * 4) + al((size_t)T * 4) +
-           3 * al((size_t)Umax * 4) + 2 * al((size_t)(Umax + 1) * 4) + al((size_t)kDecWarps * kJBlock * 4);
+           3 * al((size_t)Umax * 4) + 2 * al((size_t)(Umax + 1) * 4);
 }
 
 }  // namespace
@@ -710,13 +793,15 @@ bool decode_supported(int dtype, int T, int E, int k, int dp, int F, int Fs, int
     if (dtype != AERO_DT_Q4_K && dtype != AERO_DT_Q8_0) return false;
     if (T < 1 || T > kDecodeMaxTokens || k < 1 || k > 32 || E < k || E > 1024) return false;
     if (std::min(T * k, E) + (has_shared ? 1 : 0) > kScanItems * kDecThreads) return false;
-    // lane groups of at least 4 lanes: rows of at least 192 values (4 groups of 64 lanes' values)
+    // lane groups of at least 4 lanes: rows of at least 192 values
     if (dp % 128 || dp > 2048 || dp < 256 || F % 64 || F > 2048 || F < 192) return false;
     if (has_shared && (Fs % 64 || Fs > 2048 || Fs < 192)) return false;
     return true;
 }
 
-cudaError_t launch_decode(const DecodeArgs& args, int n_sm, cudaStream_t s) {
+int decode_barriers(int T) { return T > kDecWarps ? 4 : 3; }
+
+cudaError_t launch_decode(const DecodeArgs& args, int n_sm, cudaStream_t s, int* grid_out) {
     DecodeArgs a = args;
     const void* fn = a.gate.dtype == AERO_DT_Q4_K ? decode_kernel_for<AERO_DT_Q4_K>(a.E)
                                                   : decode_kernel_for<AERO_DT_Q8_0>(a.E);
@@ -744,6 +829,7 @@ cudaError_t launch_decode(const DecodeArgs& args, int n_sm, cudaStream_t s) {
         if (per_sm < 2) return cudaErrorCooperativeLaunchTooLarge;
         if (slot) *slot = Allowed{fn, smem};
     }
+    *grid_out = grid;
     void* params[] = {&a};
     return cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(kDecThreads), params, smem, s);
 }

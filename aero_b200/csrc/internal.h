@@ -116,15 +116,16 @@ struct DecodeArgs {
     float* logits;            // (T, lg_ld) scratch (column E: the shared-gate logit)
     int lg_ld;
     uint8_t* xq;              // T coded x rows (decode_qx_row_bytes(dp) each)
-    uint8_t* aq;              // T * k + T coded act rows (decode_qx_row_bytes(act_ld) each)
-    int32_t* idx_out;         // (T * k) selected experts, written for the host
+    float* act;               // (T * k + T, act_ld) f32 act rows by sorted position (shared expert: T * k + t)
+    int32_t* idx_out;         // (T * k) selected experts (also the exchange of a call whose top-k is spread)
     float* w_out;             // (T * k)
+    float* sgate_out;         // (T) shared-expert gates (exchange of a spread top-k)
     int32_t* n_active_out;    // active experts of the call
     int32_t* p_real_out;      // T * k
     float* y;                 // (T * k + T, dp) f32: each pair's expert output (shared expert: rows T * k + t)
     float* out;               // (T, dp) f32
     uint32_t* bar;            // grid-barrier counter (only grows; zero when the handle's scratch is made)
-    uint32_t seq;             // launches made on this counter before this one
+    uint32_t bar_base;        // arrivals on it from the earlier launches
     int32_t* err;
     int32_t* err_host;
     uint64_t wait_ns;
@@ -132,7 +133,10 @@ struct DecodeArgs {
 };
 bool decode_supported(int dtype, int T, int E, int k, int dp, int F, int Fs, int has_shared);
 int64_t decode_qx_row_bytes(int K);
-cudaError_t launch_decode(const DecodeArgs& a, int n_sm, cudaStream_t s);
+// Grid barriers a launch of T tokens passes (each CTA adds one arrival per barrier).
+int decode_barriers(int T);
+// Launches the kernel on *grid_out CTAs.
+cudaError_t launch_decode(const DecodeArgs& a, int n_sm, cudaStream_t s, int* grid_out);
 
 // Expert-parallel exchange (ep.cu). Rank r owns experts [begin[r], begin[r+1]).
 constexpr int kEpMaxRanks = 64;

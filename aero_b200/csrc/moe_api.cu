@@ -61,8 +61,8 @@ struct Scratch {
     size_t gemm_ws_bytes = 0;
     int gemv_cap = 0;
     // fused decode path: coded x and act rows, grid-barrier counter and error word
-    uint8_t *dxq = nullptr, *daq = nullptr;
-    float* dy = nullptr;
+    uint8_t* dxq = nullptr;
+    float *dact = nullptr, *dy = nullptr;
     uint32_t* dbar = nullptr;
     int32_t* derr = nullptr;
     uint64_t* dstamps = nullptr;  // phase stamps of the fused decode kernel (profiling)
@@ -125,7 +125,7 @@ struct Handle {
     int32_t* err_host = nullptr;
     uint64_t peer_wait_ns = 5000000000ull;  // AERO_CUDA_OPT_PEER_WAIT_MS
     bool decode_enabled = true;             // AERO_CUDA_OPT_DECODE_FUSED
-    uint32_t dec_seq = 0;                   // fused decode launches on the current barrier counter
+    uint32_t dec_bar = 0;                   // arrivals on the fused decode kernel's barrier counter so far
     // prefill (tcgen05 grouped GEMM) path
     bool gemm_ok = false;     // layer shape/type supports it
     int gemm_min_tokens = 64; // calls with at least this many tokens use it
@@ -313,7 +313,7 @@ bool ensure_scratch(Handle& h, int T) {
     const int dT = std::min(cap, kDecodeMaxTokens);
     const bool dec = h.dtype != AERO_DT_F32;
     const size_t o_dxq = take(dec ? (size_t)dT * decode_qx_row_bytes(h.dp) : 0);
-    const size_t o_daq = take(dec ? (size_t)(dT * h.k + dT) * decode_qx_row_bytes(h.act_ld) : 0);
+    const size_t o_dact = take(dec ? (size_t)(dT * h.k + dT) * h.act_ld * 4 : 0);
     const size_t o_dy = take(dec ? (size_t)(dT * h.k + dT) * h.dp * 4 : 0);
     const size_t o_dbar = take(8);
     const size_t o_dst = take(6 * 8);
@@ -356,12 +356,12 @@ bool ensure_scratch(Handle& h, int T) {
     s.ep_bad = (int32_t*)(b + o_bad);
     s.tc_err = (int32_t*)(b + o_tce);
     s.dxq = dec ? (uint8_t*)(b + o_dxq) : nullptr;
-    s.daq = dec ? (uint8_t*)(b + o_daq) : nullptr;
+    s.dact = dec ? (float*)(b + o_dact) : nullptr;
     s.dy = dec ? (float*)(b + o_dy) : nullptr;
     s.dbar = (uint32_t*)(b + o_dbar);
     s.derr = (int32_t*)(b + o_dbar + 4);
     s.dstamps = (uint64_t*)(b + o_dst);
-    h.dec_seq = 0;  // the new scratch is cleared below: the barrier counter starts at zero
+    h.dec_bar = 0;  // the new scratch is cleared below: the barrier counter starts at zero
     s.lg_part = part_rows ? (float*)(b + o_lgp) : nullptr;
     s.lg_part_rows = part_rows;
     s.dwork = b + o_dw;
@@ -613,7 +613,8 @@ bool decode_call(Handle& h, const float* x, int T, const float* logits_in, float
     a.logits = s.logits;
     a.lg_ld = h.lg_ld;
     a.xq = s.dxq;
-    a.aq = s.daq;
+    a.act = s.dact;
+    a.sgate_out = s.sgate;
     a.idx_out = s.idx;
     a.w_out = s.w;
     a.n_active_out = s.n_active;
@@ -621,15 +622,16 @@ bool decode_call(Handle& h, const float* x, int T, const float* logits_in, float
     a.y = s.dy;
     a.out = out;
     a.bar = s.dbar;
-    a.seq = h.dec_seq;
+    a.bar_base = h.dec_bar;
     a.err = s.derr;
     a.err_host = h.err_host;
     a.wait_ns = 1000000000ull;  // a grid barrier normally completes in microseconds
     a.stamps = h.profiling ? s.dstamps : nullptr;
     for (int i = 0; i < 4; ++i) h.mark(i);
-    if (!h.cuda_ok(launch_decode(a, h.n_sm, h.stream), "decode layer")) return false;
+    int grid = 0;
+    if (!h.cuda_ok(launch_decode(a, h.n_sm, h.stream, &grid), "decode layer")) return false;
     h.last_decode = true;
-    h.dec_seq += 1;
+    h.dec_bar += (uint32_t)grid * (uint32_t)decode_barriers(T);
     h.launches += 1;
     h.last_gemm = false;
     h.last_shared_rows = h.has_shared ? T : 0;
@@ -666,7 +668,7 @@ bool check_pipeline(Handle& h) {
             return h.cuda_ok(cudaGetLastError(), "error flag");
         if (code != 0) {
             cudaMemset(h.sc.dbar, 0, 8);
-            h.dec_seq = 0;
+            h.dec_bar = 0;
             return h.fail("decode grid barrier wait expired (code %d); the call's output is invalid", code);
         }
     }
@@ -698,7 +700,7 @@ bool take_async_error(Handle& h) {
     if (h.sc.base) {
         cudaMemsetAsync(h.sc.tc_err, 0, 4, h.stream);
         cudaMemsetAsync(h.sc.dbar, 0, 8, h.stream);  // barrier counter and decode error word
-        h.dec_seq = 0;
+        h.dec_bar = 0;
     }
     if (h.gb_ready) cudaMemsetAsync(h.gb.err, 0, 4, h.stream);
     return h.fail("a bounded device wait of an earlier call on this handle gave up (code %d): that call's output is "
@@ -1253,7 +1255,7 @@ int aero_cuda_moe_status(void* handle) {
     if (h->gb_ready) cudaMemset(h->gb.err, 0, 4);
     if (dev[3] != 0) {
         cudaMemset(h->sc.dbar, 0, 8);
-        h->dec_seq = 0;
+        h->dec_bar = 0;
     }
     if (!h->cuda_ok(cudaGetLastError(), "status")) return -1;
     return code;
