@@ -341,9 +341,12 @@ __device__ __forceinline__ void xs_code_f32(const float* row, int gl, XSlice& x)
 struct Cursor {
     int u, i, blk, c;   // unit, its input row, block, chunk of the block
     int n_i, n_blk, n_c;
-    int G;              // lane group (K of the unit's matrices)
-    int K;
+    int lg;             // log2 of the lane group G = pow2(K / 64)
+    int k64;            // K / 64: lanes of a group that hold values
     bool sh;
+    // the unit's expert matrices (gate/up: 0 gate, 1 up; down: 0) and row strides
+    const uint8_t *q0, *m0, *q1, *m1;
+    int64_t qs_row, mt_row;
 };
 
 // ------------------------------------------------------------ shared state
@@ -396,19 +399,38 @@ __device__ __forceinline__ int find_unit(const int32_t* pre, int U, int task) {
     return lo;
 }
 
+__host__ __device__ inline int log2_pow2(int p) {
+    int l = 0;
+    while ((1 << l) < p) ++l;
+    return l;
+}
+
 // Unit parameters of a cursor (gateup: the gate/up stream, else the down stream).
 __device__ __forceinline__ void cursor_unit(Cursor& c, const DecShared& S, const DecodeArgs& a, bool gateup) {
     c.sh = S.u_e[c.u] < 0;
     c.n_i = S.u_n[c.u];
+    const int e = c.sh ? 0 : S.u_e[c.u];
+    int K;
+    const QMat *A, *B;
     if (gateup) {
-        c.K = a.dp;
+        K = a.dp;
         c.n_blk = (c.sh ? a.Fs : a.F) / kJBlock;
+        A = c.sh ? &a.sg : &a.gate;
+        B = c.sh ? &a.su : &a.up;
     } else {
-        c.K = c.sh ? a.Fs : a.F;
+        K = c.sh ? a.Fs : a.F;
         c.n_blk = a.dp / 32;
+        A = B = c.sh ? &a.sd : &a.down;
     }
-    c.G = pow2_at_least(c.K / 64);
-    c.n_c = c.G / kChunk;
+    c.k64 = K / 64;
+    c.lg = log2_pow2(c.k64);
+    c.n_c = (1 << c.lg) / kChunk;
+    c.q0 = A->qs + (int64_t)e * A->qs_estride;
+    c.m0 = A->meta + (int64_t)e * A->meta_estride;
+    c.q1 = B->qs + (int64_t)e * B->qs_estride;
+    c.m1 = B->meta + (int64_t)e * B->meta_estride;
+    c.qs_row = qm_row_qs_bytes(A->dtype, A->cols);
+    c.mt_row = qm_row_meta_bytes(A->dtype, A->cols);
 }
 
 __device__ __forceinline__ void cursor_at(Cursor& c, int chunk, const int32_t* pre, int U, const DecShared& S,
@@ -434,23 +456,20 @@ __device__ __forceinline__ void cursor_next(Cursor& c, const DecShared& S, const
 
 // Weights of item s of the cursor's chunk for this lane.
 template <int DT>
-__device__ __forceinline__ void cursor_load(const Cursor& c, int s, const DecShared& S, const DecodeArgs& a,
-                                            bool gateup, int lane, WSlice<DT>& w) {
-    const int gl = lane % c.G, sub = lane / c.G, rpw = 32 / c.G;
-    if (gl >= c.K / 64) return;
-    const int e = c.sh ? 0 : S.u_e[c.u];
-    const QMat* M;
-    int row;
+__device__ __forceinline__ void cursor_load(const Cursor& c, int s, bool gateup, int lane, WSlice<DT>& w) {
+    const int gl = lane & ((1 << c.lg) - 1), sub = lane >> c.lg;
+    if (gl >= c.k64) return;
+    const int q = kChunk * c.c + s;
+    const int shr = 5 - c.lg;  // log2 of the rows a pass covers
     if (gateup) {
-        const int q = kChunk * c.c + s;
-        M = (q & 1) ? (c.sh ? &a.su : &a.up) : (c.sh ? &a.sg : &a.gate);
-        row = c.blk * kJBlock + (q >> 1) * rpw + sub;
+        const int row = c.blk * kJBlock + ((q >> 1) << shr) + sub;
+        if (q & 1)
+            ws_load<DT>(c.q1, c.m1, c.qs_row, c.mt_row, row, gl, w);
+        else
+            ws_load<DT>(c.q0, c.m0, c.qs_row, c.mt_row, row, gl, w);
     } else {
-        M = c.sh ? &a.sd : &a.down;
-        row = c.blk * 32 + (kChunk * c.c + s) * rpw + sub;
+        ws_load<DT>(c.q0, c.m0, c.qs_row, c.mt_row, c.blk * 32 + (q << shr) + sub, gl, w);
     }
-    const int64_t qs_row = qm_row_qs_bytes(M->dtype, M->cols), mt_row = qm_row_meta_bytes(M->dtype, M->cols);
-    ws_load<DT>(M->qs + (int64_t)e * M->qs_estride, M->meta + (int64_t)e * M->meta_estride, qs_row, mt_row, row, gl, w);
 }
 
 // A warp's contiguous range [lo, hi) of a chunk stream: 4 row dots per chunk,
@@ -477,14 +496,14 @@ __device__ __forceinline__ void gemv_stream(int lo, int hi, const int32_t* pre, 
 #pragma unroll
     for (int r = 0; r < kRing; ++r)
         if (left > 0) {
-            cursor_load<DT>(lc, ls, S, a, gateup, lane, ring[r]);
+            cursor_load<DT>(lc, ls, gateup, lane, ring[r]);
             advance_load();
         }
     XSlice x;
     int xu = -1, xi = -1;
     for (int chunk = lo; chunk < hi; ++chunk) {
-        const int gl = lane % cc.G;
-        const bool on = gl < cc.K / 64;
+        const int gl = lane & ((1 << cc.lg) - 1);
+        const bool on = gl < cc.k64;
         if (cc.u != xu || cc.i != xi) {
             if (on) make_x(cc, gl, x);
             xu = cc.u;
@@ -495,11 +514,11 @@ __device__ __forceinline__ void gemv_stream(int lo, int hi, const int32_t* pre, 
         for (int s = 0; s < kChunk; ++s) {
             acc[s] = on ? ws_dot<DT>(ring[s % kRing], gl, x) : 0.f;
             if (left > 0) {
-                cursor_load<DT>(lc, ls, S, a, gateup, lane, ring[s % kRing]);
+                cursor_load<DT>(lc, ls, gateup, lane, ring[s % kRing]);
                 advance_load();
             }
         }
-        chunk_reduce(acc, cc.G, lane);
+        chunk_reduce(acc, 1 << cc.lg, lane);
         emit(cc, acc[0]);
         if (chunk + 1 < hi) cursor_next(cc, S, a, gateup, U);
     }
@@ -713,11 +732,11 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
             xs_load(a.xq + (int64_t)tok * qx_row_bytes(a.dp), a.dp, gl, x);
         };
         auto emit = [&](const Cursor& c, float v) {
-            const int gl = lane % c.G, spread = c.G / kChunk;
-            const int q = kChunk * c.c + gl / spread;  // this lane's item of the chunk
-            const float partner = __shfl_xor_sync(0xffffffffu, v, spread);  // the other matrix of the row
-            if ((q & 1) == 0 && gl % spread == 0) {
-                const int row = c.blk * kJBlock + (q >> 1) * (32 / c.G) + lane / c.G;
+            const int gl = lane & ((1 << c.lg) - 1), ls = c.lg - 2;  // log2 of the lanes sharing an item
+            const int q = kChunk * c.c + (gl >> ls);                // this lane's item of the chunk
+            const float partner = __shfl_xor_sync(0xffffffffu, v, 1 << ls);  // the other matrix of the row
+            if ((q & 1) == 0 && (gl & ((1 << ls) - 1)) == 0) {
+                const int row = c.blk * kJBlock + ((q >> 1) << (5 - c.lg)) + (lane >> c.lg);
                 a.act[(int64_t)(S.u_pos[c.u] + c.i) * a.act_ld + row] = silu_f(v) * partner;
             }
         };
@@ -735,9 +754,9 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
             xs_code_f32(a.act + (int64_t)(S.u_pos[c.u] + c.i) * a.act_ld, gl, x);
         };
         auto emit = [&](const Cursor& c, float v) {
-            const int gl = lane % c.G, spread = c.G / kChunk;
-            if (gl % spread == 0) {
-                const int row = c.blk * 32 + (kChunk * c.c + gl / spread) * (32 / c.G) + lane / c.G;
+            const int gl = lane & ((1 << c.lg) - 1), ls = c.lg - 2;
+            if ((gl & ((1 << ls) - 1)) == 0) {
+                const int row = c.blk * 32 + ((kChunk * c.c + (gl >> ls)) << (5 - c.lg)) + (lane >> c.lg);
                 a.y[(int64_t)(S.u_pos[c.u] + c.i) * a.dp + row] = v;
             }
         };
