@@ -635,66 +635,111 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
             if (lane == 0 && a.has_shared) S.sgate[t] = sigmoid_f(a.logits[(int64_t)t * a.lg_ld + E]);
         }
     }
-    for (int e = threadIdx.x; e < E; e += kDecThreads) S.cnt[e] = 0;
     __syncthreads();
-    for (int p = threadIdx.x; p < P; p += kDecThreads) atomicAdd(&S.cnt[S.idx[p]], 1);
-    __syncthreads();
-    // expert offsets (exclusive prefix of the counts)
-    for (int e = threadIdx.x; e < E; e += kDecThreads) S.off[e] = S.cnt[e];
-    __syncthreads();
-    block_excl_scan<Scan>(S.off, E, scan_tmp);
-    if (threadIdx.x == 0) S.off[E] = P;
-    // the active units: experts in ascending order, then the shared expert
-    {
-        int in[kScanItems], out[kScanItems], tot;
+    if (P <= 32) {
+        // one warp: the pairs sorted by (expert, pair) with a bitonic exchange
+        // across the lanes; lane = sorted position
+        if (warp == 0) {
+            const bool valid = lane < P;
+            uint32_t key = valid ? ((uint32_t)S.idx[lane] << 5) | (uint32_t)lane : 0xFFFFFFFFu;
 #pragma unroll
-        for (int j = 0; j < kScanItems; ++j) {
-            const int e = kScanItems * threadIdx.x + j;
-            in[j] = e < E && S.cnt[e] > 0 ? 1 : 0;
-        }
-        Scan(scan_tmp).ExclusiveSum(in, out, tot);
+            for (int size = 2; size <= 32; size <<= 1)
 #pragma unroll
-        for (int j = 0; j < kScanItems; ++j) {
-            const int e = kScanItems * threadIdx.x + j;
-            if (in[j]) {
-                S.u_e[out[j]] = e;
-                S.u_pos[out[j]] = S.off[e];
-                S.u_n[out[j]] = S.cnt[e];
-            }
-        }
-        if (threadIdx.x == 0) {
-            int U = tot;
-            if (a.has_shared) {
-                S.u_e[U] = -1;
-                S.u_pos[U] = P;
-                S.u_n[U] = T;
-                ++U;
-            }
-            n_units_s = U;
-        }
-    }
-    __syncthreads();
-    // stable scatter (warp 0): pairs in order, equal experts ranked by __match_any_sync
-    for (int e = threadIdx.x; e < E; e += kDecThreads) S.cnt[e] = S.off[e];  // cursor
-    __syncthreads();
-    if (warp == 0) {
-        for (int base = 0; base < P; base += 32) {
-            const int p = base + lane;
-            const bool valid = p < P;
-            const int e = valid ? S.idx[p] : -1 - lane;
-            const unsigned peers = __match_any_sync(0xffffffffu, e);
-            const int rank = __popc(peers & ((1u << lane) - 1u));
-            const int pos = valid ? S.cnt[e] + rank : 0;
-            __syncwarp();
+                for (int stride = size >> 1; stride > 0; stride >>= 1) {
+                    const uint32_t other = __shfl_xor_sync(0xffffffffu, key, stride);
+                    const bool keep_min = ((lane & stride) == 0) == ((lane & size) == 0);
+                    key = keep_min ? min(key, other) : max(key, other);
+                }
+            const int pr = (int)(key & 31u), e = (int)(key >> 5);
             if (valid) {
-                S.perm[pos] = p;
-                S.inv[p] = pos;
-                if ((peers >> lane) == 1u) S.cnt[e] = pos + 1;
+                S.perm[lane] = pr;
+                S.inv[pr] = lane;
             }
-            __syncwarp();
+            const int prev_e = __shfl_up_sync(0xffffffffu, e, 1);
+            const bool start = valid && (lane == 0 || prev_e != e);
+            const unsigned starts = __ballot_sync(0xffffffffu, start);
+            if (start) {
+                const int u = __popc(starts & ((1u << lane) - 1u));
+                const unsigned later = starts & ~((2u << lane) - 1u);
+                const int end = later ? __ffs(later) - 1 : P;
+                S.u_e[u] = e;
+                S.u_pos[u] = lane;
+                S.u_n[u] = end - lane;
+            }
+            if (lane == 0) {
+                int U = __popc(starts);
+                if (a.has_shared) {
+                    S.u_e[U] = -1;
+                    S.u_pos[U] = P;
+                    S.u_n[U] = T;
+                    ++U;
+                }
+                n_units_s = U;
+            }
         }
+        __syncthreads();
+    } else {
+        for (int e = threadIdx.x; e < E; e += kDecThreads) S.cnt[e] = 0;
+        __syncthreads();
+        for (int p = threadIdx.x; p < P; p += kDecThreads) atomicAdd(&S.cnt[S.idx[p]], 1);
+        __syncthreads();
+        // expert offsets (exclusive prefix of the counts)
+        for (int e = threadIdx.x; e < E; e += kDecThreads) S.off[e] = S.cnt[e];
+        __syncthreads();
+        block_excl_scan<Scan>(S.off, E, scan_tmp);
+        if (threadIdx.x == 0) S.off[E] = P;
+        // the active units: experts in ascending order, then the shared expert
+        {
+            int in[kScanItems], out[kScanItems], tot;
+    #pragma unroll
+            for (int j = 0; j < kScanItems; ++j) {
+                const int e = kScanItems * threadIdx.x + j;
+                in[j] = e < E && S.cnt[e] > 0 ? 1 : 0;
+            }
+            Scan(scan_tmp).ExclusiveSum(in, out, tot);
+    #pragma unroll
+            for (int j = 0; j < kScanItems; ++j) {
+                const int e = kScanItems * threadIdx.x + j;
+                if (in[j]) {
+                    S.u_e[out[j]] = e;
+                    S.u_pos[out[j]] = S.off[e];
+                    S.u_n[out[j]] = S.cnt[e];
+                }
+            }
+            if (threadIdx.x == 0) {
+                int U = tot;
+                if (a.has_shared) {
+                    S.u_e[U] = -1;
+                    S.u_pos[U] = P;
+                    S.u_n[U] = T;
+                    ++U;
+                }
+                n_units_s = U;
+            }
+        }
+        __syncthreads();
+        // stable scatter (warp 0): pairs in order, equal experts ranked by __match_any_sync
+        for (int e = threadIdx.x; e < E; e += kDecThreads) S.cnt[e] = S.off[e];  // cursor
+        __syncthreads();
+        if (warp == 0) {
+            for (int base = 0; base < P; base += 32) {
+                const int p = base + lane;
+                const bool valid = p < P;
+                const int e = valid ? S.idx[p] : -1 - lane;
+                const unsigned peers = __match_any_sync(0xffffffffu, e);
+                const int rank = __popc(peers & ((1u << lane) - 1u));
+                const int pos = valid ? S.cnt[e] + rank : 0;
+                __syncwarp();
+                if (valid) {
+                    S.perm[pos] = p;
+                    S.inv[p] = pos;
+                    if ((peers >> lane) == 1u) S.cnt[e] = pos + 1;
+                }
+                __syncwarp();
+            }
+        }
+        __syncthreads();
     }
-    __syncthreads();
     const int U = n_units_s;
     // chunks per unit: input rows x blocks x (G / 4)
     for (int u = threadIdx.x; u < U; u += kDecThreads) {
