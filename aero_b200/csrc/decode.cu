@@ -1,35 +1,38 @@
 // Decode (calls of up to 32 tokens): the whole MoE layer in one cooperative
-// launch, five phases separated by three grid barriers.
+// launch (two CTAs per SM), five phases separated by grid barriers.
 //
 //   A  router logits (f32, x . W_r + bias, plus the shared-gate column) and the
-//      call's x rows coded as integer input                         | barrier 1
-//   B  in every CTA, from the logits: top-k per token (src/moe.cpp:26-66, the
-//      same selection as the top-k kernel) and the dispatch of the T*k pairs
-//      into expert segments (counting sort, stable in (token, slot) order),
-//      kept in shared memory
-//   C  gate/up GEMVs over the active experts and the shared expert: act =
-//      silu(gate . x) * (up . x) per (pair, 16-row block), coded as integer
-//      input for the down product                                    | barrier 2
-//   D  down GEMVs per (pair, 32-row batch): y[pair] in f32            | barrier 3
+//      call's x rows coded as integer input                         | barrier
+//   B  top-k per token (src/moe.cpp:26-66, the same selection as the top-k
+//      kernel): in every CTA for calls of up to 8 tokens, else one warp per
+//      token over the grid followed by a barrier; then, in every CTA, the
+//      dispatch of the T*k pairs into expert segments (stable in (token, slot)
+//      order: one warp's bitonic sort for up to 32 pairs, a counting sort
+//      above), kept in shared memory
+//   C  gate/up GEMVs over the active experts and the shared expert:
+//      act[pair][row] = silu(gate . x) * (up . x) in f32       | barrier
+//   D  down GEMVs: y[pair][row] = down row . act[pair], act coded as integer
+//      input by each lane for its own 64 values                 | barrier
 //   E  combine: out[t] = sum over slots in order of w * y + sgate * y_shared
 //      (src/moe.cpp:68-120)
 //
 // GEMV lanes. A lane owns 64 consecutive values of a row: for Q4_K the 32 code
 // bytes of sub-blocks 2g and 2g+1 of one super-block plus that super-block's
-// 16-byte header (one header load and one scale decode per row and lane);
-// for Q8_0 two whole 32-value blocks and their two fp16 scales. Rows of K values
-// take a group of G = pow2(K/64) lanes; a warp covers 32/G rows per pass. A warp
-// task takes G passes (one row per lane group per pass) with the next passes'
-// weights in flight (a ring of kRing loads), accumulating one partial per pass
-// in each lane; a reduce-scatter across the group then leaves every lane with
-// the full sum of one pass (G - 1 shuffles per lane for G rows, instead of
-// log2 G per row). Only the selected experts' blocks are read from HBM, once
-// per pair (a pair's token re-reads its expert's rows from L2 when the expert
-// has several tokens); accumulation is f32.
+// 16-byte header (one header load and one scale decode per row and lane); for
+// Q8_0 two whole 32-value blocks and their two fp16 scales. Rows of K values
+// take a group of G = pow2(K/64) >= 4 lanes; a warp covers 32/G rows per pass.
+// Phases C and D are streams of chunks of 4 row dots (a unit = an expert with
+// its pairs, or the shared expert; per unit its input rows, blocks of rows, and
+// the chunks of a block): each warp takes a contiguous range of chunks, keeps
+// kRing rows' weights in flight across chunk boundaries, accumulates one
+// partial per row dot, and a partial reduce-scatter across the lane group
+// leaves each lane with the full sum of one row dot of the chunk. Only the
+// selected experts' blocks are read from HBM, once per pair (an expert's second
+// token re-reads its rows from L2); accumulation is f32.
 //
-// Integer input (x and act rows), per 16 values: a 15-bit code split into two
-// int8 planes (v ~= sx * (128 q1 + q0), |128 q1 + q0| <= 16383) and the exact f32
-// sum of the 16 values (the Q4_K min term). A lane's 64 values are four blocks:
+// Integer input (x and act), per 16 values: a 15-bit code split into two int8
+// planes (v ~= sx * (128 q1 + q0), |128 q1 + q0| <= 16383) and the exact f32 sum
+// of the 16 values (the Q4_K min term). A lane's 64 values are four blocks:
 // sum(q x) is two chains of dp4a over the raw code bytes per block, and the
 // per-sub-block factorisation of the quantised dot (src/kernels.cpp:78-84,
 // 123-156) applies the scales once per block:
