@@ -149,6 +149,12 @@ def layer_bytes(spec):
 # names the capture it comes from; a kernel changed since its capture has no
 # entry (traffic: null) until it is captured again.
 TRAFFIC = {
+    # profiles/traffic_c5_8192tok.md (ncu launch list of bench.py --profile --workload c5 --tokens 8192)
+    ("c5_prefill_q4_k_shared", "grouped_gemm_gate_up"): (1052660224, "profiles/traffic_c5_8192tok.md"),
+    ("c5_prefill_q4_k_shared", "grouped_gemm_down"): (707158528, "profiles/traffic_c5_8192tok.md"),
+    # profiles/decode_kernel_c1.md, profiles/decode_kernel_c3.md (one call of the fused decode kernel)
+    ("c1_decode_q8_0", "decode_layer"): (41298176, "profiles/decode_kernel_c1.md"),
+    ("c3_decode_q4_k_shared", "decode_layer"): (539513856, "profiles/decode_kernel_c3.md"),
 }
 
 
@@ -602,7 +608,8 @@ def decode_records(args, dev, stream, pk) -> dict:
         gbs = nbytes / (ms / 1000.0) / 1e9
         out[key] = {"workload": wl.name, "tokens_per_call": T, "calls_per_step": wl.calls, "ms_per_step": ms,
                     "us_per_call": 1000.0 * ms / wl.calls, "tokens_per_s": T * wl.calls / (ms / 1000.0),
-                    "hbm_bytes_per_step": nbytes, "achieved_gbs": gbs, "frac_of_hbm": gbs / pk["hbm_gbs"]}
+                    "hbm_bytes_per_step": nbytes, "achieved_gbs": gbs, "frac_of_hbm": gbs / pk["hbm_gbs"],
+                    "traffic_per_call": traffic_record(wl.name, "decode_layer")}
         L.close()
         del x, o
     return out
