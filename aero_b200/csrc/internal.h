@@ -63,6 +63,13 @@ cudaError_t launch_topk(const float* logits, int ld, int T, int E, int k, int no
                         float* w, float* sgate, const float* x, QInput xq, cudaStream_t s,
                         SingleDispatch one = SingleDispatch{});
 
+// Resident-subset layers: idx[0..n) global expert ids -> slot[id] (the
+// expert's position in the layer's planes). An id whose slot is -1 records
+// kErrNotResident in *err (and *err_host when non-null) and maps to slot 0.
+constexpr int kErrNotResident = 41;
+cudaError_t launch_resident_remap(int32_t* idx, int n, const int32_t* slot, int32_t* err, int32_t* err_host,
+                                  cudaStream_t s);
+
 // Dispatch: expert-contiguous permutation of the T*k pairs. Writes offsets[E+1],
 // perm[P] (sorted position -> pair), inv[P] (pair -> sorted position), the active
 // list act_e[n_active] / act_off[n_active+1] (segment starts, in sorted

@@ -96,6 +96,11 @@ struct Handle {
     std::mutex mu;
     int d = 0, dp = 0, E = 0, k = 0, F = 0, Fp = 0, Fs = 0, Fsp = 0, norm = 1, has_shared = 0;
     int e_begin = 0, e_end = 0, has_router = 0, act_ld = 0;
+    // resident subset: the planes hold the experts listed at open; slot[E] maps
+    // a global id to its plane position (-1: not resident). Routed ids are
+    // remapped after top-k, so dispatch and the expert products see slots.
+    bool subset = false;
+    int32_t* slot = nullptr;
     int dtype = 0, sh_dtype = 0;
     QMat gate{}, up{}, down{}, sg{}, su{}, sd{};
     float* router_ext = nullptr;  // (E + 1, dp): row E = shared gate input (or zeros)
@@ -431,7 +436,7 @@ bool route_stage(Handle& h, const float* x, int T, const float* logits_in, bool 
     QInput xq = qx ? s.xq : QInput{};
     // a single token's dispatch comes from the top-k pass (expert_stage skips the sort)
     SingleDispatch one{};
-    if (T == 1) {
+    if (T == 1 && !h.subset) {
         one.perm = s.perm;
         one.inv = s.inv;
         one.act_e = s.act_e;
@@ -443,6 +448,11 @@ bool route_stage(Handle& h, const float* x, int T, const float* logits_in, bool 
                    "top-k"))
         return false;
     h.launches += 1;
+    if (h.subset) {
+        if (!h.cuda_ok(launch_resident_remap(s.idx, T * h.k, h.slot, s.derr, h.err_host, st), "resident slots"))
+            return false;
+        h.launches += 1;
+    }
     h.mark(2);
     return true;
 }
@@ -459,7 +469,7 @@ bool expert_stage(Handle& h, const void* x, bool x_f16, int T, int Tsh, bool ski
     const int P = T * h.k;
     const int n_buckets = skip_slots ? h.E + 1 : h.E;
     // (a single token's pairs were laid out by route_stage's top-k pass)
-    if (T != 1 || skip_slots) {
+    if (T != 1 || skip_slots || h.subset) {
         if (!h.cuda_ok(launch_dispatch(s.idx, P, n_buckets, s.offsets, s.perm, s.inv, s.act_e, s.act_off, s.n_active,
                                        s.dwork, st, h.E),
                        "dispatch"))
@@ -669,6 +679,10 @@ bool check_pipeline(Handle& h) {
         if (code != 0) {
             cudaMemset(h.sc.dbar, 0, 8);
             h.dec_bar = 0;
+            if (code == kErrNotResident)
+                return h.fail("the routing selected an expert this resident-subset layer does not hold (code %d); "
+                              "the call's output is invalid",
+                              code);
             return h.fail("decode grid barrier wait expired (code %d); the call's output is invalid", code);
         }
     }
@@ -703,6 +717,10 @@ bool take_async_error(Handle& h) {
         h.dec_bar = 0;
     }
     if (h.gb_ready) cudaMemsetAsync(h.gb.err, 0, 4, h.stream);
+    if (code == kErrNotResident)
+        return h.fail("an earlier call on this handle routed to an expert this resident-subset layer does not hold "
+                      "(code %d): that call's output is invalid; this call was not run",
+                      code);
     return h.fail("a bounded device wait of an earlier call on this handle gave up (code %d): that call's output is "
                   "invalid; this call was not run",
                   code);
@@ -807,6 +825,27 @@ Handle* open_desc(const aero_cuda_moe_desc* d, std::string* why) {
     h->e_end = d->expert_end;
     if (h->e_begin == 0 && h->e_end == 0) h->e_end = h->E;
     if (h->e_begin < 0 || h->e_end > h->E || h->e_begin >= h->e_end) return bad("bad expert range");
+    // resident subset: the expert tensors hold n_resident experts; their slots
+    // are [0, n_resident) in the planes (the range bookkeeping below)
+    int src_experts = h->E;
+    std::vector<int32_t> slot_host;
+    if (d->n_resident < 0) return bad("n_resident < 0");
+    if (d->n_resident > 0) {
+        if (d->expert_begin != 0 || d->expert_end != 0) return bad("a resident subset takes no expert range");
+        if (!d->resident_ids) return bad("n_resident > 0 needs resident_ids");
+        if (d->n_resident > h->E) return bad("n_resident > n_expert");
+        slot_host.assign((size_t)h->E, -1);
+        for (int i = 0; i < d->n_resident; ++i) {
+            const int g = d->resident_ids[i];
+            if (g < 0 || g >= h->E || (i > 0 && g <= d->resident_ids[i - 1]))
+                return bad("resident_ids must be ascending, distinct ids in [0, n_expert)");
+            slot_host[(size_t)g] = i;
+        }
+        src_experts = d->n_resident;
+        h->subset = d->n_resident < h->E;  // all n_expert ids ascending: the identity map, a whole layer
+        h->e_begin = 0;
+        h->e_end = d->n_resident;
+    }
     h->dtype = d->gate_exps.dtype;
     if (d->up_exps.dtype != h->dtype || d->down_exps.dtype != h->dtype)
         return bad("gate/up/down expert tensors must share one ggml type");
@@ -876,12 +915,22 @@ Handle* open_desc(const aero_cuda_moe_desc* d, std::string* why) {
             return bad("");
         h->rtc_ok = true;
     }
-    if (!upload_family(*h, d->gate_exps, h->E, h->e_begin, h->e_end, h->F, h->d, h->Fp, h->dp, h->gate, "ffn_gate_exps"))
+    if (!upload_family(*h, d->gate_exps, src_experts, h->e_begin, h->e_end, h->F, h->d, h->Fp, h->dp, h->gate,
+                       "ffn_gate_exps"))
         return bad("");
-    if (!upload_family(*h, d->up_exps, h->E, h->e_begin, h->e_end, h->F, h->d, h->Fp, h->dp, h->up, "ffn_up_exps"))
+    if (!upload_family(*h, d->up_exps, src_experts, h->e_begin, h->e_end, h->F, h->d, h->Fp, h->dp, h->up, "ffn_up_exps"))
         return bad("");
-    if (!upload_family(*h, d->down_exps, h->E, h->e_begin, h->e_end, h->d, h->F, h->dp, h->Fp, h->down, "ffn_down_exps"))
+    if (!upload_family(*h, d->down_exps, src_experts, h->e_begin, h->e_end, h->d, h->F, h->dp, h->Fp, h->down,
+                       "ffn_down_exps"))
         return bad("");
+    if (h->subset) {
+        h->slot = (int32_t*)h->dalloc((size_t)h->E * 4, kWeightsResident, "resident slots");
+        if (!h->slot) return bad("");
+        // pageable source: the copy has taken the bytes when the call returns
+        if (!h->cuda_ok(cudaMemcpyAsync(h->slot, slot_host.data(), (size_t)h->E * 4, cudaMemcpyHostToDevice, h->stream),
+                        "resident slots"))
+            return bad("");
+    }
     if (h->has_shared) {
         if (!upload_family(*h, d->shexp_gate, 1, 0, 1, h->Fs, h->d, h->Fsp, h->dp, h->sg, "ffn_gate_shexp")) return bad("");
         if (!upload_family(*h, d->shexp_up, 1, 0, 1, h->Fs, h->d, h->Fsp, h->dp, h->su, "ffn_up_shexp")) return bad("");
@@ -938,7 +987,7 @@ int aero_cuda_moe_forward(void* handle, int layer, const float* h_in, int T, int
         h->fail("hidden width %d != n_embd %d", n_embd, h->d);
         return 0;
     }
-    if (h->e_begin != 0 || h->e_end != h->E) {
+    if (!h->subset && (h->e_begin != 0 || h->e_end != h->E)) {
         h->fail("this handle owns experts [%d, %d) only; use the expert-parallel entry points", h->e_begin, h->e_end);
         return 0;
     }
@@ -953,7 +1002,7 @@ int aero_cuda_moe_ffn_block(void* handle, const float* h_in, const float* router
         h->fail("router_logits is required");
         return -1;
     }
-    if (h->e_begin != 0 || h->e_end != h->E) {
+    if (!h->subset && (h->e_begin != 0 || h->e_end != h->E)) {
         h->fail("this handle owns experts [%d, %d) only", h->e_begin, h->e_end);
         return -1;
     }
@@ -1281,6 +1330,7 @@ int aero_cuda_ep_meta_ld(void* handle) {
 }
 
 static bool ep_rank_table(Handle& h, int n_ranks, int rank, const int32_t* begin, aero::EpRankTable* rt) {
+    if (h.subset) return h.fail("a resident-subset handle takes no expert-parallel entry points");
     if (n_ranks < 1 || n_ranks > aero::kEpMaxRanks) return h.fail("n_ranks=%d outside [1, %d]", n_ranks, aero::kEpMaxRanks);
     if (rank < 0 || rank >= n_ranks) return h.fail("rank %d outside [0, %d)", rank, n_ranks);
     if (!begin) return h.fail("rank_expert_begin is required");
@@ -1334,6 +1384,7 @@ int aero_cuda_ep_expert_block(void* handle, const void* rows, int row_dtype, con
     auto* h = static_cast<Handle*>(handle);
     if (!h) return -1;
     std::lock_guard<std::mutex> lk(h->mu);
+    if (h->subset) return h->fail("a resident-subset handle takes no expert-parallel entry points"), -1;
     if (R < 0 || n_shared < 0 || n_shared > R) return h->fail("R=%d n_shared=%d", R, n_shared), -1;
     if (row_dtype != AERO_EP_ROWS_F32 && row_dtype != AERO_EP_ROWS_F16) return h->fail("row_dtype %d", row_dtype), -1;
     if (out_dtype != AERO_EP_ROWS_F32 && out_dtype != AERO_EP_ROWS_F16) return h->fail("out_dtype %d", out_dtype), -1;

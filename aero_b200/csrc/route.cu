@@ -335,7 +335,27 @@ __global__ void qinput_kernel(const float* __restrict__ x, int R, int ld, QInput
                  q.sx + (int64_t)r * nb + b, q.s16 + (int64_t)r * (q.K / 16) + 2 * b);
 }
 
+// Routed global expert ids -> resident slots. An id without a slot records
+// kErrNotResident and takes slot 0, so the rest of the call stays in bounds
+// (its output is then reported invalid).
+__global__ void resident_remap_kernel(int32_t* __restrict__ idx, int n, const int32_t* __restrict__ slot,
+                                      int32_t* __restrict__ err, int32_t* err_host) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    const int32_t r = slot[idx[i]];
+    if (r < 0 && atomicCAS(err, 0, kErrNotResident) == 0 && err_host)
+        *reinterpret_cast<volatile int32_t*>(err_host) = kErrNotResident;
+    idx[i] = r < 0 ? 0 : r;
+}
+
 }  // namespace
+
+cudaError_t launch_resident_remap(int32_t* idx, int n, const int32_t* slot, int32_t* err, int32_t* err_host,
+                                  cudaStream_t s) {
+    if (n <= 0) return cudaSuccess;
+    resident_remap_kernel<<<(unsigned)((n + 255) / 256), 256, 0, s>>>(idx, n, slot, err, err_host);
+    return cudaGetLastError();
+}
 
 cudaError_t launch_qinput(const float* x, int R, int ld, QInput q, cudaStream_t s) {
     const int64_t n = (int64_t)R * (q.K / 32);

@@ -114,11 +114,15 @@ class CudaMoeLayer:
 
     @classmethod
     def from_tensors(cls, cfg: MoeConfig, gate, up, down, dtype: int, router=None, router_bias=None,
-                     shexp: Optional[dict] = None, device: int = 0, expert_range=None) -> "CudaMoeLayer":
+                     shexp: Optional[dict] = None, device: int = 0, expert_range=None,
+                     resident_ids=None) -> "CudaMoeLayer":
         """Open a layer from GGUF-format bytes (or f32 arrays for DTYPE_F32).
 
         gate/up are (E, F, d), down (E, d, F); shexp holds gate_inp (d,), gate,
-        up, down and optionally dtype / ffn_len for the shared expert."""
+        up, down and optionally dtype / ffn_len for the shared expert. With
+        resident_ids (ascending global expert ids) the expert tensors hold only
+        those experts, in that order (E = len(resident_ids)); routing stays over
+        all cfg.n_expert logits, and a call that selects another expert fails."""
         L = nc.lib()
         nc.require_gpu()
         _check_k(cfg)
@@ -130,6 +134,11 @@ class CudaMoeLayer:
         desc.device = device
         if expert_range:
             desc.expert_begin, desc.expert_end = expert_range
+        if resident_ids is not None:
+            ids = np.ascontiguousarray(resident_ids, dtype=np.int32).reshape(-1)
+            keep.append(ids)
+            desc.n_resident = int(ids.size)
+            desc.resident_ids = ids.ctypes.data
 
         def tensor(src, dt):
             addr, n, k = _as_bytes_view(src)
@@ -323,21 +332,27 @@ def ffn_block(h, router_logits, n_expert, n_expert_used, ffn_len, norm_topk_prob
     _check_k(cfg)
     if lg.shape != (T, cfg.n_expert):
         raise ValueError(f"router_logits shape {lg.shape} != ({T}, {cfg.n_expert})")
+    if T == 0:
+        return np.zeros((0, d), dtype=np.float32)
+    # the routing on the device, then only the selected experts are fetched and
+    # uploaded (a compact (n_sel, ...) layer whose slots map the global ids)
     idx, _ = nc.route(lg, cfg.n_expert, cfg.n_expert_used, cfg.norm_topk_prob)
+    sel = np.unique(idx.reshape(-1)).astype(np.int32)
     F = cfg.ffn_len
-    gate = np.zeros((cfg.n_expert, F, d), dtype=np.float32)
-    up = np.zeros_like(gate)
-    down = np.zeros((cfg.n_expert, d, F), dtype=np.float32)
-    for e in sorted(set(int(v) for v in idx.reshape(-1))):
-        gate[e] = nc.f32c(expert_rows(_NAMES[0], e, block_rows)).reshape(F, d)
-        up[e] = nc.f32c(expert_rows(_NAMES[1], e, block_rows)).reshape(F, d)
-        down[e] = nc.f32c(expert_rows(_NAMES[2], e, block_rows)).reshape(d, F)
+    gate = np.empty((sel.size, F, d), dtype=np.float32)
+    up = np.empty_like(gate)
+    down = np.empty((sel.size, d, F), dtype=np.float32)
+    for i, e in enumerate(int(v) for v in sel):
+        gate[i] = nc.f32c(expert_rows(_NAMES[0], e, block_rows)).reshape(F, d)
+        up[i] = nc.f32c(expert_rows(_NAMES[1], e, block_rows)).reshape(F, d)
+        down[i] = nc.f32c(expert_rows(_NAMES[2], e, block_rows)).reshape(d, F)
     sh = None
     if shexp:
         sg = nc.f32c(shexp["gate"])
         sh = {"gate_inp": nc.f32c(shexp["gate_inp"]).reshape(-1), "gate": sg, "up": nc.f32c(shexp["up"]),
               "down": nc.f32c(shexp["down"]), "dtype": DTYPE_F32, "ffn_len": sg.shape[0]}
-    layer = CudaMoeLayer.from_tensors(cfg, gate, up, down, DTYPE_F32, router=None, shexp=sh, device=device)
+    layer = CudaMoeLayer.from_tensors(cfg, gate, up, down, DTYPE_F32, router=None, shexp=sh, device=device,
+                                      resident_ids=sel)
     try:
         return layer.ffn_block(h, lg)
     finally:

@@ -47,10 +47,11 @@ class Desc(Structure):
     _fields_ = [
         ("n_embd", c_int32), ("n_expert", c_int32), ("n_expert_used", c_int32), ("ffn_len", c_int32),
         ("norm_topk_prob", c_int32), ("has_shared", c_int32), ("ffn_len_shared", c_int32), ("device", c_int32),
-        ("expert_begin", c_int32), ("expert_end", c_int32), ("reserved", c_int32 * 6),
+        ("expert_begin", c_int32), ("expert_end", c_int32), ("n_resident", c_int32), ("reserved", c_int32 * 5),
         ("gate_exps", Tensor), ("up_exps", Tensor), ("down_exps", Tensor),
         ("router", c_void_p), ("router_bias", c_void_p), ("shexp_gate_inp", c_void_p),
         ("shexp_gate", Tensor), ("shexp_up", Tensor), ("shexp_down", Tensor),
+        ("resident_ids", c_void_p),
     ]
 
 

@@ -50,12 +50,21 @@ typedef struct aero_cuda_moe_desc {
     /* Expert-parallel ownership: this handle uploads and computes experts
      * [expert_begin, expert_end); 0,0 means all. Routing is over all experts. */
     int32_t expert_begin, expert_end;
-    int32_t reserved[6];
+    /* Resident subset: when n_resident > 0 the expert tensors hold only
+     * n_resident experts, those with the global ids resident_ids[0..n_resident)
+     * (ascending, distinct, < n_expert), in that order. Routing stays over all
+     * n_expert logits (same selection and weights as the whole layer); a call
+     * whose routing selects an expert that is not resident fails with status
+     * code 41 and its output is invalid. Not combined with an expert range nor
+     * with the expert-parallel entry points. 0: the tensors hold all experts. */
+    int32_t n_resident;
+    int32_t reserved[5];
     aero_cuda_tensor gate_exps, up_exps, down_exps;
     const float* router;         /* may be NULL: then only the *_ffn_block and route calls work */
     const float* router_bias;    /* (n_expert,) added to the logits, or NULL */
     const float* shexp_gate_inp; /* required when has_shared */
     aero_cuda_tensor shexp_gate, shexp_up, shexp_down;
+    const int32_t* resident_ids; /* host array of n_resident ids; read only when n_resident > 0 */
 } aero_cuda_moe_desc;
 
 /* Open a layer: upload the experts once into device-resident, expert-major,
@@ -166,11 +175,13 @@ int aero_cuda_moe_set_option(void* handle, int option, int64_t value);
 
 /* 0, or the code of the first bounded device wait of this handle's kernels that
  * gave up since the last status read (router pipeline, prefill GEMM pipeline,
- * peer exchange: 21 rows, 22 returns), after synchronising the handle's stream.
- * A wait that gives up during a call with device pointers (which returns
- * without synchronising) is also reported by the handle's next call, which is
- * then refused. No reference counterpart (the reference has no device waits).
- * The pipeline codes are cleared by the read; a peer-exchange code stays. */
+ * fused decode: 31, peer exchange: 21 rows, 22 returns), or 41 when a routing
+ * selected an expert that a resident-subset handle does not hold, after
+ * synchronising the handle's stream. Such a code raised during a call with
+ * device pointers (which returns without synchronising) is also reported by the
+ * handle's next call, which is then refused. No reference counterpart (the
+ * reference has no device waits). The pipeline codes are cleared by the read;
+ * a peer-exchange code stays. */
 int aero_cuda_moe_status(void* handle);
 
 /* ------------------------------------------------------- expert parallel

@@ -284,6 +284,109 @@ def test_fetch_failure_propagates():
         M.moe_ffn(np.ones((1, 16), np.float32), cfg, rows, router_fn=lambda hv: np.arange(6, dtype=np.float32))
 
 
+def _loop_reference(h, lg, k, norm, rows, sh=None):
+    """engine/native_ssm.py ffn_block as a plain f64 loop over the routed experts."""
+    out = np.zeros(h.shape, np.float64)
+    for t in range(h.shape[0]):
+        idx, w = O.route(lg[t], k, norm)
+        x = h[t].astype(np.float64)
+        for e, wt in zip(idx, w):
+            g = rows("ffn_gate_exps.weight", int(e), 64) @ x
+            u = rows("ffn_up_exps.weight", int(e), 64) @ x
+            out[t] += float(wt) * (rows("ffn_down_exps.weight", int(e), 64) @ (g / (1 + np.exp(-g)) * u))
+        if sh is not None:
+            gs = sh["gate"] @ x
+            a = gs / (1 + np.exp(-gs)) * (sh["up"] @ x)
+            out[t] += (1 / (1 + np.exp(-(sh["gate_inp"].reshape(-1) @ x)))) * (sh["down"] @ a)
+    return out
+
+
+@pytest.mark.parametrize("norm,T,shared", [(True, 1, False), (False, 2, True)])
+def test_generic_block_uploads_only_the_selected_experts(monkeypatch, norm, T, shared):
+    """A c1-shaped call (128 experts, k = 8, n_embd 2048, ffn 768) through a host reader of
+    fp32 matrices: the reader is asked for the routed experts only and the device layer
+    holds only those (a compact layer whose slot map keeps the global ids), while the
+    routing is over all 128 logits, so norm_topk_prob = 0 keeps the full-softmax weights."""
+    d, F, E, k = 2048, 768, 128, 8
+    cache = {}
+
+    def rows(name, expert, block_rows):
+        key = (name, expert)
+        if key not in cache:
+            r = np.random.default_rng([7, expert, len(name)])
+            shape = (d, F) if name == "ffn_down_exps.weight" else (F, d)
+            cache[key] = (r.standard_normal(shape) * 0.03).astype(np.float32)
+        return cache[key]
+
+    fetched = []
+
+    def reader(name, expert, block_rows):
+        fetched.append(expert)
+        return rows(name, expert, block_rows)
+
+    rng = np.random.default_rng(11 + T)
+    h = rng.standard_normal((T, d)).astype(np.float32)
+    lg = (rng.standard_normal((T, E)) * 2).astype(np.float32)
+    sh = None
+    if shared:
+        sh = {"gate_inp": (rng.standard_normal((1, d)) * 0.05).astype(np.float32),
+              "gate": (rng.standard_normal((F, d)) * 0.03).astype(np.float32),
+              "up": (rng.standard_normal((F, d)) * 0.03).astype(np.float32),
+              "down": (rng.standard_normal((d, F)) * 0.03).astype(np.float32)}
+    guard = nc.MemoryGuard()
+    base = guard.committed(nc.MEM_WEIGHTS_RESIDENT)
+    seen = {}
+    orig = M.CudaMoeLayer.from_tensors.__func__
+
+    def spy(cls, cfg, gate, up, down, *a, **kw):
+        layer = orig(cls, cfg, gate, up, down, *a, **kw)
+        seen["experts"] = gate.shape[0]
+        seen["ids"] = np.asarray(kw["resident_ids"]).tolist()
+        seen["weights"] = guard.committed(nc.MEM_WEIGHTS_RESIDENT) - base
+        return layer
+
+    monkeypatch.setattr(M.CudaMoeLayer, "from_tensors", classmethod(spy))
+    out = M.ffn_block(h, lg, E, k, F, norm, sh, reader)
+    routed = sorted({int(e) for t in range(T) for e in O.route(lg[t], k, norm)[0]})
+    assert sorted(set(fetched)) == routed and len(fetched) == 3 * len(routed)
+    assert seen["ids"] == routed and seen["experts"] == len(routed)
+    per_expert = 3 * F * d * 4
+    assert seen["weights"] < (len(routed) + 4) * per_expert, seen
+    ref = _loop_reference(h, lg, k, norm, rows, sh)
+    assert rel_err(out, ref) <= 1e-4, rel_err(out, ref)
+
+
+def test_resident_subset_refuses_an_expert_it_does_not_hold():
+    """A layer holding experts {1, 4} of 6: routing to them works; routing that selects
+    another expert fails the call (status code 41), and the next call runs."""
+    d, F, E = 64, 32, 6
+    rng = np.random.default_rng(5)
+    gate = (rng.standard_normal((2, F, d)) * 0.1).astype(np.float32)
+    up = (rng.standard_normal((2, F, d)) * 0.1).astype(np.float32)
+    down = (rng.standard_normal((2, d, F)) * 0.1).astype(np.float32)
+    cfg = M.MoeConfig(n_expert=E, n_expert_used=2, n_embd=d, ffn_len=F, has_shared=False)
+    L = M.CudaMoeLayer.from_tensors(cfg, gate, up, down, Q.DTYPE_F32, resident_ids=[1, 4])
+    try:
+        x = rng.standard_normal((3, d)).astype(np.float32)
+        good = np.full((3, E), -5.0, np.float32)
+        good[:, 1], good[:, 4] = 1.0, 0.5
+        a = L.ffn_block(x, good)
+        full = {"ffn_gate_exps.weight": {1: gate[0], 4: gate[1]}, "ffn_up_exps.weight": {1: up[0], 4: up[1]},
+                "ffn_down_exps.weight": {1: down[0], 4: down[1]}}
+        ref = _loop_reference(x, good, 2, True, lambda n, e, b: full[n][e])
+        assert rel_err(a, ref) <= 1e-5
+        bad = good.copy()
+        bad[1, 2] = 3.0
+        with pytest.raises(ValueError, match="does not hold"):
+            L.ffn_block(x, bad)
+        assert np.array_equal(L.ffn_block(x, good), a)
+        assert L.status() == 0
+    finally:
+        L.close()
+    with pytest.raises(RuntimeError, match="ascending"):
+        M.CudaMoeLayer.from_tensors(cfg, gate, up, down, Q.DTYPE_F32, resident_ids=[4, 1])
+
+
 def test_device_layer_with_its_router(golden):
     layer, g = block(golden, "b_q8")
     L = synth.open_layer(layer)
