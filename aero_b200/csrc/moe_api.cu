@@ -82,6 +82,9 @@ struct PeerCtx {
     size_t aux_bytes = 0;
     std::vector<char*> mapped;  // peers' windows opened here
     uint32_t epoch = 0;
+    // first code of a peer wait that gave up, once the host has seen it: the
+    // exchange's waits return at once from then on, so later steps are refused
+    int32_t failed = 0;
     // phase timing (profiling): route, plan, pack, rows wait + unpack, experts, return, combine
     static constexpr int kPhases = 7;
     bool prof = false;
@@ -711,6 +714,7 @@ bool take_async_error(Handle& h) {
     const int32_t code = *reinterpret_cast<volatile int32_t*>(h.err_host);
     if (code == 0) return true;
     *reinterpret_cast<volatile int32_t*>(h.err_host) = 0;
+    if (h.peer.open && (code == kEpErrRowsWait || code == kEpErrBackWait) && !h.peer.failed) h.peer.failed = code;
     if (h.sc.base) {
         cudaMemsetAsync(h.sc.tc_err, 0, 4, h.stream);
         cudaMemsetAsync(h.sc.dbar, 0, 8, h.stream);  // barrier counter and decode error word
@@ -1298,6 +1302,7 @@ int aero_cuda_moe_status(void* handle) {
     if (h->peer.open) cudaMemcpy(&dev[2], h->peer.window + h->peer.tab.off_err, 4, cudaMemcpyDeviceToHost);
     for (int32_t v : dev)
         if (code == 0) code = v;
+    if (dev[2] != 0 && !h->peer.failed) h->peer.failed = dev[2];
     // the pipeline codes are cleared; a peer exchange's code stays (its waits return at once from then on)
     if (h->err_host) *reinterpret_cast<volatile int32_t*>(h->err_host) = 0;
     if (h->sc.base && h->rtc_ok) cudaMemset(h->sc.tc_err, 0, 4);
@@ -1635,6 +1640,10 @@ int aero_cuda_ep_peer_step(void* handle, const float* x, int T, float* out) {
     const auto& tab = pc.tab;
     if (T < 0 || T > tab.slab) return h->fail("T=%d outside [0, slab_rows=%d]", T, tab.slab), -1;
     if (!aero::take_async_error(*h)) return -1;
+    if (pc.failed)
+        return h->fail("a wait of this peer exchange gave up earlier (code %d); close and reopen the exchange",
+                       pc.failed),
+               -1;
     if (T > 0) {
         if (!x || !out) return h->fail("null buffer"), -1;
         for (const void* p : {(const void*)x, (const void*)out})
@@ -1718,6 +1727,7 @@ int aero_cuda_ep_peer_status(void* handle) {
     if (!h->cuda_ok(cudaMemcpyAsync(&v, pc.window + pc.tab.off_err, 4, cudaMemcpyDeviceToHost, h->stream), "status") ||
         !h->cuda_ok(cudaStreamSynchronize(h->stream), "status"))
         return -1;
+    if (v != 0 && !pc.failed) pc.failed = v;
     return v;
 }
 

@@ -264,7 +264,9 @@ int aero_cuda_ep_peer_connect(void* handle, const void* ipc_all);
  * stops stepping) leaves the other ranks' waits to give up after the handle's
  * peer wait limit (AERO_CUDA_OPT_PEER_WAIT_MS, 5 s by default); their
  * aero_cuda_ep_peer_status then reports it, their outputs are not valid, and
- * their next step is refused once with the code in the error message. */
+ * once the host has seen the code (a status read, or the next step's entry)
+ * every later step is refused with the code in the error message, until the
+ * exchange is closed (aero_cuda_ep_peer_close) and opened again. */
 int aero_cuda_ep_peer_step(void* handle, const float* x, int T, float* out);
 /* 0, or the code of the first wait that gave up (21 rows, 22 returns);
  * synchronises the handle's stream. */
