@@ -61,7 +61,89 @@ float* small_f32(const aero::GgufFile& f, const aero::GgufTensor& t, int device,
     return (float*)dst;
 }
 
+// One MoE layer's tensors in an open GGUF file, with their shapes checked.
+struct LayerTensors {
+    const aero::GgufTensor *gate = nullptr, *up = nullptr, *down = nullptr, *router = nullptr;
+    const aero::GgufTensor *sh_inp = nullptr, *sh_gate = nullptr, *sh_up = nullptr, *sh_down = nullptr;
+    int64_t E = 0, F = 0, d = 0, n_used = -1, Fs = 0;
+};
+
+bool find_layer(const aero::GgufFile& f, int layer, LayerTensors* L, std::string* why) {
+    const std::string p = "blk." + std::to_string(layer) + ".";
+    L->gate = f.find(p + "ffn_gate_exps.weight");
+    L->up = f.find(p + "ffn_up_exps.weight");
+    L->down = f.find(p + "ffn_down_exps.weight");
+    L->router = f.find(p + "ffn_gate_inp.weight");
+    const aero::GgufTensor *tg = L->gate, *tu = L->up, *td = L->down;
+    if (!tg || !tu || !td) {
+        *why = p + "ffn_{gate,up,down}_exps.weight missing: not a MoE layer";
+        return false;
+    }
+    if (tg->dims.size() != 3 || tu->dims.size() != 3 || td->dims.size() != 3) {
+        *why = p + "expert tensors must be 3-D (n_expert, out, in)";
+        return false;
+    }
+    L->E = tg->shape(0);
+    L->F = tg->shape(1);
+    L->d = tg->shape(2);
+    if (tu->shape(0) != L->E || tu->shape(1) != L->F || tu->shape(2) != L->d || td->shape(0) != L->E ||
+        td->shape(1) != L->d || td->shape(2) != L->F) {
+        *why = p + "gate/up must be (E, F, d) and down (E, d, F)";
+        return false;
+    }
+    const std::string arch = f.arch();
+    int64_t n_exp = L->E;
+    f.get_int(arch + ".expert_count", &n_exp);
+    if (!f.get_int(arch + ".expert_used_count", &L->n_used)) {
+        *why = arch + ".expert_used_count missing; refusing to guess routing";
+        return false;
+    }
+    if (n_exp != L->E) {
+        *why = "expert_count disagrees with the expert tensors";
+        return false;
+    }
+    if (L->router && L->router->n_values != L->E * L->d) {
+        *why = p + "ffn_gate_inp.weight must be (n_expert, n_embd)";
+        return false;
+    }
+    L->sh_inp = f.find(p + "ffn_gate_inp_shexp.weight");
+    L->sh_gate = f.find(p + "ffn_gate_shexp.weight");
+    L->sh_up = f.find(p + "ffn_up_shexp.weight");
+    L->sh_down = f.find(p + "ffn_down_shexp.weight");
+    const aero::GgufTensor *sgi = L->sh_inp, *sg = L->sh_gate, *su = L->sh_up, *sd = L->sh_down;
+    if (sg) {
+        if (!sgi || !su || !sd || sg->dims.size() != 2 || su->dims.size() != 2 || sd->dims.size() != 2) {
+            *why = p + "incomplete shared expert";
+            return false;
+        }
+        L->Fs = sg->shape(0);
+        if (sg->shape(1) != L->d || su->shape(0) != L->Fs || su->shape(1) != L->d || sd->shape(0) != L->d ||
+            sd->shape(1) != L->Fs || sgi->n_values != L->d) {
+            *why = p + "shared expert shapes do not match n_embd";
+            return false;
+        }
+    }
+    return true;
+}
+
 }  // namespace
+
+extern "C" int aero_cuda_moe_gguf_info(const char* path, int layer, int64_t* out8, char* err, int errlen) {
+    aero::GgufFile f;
+    std::string why;
+    if (!path || !out8) {
+        put_err(err, errlen, "null argument");
+        return -1;
+    }
+    LayerTensors L;
+    if (!f.open(path, &why) || !find_layer(f, layer, &L, &why)) {
+        put_err(err, errlen, why);
+        return -1;
+    }
+    const int64_t v[8] = {L.d, L.E, L.n_used, L.F, L.Fs, L.sh_gate ? 1 : 0, L.gate->type, L.router ? 1 : 0};
+    for (int i = 0; i < 8; ++i) out8[i] = v[i];
+    return 0;
+}
 
 extern "C" void* aero_cuda_moe_open_gguf(const char* path, int layer, int device, int expert_begin, int expert_end,
                                          char* err, int errlen) {
@@ -71,36 +153,13 @@ extern "C" void* aero_cuda_moe_open_gguf(const char* path, int layer, int device
         put_err(err, errlen, path ? why : "null path");
         return nullptr;
     }
-    const std::string p = "blk." + std::to_string(layer) + ".";
-    const aero::GgufTensor* tg = f.find(p + "ffn_gate_exps.weight");
-    const aero::GgufTensor* tu = f.find(p + "ffn_up_exps.weight");
-    const aero::GgufTensor* td = f.find(p + "ffn_down_exps.weight");
-    const aero::GgufTensor* tr = f.find(p + "ffn_gate_inp.weight");
-    if (!tg || !tu || !td) {
-        put_err(err, errlen, p + "ffn_{gate,up,down}_exps.weight missing: not a MoE layer");
+    LayerTensors L;
+    if (!find_layer(f, layer, &L, &why)) {
+        put_err(err, errlen, why);
         return nullptr;
     }
-    if (tg->dims.size() != 3 || tu->dims.size() != 3 || td->dims.size() != 3) {
-        put_err(err, errlen, p + "expert tensors must be 3-D (n_expert, out, in)");
-        return nullptr;
-    }
-    const int64_t E = tg->shape(0), F = tg->shape(1), d = tg->shape(2);
-    if (tu->shape(0) != E || tu->shape(1) != F || tu->shape(2) != d || td->shape(0) != E || td->shape(1) != d ||
-        td->shape(2) != F) {
-        put_err(err, errlen, p + "gate/up must be (E, F, d) and down (E, d, F)");
-        return nullptr;
-    }
-    const std::string arch = f.arch();
-    int64_t n_exp = E, n_used = -1;
-    f.get_int(arch + ".expert_count", &n_exp);
-    if (!f.get_int(arch + ".expert_used_count", &n_used)) {
-        put_err(err, errlen, arch + ".expert_used_count missing; refusing to guess routing");
-        return nullptr;
-    }
-    if (n_exp != E) {
-        put_err(err, errlen, "expert_count disagrees with the expert tensors");
-        return nullptr;
-    }
+    const aero::GgufTensor *tg = L.gate, *tu = L.up, *td = L.down, *tr = L.router;
+    const int64_t E = L.E, F = L.F, d = L.d, n_used = L.n_used;
     std::vector<std::pair<void*, size_t>> tmp;
     aero_cuda_moe_desc desc{};
     desc.n_embd = (int)d;
@@ -117,35 +176,17 @@ extern "C" void* aero_cuda_moe_open_gguf(const char* path, int layer, int device
     void* result = nullptr;
     do {
         if (tr) {
-            if (tr->n_values != E * d) {
-                why = p + "ffn_gate_inp.weight must be (n_expert, n_embd)";
-                break;
-            }
             desc.router = small_f32(f, *tr, device, tmp, &why);
             if (!desc.router) break;
         }
-        const aero::GgufTensor* sgi = f.find(p + "ffn_gate_inp_shexp.weight");
-        const aero::GgufTensor* sg = f.find(p + "ffn_gate_shexp.weight");
-        const aero::GgufTensor* su = f.find(p + "ffn_up_shexp.weight");
-        const aero::GgufTensor* sd = f.find(p + "ffn_down_shexp.weight");
-        if (sg) {
-            if (!sgi || !su || !sd || sg->dims.size() != 2 || su->dims.size() != 2 || sd->dims.size() != 2) {
-                why = p + "incomplete shared expert";
-                break;
-            }
-            const int64_t Fs = sg->shape(0);
-            if (sg->shape(1) != d || su->shape(0) != Fs || su->shape(1) != d || sd->shape(0) != d || sd->shape(1) != Fs ||
-                sgi->n_values != d) {
-                why = p + "shared expert shapes do not match n_embd";
-                break;
-            }
+        if (L.sh_gate) {
             desc.has_shared = 1;
-            desc.ffn_len_shared = (int)Fs;
-            desc.shexp_gate_inp = small_f32(f, *sgi, device, tmp, &why);
+            desc.ffn_len_shared = (int)L.Fs;
+            desc.shexp_gate_inp = small_f32(f, *L.sh_inp, device, tmp, &why);
             if (!desc.shexp_gate_inp) break;
-            desc.shexp_gate = {sg->type, 0, f.data(*sg), sg->nbytes};
-            desc.shexp_up = {su->type, 0, f.data(*su), su->nbytes};
-            desc.shexp_down = {sd->type, 0, f.data(*sd), sd->nbytes};
+            desc.shexp_gate = {L.sh_gate->type, 0, f.data(*L.sh_gate), L.sh_gate->nbytes};
+            desc.shexp_up = {L.sh_up->type, 0, f.data(*L.sh_up), L.sh_up->nbytes};
+            desc.shexp_down = {L.sh_down->type, 0, f.data(*L.sh_down), L.sh_down->nbytes};
         }
         char e2[512] = {0};
         result = aero_cuda_moe_open(&desc, e2, sizeof(e2));

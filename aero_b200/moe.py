@@ -294,6 +294,18 @@ class CudaMoeLayer:
         raise TypeError("CudaMoeLayer keeps experts quantised on the device; pass it to moe_ffn as expert_rows")
 
 
+def gguf_layer_info(path: str, layer: int) -> dict:
+    """One MoE layer's description read from a GGUF file without opening it on a
+    device (the metadata and tensor-shape reads of engine/model.py:193-224)."""
+    out = (nc.c_int64 * 8)()
+    err = nc.ctypes.create_string_buffer(512)
+    if nc.lib().aero_cuda_moe_gguf_info(str(path).encode(), int(layer), out, err, 512) != 0:
+        raise ValueError(f"gguf layer {layer} of {path}: {err.value.decode()}")
+    d, E, k, F, Fs, has_sh, dt, has_router = (int(v) for v in out)
+    return {"config": MoeConfig(n_expert=E, n_expert_used=k, n_embd=d, ffn_len=F, has_shared=bool(has_sh)),
+            "ffn_len_shared": Fs, "dtype": dt, "has_router": bool(has_router)}
+
+
 class DeviceRouter:
     """The layer's own router as a router_fn: moe_ffn recognises it and keeps
     the projection on the device; called directly it returns one token's logits."""

@@ -66,6 +66,7 @@ _P = c_void_p
 SYMBOLS = [
     ("aero_cuda_moe_open", c_void_p, [POINTER(Desc), c_char_p, c_int]),
     ("aero_cuda_moe_open_gguf", c_void_p, [c_char_p, c_int, c_int, c_int, c_int, c_char_p, c_int]),
+    ("aero_cuda_moe_gguf_info", c_int, [c_char_p, c_int, _P, c_char_p, c_int]),
     ("aero_cuda_moe_close", None, [_P]),
     ("aero_cuda_moe_forward", c_int, [_P, c_int, _P, c_int, c_int, _P]),
     ("aero_cuda_moe_ffn_block", c_int, [_P, _P, _P, c_int, _P]),

@@ -81,6 +81,13 @@ void* aero_cuda_moe_open(const aero_cuda_moe_desc* desc, char* err, int errlen);
  * (engine/gguf.py:297-314) on this path. */
 void* aero_cuda_moe_open_gguf(const char* path, int layer, int device, int expert_begin,
                               int expert_end, char* err, int errlen);
+/* The same layer's description without opening it (no device work): out8 =
+ * n_embd, n_expert, n_expert_used, ffn_len, ffn_len_shared, has_shared, the
+ * expert tensors' ggml type, whether ffn_gate_inp.weight is present. The
+ * shape checks are aero_cuda_moe_open_gguf's. 0 / -1 with the reason in err.
+ * Replaces the metadata reads of GGUFReader (engine/gguf.py:186-230) that the
+ * reference's loader makes before it plans a layer (engine/model.py:193-224). */
+int aero_cuda_moe_gguf_info(const char* path, int layer, int64_t* out8, char* err, int errlen);
 
 void aero_cuda_moe_close(void* handle);
 

@@ -21,7 +21,10 @@ What it records, each produced by the reference's code:
     (engine/model.py:665-666). Layer bytes are NOT stored: they are regenerated
     by aero_b200.synth with the stored seed and checked against a stored
     SHA-256, which keeps the fixture small.
-The GPU box has no reference tree; the tests read only the .npz.
+  * GGUF files written by the reference's own GGUFWriter (engine/gguf.py:448-526)
+    around synth layers, with the reference block's outputs on them
+    (ref_writer_<name>.gguf beside the .npz, their SHA-256 in it).
+The GPU box has no reference tree; the tests read only the .npz and the .gguf files.
 """
 
 from __future__ import annotations
@@ -201,6 +204,52 @@ def block_case(M, Q, spec, T, seed, zipf_s=0.0):
     }
 
 
+GGUF_CASES = {
+    # name: (spec, tokens, seed, layer index)
+    "g_q8_shared": (synth.LayerSpec(256, 4, 2, 64, 64, DTYPE_Q8_0), 5, 31, 1),
+    "g_q4k": (synth.LayerSpec(256, 2, 1, 256, 0, DTYPE_Q4_K), 3, 32, 0),
+}
+
+
+def gguf_case(G, M, Q, name, spec, T, seed, layer_index):
+    """The layer's bytes written by the reference's own GGUFWriter (engine/gguf.py:448-526),
+    with metadata of every value kind around the MoE tensors, and the reference block's
+    output on it (block_case on the same seed)."""
+    layer = synth.make_layer(spec, seed)
+    arch = "qwen3moe"
+    w = G.GGUFWriter(arch)
+    w.add_kv(f"{arch}.block_count", G.GGUF_UINT32, layer_index + 1)
+    w.add_kv(f"{arch}.expert_count", G.GGUF_UINT32, spec.E)
+    w.add_kv(f"{arch}.expert_used_count", G.GGUF_UINT32, spec.k)
+    w.add_kv(f"{arch}.embedding_length", G.GGUF_UINT32, spec.d)
+    w.add_kv(f"{arch}.rope.freq_base", G.GGUF_FLOAT32, 1000000.0)
+    w.add_kv("general.name", G.GGUF_STRING, f"aero-b200 fixture {name}")
+    w.add_kv("tokenizer.ggml.tokens", G.GGUF_ARRAY, (G.GGUF_STRING, ["<s>", "</s>", "a", "b"]))
+    w.add_kv("tokenizer.ggml.scores", G.GGUF_ARRAY, (G.GGUF_FLOAT32, [0.0, -1.0, -2.5, -3.0]))
+    w.add_kv("general.file_type", G.GGUF_UINT64, 7)
+    d, E, F = spec.d, spec.E, spec.F
+    w.add_tensor("token_embd.weight", (4, d), np.ones((4, d), np.float32).tobytes(), G.T_F32)
+    p = f"blk.{layer_index}."
+    w.add_tensor(p + "ffn_gate_inp.weight", (E, d), layer.router.astype(np.float32).tobytes(), G.T_F32)
+    w.add_tensor(p + "ffn_gate_exps.weight", (E, F, d), np.asarray(layer.gate).tobytes(), spec.dtype)
+    w.add_tensor(p + "ffn_up_exps.weight", (E, F, d), np.asarray(layer.up).tobytes(), spec.dtype)
+    w.add_tensor(p + "ffn_down_exps.weight", (E, d, F), np.asarray(layer.down).tobytes(), spec.dtype)
+    if layer.shexp:
+        sh = layer.shexp
+        w.add_tensor(p + "ffn_gate_inp_shexp.weight", (d,), np.asarray(sh["gate_inp"], np.float32).tobytes(), G.T_F32)
+        w.add_tensor(p + "ffn_gate_shexp.weight", (spec.Fs, d), np.asarray(sh["gate"]).tobytes(), sh["dtype"])
+        w.add_tensor(p + "ffn_up_shexp.weight", (spec.Fs, d), np.asarray(sh["up"]).tobytes(), sh["dtype"])
+        w.add_tensor(p + "ffn_down_shexp.weight", (d, spec.Fs), np.asarray(sh["down"]).tobytes(), sh["dtype"])
+    w.add_tensor(p + "attn_norm.weight", (d,), np.ones(d, np.float32).tobytes(), G.T_F32)
+    path = os.path.join(HERE, f"ref_writer_{name}.gguf")
+    w.write(path)
+    with open(path, "rb") as fh:
+        file_sha = hashlib.sha256(fh.read()).hexdigest()
+    case = block_case(M, Q, spec, T, seed)
+    return {"layer": np.int64(layer_index), "file_sha": np.array(file_sha), "spec": case["spec"],
+            "x": case["x"], "logits": case["logits"], "out": case["out"]}
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("AERO_REF") or os.path.abspath(
@@ -222,6 +271,12 @@ def main():
         for key, v in block_case(M, Q, spec, T, seed, zs).items():
             out[f"{name}_{key}"] = v
     out["block_names"] = np.array(list(blocks))
+    sys.path.insert(0, args.ref)
+    from engine import gguf as G  # noqa: E402
+    for name, (spec, T, seed, li) in GGUF_CASES.items():
+        for key, v in gguf_case(G, M, Q, name, spec, T, seed, li).items():
+            out[f"{name}_{key}"] = v
+    out["gguf_names"] = np.array(list(GGUF_CASES))
     path = os.path.join(HERE, "golden.npz")
     np.savez_compressed(path, **out)
     print(f"wrote {path} ({os.path.getsize(path)} bytes, {len(out)} arrays)")
