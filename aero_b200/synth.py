@@ -253,3 +253,109 @@ def write_gguf(layer: SynthLayer, path: str, layer_index: int = 0, arch: str = "
         w.add_tensor(names["shexp_up"], (sp.Fs, sp.d), np.asarray(sh["up"]).tobytes(), sh["dtype"])
         w.add_tensor(names["shexp_down"], (sp.d, sp.Fs), np.asarray(sh["down"]).tobytes(), sh["dtype"])
     w.write(path)
+
+
+# ---------------------------------------------------------------- decoder
+@dataclass
+class DecoderSpec:
+    """A qwen-style decoder around the MoE layer (the reference's block loop,
+    src/model.cpp:234-330): per layer RMSNorm -> GQA attention (q/k RMSNorm per
+    head, neox RoPE) -> residual -> RMSNorm (post_attention_norm) -> MoE FFN ->
+    residual; then output_norm and the LM head on the last position."""
+    n_layer: int
+    d: int
+    n_head: int
+    n_kv: int
+    head_dim: int
+    vocab: int
+    moe: LayerSpec
+    rope_base: float = 1e6
+    eps: float = 1e-6
+    attn_dtype: int = DTYPE_Q8_0
+    embd_dtype: int = DTYPE_Q8_0
+    tied: bool = False
+    qk_norm: bool = True
+
+
+# config 4 (the 48-layer decoder): GQA 32 q / 4 kv heads of 128, RoPE 1e6, every FFN the
+# 128-expert top-8 Q4_K MoE (F 768), vocab 151936 with Q8_0 embedding and head
+DECODER_C4 = DecoderSpec(48, 2048, 32, 4, 128, 151936, LayerSpec(2048, 128, 8, 768, 0, DTYPE_Q4_K))
+
+
+@dataclass
+class SynthDecoder:
+    spec: DecoderSpec
+    tensors: dict                           # name -> (row-major shape, ggml type, bytes as uint8 / f32 array)
+    moe: list                               # SynthLayer per layer
+
+
+def _norm_weight(seed: int, i: int, n: int) -> np.ndarray:
+    return (np.float32(1.0) + _normal_np(seed, i, n, 0.1)).astype(np.float32)
+
+
+def make_decoder(spec: DecoderSpec, seed: int = 0, device_gen: bool = False) -> SynthDecoder:
+    """Seeded random-init weights of the decoder: projections N(0, 0.02) quantised to
+    attn_dtype, the embedding N(0, 1) quantised to embd_dtype, norm weights 1 + N(0, 0.1),
+    the MoE layers from make_layer (seed * 100 + layer)."""
+    gen = _quant_gpu if device_gen else _quant_np
+    d, H, HK, D = spec.d, spec.n_head, spec.n_kv, spec.head_dim
+    t = {}
+
+    def q(name, shape, i, dt, scale=0.02):
+        n = int(np.prod(shape))
+        if scale == 0.02:
+            raw = gen(seed, i, n, dt)
+        else:
+            w = _normal_np(seed, i, n, scale)
+            raw = w if dt == DTYPE_F32 else np.frombuffer(quantize(w, dt), dtype=np.uint8)
+        t[name] = (tuple(shape), dt, raw)
+
+    q("token_embd.weight", (spec.vocab, d), 900, spec.embd_dtype, scale=1.0)
+    if not spec.tied:
+        q("output.weight", (spec.vocab, d), 901, spec.embd_dtype)
+    t["output_norm.weight"] = ((d,), DTYPE_F32, _norm_weight(seed, 902, d))
+    moe = []
+    for L in range(spec.n_layer):
+        p, b = f"blk.{L}.", 1000 + 20 * L
+        t[p + "attn_norm.weight"] = ((d,), DTYPE_F32, _norm_weight(seed, b, d))
+        t[p + "post_attention_norm.weight"] = ((d,), DTYPE_F32, _norm_weight(seed, b + 1, d))
+        q(p + "attn_q.weight", (H * D, d), b + 2, spec.attn_dtype)
+        q(p + "attn_k.weight", (HK * D, d), b + 3, spec.attn_dtype)
+        q(p + "attn_v.weight", (HK * D, d), b + 4, spec.attn_dtype)
+        q(p + "attn_output.weight", (d, H * D), b + 5, spec.attn_dtype)
+        if spec.qk_norm:
+            t[p + "attn_q_norm.weight"] = ((D,), DTYPE_F32, _norm_weight(seed, b + 6, D))
+            t[p + "attn_k_norm.weight"] = ((D,), DTYPE_F32, _norm_weight(seed, b + 7, D))
+        moe.append(make_layer(spec.moe, seed * 100 + L, device_gen=device_gen))
+    return SynthDecoder(spec, t, moe)
+
+
+def write_decoder_gguf(dec: SynthDecoder, path: str, arch: str = "qwen3moe") -> None:
+    """The decoder as a GGUF file: the reference's metadata keys (arch-prefixed) and
+    tensor names, the MoE tensors per layer in the qwen35moe naming."""
+    from .gguf import GGUF_FLOAT32, GGUFWriter, moe_tensor_names
+    sp = dec.spec
+    w = GGUFWriter(arch)
+    for key, v in (("block_count", sp.n_layer), ("embedding_length", sp.d), ("attention.head_count", sp.n_head),
+                   ("attention.head_count_kv", sp.n_kv), ("attention.key_length", sp.head_dim),
+                   ("attention.value_length", sp.head_dim), ("expert_count", sp.moe.E),
+                   ("expert_used_count", sp.moe.k), ("vocab_size", sp.vocab)):
+        w.add_u32(f"{arch}.{key}", v)
+    w.add_kv(f"{arch}.rope.freq_base", GGUF_FLOAT32, float(sp.rope_base))
+    w.add_kv(f"{arch}.attention.layer_norm_rms_epsilon", GGUF_FLOAT32, float(sp.eps))
+    for name, (shape, dt, raw) in dec.tensors.items():
+        w.add_tensor(name, shape, np.asarray(raw).tobytes(), dt)
+    for L, layer in enumerate(dec.moe):
+        names = moe_tensor_names(L)
+        m = layer.spec
+        w.add_tensor(names["router"], (m.E, m.d), layer.router.astype(np.float32).tobytes(), DTYPE_F32)
+        w.add_tensor(names["gate"], (m.E, m.F, m.d), np.asarray(layer.gate).tobytes(), m.dtype)
+        w.add_tensor(names["up"], (m.E, m.F, m.d), np.asarray(layer.up).tobytes(), m.dtype)
+        w.add_tensor(names["down"], (m.E, m.d, m.F), np.asarray(layer.down).tobytes(), m.dtype)
+        if layer.shexp:
+            sh = layer.shexp
+            w.add_tensor(names["shexp_gate_inp"], (m.d,), np.asarray(sh["gate_inp"], np.float32).tobytes(), DTYPE_F32)
+            w.add_tensor(names["shexp_gate"], (m.Fs, m.d), np.asarray(sh["gate"]).tobytes(), sh["dtype"])
+            w.add_tensor(names["shexp_up"], (m.Fs, m.d), np.asarray(sh["up"]).tobytes(), sh["dtype"])
+            w.add_tensor(names["shexp_down"], (m.d, m.Fs), np.asarray(sh["down"]).tobytes(), sh["dtype"])
+    w.write(path)
