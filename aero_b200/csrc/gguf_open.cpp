@@ -196,3 +196,77 @@ extern "C" void* aero_cuda_moe_open_gguf(const char* path, int layer, int device
     if (!result) put_err(err, errlen, why);
     return result;
 }
+
+// ---------------------------------------------------------------- model table
+// Every MoE layer of a GGUF file opened as one table whose forward has the
+// reference's aero_moe_fn signature, so a single hook context serves the whole
+// block loop (src/model.cpp:166-170, 385-387): aero_model_set_moe(model,
+// aero_cuda_moe_model_forward, table).
+namespace {
+struct MoeModel {
+    std::vector<void*> layers;  // null: not a MoE layer
+};
+}  // namespace
+
+extern "C" void* aero_cuda_moe_model_open_gguf(const char* path, int n_layer, int device, char* err, int errlen) {
+    aero::GgufFile f;
+    std::string why;
+    if (!path || !f.open(path, &why)) {
+        put_err(err, errlen, path ? why : "null path");
+        return nullptr;
+    }
+    int64_t nl = n_layer;
+    if (nl <= 0 && !f.get_int(f.arch() + ".block_count", &nl)) {
+        put_err(err, errlen, f.arch() + ".block_count missing and no layer count given");
+        return nullptr;
+    }
+    if (nl <= 0 || nl > 4096) {
+        put_err(err, errlen, "layer count out of range");
+        return nullptr;
+    }
+    auto* m = new MoeModel();
+    m->layers.assign((size_t)nl, nullptr);
+    int n_moe = 0;
+    for (int L = 0; L < (int)nl; ++L) {
+        const std::string p = "blk." + std::to_string(L) + ".";
+        if (!f.find(p + "ffn_gate_exps.weight") && !f.find(p + "ffn_up_exps.weight") &&
+            !f.find(p + "ffn_down_exps.weight"))
+            continue;  // a dense (or absent) FFN: the table refuses that layer
+        char e2[512] = {0};
+        m->layers[(size_t)L] = aero_cuda_moe_open_gguf(path, L, device, 0, 0, e2, sizeof(e2));
+        if (!m->layers[(size_t)L]) {
+            put_err(err, errlen, "layer " + std::to_string(L) + ": " + e2);
+            for (void* h : m->layers)
+                if (h) aero_cuda_moe_close(h);
+            delete m;
+            return nullptr;
+        }
+        ++n_moe;
+    }
+    if (n_moe == 0) {
+        put_err(err, errlen, "no MoE layer in the file");
+        delete m;
+        return nullptr;
+    }
+    return m;
+}
+
+extern "C" int aero_cuda_moe_model_forward(void* table, int layer, const float* h, int T, int n_embd, float* out) {
+    auto* m = static_cast<MoeModel*>(table);
+    if (!m || layer < 0 || layer >= (int)m->layers.size() || !m->layers[(size_t)layer]) return 0;
+    return aero_cuda_moe_forward(m->layers[(size_t)layer], layer, h, T, n_embd, out);
+}
+
+extern "C" void* aero_cuda_moe_model_layer(void* table, int layer) {
+    auto* m = static_cast<MoeModel*>(table);
+    if (!m || layer < 0 || layer >= (int)m->layers.size()) return nullptr;
+    return m->layers[(size_t)layer];
+}
+
+extern "C" void aero_cuda_moe_model_close(void* table) {
+    auto* m = static_cast<MoeModel*>(table);
+    if (!m) return;
+    for (void* h : m->layers)
+        if (h) aero_cuda_moe_close(h);
+    delete m;
+}

@@ -91,6 +91,19 @@ int aero_cuda_moe_gguf_info(const char* path, int layer, int64_t* out8, char* er
 
 void aero_cuda_moe_close(void* handle);
 
+/* Every MoE layer of a GGUF file as one table (n_layer <= 0: "<arch>.block_count").
+ * Layers without expert tensors stay empty and their hook call returns 0.
+ * aero_cuda_moe_model_forward has the aero_moe_fn signature and dispatches on
+ * `layer`, so the reference's block loop takes the whole model with one call:
+ *   aero_model_set_moe(model, aero_cuda_moe_model_forward, table);
+ * (src/model.cpp:166-170, 385-387; the loop's is_moe flag marks the layers).
+ * _layer returns the layer's handle (NULL for an empty layer) for the per-layer
+ * calls above; _close closes every handle. */
+void* aero_cuda_moe_model_open_gguf(const char* path, int n_layer, int device, char* err, int errlen);
+int aero_cuda_moe_model_forward(void* table, int layer, const float* h, int T, int n_embd, float* out);
+void* aero_cuda_moe_model_layer(void* table, int layer);
+void aero_cuda_moe_model_close(void* table);
+
 /* The block hook: exactly the aero_moe_fn signature (include/aero/model.hpp:83-84,
  * 176-177), so aero_model_set_moe(model, aero_cuda_moe_forward, handle) plugs it
  * in. Router logits are computed on the device from the layer's router
