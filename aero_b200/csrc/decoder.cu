@@ -1,0 +1,977 @@
+// The decoder around the MoE layer (include/aero_cuda_decoder.h): one step of
+// the reference's block loop (src/model.cpp:234-330, qwen layers) for T tokens,
+// each of its own sequence at its own position.
+//
+// Kernels per layer (all on the decoder's stream):
+//   norm_kernel          x (+)= the previous residual term; h = RMSNorm(x, w)
+//                        (src/tensor.cpp:128-134), written as f32 rows and/or as
+//                        the integer-coded input rows of the GEMVs (QInput)
+//   dense_gemv_kernel    y = W h for Q8_0 / Q4_K rows (the fused q|k|v matrix,
+//                        the output projection, the head): one warp per row, its
+//                        32 lanes splitting the row into 16-byte code chunks,
+//                        dp4a over the coded input, f32 accumulation; a CTA takes
+//                        up to 16 tokens so a row is read once for all of them
+//   qk_rope_kv_kernel    per (token, head): q/k RMSNorm over the head, neox RoPE
+//                        (src/transformer.cpp:27-91), k and v stored f16 into the
+//                        sequence's cache rows
+//   attn_partial_kernel  per (64-position chunk, token, kv head): the chunk's K/V
+//                        rows staged in shared memory once for the kv head's
+//                        group of query heads, causal scores, chunk softmax
+//                        (max, sum) and P V
+//   attn_combine_kernel  merges the chunks of each (token, head)
+//                        (src/transformer.cpp:120-205 computes the same online
+//                        softmax in 1024-position blocks)
+//   the MoE layer        aero_cuda_moe_forward on the layer's handle, device
+//                        pointers, same stream
+// and per step the embedding row gather (Q8_0, the reference's dequantised row,
+// src/model.cpp:296-313) and, for the tokens whose logits are asked for, the
+// final RMSNorm and the head GEMV.
+#include <cuda_fp16.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <set>
+#include <string>
+#include <utility>
+#include <vector>
+
+#include "../../include/aero_cuda_decoder.h"
+#include "gemv_rows.cuh"
+#include "gguf_loader.h"
+#include "internal.h"
+
+namespace aero {
+namespace {
+
+constexpr int kTokGroup = 16;   // tokens per dense GEMV CTA: a weight row is read once for all of them
+// 16-byte chunks per lane per pass over a row (Q4_K chunks carry two runs of input codes)
+template <int DT>
+constexpr int gemv_cpl() { return DT == AERO_DT_Q4_K ? 2 : 4; }
+constexpr int kAttnChunk = 64;  // cache positions per attention CTA
+constexpr int kMaxGroup = 16;   // query heads per kv head
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ------------------------------------------------------------ embedding gather
+// x[t] = the Q8_0 row tok[t] dequantised: d * q with one f32 rounding (the
+// reference's dequant_ref, src/kernels.cpp:337-350). One thread per 32-value block.
+__global__ void embed_q8_kernel(QMat E, const int32_t* __restrict__ tok, int T, float* __restrict__ x) {
+    const int d = E.cols, nb = d / 32;
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)T * nb) return;
+    const int t = (int)(i / nb), b = (int)(i % nb);
+    const int r = tok[t];
+    const uint8_t* qs = qm_row_qs(E, 0, r) + 32 * b;
+    const float sc =
+        __half2float(__ushort_as_half(__ldg(reinterpret_cast<const unsigned short*>(qm_row_meta(E, 0, r)) + b)));
+    const uint4 a = __ldg(reinterpret_cast<const uint4*>(qs)), c = __ldg(reinterpret_cast<const uint4*>(qs + 16));
+    const uint32_t w[8] = {a.x, a.y, a.z, a.w, c.x, c.y, c.z, c.w};
+    float4* o = reinterpret_cast<float4*>(x + (int64_t)t * d + 32 * b);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        float4 v;
+        v.x = __fmul_rn(sc, (float)(int8_t)(w[k] & 0xFFu));
+        v.y = __fmul_rn(sc, (float)(int8_t)((w[k] >> 8) & 0xFFu));
+        v.z = __fmul_rn(sc, (float)(int8_t)((w[k] >> 16) & 0xFFu));
+        v.w = __fmul_rn(sc, (float)(int8_t)(w[k] >> 24));
+        o[k] = v;
+    }
+}
+
+// ------------------------------------------------------------------ RMSNorm
+// Row r0 + b of x (b = blockIdx.x): with add non-null, x += add first (the
+// residual, written back); then h = x * inv * w, inv = 1 / sqrt(mean(x^2) + eps).
+// Output row b of h32 (f32) and/or of hq (coded input rows), either may be null.
+__global__ void __launch_bounds__(256) norm_kernel(float* __restrict__ x, int d, const float* __restrict__ add,
+                                                   const float* __restrict__ w, float eps, int r0,
+                                                   float* __restrict__ h32, QInput hq) {
+    extern __shared__ float sh[];  // d values, then 8 partial sums
+    const int t = r0 + (int)blockIdx.x, o = (int)blockIdx.x;
+    float* xr = x + (int64_t)t * d;
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        float v = xr[i];
+        if (add) {
+            v += add[(int64_t)t * d + i];
+            xr[i] = v;
+        }
+        sh[i] = v;
+        ss = fmaf(v, v, ss);
+    }
+    float* red = sh + d;
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        v = warp_sum(v);
+        if (threadIdx.x == 0) red[0] = v;
+    }
+    __syncthreads();
+    const float inv = 1.0f / sqrtf(red[0] / (float)d + eps);
+    for (int i = threadIdx.x; i < d; i += blockDim.x) {
+        const float h = sh[i] * inv * w[i];
+        sh[i] = h;
+        if (h32) h32[(int64_t)o * d + i] = h;
+    }
+    if (!hq.q1) return;
+    __syncthreads();
+    for (int b = threadIdx.x; b < d / 32; b += blockDim.x)
+        qinput_block(sh + 32 * b, hq.q1 + (int64_t)o * hq.K + 32 * b, hq.q0 + (int64_t)o * hq.K + 32 * b,
+                     hq.sx + (int64_t)o * (hq.K / 32) + b, hq.s16 + (int64_t)o * (hq.K / 16) + 2 * b);
+}
+
+// ------------------------------------------------------------------ dense GEMV
+// y[t][r] = W[r] . in[t] for the tokens t0 + [0, 16) of blockIdx.y. One warp per
+// row at a time (rows blockIdx.x * 8 + warp, stepping over the grid); a row is
+// loaded once per pass of 32 x gemv_cpl chunks and dotted with every token of the
+// CTA. ONE: a single token whose row fits one pass: its input stays in
+// registers and the next row's chunks are prefetched while the current one is
+// reduced.
+template <int DT, bool ONE>
+__global__ void __launch_bounds__(256, 2) dense_gemv_kernel(QMat W, QInput in, int T, float* __restrict__ y,
+                                                            int ldy) {
+    constexpr int CPL = gemv_cpl<DT>(), LPR = 32;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nch = Layout<DT>::chunks(W.cols);
+    const int t0 = (int)blockIdx.y * kTokGroup;
+    const int nt = min(kTokGroup, T - t0);
+    const int stride = (int)gridDim.x * 8;
+    int r = (int)blockIdx.x * 8 + warp;
+    if (ONE) {
+        LaneInput<DT, CPL> xin;
+        input_load<DT, LPR, CPL>(nullptr, in, t0, lane, nch, xin);
+        RowRaw<DT, CPL> w{}, nx{};
+        if (r < W.rows) row_load<DT, LPR, CPL>(W, 0, r, lane, nch, w);
+        for (; r < W.rows; r += stride) {
+            if (r + stride < W.rows) row_load<DT, LPR, CPL>(W, 0, r + stride, lane, nch, nx);
+            const float v = warp_sum(row_dot<DT, LPR, CPL>(w, xin, lane, nch));
+            if (lane == 0) y[(int64_t)t0 * ldy + r] = v;
+            w = nx;
+        }
+        return;
+    }
+    for (; r < W.rows; r += stride) {
+        float acc[kTokGroup];
+#pragma unroll
+        for (int j = 0; j < kTokGroup; ++j) acc[j] = 0.f;
+        for (int base = 0; base < nch; base += LPR * CPL) {
+            RowRaw<DT, CPL> w;
+            row_load<DT, LPR, CPL>(W, 0, r, lane, nch, w, base);
+#pragma unroll
+            for (int j = 0; j < kTokGroup; ++j) {
+                if (j < nt) {
+                    LaneInput<DT, CPL> xin;
+                    input_load<DT, LPR, CPL>(nullptr, in, t0 + j, lane, nch, xin, base);
+                    acc[j] += row_dot<DT, LPR, CPL>(w, xin, lane, nch, base);
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kTokGroup; ++j) {
+            if (j < nt) {
+                const float v = warp_sum(acc[j]);
+                if (lane == 0) y[(int64_t)(t0 + j) * ldy + r] = v;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------- q/k norm, RoPE, cache
+// One warp per (token, head j) of the step's q|k|v rows (j < H: query head,
+// then H_kv key heads, then H_kv value heads); lane l holds values i * 32 + l,
+// so the neox pairs (p, p + D/2) are lane-local. Queries are written back f32,
+// keys and values f16 into the cache row (seq, head, pos).
+template <int NV>
+__global__ void __launch_bounds__(128) qk_rope_kv_kernel(float* __restrict__ qkv, int T, int H, int HK, int ld,
+                                                         const float* __restrict__ q_norm,
+                                                         const float* __restrict__ k_norm, float eps, float rope_base,
+                                                         const int64_t* __restrict__ pos,
+                                                         const int32_t* __restrict__ seq, __half* __restrict__ kc,
+                                                         __half* __restrict__ vc, int n_ctx) {
+    constexpr int D = NV * 32, HV = NV / 2;
+    const int item = (int)blockIdx.x * 4 + (int)(threadIdx.x >> 5), lane = threadIdx.x & 31;
+    const int per = H + 2 * HK;
+    if (item >= T * per) return;
+    const int t = item / per, j = item % per;
+    float* src = qkv + (int64_t)t * ld + (int64_t)j * D;
+    float v[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) v[i] = src[i * 32 + lane];
+    const int64_t p = pos[t];
+    if (j < H + HK) {
+        const float* w = j < H ? q_norm : k_norm;
+        if (w) {
+            float ss = 0.f;
+#pragma unroll
+            for (int i = 0; i < NV; ++i) ss = fmaf(v[i], v[i], ss);
+            ss = warp_sum(ss);
+            const float inv = 1.0f / sqrtf(ss / (float)D + eps);
+#pragma unroll
+            for (int i = 0; i < NV; ++i) v[i] = v[i] * inv * w[i * 32 + lane];
+        }
+#pragma unroll
+        for (int i = 0; i < HV; ++i) {
+            const int pi = i * 32 + lane;
+            const float e = (float)pi * 2.0f / (float)D;
+            const float invf = 1.0f / powf(rope_base, e);
+            const float ang = (float)p * invf;
+            const float c = cosf(ang), s = sinf(ang);
+            const float x0 = v[i], x1 = v[i + HV];
+            v[i] = x0 * c - x1 * s;
+            v[i + HV] = x0 * s + x1 * c;
+        }
+    }
+    if (j < H) {
+#pragma unroll
+        for (int i = 0; i < NV; ++i) src[i * 32 + lane] = v[i];
+        return;
+    }
+    const bool is_k = j < H + HK;
+    const int hk = is_k ? j - H : j - H - HK;
+    __half* dst = (is_k ? kc : vc) + (((int64_t)seq[t] * HK + hk) * n_ctx + p) * D;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) dst[i * 32 + lane] = __float2half_rn(v[i]);
+}
+
+// ------------------------------------------------------------------ attention
+// CTA = (chunk c of 64 positions, token t, kv head hk): the chunk's K and V rows
+// of (seq[t], hk) staged once in shared memory (rows padded to an odd number of
+// 16-byte units: conflict-free 16-byte reads of different rows), scores of the
+// group's R query heads for positions <= pos[t] (masked to -inf otherwise,
+// scaled by 1/sqrt(D)), the chunk's max m and sum l of exp(s - m), and P V.
+// part[t][h][c] = (m, l, acc[D]).
+template <int NV>
+__global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restrict__ qkv, int ld, int H, int HK,
+                                                           const __half* __restrict__ kc,
+                                                           const __half* __restrict__ vc, int n_ctx,
+                                                           const int64_t* __restrict__ pos,
+                                                           const int32_t* __restrict__ seq, float scale,
+                                                           float* __restrict__ part, int n_chunk) {
+    constexpr int D = NV * 32;
+    constexpr int KS = D * 2 + 16;
+    constexpr int C = kAttnChunk;
+    const int c = (int)blockIdx.x, t = (int)blockIdx.y / HK, hk = (int)blockIdx.y % HK;
+    const int64_t qp = pos[t];
+    const int start = c * C;
+    if (start > qp) return;
+    const int nv = (int)min((int64_t)C, qp - start + 1);
+    const int R = H / HK;
+    extern __shared__ __align__(16) uint8_t sm[];
+    uint8_t* ks = sm;
+    uint8_t* vs = ks + C * KS;
+    float* qs = reinterpret_cast<float*>(vs + C * KS);
+    float* S = qs + R * D;
+    float* ml = S + R * C;
+    const int64_t base = (((int64_t)seq[t] * HK + hk) * n_ctx + start) * D;
+    constexpr int pieces = D / 8;
+    for (int i = threadIdx.x; i < nv * pieces; i += blockDim.x) {
+        const int row = i / pieces, pc = i % pieces;
+        *reinterpret_cast<uint4*>(ks + row * KS + pc * 16) =
+            __ldg(reinterpret_cast<const uint4*>(kc + base + (int64_t)row * D) + pc);
+        *reinterpret_cast<uint4*>(vs + row * KS + pc * 16) =
+            __ldg(reinterpret_cast<const uint4*>(vc + base + (int64_t)row * D) + pc);
+    }
+    for (int i = threadIdx.x; i < R * D; i += blockDim.x)
+        qs[i] = qkv[(int64_t)t * ld + (int64_t)(hk * R) * D + i];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int pr = warp; pr < R * (C / 32); pr += 8) {
+        const int r = pr % R, j = (pr / R) * 32 + lane;
+        float s = -INFINITY;
+        if (j < nv) {
+            const float* q = qs + r * D;
+            const uint8_t* kr = ks + j * KS;
+            float a = 0.f;
+#pragma unroll 4
+            for (int d8 = 0; d8 < D; d8 += 8) {
+                const uint4 kw = *reinterpret_cast<const uint4*>(kr + d8 * 2);
+                const float4 q0 = *reinterpret_cast<const float4*>(q + d8);
+                const float4 q1 = *reinterpret_cast<const float4*>(q + d8 + 4);
+                const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&kw.x));
+                const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&kw.y));
+                const float2 k2 = __half22float2(*reinterpret_cast<const __half2*>(&kw.z));
+                const float2 k3 = __half22float2(*reinterpret_cast<const __half2*>(&kw.w));
+                a = fmaf(q0.x, k0.x, a);
+                a = fmaf(q0.y, k0.y, a);
+                a = fmaf(q0.z, k1.x, a);
+                a = fmaf(q0.w, k1.y, a);
+                a = fmaf(q1.x, k2.x, a);
+                a = fmaf(q1.y, k2.y, a);
+                a = fmaf(q1.z, k3.x, a);
+                a = fmaf(q1.w, k3.y, a);
+            }
+            s = a * scale;
+        }
+        S[r * C + j] = s;
+    }
+    __syncthreads();
+    for (int r = warp; r < R; r += 8) {
+        const float s0 = S[r * C + lane], s1 = S[r * C + lane + 32];
+        const float m = warp_max(fmaxf(s0, s1));  // finite: position start is always kept
+        const float p0 = lane < nv ? expf(s0 - m) : 0.f;
+        const float p1 = lane + 32 < nv ? expf(s1 - m) : 0.f;
+        S[r * C + lane] = p0;
+        S[r * C + lane + 32] = p1;
+        const float l = warp_sum(p0 + p1);
+        if (lane == 0) {
+            ml[2 * r] = m;
+            ml[2 * r + 1] = l;
+        }
+    }
+    __syncthreads();
+    float* outp = part + (((int64_t)t * H + (int64_t)hk * R) * n_chunk + c) * (D + 2);
+    for (int i = threadIdx.x; i < R * (D / 2); i += blockDim.x) {
+        const int r = i / (D / 2), dp = i % (D / 2);
+        const float* P = S + r * C;
+        float ax = 0.f, ay = 0.f;
+        for (int j = 0; j < nv; ++j) {
+            const float pj = P[j];
+            const float2 vv = __half22float2(*reinterpret_cast<const __half2*>(vs + j * KS + dp * 4));
+            ax = fmaf(pj, vv.x, ax);
+            ay = fmaf(pj, vv.y, ay);
+        }
+        float* op = outp + (int64_t)r * n_chunk * (D + 2);
+        op[2 + 2 * dp] = ax;
+        op[3 + 2 * dp] = ay;
+        if (dp == 0) {
+            op[0] = ml[2 * r];
+            op[1] = ml[2 * r + 1];
+        }
+    }
+}
+
+// CTA = (token, head), D threads: out = sum_c e^(m_c - M) acc_c / sum_c e^(m_c - M) l_c.
+__global__ void attn_combine_kernel(const float* __restrict__ part, int H, int D, int n_chunk,
+                                    const int64_t* __restrict__ pos, float* __restrict__ att) {
+    const int t = (int)blockIdx.x / H, h = (int)blockIdx.x % H;
+    const int nc = (int)(pos[t] / kAttnChunk) + 1;
+    const float* pb = part + ((int64_t)t * H + h) * n_chunk * (D + 2);
+    float M = -INFINITY;
+    for (int c = 0; c < nc; ++c) M = fmaxf(M, pb[(int64_t)c * (D + 2)]);
+    float L = 0.f, acc = 0.f;
+    for (int c = 0; c < nc; ++c) {
+        const float* q = pb + (int64_t)c * (D + 2);
+        const float e = expf(q[0] - M);
+        L = fmaf(e, q[1], L);
+        acc = fmaf(e, q[2 + threadIdx.x], acc);
+    }
+    att[((int64_t)t * H + h) * D + threadIdx.x] = acc / fmaxf(L, 1e-30f);
+}
+
+// ------------------------------------------------------------------ launchers
+template <int DT>
+cudaError_t gemv_dense_dt(const QMat& W, const QInput& in, int T, float* y, int ldy, int n_sm, cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    const int nch = Layout<DT>::chunks(W.cols);
+    const dim3 grid((unsigned)std::max(1, std::min((W.rows + 7) / 8, n_sm * 4)), (unsigned)((T + kTokGroup - 1) / kTokGroup));
+    if (T == 1 && nch <= 32 * gemv_cpl<DT>())
+        dense_gemv_kernel<DT, true><<<grid, 256, 0, s>>>(W, in, T, y, ldy);
+    else
+        dense_gemv_kernel<DT, false><<<grid, 256, 0, s>>>(W, in, T, y, ldy);
+    return cudaGetLastError();
+}
+
+cudaError_t gemv_dense(const QMat& W, const QInput& in, int T, float* y, int ldy, int n_sm, cudaStream_t s) {
+    if (W.dtype == AERO_DT_Q8_0) return gemv_dense_dt<AERO_DT_Q8_0>(W, in, T, y, ldy, n_sm, s);
+    if (W.dtype == AERO_DT_Q4_K) return gemv_dense_dt<AERO_DT_Q4_K>(W, in, T, y, ldy, n_sm, s);
+    return cudaErrorInvalidValue;
+}
+
+template <int NV>
+size_t attn_smem(int R) {
+    return (size_t)2 * kAttnChunk * (NV * 64 + 16) + (size_t)R * NV * 32 * 4 + (size_t)R * kAttnChunk * 4 + (size_t)R * 8;
+}
+
+template <int NV>
+cudaError_t attention_nv(float* qkv, int ld, int T, int H, int HK, const float* qn, const float* kn, float eps,
+                         float base, const int64_t* pos, const int32_t* seq, __half* kc, __half* vc, int n_ctx,
+                         float* part, int n_chunk, float* att, cudaStream_t s) {
+    const int per = H + 2 * HK;
+    qk_rope_kv_kernel<NV><<<(unsigned)((T * per + 3) / 4), 128, 0, s>>>(qkv, T, H, HK, ld, qn, kn, eps, base, pos, seq,
+                                                                        kc, vc, n_ctx);
+    const int R = H / HK;
+    const size_t smem = attn_smem<NV>(R);
+    static thread_local size_t smem_set = 0;
+    if (smem > 48 * 1024 && smem > smem_set) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(attn_partial_kernel<NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        smem_set = smem;
+    }
+    const float scale = 1.0f / std::sqrt((float)(NV * 32));
+    attn_partial_kernel<NV><<<dim3((unsigned)n_chunk, (unsigned)(T * HK)), 256, smem, s>>>(
+        qkv, ld, H, HK, kc, vc, n_ctx, pos, seq, scale, part, n_chunk);
+    attn_combine_kernel<<<(unsigned)(T * H), NV * 32, 0, s>>>(part, H, NV * 32, n_chunk, pos, att);
+    return cudaGetLastError();
+}
+
+cudaError_t attention(int D, float* qkv, int ld, int T, int H, int HK, const float* qn, const float* kn, float eps,
+                      float base, const int64_t* pos, const int32_t* seq, __half* kc, __half* vc, int n_ctx,
+                      float* part, int n_chunk, float* att, cudaStream_t s) {
+    switch (D) {
+        case 64: return attention_nv<2>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, s);
+        case 128: return attention_nv<4>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, s);
+        case 192: return attention_nv<6>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, s);
+        case 256: return attention_nv<8>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, s);
+    }
+    return cudaErrorInvalidValue;
+}
+
+// ------------------------------------------------------------------ host side
+struct DLayer {
+    QMat qkv{}, o{};
+    float *attn_norm = nullptr, *ffn_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+    void* moe = nullptr;
+    bool own_moe = false;
+    __half *kc = nullptr, *vc = nullptr;
+};
+
+struct Decoder {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    int n_layer = 0, d = 0, H = 0, HK = 0, D = 0, vocab = 0, n_seq = 0, n_ctx = 0, n_chunk = 0, n_sm = 148;
+    float eps = 1e-6f, rope_base = 10000.f;
+    QMat embd{}, head{};
+    float* out_norm = nullptr;
+    std::vector<DLayer> L;
+    struct Alloc {
+        void* p;
+        size_t bytes;
+        int cls;
+    };
+    std::vector<Alloc> allocs;
+    // step scratch, for up to cap tokens
+    int cap = 0;
+    void* sbase = nullptr;
+    size_t sbytes = 0;
+    float *x = nullptr, *h32 = nullptr, *qkv = nullptr, *att = nullptr, *o = nullptr, *dm = nullptr, *part = nullptr,
+          *logits = nullptr;
+    int32_t *tok = nullptr, *seq = nullptr;
+    int64_t* pos = nullptr;
+    QInput hq{}, aq{};
+    std::string err;
+    // profiling
+    bool prof = false;
+    double ms[5] = {};
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> ev_phase;
+    int n_ev = 0;
+
+    bool fail(const char* fmt, ...) {
+        char buf[512];
+        va_list ap;
+        va_start(ap, fmt);
+        std::vsnprintf(buf, sizeof(buf), fmt, ap);
+        va_end(ap);
+        err = buf;
+        return false;
+    }
+    bool ok(cudaError_t e, const char* what) {
+        if (e == cudaSuccess) return true;
+        cudaGetLastError();
+        return fail("%s: %s", what, cudaGetErrorString(e));
+    }
+    void* alloc(size_t bytes, int cls, const char* what) {
+        void* p = nullptr;
+        if (guarded_malloc(&p, bytes, cls) != cudaSuccess) {
+            cudaGetLastError();
+            fail("device allocation of %zu bytes for %s refused (memory guard budget or device memory)", bytes, what);
+            return nullptr;
+        }
+        allocs.push_back({p, bytes, cls});
+        return p;
+    }
+    void mark(int phase) {
+        if (!prof) return;
+        if (n_ev == (int)ev.size()) {
+            cudaEvent_t e;
+            cudaEventCreate(&e);
+            ev.push_back(e);
+            ev_phase.push_back(0);
+        }
+        ev_phase[(size_t)n_ev] = phase;
+        cudaEventRecord(ev[(size_t)n_ev++], stream);
+    }
+    void collect() {
+        if (!prof || n_ev < 2) {
+            n_ev = 0;
+            return;
+        }
+        cudaEventSynchronize(ev[(size_t)n_ev - 1]);
+        for (int i = 0; i + 1 < n_ev; ++i) {
+            float m = 0.f;
+            cudaEventElapsedTime(&m, ev[(size_t)i], ev[(size_t)i + 1]);
+            ms[ev_phase[(size_t)i]] += m;
+        }
+        n_ev = 0;
+    }
+    ~Decoder() {
+        if (stream) cudaStreamSynchronize(stream);
+        for (auto& l : L)
+            if (l.own_moe && l.moe) aero_cuda_moe_close(l.moe);
+        for (auto& a : allocs) guarded_free(a.p, a.bytes, a.cls);
+        if (sbase) guarded_free(sbase, sbytes, kScratch);
+        for (auto e : ev) cudaEventDestroy(e);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+int64_t row_bytes_gguf(int dt, int cols) {
+    return dt == AERO_DT_Q8_0 ? (int64_t)cols / 32 * 34 : dt == AERO_DT_Q4_K ? (int64_t)cols / 256 * 144 : -1;
+}
+
+// A (rows, cols) quantised matrix for the dense GEMVs: planes allocated here,
+// filled by put_rows.
+bool alloc_qmat(Decoder& g, int dt, int rows, int cols, QMat& m, const char* what) {
+    if (dt != AERO_DT_Q8_0 && dt != AERO_DT_Q4_K)
+        return g.fail("%s: ggml type %d (the decoder reads Q8_0 and Q4_K projections)", what, dt);
+    if (cols % (dt == AERO_DT_Q8_0 ? 32 : 256))
+        return g.fail("%s: row width %d is not a multiple of the block", what, cols);
+    m.dtype = dt;
+    m.rows = rows;
+    m.cols = cols;
+    m.n_expert = 1;
+    m.qs_estride = align128((int64_t)rows * qm_row_qs_bytes(dt, cols));
+    m.meta_estride = align128((int64_t)rows * qm_row_meta_bytes(dt, cols));
+    m.qs = (const uint8_t*)g.alloc((size_t)m.qs_estride, kWeightsResident, what);
+    m.meta = m.qs ? (const uint8_t*)g.alloc((size_t)m.meta_estride, kWeightsResident, what) : nullptr;
+    return m.meta != nullptr;
+}
+
+bool put_rows(Decoder& g, QMat& m, int row0, const aero_cuda_tensor& t, int rows, const char* what) {
+    if (t.dtype != m.dtype) return g.fail("%s: ggml type %d, expected %d", what, t.dtype, m.dtype);
+    const int64_t rb = row_bytes_gguf(m.dtype, m.cols);
+    const int64_t need = rb * rows;
+    if (!t.data || t.nbytes < need) return g.fail("%s: %lld bytes given, %lld needed", what, (long long)t.nbytes, (long long)need);
+    const bool dev = is_device_ptr(t.data);
+    const uint8_t* src = static_cast<const uint8_t*>(t.data);
+    void* stage = nullptr;
+    const int64_t chunk_rows = std::max<int64_t>(1, std::min<int64_t>(rows, (128ll << 20) / rb));
+    if (!dev) {
+        if (guarded_malloc(&stage, (size_t)(chunk_rows * rb), kScratch) != cudaSuccess) {
+            cudaGetLastError();
+            return g.fail("%s: staging buffer refused", what);
+        }
+    } else if (m.dtype == AERO_DT_Q4_K && ((uintptr_t)src & 15) != 0) {
+        return g.fail("%s: device source is not 16-byte aligned", what);
+    }
+    bool good = true;
+    uint8_t* qs = const_cast<uint8_t*>(m.qs) + (int64_t)row0 * qm_row_qs_bytes(m.dtype, m.cols);
+    uint8_t* meta = const_cast<uint8_t*>(m.meta) + (int64_t)row0 * qm_row_meta_bytes(m.dtype, m.cols);
+    for (int64_t r0 = 0; r0 < rows && good; r0 += chunk_rows) {
+        const int64_t n = std::min<int64_t>(chunk_rows, rows - r0);
+        const uint8_t* s = src + r0 * rb;
+        if (!dev) {
+            good = g.ok(cudaMemcpyAsync(stage, s, (size_t)(n * rb), cudaMemcpyHostToDevice, g.stream), what);
+            s = static_cast<const uint8_t*>(stage);
+        }
+        if (good)
+            good = g.ok(launch_repack(m.dtype, s, n, m.cols, (int)n, 0, qs + r0 * qm_row_qs_bytes(m.dtype, m.cols),
+                                      meta + r0 * qm_row_meta_bytes(m.dtype, m.cols), m.qs_estride, m.meta_estride,
+                                      g.stream),
+                        what);
+        if (good) good = g.ok(cudaStreamSynchronize(g.stream), what);
+    }
+    if (stage) guarded_free(stage, (size_t)(chunk_rows * rb), kScratch);
+    return good;
+}
+
+float* put_f32(Decoder& g, const float* src, int n, const char* what) {
+    if (!src) {
+        g.fail("%s is required", what);
+        return nullptr;
+    }
+    float* p = (float*)g.alloc((size_t)n * 4, kWeightsResident, what);
+    if (!p) return nullptr;
+    if (!g.ok(cudaMemcpyAsync(p, src, (size_t)n * 4, is_device_ptr(src) ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                              g.stream),
+              what))
+        return nullptr;
+    return p;
+}
+
+bool ensure_step_scratch(Decoder& g, int T) {
+    if (T <= g.cap && g.sbase) return true;
+    const int cap = std::max(T, std::max(2 * g.cap, 16));
+    const int HD = g.H * g.D, KD = g.HK * g.D, qkv_ld = HD + 2 * KD;
+    size_t off = 0;
+    auto take = [&](size_t b) {
+        const size_t o = off;
+        off += (b + 255) & ~(size_t)255;
+        return o;
+    };
+    const size_t o_x = take((size_t)cap * g.d * 4), o_h = take((size_t)cap * g.d * 4);
+    const size_t o_qkv = take((size_t)cap * qkv_ld * 4), o_att = take((size_t)cap * HD * 4);
+    const size_t o_o = take((size_t)cap * g.d * 4), o_dm = take((size_t)cap * g.d * 4);
+    const size_t o_part = take((size_t)cap * g.H * g.n_chunk * (g.D + 2) * 4);
+    const size_t o_hq = take(qinput_bytes(cap, g.d)), o_aq = take(qinput_bytes(cap, HD));
+    const size_t o_tok = take((size_t)cap * 4), o_seq = take((size_t)cap * 4), o_pos = take((size_t)cap * 8);
+    const size_t o_lg = take((size_t)cap * g.vocab * 4);
+    void* p = nullptr;
+    if (guarded_malloc(&p, off, kScratch) != cudaSuccess) {
+        cudaGetLastError();
+        return g.fail("step scratch of %zu bytes for %d tokens refused", off, cap);
+    }
+    if (g.sbase) {
+        cudaStreamSynchronize(g.stream);
+        guarded_free(g.sbase, g.sbytes, kScratch);
+    }
+    g.sbase = p;
+    g.sbytes = off;
+    g.cap = cap;
+    uint8_t* b = static_cast<uint8_t*>(p);
+    g.x = (float*)(b + o_x);
+    g.h32 = (float*)(b + o_h);
+    g.qkv = (float*)(b + o_qkv);
+    g.att = (float*)(b + o_att);
+    g.o = (float*)(b + o_o);
+    g.dm = (float*)(b + o_dm);
+    g.part = (float*)(b + o_part);
+    g.hq = qinput_at(b + o_hq, cap, g.d);
+    g.aq = qinput_at(b + o_aq, cap, HD);
+    g.tok = (int32_t*)(b + o_tok);
+    g.seq = (int32_t*)(b + o_seq);
+    g.pos = (int64_t*)(b + o_pos);
+    g.logits = (float*)(b + o_lg);
+    return true;
+}
+
+// The step on device buffers: head rows [r0, r0 + nh) of the step get logits
+// into lg (row stride vocab), nh = 0: none.
+bool run_step(Decoder& g, int T, int r0, int nh, float* lg) {
+    cudaStream_t s = g.stream;
+    const int HD = g.H * g.D, KD = g.HK * g.D, qkv_ld = HD + 2 * KD;
+    const size_t norm_smem = (size_t)g.d * 4 + 64;
+    g.mark(0);
+    const int64_t nb = (int64_t)T * (g.d / 32);
+    embed_q8_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, s>>>(g.embd, g.tok, T, g.x);
+    if (!g.ok(cudaGetLastError(), "embedding")) return false;
+    for (int l = 0; l < g.n_layer; ++l) {
+        DLayer& Ly = g.L[(size_t)l];
+        g.mark(0);
+        norm_kernel<<<(unsigned)T, 256, norm_smem, s>>>(g.x, g.d, l > 0 ? g.dm : nullptr, Ly.attn_norm, g.eps, 0, nullptr,
+                                                      g.hq);
+        g.mark(1);
+        if (!g.ok(gemv_dense(Ly.qkv, g.hq, T, g.qkv, qkv_ld, g.n_sm, s), "q/k/v projection")) return false;
+        g.mark(2);
+        if (!g.ok(attention(g.D, g.qkv, qkv_ld, T, g.H, g.HK, Ly.q_norm, Ly.k_norm, g.eps, g.rope_base, g.pos, g.seq,
+                            Ly.kc, Ly.vc, g.n_ctx, g.part, g.n_chunk, g.att, s),
+                  "attention"))
+            return false;
+        if (!g.ok(launch_qinput(g.att, T, HD, g.aq, s), "attention rows")) return false;
+        g.mark(1);
+        if (!g.ok(gemv_dense(Ly.o, g.aq, T, g.o, g.d, g.n_sm, s), "output projection")) return false;
+        g.mark(0);
+        norm_kernel<<<(unsigned)T, 256, norm_smem, s>>>(g.x, g.d, g.o, Ly.ffn_norm, g.eps, 0, g.h32, QInput{});
+        if (!g.ok(cudaGetLastError(), "norm")) return false;
+        g.mark(3);
+        if (aero_cuda_moe_forward(Ly.moe, l, g.h32, T, g.d, g.dm) != 1)
+            return g.fail("layer %d MoE: %s", l, aero_cuda_moe_last_error(Ly.moe));
+    }
+    g.mark(0);
+    // the last layer's FFN output joins the residual for every row; the head rows are normed
+    norm_kernel<<<(unsigned)T, 256, norm_smem, s>>>(g.x, g.d, g.dm, g.out_norm, g.eps, 0, nullptr,
+                                                  nh > 0 ? g.hq : QInput{});
+    if (!g.ok(cudaGetLastError(), "output norm")) return false;
+    if (nh > 0) {
+        g.mark(4);
+        QInput hq = g.hq;
+        hq.q1 += (int64_t)r0 * hq.K;
+        hq.q0 += (int64_t)r0 * hq.K;
+        hq.sx += (int64_t)r0 * (hq.K / 32);
+        hq.s16 += (int64_t)r0 * (hq.K / 16);
+        if (!g.ok(gemv_dense(g.head, hq, nh, lg, g.vocab, g.n_sm, s), "head")) return false;
+    }
+    g.mark(0);
+    return true;
+}
+
+bool step_entry(Decoder& g, const int32_t* tokens, const int32_t* seqs, const int64_t* positions, int T, float* logits,
+                bool last_only) {
+    if (T <= 0) return g.fail("T=%d", T);
+    if (!tokens || !positions) return g.fail("null tokens or positions");
+    std::set<std::pair<int32_t, int64_t>> seen;
+    for (int i = 0; i < T; ++i) {
+        const int32_t sq = seqs ? seqs[i] : 0;
+        if (tokens[i] < 0 || tokens[i] >= g.vocab) return g.fail("token %d = %d outside [0, %d)", i, tokens[i], g.vocab);
+        if (sq < 0 || sq >= g.n_seq) return g.fail("sequence %d = %d outside [0, %d)", i, sq, g.n_seq);
+        if (positions[i] < 0 || positions[i] >= g.n_ctx)
+            return g.fail("position %d = %lld outside [0, %d)", i, (long long)positions[i], g.n_ctx);
+        if (!seen.insert({sq, positions[i]}).second)
+            return g.fail("sequence %d position %lld appears twice in the step", sq, (long long)positions[i]);
+    }
+    if (cudaSetDevice(g.device) != cudaSuccess) return g.fail("cudaSetDevice(%d) failed", g.device);
+    if (!ensure_step_scratch(g, T)) return false;
+    // pageable host sources: each copy has taken the bytes when the call returns
+    if (!g.ok(cudaMemcpyAsync(g.tok, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, g.stream), "tokens") ||
+        !g.ok(cudaMemcpyAsync(g.pos, positions, (size_t)T * 8, cudaMemcpyHostToDevice, g.stream), "positions"))
+        return false;
+    if (seqs) {
+        if (!g.ok(cudaMemcpyAsync(g.seq, seqs, (size_t)T * 4, cudaMemcpyHostToDevice, g.stream), "sequences")) return false;
+    } else if (!g.ok(cudaMemsetAsync(g.seq, 0, (size_t)T * 4, g.stream), "sequences")) {
+        return false;
+    }
+    const int r0 = last_only ? T - 1 : 0, nh = logits ? (last_only ? 1 : T) : 0;
+    const bool dev_out = logits && is_device_ptr(logits);
+    float* lg = dev_out ? logits : g.logits;
+    if (!run_step(g, T, r0, nh, lg)) return false;
+    if (logits && !dev_out) {
+        if (!g.ok(cudaMemcpyAsync(logits, g.logits, (size_t)nh * g.vocab * 4, cudaMemcpyDeviceToHost, g.stream), "logits"))
+            return false;
+        if (!g.ok(cudaStreamSynchronize(g.stream), "step")) return false;
+        for (auto& l : g.L)
+            if (aero_cuda_moe_status(l.moe) != 0) return g.fail("a MoE layer's device wait gave up: the step is invalid");
+    }
+    g.collect();
+    return true;
+}
+
+Decoder* open_decoder(const aero_cuda_decoder_desc* d, std::string* why, bool own_moe) {
+    if (!d) {
+        *why = "null descriptor";
+        return nullptr;
+    }
+    auto* g = new Decoder();
+    auto bad = [&](const std::string& m) {
+        *why = m.empty() ? g->err : m;
+        delete g;  // closes the MoE handles it owns
+        return (Decoder*)nullptr;
+    };
+    if (d->n_layer > 0 && d->n_layer <= 4096 && d->layers) {
+        // take the handles first, so an owned one is closed whatever fails below
+        g->L.resize((size_t)d->n_layer);
+        for (int l = 0; l < d->n_layer; ++l) {
+            g->L[(size_t)l].moe = d->layers[l].moe;
+            g->L[(size_t)l].own_moe = own_moe;
+        }
+    }
+    g->device = d->device;
+    g->n_layer = d->n_layer;
+    g->d = d->n_embd;
+    g->H = d->n_head;
+    g->HK = d->n_head_kv;
+    g->D = d->head_dim;
+    g->vocab = d->vocab;
+    g->n_seq = d->n_seq;
+    g->n_ctx = d->n_ctx;
+    g->eps = d->eps;
+    g->rope_base = d->rope_base;
+    if (g->n_layer <= 0 || g->n_layer > 4096 || g->d <= 0 || g->d % 32 || g->vocab <= 0 || g->n_seq <= 0 || g->n_ctx <= 0)
+        return bad("n_layer, vocab, n_seq, n_ctx must be positive and n_embd a multiple of 32");
+    if (g->H <= 0 || g->HK <= 0 || g->H % g->HK || g->H / g->HK > kMaxGroup)
+        return bad("n_head must be a multiple of n_head_kv with at most 16 query heads per kv head");
+    if (g->D != 64 && g->D != 128 && g->D != 192 && g->D != 256) return bad("head_dim must be 64, 128, 192 or 256");
+    if (!d->layers) return bad("layers are required");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0) {
+        cudaGetLastError();
+        return bad("no CUDA device is available (this library has no CPU path)");
+    }
+    if (g->device < 0 || g->device >= ndev) return bad("device does not exist");
+    cudaSetDevice(g->device);
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, g->device) == cudaSuccess) g->n_sm = prop.multiProcessorCount;
+    if (cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking) != cudaSuccess) return bad("stream creation failed");
+    g->n_chunk = (g->n_ctx + kAttnChunk - 1) / kAttnChunk;
+    const int HD = g->H * g->D, KD = g->HK * g->D;
+    // weights
+    if (d->token_embd.dtype != AERO_DT_Q8_0) return bad("token_embd must be Q8_0");
+    if (!alloc_qmat(*g, AERO_DT_Q8_0, g->vocab, g->d, g->embd, "token_embd") ||
+        !put_rows(*g, g->embd, 0, d->token_embd, g->vocab, "token_embd"))
+        return bad("");
+    if (d->output.data) {
+        if (!alloc_qmat(*g, d->output.dtype, g->vocab, g->d, g->head, "output") ||
+            !put_rows(*g, g->head, 0, d->output, g->vocab, "output"))
+            return bad("");
+    } else {
+        g->head = g->embd;
+    }
+    g->out_norm = put_f32(*g, d->output_norm, g->d, "output_norm");
+    if (!g->out_norm) return bad("");
+    const size_t kv_bytes = (size_t)g->n_seq * g->HK * g->n_ctx * g->D * 2;
+    for (int l = 0; l < g->n_layer; ++l) {
+        const aero_cuda_decoder_layer& s = d->layers[l];
+        DLayer& Ly = g->L[(size_t)l];
+        if (!s.moe) return bad("layer " + std::to_string(l) + ": no MoE handle");
+        int32_t info[8] = {0};
+        aero_cuda_moe_info(s.moe, info);
+        if (info[0] != g->d) return bad("layer " + std::to_string(l) + ": the MoE handle's n_embd differs");
+        char what[64];
+        std::snprintf(what, sizeof(what), "blk.%d.attn_qkv", l);
+        if (s.attn_q.dtype != s.attn_k.dtype || s.attn_q.dtype != s.attn_v.dtype)
+            return bad(std::string(what) + ": q, k and v must share one ggml type");
+        if (!alloc_qmat(*g, s.attn_q.dtype, HD + 2 * KD, g->d, Ly.qkv, what) ||
+            !put_rows(*g, Ly.qkv, 0, s.attn_q, HD, what) || !put_rows(*g, Ly.qkv, HD, s.attn_k, KD, what) ||
+            !put_rows(*g, Ly.qkv, HD + KD, s.attn_v, KD, what))
+            return bad("");
+        std::snprintf(what, sizeof(what), "blk.%d.attn_output", l);
+        if (!alloc_qmat(*g, s.attn_output.dtype, g->d, HD, Ly.o, what) || !put_rows(*g, Ly.o, 0, s.attn_output, g->d, what))
+            return bad("");
+        Ly.attn_norm = put_f32(*g, s.attn_norm, g->d, "attn_norm");
+        Ly.ffn_norm = Ly.attn_norm ? put_f32(*g, s.ffn_norm, g->d, "post_attention_norm") : nullptr;
+        if (!Ly.ffn_norm) return bad("");
+        if (s.q_norm && !(Ly.q_norm = put_f32(*g, s.q_norm, g->D, "attn_q_norm"))) return bad("");
+        if (s.k_norm && !(Ly.k_norm = put_f32(*g, s.k_norm, g->D, "attn_k_norm"))) return bad("");
+        Ly.kc = (__half*)g->alloc(kv_bytes, kKVCache, "key cache");
+        Ly.vc = Ly.kc ? (__half*)g->alloc(kv_bytes, kKVCache, "value cache") : nullptr;
+        if (!Ly.vc) return bad("");
+        if (!g->ok(cudaMemsetAsync(Ly.kc, 0, kv_bytes, g->stream), "cache") ||
+            !g->ok(cudaMemsetAsync(Ly.vc, 0, kv_bytes, g->stream), "cache"))
+            return bad("");
+        aero_cuda_moe_set_stream(s.moe, g->stream);
+    }
+    if (!g->ok(cudaStreamSynchronize(g->stream), "upload")) return bad("");
+    return g;
+}
+
+}  // namespace
+}  // namespace aero
+
+using aero::Decoder;
+
+extern "C" {
+
+void* aero_cuda_decoder_open(const aero_cuda_decoder_desc* desc, char* err, int errlen) {
+    std::string why;
+    Decoder* g = aero::open_decoder(desc, &why, false);
+    if (!g && err && errlen > 0) std::snprintf(err, (size_t)errlen, "%s", why.c_str());
+    return g;
+}
+
+void* aero_cuda_decoder_open_gguf(const char* path, int device, int n_seq, int n_ctx, char* err, int errlen) {
+    auto put = [&](const std::string& m) {
+        if (err && errlen > 0) std::snprintf(err, (size_t)errlen, "%s", m.c_str());
+        return (void*)nullptr;
+    };
+    aero::GgufFile f;
+    std::string why;
+    if (!path || !f.open(path, &why)) return put(path ? why : "null path");
+    const std::string arch = f.arch();
+    auto hp = [&](const char* key, int64_t def) {
+        int64_t v = def;
+        if (!f.get_int(arch + "." + key, &v)) f.get_int(key, &v);
+        return v;
+    };
+    auto hpf = [&](const char* key, double def) {
+        double v = def;
+        if (!f.get_float(arch + "." + key, &v)) f.get_float(key, &v);
+        return v;
+    };
+    aero_cuda_decoder_desc d{};
+    d.n_layer = (int)hp("block_count", 0);
+    d.n_embd = (int)hp("embedding_length", 0);
+    d.n_head = (int)hp("attention.head_count", 0);
+    d.n_head_kv = (int)hp("attention.head_count_kv", d.n_head);
+    d.head_dim = (int)hp("attention.key_length", d.n_head > 0 ? d.n_embd / d.n_head : 0);
+    if (hp("attention.value_length", d.head_dim) != d.head_dim) return put("value_length != key_length is not supported");
+    if (hp("rope.dimension_count", d.head_dim) != d.head_dim) return put("partial RoPE is not supported");
+    d.eps = (float)hpf("attention.layer_norm_rms_epsilon", 1e-6);
+    d.rope_base = (float)hpf("rope.freq_base", 10000.0);
+    d.n_seq = n_seq;
+    d.n_ctx = n_ctx;
+    d.device = device;
+    const aero::GgufTensor* te = f.find("token_embd.weight");
+    const aero::GgufTensor* to = f.find("output.weight");
+    const aero::GgufTensor* tn = f.find("output_norm.weight");
+    if (!te || te->dims.size() != 2 || !tn || tn->type != 0) return put("token_embd.weight / output_norm.weight (F32) missing");
+    d.vocab = (int)te->shape(0);
+    d.token_embd = {te->type, 0, f.data(*te), te->nbytes};
+    if (to) d.output = {to->type, 0, f.data(*to), to->nbytes};
+    d.output_norm = reinterpret_cast<const float*>(f.data(*tn));
+    if (d.n_layer <= 0 || d.n_layer > 4096) return put(arch + ".block_count missing or out of range");
+    std::vector<aero_cuda_decoder_layer> layers((size_t)d.n_layer);
+    std::vector<void*> moes;
+    auto close_moes = [&]() {
+        for (void* m : moes) aero_cuda_moe_close(m);
+    };
+    for (int l = 0; l < d.n_layer; ++l) {
+        const std::string p = "blk." + std::to_string(l) + ".";
+        auto T = [&](const char* n) { return f.find(p + n); };
+        const aero::GgufTensor *an = T("attn_norm.weight"), *pn = T("post_attention_norm.weight");
+        if (!pn) pn = T("ffn_norm.weight");
+        const aero::GgufTensor *q = T("attn_q.weight"), *k = T("attn_k.weight"), *v = T("attn_v.weight"),
+                               *o = T("attn_output.weight"), *qn = T("attn_q_norm.weight"), *kn = T("attn_k_norm.weight");
+        if (!an || !pn || !q || !k || !v || !o || an->type != 0 || pn->type != 0 || (qn && qn->type != 0) ||
+            (kn && kn->type != 0)) {
+            close_moes();
+            return put(p + "attention tensors or F32 norms missing");
+        }
+        char e2[512] = {0};
+        void* m = aero_cuda_moe_open_gguf(path, l, device, 0, 0, e2, sizeof(e2));
+        if (!m) {
+            close_moes();
+            return put(p + "MoE: " + e2);
+        }
+        moes.push_back(m);
+        aero_cuda_decoder_layer& L = layers[(size_t)l];
+        L.attn_q = {q->type, 0, f.data(*q), q->nbytes};
+        L.attn_k = {k->type, 0, f.data(*k), k->nbytes};
+        L.attn_v = {v->type, 0, f.data(*v), v->nbytes};
+        L.attn_output = {o->type, 0, f.data(*o), o->nbytes};
+        L.attn_norm = reinterpret_cast<const float*>(f.data(*an));
+        L.ffn_norm = reinterpret_cast<const float*>(f.data(*pn));
+        L.q_norm = qn ? reinterpret_cast<const float*>(f.data(*qn)) : nullptr;
+        L.k_norm = kn ? reinterpret_cast<const float*>(f.data(*kn)) : nullptr;
+        L.moe = m;
+    }
+    d.layers = layers.data();
+    Decoder* g = aero::open_decoder(&d, &why, true);  // owns the MoE handles, closed on failure too
+    if (!g) return put(why);
+    return g;
+}
+
+int aero_cuda_decoder_forward(void* dec, const int32_t* tokens, int n_tokens, const int64_t* positions, float* logits) {
+    auto* g = static_cast<Decoder*>(dec);
+    if (!g || !logits) return 0;
+    return aero::step_entry(*g, tokens, nullptr, positions, n_tokens, logits, true) ? 1 : 0;
+}
+
+int aero_cuda_decoder_step(void* dec, const int32_t* tokens, const int32_t* seqs, const int64_t* positions, int T,
+                           float* logits) {
+    auto* g = static_cast<Decoder*>(dec);
+    if (!g) return -1;
+    return aero::step_entry(*g, tokens, seqs, positions, T, logits, false) ? 0 : -1;
+}
+
+int aero_cuda_decoder_kv(void* dec, int layer, void** k, void** v) {
+    auto* g = static_cast<Decoder*>(dec);
+    if (!g || layer < 0 || layer >= g->n_layer || !k || !v) return -1;
+    *k = g->L[(size_t)layer].kc;
+    *v = g->L[(size_t)layer].vc;
+    return 0;
+}
+
+int aero_cuda_decoder_profile(void* dec, int on, double* ms) {
+    auto* g = static_cast<Decoder*>(dec);
+    if (!g) return -1;
+    if (ms) {
+        for (int i = 0; i < 5; ++i) ms[i] = g->ms[i];
+        for (double& m : g->ms) m = 0.0;
+    }
+    g->prof = on != 0;
+    return 0;
+}
+
+int aero_cuda_decoder_info(void* dec, int64_t* out8) {
+    auto* g = static_cast<Decoder*>(dec);
+    if (!g || !out8) return -1;
+    const int64_t v[8] = {g->n_layer, g->d, g->H, g->HK, g->D, g->vocab, g->n_seq, g->n_ctx};
+    for (int i = 0; i < 8; ++i) out8[i] = v[i];
+    return 0;
+}
+
+const char* aero_cuda_decoder_last_error(void* dec) {
+    auto* g = static_cast<Decoder*>(dec);
+    return g ? g->err.c_str() : "null decoder";
+}
+
+void aero_cuda_decoder_close(void* dec) { delete static_cast<Decoder*>(dec); }
+
+}  // extern "C"

@@ -153,9 +153,19 @@ bool GgufFile::open(const std::string& path, std::string* err) {
         int64_t iv = 0;
         std::string sv;
         const bool has_int = t != V_STR && t != V_ARR && t != V_F32 && t != V_F64;
+        const size_t at = c.off;
         c.value(t, &iv, &sv);
         if (has_int) ints_[key] = iv;
         if (t == V_STR) strs_[key] = sv;
+        if (c.ok && t == V_F32) {
+            float f;
+            std::memcpy(&f, map_ + at, 4);
+            floats_[key] = f;
+        } else if (c.ok && t == V_F64) {
+            double f;
+            std::memcpy(&f, map_ + at, 8);
+            floats_[key] = f;
+        }
     }
     if (!c.ok) {
         *err = path + ": truncated metadata";
@@ -214,6 +224,13 @@ const uint8_t* GgufFile::data(const GgufTensor& t) const { return map_ + data_of
 bool GgufFile::get_int(const std::string& key, int64_t* v) const {
     auto it = ints_.find(key);
     if (it == ints_.end()) return false;
+    *v = it->second;
+    return true;
+}
+
+bool GgufFile::get_float(const std::string& key, double* v) const {
+    auto it = floats_.find(key);
+    if (it == floats_.end()) return false;
     *v = it->second;
     return true;
 }

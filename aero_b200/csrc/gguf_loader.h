@@ -31,6 +31,7 @@ public:
     const GgufTensor* find(const std::string& name) const;
     const uint8_t* data(const GgufTensor& t) const;
     bool get_int(const std::string& key, int64_t* v) const;
+    bool get_float(const std::string& key, double* v) const;  // F32 / F64 values
     std::string arch() const;
     uint64_t alignment() const { return alignment_; }
 
@@ -40,6 +41,7 @@ private:
     uint32_t version_ = 0;
     uint64_t alignment_ = 32, data_off_ = 0;
     std::map<std::string, int64_t> ints_;
+    std::map<std::string, double> floats_;
     std::map<std::string, std::string> strs_;
     std::map<std::string, GgufTensor> tensors_;
 };

@@ -230,6 +230,8 @@ bool guard_try_reserve(size_t bytes, int cls);
 void guard_release(size_t bytes, int cls);
 // cudaMalloc charged to the guard; returns cudaErrorMemoryAllocation when refused.
 cudaError_t guarded_malloc(void** p, size_t bytes, int cls);
+// Device (or managed) memory, as cudaPointerGetAttributes reports it.
+bool is_device_ptr(const void* p);
 void guarded_free(void* p, size_t bytes, int cls);
 
 std::string fmt_bytes(size_t b);

@@ -22,12 +22,6 @@
 #include "internal.h"
 
 namespace aero {
-namespace {
-
-thread_local std::string g_free_error;
-
-int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
-
 bool is_device_ptr(const void* p) {
     if (!p) return false;
     cudaPointerAttributes a;
@@ -37,6 +31,12 @@ bool is_device_ptr(const void* p) {
     }
     return a.type == cudaMemoryTypeDevice || a.type == cudaMemoryTypeManaged;
 }
+
+namespace {
+
+thread_local std::string g_free_error;
+
+int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 
 struct Alloc {
     void* p;

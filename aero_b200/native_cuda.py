@@ -55,6 +55,21 @@ class Desc(Structure):
     ]
 
 
+class DecoderLayer(Structure):
+    """aero_cuda_decoder_layer (include/aero_cuda_decoder.h)."""
+    _fields_ = [("attn_q", Tensor), ("attn_k", Tensor), ("attn_v", Tensor), ("attn_output", Tensor),
+                ("attn_norm", c_void_p), ("ffn_norm", c_void_p), ("q_norm", c_void_p), ("k_norm", c_void_p),
+                ("moe", c_void_p)]
+
+
+class DecoderDesc(Structure):
+    """aero_cuda_decoder_desc (include/aero_cuda_decoder.h)."""
+    _fields_ = [("n_layer", c_int32), ("n_embd", c_int32), ("n_head", c_int32), ("n_head_kv", c_int32),
+                ("head_dim", c_int32), ("vocab", c_int32), ("n_seq", c_int32), ("n_ctx", c_int32),
+                ("device", c_int32), ("reserved", c_int32), ("eps", c_float), ("rope_base", c_float),
+                ("token_embd", Tensor), ("output", Tensor), ("output_norm", c_void_p), ("layers", POINTER(DecoderLayer))]
+
+
 EVICT_FN = CFUNCTYPE(c_size_t, c_void_p, c_size_t)
 BREACH_FN = CFUNCTYPE(None, c_void_p, c_size_t, c_size_t)
 
@@ -72,6 +87,15 @@ SYMBOLS = [
     ("aero_cuda_moe_model_forward", c_int, [_P, c_int, _P, c_int, c_int, _P]),
     ("aero_cuda_moe_model_layer", c_void_p, [_P, c_int]),
     ("aero_cuda_moe_model_close", None, [_P]),
+    ("aero_cuda_decoder_open", c_void_p, [POINTER(DecoderDesc), c_char_p, c_int]),
+    ("aero_cuda_decoder_open_gguf", c_void_p, [c_char_p, c_int, c_int, c_int, c_char_p, c_int]),
+    ("aero_cuda_decoder_forward", c_int, [_P, _P, c_int, _P, _P]),
+    ("aero_cuda_decoder_step", c_int, [_P, _P, _P, _P, c_int, _P]),
+    ("aero_cuda_decoder_kv", c_int, [_P, c_int, POINTER(c_void_p), POINTER(c_void_p)]),
+    ("aero_cuda_decoder_profile", c_int, [_P, c_int, _P]),
+    ("aero_cuda_decoder_info", c_int, [_P, _P]),
+    ("aero_cuda_decoder_last_error", c_char_p, [_P]),
+    ("aero_cuda_decoder_close", None, [_P]),
     ("aero_cuda_moe_forward", c_int, [_P, c_int, _P, c_int, c_int, _P]),
     ("aero_cuda_moe_ffn_block", c_int, [_P, _P, _P, c_int, _P]),
     ("aero_cuda_moe_router_logits", c_int, [_P, _P, c_int, _P]),

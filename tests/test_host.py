@@ -2,6 +2,7 @@
 library's exports, the memory guard's accounting, and the GGUF parser's
 refusals."""
 
+import glob
 import os
 import re
 import struct
@@ -57,9 +58,14 @@ def test_gguf_writer_layout(tmp_path):
 
 
 # ---------------------------------------------------------------- the C ABI
+def _headers():
+    """Every header under include/, comments removed."""
+    srcs = [open(p).read() for p in sorted(glob.glob(os.path.join(ROOT, "include", "*.h")))]
+    return re.sub(r"/\*.*?\*/", "", "\n".join(srcs), flags=re.S)
+
+
 def _header_functions():
-    src = open(os.path.join(ROOT, "include", "aero_cuda_moe.h")).read()
-    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    src = _headers()
     names = re.findall(r"\b(aero_cuda_\w+)\s*\(", src)
     return sorted(set(n for n in names if not n.endswith("_fn")))
 
@@ -257,8 +263,7 @@ def test_ctypes_signatures_match_header():
     """Every ctypes declaration has as many arguments as the header's prototype."""
     from aero_b200 import native_cuda as nc
 
-    src = open(os.path.join(ROOT, "include", "aero_cuda_moe.h")).read()
-    src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
+    src = _headers()
     protos = {}
     for m in re.finditer(r"\b(aero_cuda_\w+)\s*\(([^;{]*?)\)\s*;", src, flags=re.S):
         name, params = m.group(1), " ".join(m.group(2).split())
