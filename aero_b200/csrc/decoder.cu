@@ -435,7 +435,7 @@ struct DLayer {
 
 struct Decoder {
     int device = 0;
-    cudaStream_t stream = nullptr;
+    cudaStream_t stream = nullptr, own_stream = nullptr;
     int n_layer = 0, d = 0, H = 0, HK = 0, D = 0, vocab = 0, n_seq = 0, n_ctx = 0, n_chunk = 0, n_sm = 148;
     float eps = 1e-6f, rope_base = 10000.f;
     QMat embd{}, head{};
@@ -514,12 +514,15 @@ struct Decoder {
     }
     ~Decoder() {
         if (stream) cudaStreamSynchronize(stream);
+        // borrowed MoE handles go back to their own streams
+        for (auto& l : L)
+            if (!l.own_moe && l.moe) aero_cuda_moe_set_stream(l.moe, nullptr);
         for (auto& l : L)
             if (l.own_moe && l.moe) aero_cuda_moe_close(l.moe);
         for (auto& a : allocs) guarded_free(a.p, a.bytes, a.cls);
         if (sbase) guarded_free(sbase, sbytes, kScratch);
         for (auto e : ev) cudaEventDestroy(e);
-        if (stream) cudaStreamDestroy(stream);
+        if (own_stream) cudaStreamDestroy(own_stream);
     }
 };
 
@@ -778,7 +781,8 @@ Decoder* open_decoder(const aero_cuda_decoder_desc* d, std::string* why, bool ow
     cudaSetDevice(g->device);
     cudaDeviceProp prop;
     if (cudaGetDeviceProperties(&prop, g->device) == cudaSuccess) g->n_sm = prop.multiProcessorCount;
-    if (cudaStreamCreateWithFlags(&g->stream, cudaStreamNonBlocking) != cudaSuccess) return bad("stream creation failed");
+    if (cudaStreamCreateWithFlags(&g->own_stream, cudaStreamNonBlocking) != cudaSuccess) return bad("stream creation failed");
+    g->stream = g->own_stream;
     g->n_chunk = (g->n_ctx + kAttnChunk - 1) / kAttnChunk;
     const int HD = g->H * g->D, KD = g->HK * g->D;
     // weights
@@ -938,6 +942,16 @@ int aero_cuda_decoder_step(void* dec, const int32_t* tokens, const int32_t* seqs
     auto* g = static_cast<Decoder*>(dec);
     if (!g) return -1;
     return aero::step_entry(*g, tokens, seqs, positions, T, logits, false) ? 0 : -1;
+}
+
+int aero_cuda_decoder_set_stream(void* dec, void* stream) {
+    auto* g = static_cast<Decoder*>(dec);
+    if (!g) return -1;
+    cudaStreamSynchronize(g->stream);
+    g->stream = stream ? static_cast<cudaStream_t>(stream) : g->own_stream;
+    for (auto& l : g->L)
+        if (l.moe) aero_cuda_moe_set_stream(l.moe, g->stream);
+    return 0;
 }
 
 int aero_cuda_decoder_kv(void* dec, int layer, void** k, void** v) {

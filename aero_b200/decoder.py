@@ -136,6 +136,11 @@ class CudaDecoder:
             raise RuntimeError(f"decoder step refused: {self.last_error()}")
         return out
 
+    def set_stream(self, stream) -> None:
+        """Run on a cudaStream_t (int) or torch.cuda.Stream; None restores the decoder's own."""
+        st = getattr(stream, "cuda_stream", stream)
+        self._lib.aero_cuda_decoder_set_stream(self.handle, st or None)
+
     def kv(self, layer: int):
         """Device addresses of the layer's key and value caches."""
         k, v = ctypes.c_void_p(), ctypes.c_void_p()

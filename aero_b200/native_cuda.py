@@ -91,6 +91,7 @@ SYMBOLS = [
     ("aero_cuda_decoder_open_gguf", c_void_p, [c_char_p, c_int, c_int, c_int, c_char_p, c_int]),
     ("aero_cuda_decoder_forward", c_int, [_P, _P, c_int, _P, _P]),
     ("aero_cuda_decoder_step", c_int, [_P, _P, _P, _P, c_int, _P]),
+    ("aero_cuda_decoder_set_stream", c_int, [_P, _P]),
     ("aero_cuda_decoder_kv", c_int, [_P, c_int, POINTER(c_void_p), POINTER(c_void_p)]),
     ("aero_cuda_decoder_profile", c_int, [_P, c_int, _P]),
     ("aero_cuda_decoder_info", c_int, [_P, _P]),

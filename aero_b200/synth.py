@@ -104,13 +104,13 @@ def _quant_np(seed, i, n, dtype):
     return np.frombuffer(quantize(w, dtype), dtype=np.uint8)
 
 
-def _quant_gpu(seed, i, n, dtype):
+def _quant_gpu(seed, i, n, dtype, scale=0.02):
     import torch
 
     from . import native_cuda as nc
     g = torch.Generator(device="cuda")
     g.manual_seed(seed * 1000 + i)
-    w = torch.randn(n, generator=g, device="cuda", dtype=torch.float32) * 0.02
+    w = torch.randn(n, generator=g, device="cuda", dtype=torch.float32) * scale
     if dtype == DTYPE_F32:
         return w.cpu().numpy()
     b = nc.quantize(dtype, w)
@@ -305,6 +305,8 @@ def make_decoder(spec: DecoderSpec, seed: int = 0, device_gen: bool = False) -> 
         n = int(np.prod(shape))
         if scale == 0.02:
             raw = gen(seed, i, n, dt)
+        elif device_gen:
+            raw = _quant_gpu(seed, i, n, dt, scale)
         else:
             w = _normal_np(seed, i, n, scale)
             raw = w if dt == DTYPE_F32 else np.frombuffer(quantize(w, dt), dtype=np.uint8)

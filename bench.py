@@ -251,6 +251,7 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="skip the decode sub-record")
+    ap.add_argument("--no-decoder", action="store_true", help="skip the config-4 decoder sub-record")
     ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
                     help="expert parallel (N > 1): rows cross by peer-memory stores (default) or NCCL all-to-all")
     ap.add_argument("--profile", action="store_true",
@@ -550,6 +551,8 @@ def run_ours(args, ws, rank, dev, cuda, wl, spec, T, seed, clk):
         moe.set_profiling(False)
     if ws == 1 and not args.no_decode and not wl.name.startswith(("c1", "c3", "c4")):
         result["decode"] = decode_records(args, dev, stream, pk)
+    if ws == 1 and not args.no_decoder and not wl.name.startswith(("c1", "c3", "c4")):
+        result["decoder"] = decoder_records(args, dev, stream, pk)
     if rank == 0 and ws == 1 and not args.no_cpu_baseline:
         lg = x_host @ layer.router.T + (layer.router_bias if layer.router_bias is not None else 0)
         threads = os.cpu_count() or 1
@@ -612,6 +615,107 @@ def decode_records(args, dev, stream, pk) -> dict:
                     "traffic_per_call": traffic_record(wl.name, "decode_layer")}
         L.close()
         del x, o
+    return out
+
+
+def decoder_step_bytes(spec, B: int, kv_len: int, experts_per_layer: float) -> int:
+    """Algorithmic HBM bytes of one decoder step over B sequences whose caches hold
+    kv_len positions: every layer's q/k/v/o projections and f32 router once, the
+    distinct experts the step routes to (gate, up, down), each sequence's K and V
+    rows read (and the new ones written), the embedding rows and the head once."""
+    from aero_b200 import synth
+    H, HK, D, d = spec.n_head, spec.n_kv, spec.head_dim, spec.d
+    m = spec.moe
+    q8 = lambda n: n // 32 * 34  # noqa: E731
+    attn = q8((H * D + 2 * HK * D) * d) + q8(d * H * D)
+    per_expert = layer_bytes(synth.LayerSpec(m.d, 1, 1, m.F, 0, m.dtype))[0]
+    kv = B * (kv_len + 1) * HK * D * 2 * 2
+    layer = attn + int(round(experts_per_layer * per_expert)) + m.E * m.d * 4 + kv
+    head = q8(spec.vocab * d) if not spec.tied else 0
+    return spec.n_layer * layer + head + B * q8(d)
+
+
+def decoder_records(args, dev, stream, pk) -> dict:
+    """Config 4: the 48-layer decoder (GQA 32/4 x 128, RoPE 1e6, the Q4_K 128-expert
+    MoE in every layer, vocab 151936 Q8_0), decode steps at batch 1 and 16 over a
+    4096-position f16 cache per sequence (filled with N(0, 1) values: a synthetic
+    stand-in for a prefilled cache, the step's cost does not depend on them), random
+    token ids. One step = one token per sequence through the whole model and the head;
+    timed by CUDA events on the decoder's stream over `args.steps` steps."""
+    import torch
+    from aero_b200 import synth
+    from aero_b200.decoder import CudaDecoder
+
+    spec = synth.DECODER_C4
+    n_kv = 4096
+    n_ctx = n_kv + 2 * (args.warmup + args.steps) + 2
+    t0 = time.time()
+    dec_s = synth.make_decoder(spec, 0, device_gen=True)
+    D = CudaDecoder.from_synth(dec_s, n_seq=16, n_ctx=n_ctx, device=dev)
+    del dec_s
+    build_s = time.time() - t0
+
+    class _Cai:
+        def __init__(self, ptr, shape):
+            self.__cuda_array_interface__ = {"data": (ptr, False), "shape": shape, "typestr": "<f2", "version": 3}
+
+    g = torch.Generator(device=f"cuda:{dev}")
+    g.manual_seed(4)
+    shape = (16, spec.n_kv, n_ctx, spec.head_dim)
+    for li in range(spec.n_layer):
+        for ptr in D.kv(li):
+            t = torch.as_tensor(_Cai(ptr, shape), device=f"cuda:{dev}")
+            t[:, :, :n_kv].normal_(generator=g)
+    torch.cuda.synchronize(dev)
+    D.set_stream(stream)
+    rng = np.random.default_rng(3)
+    out = {"config": "c4_decoder_48l_gqa32x4_q4k128e_top8_vocab151936", "kv_positions": n_kv,
+           "build_s": round(build_s, 1), "data": "synthetic weights and cache, random token ids"}
+    try:
+        for B in (1, 16):
+            pos = n_kv  # every batch size decodes after the same 4096 cached positions
+            logits = torch.empty((B, spec.vocab), device=f"cuda:{dev}")
+            seqs = np.arange(B)
+
+            def step(p):
+                D.step(rng.integers(0, spec.vocab, B), seqs, np.full(B, p), logits=logits)
+
+            # distinct experts per layer: read once from the MoE layers' profiled call
+            for m in D._keep:
+                m.set_profiling(True)
+            step(pos)
+            pos += 1
+            stream.synchronize()
+            active = [m.stats()["last_active"] for m in D._keep]
+            for m in D._keep:
+                m.set_profiling(False)
+            for _ in range(args.warmup):
+                step(pos)
+                pos += 1
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            p0 = pos
+            e0.record(stream)
+            for _ in range(args.steps):
+                step(pos)
+                pos += 1
+            e1.record(stream)
+            e1.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            D.profile(True)
+            step(pos)
+            pos += 1
+            stream.synchronize()
+            phases = D.profile(False)
+            ex = float(np.mean(active))
+            nbytes = decoder_step_bytes(spec, B, (p0 + pos) // 2, ex)
+            gbs = nbytes / (ms / 1000.0) / 1e9
+            out[f"batch{B}"] = {"ms_per_step": round(ms, 4), "tokens_per_s": round(B / (ms / 1000.0), 1),
+                                "hbm_bytes_per_step": nbytes, "achieved_gbs": round(gbs, 1),
+                                "frac_of_hbm": round(gbs / pk["hbm_gbs"], 4), "experts_per_layer": round(ex, 2),
+                                "phases_ms": {k: round(v, 4) for k, v in phases.items()}}
+            del logits
+    finally:
+        D.close()
     return out
 
 

@@ -79,6 +79,10 @@ int aero_cuda_decoder_forward(void* dec, const int32_t* tokens, int n_tokens, co
 int aero_cuda_decoder_step(void* dec, const int32_t* tokens, const int32_t* seqs, const int64_t* positions, int T,
                            float* logits);
 
+/* Run on a cudaStream_t (the layers' MoE handles follow); NULL restores the
+ * decoder's own. Calls with host logits synchronise it; others only enqueue. 0 / -1. */
+int aero_cuda_decoder_set_stream(void* dec, void* stream);
+
 /* Device pointers of layer's caches: (n_seq, n_head_kv, n_ctx, head_dim) f16 each. 0 / -1. */
 int aero_cuda_decoder_kv(void* dec, int layer, void** k, void** v);
 
