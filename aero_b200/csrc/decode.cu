@@ -72,14 +72,13 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
     return v;
 }
 
-// Grid barrier b of this launch: every CTA adds one to the counter, which only
-// grows (barrier b completes when it reaches bar_base + (b + 1) * gridDim.x,
-// modulo 2^32; bar_base counts the arrivals of the earlier launches). False when
-// the wait ran out (the error is recorded).
+// Grid barrier b of this launch: every CTA adds one to the counter, which
+// starts the launch at zero (barrier b completes when it reaches
+// (b + 1) * gridDim.x). False when the wait ran out (the error is recorded).
 __device__ bool grid_barrier(const DecodeArgs& a, int b, volatile int* abort_s) {
     __syncthreads();
     if (threadIdx.x == 0) {
-        const uint32_t target = a.bar_base + ((uint32_t)b + 1u) * gridDim.x;
+        const uint32_t target = ((uint32_t)b + 1u) * gridDim.x;
         __threadfence();
         atomicAdd(a.bar, 1u);
         const uint64_t t0 = dec_gtimer();
@@ -812,6 +811,16 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
     }
     if (!barrier()) return;
     stamp(4);
+    // Every CTA has passed the last barrier and no longer reads the counter: the
+    // last one here zeroes it (and the exit count), so the next launch, or a
+    // replay of this one, starts from zero.
+    if (threadIdx.x == 0) {
+        __threadfence();
+        if (atomicAdd(a.bar + 2, 1u) == gridDim.x - 1) {
+            atomicExch(a.bar, 0u);
+            atomicExch(a.bar + 2, 0u);
+        }
+    }
 
     // ---------------------------------------------------------------- phase E
     // out[t][n] = sum_s w[t][s] * y[inv(t, s)][n] (slot order) + sgate[t] * y[P + t][n]

@@ -32,7 +32,10 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
+#include <map>
 #include <set>
+#include <tuple>
 #include <string>
 #include <utility>
 #include <vector>
@@ -457,6 +460,20 @@ struct Decoder {
     int64_t* pos = nullptr;
     QInput hq{}, aq{};
     std::string err;
+    // CUDA graphs of decode steps (T <= kDecodeMaxTokens): keyed by (T, first head
+    // row, head rows, logits pointer); a key runs eagerly once (sizing every
+    // scratch and setting kernel attributes), is captured on its second call and
+    // replayed from then on. Dropped when the decoder's scratch is reallocated or a
+    // step larger than any before runs (the MoE layers may then reallocate theirs).
+    bool use_graphs = true;
+    int max_T = 0;
+    std::set<std::tuple<int, int, int, uintptr_t>> seen;
+    std::map<std::tuple<int, int, int, uintptr_t>, cudaGraphExec_t> graphs;
+    void drop_graphs() {
+        for (auto& kv : graphs) cudaGraphExecDestroy(kv.second);
+        graphs.clear();
+        seen.clear();
+    }
     // profiling
     bool prof = false;
     double ms[5] = {};
@@ -514,6 +531,7 @@ struct Decoder {
     }
     ~Decoder() {
         if (stream) cudaStreamSynchronize(stream);
+        drop_graphs();
         // borrowed MoE handles go back to their own streams
         for (auto& l : L)
             if (!l.own_moe && l.moe) aero_cuda_moe_set_stream(l.moe, nullptr);
@@ -626,6 +644,7 @@ bool ensure_step_scratch(Decoder& g, int T) {
         cudaStreamSynchronize(g.stream);
         guarded_free(g.sbase, g.sbytes, kScratch);
     }
+    g.drop_graphs();
     g.sbase = p;
     g.sbytes = off;
     g.cap = cap;
@@ -696,6 +715,37 @@ bool run_step(Decoder& g, int T, int r0, int nh, float* lg) {
     return true;
 }
 
+// run_step through a CUDA graph where one applies (see Decoder::graphs). A
+// capture that fails (an error in the step, or a call the capture refuses)
+// switches graphs off for this decoder and runs the step eagerly.
+bool run_graphed(Decoder& g, int T, int r0, int nh, float* lg) {
+    if (!g.use_graphs || g.prof || T > kDecodeMaxTokens) return run_step(g, T, r0, nh, lg);
+    const auto key = std::make_tuple(T, r0, nh, (uintptr_t)lg);
+    auto it = g.graphs.find(key);
+    if (it != g.graphs.end()) return g.ok(cudaGraphLaunch(it->second, g.stream), "step graph");
+    if (g.seen.insert(key).second) return run_step(g, T, r0, nh, lg);
+    if (cudaStreamBeginCapture(g.stream, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+        cudaGetLastError();
+        g.use_graphs = false;
+        return run_step(g, T, r0, nh, lg);
+    }
+    const bool ran = run_step(g, T, r0, nh, lg);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(g.stream, &graph);
+    cudaGraphExec_t exec = nullptr;
+    const bool captured = ran && e == cudaSuccess && graph &&
+                          cudaGraphInstantiate(&exec, graph, 0) == cudaSuccess;
+    if (graph) cudaGraphDestroy(graph);
+    if (!captured) {
+        cudaGetLastError();
+        g.use_graphs = false;
+        g.err.clear();
+        return run_step(g, T, r0, nh, lg);
+    }
+    g.graphs[key] = exec;
+    return g.ok(cudaGraphLaunch(exec, g.stream), "step graph");
+}
+
 bool step_entry(Decoder& g, const int32_t* tokens, const int32_t* seqs, const int64_t* positions, int T, float* logits,
                 bool last_only) {
     if (T <= 0) return g.fail("T=%d", T);
@@ -724,7 +774,11 @@ bool step_entry(Decoder& g, const int32_t* tokens, const int32_t* seqs, const in
     const int r0 = last_only ? T - 1 : 0, nh = logits ? (last_only ? 1 : T) : 0;
     const bool dev_out = logits && is_device_ptr(logits);
     float* lg = dev_out ? logits : g.logits;
-    if (!run_step(g, T, r0, nh, lg)) return false;
+    if (T > g.max_T) {
+        g.drop_graphs();
+        g.max_T = T;
+    }
+    if (!run_graphed(g, T, r0, nh, lg)) return false;
     if (logits && !dev_out) {
         if (!g.ok(cudaMemcpyAsync(logits, g.logits, (size_t)nh * g.vocab * 4, cudaMemcpyDeviceToHost, g.stream), "logits"))
             return false;
@@ -784,6 +838,7 @@ Decoder* open_decoder(const aero_cuda_decoder_desc* d, std::string* why, bool ow
     if (cudaStreamCreateWithFlags(&g->own_stream, cudaStreamNonBlocking) != cudaSuccess) return bad("stream creation failed");
     g->stream = g->own_stream;
     g->n_chunk = (g->n_ctx + kAttnChunk - 1) / kAttnChunk;
+    if (const char* v = std::getenv("AERO_DECODER_GRAPHS")) g->use_graphs = std::atoi(v) != 0;
     const int HD = g->H * g->D, KD = g->HK * g->D;
     // weights
     if (d->token_embd.dtype != AERO_DT_Q8_0) return bad("token_embd must be Q8_0");

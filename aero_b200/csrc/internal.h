@@ -131,8 +131,8 @@ struct DecodeArgs {
     int32_t* p_real_out;      // T * k
     float* y;                 // (T * k + T, dp) f32: each pair's expert output (shared expert: rows T * k + t)
     float* out;               // (T, dp) f32
-    uint32_t* bar;            // grid-barrier counter (only grows; zero when the handle's scratch is made)
-    uint32_t bar_base;        // arrivals on it from the earlier launches
+    uint32_t* bar;            // [0] grid-barrier counter, [2] exit counter: both zero at every launch's
+                              // start (the kernel's last CTA resets them; the host after an abort)
     int32_t* err;
     int32_t* err_host;
     uint64_t wait_ns;

@@ -133,7 +133,6 @@ struct Handle {
     int32_t* err_host = nullptr;
     uint64_t peer_wait_ns = 5000000000ull;  // AERO_CUDA_OPT_PEER_WAIT_MS
     bool decode_enabled = true;             // AERO_CUDA_OPT_DECODE_FUSED
-    uint32_t dec_bar = 0;                   // arrivals on the fused decode kernel's barrier counter so far
     // prefill (tcgen05 grouped GEMM) path
     bool gemm_ok = false;     // layer shape/type supports it
     int gemm_min_tokens = 64; // calls with at least this many tokens use it
@@ -323,7 +322,7 @@ bool ensure_scratch(Handle& h, int T) {
     const size_t o_dxq = take(dec ? (size_t)dT * decode_qx_row_bytes(h.dp) : 0);
     const size_t o_dact = take(dec ? (size_t)(dT * h.k + dT) * h.act_ld * 4 : 0);
     const size_t o_dy = take(dec ? (size_t)(dT * h.k + dT) * h.dp * 4 : 0);
-    const size_t o_dbar = take(8);
+    const size_t o_dbar = take(16);  // decode barrier counter, error word, exit counter
     const size_t o_dst = take(6 * 8);
     // split-K partial logits of the tensor-core router (small batches)
     const int part_rows = h.rtc_ok ? (int)std::min<int64_t>(kRouterPartRows, (int64_t)8 * cap) : 0;
@@ -369,7 +368,6 @@ bool ensure_scratch(Handle& h, int T) {
     s.dbar = (uint32_t*)(b + o_dbar);
     s.derr = (int32_t*)(b + o_dbar + 4);
     s.dstamps = (uint64_t*)(b + o_dst);
-    h.dec_bar = 0;  // the new scratch is cleared below: the barrier counter starts at zero
     s.lg_part = part_rows ? (float*)(b + o_lgp) : nullptr;
     s.lg_part_rows = part_rows;
     s.dwork = b + o_dw;
@@ -635,7 +633,6 @@ bool decode_call(Handle& h, const float* x, int T, const float* logits_in, float
     a.y = s.dy;
     a.out = out;
     a.bar = s.dbar;
-    a.bar_base = h.dec_bar;
     a.err = s.derr;
     a.err_host = h.err_host;
     a.wait_ns = 1000000000ull;  // a grid barrier normally completes in microseconds
@@ -644,7 +641,6 @@ bool decode_call(Handle& h, const float* x, int T, const float* logits_in, float
     int grid = 0;
     if (!h.cuda_ok(launch_decode(a, h.n_sm, h.stream, &grid), "decode layer")) return false;
     h.last_decode = true;
-    h.dec_bar += (uint32_t)grid * (uint32_t)decode_barriers(T);
     h.launches += 1;
     h.last_gemm = false;
     h.last_shared_rows = h.has_shared ? T : 0;
@@ -680,8 +676,7 @@ bool check_pipeline(Handle& h) {
         if (cudaMemcpy(&code, h.sc.derr, 4, cudaMemcpyDeviceToHost) != cudaSuccess)
             return h.cuda_ok(cudaGetLastError(), "error flag");
         if (code != 0) {
-            cudaMemset(h.sc.dbar, 0, 8);
-            h.dec_bar = 0;
+            cudaMemset(h.sc.dbar, 0, 12);
             if (code == kErrNotResident)
                 return h.fail("the routing selected an expert this resident-subset layer does not hold (code %d); "
                               "the call's output is invalid",
@@ -717,8 +712,7 @@ bool take_async_error(Handle& h) {
     if (h.peer.open && (code == kEpErrRowsWait || code == kEpErrBackWait) && !h.peer.failed) h.peer.failed = code;
     if (h.sc.base) {
         cudaMemsetAsync(h.sc.tc_err, 0, 4, h.stream);
-        cudaMemsetAsync(h.sc.dbar, 0, 8, h.stream);  // barrier counter and decode error word
-        h.dec_bar = 0;
+        cudaMemsetAsync(h.sc.dbar, 0, 12, h.stream);  // barrier counter, decode error word, exit counter
     }
     if (h.gb_ready) cudaMemsetAsync(h.gb.err, 0, 4, h.stream);
     if (code == kErrNotResident)
@@ -1308,8 +1302,7 @@ int aero_cuda_moe_status(void* handle) {
     if (h->sc.base && h->rtc_ok) cudaMemset(h->sc.tc_err, 0, 4);
     if (h->gb_ready) cudaMemset(h->gb.err, 0, 4);
     if (dev[3] != 0) {
-        cudaMemset(h->sc.dbar, 0, 8);
-        h->dec_bar = 0;
+        cudaMemset(h->sc.dbar, 0, 12);
     }
     if (!h->cuda_ok(cudaGetLastError(), "status")) return -1;
     return code;

@@ -116,3 +116,34 @@ def test_decoder_refusals(golden, tmp_path):
         dec.close()
     with pytest.raises(RuntimeError):
         CudaDecoder.from_gguf(str(tmp_path / "missing.gguf"))
+
+
+def test_decoder_graph_replay_equals_eager(golden, tmp_path, monkeypatch):
+    """Decode steps replayed from the captured CUDA graph (from a key's third call on)
+    give the same logits as eager steps, batched and single, with host and device logits."""
+    torch = pytest.importorskip("torch")
+    spec, path = decoder_fixture(golden, "dec_q8", tmp_path)
+    monkeypatch.setenv("AERO_DECODER_GRAPHS", "0")
+    E = CudaDecoder.from_gguf(path, n_seq=3, n_ctx=64)
+    monkeypatch.setenv("AERO_DECODER_GRAPHS", "1")
+    G = CudaDecoder.from_gguf(path, n_seq=3, n_ctx=64)
+    try:
+        rng = np.random.default_rng(8)
+        prompt = rng.integers(0, spec.vocab, 12)
+        seqs = np.repeat(np.arange(3), 4)
+        pos = np.tile(np.arange(4), 3)
+        assert np.array_equal(E.step(prompt, seqs, pos), G.step(prompt, seqs, pos))
+        dev_e = torch.empty((3, spec.vocab), device="cuda")
+        dev_g = torch.empty((3, spec.vocab), device="cuda")
+        for i in range(6):
+            tok = rng.integers(0, spec.vocab, 3)
+            p = np.full(3, 4 + i)
+            a, b = E.step(tok, [0, 1, 2], p), G.step(tok, [0, 1, 2], p)
+            assert np.array_equal(a, b), i
+            E.step(tok[:1], [0], [20 + i], logits=dev_e[:1])
+            G.step(tok[:1], [0], [20 + i], logits=dev_g[:1])
+            torch.cuda.synchronize()
+            assert torch.equal(dev_e[:1], dev_g[:1]), i
+    finally:
+        E.close()
+        G.close()
