@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(128) qk_rope_kv_kernel(float* __restrict__ qkv
 // 16-byte units: conflict-free 16-byte reads of different rows), scores of the
 // group's R query heads for positions <= pos[t] (masked to -inf otherwise,
 // scaled by 1/sqrt(D)), the chunk's max m and sum l of exp(s - m), and P V.
-// part[t][h][c] = (m, l, acc[D]).
+// part[t][h][c] = (m, l, -, -, acc[D]) (acc 16-byte aligned).
 template <int NV>
 __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restrict__ qkv, int ld, int H, int HK,
                                                            const __half* __restrict__ kc,
@@ -329,7 +329,7 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
         }
     }
     __syncthreads();
-    float* outp = part + (((int64_t)t * H + (int64_t)hk * R) * n_chunk + c) * (D + 2);
+    float* outp = part + (((int64_t)t * H + (int64_t)hk * R) * n_chunk + c) * (D + 4);
     for (int i = threadIdx.x; i < R * (D / 2); i += blockDim.x) {
         const int r = i / (D / 2), dp = i % (D / 2);
         const float* P = S + r * C;
@@ -340,9 +340,9 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
             ax = fmaf(pj, vv.x, ax);
             ay = fmaf(pj, vv.y, ay);
         }
-        float* op = outp + (int64_t)r * n_chunk * (D + 2);
-        op[2 + 2 * dp] = ax;
-        op[3 + 2 * dp] = ay;
+        float* op = outp + (int64_t)r * n_chunk * (D + 4);
+        op[4 + 2 * dp] = ax;
+        op[5 + 2 * dp] = ay;
         if (dp == 0) {
             op[0] = ml[2 * r];
             op[1] = ml[2 * r + 1];
@@ -350,22 +350,61 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
     }
 }
 
-// CTA = (token, head), D threads: out = sum_c e^(m_c - M) acc_c / sum_c e^(m_c - M) l_c.
-__global__ void attn_combine_kernel(const float* __restrict__ part, int H, int D, int n_chunk,
-                                    const int64_t* __restrict__ pos, float* __restrict__ att) {
+// CTA = (token, head), 128 threads: out = sum_c e^(m_c - M) acc_c / sum_c e^(m_c - M) l_c.
+// The chunks' (m, l) are read in parallel (one chunk per thread, block max and
+// sum); then warp w adds the acc rows of chunks w, w + 4, ... (float4 per lane)
+// and the four warps' sums meet in shared memory.
+__global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restrict__ part, int H, int D, int n_chunk,
+                                                           const int64_t* __restrict__ pos, float* __restrict__ att) {
+    __shared__ float ew[1024];  // e^(m_c - M), chunk c (n_chunk <= 1024)
+    __shared__ float red[4];
+    __shared__ float4 accs[4][64];
     const int t = (int)blockIdx.x / H, h = (int)blockIdx.x % H;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nc = (int)(pos[t] / kAttnChunk) + 1;
-    const float* pb = part + ((int64_t)t * H + h) * n_chunk * (D + 2);
-    float M = -INFINITY;
-    for (int c = 0; c < nc; ++c) M = fmaxf(M, pb[(int64_t)c * (D + 2)]);
-    float L = 0.f, acc = 0.f;
-    for (int c = 0; c < nc; ++c) {
-        const float* q = pb + (int64_t)c * (D + 2);
-        const float e = expf(q[0] - M);
-        L = fmaf(e, q[1], L);
-        acc = fmaf(e, q[2 + threadIdx.x], acc);
+    const float* pb = part + ((int64_t)t * H + h) * n_chunk * (D + 4);
+    float m = -INFINITY;
+    for (int c = threadIdx.x; c < nc; c += 128) m = fmaxf(m, pb[(int64_t)c * (D + 4)]);
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();
+    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    __syncthreads();
+    float L = 0.f;
+    for (int c = threadIdx.x; c < nc; c += 128) {
+        const float e = expf(pb[(int64_t)c * (D + 4)] - M);
+        ew[c] = e;
+        L = fmaf(e, pb[(int64_t)c * (D + 4) + 1], L);
     }
-    att[((int64_t)t * H + h) * D + threadIdx.x] = acc / fmaxf(L, 1e-30f);
+    L = warp_sum(L);
+    if (lane == 0) red[warp] = L;
+    __syncthreads();
+    const float Ls = red[0] + red[1] + red[2] + red[3];
+    const int nq = D / 4;  // float4 per acc row (<= 64)
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int q = lane; q < nq; q += 32) {
+        a = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int c = warp; c < nc; c += 4) {
+            const float e = ew[c];
+            const float4 v = *reinterpret_cast<const float4*>(pb + (int64_t)c * (D + 4) + 4 + 4 * q);
+            a.x = fmaf(e, v.x, a.x);
+            a.y = fmaf(e, v.y, a.y);
+            a.z = fmaf(e, v.z, a.z);
+            a.w = fmaf(e, v.w, a.w);
+        }
+        accs[warp][q] = a;
+    }
+    __syncthreads();
+    const float inv = 1.0f / fmaxf(Ls, 1e-30f);
+    for (int q = threadIdx.x; q < nq; q += 128) {
+        const float4 a0 = accs[0][q], a1 = accs[1][q], a2 = accs[2][q], a3 = accs[3][q];
+        float4 o;
+        o.x = (a0.x + a1.x + a2.x + a3.x) * inv;
+        o.y = (a0.y + a1.y + a2.y + a3.y) * inv;
+        o.z = (a0.z + a1.z + a2.z + a3.z) * inv;
+        o.w = (a0.w + a1.w + a2.w + a3.w) * inv;
+        *reinterpret_cast<float4*>(att + ((int64_t)t * H + h) * D + 4 * q) = o;
+    }
 }
 
 // ------------------------------------------------------------------ launchers
@@ -411,7 +450,7 @@ cudaError_t attention_nv(float* qkv, int ld, int T, int H, int HK, const float* 
     const float scale = 1.0f / std::sqrt((float)(NV * 32));
     attn_partial_kernel<NV><<<dim3((unsigned)n_chunk, (unsigned)(T * HK)), 256, smem, s>>>(
         qkv, ld, H, HK, kc, vc, n_ctx, pos, seq, scale, part, n_chunk);
-    attn_combine_kernel<<<(unsigned)(T * H), NV * 32, 0, s>>>(part, H, NV * 32, n_chunk, pos, att);
+    attn_combine_kernel<<<(unsigned)(T * H), 128, 0, s>>>(part, H, NV * 32, n_chunk, pos, att);
     return cudaGetLastError();
 }
 
@@ -631,7 +670,7 @@ bool ensure_step_scratch(Decoder& g, int T) {
     const size_t o_x = take((size_t)cap * g.d * 4), o_h = take((size_t)cap * g.d * 4);
     const size_t o_qkv = take((size_t)cap * qkv_ld * 4), o_att = take((size_t)cap * HD * 4);
     const size_t o_o = take((size_t)cap * g.d * 4), o_dm = take((size_t)cap * g.d * 4);
-    const size_t o_part = take((size_t)cap * g.H * g.n_chunk * (g.D + 2) * 4);
+    const size_t o_part = take((size_t)cap * g.H * g.n_chunk * (g.D + 4) * 4);
     const size_t o_hq = take(qinput_bytes(cap, g.d)), o_aq = take(qinput_bytes(cap, HD));
     const size_t o_tok = take((size_t)cap * 4), o_seq = take((size_t)cap * 4), o_pos = take((size_t)cap * 8);
     const size_t o_lg = take((size_t)cap * g.vocab * 4);
@@ -822,6 +861,7 @@ Decoder* open_decoder(const aero_cuda_decoder_desc* d, std::string* why, bool ow
     g->rope_base = d->rope_base;
     if (g->n_layer <= 0 || g->n_layer > 4096 || g->d <= 0 || g->d % 32 || g->vocab <= 0 || g->n_seq <= 0 || g->n_ctx <= 0)
         return bad("n_layer, vocab, n_seq, n_ctx must be positive and n_embd a multiple of 32");
+    if (g->n_ctx > 1024 * kAttnChunk) return bad("n_ctx above 65536 positions per sequence");
     if (g->H <= 0 || g->HK <= 0 || g->H % g->HK || g->H / g->HK > kMaxGroup)
         return bad("n_head must be a multiple of n_head_kv with at most 16 query heads per kv head");
     if (g->D != 64 && g->D != 128 && g->D != 192 && g->D != 256) return bad("head_dim must be 64, 128, 192 or 256");

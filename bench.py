@@ -259,12 +259,17 @@ def main():
     ap.add_argument("--tokens", type=int, default=0, help="--profile: tokens per call (default: the workload's)")
     ap.add_argument("--calls", type=int, default=3, help="--profile: layer calls")
     ap.add_argument("--gemm-min", type=int, default=0, help="--profile: GEMM path threshold (0: library default)")
+    ap.add_argument("--decoder-layers", type=int, default=0,
+                    help="--profile --workload decoder: layers of the config-4 decoder (0: all 48)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
     ws, rank, local = dist_env()
     from aero_b200 import synth
 
+    if args.profile and args.workload == "decoder":
+        run_profile_decoder(args)
+        return
     wl = synth.CONFIGS[args.workload]
     if args.impl == "reference":
         if rank == 0:
@@ -359,6 +364,48 @@ def run_profile(args, wl):
     L.close()
     print(json.dumps({"workload": wl.name, "tokens": T, "stages_ms": {k: v[0] / max(v[1], 1) for k, v in st.items()},
                       "checksum": float(np.abs(out.cpu().numpy()).sum())}))
+
+
+def run_profile_decoder(args):
+    """The config-4 decoder (--decoder-layers of its 48 layers) with a 4096-position
+    cache: --calls eager decode steps of --tokens sequences (default 1), then the
+    phase times of one more (the command the decoder profile captures run)."""
+    import dataclasses
+
+    import torch
+    from aero_b200 import synth
+    from aero_b200.decoder import CudaDecoder
+
+    os.environ["AERO_DECODER_GRAPHS"] = "0"  # every kernel its own launch in the capture
+    spec = synth.DECODER_C4
+    if args.decoder_layers:
+        spec = dataclasses.replace(spec, n_layer=args.decoder_layers)
+    B = args.tokens or 1
+    n_kv = 4096
+    D = CudaDecoder.from_synth(synth.make_decoder(spec, 0, device_gen=True), n_seq=B, n_ctx=n_kv + args.calls + 2)
+    shape = (B, spec.n_kv, D.n_ctx, spec.head_dim)
+    for li in range(spec.n_layer):
+        for ptr in D.kv(li):
+            t = torch.as_tensor(_CudaArray(ptr, shape, "<f2"), device="cuda")
+            t[:, :, :n_kv].normal_()
+    logits = torch.empty((B, spec.vocab), device="cuda")
+    rng = np.random.default_rng(3)
+    for i in range(args.calls):
+        D.step(rng.integers(0, spec.vocab, B), np.arange(B), np.full(B, n_kv + i), logits=logits)
+    D.profile(True)
+    D.step(rng.integers(0, spec.vocab, B), np.arange(B), np.full(B, n_kv + args.calls), logits=logits)
+    torch.cuda.synchronize()
+    ph = D.profile(False)
+    D.close()
+    print(json.dumps({"workload": f"decoder_{spec.n_layer}l", "batch": B, "phases_ms": ph,
+                      "checksum": float(logits.abs().sum().item())}))
+
+
+class _CudaArray:
+    """A device buffer (address, shape, numpy type string) for torch.as_tensor."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape), "typestr": typestr, "version": 3}
 
 
 def run_ours(args, ws, rank, dev, cuda, wl, spec, T, seed, clk):
@@ -655,16 +702,12 @@ def decoder_records(args, dev, stream, pk) -> dict:
     del dec_s
     build_s = time.time() - t0
 
-    class _Cai:
-        def __init__(self, ptr, shape):
-            self.__cuda_array_interface__ = {"data": (ptr, False), "shape": shape, "typestr": "<f2", "version": 3}
-
     g = torch.Generator(device=f"cuda:{dev}")
     g.manual_seed(4)
     shape = (16, spec.n_kv, n_ctx, spec.head_dim)
     for li in range(spec.n_layer):
         for ptr in D.kv(li):
-            t = torch.as_tensor(_Cai(ptr, shape), device=f"cuda:{dev}")
+            t = torch.as_tensor(_CudaArray(ptr, shape, "<f2"), device=f"cuda:{dev}")
             t[:, :, :n_kv].normal_(generator=g)
     torch.cuda.synchronize(dev)
     D.set_stream(stream)
