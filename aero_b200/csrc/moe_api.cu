@@ -93,6 +93,8 @@ struct PeerCtx {
     long n_prof = 0;
 };
 
+constexpr int kAsyncSlots = 4;
+
 struct Handle {
     int device = 0;
     cudaStream_t stream = nullptr, own_stream = nullptr;
@@ -146,6 +148,17 @@ struct Handle {
     bool last_gemm = false;   // whether it took the GEMM path
     bool last_decode = false; // whether it took the fused decode kernel
     PeerCtx peer;
+    // asynchronous host-buffer calls (aero_cuda_moe_submit / _wait): kAsyncSlots slots,
+    // each with its device input / output rows; copies in and out run on their
+    // own streams so one call's copies overlap another's block
+    struct AsyncSlot {
+        float *x = nullptr, *out = nullptr;  // (cap, dp) each, one allocation
+        size_t bytes = 0;
+        int cap = 0, T = 0;
+        bool pending = false;
+        cudaEvent_t in = nullptr, done = nullptr, copied = nullptr;
+    } aslot[kAsyncSlots];
+    cudaStream_t s_in = nullptr, s_out = nullptr;
 
     void peer_release() {
         for (char* m : peer.mapped)
@@ -166,6 +179,14 @@ struct Handle {
             cudaStreamSynchronize(stream);
             peer_release();
         }
+        for (auto& q : aslot) {
+            if (q.copied) cudaEventSynchronize(q.copied);
+            if (q.x) guarded_free(q.x, q.bytes, kScratch);
+            for (cudaEvent_t e : {q.in, q.done, q.copied})
+                if (e) cudaEventDestroy(e);
+        }
+        if (s_in) cudaStreamDestroy(s_in);
+        if (s_out) cudaStreamDestroy(s_out);
         for (auto& a : allocs) guarded_free(a.p, a.bytes, a.cls);
         if (sc.base) guarded_free(sc.base, sc.bytes, kScratch);
         if (ev0) cudaEventDestroy(ev0);
@@ -990,6 +1011,78 @@ int aero_cuda_moe_forward(void* handle, int layer, const float* h_in, int T, int
         return 0;
     }
     return aero::block_entry(*h, h_in, T, nullptr, out) ? 1 : 0;
+}
+
+int aero_cuda_moe_wait(void* handle, int slot) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (slot < 0 || slot >= aero::kAsyncSlots) return h->fail("slot %d outside [0, %d)", slot, aero::kAsyncSlots), -1;
+    auto& q = h->aslot[slot];
+    if (!q.pending) return 0;
+    q.pending = false;
+    if (!h->cuda_ok(cudaEventSynchronize(q.copied), "asynchronous call")) return -1;
+    if (!aero::take_async_error(*h)) return -1;
+    h->calls++;
+    h->tokens += q.T;
+    return 0;
+}
+
+int aero_cuda_moe_submit(void* handle, int slot, const float* h_in, int T, float* out) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    if (slot < 0 || slot >= aero::kAsyncSlots) return h->fail("slot %d outside [0, %d)", slot, aero::kAsyncSlots), -1;
+    if (h->aslot[slot].pending && aero_cuda_moe_wait(handle, slot) != 0) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (!h->subset && (h->e_begin != 0 || h->e_end != h->E))
+        return h->fail("this handle owns experts [%d, %d) only", h->e_begin, h->e_end), -1;
+    if (T < 0) return h->fail("T=%d", T), -1;
+    if (T == 0) return 0;
+    if (!h_in || !out) return h->fail("null buffer"), -1;
+    if (aero::is_device_ptr(h_in) || aero::is_device_ptr(out))
+        return h->fail("submit takes host buffers (device buffers: aero_cuda_moe_forward enqueues already)"), -1;
+    if (!aero::take_async_error(*h)) return -1;
+    if (cudaSetDevice(h->device) != cudaSuccess) return h->fail("cudaSetDevice(%d) failed", h->device), -1;
+    auto& q = h->aslot[slot];
+    if (!h->s_in && (cudaStreamCreateWithFlags(&h->s_in, cudaStreamNonBlocking) != cudaSuccess ||
+                     cudaStreamCreateWithFlags(&h->s_out, cudaStreamNonBlocking) != cudaSuccess))
+        return h->fail("copy stream creation failed"), -1;
+    if (!q.in && (cudaEventCreateWithFlags(&q.in, cudaEventDisableTiming) != cudaSuccess ||
+                  cudaEventCreateWithFlags(&q.done, cudaEventDisableTiming) != cudaSuccess ||
+                  cudaEventCreateWithFlags(&q.copied, cudaEventDisableTiming) != cudaSuccess))
+        return h->fail("event creation failed"), -1;
+    if (T > q.cap) {
+        const int cap = std::max(T, 2 * q.cap);
+        const size_t rows = (size_t)cap * h->dp * 4;
+        void* p = nullptr;
+        if (aero::guarded_malloc(&p, 2 * rows, aero::kScratch) != cudaSuccess) {
+            cudaGetLastError();
+            return h->fail("device rows for asynchronous calls of %d tokens refused", cap), -1;
+        }
+        if (q.x) aero::guarded_free(q.x, q.bytes, aero::kScratch);  // the slot's earlier call has completed
+        q.x = static_cast<float*>(p);
+        q.out = q.x + (size_t)cap * h->dp;
+        q.bytes = 2 * rows;
+        q.cap = cap;
+        if (h->dp != h->d && !h->cuda_ok(cudaMemsetAsync(q.x, 0, rows, h->s_in), "rows")) return -1;
+    }
+    if (!aero::ensure_scratch(*h, T)) return -1;
+    const size_t rb = (size_t)h->d * 4, pitch = (size_t)h->dp * 4;
+    // in: copy stream; block: the handle's stream after the copy; out: copy stream after the block
+    if (!h->cuda_ok(cudaMemcpy2DAsync(q.x, pitch, h_in, rb, rb, (size_t)T, cudaMemcpyHostToDevice, h->s_in), "input copy") ||
+        !h->cuda_ok(cudaEventRecord(q.in, h->s_in), "event") ||
+        !h->cuda_ok(cudaStreamWaitEvent(h->stream, q.in, 0), "event"))
+        return -1;
+    if (!aero::run_block(*h, q.x, T, nullptr, q.out)) return -1;
+    if (!h->cuda_ok(cudaEventRecord(q.done, h->stream), "event") ||
+        !h->cuda_ok(cudaStreamWaitEvent(h->s_out, q.done, 0), "event") ||
+        !h->cuda_ok(cudaMemcpy2DAsync(out, rb, q.out, pitch, rb, (size_t)T, cudaMemcpyDeviceToHost, h->s_out),
+                    "output copy") ||
+        !h->cuda_ok(cudaEventRecord(q.copied, h->s_out), "event"))
+        return -1;
+    q.T = T;
+    q.pending = true;
+    return 0;
 }
 
 int aero_cuda_moe_ffn_block(void* handle, const float* h_in, const float* router_logits, int T, float* out) {

@@ -98,6 +98,8 @@ SYMBOLS = [
     ("aero_cuda_decoder_last_error", c_char_p, [_P]),
     ("aero_cuda_decoder_close", None, [_P]),
     ("aero_cuda_moe_forward", c_int, [_P, c_int, _P, c_int, c_int, _P]),
+    ("aero_cuda_moe_submit", c_int, [_P, c_int, _P, c_int, _P]),
+    ("aero_cuda_moe_wait", c_int, [_P, c_int]),
     ("aero_cuda_moe_ffn_block", c_int, [_P, _P, _P, c_int, _P]),
     ("aero_cuda_moe_router_logits", c_int, [_P, _P, c_int, _P]),
     ("aero_cuda_moe_route", c_int, [_P, _P, c_int, _P, _P]),

@@ -111,6 +111,19 @@ void aero_cuda_moe_model_close(void* table);
  * per layer). Returns 1 on success, 0 on refusal (src/model.cpp:169). */
 int aero_cuda_moe_forward(void* handle, int layer, const float* h, int T, int n_embd, float* out);
 
+/* Asynchronous calls with host buffers, for a stream of layer calls (serving):
+ * submit enqueues the copy of h (T rows, host memory; pinned memory lets the
+ * copies overlap the GPU's work) into slot `slot` (0 to 3), the block, and the
+ * copy of the result into out, and returns at once; aero_cuda_moe_wait(handle,
+ * slot) returns when that output is in `out` (and reports a bounded device wait
+ * that gave up). Copies run on two streams of the handle besides its compute
+ * stream, so later slots' inputs and earlier slots' outputs cross PCIe while
+ * a block computes (three slots in turn keep both directions busy). h and out must stay untouched until the wait; a submit to a
+ * slot still pending waits for it first. No reference counterpart (the
+ * reference's calls are synchronous). 0 / -1. */
+int aero_cuda_moe_submit(void* handle, int slot, const float* h, int T, float* out);
+int aero_cuda_moe_wait(void* handle, int slot);
+
 /* The block with caller-supplied router logits (T, n_expert): the contract of
  * aero_moe_ffn_block (include/aero/moe.hpp:43-52) with the experts already
  * resident. Returns 0 on success, -1 on refusal. */

@@ -432,3 +432,34 @@ def test_guard_injected_allocation_failure_leaks_nothing():
     assert g.committed() > base
     L.close()
     assert g.committed() == base
+
+
+def test_asynchronous_submit_wait_equals_forward():
+    """aero_cuda_moe_submit / _wait over slots 0 and 1 give the synchronous call's outputs,
+    for a decode-size and a prefill-size call (GEMM path) interleaved, pinned and pageable
+    host buffers; device buffers are refused."""
+    torch = pytest.importorskip("torch")
+    spec = synth.LayerSpec(512, 16, 4, 256, 256, Q.DTYPE_Q4_K)
+    layer = synth.make_layer(spec, 61)
+    L = synth.open_layer(layer)
+    lib = nc.lib()
+    try:
+        xs = [synth.make_x(T, spec.d, 61 + T) for T in (3, 200, 1, 96)]
+        want = [L.forward(x) for x in xs]
+        ins = [torch.from_numpy(x).pin_memory() if i % 2 else torch.from_numpy(x.copy()) for i, x in enumerate(xs)]
+        outs = [torch.empty_like(t).pin_memory() if i % 2 else torch.empty_like(t) for i, t in enumerate(ins)]
+        for rnd in range(2):
+            for i, (xi, oi) in enumerate(zip(ins, outs)):
+                assert lib.aero_cuda_moe_submit(L.handle, i % 2, xi.data_ptr(), xi.shape[0], oi.data_ptr()) == 0, \
+                    nc.last_error(L.handle)
+            for slot in (0, 1):
+                assert lib.aero_cuda_moe_wait(L.handle, slot) == 0
+            # the first two calls were waited for by the later submits to their slots
+            for i in range(4):
+                assert np.array_equal(outs[i].numpy(), want[i]), (rnd, i)
+        xd = torch.from_numpy(xs[0]).cuda()
+        assert lib.aero_cuda_moe_submit(L.handle, 0, xd.data_ptr(), 3, outs[0].data_ptr()) == -1
+        assert "host buffers" in nc.last_error(L.handle)
+        assert lib.aero_cuda_moe_submit(L.handle, 4, ins[0].data_ptr(), 3, outs[0].data_ptr()) == -1
+    finally:
+        L.close()
