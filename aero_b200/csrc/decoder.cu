@@ -20,7 +20,8 @@
 //                        (max, sum) and P V
 //   attn_combine_kernel  merges the chunks of each (token, head)
 //                        (src/transformer.cpp:120-205 computes the same online
-//                        softmax in 1024-position blocks)
+//                        softmax in 1024-position blocks) and codes the head's
+//                        values as the output projection's input
 //   the MoE layer        aero_cuda_moe_forward on the layer's handle, device
 //                        pointers, same stream
 // and per step the embedding row gather (Q8_0, the reference's dequantised row,
@@ -51,9 +52,15 @@ namespace {
 constexpr int kTokGroup = 16;   // tokens per dense GEMV CTA: a weight row is read once for all of them
 // 16-byte chunks per lane per pass over a row (Q4_K chunks carry two runs of input codes)
 template <int DT>
-constexpr int gemv_cpl() { return DT == AERO_DT_Q4_K ? 2 : 4; }
+__host__ __device__ constexpr int gemv_cpl() { return DT == AERO_DT_Q4_K ? 2 : 4; }
 constexpr int kAttnChunk = 64;  // cache positions per attention CTA
 constexpr int kMaxGroup = 16;   // query heads per kv head
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
@@ -160,29 +167,24 @@ __global__ void __launch_bounds__(256, 2) dense_gemv_kernel(QMat W, QInput in, i
         }
         return;
     }
+    // several tokens: one copy of the dot in the code (a loop over the tokens, not
+    // unrolled: the kernel body stays small), each token's sum reduced across the
+    // warp at once and kept by lane 0 in shared memory across the row's passes
+    __shared__ float acc_s[8][kTokGroup];
     for (; r < W.rows; r += stride) {
-        float acc[kTokGroup];
-#pragma unroll
-        for (int j = 0; j < kTokGroup; ++j) acc[j] = 0.f;
         for (int base = 0; base < nch; base += LPR * CPL) {
             RowRaw<DT, CPL> w;
             row_load<DT, LPR, CPL>(W, 0, r, lane, nch, w, base);
-#pragma unroll
-            for (int j = 0; j < kTokGroup; ++j) {
-                if (j < nt) {
-                    LaneInput<DT, CPL> xin;
-                    input_load<DT, LPR, CPL>(nullptr, in, t0 + j, lane, nch, xin, base);
-                    acc[j] += row_dot<DT, LPR, CPL>(w, xin, lane, nch, base);
-                }
+#pragma unroll 1
+            for (int j = 0; j < nt; ++j) {
+                LaneInput<DT, CPL> xin;
+                input_load<DT, LPR, CPL>(nullptr, in, t0 + j, lane, nch, xin, base);
+                const float v = warp_sum(row_dot<DT, LPR, CPL>(w, xin, lane, nch, base));
+                if (lane == 0) acc_s[warp][j] = base == 0 ? v : acc_s[warp][j] + v;
             }
         }
-#pragma unroll
-        for (int j = 0; j < kTokGroup; ++j) {
-            if (j < nt) {
-                const float v = warp_sum(acc[j]);
-                if (lane == 0) y[(int64_t)(t0 + j) * ldy + r] = v;
-            }
-        }
+        if (lane < nt) y[(int64_t)(t0 + lane) * ldy + r] = acc_s[warp][lane];
+        __syncwarp();
     }
 }
 
@@ -273,16 +275,16 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
     float* S = qs + R * D;
     float* ml = S + R * C;
     const int64_t base = (((int64_t)seq[t] * HK + hk) * n_ctx + start) * D;
+    // the chunk's rows copied asynchronously, all in flight at once, while the queries load
     constexpr int pieces = D / 8;
     for (int i = threadIdx.x; i < nv * pieces; i += blockDim.x) {
         const int row = i / pieces, pc = i % pieces;
-        *reinterpret_cast<uint4*>(ks + row * KS + pc * 16) =
-            __ldg(reinterpret_cast<const uint4*>(kc + base + (int64_t)row * D) + pc);
-        *reinterpret_cast<uint4*>(vs + row * KS + pc * 16) =
-            __ldg(reinterpret_cast<const uint4*>(vc + base + (int64_t)row * D) + pc);
+        cp_async16(ks + row * KS + pc * 16, kc + base + (int64_t)row * D + pc * 8);
+        cp_async16(vs + row * KS + pc * 16, vc + base + (int64_t)row * D + pc * 8);
     }
     for (int i = threadIdx.x; i < R * D; i += blockDim.x)
         qs[i] = qkv[(int64_t)t * ld + (int64_t)(hk * R) * D + i];
+    cp_async_wait_all();
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int pr = warp; pr < R * (C / 32); pr += 8) {
@@ -355,7 +357,8 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
 // sum); then warp w adds the acc rows of chunks w, w + 4, ... (float4 per lane)
 // and the four warps' sums meet in shared memory.
 __global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restrict__ part, int H, int D, int n_chunk,
-                                                           const int64_t* __restrict__ pos, float* __restrict__ att) {
+                                                           const int64_t* __restrict__ pos, float* __restrict__ att,
+                                                           QInput aq) {
     __shared__ float ew[1024];  // e^(m_c - M), chunk c (n_chunk <= 1024)
     __shared__ float red[4];
     __shared__ float4 accs[4][64];
@@ -404,6 +407,15 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restri
         o.z = (a0.z + a1.z + a2.z + a3.z) * inv;
         o.w = (a0.w + a1.w + a2.w + a3.w) * inv;
         *reinterpret_cast<float4*>(att + ((int64_t)t * H + h) * D + 4 * q) = o;
+        accs[0][q] = o;
+    }
+    // the head's D values coded as the output projection's input (row t, columns h * D ...)
+    __syncthreads();
+    if (threadIdx.x < D / 32) {
+        const int b = threadIdx.x, c = h * D + 32 * b;
+        qinput_block(reinterpret_cast<const float*>(&accs[0][0]) + 32 * b, aq.q1 + (int64_t)t * aq.K + c,
+                     aq.q0 + (int64_t)t * aq.K + c, aq.sx + (int64_t)t * (aq.K / 32) + (c >> 5),
+                     aq.s16 + (int64_t)t * (aq.K / 16) + (c >> 4));
     }
 }
 
@@ -434,7 +446,7 @@ size_t attn_smem(int R) {
 template <int NV>
 cudaError_t attention_nv(float* qkv, int ld, int T, int H, int HK, const float* qn, const float* kn, float eps,
                          float base, const int64_t* pos, const int32_t* seq, __half* kc, __half* vc, int n_ctx,
-                         float* part, int n_chunk, float* att, cudaStream_t s) {
+                         float* part, int n_chunk, float* att, QInput aq, cudaStream_t s) {
     const int per = H + 2 * HK;
     qk_rope_kv_kernel<NV><<<(unsigned)((T * per + 3) / 4), 128, 0, s>>>(qkv, T, H, HK, ld, qn, kn, eps, base, pos, seq,
                                                                         kc, vc, n_ctx);
@@ -450,18 +462,18 @@ cudaError_t attention_nv(float* qkv, int ld, int T, int H, int HK, const float* 
     const float scale = 1.0f / std::sqrt((float)(NV * 32));
     attn_partial_kernel<NV><<<dim3((unsigned)n_chunk, (unsigned)(T * HK)), 256, smem, s>>>(
         qkv, ld, H, HK, kc, vc, n_ctx, pos, seq, scale, part, n_chunk);
-    attn_combine_kernel<<<(unsigned)(T * H), 128, 0, s>>>(part, H, NV * 32, n_chunk, pos, att);
+    attn_combine_kernel<<<(unsigned)(T * H), 128, 0, s>>>(part, H, NV * 32, n_chunk, pos, att, aq);
     return cudaGetLastError();
 }
 
 cudaError_t attention(int D, float* qkv, int ld, int T, int H, int HK, const float* qn, const float* kn, float eps,
                       float base, const int64_t* pos, const int32_t* seq, __half* kc, __half* vc, int n_ctx,
-                      float* part, int n_chunk, float* att, cudaStream_t s) {
+                      float* part, int n_chunk, float* att, QInput aq, cudaStream_t s) {
     switch (D) {
-        case 64: return attention_nv<2>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, s);
-        case 128: return attention_nv<4>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, s);
-        case 192: return attention_nv<6>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, s);
-        case 256: return attention_nv<8>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, s);
+        case 64: return attention_nv<2>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, aq, s);
+        case 128: return attention_nv<4>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, aq, s);
+        case 192: return attention_nv<6>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, aq, s);
+        case 256: return attention_nv<8>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, aq, s);
     }
     return cudaErrorInvalidValue;
 }
@@ -723,10 +735,9 @@ bool run_step(Decoder& g, int T, int r0, int nh, float* lg) {
         if (!g.ok(gemv_dense(Ly.qkv, g.hq, T, g.qkv, qkv_ld, g.n_sm, s), "q/k/v projection")) return false;
         g.mark(2);
         if (!g.ok(attention(g.D, g.qkv, qkv_ld, T, g.H, g.HK, Ly.q_norm, Ly.k_norm, g.eps, g.rope_base, g.pos, g.seq,
-                            Ly.kc, Ly.vc, g.n_ctx, g.part, g.n_chunk, g.att, s),
+                            Ly.kc, Ly.vc, g.n_ctx, g.part, g.n_chunk, g.att, g.aq, s),
                   "attention"))
             return false;
-        if (!g.ok(launch_qinput(g.att, T, HD, g.aq, s), "attention rows")) return false;
         g.mark(1);
         if (!g.ok(gemv_dense(Ly.o, g.aq, T, g.o, g.d, g.n_sm, s), "output projection")) return false;
         g.mark(0);
