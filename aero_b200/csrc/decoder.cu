@@ -96,45 +96,105 @@ __global__ void embed_q8_kernel(QMat E, const int32_t* __restrict__ tok, int T, 
 
 // ------------------------------------------------------------------ RMSNorm
 // Row r0 + b of x (b = blockIdx.x): with add non-null, x += add first (the
-// residual, written back); then h = x * inv * w, inv = 1 / sqrt(mean(x^2) + eps).
-// Output row b of h32 (f32) and/or of hq (coded input rows), either may be null.
+// residual, written back); then h = x * inv * w, inv = 1 / sqrt(mean(x^2) + eps)
+// (src/tensor.cpp:128-134). Output row b of h32 (f32) and/or of hq (the coded
+// GEMV input), either may be null. Thread t holds the 8-value groups t, t + 256,
+// ... (all loads issued at once); the four threads of a 32-value block code it
+// together (max and 16-value sums by shuffles within the quad). d <= 8192.
+constexpr int kNormGroups = 4;  // 8-value groups per thread at most: d <= 4 * 256 * 8
+template <int NG>
 __global__ void __launch_bounds__(256) norm_kernel(float* __restrict__ x, int d, const float* __restrict__ add,
                                                    const float* __restrict__ w, float eps, int r0,
                                                    float* __restrict__ h32, QInput hq) {
-    extern __shared__ float sh[];  // d values, then 8 partial sums
+    __shared__ float red[8];
     const int t = r0 + (int)blockIdx.x, o = (int)blockIdx.x;
+    const int ng = d / 8;
     float* xr = x + (int64_t)t * d;
+    float v[NG][8], wv[NG][8];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        float v = xr[i];
-        if (add) {
-            v += add[(int64_t)t * d + i];
-            xr[i] = v;
+#pragma unroll
+    for (int k = 0; k < NG; ++k) {
+        const int g = threadIdx.x + 256 * k;
+        if (g < ng) {
+            float4 a0 = *reinterpret_cast<const float4*>(xr + 8 * g), a1 = *reinterpret_cast<const float4*>(xr + 8 * g + 4);
+            const float4 w0 = __ldg(reinterpret_cast<const float4*>(w + 8 * g)),
+                         w1 = __ldg(reinterpret_cast<const float4*>(w + 8 * g + 4));
+            if (add) {
+                const float4 b0 = *reinterpret_cast<const float4*>(add + (int64_t)t * d + 8 * g),
+                             b1 = *reinterpret_cast<const float4*>(add + (int64_t)t * d + 8 * g + 4);
+                a0.x += b0.x, a0.y += b0.y, a0.z += b0.z, a0.w += b0.w;
+                a1.x += b1.x, a1.y += b1.y, a1.z += b1.z, a1.w += b1.w;
+                *reinterpret_cast<float4*>(xr + 8 * g) = a0;
+                *reinterpret_cast<float4*>(xr + 8 * g + 4) = a1;
+            }
+            const float vv[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+            const float ww[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                v[k][i] = vv[i];
+                wv[k][i] = ww[i];
+                ss = fmaf(vv[i], vv[i], ss);
+            }
         }
-        sh[i] = v;
-        ss = fmaf(v, v, ss);
     }
-    float* red = sh + d;
     ss = warp_sum(ss);
     if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
     __syncthreads();
-    if (threadIdx.x < 32) {
-        float v = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-        v = warp_sum(v);
-        if (threadIdx.x == 0) red[0] = v;
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[i];
+    const float inv = 1.0f / sqrtf(tot / (float)d + eps);
+    const int q = threadIdx.x & 3;  // this thread's quarter of its 32-value blocks
+#pragma unroll
+    for (int k = 0; k < NG; ++k) {
+        const int g = threadIdx.x + 256 * k;
+        const bool on = g < ng;
+        float h[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) h[i] = on ? v[k][i] * inv * wv[k][i] : 0.f;
+        if (on && h32) {
+            float* hp = h32 + (int64_t)o * d + 8 * g;
+            *reinterpret_cast<float4*>(hp) = make_float4(h[0], h[1], h[2], h[3]);
+            *reinterpret_cast<float4*>(hp + 4) = make_float4(h[4], h[5], h[6], h[7]);
+        }
+        if (!hq.q1) continue;
+        float mx = 0.f, sum8 = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            mx = fmaxf(mx, fabsf(h[i]));
+            sum8 += h[i];
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float s16 = sum8 + __shfl_xor_sync(0xffffffffu, sum8, 1);
+        if (!on) continue;
+        const float cinv = mx > 0.f ? 16383.0f / mx : 0.f;
+        uint32_t p1[2] = {0u, 0u}, p0[2] = {0u, 0u};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int c = __float2int_rn(h[i] * cinv);  // |c| <= 16383
+            p1[i >> 2] |= (uint32_t)(c >> 7 & 0xFF) << (8 * (i & 3));
+            p0[i >> 2] |= (uint32_t)(c & 127) << (8 * (i & 3));
+        }
+        const int64_t col = 8 * (int64_t)g;
+        *reinterpret_cast<uint2*>(hq.q1 + (int64_t)o * hq.K + col) = make_uint2(p1[0], p1[1]);
+        *reinterpret_cast<uint2*>(hq.q0 + (int64_t)o * hq.K + col) = make_uint2(p0[0], p0[1]);
+        if (q == 0) hq.sx[(int64_t)o * (hq.K / 32) + (col >> 5)] = mx / 16383.0f;
+        if ((q & 1) == 0) hq.s16[(int64_t)o * (hq.K / 16) + (col >> 4)] = s16;
     }
-    __syncthreads();
-    const float inv = 1.0f / sqrtf(red[0] / (float)d + eps);
-    for (int i = threadIdx.x; i < d; i += blockDim.x) {
-        const float h = sh[i] * inv * w[i];
-        sh[i] = h;
-        if (h32) h32[(int64_t)o * d + i] = h;
-    }
-    if (!hq.q1) return;
-    __syncthreads();
-    for (int b = threadIdx.x; b < d / 32; b += blockDim.x)
-        qinput_block(sh + 32 * b, hq.q1 + (int64_t)o * hq.K + 32 * b, hq.q0 + (int64_t)o * hq.K + 32 * b,
-                     hq.sx + (int64_t)o * (hq.K / 32) + b, hq.s16 + (int64_t)o * (hq.K / 16) + 2 * b);
+}
+
+cudaError_t launch_norm(float* x, int T, int d, const float* add, const float* w, float eps, float* h32, QInput hq,
+                        cudaStream_t s) {
+    if (T <= 0) return cudaSuccess;
+    const int ng = (d / 8 + 255) / 256;
+    if (ng <= 1)
+        norm_kernel<1><<<(unsigned)T, 256, 0, s>>>(x, d, add, w, eps, 0, h32, hq);
+    else if (ng == 2)
+        norm_kernel<2><<<(unsigned)T, 256, 0, s>>>(x, d, add, w, eps, 0, h32, hq);
+    else
+        norm_kernel<kNormGroups><<<(unsigned)T, 256, 0, s>>>(x, d, add, w, eps, 0, h32, hq);
+    return cudaGetLastError();
 }
 
 // ------------------------------------------------------------------ dense GEMV
@@ -721,7 +781,6 @@ bool ensure_step_scratch(Decoder& g, int T) {
 bool run_step(Decoder& g, int T, int r0, int nh, float* lg) {
     cudaStream_t s = g.stream;
     const int HD = g.H * g.D, KD = g.HK * g.D, qkv_ld = HD + 2 * KD;
-    const size_t norm_smem = (size_t)g.d * 4 + 64;
     g.mark(0);
     const int64_t nb = (int64_t)T * (g.d / 32);
     embed_q8_kernel<<<(unsigned)((nb + 255) / 256), 256, 0, s>>>(g.embd, g.tok, T, g.x);
@@ -729,8 +788,8 @@ bool run_step(Decoder& g, int T, int r0, int nh, float* lg) {
     for (int l = 0; l < g.n_layer; ++l) {
         DLayer& Ly = g.L[(size_t)l];
         g.mark(0);
-        norm_kernel<<<(unsigned)T, 256, norm_smem, s>>>(g.x, g.d, l > 0 ? g.dm : nullptr, Ly.attn_norm, g.eps, 0, nullptr,
-                                                      g.hq);
+        if (!g.ok(launch_norm(g.x, T, g.d, l > 0 ? g.dm : nullptr, Ly.attn_norm, g.eps, nullptr, g.hq, s), "norm"))
+            return false;
         g.mark(1);
         if (!g.ok(gemv_dense(Ly.qkv, g.hq, T, g.qkv, qkv_ld, g.n_sm, s), "q/k/v projection")) return false;
         g.mark(2);
@@ -741,17 +800,15 @@ bool run_step(Decoder& g, int T, int r0, int nh, float* lg) {
         g.mark(1);
         if (!g.ok(gemv_dense(Ly.o, g.aq, T, g.o, g.d, g.n_sm, s), "output projection")) return false;
         g.mark(0);
-        norm_kernel<<<(unsigned)T, 256, norm_smem, s>>>(g.x, g.d, g.o, Ly.ffn_norm, g.eps, 0, g.h32, QInput{});
-        if (!g.ok(cudaGetLastError(), "norm")) return false;
+        if (!g.ok(launch_norm(g.x, T, g.d, g.o, Ly.ffn_norm, g.eps, g.h32, QInput{}, s), "norm")) return false;
         g.mark(3);
         if (aero_cuda_moe_forward(Ly.moe, l, g.h32, T, g.d, g.dm) != 1)
             return g.fail("layer %d MoE: %s", l, aero_cuda_moe_last_error(Ly.moe));
     }
     g.mark(0);
     // the last layer's FFN output joins the residual for every row; the head rows are normed
-    norm_kernel<<<(unsigned)T, 256, norm_smem, s>>>(g.x, g.d, g.dm, g.out_norm, g.eps, 0, nullptr,
-                                                  nh > 0 ? g.hq : QInput{});
-    if (!g.ok(cudaGetLastError(), "output norm")) return false;
+    if (!g.ok(launch_norm(g.x, T, g.d, g.dm, g.out_norm, g.eps, nullptr, nh > 0 ? g.hq : QInput{}, s), "output norm"))
+        return false;
     if (nh > 0) {
         g.mark(4);
         QInput hq = g.hq;
@@ -873,6 +930,7 @@ Decoder* open_decoder(const aero_cuda_decoder_desc* d, std::string* why, bool ow
     if (g->n_layer <= 0 || g->n_layer > 4096 || g->d <= 0 || g->d % 32 || g->vocab <= 0 || g->n_seq <= 0 || g->n_ctx <= 0)
         return bad("n_layer, vocab, n_seq, n_ctx must be positive and n_embd a multiple of 32");
     if (g->n_ctx > 1024 * kAttnChunk) return bad("n_ctx above 65536 positions per sequence");
+    if (g->d > kNormGroups * 256 * 8) return bad("n_embd above 8192");
     if (g->H <= 0 || g->HK <= 0 || g->H % g->HK || g->H / g->HK > kMaxGroup)
         return bad("n_head must be a multiple of n_head_kv with at most 16 query heads per kv head");
     if (g->D != 64 && g->D != 128 && g->D != 192 && g->D != 256) return bad("head_dim must be 64, 128, 192 or 256");
@@ -891,6 +949,13 @@ Decoder* open_decoder(const aero_cuda_decoder_desc* d, std::string* why, bool ow
     g->n_chunk = (g->n_ctx + kAttnChunk - 1) / kAttnChunk;
     if (const char* v = std::getenv("AERO_DECODER_GRAPHS")) g->use_graphs = std::atoi(v) != 0;
     const int HD = g->H * g->D, KD = g->HK * g->D;
+    // plan the whole load (weights and caches; the MoE handles planned their own)
+    // before allocating (admit_plan, src/memory_guard.cpp:192-213)
+    {
+        const size_t plan = (size_t)aero_cuda_decoder_plan_bytes(d, nullptr);
+        char why2[256];
+        if (!aero_cuda_guard_admit_plan(plan, why2, sizeof(why2))) return bad(std::string("load refused: ") + why2);
+    }
     // weights
     if (d->token_embd.dtype != AERO_DT_Q8_0) return bad("token_embd must be Q8_0");
     if (!alloc_qmat(*g, AERO_DT_Q8_0, g->vocab, g->d, g->embd, "token_embd") ||
@@ -945,6 +1010,32 @@ Decoder* open_decoder(const aero_cuda_decoder_desc* d, std::string* why, bool ow
 }  // namespace aero
 
 using aero::Decoder;
+
+extern "C" int64_t aero_cuda_decoder_plan_bytes(const aero_cuda_decoder_desc* d, int64_t* by_class) {
+    if (!d || d->n_layer <= 0 || d->n_embd <= 0 || d->vocab <= 0) return -1;
+    auto qmat = [](int dt, int64_t rows, int64_t cols) -> int64_t {
+        if (dt != AERO_DT_Q8_0 && dt != AERO_DT_Q4_K) return 0;
+        return align128(rows * qm_row_qs_bytes(dt, (int)cols)) +
+               align128(rows * qm_row_meta_bytes(dt, (int)cols));
+    };
+    const int64_t dm = d->n_embd, HD = (int64_t)d->n_head * d->head_dim, KD = (int64_t)d->n_head_kv * d->head_dim;
+    int64_t w = qmat(AERO_DT_Q8_0, d->vocab, dm) + dm * 4;
+    if (d->output.data) w += qmat(d->output.dtype, d->vocab, dm);
+    int64_t kv = 0;
+    for (int l = 0; l < d->n_layer; ++l) {
+        const int dt = d->layers ? d->layers[l].attn_q.dtype : AERO_DT_Q8_0;
+        const int dto = d->layers ? d->layers[l].attn_output.dtype : AERO_DT_Q8_0;
+        w += qmat(dt, HD + 2 * KD, dm) + qmat(dto, dm, HD) + 2 * dm * 4;
+        if (d->layers && d->layers[l].q_norm) w += (int64_t)d->head_dim * 4;
+        if (d->layers && d->layers[l].k_norm) w += (int64_t)d->head_dim * 4;
+        kv += 2 * (int64_t)d->n_seq * KD * d->n_ctx * 2;
+    }
+    if (by_class) {
+        by_class[0] = w;   // weights resident
+        by_class[1] = kv;  // KV cache
+    }
+    return w + kv;
+}
 
 extern "C" {
 

@@ -797,6 +797,38 @@ void copy_err(const std::string& s, char* err, int errlen) {
     if (err && errlen > 0) std::snprintf(err, (size_t)errlen, "%s", s.c_str());
 }
 
+// Device bytes a handle opened from d keeps resident (router rows, the
+// tensor-core router split, the expert and shared planes, a resident subset's
+// slot table), as the guard charges them; -1 for a description open refuses on
+// its face. Scratch is not included (it grows with the calls).
+int64_t plan_resident_bytes(const aero_cuda_moe_desc* d) {
+    if (!d || d->n_embd <= 0 || d->n_expert <= 0 || d->ffn_len <= 0) return -1;
+    const int dt = d->gate_exps.dtype;
+    const bool f32 = dt == AERO_DT_F32;
+    const int64_t E = d->n_expert, dp = f32 ? round_up(d->n_embd, 16) : d->n_embd;
+    const int64_t F = d->ffn_len, Fs = d->has_shared ? (d->ffn_len_shared > 0 ? d->ffn_len_shared : F) : 0;
+    int64_t ne = E;
+    if (d->n_resident > 0)
+        ne = d->n_resident;
+    else if (d->expert_begin != 0 || d->expert_end != 0)
+        ne = (int64_t)d->expert_end - d->expert_begin;
+    auto fam = [&](int t, int64_t rows, int64_t cols, int64_t n) {
+        const int64_t pr = t == AERO_DT_F32 ? round_up(rows, 16) : rows;
+        const int64_t pc = t == AERO_DT_F32 ? round_up(cols, 16) : cols;
+        return n * (align128(pr * qm_row_qs_bytes(t, (int)pc)) + align128(pr * qm_row_meta_bytes(t, (int)pc)));
+    };
+    int64_t b = (E + 1) * dp * 4;  // router rows + the shared gate input
+    if (d->router_bias) b += E * 4;
+    if (d->router && router_tc_tile_rows((int)E) > 0 && dp % 32 == 0) b += 2 * E * dp * 4;
+    b += 2 * fam(dt, F, d->n_embd, ne) + fam(dt, d->n_embd, F, ne);
+    if (d->has_shared) {
+        const int st = d->shexp_gate.dtype;
+        b += 2 * fam(st, Fs, d->n_embd, 1) + fam(st, d->n_embd, Fs, 1);
+    }
+    if (d->n_resident > 0 && d->n_resident < E) b += E * 4;
+    return b;
+}
+
 Handle* open_desc(const aero_cuda_moe_desc* d, std::string* why) {
     if (!d) {
         *why = "null descriptor";
@@ -996,6 +1028,8 @@ void* aero_cuda_moe_open(const aero_cuda_moe_desc* desc, char* err, int errlen) 
 }
 
 void aero_cuda_moe_close(void* handle) { delete static_cast<Handle*>(handle); }
+
+int64_t aero_cuda_moe_plan_bytes(const aero_cuda_moe_desc* desc) { return aero::plan_resident_bytes(desc); }
 
 int aero_cuda_moe_forward(void* handle, int layer, const float* h_in, int T, int n_embd, float* out) {
     (void)layer;

@@ -27,6 +27,49 @@ def _i64(a) -> np.ndarray:
     return np.ascontiguousarray(np.asarray(a).reshape(-1), dtype=np.int64)
 
 
+def plan_footprint(spec, n_seq: int = 1, n_ctx: int = 4096) -> dict:
+    """Device bytes the decoder of a synth.DecoderSpec holds once open, as the memory
+    guard charges them: the decoder's weights and caches (aero_cuda_decoder_plan_bytes)
+    and every layer's MoE handle (aero_cuda_moe_plan_bytes: router rows, the
+    tensor-core router's split copy, the quantised expert planes). Replaces the
+    reference's plan_footprint (engine/model.py:776-840), whose expert term
+    (:828-832) counts the fp32 bytes of the active experts, for this device layout.
+    The descriptions passed to the library carry shapes and types only (their
+    pointers are tested for presence, never read)."""
+    L = nc.lib()
+    present = ctypes.c_void_p(1).value
+    layers = (nc.DecoderLayer * spec.n_layer)()
+    for ly in layers:
+        ly.attn_q.dtype = ly.attn_k.dtype = ly.attn_v.dtype = ly.attn_output.dtype = spec.attn_dtype
+        if spec.qk_norm:
+            ly.q_norm = ly.k_norm = present
+    d = nc.DecoderDesc()
+    d.n_layer, d.n_embd, d.n_head, d.n_head_kv, d.head_dim, d.vocab = (spec.n_layer, spec.d, spec.n_head, spec.n_kv,
+                                                                      spec.head_dim, spec.vocab)
+    d.n_seq, d.n_ctx = int(n_seq), int(n_ctx)
+    d.token_embd.dtype = spec.embd_dtype
+    if not spec.tied:
+        d.output.dtype, d.output.data = spec.embd_dtype, present
+    d.layers = layers
+    by = (ctypes.c_int64 * 2)()
+    if L.aero_cuda_decoder_plan_bytes(ctypes.byref(d), by) < 0:
+        raise ValueError("invalid decoder description")
+    m = spec.moe
+    md = nc.Desc()
+    md.n_embd, md.n_expert, md.n_expert_used, md.ffn_len = m.d, m.E, m.k, m.F
+    md.router = present
+    md.gate_exps.dtype = md.up_exps.dtype = md.down_exps.dtype = m.dtype
+    if m.Fs:
+        md.has_shared, md.ffn_len_shared = 1, m.Fs
+        md.shexp_gate.dtype = md.shexp_up.dtype = md.shexp_down.dtype = m.dtype
+    moe = L.aero_cuda_moe_plan_bytes(ctypes.byref(md))
+    if moe < 0:
+        raise ValueError("invalid MoE description")
+    weights = int(by[0]) + spec.n_layer * int(moe)
+    return {"weights_resident": weights, "kv_cache": int(by[1]), "moe_weights": spec.n_layer * int(moe),
+            "total": weights + int(by[1])}
+
+
 class CudaDecoder:
     def __init__(self, handle: int, keep=None) -> None:
         if not handle:

@@ -83,12 +83,14 @@ SYMBOLS = [
     ("aero_cuda_moe_open_gguf", c_void_p, [c_char_p, c_int, c_int, c_int, c_int, c_char_p, c_int]),
     ("aero_cuda_moe_gguf_info", c_int, [c_char_p, c_int, _P, c_char_p, c_int]),
     ("aero_cuda_moe_close", None, [_P]),
+    ("aero_cuda_moe_plan_bytes", c_int64, [POINTER(Desc)]),
     ("aero_cuda_moe_model_open_gguf", c_void_p, [c_char_p, c_int, c_int, c_char_p, c_int]),
     ("aero_cuda_moe_model_forward", c_int, [_P, c_int, _P, c_int, c_int, _P]),
     ("aero_cuda_moe_model_layer", c_void_p, [_P, c_int]),
     ("aero_cuda_moe_model_close", None, [_P]),
     ("aero_cuda_decoder_open", c_void_p, [POINTER(DecoderDesc), c_char_p, c_int]),
     ("aero_cuda_decoder_open_gguf", c_void_p, [c_char_p, c_int, c_int, c_int, c_char_p, c_int]),
+    ("aero_cuda_decoder_plan_bytes", c_int64, [POINTER(DecoderDesc), _P]),
     ("aero_cuda_decoder_forward", c_int, [_P, _P, c_int, _P, _P]),
     ("aero_cuda_decoder_step", c_int, [_P, _P, _P, _P, c_int, _P]),
     ("aero_cuda_decoder_set_stream", c_int, [_P, _P]),

@@ -56,6 +56,16 @@ typedef struct aero_cuda_decoder_desc {
  * over the whole head. NULL with the reason in err. */
 void* aero_cuda_decoder_open(const aero_cuda_decoder_desc* desc, char* err, int errlen);
 
+/* Device bytes the decoder itself allocates for this description (its weights
+ * and caches; the MoE handles are planned by aero_cuda_moe_open), as the memory
+ * guard charges them: the total, and by_class[0] weights / by_class[1] KV cache
+ * when by_class is not NULL. Open checks this plan with admit_plan before it
+ * allocates. With the MoE handles' own plans (aero_b200.decoder.plan_footprint
+ * adds them) it replaces the reference's plan_footprint (engine/model.py:776-840),
+ * whose expert term (:828-832) counts fp32 bytes of the active experts, with
+ * quantised device bytes. -1 for an invalid description. */
+int64_t aero_cuda_decoder_plan_bytes(const aero_cuda_decoder_desc* desc, int64_t* by_class);
+
 /* The same from a GGUF file: metadata "<arch>.block_count", embedding_length,
  * attention.head_count, attention.head_count_kv, attention.key_length,
  * rope.freq_base, attention.layer_norm_rms_epsilon (engine/model.py:193-224);

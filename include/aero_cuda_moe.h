@@ -91,6 +91,14 @@ int aero_cuda_moe_gguf_info(const char* path, int layer, int64_t* out8, char* er
 
 void aero_cuda_moe_close(void* handle);
 
+/* Device bytes a handle opened from desc keeps resident (router rows, the
+ * tensor-core router's split copy, the quantised expert and shared-expert
+ * planes), as the memory guard charges them; no device work, the tensor data
+ * is not read. The expert term of the reference's plan_footprint
+ * (engine/model.py:828-832: fp32 bytes of the active experts) in the device
+ * bytes this library actually holds. -1 for an invalid description. */
+int64_t aero_cuda_moe_plan_bytes(const aero_cuda_moe_desc* desc);
+
 /* Every MoE layer of a GGUF file as one table (n_layer <= 0: "<arch>.block_count").
  * Layers without expert tensors stay empty and their hook call returns 0.
  * aero_cuda_moe_model_forward has the aero_moe_fn signature and dispatches on

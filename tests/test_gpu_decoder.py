@@ -147,3 +147,26 @@ def test_decoder_graph_replay_equals_eager(golden, tmp_path, monkeypatch):
     finally:
         E.close()
         G.close()
+
+
+def test_decoder_open_charges_exactly_its_plan(golden, tmp_path):
+    """Opening a decoder (its MoE handles and its own weights and caches) adds exactly
+    plan_footprint's bytes to the guard's resident-weights and KV-cache classes, and
+    closing it returns them."""
+    from aero_b200.decoder import plan_footprint
+    spec, _ = decoder_fixture(golden, "dec_q8", tmp_path)
+    seed = int(golden["dec_q8_spec"][-1])
+    g = nc.MemoryGuard()
+
+    def held():
+        return g.committed(nc.MEM_WEIGHTS_RESIDENT) + g.committed(nc.MEM_KV_CACHE)
+
+    before = held()
+    plan = plan_footprint(spec, n_seq=3, n_ctx=48)
+    D = CudaDecoder.from_synth(synth.make_decoder(spec, seed), n_seq=3, n_ctx=48)
+    try:
+        assert held() - before == plan["total"], (held() - before, plan)
+        assert g.committed(nc.MEM_KV_CACHE) >= plan["kv_cache"]
+    finally:
+        D.close()
+    assert held() == before

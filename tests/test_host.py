@@ -274,3 +274,23 @@ def test_ctypes_signatures_match_header():
     for name, _restype, argtypes in nc.SYMBOLS:
         assert name in protos, name
         assert len(argtypes) == protos[name], (name, len(argtypes), protos[name])
+
+
+def test_decoder_plan_footprint_config4(cuda_lib):
+    """The config-4 decoder's device plan (no device work): the f16 caches of 16 sequences
+    of 4096 positions, Q8_0 projections / embedding / head, and 48 MoE layers in
+    quantised planes (the reference's fp32 active-expert term would be 8 x 3 x 2048 x
+    768 x 4 B per layer)."""
+    from aero_b200.decoder import plan_footprint
+    sp = synth.DECODER_C4
+    p = plan_footprint(sp, n_seq=16, n_ctx=4096)
+    assert p["kv_cache"] == 2 * 16 * 4 * 128 * 4096 * 2 * 48
+    q8 = lambda n: n // 32 * 34  # noqa: E731
+    attn = q8((32 * 128 + 2 * 4 * 128) * 2048) + q8(2048 * 32 * 128)
+    expert = 3 * 768 * 2048 // 256 * 144
+    # device planes hold the GGUF bytes (plus 128-byte alignment per plane); the router f32
+    assert 48 * 128 * expert < p["moe_weights"] < 48 * (128 * expert + 129 * 2048 * 4 * 3 + 1 << 16)
+    assert 48 * attn + 2 * q8(151936 * 2048) < p["weights_resident"] - p["moe_weights"] < \
+        48 * attn + 2 * q8(151936 * 2048) + (1 << 22)
+    assert p["total"] == p["weights_resident"] + p["kv_cache"]
+    assert 23e9 < p["total"] < 26e9
