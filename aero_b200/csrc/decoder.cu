@@ -62,6 +62,21 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// (a, b) as f16 pairs hi = f16(v), lo = f16(v - hi): hi + lo carries v to about 2^-22.
+__device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
+    const __half ha = __float2half_rn(a), hb = __float2half_rn(b);
+    const __half la = __float2half_rn(a - __half2float(ha)), lb = __float2half_rn(b - __half2float(hb));
+    hi = (uint32_t)__half_as_ushort(ha) | ((uint32_t)__half_as_ushort(hb) << 16);
+    lo = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
+}
+// D (16x8 f32) += A (16x16 f16, row-major fragments a[4]) x B (16x8 f16, b0 / b1)
+__device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
@@ -305,12 +320,31 @@ __global__ void __launch_bounds__(128) qk_rope_kv_kernel(float* __restrict__ qkv
     for (int i = 0; i < NV; ++i) dst[i * 32 + lane] = __float2half_rn(v[i]);
 }
 
+// The A fragment (m16n8k16, row-major 16 x 16) of rows g, g + 8 (zero at or past
+// `rows`) and columns c0 + 2 tq, + 1, + 8, + 9 of an f32 matrix with row stride ld,
+// split into f16 hi and lo halves: written as two uint4 (hi a0..a3, lo a0..a3).
+__device__ __forceinline__ void make_a_frag(const float* m, int ld, int rows, int c0, int lane, uint4* dst) {
+    const int g = lane >> 2, tq = lane & 3, col = c0 + 2 * tq;
+    const bool r0 = g < rows, r1 = g + 8 < rows;
+    const float* m0 = m + g * ld;
+    const float* m1 = m + (g + 8) * ld;
+    uint32_t h[4], l[4];
+    split_pair(r0 ? m0[col] : 0.f, r0 ? m0[col + 1] : 0.f, h[0], l[0]);
+    split_pair(r1 ? m1[col] : 0.f, r1 ? m1[col + 1] : 0.f, h[1], l[1]);
+    split_pair(r0 ? m0[col + 8] : 0.f, r0 ? m0[col + 9] : 0.f, h[2], l[2]);
+    split_pair(r1 ? m1[col + 8] : 0.f, r1 ? m1[col + 9] : 0.f, h[3], l[3]);
+    dst[0] = make_uint4(h[0], h[1], h[2], h[3]);
+    dst[1] = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
 // ------------------------------------------------------------------ attention
 // CTA = (chunk c of 64 positions, token t, kv head hk): the chunk's K and V rows
-// of (seq[t], hk) staged once in shared memory (rows padded to an odd number of
-// 16-byte units: conflict-free 16-byte reads of different rows), scores of the
-// group's R query heads for positions <= pos[t] (masked to -inf otherwise,
-// scaled by 1/sqrt(D)), the chunk's max m and sum l of exp(s - m), and P V.
+// of (seq[t], hk) staged once in shared memory by asynchronous copies (rows
+// padded to an odd number of 16-byte units), the scores of the group's R <= 16
+// query heads for positions <= pos[t] (masked to -inf otherwise, scaled by
+// 1/sqrt(D)) and P V as warp-level tensor-core MMAs (m16n8k16, f16 operands with
+// the f32 queries and probabilities split into hi + lo halves, f32 accumulation),
+// the chunk's max m and sum l of exp(s - m) in f32.
 // part[t][h][c] = (m, l, -, -, acc[D]) (acc 16-byte aligned).
 template <int NV>
 __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restrict__ qkv, int ld, int H, int HK,
@@ -333,7 +367,10 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
     uint8_t* vs = ks + C * KS;
     float* qs = reinterpret_cast<float*>(vs + C * KS);
     float* S = qs + R * D;
-    float* ml = S + R * C;
+    // the MMAs' A fragments, made once per CTA (every warp uses the same ones):
+    // per 16-column step and lane, the four f16x2 registers of hi then of lo
+    uint4* qa = reinterpret_cast<uint4*>(S + R * C);  // [D / 16][32][2]
+    uint4* pa = qa + (D / 16) * 64;                   // [C / 16][32][2]
     const int64_t base = (((int64_t)seq[t] * HK + hk) * n_ctx + start) * D;
     // the chunk's rows copied asynchronously, all in flight at once, while the queries load
     constexpr int pieces = D / 8;
@@ -342,41 +379,48 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
         cp_async16(ks + row * KS + pc * 16, kc + base + (int64_t)row * D + pc * 8);
         cp_async16(vs + row * KS + pc * 16, vc + base + (int64_t)row * D + pc * 8);
     }
+    for (int i = threadIdx.x; i < (C - nv) * pieces; i += blockDim.x) {
+        const int row = nv + i / pieces, pc = i % pieces;
+        *reinterpret_cast<uint4*>(ks + row * KS + pc * 16) = make_uint4(0u, 0u, 0u, 0u);
+        *reinterpret_cast<uint4*>(vs + row * KS + pc * 16) = make_uint4(0u, 0u, 0u, 0u);
+    }
     for (int i = threadIdx.x; i < R * D; i += blockDim.x)
         qs[i] = qkv[(int64_t)t * ld + (int64_t)(hk * R) * D + i];
     cp_async_wait_all();
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int pr = warp; pr < R * (C / 32); pr += 8) {
-        const int r = pr % R, j = (pr / R) * 32 + lane;
-        float s = -INFINITY;
-        if (j < nv) {
-            const float* q = qs + r * D;
-            const uint8_t* kr = ks + j * KS;
-            float a = 0.f;
+    const int g = lane >> 2, tq = lane & 3;  // the MMA fragments' row group and column pair
+    for (int kk = warp; kk < D / 16; kk += 8) make_a_frag(qs, D, R, kk * 16, lane, qa + (kk * 32 + lane) * 2);
+    __syncthreads();
+    // scores on the tensor cores: S (query heads x positions) = Q K^T with Q split
+    // into f16 hi + lo parts (two MMAs per 16 dims, f32 accumulation; K is f16 as
+    // cached); warp w takes positions 8w .. 8w + 7, heads beyond R are zero rows
+    {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint8_t* kr = ks + (8 * warp + g) * KS;
+        const bool r0 = g < R, r1 = g + 8 < R;
 #pragma unroll 4
-            for (int d8 = 0; d8 < D; d8 += 8) {
-                const uint4 kw = *reinterpret_cast<const uint4*>(kr + d8 * 2);
-                const float4 q0 = *reinterpret_cast<const float4*>(q + d8);
-                const float4 q1 = *reinterpret_cast<const float4*>(q + d8 + 4);
-                const float2 k0 = __half22float2(*reinterpret_cast<const __half2*>(&kw.x));
-                const float2 k1 = __half22float2(*reinterpret_cast<const __half2*>(&kw.y));
-                const float2 k2 = __half22float2(*reinterpret_cast<const __half2*>(&kw.z));
-                const float2 k3 = __half22float2(*reinterpret_cast<const __half2*>(&kw.w));
-                a = fmaf(q0.x, k0.x, a);
-                a = fmaf(q0.y, k0.y, a);
-                a = fmaf(q0.z, k1.x, a);
-                a = fmaf(q0.w, k1.y, a);
-                a = fmaf(q1.x, k2.x, a);
-                a = fmaf(q1.y, k2.y, a);
-                a = fmaf(q1.z, k3.x, a);
-                a = fmaf(q1.w, k3.y, a);
-            }
-            s = a * scale;
+        for (int kk = 0; kk < D / 16; ++kk) {
+            const int col = kk * 16 + 2 * tq;
+            const uint4 fh = qa[(kk * 32 + lane) * 2], fl = qa[(kk * 32 + lane) * 2 + 1];
+            const uint32_t ah[4] = {fh.x, fh.y, fh.z, fh.w}, al[4] = {fl.x, fl.y, fl.z, fl.w};
+            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + col * 2);
+            const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + (col + 8) * 2);
+            mma_f16(acc, ah, b0, b1);
+            mma_f16(acc, al, b0, b1);
         }
-        S[r * C + j] = s;
+        const int j = 8 * warp + 2 * tq;
+        if (r0) {
+            S[g * C + j] = j < nv ? acc[0] * scale : -INFINITY;
+            S[g * C + j + 1] = j + 1 < nv ? acc[1] * scale : -INFINITY;
+        }
+        if (r1) {
+            S[(g + 8) * C + j] = j < nv ? acc[2] * scale : -INFINITY;
+            S[(g + 8) * C + j + 1] = j + 1 < nv ? acc[3] * scale : -INFINITY;
+        }
     }
     __syncthreads();
+    float* outp = part + (((int64_t)t * H + (int64_t)hk * R) * n_chunk + c) * (D + 4);
     for (int r = warp; r < R; r += 8) {
         const float s0 = S[r * C + lane], s1 = S[r * C + lane + 32];
         const float m = warp_max(fmaxf(s0, s1));  // finite: position start is always kept
@@ -386,28 +430,42 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
         S[r * C + lane + 32] = p1;
         const float l = warp_sum(p0 + p1);
         if (lane == 0) {
-            ml[2 * r] = m;
-            ml[2 * r + 1] = l;
+            float* op = outp + (int64_t)r * n_chunk * (D + 4);
+            op[0] = m;
+            op[1] = l;
         }
     }
     __syncthreads();
-    float* outp = part + (((int64_t)t * H + (int64_t)hk * R) * n_chunk + c) * (D + 4);
-    for (int i = threadIdx.x; i < R * (D / 2); i += blockDim.x) {
-        const int r = i / (D / 2), dp = i % (D / 2);
-        const float* P = S + r * C;
-        float ax = 0.f, ay = 0.f;
-        for (int j = 0; j < nv; ++j) {
-            const float pj = P[j];
-            const float2 vv = __half22float2(*reinterpret_cast<const __half2*>(vs + j * KS + dp * 4));
-            ax = fmaf(pj, vv.x, ax);
-            ay = fmaf(pj, vv.y, ay);
+    for (int kk = warp; kk < C / 16; kk += 8) make_a_frag(S, C, R, kk * 16, lane, pa + (kk * 32 + lane) * 2);
+    __syncthreads();
+    // P V on the tensor cores: (heads x dims) = P (heads x positions, f16 hi + lo)
+    // times V (positions x dims, f16); warp w takes dims 8 nt .. 8 nt + 7 for
+    // nt = w, w + 8, ...; positions past nv have P = 0 and zeroed V rows
+    for (int nt = warp; nt < D / 8; nt += 8) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const int dd = nt * 8 + g;
+        const bool r0 = g < R, r1 = g + 8 < R;
+#pragma unroll
+        for (int kk = 0; kk < C / 16; ++kk) {
+            const int j = kk * 16 + 2 * tq;
+            const uint4 fh = pa[(kk * 32 + lane) * 2], fl = pa[(kk * 32 + lane) * 2 + 1];
+            const uint32_t ah[4] = {fh.x, fh.y, fh.z, fh.w}, al[4] = {fl.x, fl.y, fl.z, fl.w};
+            const uint16_t* v0 = reinterpret_cast<const uint16_t*>(vs + j * KS) + dd;
+            const uint32_t b0 = (uint32_t)v0[0] | ((uint32_t)v0[KS / 2] << 16);
+            const uint32_t b1 = (uint32_t)v0[4 * KS] | ((uint32_t)v0[9 * KS / 2] << 16);
+            mma_f16(acc, ah, b0, b1);
+            mma_f16(acc, al, b0, b1);
         }
-        float* op = outp + (int64_t)r * n_chunk * (D + 4);
-        op[4 + 2 * dp] = ax;
-        op[5 + 2 * dp] = ay;
-        if (dp == 0) {
-            op[0] = ml[2 * r];
-            op[1] = ml[2 * r + 1];
+        const int col = 4 + nt * 8 + 2 * tq;
+        if (r0) {
+            float* op = outp + (int64_t)g * n_chunk * (D + 4);
+            op[col] = acc[0];
+            op[col + 1] = acc[1];
+        }
+        if (r1) {
+            float* op = outp + (int64_t)(g + 8) * n_chunk * (D + 4);
+            op[col] = acc[2];
+            op[col + 1] = acc[3];
         }
     }
 }
@@ -500,7 +558,9 @@ cudaError_t gemv_dense(const QMat& W, const QInput& in, int T, float* y, int ldy
 
 template <int NV>
 size_t attn_smem(int R) {
-    return (size_t)2 * kAttnChunk * (NV * 64 + 16) + (size_t)R * NV * 32 * 4 + (size_t)R * kAttnChunk * 4 + (size_t)R * 8;
+    // K and V rows, the queries, the scores, the A fragments of Q and of P
+    return (size_t)2 * kAttnChunk * (NV * 64 + 16) + (size_t)R * NV * 32 * 4 + (size_t)R * kAttnChunk * 4 +
+           (size_t)(NV * 2) * 32 * 32 + (size_t)(kAttnChunk / 16) * 32 * 32;
 }
 
 template <int NV>
