@@ -57,6 +57,7 @@ constexpr int kDecThreads = 256;
 constexpr int kDecWarps = kDecThreads / 32;
 constexpr int kScanItems = (1024 + kDecThreads) / kDecThreads;  // items per thread: E + 1 <= 1025 values
 constexpr int kRouterTokGroup = 4;  // tokens per router warp task
+constexpr int kTopkInCta = 8;       // calls of up to this many tokens select their experts in every CTA
 constexpr int kJBlock = 16;         // rows of gate and of up per block of the gate/up stream
 constexpr int kRing = 2;            // weight rows in flight per lane (two CTAs per SM)
 constexpr int kErrBarrier = 31;
@@ -536,7 +537,10 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
     const int T = a.T, E = a.E, k = a.k, P = T * k;
     const int n_warps = gridDim.x * kDecWarps;
     const int gwarp = blockIdx.x * kDecWarps + warp;
-    const bool topk_spread = T > kDecWarps;  // top-k by one warp per token over the grid
+    // top-k by one warp per token over the grid (and one more barrier) for calls of
+    // more than 8 tokens; up to 8, every CTA selects them itself (measured: at 16
+    // tokens two selections per warp take longer than the spread and its barrier)
+    const bool topk_spread = T > kTopkInCta;
     int nb = 0;                              // grid barriers passed
     if (threadIdx.x == 0) abort_s = 0;
     auto stamp = [&](int i) {
@@ -549,7 +553,10 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
     {
         const int n_rows = a.logits_in ? (a.has_shared ? 1 : 0) : E + (a.has_shared ? 1 : 0);
         const int row0 = a.logits_in ? E : 0;
-        const int n_tg = (T + kRouterTokGroup - 1) / kRouterTokGroup;
+        // tokens per task: up to kRouterTokGroup (a router row read once for them), fewer
+        // while that leaves warps idle (each token of a task is one more round trip)
+        const int per_task = max(1, min(kRouterTokGroup, (T * n_rows + n_warps - 1) / max(1, n_warps)));
+        const int n_tg = (T + per_task - 1) / per_task;
         const int n_tasks = n_rows * n_tg;
         const int nf4 = a.dp / 128;  // float4 per lane (dp <= 2048: at most 16)
         for (int task = gwarp; task < n_tasks; task += n_warps) {
@@ -559,7 +566,7 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
 #pragma unroll
             for (int i = 0; i < 16; ++i)
                 if (i < nf4) wv[i] = __ldg(reinterpret_cast<const float4*>(wr) + lane + 32 * i);
-            for (int t = tg * kRouterTokGroup; t < min(T, (tg + 1) * kRouterTokGroup); ++t) {
+            for (int t = tg * per_task; t < min(T, (tg + 1) * per_task); ++t) {
                 const float4* xr = reinterpret_cast<const float4*>(a.x + (int64_t)t * a.dp);
                 float acc = 0.f;
 #pragma unroll
@@ -875,7 +882,7 @@ bool decode_supported(int dtype, int T, int E, int k, int dp, int F, int Fs, int
     return true;
 }
 
-int decode_barriers(int T) { return T > kDecWarps ? 4 : 3; }
+int decode_barriers(int T) { return T > kTopkInCta ? 4 : 3; }
 
 cudaError_t launch_decode(const DecodeArgs& args, int n_sm, cudaStream_t s, int* grid_out) {
     DecodeArgs a = args;
