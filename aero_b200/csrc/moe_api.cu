@@ -106,6 +106,7 @@ struct Handle {
     // remapped after top-k, so dispatch and the expert products see slots.
     bool subset = false;
     int32_t* slot = nullptr;
+    std::vector<int32_t> slot_owner;  // expert held by each plane slot (host mirror of `slot`)
     int dtype = 0, sh_dtype = 0;
     QMat gate{}, up{}, down{}, sg{}, su{}, sd{};
     float* router_ext = nullptr;  // (E + 1, dp): row E = shared gate input (or zeros)
@@ -894,6 +895,7 @@ Handle* open_desc(const aero_cuda_moe_desc* d, std::string* why) {
         }
         src_experts = d->n_resident;
         h->subset = d->n_resident < h->E;  // all n_expert ids ascending: the identity map, a whole layer
+        h->slot_owner.assign(d->resident_ids, d->resident_ids + d->n_resident);
         h->e_begin = 0;
         h->e_end = d->n_resident;
     }
@@ -1030,6 +1032,82 @@ void* aero_cuda_moe_open(const aero_cuda_moe_desc* desc, char* err, int errlen) 
 void aero_cuda_moe_close(void* handle) { delete static_cast<Handle*>(handle); }
 
 int64_t aero_cuda_moe_plan_bytes(const aero_cuda_moe_desc* desc) { return aero::plan_resident_bytes(desc); }
+
+int aero_cuda_moe_page_in(void* handle, int slot, int expert, const void* gate, const void* up, const void* down) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    if (!h->subset) return h->fail("paging needs a resident-subset handle (n_resident < n_expert at open)"), -1;
+    if (h->dtype != AERO_DT_Q8_0 && h->dtype != AERO_DT_Q4_K) return h->fail("paging takes Q8_0 or Q4_K experts"), -1;
+    const int n_res = (int)h->slot_owner.size();
+    if (slot < 0 || slot >= n_res) return h->fail("slot %d outside [0, %d)", slot, n_res), -1;
+    if (expert < 0 || expert >= h->E) return h->fail("expert %d outside [0, %d)", expert, h->E), -1;
+    for (int i = 0; i < n_res; ++i)
+        if (h->slot_owner[(size_t)i] == expert && i != slot)
+            return h->fail("expert %d is resident in slot %d already", expert, i), -1;
+    if (!gate || !up || !down) return h->fail("null expert bytes"), -1;
+    cudaSetDevice(h->device);
+    // one expert of each family into plane slot `slot`, through a staging buffer for host bytes
+    struct Fam {
+        QMat* m;
+        const void* src;
+        int rows, cols;
+    } fams[3] = {{&h->gate, gate, h->F, h->d}, {&h->up, up, h->F, h->d}, {&h->down, down, h->d, h->F}};
+    const int64_t per = aero::gguf_bytes(h->dtype, (int64_t)h->F * h->d);
+    void* stage = nullptr;
+    if (aero::guarded_malloc(&stage, (size_t)per, aero::kScratch) != cudaSuccess) {
+        cudaGetLastError();
+        return h->fail("staging buffer of %lld bytes refused", (long long)per), -1;
+    }
+    bool ok = true;
+    for (auto& f : fams) {
+        const void* src = f.src;
+        if (!aero::is_device_ptr(src)) {
+            ok = h->cuda_ok(cudaMemcpyAsync(stage, src, (size_t)per, cudaMemcpyHostToDevice, h->stream), "expert copy");
+            src = stage;
+        } else if (((uintptr_t)src & 15) != 0) {
+            ok = h->fail("device expert bytes must be 16-byte aligned");
+        }
+        // the planes' bases are unshifted (slots count from 0)
+        ok = ok && h->cuda_ok(aero::launch_repack(h->dtype, static_cast<const uint8_t*>(src), f.rows, f.cols, f.rows, slot,
+                                                  const_cast<uint8_t*>(f.m->qs), const_cast<uint8_t*>(f.m->meta),
+                                                  f.m->qs_estride, f.m->meta_estride, h->stream),
+                              "expert repack");
+        ok = ok && h->cuda_ok(cudaStreamSynchronize(h->stream), "expert upload");  // staging reuse
+        if (!ok) break;
+    }
+    aero::guarded_free(stage, (size_t)per, aero::kScratch);
+    // the slot map: the previous owner leaves (also when the copy failed part way: the
+    // slot then holds no expert, and a call that selects its old owner is refused)
+    const int32_t none = -1, s32 = slot;
+    const int old = h->slot_owner[(size_t)slot];
+    if (!ok) {
+        if (old >= 0) {
+            cudaGetLastError();
+            cudaMemcpy(h->slot + old, &none, 4, cudaMemcpyHostToDevice);
+            h->slot_owner[(size_t)slot] = -1;
+        }
+        return -1;
+    }
+    if (old >= 0 && old != expert &&
+        !h->cuda_ok(cudaMemcpyAsync(h->slot + old, &none, 4, cudaMemcpyHostToDevice, h->stream), "slot map"))
+        return -1;
+    if (!h->cuda_ok(cudaMemcpyAsync(h->slot + expert, &s32, 4, cudaMemcpyHostToDevice, h->stream), "slot map") ||
+        !h->cuda_ok(cudaStreamSynchronize(h->stream), "slot map"))
+        return -1;
+    h->slot_owner[(size_t)slot] = expert;
+    return 0;
+}
+
+int aero_cuda_moe_resident(void* handle, int32_t* slot_expert, int n) {
+    auto* h = static_cast<Handle*>(handle);
+    if (!h) return -1;
+    std::lock_guard<std::mutex> lk(h->mu);
+    const int n_res = (int)h->slot_owner.size();
+    if (!slot_expert || n < n_res) return n_res;
+    for (int i = 0; i < n_res; ++i) slot_expert[i] = h->slot_owner[(size_t)i];
+    return n_res;
+}
 
 int aero_cuda_moe_forward(void* handle, int layer, const float* h_in, int T, int n_embd, float* out) {
     (void)layer;

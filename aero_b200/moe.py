@@ -294,6 +294,70 @@ class CudaMoeLayer:
         raise TypeError("CudaMoeLayer keeps experts quantised on the device; pass it to moe_ffn as expert_rows")
 
 
+def _u8(b) -> np.ndarray:
+    return np.ascontiguousarray(np.frombuffer(memoryview(b).cast("B"), dtype=np.uint8))
+
+
+class PagedMoeLayer:
+    """A MoE layer whose experts live in host memory, with n_slots of them resident on
+    the device: router-ahead expert paging (the reference's design, ENGINE_DESIGN.md
+    §3.3, ENGINE_DESIGN.md:99-101: the router result for a layer is known before its
+    experts are needed, so the prefetch is exact). A call computes the routing on the
+    device, pages in the experts it selects that are not resident (evicting the least
+    recently used ones it does not need; aero_cuda_moe_page_in), then runs the block
+    on the same logits (aero_cuda_moe_ffn_block), so every selected expert is resident.
+
+    expert_bytes(e) -> (gate, up, down): expert e's GGUF bytes of each tensor (host
+    bytes / numpy, e.g. slices of an mmap). A call that selects more experts than
+    n_slots is refused (ValueError)."""
+
+    def __init__(self, cfg: MoeConfig, expert_bytes, dtype: int, router, n_slots: int, router_bias=None,
+                 shexp: Optional[dict] = None, device: int = 0) -> None:
+        _check_k(cfg)
+        if not 0 < n_slots < cfg.n_expert:
+            raise ValueError(f"n_slots {n_slots} must be in [1, {cfg.n_expert})")
+        self.cfg, self.n_slots, self._bytes = cfg, int(n_slots), expert_bytes
+        first = [[_u8(b) for b in expert_bytes(e)] for e in range(n_slots)]
+        gate, up, down = (np.concatenate([f[i] for f in first]) for i in range(3))
+        self.layer = CudaMoeLayer.from_tensors(cfg, gate, up, down, dtype, router=router, router_bias=router_bias,
+                                               shexp=shexp, device=device, resident_ids=list(range(n_slots)))
+        self.slot_expert = list(range(n_slots))
+        self._last = [0] * n_slots
+        self._clock = 0
+        self.pages = 0  # experts paged in since open
+
+    def _page(self, slot: int, expert: int) -> None:
+        g, u, d = (_u8(b) for b in self._bytes(expert))
+        lib = nc.lib()
+        if lib.aero_cuda_moe_page_in(self.layer.handle, slot, expert, g.ctypes.data, u.ctypes.data,
+                                     d.ctypes.data) != 0:
+            raise RuntimeError(f"page-in of expert {expert}: {nc.last_error(self.layer.handle)}")
+        self.slot_expert[slot] = expert
+        self.pages += 1
+
+    def forward(self, h) -> np.ndarray:
+        h = nc.f32c(h)
+        cfg = self.cfg
+        lg = self.layer.router_logits(h)
+        idx, _ = nc.route(lg, cfg.n_expert, cfg.n_expert_used, cfg.norm_topk_prob)
+        need = sorted({int(e) for e in np.asarray(idx).reshape(-1)})
+        if len(need) > self.n_slots:
+            raise ValueError(f"the call routes to {len(need)} experts; the device holds {self.n_slots}")
+        self._clock += 1
+        where = {e: s for s, e in enumerate(self.slot_expert)}
+        free = sorted((s for s, e in enumerate(self.slot_expert) if e not in need), key=lambda s: self._last[s])
+        for e in need:
+            if e not in where:
+                self._page(free.pop(0), e)
+        for s, e in enumerate(self.slot_expert):
+            if e in need:
+                self._last[s] = self._clock
+        return self.layer.ffn_block(h, lg)
+
+    def close(self) -> None:
+        self.layer.close()
+
+
 def gguf_layer_info(path: str, layer: int) -> dict:
     """One MoE layer's description read from a GGUF file without opening it on a
     device (the metadata and tensor-shape reads of engine/model.py:193-224)."""

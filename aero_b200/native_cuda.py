@@ -84,6 +84,8 @@ SYMBOLS = [
     ("aero_cuda_moe_gguf_info", c_int, [c_char_p, c_int, _P, c_char_p, c_int]),
     ("aero_cuda_moe_close", None, [_P]),
     ("aero_cuda_moe_plan_bytes", c_int64, [POINTER(Desc)]),
+    ("aero_cuda_moe_page_in", c_int, [_P, c_int, c_int, _P, _P, _P]),
+    ("aero_cuda_moe_resident", c_int, [_P, _P, c_int]),
     ("aero_cuda_moe_model_open_gguf", c_void_p, [c_char_p, c_int, c_int, c_char_p, c_int]),
     ("aero_cuda_moe_model_forward", c_int, [_P, c_int, _P, c_int, c_int, _P]),
     ("aero_cuda_moe_model_layer", c_void_p, [_P, c_int]),

@@ -91,6 +91,22 @@ int aero_cuda_moe_gguf_info(const char* path, int layer, int64_t* out8, char* er
 
 void aero_cuda_moe_close(void* handle);
 
+/* Expert paging on a resident-subset handle (its n_resident slots; for models
+ * whose experts exceed device memory): put expert `expert`'s gate, up and down
+ * bytes (one expert of each tensor, the layer's GGUF type Q8_0 / Q4_K, host or
+ * 16-byte aligned device memory) into plane slot `slot`; the expert the slot
+ * held is no longer resident. Ordered after the handle's earlier calls; returns
+ * when the slot is ready. Refused for an expert resident in another slot. With
+ * the routing computed first (aero_cuda_moe_router_logits + aero_cuda_moe_route,
+ * exact, not speculative) a caller pages in a call's experts before the block
+ * runs on the same logits: the router-ahead prefetch of ENGINE_DESIGN.md
+ * §3.3 (ENGINE_DESIGN.md:99-101). 0 / -1. */
+int aero_cuda_moe_page_in(void* handle, int slot, int expert, const void* gate, const void* up,
+                          const void* down);
+/* The expert held by each slot into slot_expert[0..n_resident) when n is at
+ * least n_resident; returns n_resident (-1 for a NULL handle). */
+int aero_cuda_moe_resident(void* handle, int32_t* slot_expert, int n);
+
 /* Device bytes a handle opened from desc keeps resident (router rows, the
  * tensor-core router's split copy, the quantised expert and shared-expert
  * planes), as the memory guard charges them; no device work, the tensor data
