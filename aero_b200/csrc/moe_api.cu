@@ -916,7 +916,10 @@ Handle* open_desc(const aero_cuda_moe_desc* d, std::string* why) {
         if (h->Fsp % 16) return bad("ffn_len_shared must be a multiple of 16");
     }
     h->act_ld = (int)round_up(std::max(h->Fp, h->Fsp), 64);
-    h->gemm_ok = !f32 && h->dp % 128 == 0 && h->Fp % 128 == 0 && (!h->has_shared || h->Fsp % 128 == 0);
+    // the grouped GEMM dequantises routed and shared blocks with one type's code: a shared
+    // expert of another type (allowed by the GGUF format) runs prefill on the GEMV path
+    h->gemm_ok = !f32 && h->dp % 128 == 0 && h->Fp % 128 == 0 &&
+                 (!h->has_shared || (h->Fsp % 128 == 0 && h->sh_dtype == h->dtype));
     if (const char* v = std::getenv("AERO_GEMM_MIN_TOKENS")) h->gemm_min_tokens = std::max(1, std::atoi(v));
     const int ne = h->e_end - h->e_begin;
     (void)ne;

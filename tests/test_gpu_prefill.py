@@ -66,6 +66,30 @@ def test_gemm_matches_oracle_and_gemv(dt):
     assert rel_err(c, ref) <= 2e-3
 
 
+def test_shared_expert_of_another_type():
+    """Q4_K routed experts with a Q8_0 shared expert (the GGUF format types each tensor
+    on its own): a 300-token call is within the prefill bar of the oracle and equals
+    the GEMV path's result (the grouped GEMM takes one type per launch, so such a
+    layer runs prefill on the GEMV path)."""
+    spec = synth.LayerSpec(1024, 24, 4, 256, 256, Q.DTYPE_Q4_K)
+    layer = synth.make_layer(spec, 37)
+    q8 = synth.make_layer(synth.LayerSpec(1024, 24, 4, 256, 256, Q.DTYPE_Q8_0), 38)
+    layer.shexp = dict(q8.shexp)
+    x = synth.make_x(300, spec.d, 37)
+    L = synth.open_layer(layer)
+    try:
+        lg = L.router_logits(x)
+        L.set_gemm_min_tokens(1)
+        a = L.ffn_block(x, lg)
+        L.set_gemm_min_tokens(1 << 20)
+        c = L.ffn_block(x, lg)
+    finally:
+        L.close()
+    ref = O.moe_block(layer, x, lg, nthreads=os.cpu_count() or 1)
+    assert np.array_equal(a, c)
+    assert rel_err(a, ref) <= 2e-3
+
+
 @pytest.mark.parametrize("key", ["c5", "c5z"])
 def test_config5_subset(key):
     """All 8192 tokens through the GPU; a seeded 256-token subset against the oracle."""
