@@ -296,7 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) grouped_gemm_kernel(const __grid_
                 const uint32_t d0 = tmem + (uint32_t)ab * kAccStride;
                 for (int kb = 0; kb < it.nkb; ++kb) {
                     const int sa = a_n % kStages;
-                    if (!mbar_wait_backoff(full(sa), (a_n / kStages) & 1, abort_flag)) {
+                    if (!mbar_wait(full(sa), (a_n / kStages) & 1, abort_flag)) {
                         fail(kErrAFull);
                         ok = false;
                         break;
