@@ -56,6 +56,35 @@ __host__ __device__ constexpr int gemv_cpl() { return DT == AERO_DT_Q4_K ? 2 : 4
 constexpr int kAttnChunk = 64;  // cache positions per attention CTA
 constexpr int kMaxGroup = 16;   // query heads per kv head
 
+// Coded input rows (the QInput codes and scales) in the integer tensor-core layout
+// of the dense projections: per group of 16 rows and 32-value block, the 16 rows'
+// 32 code bytes of the high plane, then of the low plane (a warp's fragment load of
+// 8 rows x 32 bytes reads 256 contiguous bytes), and the block's 16 scales sx.
+struct QFrag {
+    int8_t* q;  // [groups][K / 32][2][16][32]
+    float* sx;  // [groups][K / 32][16]
+    int K;
+};
+inline size_t qfrag_bytes(int rows, int K) { return (size_t)((rows + 15) / 16) * (size_t)(K / 32) * (1024 + 64); }
+inline QFrag qfrag_at(void* base, int rows, int K) {
+    const size_t groups = (size_t)((rows + 15) / 16);
+    int8_t* q = static_cast<int8_t*>(base);
+    return QFrag{q, reinterpret_cast<float*>(q + groups * (size_t)(K / 32) * 1024), K};
+}
+// Rows [16 g, ...) onward: the layout of rows starting at a group boundary.
+inline QFrag qfrag_from_group(const QFrag& f, int g) {
+    if (!f.q) return f;
+    const int64_t nb = f.K / 32;
+    return QFrag{f.q + (int64_t)g * nb * 1024, f.sx + (int64_t)g * nb * 16, f.K};
+}
+__device__ __forceinline__ int8_t* qfrag_code(const QFrag& f, int row, int col, int plane) {
+    const int64_t nb = f.K / 32;
+    return f.q + (((int64_t)(row >> 4) * nb + (col >> 5)) * 2 + plane) * 512 + (row & 15) * 32 + (col & 31);
+}
+__device__ __forceinline__ float* qfrag_sx(const QFrag& f, int row, int blk) {
+    return f.sx + ((int64_t)(row >> 4) * (f.K / 32) + blk) * 16 + (row & 15);
+}
+
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src)
                  : "memory");
@@ -70,8 +99,9 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint3
     lo = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
 }
 // D (16x8 f32) += A (16x16 f16, row-major fragments a[4]) x B (16x8 f16, b0 / b1)
+// (not volatile: the compiler may issue later loads ahead of an MMA waiting on its operands)
 __device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-    asm volatile(
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
         : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
@@ -120,7 +150,7 @@ constexpr int kNormGroups = 4;  // 8-value groups per thread at most: d <= 4 * 2
 template <int NG>
 __global__ void __launch_bounds__(256) norm_kernel(float* __restrict__ x, int d, const float* __restrict__ add,
                                                    const float* __restrict__ w, float eps, int r0,
-                                                   float* __restrict__ h32, QInput hq) {
+                                                   float* __restrict__ h32, QInput hq, QFrag hf) {
     __shared__ float red[8];
     const int t = r0 + (int)blockIdx.x, o = (int)blockIdx.x;
     const int ng = d / 8;
@@ -195,20 +225,25 @@ __global__ void __launch_bounds__(256) norm_kernel(float* __restrict__ x, int d,
         *reinterpret_cast<uint2*>(hq.q1 + (int64_t)o * hq.K + col) = make_uint2(p1[0], p1[1]);
         *reinterpret_cast<uint2*>(hq.q0 + (int64_t)o * hq.K + col) = make_uint2(p0[0], p0[1]);
         if (q == 0) hq.sx[(int64_t)o * (hq.K / 32) + (col >> 5)] = mx / 16383.0f;
+        if (hf.q) {
+            *reinterpret_cast<uint2*>(qfrag_code(hf, o, (int)col, 0)) = make_uint2(p1[0], p1[1]);
+            *reinterpret_cast<uint2*>(qfrag_code(hf, o, (int)col, 1)) = make_uint2(p0[0], p0[1]);
+            if (q == 0) *qfrag_sx(hf, o, (int)(col >> 5)) = mx / 16383.0f;
+        }
         if ((q & 1) == 0) hq.s16[(int64_t)o * (hq.K / 16) + (col >> 4)] = s16;
     }
 }
 
 cudaError_t launch_norm(float* x, int T, int d, const float* add, const float* w, float eps, float* h32, QInput hq,
-                        cudaStream_t s) {
+                        QFrag hf, cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
     const int ng = (d / 8 + 255) / 256;
     if (ng <= 1)
-        norm_kernel<1><<<(unsigned)T, 256, 0, s>>>(x, d, add, w, eps, 0, h32, hq);
+        norm_kernel<1><<<(unsigned)T, 256, 0, s>>>(x, d, add, w, eps, 0, h32, hq, hf);
     else if (ng == 2)
-        norm_kernel<2><<<(unsigned)T, 256, 0, s>>>(x, d, add, w, eps, 0, h32, hq);
+        norm_kernel<2><<<(unsigned)T, 256, 0, s>>>(x, d, add, w, eps, 0, h32, hq, hf);
     else
-        norm_kernel<kNormGroups><<<(unsigned)T, 256, 0, s>>>(x, d, add, w, eps, 0, h32, hq);
+        norm_kernel<kNormGroups><<<(unsigned)T, 256, 0, s>>>(x, d, add, w, eps, 0, h32, hq, hf);
     return cudaGetLastError();
 }
 
@@ -260,6 +295,117 @@ __global__ void __launch_bounds__(256, 2) dense_gemv_kernel(QMat W, QInput in, i
         }
         if (lane < nt) y[(int64_t)(t0 + lane) * ldy + r] = acc_s[warp][lane];
         __syncwarp();
+    }
+}
+
+// ------------------------------------------- dense Q8_0 rows x tokens, tensor cores
+// y[t][r] = W[r] . in[t] for Q8_0 rows and 2..16 tokens of blockIdx.y's group: the
+// same integer sums as the row dots above, on the tensor cores. Per 32-value block
+// (one Q8_0 scale d, one input scale sx) the block's codes give two integer MMAs
+// (m16n8k32, s8 x s8 -> s32): the weight codes against the input's high and low
+// code planes, 128 hi + lo exactly in int32, then d sx times that in f32. A CTA
+// owns 16 rows; its 8 warps take every 8th block of K (tensor-core A: the 16 rows,
+// B: 8 tokens per tile) and their partial sums meet in shared memory in warp order.
+// Thread (g, q) of a warp loads bytes [8 q, 8 q + 8) of a block for row g and row
+// g + 8 (one 8-byte load each) and the same bytes of token g's codes: the MMA sums
+// over k, so one permutation of k applied to both operands (the fragment's k
+// positions 4q..4q+3 and 16+4q..16+4q+3 read bytes 8q..8q+7) leaves the sums
+// unchanged.
+constexpr int kMmaWarps = 8;
+
+// Neither asm is volatile: the weights are read-only for the launch, and the
+// compiler may then issue the loads of later blocks ahead of the MMAs that wait.
+__device__ __forceinline__ uint2 ld_stream8(const void* p) {
+    uint2 v;
+    asm("ld.global.nc.L1::no_allocate.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void mma_s8(int (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm(
+        "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
+}
+
+template <int NT>  // 8-token tiles per CTA (1: up to 8 tokens, 2: up to 16)
+__global__ void __launch_bounds__(256) dense_mma_q8_kernel(QMat W, QFrag in, int T, float* __restrict__ y, int ldy) {
+    constexpr int U = 4;  // blocks whose loads are issued together
+    __shared__ float red[kMmaWarps][16][16];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, q = lane & 3;
+    const int r0 = (int)blockIdx.x * 16, t0 = (int)blockIdx.y * 16;
+    const int nt = min(16, T - t0);
+    const int nblk = W.cols / 32;
+    // rows past the matrix read its last row and are not stored
+    const int ra = min(r0 + g, W.rows - 1), rb = min(r0 + g + 8, W.rows - 1);
+    const uint8_t* qa = W.qs + (int64_t)ra * W.cols + 8 * q;
+    const uint8_t* qb = W.qs + (int64_t)rb * W.cols + 8 * q;
+    const unsigned short* ma = reinterpret_cast<const unsigned short*>(W.meta + (int64_t)ra * nblk * 2);
+    const unsigned short* mb = reinterpret_cast<const unsigned short*>(W.meta + (int64_t)rb * nblk * 2);
+    // this thread's B token (8 j + g) and accumulator tokens (8 j + 2 q, + 1) per
+    // tile, in the group's tensor-core layout (t0 is a multiple of 16); products of
+    // tokens past the call's are computed on stale codes and never stored
+    const int64_t grp = t0 >> 4;
+    float acc[NT][4];
+#pragma unroll
+    for (int j = 0; j < NT; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
+    // warp w takes the contiguous blocks [w nper, (w + 1) nper) (nper a multiple of U),
+    // U at a time: the U scales of a row are one 8-byte load (nblk is a multiple of U)
+    const int nper = ((nblk + kMmaWarps - 1) / kMmaWarps + U - 1) / U * U;
+    const int bend = min(nblk, (warp + 1) * nper);
+    for (int b0 = warp * nper; b0 < bend; b0 += U) {
+        uint2 wa[U], wb[U], h[U][NT], l[U][NT];
+        float s0[U][NT], s1[U][NT];
+        const uint2 sa4 = __ldg(reinterpret_cast<const uint2*>(ma + b0)), sb4 = __ldg(reinterpret_cast<const uint2*>(mb + b0));
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int b = b0 + u;  // < nblk: b0 + U <= nblk
+            wa[u] = ld_stream8(qa + (int64_t)b * 32);
+            wb[u] = ld_stream8(qb + (int64_t)b * 32);
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                const int8_t* f = in.q + ((grp * nblk + b) * 2) * 512 + (8 * j + g) * 32 + 8 * q;
+                h[u][j] = *reinterpret_cast<const uint2*>(f);
+                l[u][j] = *reinterpret_cast<const uint2*>(f + 512);
+                const float2 sv = *reinterpret_cast<const float2*>(in.sx + (grp * nblk + b) * 16 + 8 * j + 2 * q);
+                s0[u][j] = sv.x;
+                s1[u][j] = sv.y;
+            }
+        }
+        const uint32_t sav[2] = {sa4.x, sa4.y}, sbv[2] = {sb4.x, sb4.y};
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (b0 + u >= bend) break;
+            const uint32_t A[4] = {wa[u].x, wb[u].x, wa[u].y, wb[u].y};
+            const float da = __half2float(__ushort_as_half((unsigned short)(sav[u >> 1] >> (16 * (u & 1)))));
+            const float db = __half2float(__ushort_as_half((unsigned short)(sbv[u >> 1] >> (16 * (u & 1)))));
+#pragma unroll
+            for (int j = 0; j < NT; ++j) {
+                int ch[4], cl[4];
+                mma_s8(ch, A, h[u][j].x, h[u][j].y);
+                mma_s8(cl, A, l[u][j].x, l[u][j].y);
+                acc[j][0] = fmaf((float)(128 * ch[0] + cl[0]), da * s0[u][j], acc[j][0]);
+                acc[j][1] = fmaf((float)(128 * ch[1] + cl[1]), da * s1[u][j], acc[j][1]);
+                acc[j][2] = fmaf((float)(128 * ch[2] + cl[2]), db * s0[u][j], acc[j][2]);
+                acc[j][3] = fmaf((float)(128 * ch[3] + cl[3]), db * s1[u][j], acc[j][3]);
+            }
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+        const int tc = 8 * j + 2 * q;
+        red[warp][g][tc] = acc[j][0];
+        red[warp][g][tc + 1] = acc[j][1];
+        red[warp][g + 8][tc] = acc[j][2];
+        red[warp][g + 8][tc + 1] = acc[j][3];
+    }
+    __syncthreads();
+    const int row = threadIdx.x >> 4, tk = threadIdx.x & 15;
+    if (tk < nt && tk < 8 * NT && r0 + row < W.rows) {
+        float v = 0.f;
+#pragma unroll
+        for (int w = 0; w < kMmaWarps; ++w) v += red[w][row][tk];
+        y[(int64_t)(t0 + tk) * ldy + r0 + row] = v;
     }
 }
 
@@ -476,7 +622,7 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
 // and the four warps' sums meet in shared memory.
 __global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restrict__ part, int H, int D, int n_chunk,
                                                            const int64_t* __restrict__ pos, float* __restrict__ att,
-                                                           QInput aq) {
+                                                           QInput aq, QFrag af) {
     __shared__ float ew[1024];  // e^(m_c - M), chunk c (n_chunk <= 1024)
     __shared__ float red[4];
     __shared__ float4 accs[4][64];
@@ -534,15 +680,34 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restri
         qinput_block(reinterpret_cast<const float*>(&accs[0][0]) + 32 * b, aq.q1 + (int64_t)t * aq.K + c,
                      aq.q0 + (int64_t)t * aq.K + c, aq.sx + (int64_t)t * (aq.K / 32) + (c >> 5),
                      aq.s16 + (int64_t)t * (aq.K / 16) + (c >> 4));
+        if (af.q) {
+            // the block this thread just coded, copied into the tensor-core layout
+            const uint4* h1 = reinterpret_cast<const uint4*>(aq.q1 + (int64_t)t * aq.K + c);
+            const uint4* h0 = reinterpret_cast<const uint4*>(aq.q0 + (int64_t)t * aq.K + c);
+            uint4* f1 = reinterpret_cast<uint4*>(qfrag_code(af, t, c, 0));
+            uint4* f0 = reinterpret_cast<uint4*>(qfrag_code(af, t, c, 1));
+            f1[0] = h1[0], f1[1] = h1[1], f0[0] = h0[0], f0[1] = h0[1];
+            *qfrag_sx(af, t, c >> 5) = aq.sx[(int64_t)t * (aq.K / 32) + (c >> 5)];
+        }
     }
 }
 
 // ------------------------------------------------------------------ launchers
 template <int DT>
-cudaError_t gemv_dense_dt(const QMat& W, const QInput& in, int T, float* y, int ldy, int n_sm, cudaStream_t s) {
+cudaError_t gemv_dense_dt(const QMat& W, const QInput& in, const QFrag& fr, int T, float* y, int ldy, int n_sm,
+                          cudaStream_t s) {
     if (T <= 0) return cudaSuccess;
     const int nch = Layout<DT>::chunks(W.cols);
     const dim3 grid((unsigned)std::max(1, std::min((W.rows + 7) / 8, n_sm * 4)), (unsigned)((T + kTokGroup - 1) / kTokGroup));
+    if (DT == AERO_DT_Q8_0 && T >= 2 && fr.q && W.cols % 128 == 0 && fr.K == W.cols) {
+        // several tokens: the integer tensor-core form (a CTA per 16 rows)
+        const dim3 mg((unsigned)((W.rows + 15) / 16), (unsigned)((T + kTokGroup - 1) / kTokGroup));
+        if (T <= 8)
+            dense_mma_q8_kernel<1><<<mg, 256, 0, s>>>(W, fr, T, y, ldy);
+        else
+            dense_mma_q8_kernel<2><<<mg, 256, 0, s>>>(W, fr, T, y, ldy);
+        return cudaGetLastError();
+    }
     if (T == 1 && nch <= 32 * gemv_cpl<DT>())
         dense_gemv_kernel<DT, true><<<grid, 256, 0, s>>>(W, in, T, y, ldy);
     else
@@ -550,9 +715,11 @@ cudaError_t gemv_dense_dt(const QMat& W, const QInput& in, int T, float* y, int 
     return cudaGetLastError();
 }
 
-cudaError_t gemv_dense(const QMat& W, const QInput& in, int T, float* y, int ldy, int n_sm, cudaStream_t s) {
-    if (W.dtype == AERO_DT_Q8_0) return gemv_dense_dt<AERO_DT_Q8_0>(W, in, T, y, ldy, n_sm, s);
-    if (W.dtype == AERO_DT_Q4_K) return gemv_dense_dt<AERO_DT_Q4_K>(W, in, T, y, ldy, n_sm, s);
+// fr: the same input rows in the tensor-core layout (fr.q null: the CUDA-core form only)
+cudaError_t gemv_dense(const QMat& W, const QInput& in, const QFrag& fr, int T, float* y, int ldy, int n_sm,
+                       cudaStream_t s) {
+    if (W.dtype == AERO_DT_Q8_0) return gemv_dense_dt<AERO_DT_Q8_0>(W, in, fr, T, y, ldy, n_sm, s);
+    if (W.dtype == AERO_DT_Q4_K) return gemv_dense_dt<AERO_DT_Q4_K>(W, in, fr, T, y, ldy, n_sm, s);
     return cudaErrorInvalidValue;
 }
 
@@ -566,7 +733,7 @@ size_t attn_smem(int R) {
 template <int NV>
 cudaError_t attention_nv(float* qkv, int ld, int T, int H, int HK, const float* qn, const float* kn, float eps,
                          float base, const int64_t* pos, const int32_t* seq, __half* kc, __half* vc, int n_ctx,
-                         float* part, int n_chunk, float* att, QInput aq, cudaStream_t s) {
+                         float* part, int n_chunk, float* att, QInput aq, QFrag af, cudaStream_t s) {
     const int per = H + 2 * HK;
     qk_rope_kv_kernel<NV><<<(unsigned)((T * per + 3) / 4), 128, 0, s>>>(qkv, T, H, HK, ld, qn, kn, eps, base, pos, seq,
                                                                         kc, vc, n_ctx);
@@ -582,18 +749,18 @@ cudaError_t attention_nv(float* qkv, int ld, int T, int H, int HK, const float* 
     const float scale = 1.0f / std::sqrt((float)(NV * 32));
     attn_partial_kernel<NV><<<dim3((unsigned)n_chunk, (unsigned)(T * HK)), 256, smem, s>>>(
         qkv, ld, H, HK, kc, vc, n_ctx, pos, seq, scale, part, n_chunk);
-    attn_combine_kernel<<<(unsigned)(T * H), 128, 0, s>>>(part, H, NV * 32, n_chunk, pos, att, aq);
+    attn_combine_kernel<<<(unsigned)(T * H), 128, 0, s>>>(part, H, NV * 32, n_chunk, pos, att, aq, af);
     return cudaGetLastError();
 }
 
 cudaError_t attention(int D, float* qkv, int ld, int T, int H, int HK, const float* qn, const float* kn, float eps,
                       float base, const int64_t* pos, const int32_t* seq, __half* kc, __half* vc, int n_ctx,
-                      float* part, int n_chunk, float* att, QInput aq, cudaStream_t s) {
+                      float* part, int n_chunk, float* att, QInput aq, QFrag af, cudaStream_t s) {
     switch (D) {
-        case 64: return attention_nv<2>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, aq, s);
-        case 128: return attention_nv<4>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, aq, s);
-        case 192: return attention_nv<6>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, aq, s);
-        case 256: return attention_nv<8>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, aq, s);
+        case 64: return attention_nv<2>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, aq, af, s);
+        case 128: return attention_nv<4>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, aq, af, s);
+        case 192: return attention_nv<6>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, aq, af, s);
+        case 256: return attention_nv<8>(qkv, ld, T, H, HK, qn, kn, eps, base, pos, seq, kc, vc, n_ctx, part, n_chunk, att, aq, af, s);
     }
     return cudaErrorInvalidValue;
 }
@@ -630,6 +797,7 @@ struct Decoder {
     int32_t *tok = nullptr, *seq = nullptr;
     int64_t* pos = nullptr;
     QInput hq{}, aq{};
+    QFrag hf{}, af{};  // hq and aq in the dense projections' tensor-core layout
     std::string err;
     // CUDA graphs of decode steps (T <= kDecodeMaxTokens): keyed by (T, first head
     // row, head rows, logits pointer); a key runs eagerly once (sizing every
@@ -804,6 +972,7 @@ bool ensure_step_scratch(Decoder& g, int T) {
     const size_t o_o = take((size_t)cap * g.d * 4), o_dm = take((size_t)cap * g.d * 4);
     const size_t o_part = take((size_t)cap * g.H * g.n_chunk * (g.D + 4) * 4);
     const size_t o_hq = take(qinput_bytes(cap, g.d)), o_aq = take(qinput_bytes(cap, HD));
+    const size_t o_hf = take(qfrag_bytes(cap, g.d)), o_af = take(qfrag_bytes(cap, HD));
     const size_t o_tok = take((size_t)cap * 4), o_seq = take((size_t)cap * 4), o_pos = take((size_t)cap * 8);
     const size_t o_lg = take((size_t)cap * g.vocab * 4);
     void* p = nullptr;
@@ -829,6 +998,8 @@ bool ensure_step_scratch(Decoder& g, int T) {
     g.part = (float*)(b + o_part);
     g.hq = qinput_at(b + o_hq, cap, g.d);
     g.aq = qinput_at(b + o_aq, cap, HD);
+    g.hf = qfrag_at(b + o_hf, cap, g.d);
+    g.af = qfrag_at(b + o_af, cap, HD);
     g.tok = (int32_t*)(b + o_tok);
     g.seq = (int32_t*)(b + o_seq);
     g.pos = (int64_t*)(b + o_pos);
@@ -848,26 +1019,34 @@ bool run_step(Decoder& g, int T, int r0, int nh, float* lg) {
     for (int l = 0; l < g.n_layer; ++l) {
         DLayer& Ly = g.L[(size_t)l];
         g.mark(0);
-        if (!g.ok(launch_norm(g.x, T, g.d, l > 0 ? g.dm : nullptr, Ly.attn_norm, g.eps, nullptr, g.hq, s), "norm"))
+        if (!g.ok(launch_norm(g.x, T, g.d, l > 0 ? g.dm : nullptr, Ly.attn_norm, g.eps, nullptr, g.hq,
+                              T >= 2 ? g.hf : QFrag{}, s),
+                  "norm"))
             return false;
         g.mark(1);
-        if (!g.ok(gemv_dense(Ly.qkv, g.hq, T, g.qkv, qkv_ld, g.n_sm, s), "q/k/v projection")) return false;
+        if (!g.ok(gemv_dense(Ly.qkv, g.hq, T >= 2 ? g.hf : QFrag{}, T, g.qkv, qkv_ld, g.n_sm, s), "q/k/v projection"))
+            return false;
         g.mark(2);
         if (!g.ok(attention(g.D, g.qkv, qkv_ld, T, g.H, g.HK, Ly.q_norm, Ly.k_norm, g.eps, g.rope_base, g.pos, g.seq,
-                            Ly.kc, Ly.vc, g.n_ctx, g.part, g.n_chunk, g.att, g.aq, s),
+                            Ly.kc, Ly.vc, g.n_ctx, g.part, g.n_chunk, g.att, g.aq, T >= 2 ? g.af : QFrag{}, s),
                   "attention"))
             return false;
         g.mark(1);
-        if (!g.ok(gemv_dense(Ly.o, g.aq, T, g.o, g.d, g.n_sm, s), "output projection")) return false;
+        if (!g.ok(gemv_dense(Ly.o, g.aq, T >= 2 ? g.af : QFrag{}, T, g.o, g.d, g.n_sm, s), "output projection"))
+            return false;
         g.mark(0);
-        if (!g.ok(launch_norm(g.x, T, g.d, g.o, Ly.ffn_norm, g.eps, g.h32, QInput{}, s), "norm")) return false;
+        if (!g.ok(launch_norm(g.x, T, g.d, g.o, Ly.ffn_norm, g.eps, g.h32, QInput{}, QFrag{}, s), "norm")) return false;
         g.mark(3);
         if (aero_cuda_moe_forward(Ly.moe, l, g.h32, T, g.d, g.dm) != 1)
             return g.fail("layer %d MoE: %s", l, aero_cuda_moe_last_error(Ly.moe));
     }
     g.mark(0);
     // the last layer's FFN output joins the residual for every row; the head rows are normed
-    if (!g.ok(launch_norm(g.x, T, g.d, g.dm, g.out_norm, g.eps, nullptr, nh > 0 ? g.hq : QInput{}, s), "output norm"))
+    // the head rows start at r0: the tensor-core layout serves them when r0 is a group boundary
+    const bool head_frag = nh >= 2 && r0 % 16 == 0;
+    if (!g.ok(launch_norm(g.x, T, g.d, g.dm, g.out_norm, g.eps, nullptr, nh > 0 ? g.hq : QInput{},
+                          head_frag ? g.hf : QFrag{}, s),
+              "output norm"))
         return false;
     if (nh > 0) {
         g.mark(4);
@@ -876,7 +1055,10 @@ bool run_step(Decoder& g, int T, int r0, int nh, float* lg) {
         hq.q0 += (int64_t)r0 * hq.K;
         hq.sx += (int64_t)r0 * (hq.K / 32);
         hq.s16 += (int64_t)r0 * (hq.K / 16);
-        if (!g.ok(gemv_dense(g.head, hq, nh, lg, g.vocab, g.n_sm, s), "head")) return false;
+        if (!g.ok(gemv_dense(g.head, hq, head_frag ? qfrag_from_group(g.hf, r0 / 16) : QFrag{}, nh, lg, g.vocab,
+                             g.n_sm, s),
+                  "head"))
+            return false;
     }
     g.mark(0);
     return true;
