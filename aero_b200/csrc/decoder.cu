@@ -99,6 +99,22 @@ __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint3
     lo = (uint32_t)__half_as_ushort(la) | ((uint32_t)__half_as_ushort(lb) << 16);
 }
 // D (16x8 f32) += A (16x16 f16, row-major fragments a[4]) x B (16x8 f16, b0 / b1)
+// Four 8x8 f16 matrices from shared memory (lane i addresses row i % 8 of matrix
+// i / 8): r[m] is matrix m's fragment (row g, columns 2 tq, 2 tq + 1), or with TRANS
+// its transpose's (rows 2 tq, 2 tq + 1 of column g). Row addresses 16-byte aligned.
+template <bool TRANS>
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* row_addr) {
+    const uint32_t a = (uint32_t)__cvta_generic_to_shared(row_addr);
+    if (TRANS)
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                     : "r"(a));
+    else
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                     : "r"(a));
+}
+
 // (not volatile: the compiler may issue later loads ahead of an MMA waiting on its operands)
 __device__ __forceinline__ void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm(
@@ -543,17 +559,21 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
     // cached); warp w takes positions 8w .. 8w + 7, heads beyond R are zero rows
     {
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint8_t* kr = ks + (8 * warp + g) * KS;
+        // lane i addresses position 8 warp + i % 8, dims 32 kp + 8 (i / 8): two k-steps per load
+        const uint8_t* kr = ks + (8 * warp + (lane & 7)) * KS + (lane >> 3) * 16;
         const bool r0 = g < R, r1 = g + 8 < R;
-#pragma unroll 4
-        for (int kk = 0; kk < D / 16; ++kk) {
-            const int col = kk * 16 + 2 * tq;
-            const uint4 fh = qa[(kk * 32 + lane) * 2], fl = qa[(kk * 32 + lane) * 2 + 1];
-            const uint32_t ah[4] = {fh.x, fh.y, fh.z, fh.w}, al[4] = {fl.x, fl.y, fl.z, fl.w};
-            const uint32_t b0 = *reinterpret_cast<const uint32_t*>(kr + col * 2);
-            const uint32_t b1 = *reinterpret_cast<const uint32_t*>(kr + (col + 8) * 2);
-            mma_f16(acc, ah, b0, b1);
-            mma_f16(acc, al, b0, b1);
+#pragma unroll 2
+        for (int kp = 0; kp < D / 32; ++kp) {
+            uint32_t b[4];
+            ldsm_x4<false>(b, kr + kp * 64);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int kk = 2 * kp + h;
+                const uint4 fh = qa[(kk * 32 + lane) * 2], fl = qa[(kk * 32 + lane) * 2 + 1];
+                const uint32_t ah[4] = {fh.x, fh.y, fh.z, fh.w}, al[4] = {fl.x, fl.y, fl.z, fl.w};
+                mma_f16(acc, ah, b[2 * h], b[2 * h + 1]);
+                mma_f16(acc, al, b[2 * h], b[2 * h + 1]);
+            }
         }
         const int j = 8 * warp + 2 * tq;
         if (r0) {
@@ -589,18 +609,20 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
     // nt = w, w + 8, ...; positions past nv have P = 0 and zeroed V rows
     for (int nt = warp; nt < D / 8; nt += 8) {
         float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        const int dd = nt * 8 + g;
         const bool r0 = g < R, r1 = g + 8 < R;
 #pragma unroll
-        for (int kk = 0; kk < C / 16; ++kk) {
-            const int j = kk * 16 + 2 * tq;
-            const uint4 fh = pa[(kk * 32 + lane) * 2], fl = pa[(kk * 32 + lane) * 2 + 1];
-            const uint32_t ah[4] = {fh.x, fh.y, fh.z, fh.w}, al[4] = {fl.x, fl.y, fl.z, fl.w};
-            const uint16_t* v0 = reinterpret_cast<const uint16_t*>(vs + j * KS) + dd;
-            const uint32_t b0 = (uint32_t)v0[0] | ((uint32_t)v0[KS / 2] << 16);
-            const uint32_t b1 = (uint32_t)v0[4 * KS] | ((uint32_t)v0[9 * KS / 2] << 16);
-            mma_f16(acc, ah, b0, b1);
-            mma_f16(acc, al, b0, b1);
+        for (int kp = 0; kp < C / 32; ++kp) {
+            // lane i addresses position 32 kp + i, dims 8 nt .. 8 nt + 7 (transposed: two k-steps)
+            uint32_t b[4];
+            ldsm_x4<true>(b, vs + (kp * 32 + lane) * KS + nt * 16);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int kk = 2 * kp + h;
+                const uint4 fh = pa[(kk * 32 + lane) * 2], fl = pa[(kk * 32 + lane) * 2 + 1];
+                const uint32_t ah[4] = {fh.x, fh.y, fh.z, fh.w}, al[4] = {fl.x, fl.y, fl.z, fl.w};
+                mma_f16(acc, ah, b[2 * h], b[2 * h + 1]);
+                mma_f16(acc, al, b[2 * h], b[2 * h + 1]);
+            }
         }
         const int col = 4 + nt * 8 + 2 * tq;
         if (r0) {
