@@ -170,3 +170,31 @@ def test_decoder_open_charges_exactly_its_plan(golden, tmp_path):
     finally:
         D.close()
     assert held() == before
+
+
+def test_decoder_batched_steps_match_single_steps_at_full_width():
+    """At the config-4 widths (d 2048, 32 x 128 query heads, 4 kv heads; Q8_0
+    projections and head, Q4_K experts), steps of 16 sequences at once (the dense
+    projections and head on the integer tensor-core kernel) give the logits of the
+    same tokens run one at a time (the single-token CUDA-core kernels), within the
+    decode bar of their RMS; every argmax equal."""
+    spec = synth.DecoderSpec(2, 2048, 32, 4, 128, 4096, synth.LayerSpec(2048, 16, 4, 768, 0, synth.DTYPE_Q4_K))
+    dec = synth.make_decoder(spec, 5, device_gen=True)
+    B = CudaDecoder.from_synth(dec, n_seq=16, n_ctx=32)
+    S = CudaDecoder.from_synth(dec, n_seq=16, n_ctx=32)
+    try:
+        rng = np.random.default_rng(6)
+        errs = []
+        for p in range(3):
+            tok = rng.integers(0, spec.vocab, 16)
+            batched = B.step(tok, np.arange(16), np.full(16, p))
+            for sq in range(16):
+                one = S.step(tok[sq:sq + 1], [sq], [p])[0]
+                e = rel(batched[sq], one)
+                errs.append(e)
+                assert e <= TOL, (p, sq, e)
+                assert int(np.argmax(batched[sq])) == int(np.argmax(one)), (p, sq)
+        print(f"batched vs single steps: max logit error / RMS {max(errs):.2e}")
+    finally:
+        B.close()
+        S.close()
