@@ -90,6 +90,10 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
                  : "memory");
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// every group but the most recent N committed by this thread has landed
+template <int N>
+__device__ __forceinline__ void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // (a, b) as f16 pairs hi = f16(v), lo = f16(v - hi): hi + lo carries v to about 2^-22.
 __device__ __forceinline__ void split_pair(float a, float b, uint32_t& hi, uint32_t& lo) {
@@ -500,9 +504,11 @@ __device__ __forceinline__ void make_a_frag(const float* m, int ld, int rows, in
 }
 
 // ------------------------------------------------------------------ attention
-// CTA = (chunk c of 64 positions, token t, kv head hk): the chunk's K and V rows
-// of (seq[t], hk) staged once in shared memory by asynchronous copies (rows
-// padded to an odd number of 16-byte units), the scores of the group's R <= 16
+// CTA = (nch consecutive chunks of 64 positions, token t, kv head hk): each
+// chunk's K and V rows of (seq[t], hk) staged in shared memory by asynchronous
+// copies, two buffers so the next chunk's copies fly while this one is computed
+// (rows padded to an odd number of 16-byte units; the queries and their MMA
+// fragments made once per CTA), per chunk the scores of the group's R <= 16
 // query heads for positions <= pos[t] (masked to -inf otherwise, scaled by
 // 1/sqrt(D)) and P V as warp-level tensor-core MMAs (m16n8k16, f16 operands with
 // the f32 queries and probabilities split into hi + lo halves, f32 accumulation),
@@ -514,46 +520,77 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
                                                            const __half* __restrict__ vc, int n_ctx,
                                                            const int64_t* __restrict__ pos,
                                                            const int32_t* __restrict__ seq, float scale,
-                                                           float* __restrict__ part, int n_chunk) {
+                                                           float* __restrict__ part, int n_chunk, int nch) {
     constexpr int D = NV * 32;
     constexpr int KS = D * 2 + 16;
     constexpr int C = kAttnChunk;
-    const int c = (int)blockIdx.x, t = (int)blockIdx.y / HK, hk = (int)blockIdx.y % HK;
+    const int t = (int)blockIdx.y / HK, hk = (int)blockIdx.y % HK;
     const int64_t qp = pos[t];
-    const int start = c * C;
-    if (start > qp) return;
-    const int nv = (int)min((int64_t)C, qp - start + 1);
+    const int c0 = (int)blockIdx.x * nch;
+    if ((int64_t)c0 * C > qp) return;
+    const int c1 = (int)min((int64_t)min(n_chunk, c0 + nch), qp / C + 1);  // chunks [c0, c1) hold positions <= qp
     const int R = H / HK;
     extern __shared__ __align__(16) uint8_t sm[];
-    uint8_t* ks = sm;
-    uint8_t* vs = ks + C * KS;
-    float* qs = reinterpret_cast<float*>(vs + C * KS);
+    uint8_t* kbuf = sm;                    // [2][C][KS]
+    uint8_t* vbuf = kbuf + 2 * C * KS;     // [2][C][KS]
+    float* qs = reinterpret_cast<float*>(vbuf + 2 * C * KS);
     float* S = qs + R * D;
-    // the MMAs' A fragments, made once per CTA (every warp uses the same ones):
-    // per 16-column step and lane, the four f16x2 registers of hi then of lo
+    // the MMAs' A fragments (every warp uses the same ones): per 16-column step and
+    // lane, the four f16x2 registers of hi then of lo
     uint4* qa = reinterpret_cast<uint4*>(S + R * C);  // [D / 16][32][2]
     uint4* pa = qa + (D / 16) * 64;                   // [C / 16][32][2]
-    const int64_t base = (((int64_t)seq[t] * HK + hk) * n_ctx + start) * D;
-    // the chunk's rows copied asynchronously, all in flight at once, while the queries load
+    const int64_t sbase = ((int64_t)seq[t] * HK + hk) * n_ctx;
+    // chunk c's rows into buffer b, copied asynchronously (one commit group per
+    // chunk and thread); rows past the query's position are zeroed
     constexpr int pieces = D / 8;
-    for (int i = threadIdx.x; i < nv * pieces; i += blockDim.x) {
-        const int row = i / pieces, pc = i % pieces;
-        cp_async16(ks + row * KS + pc * 16, kc + base + (int64_t)row * D + pc * 8);
-        cp_async16(vs + row * KS + pc * 16, vc + base + (int64_t)row * D + pc * 8);
-    }
-    for (int i = threadIdx.x; i < (C - nv) * pieces; i += blockDim.x) {
-        const int row = nv + i / pieces, pc = i % pieces;
-        *reinterpret_cast<uint4*>(ks + row * KS + pc * 16) = make_uint4(0u, 0u, 0u, 0u);
-        *reinterpret_cast<uint4*>(vs + row * KS + pc * 16) = make_uint4(0u, 0u, 0u, 0u);
-    }
+    auto stage = [&](int c, int b) {
+        const int nvc = (int)min((int64_t)C, qp - (int64_t)c * C + 1);
+        const int64_t base = (sbase + (int64_t)c * C) * D;
+        uint8_t* ks = kbuf + b * C * KS;
+        uint8_t* vs = vbuf + b * C * KS;
+        for (int i = threadIdx.x; i < nvc * pieces; i += blockDim.x) {
+            const int row = i / pieces, pc = i % pieces;
+            cp_async16(ks + row * KS + pc * 16, kc + base + (int64_t)row * D + pc * 8);
+            cp_async16(vs + row * KS + pc * 16, vc + base + (int64_t)row * D + pc * 8);
+        }
+        for (int i = threadIdx.x; i < (C - nvc) * pieces; i += blockDim.x) {
+            const int row = nvc + i / pieces, pc = i % pieces;
+            *reinterpret_cast<uint4*>(ks + row * KS + pc * 16) = make_uint4(0u, 0u, 0u, 0u);
+            *reinterpret_cast<uint4*>(vs + row * KS + pc * 16) = make_uint4(0u, 0u, 0u, 0u);
+        }
+        cp_async_commit();
+    };
+    stage(c0, 0);
     for (int i = threadIdx.x; i < R * D; i += blockDim.x)
         qs[i] = qkv[(int64_t)t * ld + (int64_t)(hk * R) * D + i];
-    cp_async_wait_all();
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, tq = lane & 3;  // the MMA fragments' row group and column pair
     for (int kk = warp; kk < D / 16; kk += 8) make_a_frag(qs, D, R, kk * 16, lane, qa + (kk * 32 + lane) * 2);
     __syncthreads();
+    // heads of up to 128 values keep the query fragments in registers for every chunk
+    // (a warp reads them from shared memory once instead of once per chunk)
+    constexpr bool kQReg = NV <= 4;
+    uint4 qf[kQReg ? D / 16 : 1][2];
+    if constexpr (kQReg) {
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+            qf[kk][0] = qa[(kk * 32 + lane) * 2];
+            qf[kk][1] = qa[(kk * 32 + lane) * 2 + 1];
+        }
+    }
+    for (int c = c0; c < c1; ++c) {
+    const int cb = (c - c0) & 1;
+    if (c + 1 < c1) {
+        stage(c + 1, cb ^ 1);  // the other buffer's chunk was finished before the last barrier
+        cp_async_wait_group<1>();
+    } else {
+        cp_async_wait_group<0>();
+    }
+    __syncthreads();
+    const uint8_t* ks = kbuf + cb * C * KS;
+    const uint8_t* vs = vbuf + cb * C * KS;
+    const int nv = (int)min((int64_t)C, qp - (int64_t)c * C + 1);
     // scores on the tensor cores: S (query heads x positions) = Q K^T with Q split
     // into f16 hi + lo parts (two MMAs per 16 dims, f32 accumulation; K is f16 as
     // cached); warp w takes positions 8w .. 8w + 7, heads beyond R are zero rows
@@ -562,14 +599,21 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
         // lane i addresses position 8 warp + i % 8, dims 32 kp + 8 (i / 8): two k-steps per load
         const uint8_t* kr = ks + (8 * warp + (lane & 7)) * KS + (lane >> 3) * 16;
         const bool r0 = g < R, r1 = g + 8 < R;
-#pragma unroll 2
+#pragma unroll
         for (int kp = 0; kp < D / 32; ++kp) {
             uint32_t b[4];
             ldsm_x4<false>(b, kr + kp * 64);
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int kk = 2 * kp + h;
-                const uint4 fh = qa[(kk * 32 + lane) * 2], fl = qa[(kk * 32 + lane) * 2 + 1];
+                uint4 fh, fl;
+                if constexpr (kQReg) {
+                    fh = qf[kk][0];
+                    fl = qf[kk][1];
+                } else {
+                    fh = qa[(kk * 32 + lane) * 2];
+                    fl = qa[(kk * 32 + lane) * 2 + 1];
+                }
                 const uint32_t ah[4] = {fh.x, fh.y, fh.z, fh.w}, al[4] = {fl.x, fl.y, fl.z, fl.w};
                 mma_f16(acc, ah, b[2 * h], b[2 * h + 1]);
                 mma_f16(acc, al, b[2 * h], b[2 * h + 1]);
@@ -607,34 +651,53 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
     // P V on the tensor cores: (heads x dims) = P (heads x positions, f16 hi + lo)
     // times V (positions x dims, f16); warp w takes dims 8 nt .. 8 nt + 7 for
     // nt = w, w + 8, ...; positions past nv have P = 0 and zeroed V rows
-    for (int nt = warp; nt < D / 8; nt += 8) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    {
+        // warp w takes the D / 64 tiles of 8 dims nt = w, w + 8, ..., all in one pass
+        // over the P fragments (read once per warp)
+        constexpr int NT = D / 64;
+        float acc[NT][4];
+#pragma unroll
+        for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
         const bool r0 = g < R, r1 = g + 8 < R;
 #pragma unroll
         for (int kp = 0; kp < C / 32; ++kp) {
-            // lane i addresses position 32 kp + i, dims 8 nt .. 8 nt + 7 (transposed: two k-steps)
-            uint32_t b[4];
-            ldsm_x4<true>(b, vs + (kp * 32 + lane) * KS + nt * 16);
+            uint4 fh[2], fl[2];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
-                const int kk = 2 * kp + h;
-                const uint4 fh = pa[(kk * 32 + lane) * 2], fl = pa[(kk * 32 + lane) * 2 + 1];
-                const uint32_t ah[4] = {fh.x, fh.y, fh.z, fh.w}, al[4] = {fl.x, fl.y, fl.z, fl.w};
-                mma_f16(acc, ah, b[2 * h], b[2 * h + 1]);
-                mma_f16(acc, al, b[2 * h], b[2 * h + 1]);
+                fh[h] = pa[((2 * kp + h) * 32 + lane) * 2];
+                fl[h] = pa[((2 * kp + h) * 32 + lane) * 2 + 1];
+            }
+#pragma unroll
+            for (int i = 0; i < NT; ++i) {
+                const int nt = warp + 8 * i;
+                // lane l addresses position 32 kp + l, dims 8 nt .. 8 nt + 7 (transposed: two k-steps)
+                uint32_t b[4];
+                ldsm_x4<true>(b, vs + (kp * 32 + lane) * KS + nt * 16);
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const uint32_t ah[4] = {fh[h].x, fh[h].y, fh[h].z, fh[h].w};
+                    const uint32_t al[4] = {fl[h].x, fl[h].y, fl[h].z, fl[h].w};
+                    mma_f16(acc[i], ah, b[2 * h], b[2 * h + 1]);
+                    mma_f16(acc[i], al, b[2 * h], b[2 * h + 1]);
+                }
             }
         }
-        const int col = 4 + nt * 8 + 2 * tq;
-        if (r0) {
-            float* op = outp + (int64_t)g * n_chunk * (D + 4);
-            op[col] = acc[0];
-            op[col + 1] = acc[1];
+#pragma unroll
+        for (int i = 0; i < NT; ++i) {
+            const int col = 4 + (warp + 8 * i) * 8 + 2 * tq;
+            if (r0) {
+                float* op = outp + (int64_t)g * n_chunk * (D + 4);
+                op[col] = acc[i][0];
+                op[col + 1] = acc[i][1];
+            }
+            if (r1) {
+                float* op = outp + (int64_t)(g + 8) * n_chunk * (D + 4);
+                op[col] = acc[i][2];
+                op[col + 1] = acc[i][3];
+            }
         }
-        if (r1) {
-            float* op = outp + (int64_t)(g + 8) * n_chunk * (D + 4);
-            op[col] = acc[2];
-            op[col + 1] = acc[3];
-        }
+    }
+    __syncthreads();  // the buffers, the scores and the P fragments are reused by the next chunk
     }
 }
 
@@ -747,8 +810,8 @@ cudaError_t gemv_dense(const QMat& W, const QInput& in, const QFrag& fr, int T, 
 
 template <int NV>
 size_t attn_smem(int R) {
-    // K and V rows, the queries, the scores, the A fragments of Q and of P
-    return (size_t)2 * kAttnChunk * (NV * 64 + 16) + (size_t)R * NV * 32 * 4 + (size_t)R * kAttnChunk * 4 +
+    // two buffers of K and V rows, the queries, the scores, the A fragments of Q and of P
+    return (size_t)4 * kAttnChunk * (NV * 64 + 16) + (size_t)R * NV * 32 * 4 + (size_t)R * kAttnChunk * 4 +
            (size_t)(NV * 2) * 32 * 32 + (size_t)(kAttnChunk / 16) * 32 * 32;
 }
 
@@ -769,8 +832,11 @@ cudaError_t attention_nv(float* qkv, int ld, int T, int H, int HK, const float* 
         smem_set = smem;
     }
     const float scale = 1.0f / std::sqrt((float)(NV * 32));
-    attn_partial_kernel<NV><<<dim3((unsigned)n_chunk, (unsigned)(T * HK)), 256, smem, s>>>(
-        qkv, ld, H, HK, kc, vc, n_ctx, pos, seq, scale, part, n_chunk);
+    // chunks per CTA: enough CTAs for about two rounds of two per SM, at most 8 chunks each
+    const int n_sm = 148;
+    const int nch = std::max(1, std::min(8, (int)(((int64_t)n_chunk * T * HK) / (4 * n_sm))));
+    attn_partial_kernel<NV><<<dim3((unsigned)((n_chunk + nch - 1) / nch), (unsigned)(T * HK)), 256, smem, s>>>(
+        qkv, ld, H, HK, kc, vc, n_ctx, pos, seq, scale, part, n_chunk, nch);
     attn_combine_kernel<<<(unsigned)(T * H), 128, 0, s>>>(part, H, NV * 32, n_chunk, pos, att, aq, af);
     return cudaGetLastError();
 }
