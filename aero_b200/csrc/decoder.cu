@@ -539,6 +539,11 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
     // lane, the four f16x2 registers of hi then of lo
     uint4* qa = reinterpret_cast<uint4*>(S + R * C);  // [D / 16][32][2]
     uint4* pa = qa + (D / 16) * 64;                   // [C / 16][32][2]
+    // running max and sum of each head over the CTA's chunks, and the chunk's
+    // rescale factors (old sums, this chunk's) for the accumulators
+    float* mrun = reinterpret_cast<float*>(pa + (C / 16) * 64);  // [R]
+    float* lrun = mrun + kMaxGroup;                              // [R]
+    float2* fac = reinterpret_cast<float2*>(lrun + kMaxGroup);   // [R]
     const int64_t sbase = ((int64_t)seq[t] * HK + hk) * n_ctx;
     // chunk c's rows into buffer b, copied asynchronously (one commit group per
     // chunk and thread); rows past the query's position are zeroed
@@ -563,6 +568,10 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
     stage(c0, 0);
     for (int i = threadIdx.x; i < R * D; i += blockDim.x)
         qs[i] = qkv[(int64_t)t * ld + (int64_t)(hk * R) * D + i];
+    if (threadIdx.x < R) {
+        mrun[threadIdx.x] = -INFINITY;
+        lrun[threadIdx.x] = 0.f;
+    }
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, tq = lane & 3;  // the MMA fragments' row group and column pair
@@ -579,6 +588,11 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
             qf[kk][1] = qa[(kk * 32 + lane) * 2 + 1];
         }
     }
+    // the P V accumulators of this thread's tiles (heads g, g + 8), merged over the chunks
+    constexpr int NT = D / 64;
+    float accr[NT][4];
+#pragma unroll
+    for (int i = 0; i < NT; ++i) accr[i][0] = accr[i][1] = accr[i][2] = accr[i][3] = 0.f;
     for (int c = c0; c < c1; ++c) {
     const int cb = (c - c0) & 1;
     if (c + 1 < c1) {
@@ -630,7 +644,6 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
         }
     }
     __syncthreads();
-    float* outp = part + (((int64_t)t * H + (int64_t)hk * R) * n_chunk + c) * (D + 4);
     for (int r = warp; r < R; r += 8) {
         const float s0 = S[r * C + lane], s1 = S[r * C + lane + 32];
         const float m = warp_max(fmaxf(s0, s1));  // finite: position start is always kept
@@ -640,9 +653,13 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
         S[r * C + lane + 32] = p1;
         const float l = warp_sum(p0 + p1);
         if (lane == 0) {
-            float* op = outp + (int64_t)r * n_chunk * (D + 4);
-            op[0] = m;
-            op[1] = l;
+            // online merge with the CTA's earlier chunks (src/transformer.cpp:120-205
+            // merges its 1024-position blocks the same way)
+            const float mo = mrun[r], mn = fmaxf(mo, m);
+            const float alpha = expf(mo - mn), beta = expf(m - mn);
+            lrun[r] = alpha * lrun[r] + beta * l;
+            mrun[r] = mn;
+            fac[r] = make_float2(alpha, beta);
         }
     }
     __syncthreads();
@@ -654,7 +671,6 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
     {
         // warp w takes the D / 64 tiles of 8 dims nt = w, w + 8, ..., all in one pass
         // over the P fragments (read once per warp)
-        constexpr int NT = D / 64;
         float acc[NT][4];
 #pragma unroll
         for (int i = 0; i < NT; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
@@ -682,22 +698,38 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
                 }
             }
         }
+        const float2 fa = r0 ? fac[g] : make_float2(0.f, 0.f), fb = r1 ? fac[g + 8] : make_float2(0.f, 0.f);
 #pragma unroll
         for (int i = 0; i < NT; ++i) {
-            const int col = 4 + (warp + 8 * i) * 8 + 2 * tq;
-            if (r0) {
-                float* op = outp + (int64_t)g * n_chunk * (D + 4);
-                op[col] = acc[i][0];
-                op[col + 1] = acc[i][1];
-            }
-            if (r1) {
-                float* op = outp + (int64_t)(g + 8) * n_chunk * (D + 4);
-                op[col] = acc[i][2];
-                op[col + 1] = acc[i][3];
-            }
+            accr[i][0] = fmaf(fa.x, accr[i][0], fa.y * acc[i][0]);
+            accr[i][1] = fmaf(fa.x, accr[i][1], fa.y * acc[i][1]);
+            accr[i][2] = fmaf(fb.x, accr[i][2], fb.y * acc[i][2]);
+            accr[i][3] = fmaf(fb.x, accr[i][3], fb.y * acc[i][3]);
         }
     }
-    __syncthreads();  // the buffers, the scores and the P fragments are reused by the next chunk
+    __syncthreads();  // the buffers, the scores, the P fragments and the factors are reused
+    }
+    // the CTA's merged partial: part[t][h][blockIdx.x] = (m, l, -, -, acc[D])
+    const bool r0 = g < R, r1 = g + 8 < R;
+    float* outp = part + (((int64_t)t * H + (int64_t)hk * R) * n_chunk + blockIdx.x) * (D + 4);
+    if (threadIdx.x < R) {
+        float* op = outp + (int64_t)threadIdx.x * n_chunk * (D + 4);
+        op[0] = mrun[threadIdx.x];
+        op[1] = lrun[threadIdx.x];
+    }
+#pragma unroll
+    for (int i = 0; i < NT; ++i) {
+        const int col = 4 + (warp + 8 * i) * 8 + 2 * tq;
+        if (r0) {
+            float* op = outp + (int64_t)g * n_chunk * (D + 4);
+            op[col] = accr[i][0];
+            op[col + 1] = accr[i][1];
+        }
+        if (r1) {
+            float* op = outp + (int64_t)(g + 8) * n_chunk * (D + 4);
+            op[col] = accr[i][2];
+            op[col + 1] = accr[i][3];
+        }
     }
 }
 
@@ -706,14 +738,14 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
 // sum); then warp w adds the acc rows of chunks w, w + 4, ... (float4 per lane)
 // and the four warps' sums meet in shared memory.
 __global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restrict__ part, int H, int D, int n_chunk,
-                                                           const int64_t* __restrict__ pos, float* __restrict__ att,
-                                                           QInput aq, QFrag af) {
+                                                           int nch, const int64_t* __restrict__ pos,
+                                                           float* __restrict__ att, QInput aq, QFrag af) {
     __shared__ float ew[1024];  // e^(m_c - M), chunk c (n_chunk <= 1024)
     __shared__ float red[4];
     __shared__ float4 accs[4][64];
     const int t = (int)blockIdx.x / H, h = (int)blockIdx.x % H;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int nc = (int)(pos[t] / kAttnChunk) + 1;
+    const int nc = (int)(pos[t] / kAttnChunk) / nch + 1;  // the partials: one per group of nch chunks
     const float* pb = part + ((int64_t)t * H + h) * n_chunk * (D + 4);
     float m = -INFINITY;
     for (int c = threadIdx.x; c < nc; c += 128) m = fmaxf(m, pb[(int64_t)c * (D + 4)]);
@@ -810,9 +842,10 @@ cudaError_t gemv_dense(const QMat& W, const QInput& in, const QFrag& fr, int T, 
 
 template <int NV>
 size_t attn_smem(int R) {
-    // two buffers of K and V rows, the queries, the scores, the A fragments of Q and of P
+    // two buffers of K and V rows, the queries, the scores, the A fragments of Q and of
+    // P, the running max / sum and rescale factors of the heads
     return (size_t)4 * kAttnChunk * (NV * 64 + 16) + (size_t)R * NV * 32 * 4 + (size_t)R * kAttnChunk * 4 +
-           (size_t)(NV * 2) * 32 * 32 + (size_t)(kAttnChunk / 16) * 32 * 32;
+           (size_t)(NV * 2) * 32 * 32 + (size_t)(kAttnChunk / 16) * 32 * 32 + (size_t)kMaxGroup * 16;
 }
 
 template <int NV>
@@ -837,7 +870,7 @@ cudaError_t attention_nv(float* qkv, int ld, int T, int H, int HK, const float* 
     const int nch = std::max(1, std::min(8, (int)(((int64_t)n_chunk * T * HK) / (4 * n_sm))));
     attn_partial_kernel<NV><<<dim3((unsigned)((n_chunk + nch - 1) / nch), (unsigned)(T * HK)), 256, smem, s>>>(
         qkv, ld, H, HK, kc, vc, n_ctx, pos, seq, scale, part, n_chunk, nch);
-    attn_combine_kernel<<<(unsigned)(T * H), 128, 0, s>>>(part, H, NV * 32, n_chunk, pos, att, aq, af);
+    attn_combine_kernel<<<(unsigned)(T * H), 128, 0, s>>>(part, H, NV * 32, n_chunk, nch, pos, att, aq, af);
     return cudaGetLastError();
 }
 

@@ -198,3 +198,44 @@ def test_decoder_batched_steps_match_single_steps_at_full_width():
     finally:
         B.close()
         S.close()
+
+
+class _Dev:
+    """A device buffer (address, shape, numpy type string) for torch.as_tensor."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"data": (ptr, False), "shape": tuple(shape), "typestr": typestr, "version": 3}
+
+
+def test_decoder_long_cache_merged_chunks_match_single_steps():
+    """Over a 2048-position cache (the same N(0, 1) f16 keys and values in two
+    decoders), a step of 16 sequences at position 1900 (attention CTAs merge several
+    64-position chunks online before the combine) gives the logits of the same
+    tokens stepped one at a time (one chunk per CTA), within the decode bar."""
+    torch = pytest.importorskip("torch")
+    spec = synth.DecoderSpec(1, 2048, 32, 4, 128, 2048, synth.LayerSpec(2048, 8, 2, 256, 0, synth.DTYPE_Q4_K))
+    dec = synth.make_decoder(spec, 9, device_gen=True)
+    n_ctx, p = 2048, 1900
+    B = CudaDecoder.from_synth(dec, n_seq=16, n_ctx=n_ctx)
+    S = CudaDecoder.from_synth(dec, n_seq=16, n_ctx=n_ctx)
+    try:
+        g = torch.Generator(device="cuda").manual_seed(3)
+        shape = (16, spec.n_kv, n_ctx, spec.head_dim)
+        for li in range(spec.n_layer):
+            for pb, ps in zip(B.kv(li), S.kv(li)):
+                vals = torch.randn(shape, generator=g, device="cuda").half()
+                torch.as_tensor(_Dev(pb, shape, "<f2"), device="cuda").copy_(vals)
+                torch.as_tensor(_Dev(ps, shape, "<f2"), device="cuda").copy_(vals)
+        torch.cuda.synchronize()
+        tok = np.random.default_rng(4).integers(0, spec.vocab, 16)
+        batched = B.step(tok, np.arange(16), np.full(16, p))
+        errs = []
+        for sq in range(16):
+            one = S.step(tok[sq:sq + 1], [sq], [p])[0]
+            e = rel(batched[sq], one)
+            errs.append(e)
+            assert e <= TOL, (sq, e)
+        print(f"long cache, merged chunks vs single steps: max logit error / RMS {max(errs):.2e}")
+    finally:
+        B.close()
+        S.close()
