@@ -733,29 +733,35 @@ __global__ void __launch_bounds__(256) attn_partial_kernel(const float* __restri
     }
 }
 
-// CTA = (token, head), 128 threads: out = sum_c e^(m_c - M) acc_c / sum_c e^(m_c - M) l_c.
-// The chunks' (m, l) are read in parallel (one chunk per thread, block max and
-// sum); then warp w adds the acc rows of chunks w, w + 4, ... (float4 per lane)
-// and the four warps' sums meet in shared memory.
-__global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restrict__ part, int H, int D, int n_chunk,
-                                                           int nch, const int64_t* __restrict__ pos,
-                                                           float* __restrict__ att, QInput aq, QFrag af) {
-    __shared__ float ew[1024];  // e^(m_c - M), chunk c (n_chunk <= 1024)
-    __shared__ float red[4];
-    __shared__ float4 accs[4][64];
+// CTA = (token, head), kCombThreads threads: out = sum_c e^(m_c - M) acc_c / sum_c e^(m_c - M) l_c
+// over the head's partials c (one per group of nch chunks). The partials' (m, l) are read
+// in parallel (one partial per thread, block max and sum); then warp w adds the acc
+// rows of partials w, w + kCombWarps, ... (float4 per lane) and the warps' sums meet in
+// shared memory.
+constexpr int kCombWarps = 8;
+constexpr int kCombThreads = 32 * kCombWarps;
+__global__ void __launch_bounds__(kCombThreads) attn_combine_kernel(const float* __restrict__ part, int H, int D,
+                                                                    int n_chunk, int nch,
+                                                                    const int64_t* __restrict__ pos,
+                                                                    float* __restrict__ att, QInput aq, QFrag af) {
+    __shared__ float ew[1024];  // e^(m_c - M), partial c (n_chunk <= 1024)
+    __shared__ float red[kCombWarps];
+    __shared__ float4 accs[kCombWarps][64];
     const int t = (int)blockIdx.x / H, h = (int)blockIdx.x % H;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int nc = (int)(pos[t] / kAttnChunk) / nch + 1;  // the partials: one per group of nch chunks
     const float* pb = part + ((int64_t)t * H + h) * n_chunk * (D + 4);
     float m = -INFINITY;
-    for (int c = threadIdx.x; c < nc; c += 128) m = fmaxf(m, pb[(int64_t)c * (D + 4)]);
+    for (int c = threadIdx.x; c < nc; c += kCombThreads) m = fmaxf(m, pb[(int64_t)c * (D + 4)]);
     m = warp_max(m);
     if (lane == 0) red[warp] = m;
     __syncthreads();
-    const float M = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    float M = red[0];
+#pragma unroll
+    for (int w = 1; w < kCombWarps; ++w) M = fmaxf(M, red[w]);
     __syncthreads();
     float L = 0.f;
-    for (int c = threadIdx.x; c < nc; c += 128) {
+    for (int c = threadIdx.x; c < nc; c += kCombThreads) {
         const float e = expf(pb[(int64_t)c * (D + 4)] - M);
         ew[c] = e;
         L = fmaf(e, pb[(int64_t)c * (D + 4) + 1], L);
@@ -763,12 +769,14 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restri
     L = warp_sum(L);
     if (lane == 0) red[warp] = L;
     __syncthreads();
-    const float Ls = red[0] + red[1] + red[2] + red[3];
+    float Ls = 0.f;
+#pragma unroll
+    for (int w = 0; w < kCombWarps; ++w) Ls += red[w];
     const int nq = D / 4;  // float4 per acc row (<= 64)
     float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int q = lane; q < nq; q += 32) {
         a = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int c = warp; c < nc; c += 4) {
+        for (int c = warp; c < nc; c += kCombWarps) {
             const float e = ew[c];
             const float4 v = *reinterpret_cast<const float4*>(pb + (int64_t)c * (D + 4) + 4 + 4 * q);
             a.x = fmaf(e, v.x, a.x);
@@ -780,13 +788,14 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const float* __restri
     }
     __syncthreads();
     const float inv = 1.0f / fmaxf(Ls, 1e-30f);
-    for (int q = threadIdx.x; q < nq; q += 128) {
-        const float4 a0 = accs[0][q], a1 = accs[1][q], a2 = accs[2][q], a3 = accs[3][q];
-        float4 o;
-        o.x = (a0.x + a1.x + a2.x + a3.x) * inv;
-        o.y = (a0.y + a1.y + a2.y + a3.y) * inv;
-        o.z = (a0.z + a1.z + a2.z + a3.z) * inv;
-        o.w = (a0.w + a1.w + a2.w + a3.w) * inv;
+    for (int q = threadIdx.x; q < nq; q += kCombThreads) {
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < kCombWarps; ++w) {
+            const float4 aw = accs[w][q];
+            o.x += aw.x, o.y += aw.y, o.z += aw.z, o.w += aw.w;
+        }
+        o.x *= inv, o.y *= inv, o.z *= inv, o.w *= inv;
         *reinterpret_cast<float4*>(att + ((int64_t)t * H + h) * D + 4 * q) = o;
         accs[0][q] = o;
     }
@@ -870,7 +879,7 @@ cudaError_t attention_nv(float* qkv, int ld, int T, int H, int HK, const float* 
     const int nch = std::max(1, std::min(8, (int)(((int64_t)n_chunk * T * HK) / (4 * n_sm))));
     attn_partial_kernel<NV><<<dim3((unsigned)((n_chunk + nch - 1) / nch), (unsigned)(T * HK)), 256, smem, s>>>(
         qkv, ld, H, HK, kc, vc, n_ctx, pos, seq, scale, part, n_chunk, nch);
-    attn_combine_kernel<<<(unsigned)(T * H), 128, 0, s>>>(part, H, NV * 32, n_chunk, nch, pos, att, aq, af);
+    attn_combine_kernel<<<(unsigned)(T * H), kCombThreads, 0, s>>>(part, H, NV * 32, n_chunk, nch, pos, att, aq, af);
     return cudaGetLastError();
 }
 
