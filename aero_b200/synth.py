@@ -217,7 +217,12 @@ def attach_zipf(layer: SynthLayer, x: np.ndarray, s: float, seed: int = 0) -> Sy
     base = x @ layer.router.T
     bias, tau, loads = zipf_bias(base, layer.spec.k, s, seed)
     layer.router_bias = bias
+    E, k = layer.spec.E, layer.spec.k
+    # the Zipf(s) head share 1 / H(E, s) against top-k's cap: a token picks an expert at
+    # most once, so no expert can take more than 1 / k of the assignments
+    zipf_top = float(1.0 / np.sum(np.arange(1, E + 1, dtype=np.float64) ** -s))
     layer.meta.update({"zipf_s": s, "zipf_tau": tau, "top_load_share": float(loads.max() / loads.sum()),
+                       "zipf_top_share": zipf_top, "top_share_cap": 1.0 / k, "load_slope": float(_slope(loads)),
                        "max_load": int(loads.max()), "min_load": int(loads.min())})
     return layer
 

@@ -625,6 +625,8 @@ def run_ours(args, ws, rank, dev, cuda, wl, spec, T, seed, clk):
         else:
             result["ep_phases_ms"] = {k: round(v / max(moe.phase_n, 1), 5) for k, v in moe.phase_ms.items()}
         moe.set_profiling(False)
+    if ws == 1 and not args.no_decode and wl.name == synth.CONFIGS["c5"].name:
+        result["zipf"] = zipf_record(args, dev, stream)
     if ws == 1 and not args.no_decode and not wl.name.startswith(("c1", "c3", "c4")):
         result["decode"] = decode_records(args, dev, stream, pk)
     if ws == 1 and not args.no_decoder and not wl.name.startswith(("c1", "c3", "c4")):
@@ -646,6 +648,47 @@ def run_ours(args, ws, rank, dev, cuda, wl, spec, T, seed, clk):
     if ws > 1:
         torch.distributed.barrier()
         torch.distributed.destroy_process_group()
+
+
+def zipf_record(args, dev, stream) -> dict:
+    """Config 5 with Zipf(s = 1.2)-skewed routing (workload c5z) at N = 1, timed like
+    the headline line (device-resident inputs, CUDA events over `args.steps` steps),
+    with the calibration of its router bias: tau, the measured top-expert share and
+    load-curve slope, and the Zipf head share against top-k's 1 / k cap."""
+    import torch
+    from aero_b200 import native_cuda as nc
+    from aero_b200 import synth
+
+    lib = nc.lib()
+    wl = synth.CONFIGS["c5z"]
+    spec, T = wl.spec, wl.T
+    x_host = synth.make_x(T, spec.d, 0, bf16=wl.bf16_x)
+    layer = synth.make_layer(spec, 0, device_gen=True)
+    synth.attach_zipf(layer, x_host, wl.zipf_s, 0)
+    L = synth.open_layer(layer, device=dev)
+    L.set_stream(stream)
+    x = torch.from_numpy(x_host).to(f"cuda:{dev}")
+    o = torch.empty_like(x)
+
+    def step():
+        if lib.aero_cuda_moe_forward(L.handle, 0, x.data_ptr(), T, spec.d, o.data_ptr()) != 1:
+            raise RuntimeError(nc.last_error(L.handle))
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            step()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            step()
+        e1.record(stream)
+    e1.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    L.close()
+    m = layer.meta
+    return {"workload": wl.name, "tokens_per_step": T, "ms_per_step": ms, "tokens_per_s": T / (ms / 1000.0),
+            "routing": {k: m[k] for k in ("zipf_s", "zipf_tau", "top_load_share", "zipf_top_share", "top_share_cap",
+                                          "load_slope", "max_load", "min_load")}}
 
 
 def decode_records(args, dev, stream, pk) -> dict:
