@@ -188,6 +188,13 @@ def test_zipf_calibration():
     loads = np.bincount(np.argsort(-lg, axis=1)[:, :4].reshape(-1), minlength=64)
     assert abs(synth._slope(loads) + 1.1) < 0.05
     assert loads.max() > 3 * np.median(loads)
+    # the recorded calibration: the measured head share stays under top-k's 1/k cap, which
+    # the Zipf(1.1) head share over 64 experts exceeds (the reason the slope is matched)
+    m = layer.meta
+    assert m["top_share_cap"] == 1 / 4
+    assert abs(m["zipf_top_share"] - 1 / np.sum(np.arange(1, 65, dtype=np.float64) ** -1.1)) < 1e-12
+    assert m["top_load_share"] <= m["top_share_cap"] < m["zipf_top_share"]
+    assert abs(m["load_slope"] + 1.1) < 0.05
 
 
 def test_bf16_inputs_representable():
