@@ -429,6 +429,32 @@ __global__ void __launch_bounds__(256) dense_mma_q8_kernel(QMat W, QFrag in, int
     }
 }
 
+// One token over rows of up to two passes (32 x gemv_cpl chunks each): a CTA takes 4
+// rows, two warps per row, each with its half's input in registers and its half of the
+// row; the halves are added in order (first, then second) in shared memory.
+template <int DT>
+__global__ void __launch_bounds__(256) dense_gemv_split_kernel(QMat W, QInput in, float* __restrict__ y) {
+    constexpr int CPL = gemv_cpl<DT>(), LPR = 32;
+    __shared__ float part[8];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int nch = Layout<DT>::chunks(W.cols);
+    const int r = (int)blockIdx.x * 4 + (warp >> 1), base = (warp & 1) * LPR * CPL;
+    float v = 0.f;
+    if (r < W.rows) {
+        LaneInput<DT, CPL> xin;
+        input_load<DT, LPR, CPL>(nullptr, in, 0, lane, nch, xin, base);
+        RowRaw<DT, CPL> w{};
+        row_load<DT, LPR, CPL>(W, 0, r, lane, nch, w, base);
+        v = warp_sum(row_dot<DT, LPR, CPL>(w, xin, lane, nch, base));
+    }
+    if (lane == 0) part[warp] = v;
+    __syncthreads();
+    if (threadIdx.x < 4) {
+        const int rr = (int)blockIdx.x * 4 + (int)threadIdx.x;
+        if (rr < W.rows) y[rr] = part[2 * threadIdx.x] + part[2 * threadIdx.x + 1];
+    }
+}
+
 // ---------------------------------------------------- q/k norm, RoPE, cache
 // One warp per (token, head j) of the step's q|k|v rows (j < H: query head,
 // then H_kv key heads, then H_kv value heads); lane l holds values i * 32 + l,
@@ -832,6 +858,10 @@ cudaError_t gemv_dense_dt(const QMat& W, const QInput& in, const QFrag& fr, int 
             dense_mma_q8_kernel<1><<<mg, 256, 0, s>>>(W, fr, T, y, ldy);
         else
             dense_mma_q8_kernel<2><<<mg, 256, 0, s>>>(W, fr, T, y, ldy);
+        return cudaGetLastError();
+    }
+    if (T == 1 && nch > 32 * gemv_cpl<DT>() && nch <= 64 * gemv_cpl<DT>()) {
+        dense_gemv_split_kernel<DT><<<(unsigned)((W.rows + 3) / 4), 256, 0, s>>>(W, in, y);
         return cudaGetLastError();
     }
     if (T == 1 && nch <= 32 * gemv_cpl<DT>())
