@@ -172,13 +172,16 @@ def test_decoder_open_charges_exactly_its_plan(golden, tmp_path):
     assert held() == before
 
 
-def test_decoder_batched_steps_match_single_steps_at_full_width():
-    """At the config-4 widths (d 2048, 32 x 128 query heads, 4 kv heads; Q8_0
-    projections and head, Q4_K experts), steps of 16 sequences at once (the dense
-    projections and head on the integer tensor-core kernel) give the logits of the
-    same tokens run one at a time (the single-token CUDA-core kernels), within the
-    decode bar of their RMS; every argmax equal."""
-    spec = synth.DecoderSpec(2, 2048, 32, 4, 128, 4096, synth.LayerSpec(2048, 16, 4, 768, 0, synth.DTYPE_Q4_K))
+@pytest.mark.parametrize("attn_dtype", [synth.DTYPE_Q8_0, synth.DTYPE_Q4_K])
+def test_decoder_batched_steps_match_single_steps_at_full_width(attn_dtype):
+    """At the config-4 widths (d 2048, 32 x 128 query heads, 4 kv heads; Q8_0 head,
+    Q4_K experts, Q8_0 or Q4_K projections), steps of 16 sequences at once (Q8_0: the
+    dense projections and head on the integer tensor-core kernel; Q4_K projections:
+    the multi-token CUDA-core kernel) give the logits of the same tokens run one at a
+    time (the single-token kernels, the 4096-wide output projection split over two
+    warps per row), within the decode bar of their RMS; every argmax equal."""
+    spec = synth.DecoderSpec(2, 2048, 32, 4, 128, 4096, synth.LayerSpec(2048, 16, 4, 768, 0, synth.DTYPE_Q4_K),
+                             attn_dtype=attn_dtype)
     dec = synth.make_decoder(spec, 5, device_gen=True)
     B = CudaDecoder.from_synth(dec, n_seq=16, n_ctx=32)
     S = CudaDecoder.from_synth(dec, n_seq=16, n_ctx=32)
