@@ -750,16 +750,41 @@ __global__ void __launch_bounds__(kDecThreads, 2) decode_kernel(DecodeArgs a) {
         __syncthreads();
     }
     const int U = n_units_s;
-    // chunks per unit: input rows x blocks x (G / 4)
-    for (int u = threadIdx.x; u < U; u += kDecThreads) {
+    // chunks per unit: input rows x blocks x (G / 4), and their exclusive prefixes (one
+    // warp's shuffle scan for up to 32 units, a block scan above)
+    auto unit_chunks = [&](int u, int& gu, int& dn) {
         const bool sh = S.u_e[u] < 0;
         const int Fu = sh ? a.Fs : a.F;
-        S.gu_pre[u] = S.u_n[u] * (Fu / kJBlock) * (pow2_at_least(a.dp / 64) / kChunk);
-        S.dn_pre[u] = S.u_n[u] * (a.dp / 32) * (pow2_at_least(Fu / 64) / kChunk);
+        gu = S.u_n[u] * (Fu / kJBlock) * (pow2_at_least(a.dp / 64) / kChunk);
+        dn = S.u_n[u] * (a.dp / 32) * (pow2_at_least(Fu / 64) / kChunk);
+    };
+    __shared__ int tot_s[2];
+    int n_gu, n_dn;
+    if (U <= 32) {
+        if (warp == 0) {
+            int gu = 0, dn = 0;
+            if (lane < U) unit_chunks(lane, gu, dn);
+            int ig = gu, id = dn;  // inclusive prefixes
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int tg = __shfl_up_sync(0xffffffffu, ig, o), td = __shfl_up_sync(0xffffffffu, id, o);
+                if (lane >= o) ig += tg, id += td;
+            }
+            if (lane < U) {
+                S.gu_pre[lane] = ig - gu;
+                S.dn_pre[lane] = id - dn;
+            }
+            if (lane == 31) tot_s[0] = ig, tot_s[1] = id;
+        }
+        __syncthreads();
+        n_gu = tot_s[0];
+        n_dn = tot_s[1];
+    } else {
+        for (int u = threadIdx.x; u < U; u += kDecThreads) unit_chunks(u, S.gu_pre[u], S.dn_pre[u]);
+        __syncthreads();
+        n_gu = block_excl_scan<Scan>(S.gu_pre, U, scan_tmp);
+        n_dn = block_excl_scan<Scan>(S.dn_pre, U, scan_tmp);
     }
-    __syncthreads();
-    const int n_gu = block_excl_scan<Scan>(S.gu_pre, U, scan_tmp);
-    const int n_dn = block_excl_scan<Scan>(S.dn_pre, U, scan_tmp);
     if (blockIdx.x == 0) {
         // the call's routing for the host (stats, profiling)
         if (!topk_spread)
